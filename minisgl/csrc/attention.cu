@@ -1,0 +1,545 @@
+// Paged GQA attention for sm_100a: decode (split-KV flash-decoding) and
+// causal prefill/extend over a paged KV pool.
+//
+// Replaces the reference's attention backends (python/minisgl/attention/
+// trtllm.py:49-89 TRT-LLM FMHA, attention/fi.py, attention/fa.py).
+//
+// KV tiles of 64 keys x head_dim (128) bf16 are moved by TMA (2-D tensor map
+// over the whole pool, 128-byte swizzle, one box per page segment and
+// 64-column half) into a multi-stage mbarrier ring. Scores and P.V use the
+// warp-level bf16 tensor-core MMA (m16n8k16) with ldmatrix fragments read
+// from the swizzled tiles. Decode attention moves ~2 bytes per multiply-add
+// pair (GQA group <= 16 query rows per key), so it is bound by HBM bandwidth,
+// not by the tensor pipe; the design goal is to keep enough bytes in flight
+// (3 stages x 32 KB per CTA, 2 CTAs per SM) to saturate HBM3e.
+//
+// Softmax runs in the exp2 domain: q is pre-scaled by scale * log2(e).
+#include <algorithm>
+#include <stdexcept>
+
+#include "common.cuh"
+#include "ops.h"
+#include "tma_host.h"
+
+namespace minisgl {
+namespace {
+
+constexpr int kD = 128;      // head_dim supported by the tensor-core path
+constexpr int kTile = 64;    // keys per tile
+constexpr int kStages = 3;
+constexpr int kHalfBytes = kTile * 128;        // one 64-column half of a tile (8 KB)
+constexpr int kTileBytes = 2 * kHalfBytes;     // K or V tile (16 KB)
+constexpr int kStageBytes = 2 * kTileBytes;    // K + V (32 KB)
+constexpr float kLog2e = 1.4426950408889634f;
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                        uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2,
+                                          uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void mma_bf16(float (&c)[4], const uint32_t (&a)[4], uint32_t b0,
+                                         uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, "
+      "{%8,%9}, {%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+}
+
+// Byte offset of (row, 16-byte chunk 0..15) inside a 64-row tile stored as
+// two 128B-swizzled halves (chunks 0..7 and 8..15).
+__device__ __forceinline__ uint32_t tile_off(int row, int chunk) {
+  const int half = chunk >> 3;
+  const int c = chunk & 7;
+  return half * kHalfBytes + row * 128 + ((c ^ (row & 7)) << 4);
+}
+
+// Issue the TMA loads of one 64-key tile (K and V) starting at position p0.
+__device__ __forceinline__ void issue_kv_tile(uint8_t* stage, uint64_t* bar,
+                                              const CUtensorMap* tm, const AttnArgs& a,
+                                              const int32_t* pt_row, int L, int p0, int h) {
+  mbar_arrive_expect_tx(bar, kStageBytes);
+  const int P = a.page_size;
+  const int seg = P < kTile ? P : kTile;
+  for (int j = 0; j < kTile; j += seg) {
+    const int pos = p0 + j;
+    int page = 0;
+    if (pos < L) page = pt_row[pos] / P;  // positions past the end read page 0 (masked later)
+    const int64_t in_page = P < kTile ? 0 : (p0 % P);
+    const int64_t row = (static_cast<int64_t>(page) * a.hk + h) * P + in_page;
+    const int32_t rk = static_cast<int32_t>(a.k_row0 + row);
+    const int32_t rv = static_cast<int32_t>(a.v_row0 + row);
+    uint8_t* k = stage;
+    uint8_t* v = stage + kTileBytes;
+    tma_load_2d(k + j * 128, tm, bar, 0, rk);
+    tma_load_2d(k + kHalfBytes + j * 128, tm, bar, 64, rk);
+    tma_load_2d(v + j * 128, tm, bar, 0, rv);
+    tma_load_2d(v + kHalfBytes + j * 128, tm, bar, 64, rv);
+  }
+}
+
+// Load 16 query rows (rows >= nrows are zero) as m16n8k16 A fragments for the
+// 8 k-steps of d = 128, pre-scaled by `mul`.
+__device__ __forceinline__ void load_q_frags(uint32_t (&qa)[8][4], const __nv_bfloat16* q,
+                                             int64_t row_stride, int nrows, float mul) {
+  const int lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+#pragma unroll
+  for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+    for (int r = 0; r < 4; ++r) {
+      const int row = g + ((r & 1) ? 8 : 0);
+      const int col = ks * 16 + 2 * t + ((r & 2) ? 8 : 0);
+      float x0 = 0.f, x1 = 0.f;
+      if (row < nrows) {
+        const __nv_bfloat162 v =
+            *reinterpret_cast<const __nv_bfloat162*>(q + row * row_stride + col);
+        x0 = __bfloat162float(v.x) * mul;
+        x1 = __bfloat162float(v.y) * mul;
+      }
+      qa[ks][r] = pack_bf16x2(x0, x1);
+    }
+  }
+}
+
+// ============================================================== decode ====
+// grid (max_splits, hk, B); 4 warps. Warp w handles keys [16w, 16w+16) of
+// each tile for all G = hq / hk query heads of this kv head; the four
+// partial softmax states are merged at the end.
+__global__ void __launch_bounds__(128, 2)
+    decode_attn_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  const ErrorSink err{a.err};
+
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int G = a.hq / a.hk;
+  const int L = a.seq_lens[b];
+  // chunk of keys for this split: a multiple of the tile, at least one tile
+  int chunk = (L + a.max_splits - 1) / a.max_splits;
+  chunk = max(kTile, (chunk + kTile - 1) / kTile * kTile);
+  const int nsplit = max(1, (L + chunk - 1) / chunk);
+  if (split >= nsplit) return;
+  const int k_begin = split * chunk;
+  const int k_end = min(L, k_begin + chunk);
+  const int ntiles = k_end > k_begin ? (k_end - k_begin + kTile - 1) / kTile : 0;
+  const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    prefetch_tmap(&tm);
+    for (int i = 0; i < kStages && i < ntiles; ++i)
+      issue_kv_tile(smem + i * kStageBytes, &bars[i], &tm, a, pt_row, L, k_begin + i * kTile, h);
+  }
+  __syncthreads();
+
+  const __nv_bfloat16* qb =
+      reinterpret_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(b) * a.ld_q + h * G * kD;
+  uint32_t qa[8][4];
+  load_q_frags(qa, qb, kD, G, a.scale * kLog2e);
+
+  const int g = lane >> 2, t = lane & 3;
+  float m_lo = -INFINITY, m_hi = -INFINITY;  // running max for rows g and g+8
+  float l_lo = 0.f, l_hi = 0.f;
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+  bool ok = true;
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % kStages;
+    if (ok) ok = mbar_wait(&bars[s], (i / kStages) & 1u, err, 201);
+    const uint32_t kbase = smem_u32(smem + s * kStageBytes);
+    const uint32_t vbase = kbase + kTileBytes;
+    const int tok0 = warp * 16;  // this warp's 16 keys inside the tile
+    // S = Q K^T for 16 rows x 16 keys
+    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int tok = tok0 + (mi >> 1) * 8 + rr;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(kbase + tile_off(tok, ks * 2 + (mi & 1)), b0, b1, b2, b3);
+        mma_bf16(sc[0], qa[ks], b0, b1);
+        mma_bf16(sc[1], qa[ks], b2, b3);
+      }
+    }
+    // mask keys past the end of this split
+    const int pos0 = k_begin + i * kTile + tok0;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const int pos = pos0 + nt * 8 + 2 * t + (e & 1);
+        if (pos >= k_end) sc[nt][e] = -INFINITY;
+      }
+    }
+    // online softmax (rows g: elements 0,1 ; rows g+8: elements 2,3)
+    float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+    float mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+    const float new_lo = fmaxf(m_lo, mx_lo), new_hi = fmaxf(m_hi, mx_hi);
+    const float base_lo = new_lo == -INFINITY ? 0.f : new_lo;
+    const float base_hi = new_hi == -INFINITY ? 0.f : new_hi;
+    const float alpha_lo = exp2f(m_lo - base_lo), alpha_hi = exp2f(m_hi - base_hi);
+    m_lo = new_lo, m_hi = new_hi;
+    float p[2][4];
+    float sum_lo = 0.f, sum_hi = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < 2; ++nt) {
+      p[nt][0] = exp2f(sc[nt][0] - base_lo);
+      p[nt][1] = exp2f(sc[nt][1] - base_lo);
+      p[nt][2] = exp2f(sc[nt][2] - base_hi);
+      p[nt][3] = exp2f(sc[nt][3] - base_hi);
+      sum_lo += p[nt][0] + p[nt][1];
+      sum_hi += p[nt][2] + p[nt][3];
+    }
+    l_lo = l_lo * alpha_lo + sum_lo;
+    l_hi = l_hi * alpha_hi + sum_hi;
+#pragma unroll
+    for (int n = 0; n < 16; ++n) {
+      o[n][0] *= alpha_lo, o[n][1] *= alpha_lo;
+      o[n][2] *= alpha_hi, o[n][3] *= alpha_hi;
+    }
+    uint32_t pa[4];
+    pa[0] = pack_bf16x2(p[0][0], p[0][1]);
+    pa[1] = pack_bf16x2(p[0][2], p[0][3]);
+    pa[2] = pack_bf16x2(p[1][0], p[1][1]);
+    pa[3] = pack_bf16x2(p[1][2], p[1][3]);
+    // O += P V   (V rows tok0..tok0+15, all 128 columns)
+    {
+      const int mi = lane >> 3, rr = lane & 7;
+      const int tok = tok0 + (mi & 1) * 8 + rr;
+#pragma unroll
+      for (int nd = 0; nd < 16; nd += 2) {
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4_t(vbase + tile_off(tok, nd + (mi >> 1)), b0, b1, b2, b3);
+        mma_bf16(o[nd], pa, b0, b1);
+        mma_bf16(o[nd + 1], pa, b2, b3);
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && i + kStages < ntiles) {
+      fence_proxy_async_smem();
+      issue_kv_tile(smem + s * kStageBytes, &bars[s], &tm, a, pt_row, L,
+                    k_begin + (i + kStages) * kTile, h);
+    }
+  }
+
+  // ---- merge the four warps' partial states (rows < G) through shared memory
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  __syncthreads();  // pipeline buffers are free now
+  float* so = reinterpret_cast<float*>(smem);           // [4 warps][16 rows][128]
+  float* sm = so + 4 * 16 * kD;                          // [4][16]
+  float* sl = sm + 4 * 16;                               // [4][16]
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const int col = n * 8 + 2 * t;
+    so[(warp * 16 + g) * kD + col] = o[n][0];
+    so[(warp * 16 + g) * kD + col + 1] = o[n][1];
+    so[(warp * 16 + g + 8) * kD + col] = o[n][2];
+    so[(warp * 16 + g + 8) * kD + col + 1] = o[n][3];
+  }
+  if (t == 0) {
+    sm[warp * 16 + g] = m_lo;
+    sm[warp * 16 + g + 8] = m_hi;
+    sl[warp * 16 + g] = l_lo;
+    sl[warp * 16 + g + 8] = l_hi;
+  }
+  __syncthreads();
+  // each warp finishes rows warp, warp+4, ... (< G); lane covers 4 columns
+  for (int r = warp; r < G; r += 4) {
+    float mx = -INFINITY;
+    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, sm[w * 16 + r]);
+    const float base = mx == -INFINITY ? 0.f : mx;
+    float lsum = 0.f, f[4];
+    for (int w = 0; w < 4; ++w) {
+      f[w] = exp2f(sm[w * 16 + r] - base);
+      lsum += sl[w * 16 + r] * f[w];
+    }
+    float acc[4] = {0.f, 0.f, 0.f, 0.f};
+    for (int w = 0; w < 4; ++w) {
+      const float* src = so + (w * 16 + r) * kD + lane * 4;
+#pragma unroll
+      for (int c = 0; c < 4; ++c) acc[c] += src[c] * f[w];
+    }
+    const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
+    const int qh = h * G + r;
+    if (nsplit == 1) {
+      __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) +
+                           (static_cast<int64_t>(b) * a.hq + qh) * kD + lane * 4;
+      uint2 pk;
+      pk.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+      pk.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+      *reinterpret_cast<uint2*>(dst) = pk;
+    } else {
+      const int64_t slot = (static_cast<int64_t>(b) * a.hq + qh) * a.max_splits + split;
+      float* dst = a.part_o + slot * kD + lane * 4;
+      *reinterpret_cast<float4*>(dst) =
+          make_float4(acc[0] * inv, acc[1] * inv, acc[2] * inv, acc[3] * inv);
+      // log2-sum-exp of this split (in the scaled exp2 domain)
+      if (lane == 0) a.part_lse[slot] = lsum > 0.f ? base + log2f(lsum) : -INFINITY;
+    }
+  }
+}
+
+// Merge split-KV partials: grid (B), block = 32 * 4 threads, warp per head.
+__global__ void decode_combine_kernel(AttnArgs a) {
+  const int b = blockIdx.y;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int qh = blockIdx.x * 4 + warp;
+  if (qh >= a.hq) return;
+  const int L = a.seq_lens[b];
+  int chunk = (L + a.max_splits - 1) / a.max_splits;
+  chunk = max(kTile, (chunk + kTile - 1) / kTile * kTile);
+  const int nsplit = max(1, (L + chunk - 1) / chunk);
+  if (nsplit == 1) return;  // written directly by the main kernel
+  const int64_t base_slot = (static_cast<int64_t>(b) * a.hq + qh) * a.max_splits;
+  float mx = -INFINITY;
+  for (int s = 0; s < nsplit; ++s) mx = fmaxf(mx, a.part_lse[base_slot + s]);
+  const float base = mx == -INFINITY ? 0.f : mx;
+  float acc[4] = {0.f, 0.f, 0.f, 0.f}, wsum = 0.f;
+  for (int s = 0; s < nsplit; ++s) {
+    const float w = exp2f(a.part_lse[base_slot + s] - base);
+    wsum += w;
+    const float4 v = *reinterpret_cast<const float4*>(a.part_o + (base_slot + s) * kD + lane * 4);
+    acc[0] += v.x * w, acc[1] += v.y * w, acc[2] += v.z * w, acc[3] += v.w * w;
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  __nv_bfloat16* dst =
+      reinterpret_cast<__nv_bfloat16*>(a.out) + (static_cast<int64_t>(b) * a.hq + qh) * kD + lane * 4;
+  uint2 pk;
+  pk.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  pk.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(dst) = pk;
+}
+
+// ============================================================= prefill ====
+// grid (ceil(max_q / 64), hq, B); 4 warps, warp w owns query rows
+// [16w, 16w + 16) of the 64-row query tile. Causal: query i of request b sits
+// at position (L_b - q_len_b + i) and sees keys [0, position].
+__global__ void __launch_bounds__(128, 2)
+    prefill_attn_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  const ErrorSink err{a.err};
+
+  const int qt = blockIdx.x, qh = blockIdx.y, b = blockIdx.z;
+  const int q_begin = a.cu_q[b];
+  const int q_len = a.cu_q[b + 1] - q_begin;
+  if (qt * 64 >= q_len) return;
+  const int L = a.seq_lens[b];
+  const int cached = L - q_len;
+  const int G = a.hq / a.hk;
+  const int h = qh / G;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = lane >> 2, t = lane & 3;
+  const int row0 = qt * 64;                       // first query row of this CTA
+  const int last_pos = cached + min(q_len, row0 + 64) - 1;  // largest position in the tile
+  const int ntiles = last_pos / kTile + 1;
+  const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+    fence_barrier_init();
+    prefetch_tmap(&tm);
+    for (int i = 0; i < kStages && i < ntiles; ++i)
+      issue_kv_tile(smem + i * kStageBytes, &bars[i], &tm, a, pt_row, L, i * kTile, h);
+  }
+  __syncthreads();
+
+  const int wrow0 = row0 + warp * 16;  // this warp's first query row
+  const __nv_bfloat16* qb = reinterpret_cast<const __nv_bfloat16*>(a.q) +
+                            static_cast<int64_t>(q_begin + wrow0) * a.ld_q + qh * kD;
+  uint32_t qa[8][4];
+  load_q_frags(qa, qb, a.ld_q, max(0, min(16, q_len - wrow0)), a.scale * kLog2e);
+  const int pos_lo = cached + wrow0 + g;  // positions of rows g and g+8
+  const int pos_hi = pos_lo + 8;
+
+  float m_lo = -INFINITY, m_hi = -INFINITY, l_lo = 0.f, l_hi = 0.f;
+  float o[16][4];
+#pragma unroll
+  for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
+
+  bool ok = true;
+  const int warp_last = cached + min(q_len, wrow0 + 16) - 1;
+  for (int i = 0; i < ntiles; ++i) {
+    const int s = i % kStages;
+    if (ok) ok = mbar_wait(&bars[s], (i / kStages) & 1u, err, 211);
+    const uint32_t kbase = smem_u32(smem + s * kStageBytes);
+    const uint32_t vbase = kbase + kTileBytes;
+    const int kpos0 = i * kTile;
+    if (wrow0 < q_len && kpos0 <= warp_last) {
+      float sc[8][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) sc[nt][0] = sc[nt][1] = sc[nt][2] = sc[nt][3] = 0.f;
+      const int mi = lane >> 3, rr = lane & 7;
+#pragma unroll
+      for (int ks = 0; ks < 8; ++ks) {
+#pragma unroll
+        for (int np = 0; np < 4; ++np) {  // pairs of 8-key n-tiles
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kbase + tile_off(np * 16 + (mi >> 1) * 8 + rr, ks * 2 + (mi & 1)), b0, b1, b2, b3);
+          mma_bf16(sc[2 * np], qa[ks], b0, b1);
+          mma_bf16(sc[2 * np + 1], qa[ks], b2, b3);
+        }
+      }
+      // causal + length mask
+      if (kpos0 + kTile - 1 > pos_lo || kpos0 + kTile > L) {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const int kp = kpos0 + nt * 8 + 2 * t + (e & 1);
+            const int qp = (e & 2) ? pos_hi : pos_lo;
+            if (kp > qp || kp >= L) sc[nt][e] = -INFINITY;
+          }
+        }
+      }
+      float mx_lo = -INFINITY, mx_hi = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        mx_lo = fmaxf(mx_lo, fmaxf(sc[nt][0], sc[nt][1]));
+        mx_hi = fmaxf(mx_hi, fmaxf(sc[nt][2], sc[nt][3]));
+      }
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+      const float new_lo = fmaxf(m_lo, mx_lo), new_hi = fmaxf(m_hi, mx_hi);
+      const float base_lo = new_lo == -INFINITY ? 0.f : new_lo;
+      const float base_hi = new_hi == -INFINITY ? 0.f : new_hi;
+      const float alpha_lo = exp2f(m_lo - base_lo), alpha_hi = exp2f(m_hi - base_hi);
+      m_lo = new_lo, m_hi = new_hi;
+      float sum_lo = 0.f, sum_hi = 0.f;
+      uint32_t pa[4][4];
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const float p0 = exp2f(sc[nt][0] - base_lo), p1 = exp2f(sc[nt][1] - base_lo);
+        const float p2 = exp2f(sc[nt][2] - base_hi), p3 = exp2f(sc[nt][3] - base_hi);
+        sum_lo += p0 + p1;
+        sum_hi += p2 + p3;
+        // A fragment for k-step kk = nt / 2: (row g | g+8) x (keys 2t | 2t+8)
+        pa[nt >> 1][(nt & 1) * 2 + 0] = pack_bf16x2(p0, p1);
+        pa[nt >> 1][(nt & 1) * 2 + 1] = pack_bf16x2(p2, p3);
+      }
+      l_lo = l_lo * alpha_lo + sum_lo;
+      l_hi = l_hi * alpha_hi + sum_hi;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= alpha_lo, o[n][1] *= alpha_lo;
+        o[n][2] *= alpha_hi, o[n][3] *= alpha_hi;
+      }
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk) {
+        const int tok = kk * 16 + (mi & 1) * 8 + rr;
+#pragma unroll
+        for (int nd = 0; nd < 16; nd += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vbase + tile_off(tok, nd + (mi >> 1)), b0, b1, b2, b3);
+          mma_bf16(o[nd], pa[kk], b0, b1);
+          mma_bf16(o[nd + 1], pa[kk], b2, b3);
+        }
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0 && i + kStages < ntiles) {
+      fence_proxy_async_smem();
+      issue_kv_tile(smem + s * kStageBytes, &bars[s], &tm, a, pt_row, L, (i + kStages) * kTile, h);
+    }
+  }
+
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
+  l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
+  l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
+  const float inv_lo = l_lo > 0.f ? 1.f / l_lo : 0.f;
+  const float inv_hi = l_hi > 0.f ? 1.f / l_hi : 0.f;
+  __nv_bfloat16* ob = reinterpret_cast<__nv_bfloat16*>(a.out);
+  const int r_lo = wrow0 + g, r_hi = wrow0 + g + 8;
+#pragma unroll
+  for (int n = 0; n < 16; ++n) {
+    const int col = n * 8 + 2 * t;
+    if (r_lo < q_len)
+      *reinterpret_cast<uint32_t*>(ob + (static_cast<int64_t>(q_begin + r_lo) * a.hq + qh) * kD + col) =
+          pack_bf16x2(o[n][0] * inv_lo, o[n][1] * inv_lo);
+    if (r_hi < q_len)
+      *reinterpret_cast<uint32_t*>(ob + (static_cast<int64_t>(q_begin + r_hi) * a.hq + qh) * kD + col) =
+          pack_bf16x2(o[n][2] * inv_hi, o[n][3] * inv_hi);
+  }
+}
+
+constexpr int kAttnSmem = kStages * kStageBytes + 1024 + 128;
+
+CUtensorMap pool_map(const AttnArgs& a) {
+  const uint32_t box_rows = a.page_size < kTile ? a.page_size : kTile;
+  return make_tmap_bf16_2d_sw128(a.kv_pool, a.pool_rows, a.d, a.d, box_rows);
+}
+
+void check_args(const AttnArgs& a) {
+  if (a.d != kD) throw std::runtime_error("minisgl.attention: head_dim must be 128");
+  if (a.hq % a.hk != 0 || a.hq / a.hk > 16)
+    throw std::runtime_error("minisgl.attention: need hq % hk == 0 and a GQA group of at most 16");
+  if (a.page_size < 16 || (a.page_size & (a.page_size - 1)) != 0)
+    throw std::runtime_error("minisgl.attention: page_size must be a power of two >= 16");
+  if (a.pool_rows >= (int64_t(1) << 31)) throw std::runtime_error("minisgl.attention: KV pool too large for int32 rows");
+}
+
+template <int Tag, typename K>
+void set_smem_once(K kern) {
+  static bool done[64] = {};  // per kernel (Tag) and device
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!done[dev & 63]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+    done[dev & 63] = true;
+  }
+}
+
+}  // namespace
+
+void launch_decode_attention(const AttnArgs& a, cudaStream_t s) {
+  if (a.B <= 0) return;
+  check_args(a);
+  if (a.max_splits > 1 && (a.part_o == nullptr || a.part_lse == nullptr))
+    throw std::runtime_error("minisgl.attention: split-KV decode needs scratch buffers");
+  CUtensorMap tm = pool_map(a);
+  set_smem_once<0>(decode_attn_kernel);
+  dim3 grid(std::max(1, a.max_splits), a.hk, a.B);
+  decode_attn_kernel<<<grid, 128, kAttnSmem, s>>>(tm, a);
+  if (a.max_splits > 1) {
+    dim3 g2((a.hq + 3) / 4, a.B);
+    decode_combine_kernel<<<g2, 128, 0, s>>>(a);
+  }
+}
+
+void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
+  if (a.B <= 0 || a.max_q <= 0) return;
+  check_args(a);
+  CUtensorMap tm = pool_map(a);
+  set_smem_once<1>(prefill_attn_kernel);
+  dim3 grid((a.max_q + 63) / 64, a.hq, a.B);
+  prefill_attn_kernel<<<grid, 128, kAttnSmem, s>>>(tm, a);
+}
+
+}  // namespace minisgl

@@ -1,0 +1,404 @@
+// Python bindings of the minisgl native library (module `minisgl._C`).
+//
+// Every entry point validates device, dtype, shape and contiguity of its
+// tensor arguments on the host (the role of the reference's TensorMatcher,
+// python/minisgl/kernel/csrc/include/minisgl/tensor.h) and then calls the
+// plain launchers declared in ops.h on the current CUDA stream.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "ops.h"
+
+namespace minisgl {
+int64_t compare_key_raw(const void* a, int64_t na, int ea, const void* b, int64_t nb, int eb);
+}
+
+using minisgl::DType;
+
+namespace {
+
+#define MSG_CHECK(cond, ...) TORCH_CHECK(cond, "minisgl: ", __VA_ARGS__)
+
+DType dtype_of(const at::Tensor& t) {
+  switch (t.scalar_type()) {
+    case at::kBFloat16: return DType::kBF16;
+    case at::kHalf: return DType::kF16;
+    case at::kFloat: return DType::kF32;
+    default: MSG_CHECK(false, "unsupported dtype ", t.scalar_type());
+  }
+  return DType::kF32;
+}
+
+void check_cuda(const at::Tensor& t, const char* name) {
+  MSG_CHECK(t.is_cuda(), name, " must be a CUDA tensor");
+}
+void check_rowmajor(const at::Tensor& t, const char* name) {
+  MSG_CHECK(t.dim() == 2 && t.stride(1) == 1, name, " must be a 2-D tensor with unit column stride");
+}
+void check_same_device(const at::Tensor& a, const at::Tensor& b) {
+  MSG_CHECK(a.device() == b.device(), "tensors are on different devices");
+}
+void check_i32(const at::Tensor& t, const char* name) {
+  check_cuda(t, name);
+  MSG_CHECK(t.scalar_type() == at::kInt && t.is_contiguous(), name, " must be contiguous int32");
+}
+int* err_ptr(const c10::optional<at::Tensor>& err) {
+  if (!err.has_value()) return nullptr;
+  MSG_CHECK(err->scalar_type() == at::kInt && err->numel() >= 2 && err->is_cuda(),
+            "error word must be a CUDA int32 tensor with 2 elements");
+  return err->data_ptr<int>();
+}
+cudaStream_t stream_of(const at::Tensor& t) {
+  return at::cuda::getCurrentCUDAStream(t.device().index()).stream();
+}
+
+// ------------------------------------------------------------------- GEMM
+void gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w,
+          const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& workspace,
+          int64_t force_splits, int64_t force_mode, const c10::optional<at::Tensor>& err) {
+  check_cuda(x, "x");
+  check_cuda(w, "w");
+  check_cuda(out, "out");
+  check_same_device(x, w);
+  check_same_device(x, out);
+  check_rowmajor(x, "x");
+  check_rowmajor(w, "w");
+  check_rowmajor(out, "out");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+            "gemm inputs must be bfloat16");
+  MSG_CHECK(out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kFloat,
+            "gemm output must be bfloat16 or float32");
+  MSG_CHECK(x.size(1) == w.size(1), "gemm K mismatch: ", x.sizes(), " vs ", w.sizes());
+  MSG_CHECK(out.size(0) == x.size(0) && out.size(1) == w.size(0), "gemm output shape mismatch");
+  minisgl::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.bias = nullptr;
+  if (bias.has_value()) {
+    MSG_CHECK(bias->is_cuda() && bias->scalar_type() == at::kBFloat16 && bias->is_contiguous() &&
+                  bias->numel() == w.size(0),
+              "bias must be a contiguous bf16 vector of N elements");
+    a.bias = bias->data_ptr();
+  }
+  a.out = out.data_ptr();
+  a.workspace = nullptr;
+  a.workspace_elems = 0;
+  if (workspace.has_value()) {
+    MSG_CHECK(workspace->is_cuda() && workspace->scalar_type() == at::kFloat && workspace->is_contiguous(),
+              "workspace must be contiguous float32");
+    a.workspace = workspace->data_ptr<float>();
+    a.workspace_elems = workspace->numel();
+  }
+  a.M = static_cast<int>(x.size(0));
+  a.N = static_cast<int>(w.size(0));
+  a.K = static_cast<int>(x.size(1));
+  a.ldx = static_cast<int>(x.stride(0));
+  a.ldw = static_cast<int>(w.stride(0));
+  a.ldo = static_cast<int>(out.stride(0));
+  a.out_f32 = out.scalar_type() == at::kFloat;
+  a.force_splits = static_cast<int>(force_splits);
+  a.force_mode = static_cast<int>(force_mode);
+  a.err = err_ptr(err);
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_gemm(a, stream_of(x));
+}
+
+int64_t gemm_workspace_elems(int64_t M, int64_t N, int64_t K) {
+  return minisgl::gemm_workspace_elems(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
+}
+
+// ------------------------------------------------------------ elementwise
+void rmsnorm(at::Tensor out, const at::Tensor& x, const at::Tensor& w, double eps) {
+  check_cuda(x, "x");
+  check_rowmajor(x, "x");
+  check_rowmajor(out, "out");
+  MSG_CHECK(w.is_contiguous() && w.numel() == x.size(1), "rmsnorm weight shape");
+  MSG_CHECK(out.sizes() == x.sizes() && out.scalar_type() == x.scalar_type() &&
+                w.scalar_type() == x.scalar_type(),
+            "rmsnorm dtype/shape mismatch");
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_rmsnorm(out.data_ptr(), x.data_ptr(), w.data_ptr(), static_cast<int>(x.size(0)),
+                          static_cast<int>(x.size(1)), static_cast<int>(x.stride(0)),
+                          static_cast<int>(out.stride(0)), static_cast<float>(eps), dtype_of(x),
+                          stream_of(x));
+}
+
+void fused_add_rmsnorm(at::Tensor x, at::Tensor residual, const at::Tensor& w, double eps) {
+  check_cuda(x, "x");
+  MSG_CHECK(x.is_contiguous() && residual.is_contiguous() && x.sizes() == residual.sizes() &&
+                x.dim() == 2,
+            "fused_add_rmsnorm needs contiguous 2-D x and residual of equal shape");
+  MSG_CHECK(x.scalar_type() == residual.scalar_type() && w.scalar_type() == x.scalar_type() &&
+                w.numel() == x.size(1),
+            "fused_add_rmsnorm dtype/shape mismatch");
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_fused_add_rmsnorm(x.data_ptr(), residual.data_ptr(), w.data_ptr(),
+                                    static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
+                                    static_cast<float>(eps), dtype_of(x), stream_of(x));
+}
+
+void act_and_mul(at::Tensor out, const at::Tensor& x, int64_t act) {
+  check_cuda(x, "x");
+  MSG_CHECK(x.is_contiguous() && out.is_contiguous() && x.dim() == 2 && out.dim() == 2 &&
+                x.size(1) == 2 * out.size(1) && x.size(0) == out.size(0) &&
+                x.scalar_type() == out.scalar_type(),
+            "act_and_mul shape mismatch");
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_act_and_mul(out.data_ptr(), x.data_ptr(), static_cast<int>(x.size(0)),
+                              static_cast<int>(out.size(1)), static_cast<int>(act), dtype_of(x),
+                              stream_of(x));
+}
+
+void embedding(at::Tensor out, const at::Tensor& w, const at::Tensor& ids, int64_t vocab_lo,
+               int64_t vocab_n) {
+  check_cuda(w, "weight");
+  check_i32(ids, "ids");
+  MSG_CHECK(w.is_contiguous() && out.is_contiguous() && out.size(0) == ids.numel() &&
+                out.size(1) == w.size(1) && out.scalar_type() == w.scalar_type(),
+            "embedding shape mismatch");
+  const c10::cuda::CUDAGuard guard(w.device());
+  minisgl::launch_embedding(out.data_ptr(), w.data_ptr(), ids.data_ptr<int32_t>(),
+                            static_cast<int>(ids.numel()), static_cast<int>(w.size(1)),
+                            static_cast<int>(vocab_lo), static_cast<int>(vocab_n), dtype_of(w),
+                            stream_of(w));
+}
+
+// ------------------------------------------------------ rope + KV store
+void rope_store(at::Tensor qkv, const at::Tensor& positions, const at::Tensor& cos_sin,
+                const c10::optional<at::Tensor>& q_norm_w, const c10::optional<at::Tensor>& k_norm_w,
+                at::Tensor k_cache, at::Tensor v_cache, const at::Tensor& out_loc, int64_t hq,
+                int64_t hk, int64_t d, int64_t page_size, double eps) {
+  check_cuda(qkv, "qkv");
+  check_rowmajor(qkv, "qkv");
+  check_i32(positions, "positions");
+  check_i32(out_loc, "out_loc");
+  MSG_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == d,
+            "cos_sin cache must be float32 [max_pos, head_dim]");
+  MSG_CHECK(qkv.size(1) >= (hq + 2 * hk) * d, "qkv too narrow");
+  MSG_CHECK(positions.numel() == qkv.size(0) && out_loc.numel() == qkv.size(0), "token count mismatch");
+  MSG_CHECK(k_cache.scalar_type() == qkv.scalar_type() && v_cache.scalar_type() == qkv.scalar_type(),
+            "cache dtype mismatch");
+  minisgl::RopeStoreArgs a{};
+  a.qkv = qkv.data_ptr();
+  a.ld_qkv = static_cast<int>(qkv.stride(0));
+  a.positions = positions.data_ptr<int32_t>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.q_norm_w = q_norm_w.has_value() ? q_norm_w->data_ptr() : nullptr;
+  a.k_norm_w = k_norm_w.has_value() ? k_norm_w->data_ptr() : nullptr;
+  a.k_cache = k_cache.data_ptr();
+  a.v_cache = v_cache.data_ptr();
+  a.out_loc = out_loc.data_ptr<int32_t>();
+  a.T = static_cast<int>(qkv.size(0));
+  a.hq = static_cast<int>(hq);
+  a.hk = static_cast<int>(hk);
+  a.d = static_cast<int>(d);
+  a.rot_dim = static_cast<int>(d);
+  a.page_size = static_cast<int>(page_size);
+  a.eps = static_cast<float>(eps);
+  a.dt = dtype_of(qkv);
+  const c10::cuda::CUDAGuard guard(qkv.device());
+  minisgl::launch_rope_store(a, stream_of(qkv));
+}
+
+// -------------------------------------------------------------- attention
+minisgl::AttnArgs attn_common(const at::Tensor& q, at::Tensor& out, const at::Tensor& kv_pool,
+                              int64_t layer, const at::Tensor& page_table, const at::Tensor& req_rows,
+                              const at::Tensor& seq_lens, int64_t hq, int64_t hk, int64_t d,
+                              int64_t page_size, double scale) {
+  check_cuda(q, "q");
+  check_cuda(kv_pool, "kv_pool");
+  check_i32(page_table, "page_table");
+  check_i32(req_rows, "req_rows");
+  check_i32(seq_lens, "seq_lens");
+  MSG_CHECK(q.scalar_type() == at::kBFloat16 && kv_pool.scalar_type() == at::kBFloat16,
+            "attention needs bfloat16 q and KV pool");
+  MSG_CHECK(q.dim() == 2 && q.stride(1) == 1 && q.size(1) >= hq * d, "q must be [T, >= hq*d] row-major");
+  MSG_CHECK(out.is_contiguous() && out.numel() == q.size(0) * hq * d, "out must be contiguous [T, hq*d]");
+  // pool: [2, layers, pages, hk, page_size, d]
+  MSG_CHECK(kv_pool.dim() == 6 && kv_pool.is_contiguous() && kv_pool.size(0) == 2 &&
+                kv_pool.size(3) == hk && kv_pool.size(4) == page_size && kv_pool.size(5) == d,
+            "kv_pool must be [2, layers, pages, hk, page_size, d]");
+  MSG_CHECK(layer >= 0 && layer < kv_pool.size(1), "layer out of range");
+  minisgl::AttnArgs a{};
+  a.q = q.data_ptr();
+  a.ld_q = static_cast<int>(q.stride(0));
+  a.out = out.data_ptr();
+  a.kv_pool = kv_pool.data_ptr();
+  const int64_t L = kv_pool.size(1), P = kv_pool.size(2);
+  const int64_t rows_per_layer = P * hk * page_size;
+  a.pool_rows = 2 * L * rows_per_layer;
+  a.k_row0 = layer * rows_per_layer;
+  a.v_row0 = (L + layer) * rows_per_layer;
+  a.page_table = page_table.data_ptr<int32_t>();
+  a.ld_pt = static_cast<int>(page_table.stride(0));
+  a.req_rows = req_rows.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.B = static_cast<int>(req_rows.numel());
+  a.hq = static_cast<int>(hq);
+  a.hk = static_cast<int>(hk);
+  a.d = static_cast<int>(d);
+  a.page_size = static_cast<int>(page_size);
+  a.scale = static_cast<float>(scale);
+  return a;
+}
+
+void decode_attention(const at::Tensor& q, at::Tensor out, const at::Tensor& kv_pool, int64_t layer,
+                      const at::Tensor& page_table, const at::Tensor& req_rows,
+                      const at::Tensor& seq_lens, int64_t hq, int64_t hk, int64_t d,
+                      int64_t page_size, double scale, const c10::optional<at::Tensor>& part_o,
+                      const c10::optional<at::Tensor>& part_lse, int64_t max_splits,
+                      const c10::optional<at::Tensor>& err) {
+  auto a = attn_common(q, out, kv_pool, layer, page_table, req_rows, seq_lens, hq, hk, d, page_size, scale);
+  MSG_CHECK(q.size(0) == a.B, "decode attention expects one query token per request");
+  a.max_splits = static_cast<int>(std::max<int64_t>(1, max_splits));
+  a.part_o = nullptr;
+  a.part_lse = nullptr;
+  if (a.max_splits > 1) {
+    MSG_CHECK(part_o.has_value() && part_lse.has_value(), "split-KV decode needs part_o and part_lse");
+    MSG_CHECK(part_o->scalar_type() == at::kFloat && part_o->is_contiguous() &&
+                  part_o->numel() >= static_cast<int64_t>(a.B) * hq * a.max_splits * d,
+              "part_o too small");
+    MSG_CHECK(part_lse->scalar_type() == at::kFloat && part_lse->is_contiguous() &&
+                  part_lse->numel() >= static_cast<int64_t>(a.B) * hq * a.max_splits,
+              "part_lse too small");
+    a.part_o = part_o->data_ptr<float>();
+    a.part_lse = part_lse->data_ptr<float>();
+  }
+  a.err = err_ptr(err);
+  const c10::cuda::CUDAGuard guard(q.device());
+  minisgl::launch_decode_attention(a, stream_of(q));
+}
+
+void prefill_attention(const at::Tensor& q, at::Tensor out, const at::Tensor& kv_pool, int64_t layer,
+                       const at::Tensor& page_table, const at::Tensor& req_rows,
+                       const at::Tensor& seq_lens, const at::Tensor& cu_q, int64_t max_q,
+                       int64_t hq, int64_t hk, int64_t d, int64_t page_size, double scale,
+                       const c10::optional<at::Tensor>& err) {
+  auto a = attn_common(q, out, kv_pool, layer, page_table, req_rows, seq_lens, hq, hk, d, page_size, scale);
+  check_i32(cu_q, "cu_q");
+  MSG_CHECK(cu_q.numel() == a.B + 1, "cu_q must have B + 1 entries");
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.max_q = static_cast<int>(max_q);
+  a.err = err_ptr(err);
+  const c10::cuda::CUDAGuard guard(q.device());
+  minisgl::launch_prefill_attention(a, stream_of(q));
+}
+
+// --------------------------------------------------------------- sampling
+void argmax(at::Tensor out, const at::Tensor& logits) {
+  check_cuda(logits, "logits");
+  check_i32(out, "out");
+  MSG_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+            "logits must be float32 [B, V]");
+  MSG_CHECK(out.numel() == logits.size(0), "argmax output size");
+  const c10::cuda::CUDAGuard guard(logits.device());
+  minisgl::launch_argmax(out.data_ptr<int32_t>(), logits.data_ptr<float>(),
+                         static_cast<int>(logits.size(0)), static_cast<int>(logits.size(1)),
+                         static_cast<int>(logits.stride(0)), stream_of(logits));
+}
+
+void sample(at::Tensor out, const at::Tensor& logits, const at::Tensor& temperature,
+            const c10::optional<at::Tensor>& top_k, const c10::optional<at::Tensor>& top_p,
+            int64_t seed, const c10::optional<at::Tensor>& step) {
+  check_cuda(logits, "logits");
+  check_i32(out, "out");
+  MSG_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+            "logits must be float32 [B, V]");
+  const int64_t B = logits.size(0);
+  MSG_CHECK(out.numel() == B && temperature.numel() == B && temperature.scalar_type() == at::kFloat &&
+                temperature.is_contiguous(),
+            "temperature must be float32 [B]");
+  minisgl::SampleArgs a{};
+  a.out = out.data_ptr<int32_t>();
+  a.logits = logits.data_ptr<float>();
+  a.ld = static_cast<int>(logits.stride(0));
+  a.B = static_cast<int>(B);
+  a.V = static_cast<int>(logits.size(1));
+  a.temperature = temperature.data_ptr<float>();
+  a.top_k = nullptr;
+  a.top_p = nullptr;
+  if (top_k.has_value()) {
+    check_i32(*top_k, "top_k");
+    MSG_CHECK(top_k->numel() == B, "top_k size");
+    a.top_k = top_k->data_ptr<int32_t>();
+  }
+  if (top_p.has_value()) {
+    MSG_CHECK(top_p->scalar_type() == at::kFloat && top_p->numel() == B && top_p->is_contiguous(),
+              "top_p must be float32 [B]");
+    a.top_p = top_p->data_ptr<float>();
+  }
+  a.seed = static_cast<uint64_t>(seed);
+  a.step = nullptr;
+  if (step.has_value()) {
+    MSG_CHECK(step->scalar_type() == at::kLong && step->is_cuda(), "step must be a CUDA int64 scalar");
+    a.step = step->data_ptr<int64_t>();
+  }
+  const c10::cuda::CUDAGuard guard(logits.device());
+  minisgl::launch_sample(a, stream_of(logits));
+}
+
+// -------------------------------------------------------------------- MoE
+void moe_route(const at::Tensor& logits, const c10::optional<at::Tensor>& bias, at::Tensor topk_w,
+               at::Tensor topk_ids, int64_t scoring, bool renormalize, int64_t n_group,
+               int64_t topk_group, double routed_scale) {
+  check_cuda(logits, "router logits");
+  MSG_CHECK(logits.scalar_type() == at::kFloat && logits.is_contiguous() && logits.dim() == 2,
+            "router logits must be contiguous float32 [T, E]");
+  check_i32(topk_ids, "topk_ids");
+  MSG_CHECK(topk_w.scalar_type() == at::kFloat && topk_w.is_contiguous() &&
+                topk_w.sizes() == topk_ids.sizes() && topk_w.size(0) == logits.size(0),
+            "topk output shape");
+  minisgl::MoeRouteArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.bias = nullptr;
+  if (bias.has_value()) {
+    MSG_CHECK(bias->scalar_type() == at::kFloat && bias->numel() == logits.size(1), "router bias");
+    a.bias = bias->data_ptr<float>();
+  }
+  a.topk_w = topk_w.data_ptr<float>();
+  a.topk_ids = topk_ids.data_ptr<int32_t>();
+  a.T = static_cast<int>(logits.size(0));
+  a.E = static_cast<int>(logits.size(1));
+  a.k = static_cast<int>(topk_ids.size(1));
+  a.scoring = static_cast<int>(scoring);
+  a.renormalize = renormalize;
+  a.n_group = static_cast<int>(n_group);
+  a.topk_group = static_cast<int>(topk_group);
+  a.routed_scale = static_cast<float>(routed_scale);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  minisgl::launch_moe_route(a, stream_of(logits));
+}
+
+// ------------------------------------------------------------ host helpers
+int64_t fast_compare_key(const at::Tensor& a, const at::Tensor& b) {
+  MSG_CHECK(a.is_cpu() && b.is_cpu() && a.dim() == 1 && b.dim() == 1, "keys must be 1-D CPU tensors");
+  MSG_CHECK(a.is_contiguous() && b.is_contiguous(), "keys must be contiguous");
+  const auto ea = a.element_size(), eb = b.element_size();
+  MSG_CHECK((a.scalar_type() == at::kInt || a.scalar_type() == at::kLong) &&
+                (b.scalar_type() == at::kInt || b.scalar_type() == at::kLong),
+            "keys must be int32 or int64");
+  return minisgl::compare_key_raw(a.data_ptr(), a.numel(), static_cast<int>(ea), b.data_ptr(),
+                                  b.numel(), static_cast<int>(eb));
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "minisgl native kernels for NVIDIA B200 (sm_100a)";
+  m.def("gemm", &gemm, "tcgen05 bf16 GEMM: out = x @ w^T (+ bias)", py::arg("out"), py::arg("x"),
+        py::arg("w"), py::arg("bias") = py::none(), py::arg("workspace") = py::none(),
+        py::arg("force_splits") = 0, py::arg("force_mode") = 0, py::arg("err") = py::none());
+  m.def("gemm_workspace_elems", &gemm_workspace_elems);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
+  m.def("act_and_mul", &act_and_mul);
+  m.def("embedding", &embedding);
+  m.def("rope_store", &rope_store);
+  m.def("decode_attention", &decode_attention);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("argmax", &argmax);
+  m.def("sample", &sample);
+  m.def("moe_route", &moe_route);
+  m.def("fast_compare_key", &fast_compare_key);
+}

@@ -1,0 +1,121 @@
+// Plain-C++ launcher interface between the torch binding layer (binding.cpp)
+// and the CUDA translation units. Nothing here includes torch headers, so the
+// .cu files compile quickly and stay independent of the framework layer.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace minisgl {
+
+enum class DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
+
+// ----------------------------------------------------------------- GEMM ----
+// out[M, N] = x[M, K] @ w[N, K]^T (+ bias[N]); bf16 inputs, fp32 accumulate.
+struct GemmArgs {
+  const void* x;      // bf16 [M, K], row stride ldx elements
+  const void* w;      // bf16 [N, K], row stride ldw elements
+  const void* bias;   // bf16 [N] or nullptr
+  void* out;          // [M, N] (bf16 or fp32), row stride ldo elements
+  float* workspace;   // fp32 scratch for split-K partial sums (may be nullptr)
+  int64_t workspace_elems;
+  int M, N, K;
+  int ldx, ldw, ldo;
+  bool out_f32;
+  int force_splits;   // 0 = heuristic
+  int force_mode;     // 0 = heuristic, 1 = token-major tiles, 2 = weight-major tiles (swap)
+  int* err;           // device error word (2 x int32) or nullptr
+};
+void launch_gemm(const GemmArgs& a, cudaStream_t stream);
+// Number of fp32 workspace elements launch_gemm may need for this shape.
+int64_t gemm_workspace_elems(int M, int N, int K);
+
+// ------------------------------------------------------ elementwise / norm ----
+void launch_rmsnorm(void* out, const void* x, const void* w, int rows, int cols, int ld_x,
+                    int ld_out, float eps, DType dt, cudaStream_t s);
+// x <- rmsnorm(x + residual) * w ; residual <- x + residual  (in place)
+void launch_fused_add_rmsnorm(void* x, void* residual, const void* w, int rows, int cols,
+                              float eps, DType dt, cudaStream_t s);
+// out[t, :d] = act(x[t, :d]) * x[t, d:2d]; act 0 = silu, 1 = gelu(tanh)
+void launch_act_and_mul(void* out, const void* x, int rows, int d, int act, DType dt,
+                        cudaStream_t s);
+// out[i, :] = (lo <= ids[i] < lo + n) ? w[ids[i] - lo, :] : 0
+void launch_embedding(void* out, const void* w, const int32_t* ids, int num_tokens, int hidden,
+                      int vocab_lo, int vocab_n, DType dt, cudaStream_t s);
+
+// ----------------------------------- qk-norm + RoPE + paged KV-cache store ----
+struct RopeStoreArgs {
+  void* qkv;                 // [T, (hq + 2*hk) * d] in place: q and k get normed + rotated
+  int ld_qkv;
+  const int32_t* positions;  // [T]
+  const float* cos_sin;      // [max_pos, rot_dim]: cos(rot_dim/2) | sin(rot_dim/2)
+  const void* q_norm_w;      // [d] or nullptr
+  const void* k_norm_w;      // [d] or nullptr
+  void* k_cache;             // layer slice: [num_pages, hk, page, d]
+  void* v_cache;
+  const int32_t* out_loc;    // [T] token slot (page * page_size + offset)
+  int T, hq, hk, d, rot_dim, page_size;
+  float eps;
+  DType dt;
+};
+void launch_rope_store(const RopeStoreArgs& a, cudaStream_t s);
+
+// ------------------------------------------------------------- attention ----
+// The KV pool is one tensor [2, layers, pages, hk, page_size, d]; kernels see
+// it as a 2-D [pool_rows, d] matrix and address one layer's K (V) through the
+// row offset k_row0 (v_row0). A (page, head) block of page_size rows is
+// contiguous, so a tile of keys is a single TMA box.
+struct AttnArgs {
+  const void* q;             // [T, hq, d], token stride ld_q elements
+  int ld_q;
+  void* out;                 // [T, hq, d] contiguous
+  const void* kv_pool;       // base of the whole pool (bf16)
+  int64_t pool_rows;
+  int64_t k_row0, v_row0;    // first row of this layer's K / V
+  const int32_t* page_table; // [rows, ld_pt] token slots (page * page_size + offset)
+  int ld_pt;
+  const int32_t* req_rows;   // [B] row of page_table per request
+  const int32_t* seq_lens;   // [B] total keys per request (cached + new)
+  const int32_t* cu_q;       // [B + 1] query offsets (prefill only)
+  int B, hq, hk, d, page_size;
+  int max_q;                 // prefill: longest query segment (grid size)
+  float scale;
+  // split-KV scratch (decode): partial outputs and log-sum-exp values
+  float* part_o;             // [B, hq, max_splits, d]
+  float* part_lse;           // [B, hq, max_splits]
+  int max_splits;
+  int* err;
+};
+void launch_decode_attention(const AttnArgs& a, cudaStream_t s);
+void launch_prefill_attention(const AttnArgs& a, cudaStream_t s);
+
+// -------------------------------------------------------------- sampling ----
+// logits fp32 [B, V] (row stride ld); writes int32 token ids.
+void launch_argmax(int32_t* out, const float* logits, int B, int V, int ld, cudaStream_t s);
+struct SampleArgs {
+  int32_t* out;
+  const float* logits;       // [B, V] fp32
+  int ld, B, V;
+  const float* temperature;  // [B]
+  const int32_t* top_k;      // [B] or nullptr (<= 0 or >= V means disabled)
+  const float* top_p;        // [B] or nullptr
+  uint64_t seed;
+  const int64_t* step;       // device counter mixed into the random stream (may be nullptr)
+};
+void launch_sample(const SampleArgs& a, cudaStream_t s);
+
+// ------------------------------------------------------------------- MoE ----
+struct MoeRouteArgs {
+  const float* logits;       // [T, E] router logits (fp32)
+  const float* bias;         // [E] correction bias (sigmoid routing) or nullptr
+  float* topk_w;             // [T, k]
+  int32_t* topk_ids;         // [T, k]
+  int T, E, k;
+  int scoring;               // 0 softmax, 1 sigmoid
+  bool renormalize;
+  int n_group, topk_group;   // grouped routing (sigmoid); 1/1 disables
+  float routed_scale;
+};
+void launch_moe_route(const MoeRouteArgs& a, cudaStream_t s);
+
+}  // namespace minisgl

@@ -1,0 +1,197 @@
+// Token sampling over fp32 logits, one CTA per request row.
+//
+// Replaces torch.argmax and the flashinfer softmax / top-k / top-p sampling
+// calls of the reference sampler (python/minisgl/engine/sample.py:24-75).
+//
+// Method (exact sampling, no sort):
+//   * temperature only: Gumbel-max, argmax_i(l_i / T + G_i) with
+//     G_i = -log(-log(U_i)) is an exact draw from softmax(l / T)
+//     (Gumbel 1954; see Maddison et al., "A* Sampling", 2014). One pass.
+//   * top-k / top-p: the kept set is {i : l_i >= tau}. tau is found by a
+//     most-significant-digit radix select over the order-preserving uint32
+//     image of the fp32 logits (4 passes of 8 bits). For top-k the histogram
+//     counts elements; for top-p it accumulates exp((l - max) / T) mass and
+//     stops at the bucket where the mass from the top reaches p * Z. Gumbel-max
+//     restricted to the kept set then draws the token.
+// Random numbers: a counter-based generator, the SplitMix64 finaliser of
+// Steele, Lea and Flood ("Fast splittable pseudorandom number generators",
+// OOPSLA 2014) applied to (seed, step, row, column).
+#include <stdexcept>
+
+#include "common.cuh"
+#include "ops.h"
+
+namespace minisgl {
+namespace {
+
+constexpr int kThreads = 1024;
+
+__device__ __forceinline__ uint64_t mix64(uint64_t z) {
+  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
+  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
+  return z ^ (z >> 31);
+}
+
+// uniform in (0, 1)
+__device__ __forceinline__ float uniform(uint64_t seed, uint64_t step, int row, int col) {
+  const uint64_t key = mix64(seed ^ mix64(step * 0x9e3779b97f4a7c15ull + static_cast<uint64_t>(row)));
+  const uint64_t r = mix64(key + static_cast<uint64_t>(col) * 0x9e3779b97f4a7c15ull);
+  return (static_cast<float>(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+}
+
+// order-preserving map of fp32 to uint32 (larger float -> larger key)
+__device__ __forceinline__ uint32_t fkey(float f) {
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+struct ArgMax {
+  float v;
+  int i;
+};
+__device__ __forceinline__ ArgMax better(ArgMax a, ArgMax b) {
+  // larger value wins; ties -> smaller index (matches torch.argmax)
+  if (b.v > a.v || (b.v == a.v && b.i < a.i)) return b;
+  return a;
+}
+__device__ ArgMax block_argmax(ArgMax x) {
+  __shared__ float sv[32];
+  __shared__ int si[32];
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgMax y{__shfl_xor_sync(0xffffffffu, x.v, o), __shfl_xor_sync(0xffffffffu, x.i, o)};
+    x = better(x, y);
+  }
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) sv[warp] = x.v, si[warp] = x.i;
+  __syncthreads();
+  const int nw = blockDim.x >> 5;
+  x = lane < nw ? ArgMax{sv[lane], si[lane]} : ArgMax{-INFINITY, 0x7fffffff};
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    ArgMax y{__shfl_xor_sync(0xffffffffu, x.v, o), __shfl_xor_sync(0xffffffffu, x.i, o)};
+    x = better(x, y);
+  }
+  __syncthreads();
+  return x;
+}
+
+__device__ float block_reduce_sum(float v) {
+  __shared__ float s[32];
+  v = warp_sum(v);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (lane == 0) s[warp] = v;
+  __syncthreads();
+  v = lane < (blockDim.x >> 5) ? s[lane] : 0.f;
+  v = warp_sum(v);
+  __syncthreads();
+  return v;
+}
+
+__global__ void argmax_kernel(int32_t* out, const float* logits, int V, int ld) {
+  const float* row = logits + static_cast<int64_t>(blockIdx.x) * ld;
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{row[i], i});
+  best = block_argmax(best);
+  if (threadIdx.x == 0) out[blockIdx.x] = best.i == 0x7fffffff ? 0 : best.i;
+}
+
+// Radix select: find the largest key threshold `tau` such that the selected
+// statistic over {key >= tau} reaches `target` (count for top-k, mass for
+// top-p). Only elements with key >= floor_key take part.
+template <bool MASS>
+__device__ uint32_t radix_threshold(const float* row, int V, float target, uint32_t floor_key,
+                                    float mx, float inv_t) {
+  __shared__ float hist[256];
+  __shared__ uint32_t s_prefix;
+  __shared__ float s_above;
+  uint32_t prefix = 0;   // decided high bits
+  float above = 0.f;     // statistic of elements strictly above the current prefix range
+  for (int shift = 24; shift >= 0; shift -= 8) {
+    for (int i = threadIdx.x; i < 256; i += blockDim.x) hist[i] = 0.f;
+    __syncthreads();
+    const uint32_t hi_mask = shift == 24 ? 0u : (0xFFFFFFFFu << (shift + 8));
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float l = row[i];
+      const uint32_t k = fkey(l);
+      if (k < floor_key || (k & hi_mask) != prefix) continue;
+      const float w = MASS ? __expf((l - mx) * inv_t) : 1.f;
+      atomicAdd(&hist[(k >> shift) & 0xFFu], w);
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      float acc = above;
+      int bucket = 0;
+      for (int bkt = 255; bkt >= 0; --bkt) {
+        if (acc + hist[bkt] >= target) {
+          bucket = bkt;
+          break;
+        }
+        acc += hist[bkt];
+      }
+      s_prefix = prefix | (static_cast<uint32_t>(bucket) << shift);
+      s_above = acc;
+    }
+    __syncthreads();
+    prefix = s_prefix;
+    above = s_above;
+  }
+  return prefix;
+}
+
+__global__ void sample_kernel(SampleArgs a) {
+  const int r = blockIdx.x;
+  const float* row = a.logits + static_cast<int64_t>(r) * a.ld;
+  const int V = a.V;
+  const float T = fmaxf(a.temperature[r], 1e-6f);
+  const float inv_t = 1.f / T;
+  const uint64_t step = a.step != nullptr ? static_cast<uint64_t>(*a.step) : 0ull;
+  int top_k = a.top_k != nullptr ? a.top_k[r] : 0;
+  float top_p = a.top_p != nullptr ? a.top_p[r] : 1.f;
+  const bool use_k = top_k > 0 && top_k < V;
+  const bool use_p = top_p < 1.f;
+
+  uint32_t floor_key = 0;
+  if (use_k || use_p) {
+    ArgMax m{-INFINITY, 0};
+    for (int i = threadIdx.x; i < V; i += blockDim.x) m = better(m, ArgMax{row[i], i});
+    const float mx = block_argmax(m).v;
+    if (use_k) floor_key = radix_threshold<false>(row, V, static_cast<float>(top_k), 0u, mx, inv_t);
+    if (use_p) {
+      float z = 0.f;
+      for (int i = threadIdx.x; i < V; i += blockDim.x) {
+        const float l = row[i];
+        if (fkey(l) >= floor_key) z += __expf((l - mx) * inv_t);
+      }
+      z = block_reduce_sum(z);
+      floor_key = radix_threshold<true>(row, V, top_p * z, floor_key, mx, inv_t);
+    }
+  }
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int i = threadIdx.x; i < V; i += blockDim.x) {
+    const float l = row[i];
+    if (fkey(l) < floor_key) continue;
+    const float u = uniform(a.seed, step, r, i);
+    const float gumbel = -__logf(-__logf(u));
+    best = better(best, ArgMax{l * inv_t + gumbel, i});
+  }
+  best = block_argmax(best);
+  if (threadIdx.x == 0) a.out[r] = best.i == 0x7fffffff ? 0 : best.i;
+}
+
+__global__ void bump_step_kernel(int64_t* step) { *step += 1; }
+
+}  // namespace
+
+void launch_argmax(int32_t* out, const float* logits, int B, int V, int ld, cudaStream_t s) {
+  if (B <= 0) return;
+  argmax_kernel<<<B, kThreads, 0, s>>>(out, logits, V, ld);
+}
+
+void launch_sample(const SampleArgs& a, cudaStream_t s) {
+  if (a.B <= 0) return;
+  sample_kernel<<<a.B, kThreads, 0, s>>>(a);
+  if (a.step != nullptr) bump_step_kernel<<<1, 1, 0, s>>>(const_cast<int64_t*>(a.step));
+}
+
+}  // namespace minisgl

@@ -1,0 +1,34 @@
+"""Messages from the detokenizer back to the API server."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Dict, List
+
+from .utils import deserialize_type, serialize_type
+
+
+@dataclass
+class BaseFrontendMsg:
+    @staticmethod
+    def encoder(msg: "BaseFrontendMsg") -> Dict:
+        return serialize_type(msg)
+
+    @staticmethod
+    def decoder(data: Dict) -> "BaseFrontendMsg":
+        return deserialize_type(_CLASSES, data)
+
+
+@dataclass
+class BatchFrontendMsg(BaseFrontendMsg):
+    data: List[BaseFrontendMsg]
+
+
+@dataclass
+class UserReply(BaseFrontendMsg):
+    uid: int
+    incremental_output: str
+    finished: bool
+
+
+_CLASSES = {c.__name__: c for c in (BatchFrontendMsg, UserReply)}

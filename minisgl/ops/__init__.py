@@ -1,0 +1,324 @@
+"""Operator entry points used by the model layers.
+
+CUDA tensors always run the hand-written sm_100a kernels of ``minisgl._C``;
+if that library cannot be loaded on a GPU process the call raises instead of
+falling back. CPU tensors run the fp32 PyTorch restatement in
+``minisgl.ops.reference`` (the CPU oracle used by the CPU engine and tests).
+"""
+
+from __future__ import annotations
+
+import functools
+from typing import Optional, Tuple
+
+import torch
+
+from . import reference as ref
+
+_NATIVE = None
+_NATIVE_ERR: Optional[BaseException] = None
+
+
+def native():
+    """The loaded ``minisgl._C`` module; raises if it is unavailable."""
+    global _NATIVE, _NATIVE_ERR
+    if _NATIVE is None:
+        try:
+            from minisgl import _C  # type: ignore[attr-defined]
+
+            _NATIVE = _C
+        except BaseException as e:  # pragma: no cover - depends on the build
+            _NATIVE_ERR = e
+            raise RuntimeError(
+                "minisgl native library (minisgl/_C*.so) is not built or failed to load; "
+                "run `python setup.py build_ext --inplace`"
+            ) from e
+    return _NATIVE
+
+
+def native_available() -> bool:
+    try:
+        native()
+        return True
+    except RuntimeError:
+        return False
+
+
+# ------------------------------------------------------------------ scratch
+_WORKSPACE: dict = {}
+_ERR_WORDS: dict = {}
+GEMM_WORKSPACE_ELEMS = 8 * 1024 * 1024  # 32 MiB fp32: bounds every split-K plan
+
+
+def gemm_workspace(device: torch.device) -> torch.Tensor:
+    key = (device.type, device.index)
+    ws = _WORKSPACE.get(key)
+    if ws is None:
+        ws = torch.empty(GEMM_WORKSPACE_ELEMS, dtype=torch.float32, device=device)
+        _WORKSPACE[key] = ws
+    return ws
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    """Per-device int32[2]: (error code, site) written by kernels whose bounded
+    waits ran out. Zero means no error."""
+    key = (device.type, device.index)
+    w = _ERR_WORDS.get(key)
+    if w is None:
+        w = torch.zeros(2, dtype=torch.int32, device=device)
+        _ERR_WORDS[key] = w
+    return w
+
+
+def check_device_errors(device: torch.device) -> None:
+    w = _ERR_WORDS.get((device.type, device.index))
+    if w is None:
+        return
+    code, site = w.tolist()
+    if code != 0:
+        w.zero_()
+        raise RuntimeError(f"minisgl kernel reported error code {code} at site {site}")
+
+
+# ------------------------------------------------------------------- GEMM
+def gemm(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    bias: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    out_dtype: Optional[torch.dtype] = None,
+) -> torch.Tensor:
+    """out = x @ w^T (+ bias): the F.linear convention."""
+    out_dtype = out_dtype or (out.dtype if out is not None else x.dtype)
+    if not x.is_cuda:
+        y = ref.gemm(x, w, bias, out_dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(x.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
+    native().gemm(out, x, w, bias, gemm_workspace(x.device), 0, 0, error_word(x.device))
+    return out
+
+
+# ------------------------------------------------------------ elementwise
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not x.is_cuda:
+        y = ref.rmsnorm(x, w, eps)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty_like(x)
+    native().rmsnorm(out, x, w, eps)
+    return out
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+    if not x.is_cuda:
+        ref.fused_add_rmsnorm(x, residual, w, eps)
+        return
+    native().fused_add_rmsnorm(x, residual, w, eps)
+
+
+def silu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return _act_and_mul(x, "silu", out)
+
+
+def gelu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    return _act_and_mul(x, "gelu", out)
+
+
+def _act_and_mul(x: torch.Tensor, act: str, out: Optional[torch.Tensor]) -> torch.Tensor:
+    if not x.is_cuda:
+        y = ref.act_and_mul(x, act)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
+    native().act_and_mul(out, x, 0 if act == "silu" else 1)
+    return out
+
+
+def embedding(ids: torch.Tensor, weight: torch.Tensor, vocab_range: Optional[Tuple[int, int]] = None) -> torch.Tensor:
+    lo, n = vocab_range if vocab_range is not None else (0, weight.shape[0])
+    if not weight.is_cuda:
+        return ref.embedding(ids, weight, lo, n)
+    out = torch.empty(ids.numel(), weight.shape[1], dtype=weight.dtype, device=weight.device)
+    native().embedding(out, weight, ids.to(torch.int32), lo, n)
+    return out
+
+
+# ------------------------------------------------------- rope + KV store
+def rope_store(
+    qkv: torch.Tensor,
+    positions: torch.Tensor,
+    cos_sin: torch.Tensor,
+    q_norm_w: Optional[torch.Tensor],
+    k_norm_w: Optional[torch.Tensor],
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    out_loc: torch.Tensor,
+    hq: int,
+    hk: int,
+    d: int,
+    page_size: int,
+    eps: float,
+) -> None:
+    if not qkv.is_cuda:
+        ref.rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache, out_loc, hq, hk, d, page_size, eps)
+        return
+    native().rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache, out_loc, hq, hk, d, page_size, eps)
+
+
+# -------------------------------------------------------------- attention
+def decode_attention(
+    q: torch.Tensor,
+    kv_pool: torch.Tensor,
+    layer: int,
+    page_table: torch.Tensor,
+    req_rows: torch.Tensor,
+    seq_lens: torch.Tensor,
+    hq: int,
+    hk: int,
+    d: int,
+    page_size: int,
+    scale: float,
+    part_o: Optional[torch.Tensor] = None,
+    part_lse: Optional[torch.Tensor] = None,
+    max_splits: int = 1,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    """One query token per request; q is [B, >= hq*d] (row stride free)."""
+    B = req_rows.numel()
+    if not q.is_cuda:
+        cu = torch.arange(B + 1, dtype=torch.int32)
+        qv = q[:, : hq * d].reshape(B, hq, d)
+        y = ref.attention(qv, kv_pool, layer, page_table, req_rows, seq_lens, cu, hq, hk, d, page_size, scale)
+        y = y.view(B, hq * d)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(B, hq * d, dtype=q.dtype, device=q.device)
+    native().decode_attention(
+        q, out, kv_pool, layer, page_table, req_rows, seq_lens, hq, hk, d, page_size, scale,
+        part_o, part_lse, max_splits, error_word(q.device),
+    )
+    return out
+
+
+def prefill_attention(
+    q: torch.Tensor,
+    kv_pool: torch.Tensor,
+    layer: int,
+    page_table: torch.Tensor,
+    req_rows: torch.Tensor,
+    seq_lens: torch.Tensor,
+    cu_q: torch.Tensor,
+    max_q: int,
+    hq: int,
+    hk: int,
+    d: int,
+    page_size: int,
+    scale: float,
+    out: Optional[torch.Tensor] = None,
+) -> torch.Tensor:
+    T = q.shape[0]
+    if not q.is_cuda:
+        qv = q[:, : hq * d].reshape(T, hq, d)
+        y = ref.attention(qv, kv_pool, layer, page_table, req_rows, seq_lens, cu_q, hq, hk, d, page_size, scale)
+        y = y.view(T, hq * d)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(T, hq * d, dtype=q.dtype, device=q.device)
+    native().prefill_attention(
+        q, out, kv_pool, layer, page_table, req_rows, seq_lens, cu_q, max_q, hq, hk, d, page_size, scale,
+        error_word(q.device),
+    )
+    return out
+
+
+# --------------------------------------------------------------- sampling
+def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if not logits.is_cuda:
+        y = ref.argmax(logits)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    native().argmax(out, logits.float() if logits.dtype != torch.float32 else logits)
+    return out
+
+
+def sample(
+    logits: torch.Tensor,
+    temperature: torch.Tensor,
+    top_k: Optional[torch.Tensor] = None,
+    top_p: Optional[torch.Tensor] = None,
+    seed: int = 0,
+    step: Optional[torch.Tensor] = None,
+    out: Optional[torch.Tensor] = None,
+    generator: Optional[torch.Generator] = None,
+) -> torch.Tensor:
+    if not logits.is_cuda:
+        y = ref.sample(logits, temperature, top_k, top_p, generator)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    lf = logits if logits.dtype == torch.float32 else logits.float()
+    native().sample(out, lf, temperature, top_k, top_p, seed, step)
+    return out
+
+
+# -------------------------------------------------------------------- MoE
+def moe_route(
+    logits: torch.Tensor,
+    k: int,
+    scoring: str = "softmax",
+    renormalize: bool = True,
+    bias: Optional[torch.Tensor] = None,
+    n_group: int = 1,
+    topk_group: int = 1,
+    routed_scale: float = 1.0,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    if not logits.is_cuda:
+        return ref.moe_route(logits, k, scoring, renormalize, bias, n_group, topk_group, routed_scale)
+    T = logits.shape[0]
+    w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
+    ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    native().moe_route(
+        logits.float().contiguous(), None if bias is None else bias.float(), w, ids,
+        0 if scoring == "softmax" else 1, renormalize, n_group, topk_group, routed_scale,
+    )
+    return w, ids
+
+
+# ------------------------------------------------------------ host helpers
+@functools.lru_cache(maxsize=1)
+def _host_compare():
+    try:
+        return native().fast_compare_key
+    except RuntimeError:
+        return None
+
+
+def fast_compare_key(a: torch.Tensor, b: torch.Tensor) -> int:
+    """Length of the common prefix of two 1-D CPU integer tensors."""
+    fn = _host_compare()
+    if fn is not None:
+        return int(fn(a, b))
+    return ref.fast_compare_key(a, b)

@@ -1,0 +1,214 @@
+"""Plain-PyTorch restatement of every native op (fp32 math).
+
+This is the CPU oracle: the CPU engine path runs on it, and the GPU kernel
+tests compare the sm_100a kernels against it. Semantics (layouts, rounding
+points, masking) match the CUDA kernels in ``minisgl/csrc``.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional, Tuple
+
+import torch
+
+
+def gemm(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], out_dtype: torch.dtype) -> torch.Tensor:
+    y = x.float() @ w.float().t()
+    if bias is not None:
+        y = y + bias.float()
+    return y.to(out_dtype)
+
+
+def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
+    return (xf * inv * w.float()).to(x.dtype)
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+    s = (x.float() + residual.float()).to(x.dtype)
+    residual.copy_(s)
+    x.copy_(rmsnorm(s, w, eps))
+
+
+def act_and_mul(x: torch.Tensor, act: str) -> torch.Tensor:
+    d = x.shape[-1] // 2
+    g, u = x[..., :d].float(), x[..., d:].float()
+    if act == "silu":
+        a = g / (1.0 + torch.exp(-g))
+    elif act == "gelu":
+        a = 0.5 * g * (1.0 + torch.erf(g / math.sqrt(2.0)))
+    else:
+        raise ValueError(f"unsupported activation {act}")
+    return (a * u).to(x.dtype)
+
+
+def embedding(ids: torch.Tensor, weight: torch.Tensor, lo: int, n: int) -> torch.Tensor:
+    local = ids.long() - lo
+    inside = (local >= 0) & (local < n)
+    out = weight[local.clamp(0, max(n - 1, 0))]
+    return torch.where(inside.unsqueeze(-1), out, torch.zeros_like(out))
+
+
+def rope_store(
+    qkv: torch.Tensor,
+    positions: torch.Tensor,
+    cos_sin: torch.Tensor,
+    q_norm_w: Optional[torch.Tensor],
+    k_norm_w: Optional[torch.Tensor],
+    k_cache: torch.Tensor,
+    v_cache: torch.Tensor,
+    out_loc: torch.Tensor,
+    hq: int,
+    hk: int,
+    d: int,
+    page_size: int,
+    eps: float,
+) -> None:
+    """q/k per-head RMSNorm + NeoX RoPE in place in ``qkv``; k/v stored to the
+    paged cache (per-layer layout [pages, hk, page_size, d])."""
+    T = qkv.shape[0]
+    dt = qkv.dtype
+    q = qkv[:, : hq * d].view(T, hq, d)
+    k = qkv[:, hq * d : (hq + hk) * d].view(T, hk, d)
+    v = qkv[:, (hq + hk) * d : (hq + 2 * hk) * d].view(T, hk, d)
+
+    def norm_rope(x: torch.Tensor, w: Optional[torch.Tensor]) -> torch.Tensor:
+        xf = x.float()
+        if w is not None:
+            xf = (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps) * w.float()).to(dt).float()
+        cs = cos_sin[positions.long()]  # [T, d]
+        h = d // 2
+        cos, sin = cs[:, None, :h], cs[:, None, h:]
+        x1, x2 = xf[..., :h], xf[..., h:]
+        return torch.cat([x1 * cos - x2 * sin, x2 * cos + x1 * sin], dim=-1).to(dt)
+
+    q.copy_(norm_rope(q, q_norm_w))
+    k.copy_(norm_rope(k, k_norm_w))
+    loc = out_loc.long()
+    page, off = loc // page_size, loc % page_size
+    k_cache[page, :, off] = k
+    v_cache[page, :, off] = v
+
+
+def gather_kv(
+    kv_pool: torch.Tensor, layer: int, page_table: torch.Tensor, row: int, length: int, page_size: int
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Keys/values [length, hk, d] of one request from the paged pool."""
+    slots = page_table[row, :length].long()
+    page, off = slots // page_size, slots % page_size
+    k = kv_pool[0, layer][page, :, off]
+    v = kv_pool[1, layer][page, :, off]
+    return k, v
+
+
+def attention(
+    q: torch.Tensor,  # [T, hq, d]
+    kv_pool: torch.Tensor,
+    layer: int,
+    page_table: torch.Tensor,
+    req_rows: torch.Tensor,
+    seq_lens: torch.Tensor,
+    cu_q: torch.Tensor,
+    hq: int,
+    hk: int,
+    d: int,
+    page_size: int,
+    scale: float,
+) -> torch.Tensor:
+    """Causal paged attention: query i of request b sits at position
+    seq_len_b - q_len_b + i and sees keys [0, position]."""
+    out = torch.zeros(q.shape[0], hq, d, dtype=q.dtype, device=q.device)
+    G = hq // hk
+    rows = req_rows.tolist()
+    lens = seq_lens.tolist()
+    cu = cu_q.tolist()
+    for b, (row, L) in enumerate(zip(rows, lens)):
+        s, e = cu[b], cu[b + 1]
+        n = e - s
+        if n == 0 or L <= 0:
+            continue
+        k, v = gather_kv(kv_pool, layer, page_table, row, L, page_size)
+        qb = q[s:e].float()  # [n, hq, d]
+        kf = k.float().repeat_interleave(G, dim=1)  # [L, hq, d]
+        vf = v.float().repeat_interleave(G, dim=1)
+        scores = torch.einsum("nhd,lhd->hnl", qb, kf) * scale
+        qpos = torch.arange(L - n, L, device=q.device)
+        kpos = torch.arange(L, device=q.device)
+        mask = kpos[None, :] > qpos[:, None]
+        scores = scores.masked_fill(mask[None], float("-inf"))
+        p = torch.softmax(scores, dim=-1)
+        out[s:e] = torch.einsum("hnl,lhd->nhd", p, vf).to(q.dtype)
+    return out
+
+
+def argmax(logits: torch.Tensor) -> torch.Tensor:
+    return torch.argmax(logits.float(), dim=-1).to(torch.int32)
+
+
+def sample(
+    logits: torch.Tensor,
+    temperature: torch.Tensor,
+    top_k: Optional[torch.Tensor],
+    top_p: Optional[torch.Tensor],
+    generator: Optional[torch.Generator] = None,
+) -> torch.Tensor:
+    """Multinomial draw from softmax(logits / T) restricted to top-k / top-p."""
+    lf = logits.float() / temperature.float().clamp_min(1e-6)[:, None]
+    B, V = lf.shape
+    keep = torch.ones_like(lf, dtype=torch.bool)
+    if top_k is not None:
+        k = top_k.long().clamp(1, V)
+        kth = torch.sort(lf, dim=-1, descending=True).values.gather(1, (k - 1)[:, None])
+        use = (top_k > 0) & (top_k < V)
+        keep &= ~use[:, None] | (lf >= kth)
+    if top_p is not None:
+        masked = lf.masked_fill(~keep, float("-inf"))
+        probs = torch.softmax(masked, dim=-1)
+        sp, idx = torch.sort(probs, dim=-1, descending=True)
+        cum = sp.cumsum(-1)
+        # keep the smallest prefix whose mass reaches p
+        drop_sorted = (cum - sp) >= top_p.float()[:, None]
+        drop = torch.zeros_like(drop_sorted).scatter(1, idx, drop_sorted)
+        keep &= ~drop
+    probs = torch.softmax(lf.masked_fill(~keep, float("-inf")), dim=-1)
+    return torch.multinomial(probs, 1, generator=generator).view(-1).to(torch.int32)
+
+
+def moe_route(
+    logits: torch.Tensor,
+    k: int,
+    scoring: str,
+    renormalize: bool,
+    bias: Optional[torch.Tensor] = None,
+    n_group: int = 1,
+    topk_group: int = 1,
+    routed_scale: float = 1.0,
+) -> Tuple[torch.Tensor, torch.Tensor]:
+    lf = logits.float()
+    if scoring == "softmax":
+        scores = torch.softmax(lf, dim=-1)
+        choice = scores
+    else:
+        scores = torch.sigmoid(lf)
+        choice = scores + (bias.float() if bias is not None else 0.0)
+        if n_group > 1 and topk_group < n_group:
+            T, E = choice.shape
+            g = choice.view(T, n_group, E // n_group)
+            gs = g.topk(2, dim=-1).values.sum(-1)
+            keep = torch.zeros_like(gs, dtype=torch.bool).scatter(1, gs.topk(topk_group, dim=-1).indices, True)
+            choice = g.masked_fill(~keep[..., None], float("-inf")).view(T, E)
+    ids = choice.topk(k, dim=-1).indices
+    w = scores.gather(1, ids)
+    if renormalize:
+        w = w / (w.sum(-1, keepdim=True) + 1e-20)
+    return (w * routed_scale).float(), ids.to(torch.int32)
+
+
+def fast_compare_key(a: torch.Tensor, b: torch.Tensor) -> int:
+    n = min(len(a), len(b))
+    if n == 0:
+        return 0
+    diff = (a[:n].long() != b[:n].long()).nonzero()
+    return int(diff[0, 0]) if len(diff) > 0 else n

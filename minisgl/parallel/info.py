@@ -1,0 +1,45 @@
+"""Which tensor-parallel rank this process is (set once per process)."""
+
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import Optional
+
+
+@dataclass(frozen=True)
+class DistributedInfo:
+    rank: int
+    size: int
+
+    def __post_init__(self) -> None:
+        if not 0 <= self.rank < self.size:
+            raise ValueError(f"rank {self.rank} outside world of {self.size}")
+
+    def is_primary(self) -> bool:
+        return self.rank == 0
+
+
+_TP: Optional[DistributedInfo] = None
+
+
+def set_tp_info(rank: int, size: int) -> None:
+    global _TP
+    if _TP is not None:
+        raise RuntimeError("TP info is already set for this process")
+    _TP = DistributedInfo(rank, size)
+
+
+def get_tp_info() -> DistributedInfo:
+    if _TP is None:
+        raise RuntimeError("TP info has not been set")
+    return _TP
+
+
+def try_get_tp_info() -> Optional[DistributedInfo]:
+    return _TP
+
+
+def reset_tp_info() -> None:
+    """Forget the rank (tests and in-process engine restarts)."""
+    global _TP
+    _TP = None

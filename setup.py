@@ -1,0 +1,63 @@
+"""Build script for the minisgl native library (sm_100a only).
+
+    python setup.py build_ext --inplace
+
+produces ``minisgl/_C*.so`` next to the Python sources, so the built library
+travels with a copy of the source tree.
+"""
+
+import os
+
+from setuptools import setup
+
+NVCC_FLAGS = [
+    "-O3",
+    "-std=c++17",
+    "-lineinfo",
+    "-gencode=arch=compute_100a,code=sm_100a",
+    "--expt-relaxed-constexpr",
+    "-Xptxas=-v" if os.environ.get("MINISGL_PTXAS_VERBOSE") else "-Xptxas=-O3",
+    "-DNDEBUG",
+]
+CXX_FLAGS = ["-O3", "-std=c++17", "-DNDEBUG"]
+
+SOURCES = [
+    "minisgl/csrc/binding.cpp",
+    "minisgl/csrc/radix.cpp",
+    "minisgl/csrc/gemm.cu",
+    "minisgl/csrc/attention.cu",
+    "minisgl/csrc/elementwise.cu",
+    "minisgl/csrc/rope_store.cu",
+    "minisgl/csrc/sampling.cu",
+    "minisgl/csrc/moe.cu",
+]
+
+
+def ext_modules():
+    from torch.utils.cpp_extension import CUDAExtension
+
+    return [
+        CUDAExtension(
+            name="minisgl._C",
+            sources=SOURCES,
+            extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+        )
+    ]
+
+
+def cmdclass():
+    from torch.utils.cpp_extension import BuildExtension
+
+    return {"build_ext": BuildExtension.with_options(use_ninja=True)}
+
+
+if __name__ == "__main__":
+    # torch's own arch list must not add other targets: the gencode above is the only one
+    os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    setup(
+        name="minisgl",
+        version="0.1.0",
+        packages=[],
+        ext_modules=ext_modules(),
+        cmdclass=cmdclass(),
+    )
