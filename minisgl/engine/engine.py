@@ -1,0 +1,242 @@
+"""The per-rank engine: model, KV pool, page table, backends, sampler and
+CUDA graphs on one device.
+
+Construction order and memory budgeting follow the reference
+(python/minisgl/engine/engine.py:29-189): the model is built on the meta
+device and then receives real weights; the KV pool takes
+``memory_ratio * free_before_load - model_bytes``; ranks agree on the
+minimum free memory. B200 specifics: the KV layout is page-major per head
+(TMA friendly), pages must be a power of two of at least 16 tokens, and the
+default page is 64 tokens.
+"""
+
+from __future__ import annotations
+
+import os
+from datetime import timedelta
+from typing import Dict, NamedTuple, Optional, Tuple
+
+import torch
+
+from minisgl.attention import create_attention_backend
+from minisgl.core import Batch, Context, Req, reset_global_ctx, set_global_ctx
+from minisgl.kvcache import create_kvcache_pool
+from minisgl.layers import set_rope_device
+from minisgl.models import create_model, load_weight, random_weights
+from minisgl.moe import create_moe_backend
+from minisgl.parallel import destroy_distributed, get_tp_info, reset_tp_info, set_tp_info
+from minisgl.utils import align_ceil, init_logger, torch_dtype
+
+from .config import EngineConfig
+from .graph import GraphRunner, get_free_memory, mem_GB
+from .sample import BatchSamplingArgs, Sampler
+
+logger = init_logger(__name__)
+
+
+class ForwardOutput(NamedTuple):
+    next_tokens_gpu: torch.Tensor
+    next_tokens_cpu: torch.Tensor
+    copy_done_event: "torch.cuda.Event | _Done"
+
+
+class _Done:
+    """Stand-in for a CUDA event on the CPU path."""
+
+    def synchronize(self) -> None:
+        return None
+
+    def query(self) -> bool:
+        return True
+
+
+def _resolve_device(config: EngineConfig) -> torch.device:
+    if config.device == "cpu":
+        return torch.device("cpu")
+    if config.device.startswith("cuda:"):
+        return torch.device(config.device)
+    local = int(os.environ.get("MINISGL_DEVICE_OFFSET", "0"))
+    return torch.device(f"cuda:{local + config.tp_info.rank}")
+
+
+def _valid_page(p: int) -> bool:
+    return p >= 16 and (p & (p - 1)) == 0
+
+
+class Engine:
+    def __init__(self, config: EngineConfig) -> None:
+        set_tp_info(config.tp_info.rank, config.tp_info.size)
+        self.config = config
+        self.device = _resolve_device(config)
+        self.is_cuda = self.device.type == "cuda"
+        if self.is_cuda:
+            torch.cuda.set_device(self.device)
+            self.stream: Optional[torch.cuda.Stream] = torch.cuda.Stream(self.device)
+            torch.cuda.set_stream(self.stream)
+        else:
+            self.stream = None
+        torch.manual_seed(42)
+        self.dtype = config.dtype
+        page_size = config.page_size
+        if self.is_cuda and not _valid_page(page_size):
+            logger.warning_rank0(f"page size {page_size} is not supported by the sm_100a kernels; using 64")
+            page_size = 64
+        self.page_size = page_size
+        self.ctx = Context(page_size)
+        set_global_ctx(self.ctx)
+
+        self.tp_cpu_group = self._init_communication(config)
+        init_free = self._sync_get_memory()[1] if self.is_cuda else 0
+        if self.is_cuda:
+            logger.info_rank0(f"Free memory before loading model: {mem_GB(init_free)}")
+
+        # ------------------------------------------------------------- model
+        mcfg = config.model_config
+        self.model_config = mcfg
+        set_rope_device(self.device)
+        with torch.device("meta"), torch_dtype(config.dtype):
+            self.model = create_model(mcfg)
+        self.model.load_state_dict(self._load_weights(config))
+
+        # ---------------------------------------------------------- KV cache
+        self.num_pages = self._determine_num_pages(init_free, config)
+        num_tokens = self.num_pages * page_size
+        self.ctx.kv_cache = self.kv_cache = create_kvcache_pool(
+            mcfg, self.num_pages + 1, page_size, self.dtype, self.device)  # +1: the dummy page
+        self.max_seq_len = min(config.max_seq_len, num_tokens)
+        width = align_ceil(self.max_seq_len + page_size, max(64, page_size))
+        self.ctx.page_table = self.page_table = torch.zeros(
+            (config.max_running_req + 1, width), dtype=torch.int32, device=self.device)
+
+        # ---------------------------------------------------------- backends
+        self.ctx.attn_backend = self.attn_backend = create_attention_backend(
+            config.attention_backend, mcfg, config.max_running_req + 1)
+        if mcfg.is_moe:
+            self.ctx.moe_backend = self.moe_backend = create_moe_backend(config.moe_backend)
+        self.sampler = Sampler(self.device, mcfg.vocab_size, config.weight_seed)
+        if self.is_cuda:
+            from minisgl import ops
+
+            ops.gemm_workspace(self.device)
+            ops.error_word(self.device)
+            logger.info_rank0(f"Free memory after initialization: {mem_GB(self._sync_get_memory()[0])}")
+
+        # ------------------------------------------------------ CUDA graphs
+        self.dummy_req = Req(input_ids=torch.tensor([0], dtype=torch.int32), table_idx=config.max_running_req,
+                             cached_len=0, output_len=1, uid=-1, sampling_params=None,  # type: ignore[arg-type]
+                             cache_handle=None)  # type: ignore[arg-type]
+        self.page_table[self.dummy_req.table_idx].fill_(num_tokens)  # -> the spare page
+        self.graph_runner = GraphRunner(
+            self.stream, self.device, self.model, self.attn_backend, config.cuda_graph_bs,
+            self._graph_max_bs(config), init_free, width, mcfg.vocab_size, self.dummy_req)
+
+    # ---------------------------------------------------------------- setup
+    def _graph_max_bs(self, config: EngineConfig) -> Optional[int]:
+        if not self.is_cuda:
+            return 0
+        mx = config.cuda_graph_max_bs
+        if mx is None:
+            return min(config.max_running_req, 256)
+        return min(mx, config.max_running_req)
+
+    def _init_communication(self, config: EngineConfig):
+        import torch.distributed as dist
+
+        size = config.tp_info.size
+        if size == 1:
+            return None
+        if dist.is_initialized():
+            return dist.group.WORLD
+        backend = "cpu:gloo,cuda:nccl" if self.is_cuda else "gloo"
+        dist.init_process_group(backend=backend, rank=config.tp_info.rank, world_size=size,
+                                timeout=timedelta(seconds=config.distributed_timeout),
+                                init_method=config.distributed_addr,
+                                device_id=self.device if self.is_cuda else None)
+        self._owns_pg = True
+        if self.is_cuda and config.comm == "fused":
+            from minisgl.parallel.symm import enable_symm_comm
+
+            enable_symm_comm(self.device, config.max_forward_len * config.model_config.hidden_size
+                             * self.dtype.itemsize)
+        return dist.group.WORLD
+
+    def _load_weights(self, config: EngineConfig) -> Dict[str, torch.Tensor]:
+        if config.use_dummy_weight:
+            return random_weights(self.model.state_dict(), self.device, seed=config.weight_seed,
+                                  gen_device=config.dummy_weight_device)
+        out: Dict[str, torch.Tensor] = {}
+        for name, t in load_weight(config.model_path, self.device, ep_size=config.ep_size,
+                                   ep_rank=config.tp_info.rank if config.ep_size > 1 else 0):
+            keep_fp32 = t.dtype == torch.float32 and "correction_bias" in name
+            out[name] = t if keep_fp32 else t.to(self.dtype)
+        return out
+
+    def _determine_num_pages(self, init_free: int, config: EngineConfig) -> int:
+        mcfg = config.model_config
+        per_page = self._bytes_per_page()
+        if config.num_page_override is not None:
+            pages = config.num_page_override
+        elif self.is_cuda:
+            model_bytes = init_free - self._sync_get_memory()[1]
+            pages = int(config.memory_ratio * init_free - model_bytes) // per_page
+        else:
+            pages = (config.max_running_req * min(config.max_seq_len, 4096)) // self.page_size
+        if pages <= 1:
+            raise RuntimeError("not enough memory for the KV cache; lower --num-pages or the model size")
+        logger.info_rank0(f"KV cache: {pages * self.page_size} tokens in {pages} pages of {self.page_size} "
+                          f"({mem_GB(pages * per_page)}), model {mcfg.architectures[0]}")
+        return pages
+
+    def _bytes_per_page(self) -> int:
+        m = self.model_config
+        itemsize = self.dtype.itemsize
+        if m.is_mla:
+            return m.num_layers * self.page_size * (m.kv_lora_rank + m.qk_rope_head_dim) * itemsize
+        from minisgl.utils import div_even
+
+        kv = div_even(m.num_kv_heads, get_tp_info().size, allow_replicate=True)
+        return 2 * m.num_layers * kv * self.page_size * m.head_dim * itemsize
+
+    def _sync_get_memory(self) -> Tuple[int, int]:
+        """(min, max) free device memory over the TP ranks."""
+        torch.cuda.synchronize(self.device)
+        torch.cuda.empty_cache()
+        free = get_free_memory(self.device)
+        if self.tp_cpu_group is None:
+            return free, free
+        import torch.distributed as dist
+
+        t = torch.tensor([free, -free], dtype=torch.int64)
+        dist.all_reduce(t, op=dist.ReduceOp.MIN, group=self.tp_cpu_group)
+        lo, hi = int(t[0]), -int(t[1])
+        if hi - lo > (2 << 30):
+            raise RuntimeError(f"free memory differs across TP ranks: {mem_GB(lo)} vs {mem_GB(hi)}")
+        return lo, hi
+
+    # -------------------------------------------------------------- forward
+    def forward_batch(self, batch: Batch, args: BatchSamplingArgs) -> ForwardOutput:
+        with self.ctx.forward_batch(batch):
+            if self.graph_runner.can_use_cuda_graph(batch):
+                logits = self.graph_runner.replay(batch)
+            else:
+                logits = self.model.forward()
+        for r in batch.reqs:
+            r.complete_one()
+        next_gpu = self.sampler.sample(logits[: batch.size], args)
+        if not self.is_cuda:
+            return ForwardOutput(next_gpu, next_gpu, _Done())
+        next_cpu = torch.empty(next_gpu.shape, dtype=next_gpu.dtype, pin_memory=True)
+        next_cpu.copy_(next_gpu, non_blocking=True)
+        event = torch.cuda.Event()
+        event.record(self.stream)
+        return ForwardOutput(next_gpu, next_cpu, event)
+
+    def shutdown(self) -> None:
+        self.graph_runner.destroy_cuda_graphs()
+        import torch.distributed as dist
+
+        destroy_distributed()
+        if getattr(self, "_owns_pg", False) and dist.is_initialized():
+            dist.destroy_process_group()
+        reset_global_ctx()
+        reset_tp_info()

@@ -1,0 +1,124 @@
+"""CUDA-graph capture and replay of decode steps.
+
+One graph per padded batch size (1, 2, 4, then multiples of 8 up to the
+maximum), captured largest first into a shared memory pool. A graph reads
+its inputs from static buffers (token ids, positions, KV write slots and the
+attention metadata) and writes fp32 logits to a static buffer; replay copies
+the batch's tensors into those buffers on the engine stream. Batches are
+padded with a dummy request whose page-table row points at a spare page.
+The batch-size list and its memory-based default follow the reference
+(python/minisgl/engine/graph.py:47-64, 152-166).
+"""
+
+from __future__ import annotations
+
+import gc
+from typing import TYPE_CHECKING, Dict, List, Optional
+
+import torch
+
+from minisgl import ops
+from minisgl.core import Batch, Req, get_global_ctx
+from minisgl.utils import init_logger
+
+if TYPE_CHECKING:
+    from minisgl.attention import BaseAttnBackend
+    from minisgl.models import BaseLLMModel
+
+logger = init_logger(__name__)
+
+
+def mem_GB(n: int) -> str:
+    return f"{n / (1 << 30):.2f} GiB"
+
+
+def get_free_memory(device: torch.device) -> int:
+    return torch.cuda.mem_get_info(device)[0]
+
+
+def determine_cuda_graph_bs(bs: Optional[List[int]], max_bs: Optional[int], free_memory: int) -> List[int]:
+    if bs is not None:
+        return sorted(set(bs))
+    if max_bs is None:
+        max_bs = 256 if free_memory > (80 << 30) else 160
+    if max_bs < 1:
+        return []
+    return sorted({b for b in [1, 2, 4] + list(range(8, max_bs + 1, 8)) if b <= max_bs} | {max_bs})
+
+
+class GraphRunner:
+    def __init__(self, stream: Optional[torch.cuda.Stream], device: torch.device, model: "BaseLLMModel",
+                 attn_backend: "BaseAttnBackend", cuda_graph_bs: Optional[List[int]],
+                 cuda_graph_max_bs: Optional[int], free_memory: int, max_seq_len: int, vocab_size: int,
+                 dummy_req: Req) -> None:
+        self.stream = stream
+        self.device = device
+        self.attn_backend = attn_backend
+        self.dummy_req = dummy_req
+        self.graph_map: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.graph_launches: Dict[int, int] = {}  # native kernels inside each graph
+        bs_list = determine_cuda_graph_bs(cuda_graph_bs, cuda_graph_max_bs, free_memory) if device.type == "cuda" else []
+        self.graph_bs_list = bs_list
+        self.max_graph_bs = max(bs_list) if bs_list else 0
+        if self.max_graph_bs > 0:
+            self._capture(model, max_seq_len, vocab_size)
+        else:
+            logger.info_rank0("CUDA graph is disabled.")
+
+    def _capture(self, model: "BaseLLMModel", max_seq_len: int, vocab_size: int) -> None:
+        n = self.max_graph_bs
+        self.input_ids = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self.positions = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self.out_loc = torch.zeros(n, dtype=torch.int32, device=self.device)
+        self.logits = torch.empty(n, vocab_size, dtype=torch.float32, device=self.device)
+        self.attn_backend.init_capture_graph(max_seq_len, self.graph_bs_list)
+        torch.cuda.synchronize(self.device)
+        logger.info_rank0(f"Capturing CUDA graphs for batch sizes {self.graph_bs_list}; "
+                          f"free memory {mem_GB(get_free_memory(self.device))}")
+        ctx = get_global_ctx()
+        pool = None
+        for bs in sorted(self.graph_bs_list, reverse=True):
+            batch = Batch(reqs=[self.dummy_req] * bs, phase="decode")
+            batch.padded_reqs = batch.reqs
+            batch.input_ids = self.input_ids[:bs]
+            batch.positions = self.positions[:bs]
+            batch.out_loc = self.out_loc[:bs]
+            self.attn_backend.prepare_for_capture(batch)
+            graph = torch.cuda.CUDAGraph()
+            with ctx.forward_batch(batch):
+                self.logits[:bs] = model.forward()  # warm-up outside the capture
+                before = ops.LAUNCHES[0]
+                with torch.cuda.graph(graph, pool=pool, stream=self.stream):
+                    self.logits[:bs] = model.forward()
+                self.graph_launches[bs] = ops.LAUNCHES[0] - before
+                ops.LAUNCHES[0] = before
+            if pool is None:
+                pool = graph.pool()
+            self.graph_map[bs] = graph
+        torch.cuda.synchronize(self.device)
+        logger.info_rank0(f"CUDA graphs ready; free memory {mem_GB(get_free_memory(self.device))}")
+
+    def can_use_cuda_graph(self, batch: Batch) -> bool:
+        return batch.is_decode and batch.size <= self.max_graph_bs
+
+    def pad_batch(self, batch: Batch) -> None:
+        size = batch.size
+        if self.can_use_cuda_graph(batch):
+            size = next(b for b in self.graph_bs_list if b >= batch.size)
+        batch.padded_reqs = batch.reqs + [self.dummy_req] * (size - batch.size)
+
+    def replay(self, batch: Batch) -> torch.Tensor:
+        bs = batch.padded_size
+        self.input_ids[:bs].copy_(batch.input_ids)
+        self.positions[:bs].copy_(batch.positions)
+        self.out_loc[:bs].copy_(batch.out_loc)
+        self.attn_backend.prepare_for_replay(batch)
+        self.graph_map[bs].replay()
+        ops.LAUNCHES[0] += self.graph_launches[bs]
+        return self.logits[: batch.size]
+
+    def destroy_cuda_graphs(self) -> None:
+        """Release graphs first: graphs holding collectives must go before
+        the communicators they captured."""
+        self.graph_map.clear()
+        gc.collect()

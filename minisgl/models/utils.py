@@ -1,0 +1,78 @@
+"""Building blocks shared by the decoder families."""
+
+from __future__ import annotations
+
+from typing import TYPE_CHECKING
+
+from minisgl.layers import (
+    AttentionLayer,
+    BaseOP,
+    LinearColParallelMerged,
+    LinearOProj,
+    LinearQKVMerged,
+    LinearReplicated,
+    LinearRowParallel,
+    MoELayer,
+    RMSNorm,
+    gelu_and_mul,
+    silu_and_mul,
+)
+from minisgl.utils import nvtx_annotate
+
+if TYPE_CHECKING:
+    import torch
+
+    from .config import ModelConfig
+
+_ACT = {"silu": silu_and_mul, "gelu": gelu_and_mul, "gelu_pytorch_tanh": gelu_and_mul}
+
+
+class GatedMLP(BaseOP):
+    """down(act(gate(x)) * up(x)) with gate|up fused into one GEMM."""
+
+    def __init__(self, config: "ModelConfig", intermediate_size: int | None = None) -> None:
+        inter = intermediate_size or config.intermediate_size
+        self.gate_up_proj = LinearColParallelMerged(config.hidden_size, [inter, inter], has_bias=False)
+        if config.hidden_act not in _ACT:
+            raise ValueError(f"unsupported activation {config.hidden_act}")
+        self._act = _ACT[config.hidden_act]
+        self.down_proj = LinearRowParallel(inter, config.hidden_size, has_bias=False)
+
+    @nvtx_annotate("MLP")
+    def forward(self, x: "torch.Tensor") -> "torch.Tensor":
+        h = self.gate_up_proj.forward(x)
+        return self.down_proj.forward(self._act(h))
+
+
+class MoEMLP(BaseOP):
+    """Replicated router + routed experts (Qwen3-MoE style)."""
+
+    def __init__(self, config: "ModelConfig") -> None:
+        self.experts = MoELayer(config.num_experts, config.num_experts_per_tok, config.hidden_size,
+                                config.moe_intermediate_size, renormalize=config.norm_topk_prob)
+        self.gate = LinearReplicated(config.hidden_size, config.num_experts, has_bias=False)
+
+    @nvtx_annotate("MoE")
+    def forward(self, x: "torch.Tensor") -> "torch.Tensor":
+        return self.experts.forward(x, self.gate.forward(x))
+
+
+class RopeAttn(BaseOP):
+    """qkv projection -> fused norm/RoPE/KV-store + paged attention -> o_proj."""
+
+    def __init__(self, config: "ModelConfig", layer_id: int, *, has_attn_bias: bool = False,
+                 has_qk_norm: bool = False) -> None:
+        d = config.head_dim
+        self.qkv_proj = LinearQKVMerged(config.hidden_size, d, config.num_qo_heads, config.num_kv_heads, has_attn_bias)
+        self.q_norm = RMSNorm(d, config.rms_norm_eps) if has_qk_norm else None
+        self.k_norm = RMSNorm(d, config.rms_norm_eps) if has_qk_norm else None
+        self.attn = AttentionLayer(layer_id, config.num_qo_heads, config.num_kv_heads, d, config.rotary_config,
+                                   self.q_norm, self.k_norm, eps=config.rms_norm_eps)
+        self.o_proj = LinearOProj(d * config.num_qo_heads, config.hidden_size, has_bias=False)
+
+    @nvtx_annotate("MHA")
+    def forward(self, x: "torch.Tensor") -> "torch.Tensor":
+        return self.o_proj.forward(self.attn.forward(self.qkv_proj.forward(x)))
+
+
+__all__ = ["GatedMLP", "MoEMLP", "RopeAttn"]

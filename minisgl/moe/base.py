@@ -1,0 +1,15 @@
+from __future__ import annotations
+
+from abc import ABC, abstractmethod
+from typing import Optional
+
+import torch
+
+
+class BaseMoeBackend(ABC):
+    @abstractmethod
+    def forward(self, hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, gating_output: torch.Tensor,
+                topk: int, renormalize: bool, activation: str = "silu", scoring: str = "softmax",
+                correction_bias: Optional[torch.Tensor] = None, n_group: int = 1, topk_group: int = 1,
+                routed_scale: float = 1.0) -> torch.Tensor:
+        """sum_k w[t, k] * down_e(act(gate_up_e(x_t))) for the k routed experts."""

@@ -18,6 +18,14 @@ from . import reference as ref
 _NATIVE = None
 _NATIVE_ERR: Optional[BaseException] = None
 
+# Host-side count of native kernel launches issued through this module
+# (CUDA-graph replays are added by the graph runner). Benchmarks report it.
+LAUNCHES = [0]
+
+
+def _count(n: int = 1) -> None:
+    LAUNCHES[0] += n
+
 
 def native():
     """The loaded ``minisgl._C`` module; raises if it is unavailable."""
@@ -81,6 +89,18 @@ def check_device_errors(device: torch.device) -> None:
 
 
 # ------------------------------------------------------------------- GEMM
+_GEMM_KERNELS: dict = {}
+
+
+def _gemm_kernels(M: int, N: int, K: int) -> int:
+    """1, or 2 when the split-K plan adds its reduction kernel."""
+    key = (M, N, K)
+    n = _GEMM_KERNELS.get(key)
+    if n is None:
+        n = 2 if native().gemm_workspace_elems(M, N, K) > 0 else 1
+        _GEMM_KERNELS[key] = n
+    return n
+
 def gemm(
     x: torch.Tensor,
     w: torch.Tensor,
@@ -98,6 +118,7 @@ def gemm(
         return y
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
+    _count(_gemm_kernels(x.shape[0], w.shape[0], x.shape[1]))
     native().gemm(out, x, w, bias, gemm_workspace(x.device), 0, 0, error_word(x.device))
     return out
 
@@ -112,6 +133,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Te
         return y
     if out is None:
         out = torch.empty_like(x)
+    _count()
     native().rmsnorm(out, x, w, eps)
     return out
 
@@ -120,6 +142,7 @@ def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, 
     if not x.is_cuda:
         ref.fused_add_rmsnorm(x, residual, w, eps)
         return
+    _count()
     native().fused_add_rmsnorm(x, residual, w, eps)
 
 
@@ -140,6 +163,7 @@ def _act_and_mul(x: torch.Tensor, act: str, out: Optional[torch.Tensor]) -> torc
         return y
     if out is None:
         out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
+    _count()
     native().act_and_mul(out, x, 0 if act == "silu" else 1)
     return out
 
@@ -149,6 +173,7 @@ def embedding(ids: torch.Tensor, weight: torch.Tensor, vocab_range: Optional[Tup
     if not weight.is_cuda:
         return ref.embedding(ids, weight, lo, n)
     out = torch.empty(ids.numel(), weight.shape[1], dtype=weight.dtype, device=weight.device)
+    _count()
     native().embedding(out, weight, ids.to(torch.int32), lo, n)
     return out
 
@@ -172,6 +197,7 @@ def rope_store(
     if not qkv.is_cuda:
         ref.rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache, out_loc, hq, hk, d, page_size, eps)
         return
+    _count()
     native().rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache, out_loc, hq, hk, d, page_size, eps)
 
 
@@ -206,6 +232,7 @@ def decode_attention(
         return y
     if out is None:
         out = torch.empty(B, hq * d, dtype=q.dtype, device=q.device)
+    _count(2 if max_splits > 1 else 1)
     native().decode_attention(
         q, out, kv_pool, layer, page_table, req_rows, seq_lens, hq, hk, d, page_size, scale,
         part_o, part_lse, max_splits, error_word(q.device),
@@ -240,6 +267,7 @@ def prefill_attention(
         return y
     if out is None:
         out = torch.empty(T, hq * d, dtype=q.dtype, device=q.device)
+    _count()
     native().prefill_attention(
         q, out, kv_pool, layer, page_table, req_rows, seq_lens, cu_q, max_q, hq, hk, d, page_size, scale,
         error_word(q.device),
@@ -257,6 +285,7 @@ def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
         return y
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _count()
     native().argmax(out, logits.float() if logits.dtype != torch.float32 else logits)
     return out
 
@@ -280,6 +309,7 @@ def sample(
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
     lf = logits if logits.dtype == torch.float32 else logits.float()
+    _count(2 if step is not None else 1)
     native().sample(out, lf, temperature, top_k, top_p, seed, step)
     return out
 
@@ -300,6 +330,7 @@ def moe_route(
     T = logits.shape[0]
     w = torch.empty(T, k, dtype=torch.float32, device=logits.device)
     ids = torch.empty(T, k, dtype=torch.int32, device=logits.device)
+    _count()
     native().moe_route(
         logits.float().contiguous(), None if bias is None else bias.float(), w, ids,
         0 if scoring == "softmax" else 1, renormalize, n_group, topk_group, routed_scale,

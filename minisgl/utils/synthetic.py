@@ -1,0 +1,138 @@
+"""Synthetic model folders for benchmarks and tests (no network needed).
+
+``make_model_dir("qwen3-0.6b")`` writes a Hugging Face style folder with a
+``config.json`` of the named shape and a word-level tokenizer covering the
+whole vocabulary (token ``i`` is the word ``t{i}``). Engines started on it
+with ``use_dummy_weight=True`` (``--dummy-weight``) draw random weights, so
+the shapes, kernels and scheduling are real while no checkpoint is read.
+"""
+
+from __future__ import annotations
+
+import copy
+import hashlib
+import json
+import os
+import shutil
+import tempfile
+from typing import Any, Dict, Optional
+
+_QWEN3_BASE: Dict[str, Any] = {
+    "model_type": "qwen3",
+    "architectures": ["Qwen3ForCausalLM"],
+    "hidden_act": "silu",
+    "rms_norm_eps": 1e-6,
+    "rope_theta": 1000000.0,
+    "max_position_embeddings": 40960,
+    "torch_dtype": "bfloat16",
+    "bos_token_id": 0,
+    "eos_token_id": 1,
+    "attention_bias": False,
+}
+
+SHAPES: Dict[str, Dict[str, Any]] = {
+    # tiny Qwen3-style decoder (CPU, fp32)
+    "tiny-qwen3": dict(_QWEN3_BASE, num_hidden_layers=2, hidden_size=256, num_attention_heads=4,
+                       num_key_value_heads=2, head_dim=64, intermediate_size=512, vocab_size=1024,
+                       tie_word_embeddings=True, max_position_embeddings=4096, torch_dtype="float32"),
+    # BASELINE config 2
+    "qwen3-0.6b": dict(_QWEN3_BASE, num_hidden_layers=28, hidden_size=1024, num_attention_heads=16,
+                       num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=151936,
+                       tie_word_embeddings=True),
+    # small GPU smoke / numerics shape (head_dim 128 like the real models)
+    "small-qwen3": dict(_QWEN3_BASE, num_hidden_layers=2, hidden_size=1024, num_attention_heads=16,
+                        num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=4096,
+                        tie_word_embeddings=False, max_position_embeddings=8192),
+    # BASELINE config 3
+    "qwen3-32b": dict(_QWEN3_BASE, num_hidden_layers=64, hidden_size=5120, num_attention_heads=64,
+                      num_key_value_heads=8, head_dim=128, intermediate_size=25600, vocab_size=151936,
+                      tie_word_embeddings=False),
+    "qwen3-8b": dict(_QWEN3_BASE, num_hidden_layers=36, hidden_size=4096, num_attention_heads=32,
+                     num_key_value_heads=8, head_dim=128, intermediate_size=12288, vocab_size=151936,
+                     tie_word_embeddings=False),
+    "qwen3-30b-a3b": dict(_QWEN3_BASE, model_type="qwen3_moe", architectures=["Qwen3MoeForCausalLM"],
+                          num_hidden_layers=48, hidden_size=2048, num_attention_heads=32, num_key_value_heads=4,
+                          head_dim=128, intermediate_size=6144, moe_intermediate_size=768, num_experts=128,
+                          num_experts_per_tok=8, norm_topk_prob=True, vocab_size=151936,
+                          tie_word_embeddings=False),
+    "tiny-qwen3-moe": dict(_QWEN3_BASE, model_type="qwen3_moe", architectures=["Qwen3MoeForCausalLM"],
+                           num_hidden_layers=2, hidden_size=256, num_attention_heads=4, num_key_value_heads=2,
+                           head_dim=64, intermediate_size=512, moe_intermediate_size=128, num_experts=8,
+                           num_experts_per_tok=2, norm_topk_prob=True, vocab_size=1024,
+                           tie_word_embeddings=False, max_position_embeddings=4096, torch_dtype="float32"),
+    "tiny-llama": {
+        "model_type": "llama", "architectures": ["LlamaForCausalLM"], "hidden_act": "silu", "rms_norm_eps": 1e-5,
+        "rope_theta": 500000.0, "max_position_embeddings": 4096, "num_hidden_layers": 2, "hidden_size": 256,
+        "num_attention_heads": 4, "num_key_value_heads": 2, "intermediate_size": 512, "vocab_size": 1024,
+        "tie_word_embeddings": False, "torch_dtype": "float32", "bos_token_id": 0, "eos_token_id": 1,
+        "rope_scaling": {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
+                         "original_max_position_embeddings": 1024},
+    },
+    # BASELINE config 4 / 5: Kimi-K2 shape (DeepSeek-V3 architecture)
+    "kimi-k2": {
+        "model_type": "kimi_k2", "architectures": ["DeepseekV3ForCausalLM"], "hidden_act": "silu",
+        "rms_norm_eps": 1e-6, "rope_theta": 50000.0, "max_position_embeddings": 262144,
+        "num_hidden_layers": 61, "hidden_size": 7168, "num_attention_heads": 64, "num_key_value_heads": 64,
+        "intermediate_size": 18432, "moe_intermediate_size": 2048, "n_routed_experts": 384, "n_shared_experts": 1,
+        "num_experts_per_tok": 8, "first_k_dense_replace": 1, "n_group": 1, "topk_group": 1,
+        "norm_topk_prob": True, "routed_scaling_factor": 2.827, "scoring_func": "sigmoid",
+        "q_lora_rank": 1536, "kv_lora_rank": 512, "qk_nope_head_dim": 128, "qk_rope_head_dim": 64,
+        "v_head_dim": 128, "vocab_size": 163840, "tie_word_embeddings": False, "torch_dtype": "bfloat16",
+        "bos_token_id": 0, "eos_token_id": 1,
+        "rope_scaling": {"type": "yarn", "factor": 32.0, "beta_fast": 1.0, "beta_slow": 1.0, "mscale": 1.0,
+                         "mscale_all_dim": 1.0, "original_max_position_embeddings": 4096},
+    },
+}
+SHAPES["tiny-kimi"] = dict(copy.deepcopy(SHAPES["kimi-k2"]), num_hidden_layers=2, hidden_size=256,
+                           num_attention_heads=4, num_key_value_heads=4, intermediate_size=512,
+                           moe_intermediate_size=128, n_routed_experts=8, num_experts_per_tok=2,
+                           q_lora_rank=96, kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16,
+                           v_head_dim=32, vocab_size=1024, torch_dtype="float32", max_position_embeddings=4096)
+
+_CHAT_TEMPLATE = (
+    "{% for m in messages %}<|{{ m['role'] }}|>{{ m['content'] }}<|end|>{% endfor %}"
+    "{% if add_generation_prompt %}<|assistant|>{% endif %}"
+)
+
+
+def _write_tokenizer(folder: str, vocab_size: int) -> None:
+    from tokenizers import Tokenizer, models, pre_tokenizers
+    from transformers import PreTrainedTokenizerFast
+
+    vocab = {f"t{i}": i for i in range(vocab_size)}
+    tok = Tokenizer(models.WordLevel(vocab=vocab, unk_token="t2"))
+    tok.pre_tokenizer = pre_tokenizers.WhitespaceSplit()
+    fast = PreTrainedTokenizerFast(tokenizer_object=tok, bos_token="t0", eos_token="t1", unk_token="t2",
+                                   pad_token="t3")
+    fast.chat_template = _CHAT_TEMPLATE
+    fast.save_pretrained(folder)
+
+
+def make_model_dir(shape: str, folder: Optional[str] = None, overrides: Optional[Dict[str, Any]] = None) -> str:
+    """Create (or reuse) a synthetic model folder of a named shape."""
+    if shape not in SHAPES:
+        raise KeyError(f"unknown synthetic shape {shape!r}; have {sorted(SHAPES)}")
+    cfg = dict(copy.deepcopy(SHAPES[shape]), **(overrides or {}))
+    if folder is None:
+        key = hashlib.sha1(json.dumps(cfg, sort_keys=True).encode()).hexdigest()[:12]
+        folder = os.path.join(tempfile.gettempdir(), f"minisgl_synthetic_{shape}_{key}")
+    if os.path.isfile(os.path.join(folder, "config.json")):
+        return folder
+    # build in a private folder, then publish it with one rename (several
+    # ranks may race to create the same folder)
+    parent = os.path.dirname(os.path.abspath(folder))
+    os.makedirs(parent, exist_ok=True)
+    tmp = tempfile.mkdtemp(prefix=".tmp_minisgl_", dir=parent)
+    _write_tokenizer(tmp, cfg["vocab_size"])
+    with open(os.path.join(tmp, "config.json"), "w") as f:
+        json.dump(cfg, f, indent=1)
+    try:
+        os.rename(tmp, folder)
+    except OSError:  # another process won the race (or the folder exists)
+        shutil.rmtree(tmp, ignore_errors=True)
+        if not os.path.isfile(os.path.join(folder, "config.json")):
+            os.makedirs(folder, exist_ok=True)
+            _write_tokenizer(folder, cfg["vocab_size"])
+            with open(os.path.join(folder, "config.json"), "w") as f:
+                json.dump(cfg, f, indent=1)
+    return folder
