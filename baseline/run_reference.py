@@ -48,7 +48,8 @@ def main() -> None:
 
     import minisgl  # the reference package from baseline/_ref
 
-    assert os.path.abspath(minisgl.__file__).startswith(REF), minisgl.__file__
+    where = os.path.abspath(list(minisgl.__path__)[0])
+    assert where.startswith(REF), where
     import minisgl.engine.config as ref_cfg
     import torch
     from minisgl.core import SamplingParams

@@ -1,0 +1,157 @@
+"""Per-kernel timings at serving shapes, with roofline fractions.
+
+    python -m minisgl.benchmark.kernels [--shape qwen3-0.6b] [--json out.json]
+
+Denominators are the measured B200 peaks in MEASURED_PEAKS.json when present
+(STREAM-style copy bandwidth and cuBLAS bf16 GEMM throughput), else the
+fallback figures 6650 GB/s and 1590 TFLOP/s. Each line reports the kernel's
+time (CUDA events, L2 flushed between calls), its algorithmic bytes / FLOPs
+and the achieved fraction of the relevant peak. cuBLAS (torch.matmul) is
+timed on the same GEMM shapes as a baseline.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import random
+from typing import Dict, List
+
+import torch
+
+from minisgl import ops
+
+from .perf import time_kernel
+
+
+def _peaks() -> Dict[str, float]:
+    root = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    path = os.path.join(root, "MEASURED_PEAKS.json")
+    if os.path.isfile(path):
+        with open(path) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "tflops": d["bf16_tflops"], "source": "measured"}
+    return {"hbm_gbs": 6650.0, "tflops": 1590.0, "source": "fallback"}
+
+
+def _pool(lens: List[int], hk: int, d: int, page: int, layers: int = 1):
+    pages_per = [(L + page - 1) // page for L in lens]
+    num_pages = sum(pages_per) + 1
+    pool = torch.randn(2, layers, num_pages, hk, page, d, device="cuda", dtype=torch.bfloat16) * 0.5
+    width = (max(lens) + page + 63) // 64 * 64
+    pt = torch.zeros(len(lens), width, dtype=torch.int32)
+    perm = torch.randperm(num_pages - 1).tolist()
+    for b, L in enumerate(lens):
+        pages = [perm.pop() for _ in range(pages_per[b])]
+        pos = torch.arange(L)
+        pt[b, :L] = torch.tensor(pages)[pos // page] * page + pos % page
+    return pool, pt.cuda(), torch.arange(len(lens), dtype=torch.int32, device="cuda")
+
+
+def bench_decode_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) -> Dict:
+    d = 128
+    lens = [L] * B
+    pool, pt, rows = _pool(lens, hk, d, page)
+    seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, hq * d, device="cuda", dtype=torch.bfloat16)
+    from minisgl.attention.native import MAX_SPLITS, decode_splits
+
+    splits = decode_splits(B, hk)
+    part_o = torch.empty(B * hq * MAX_SPLITS * d, device="cuda")
+    part_lse = torch.empty(B * hq * MAX_SPLITS, device="cuda")
+    ms = time_kernel(lambda: ops.decode_attention(q, pool, 0, pt, rows, seq, hq, hk, d, page, d ** -0.5,
+                                                  part_o, part_lse, splits))
+    nbytes = 2 * B * L * hk * d * 2
+    gbs = nbytes / ms / 1e6
+    return {"kernel": "decode_attention", "B": B, "L": L, "hq": hq, "hk": hk, "page": page, "splits": splits,
+            "ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
+
+
+def bench_prefill_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) -> Dict:
+    d = 128
+    lens = [L] * B
+    pool, pt, rows = _pool(lens, hk, d, page)
+    seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device="cuda")
+    q = torch.randn(B * L, hq * d, device="cuda", dtype=torch.bfloat16)
+    ms = time_kernel(lambda: ops.prefill_attention(q, pool, 0, pt, rows, seq, cu, L, hq, hk, d, page, d ** -0.5),
+                     iters=5)
+    flops = 4 * B * hq * d * L * (L + 1) / 2
+    tf = flops / ms / 1e9
+    return {"kernel": "prefill_attention", "B": B, "L": L, "hq": hq, "hk": hk, "ms": round(ms, 4),
+            "TFLOP/s": round(tf, 1), "frac_tensor": round(tf / peaks["tflops"], 3)}
+
+
+def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    ms = time_kernel(lambda: ops.gemm(x, w, out=out))
+    ms_cublas = time_kernel(lambda: torch.matmul(x, w.t(), out=out))
+    flops = 2 * M * N * K
+    nbytes = 2 * (M * K + N * K + M * N)
+    tf, gbs = flops / ms / 1e9, nbytes / ms / 1e6
+    bound = max(flops / (peaks["tflops"] * 1e9), nbytes / (peaks["hbm_gbs"] * 1e6))  # roofline ms
+    return {"kernel": f"gemm[{label}]", "M": M, "N": N, "K": K, "ms": round(ms, 4), "cublas_ms": round(ms_cublas, 4),
+            "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "frac_roofline": round(bound / ms, 3)}
+
+
+def bench_elementwise(peaks) -> List[Dict]:
+    out = []
+    T, H = 16384, 1024
+    x = torch.randn(T, H, device="cuda", dtype=torch.bfloat16)
+    r = torch.randn_like(x)
+    w = torch.ones(H, device="cuda", dtype=torch.bfloat16)
+    ms = time_kernel(lambda: ops.fused_add_rmsnorm(x, r, w, 1e-6))
+    gbs = 4 * T * H * 2 / ms / 1e6
+    out.append({"kernel": "fused_add_rmsnorm", "T": T, "H": H, "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)})
+    gu = torch.randn(T, 2 * 3072, device="cuda", dtype=torch.bfloat16)
+    ms = time_kernel(lambda: ops.silu_and_mul(gu))
+    gbs = 3 * T * 3072 * 2 / ms / 1e6
+    out.append({"kernel": "silu_and_mul", "T": T, "I": 3072, "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)})
+    logits = torch.randn(256, 151936, device="cuda")
+    t = torch.full((256,), 0.6, device="cuda")
+    ms = time_kernel(lambda: ops.sample(logits, t))
+    gbs = logits.numel() * 4 / ms / 1e6
+    out.append({"kernel": "sample(temperature)", "B": 256, "V": 151936, "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)})
+    return out
+
+
+def main() -> None:
+    p = argparse.ArgumentParser()
+    p.add_argument("--json", default="")
+    p.add_argument("--quick", action="store_true")
+    args = p.parse_args()
+    peaks = _peaks()
+    random.seed(0)
+    torch.manual_seed(0)
+    rows: List[Dict] = []
+    for B, L in [(256, 800), (128, 800), (32, 2000), (1, 4000)]:
+        rows.append(bench_decode_attention(B, L, 16, 8, 64, peaks))
+    rows.append(bench_decode_attention(64, 2000, 64, 8, 64, peaks))  # Qwen3-32B (GQA 8)
+    rows.append(bench_decode_attention(64, 2000, 8, 1, 64, peaks))   # Qwen3-32B TP8
+    rows.append(bench_prefill_attention(16, 1024, 16, 8, 64, peaks))
+    H, I, V = 1024, 3072, 151936
+    for M in (1, 64, 256):
+        rows.append(bench_gemm(M, 4096, H, peaks, f"qkv M={M}"))
+        rows.append(bench_gemm(M, H, 2048, peaks, f"o M={M}"))
+        rows.append(bench_gemm(M, 2 * I, H, peaks, f"gate_up M={M}"))
+        rows.append(bench_gemm(M, H, I, peaks, f"down M={M}"))
+    rows.append(bench_gemm(256, V, H, peaks, "lm_head M=256"))
+    rows.append(bench_gemm(16384, 2 * I, H, peaks, "gate_up prefill"))
+    rows.append(bench_gemm(8192, 8192, 8192, peaks, "square 8192"))
+    rows.extend(bench_elementwise(peaks))
+    for r in rows:
+        r["peaks"] = peaks["source"]
+        print(json.dumps(r), flush=True)
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(rows, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()

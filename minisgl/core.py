@@ -54,6 +54,7 @@ class Req:
 
     def __post_init__(self) -> None:
         assert self.input_ids.device.type == "cpu"
+        self._appended: List[int] = []  # sampled tokens not yet folded into input_ids
         self.device_len = len(self.input_ids)
         self.max_device_len = len(self.input_ids) + self.output_len
         assert 0 <= self.cached_len < self.device_len <= self.max_device_len, self
@@ -76,8 +77,21 @@ class Req:
         self.cached_len = self.device_len
         self.device_len += 1
 
-    def append_host(self, next_token: torch.Tensor) -> None:
-        self.input_ids = torch.cat([self.input_ids, next_token])
+    def append_host(self, next_token) -> None:
+        """Record a sampled token on the host (an int or a 1-element tensor).
+        Appends are buffered in a list; ``all_ids`` folds them in."""
+        if isinstance(next_token, torch.Tensor):
+            self._appended.extend(int(t) for t in next_token.reshape(-1).tolist())
+        else:
+            self._appended.append(int(next_token))
+
+    def all_ids(self) -> torch.Tensor:
+        """Every host-known token of the request (prompt + sampled)."""
+        if self._appended:
+            extra = torch.tensor(self._appended, dtype=self.input_ids.dtype)
+            self.input_ids = torch.cat([self.input_ids, extra])
+            self._appended = []
+        return self.input_ids
 
     def __repr__(self) -> str:
         return (f"{type(self).__name__}(uid={self.uid}, table_idx={self.table_idx}, cached_len={self.cached_len}, "

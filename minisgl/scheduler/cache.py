@@ -71,7 +71,7 @@ class CacheManager:
         """Insert the request's computed prefix into the prefix cache and
         release slots that became duplicates; on finish also release the
         tail that could not be cached (partial last page)."""
-        ids = req.input_ids[: req.cached_len]
+        ids = req.all_ids()[: req.cached_len]
         slots = self.page_table[req.table_idx, : req.cached_len]
         old = req.cache_handle
         already, new = self.prefix_cache.insert_prefix(ids, slots)

@@ -14,6 +14,7 @@ shipped in ONE pinned host buffer / one asynchronous copy per step.
 
 from __future__ import annotations
 
+import os
 import time
 from typing import TYPE_CHECKING, List, NamedTuple, Optional, Set, Tuple
 
@@ -81,6 +82,11 @@ class Scheduler(SchedulerIOMixin):
         self.h2d_bytes = 0
         self.d2h_bytes = 0
         self._stats_t = time.perf_counter()
+        self.profiler = None
+        if self.is_cuda and os.environ.get("MINISGL_PROFILE_STEPS", "0") == "1":
+            from .profile import StepProfiler
+
+            self.profiler = StepProfiler()
         super().__init__(config, self.engine.tp_cpu_group)
 
     # --------------------------------------------------------------- loops
@@ -147,7 +153,7 @@ class Scheduler(SchedulerIOMixin):
                 if isinstance(req, ChunkedReq):
                     continue
                 tok = tokens[i]
-                req.append_host(torch.tensor([tok], dtype=torch.int32))
+                req.append_host(tok)
                 done = not req.can_decode
                 if not req.sampling_params.ignore_eos and tok == self.eos_token_id:
                     done = True
@@ -228,8 +234,11 @@ class Scheduler(SchedulerIOMixin):
 
     def _forward(self, fin: ForwardInput) -> "ForwardOutput":
         batch = fin.batch
+        prof = self.profiler.begin() if self.profiler is not None else None
         batch.input_ids = self.token_pool[fin.input_tuple]
         out = self.engine.forward_batch(batch, fin.sample_args)
+        if prof is not None:
+            self.profiler.end(batch.phase, batch.size, prof)
         self.token_pool[fin.write_tuple] = out.next_tokens_gpu
         self.decode_manager.filter_reqs(batch.reqs)
         self.step_count += 1
