@@ -22,7 +22,7 @@ import torch
 
 from minisgl import ops
 
-from .perf import time_kernel
+from .perf import time_graph, time_kernel
 
 
 def _peaks() -> Dict[str, float]:
@@ -89,11 +89,14 @@ def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     ms = time_kernel(lambda: ops.gemm(x, w, out=out))
     ms_cublas = time_kernel(lambda: torch.matmul(x, w.t(), out=out))
+    ms_graph = time_graph(lambda: ops.gemm(x, w, out=out), iters=50)
+    ms_cublas_graph = time_graph(lambda: torch.matmul(x, w.t(), out=out), iters=50)
     flops = 2 * M * N * K
     nbytes = 2 * (M * K + N * K + M * N)
     tf, gbs = flops / ms / 1e9, nbytes / ms / 1e6
     bound = max(flops / (peaks["tflops"] * 1e9), nbytes / (peaks["hbm_gbs"] * 1e6))  # roofline ms
     return {"kernel": f"gemm[{label}]", "M": M, "N": N, "K": K, "ms": round(ms, 4), "cublas_ms": round(ms_cublas, 4),
+            "graph_ms": round(ms_graph, 4), "cublas_graph_ms": round(ms_cublas_graph, 4),
             "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "frac_roofline": round(bound / ms, 3)}
 
 
@@ -125,26 +128,32 @@ def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--json", default="")
     p.add_argument("--quick", action="store_true")
+    p.add_argument("--only", default="", help="run only cases whose label contains this text")
     args = p.parse_args()
     peaks = _peaks()
     random.seed(0)
     torch.manual_seed(0)
-    rows: List[Dict] = []
+    cases = []
     for B, L in [(256, 800), (128, 800), (32, 2000), (1, 4000)]:
-        rows.append(bench_decode_attention(B, L, 16, 8, 64, peaks))
-    rows.append(bench_decode_attention(64, 2000, 64, 8, 64, peaks))  # Qwen3-32B (GQA 8)
-    rows.append(bench_decode_attention(64, 2000, 8, 1, 64, peaks))   # Qwen3-32B TP8
-    rows.append(bench_prefill_attention(16, 1024, 16, 8, 64, peaks))
+        cases.append((f"decode_attention B={B} L={L}", lambda B=B, L=L: bench_decode_attention(B, L, 16, 8, 64, peaks)))
+    cases.append(("decode_attention qwen3-32b", lambda: bench_decode_attention(64, 2000, 64, 8, 64, peaks)))
+    cases.append(("decode_attention qwen3-32b tp8", lambda: bench_decode_attention(64, 2000, 8, 1, 64, peaks)))
+    cases.append(("prefill_attention", lambda: bench_prefill_attention(16, 1024, 16, 8, 64, peaks)))
     H, I, V = 1024, 3072, 151936
     for M in (1, 64, 256):
-        rows.append(bench_gemm(M, 4096, H, peaks, f"qkv M={M}"))
-        rows.append(bench_gemm(M, H, 2048, peaks, f"o M={M}"))
-        rows.append(bench_gemm(M, 2 * I, H, peaks, f"gate_up M={M}"))
-        rows.append(bench_gemm(M, H, I, peaks, f"down M={M}"))
-    rows.append(bench_gemm(256, V, H, peaks, "lm_head M=256"))
-    rows.append(bench_gemm(16384, 2 * I, H, peaks, "gate_up prefill"))
-    rows.append(bench_gemm(8192, 8192, 8192, peaks, "square 8192"))
-    rows.extend(bench_elementwise(peaks))
+        for lab, N, K in (("qkv", 4096, H), ("o", H, 2048), ("gate_up", 2 * I, H), ("down", H, I)):
+            name = f"{lab} M={M}"
+            cases.append((f"gemm[{name}]", lambda M=M, N=N, K=K, name=name: bench_gemm(M, N, K, peaks, name)))
+    cases.append(("gemm[lm_head M=256]", lambda: bench_gemm(256, V, H, peaks, "lm_head M=256")))
+    cases.append(("gemm[gate_up prefill]", lambda: bench_gemm(16384, 2 * I, H, peaks, "gate_up prefill")))
+    cases.append(("gemm[square 8192]", lambda: bench_gemm(8192, 8192, 8192, peaks, "square 8192")))
+    cases.append(("elementwise", lambda: bench_elementwise(peaks)))
+    rows: List[Dict] = []
+    for label, fn in cases:
+        if args.only and args.only not in label:
+            continue
+        r = fn()
+        rows.extend(r if isinstance(r, list) else [r])
     for r in rows:
         r["peaks"] = peaks["source"]
         print(json.dumps(r), flush=True)

@@ -16,15 +16,19 @@
 //               and store.
 //
 // Two tile orientations:
-//   token-major   (A = x, B = w): rows of the tile are tokens. Used when M is
-//                 large (prefill).
+//   token-major   (A = x, B = w): rows of the tile are tokens (prefill).
 //   weight-major  (A = w, B = x): rows are output features and the token
-//                 count becomes the MMA N dimension (16..256). Used for small
-//                 M (decode) so the 128-row MMA is filled by weights rather
-//                 than by padding rows.
-// Split-K spreads the K loop over gridDim.z CTAs when there are too few tiles
-// to cover the 148 SMs; partial sums go to an fp32 workspace and a small
-// reduction kernel finishes the tile (bias, conversion).
+//                 count becomes the MMA N dimension (16..128). Used for small
+//                 M (decode) so the 128-row MMA is filled by weights.
+//
+// Decode GEMMs are latency bound, so two launch-level features matter:
+//   * programmatic dependent launch: the kernel lets its successor start
+//     early, and its own producer streams the first weight stages before
+//     griddepcontrol.wait (weights never depend on the previous kernel);
+//   * split-K inside a thread-block cluster: the S CTAs that share an output
+//     tile (cluster dims 1x1xS) each reduce a K range, park their fp32 tile
+//     in shared memory and sum the S tiles through distributed shared memory
+//     (mapa + ld.shared::cluster). No global workspace, no second kernel.
 #include <algorithm>
 #include <stdexcept>
 #include <string>
@@ -42,7 +46,6 @@ constexpr int kThreads = 192;
 
 struct KParams {
   void* out;
-  float* ws;
   const __nv_bfloat16* bias;
   int M, N;            // logical output is out[M, N] (M = tokens, N = features)
   int ldo;
@@ -56,7 +59,11 @@ template <int BN, int STAGES>
 struct Smem {
   static constexpr uint32_t kA = BM * BK * 2;
   static constexpr uint32_t kB = BN * BK * 2;
-  static constexpr uint32_t kBytes = STAGES * (kA + kB) + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t kPipe = STAGES * (kA + kB);
+  // split-K reduction tile: 128 rows x BN fp32, rows padded by 4 floats
+  static constexpr uint32_t kRed = BM * (BN + 4) * 4;
+  static constexpr uint32_t kMain = kPipe > kRed ? kPipe : kRed;
+  static constexpr uint32_t kBytes = kMain + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 template <int N>
@@ -64,7 +71,15 @@ struct TmemCols {
   static constexpr uint32_t value = N <= 32 ? 32 : (N <= 64 ? 64 : (N <= 128 ? 128 : 256));
 };
 
-// SWAP = weight-major tiles; SPLIT = write fp32 partials to the workspace.
+__device__ __forceinline__ void store_out(const KParams& p, int m, int n, float v) {
+  if (p.out_f32) {
+    reinterpret_cast<float*>(p.out)[static_cast<size_t>(m) * p.ldo + n] = v;
+  } else {
+    reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(m) * p.ldo + n] = __float2bfloat16_rn(v);
+  }
+}
+
+// SWAP = weight-major tiles; SPLIT = cluster split-K (gridDim.z CTAs per tile).
 template <int BN, int STAGES, bool SWAP, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -75,7 +90,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sA = smem;
   uint8_t* sB = smem + STAGES * S::kA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(sB + STAGES * S::kB);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kMain);
   uint64_t* empty = full + STAGES;
   uint64_t* done = empty + STAGES;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
@@ -87,8 +102,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int b_row0 = blockIdx.x * BN;
   const int kb0 = blockIdx.z * p.kb_per_split;
   const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
-  const int nkb = kb1 - kb0;
+  const int nkb = max(0, kb1 - kb0);
 
+  pdl_launch_dependents();
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -110,14 +126,30 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      for (int i = 0; i < nkb; ++i) {
+      // weights first: they do not depend on the previous kernel
+      const CUtensorMap* tw = SWAP ? &tmA : &tmB;
+      const CUtensorMap* tx = SWAP ? &tmB : &tmA;
+      const int w_row = SWAP ? a_row0 : b_row0;
+      const int x_row = SWAP ? b_row0 : a_row0;
+      uint8_t* sW = SWAP ? sA : sB;
+      uint8_t* sX = SWAP ? sB : sA;
+      constexpr uint32_t kW = SWAP ? S::kA : S::kB;
+      constexpr uint32_t kX = SWAP ? S::kB : S::kA;
+      const int pre = min(nkb, STAGES);
+      for (int i = 0; i < pre; ++i) {
+        mbar_arrive_expect_tx(&full[i], S::kA + S::kB);
+        tma_load_2d(sW + i * kW, tw, &full[i], (kb0 + i) * BK, w_row);
+      }
+      pdl_wait();
+      for (int i = 0; i < pre; ++i) tma_load_2d(sX + i * kX, tx, &full[i], (kb0 + i) * BK, x_row);
+      for (int i = pre; i < nkb; ++i) {
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 101)) break;
         mbar_arrive_expect_tx(&full[s], S::kA + S::kB);
         const int kc = (kb0 + i) * BK;
-        tma_load_2d(sA + s * S::kA, &tmA, &full[s], kc, a_row0);
-        tma_load_2d(sB + s * S::kB, &tmB, &full[s], kc, b_row0);
+        tma_load_2d(sW + s * kW, tw, &full[s], kc, w_row);
+        tma_load_2d(sX + s * kX, tx, &full[s], kc, x_row);
       }
     }
   } else if (warp == 1) {
@@ -139,14 +171,17 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_commit(done);
     }
-  } else {
-    // ------------------------------------------------------- epilogue ----
+  }
+
+  // ------------------------------------------------------------ epilogue ----
+  constexpr int CH = BN < 32 ? BN : 32;
+  if (warp >= 2) {
     const bool ok = mbar_wait(done, 0, p.err, 103);
     tc_fence_after();
     const int sub = warp & 3;
     const int row = sub * 32 + lane;  // TMEM lane == tile row
     const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-    constexpr int CH = BN < 32 ? BN : 32;
+    float* red = reinterpret_cast<float*>(smem);  // split-K: [BM][BN + 4]
 #pragma unroll 1
     for (int c = 0; c < BN; c += CH) {
       uint32_t r[32];
@@ -159,57 +194,54 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int j = 0; j < 16; ++j) r[j] = r16[j];
       }
       tc_wait_ld();
+      if constexpr (SPLIT) {
+        // park the partial tile (zeros if the pipeline failed or nkb == 0)
+#pragma unroll
+        for (int j = 0; j < CH; j += 4) {
+          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+          if (ok && nkb > 0)
+            v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                            __uint_as_float(r[j + 3]));
+          *reinterpret_cast<float4*>(red + row * (BN + 4) + c + j) = v;
+        }
+        continue;
+      }
       if (!ok) continue;
       if constexpr (!SWAP) {
         const int m = a_row0 + row;
         if (m >= p.M) continue;
         const int n0 = b_row0 + c;
-        if constexpr (SPLIT) {
-          float* dst = p.ws + (static_cast<size_t>(blockIdx.z) * p.M + m) * p.N;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < CH; ++j) {
+          v[j] = __uint_as_float(r[j]);
+          if (p.bias != nullptr && n0 + j < p.N) v[j] += __bfloat162float(p.bias[n0 + j]);
+        }
+        if (p.out_f32) {
+          float* dst = reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo;
 #pragma unroll
           for (int j = 0; j < CH; j += 4) {
             const int n = n0 + j;
             if (n + 4 <= p.N) {
-              *reinterpret_cast<float4*>(dst + n) =
-                  make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]),
-                              __uint_as_float(r[j + 2]), __uint_as_float(r[j + 3]));
+              *reinterpret_cast<float4*>(dst + n) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
             } else {
-              for (int q = 0; q < 4 && n + q < p.N; ++q) dst[n + q] = __uint_as_float(r[j + q]);
+              for (int q = 0; q < 4 && n + q < p.N; ++q) dst[n + q] = v[j + q];
             }
           }
         } else {
-          float v[32];
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo;
 #pragma unroll
-          for (int j = 0; j < CH; ++j) {
-            v[j] = __uint_as_float(r[j]);
-            if (p.bias != nullptr && n0 + j < p.N) v[j] += __bfloat162float(p.bias[n0 + j]);
-          }
-          if (p.out_f32) {
-            float* dst = reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo;
-#pragma unroll
-            for (int j = 0; j < CH; j += 4) {
-              const int n = n0 + j;
-              if (n + 4 <= p.N) {
-                *reinterpret_cast<float4*>(dst + n) = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-              } else {
-                for (int q = 0; q < 4 && n + q < p.N; ++q) dst[n + q] = v[j + q];
-              }
-            }
-          } else {
-            __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo;
-#pragma unroll
-            for (int j = 0; j < CH; j += 8) {
-              const int n = n0 + j;
-              if (n + 8 <= p.N) {
-                uint4 pk;
-                pk.x = pack_bf16x2(v[j], v[j + 1]);
-                pk.y = pack_bf16x2(v[j + 2], v[j + 3]);
-                pk.z = pack_bf16x2(v[j + 4], v[j + 5]);
-                pk.w = pack_bf16x2(v[j + 6], v[j + 7]);
-                *reinterpret_cast<uint4*>(dst + n) = pk;
-              } else {
-                for (int q = 0; q < 8 && n + q < p.N; ++q) dst[n + q] = __float2bfloat16_rn(v[j + q]);
-              }
+          for (int j = 0; j < CH; j += 8) {
+            const int n = n0 + j;
+            if (n + 8 <= p.N) {
+              uint4 pk;
+              pk.x = pack_bf16x2(v[j], v[j + 1]);
+              pk.y = pack_bf16x2(v[j + 2], v[j + 3]);
+              pk.z = pack_bf16x2(v[j + 4], v[j + 5]);
+              pk.w = pack_bf16x2(v[j + 6], v[j + 7]);
+              *reinterpret_cast<uint4*>(dst + n) = pk;
+            } else {
+              for (int q = 0; q < 8 && n + q < p.N; ++q) dst[n + q] = __float2bfloat16_rn(v[j + q]);
             }
           }
         }
@@ -217,23 +249,49 @@ __global__ void __launch_bounds__(kThreads, 1)
         // weight-major: this thread owns feature f; columns are tokens
         const int f = a_row0 + row;
         if (f >= p.N) continue;
-        const float b = (!SPLIT && p.bias != nullptr) ? __bfloat162float(p.bias[f]) : 0.f;
+        const float b = p.bias != nullptr ? __bfloat162float(p.bias[f]) : 0.f;
 #pragma unroll
         for (int j = 0; j < CH; ++j) {
           const int t = b_row0 + c + j;
           if (t >= p.M) break;
-          const float v = __uint_as_float(r[j]);
-          if constexpr (SPLIT) {
-            p.ws[(static_cast<size_t>(blockIdx.z) * p.M + t) * p.N + f] = v;
-          } else if (p.out_f32) {
-            reinterpret_cast<float*>(p.out)[static_cast<size_t>(t) * p.ldo + f] = v + b;
-          } else {
-            reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(t) * p.ldo + f] =
-                __float2bfloat16_rn(v + b);
-          }
+          store_out(p, t, f, __uint_as_float(r[j]) + b);
         }
       }
     }
+  }
+
+  if constexpr (SPLIT) {
+    __syncwarp();  // reconverge the producer / MMA warps before the aligned barrier
+    // sum the cluster's partial tiles through distributed shared memory; CTA
+    // rank r finalises rows [r * BM / S, (r + 1) * BM / S) of the tile
+    cluster_sync();
+    const uint32_t nsplit = gridDim.z;  // == cluster size along z
+    const uint32_t rank = cluster_ctarank();
+    const int rows_per = BM / static_cast<int>(nsplit);
+    const int r0 = static_cast<int>(rank) * rows_per;
+    const uint32_t red_base = smem_u32(smem);
+    const int total = rows_per * BN;
+    for (int e = threadIdx.x; e < total; e += kThreads) {
+      // consecutive threads walk the output's contiguous dimension
+      int tr, tc;
+      if constexpr (SWAP) {
+        tr = r0 + e % rows_per;  // tile row = feature
+        tc = e / rows_per;       // tile column = token
+      } else {
+        tr = r0 + e / BN;        // tile row = token
+        tc = e % BN;             // tile column = feature
+      }
+      const uint32_t off = static_cast<uint32_t>((tr * (BN + 4) + tc) * 4);
+      float acc = 0.f;
+      for (uint32_t q = 0; q < nsplit; ++q) acc += ld_shared_cluster_f32(map_shared_rank(red_base + off, q));
+      const int m = SWAP ? b_row0 + tc : a_row0 + tr;
+      const int n = SWAP ? a_row0 + tr : b_row0 + tc;
+      if (m < p.M && n < p.N) {
+        if (p.bias != nullptr) acc += __bfloat162float(p.bias[n]);
+        store_out(p, m, n, acc);
+      }
+    }
+    cluster_sync();  // peers may still be reading this CTA's tile
   }
 
   tc_fence_before();
@@ -244,42 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
-// out = sum over splits of ws (+ bias), converted to the output dtype.
-__global__ void splitk_reduce_kernel(const float* __restrict__ ws, void* out,
-                                     const __nv_bfloat16* __restrict__ bias, int M, int N, int ldo,
-                                     int splits, int out_f32) {
-  const int n4 = N / 4;
-  const size_t total = static_cast<size_t>(M) * n4;
-  const size_t stride_split = static_cast<size_t>(M) * N;
-  for (size_t i = blockIdx.x * static_cast<size_t>(blockDim.x) + threadIdx.x; i < total;
-       i += static_cast<size_t>(gridDim.x) * blockDim.x) {
-    const int m = static_cast<int>(i / n4);
-    const int n = static_cast<int>(i % n4) * 4;
-    const float* src = ws + static_cast<size_t>(m) * N + n;
-    float4 acc = *reinterpret_cast<const float4*>(src);
-    for (int s = 1; s < splits; ++s) {
-      const float4 v = *reinterpret_cast<const float4*>(src + s * stride_split);
-      acc.x += v.x, acc.y += v.y, acc.z += v.z, acc.w += v.w;
-    }
-    if (bias != nullptr) {
-      acc.x += __bfloat162float(bias[n]);
-      acc.y += __bfloat162float(bias[n + 1]);
-      acc.z += __bfloat162float(bias[n + 2]);
-      acc.w += __bfloat162float(bias[n + 3]);
-    }
-    if (out_f32) {
-      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + static_cast<size_t>(m) * ldo + n) = acc;
-    } else {
-      uint2 pk;
-      pk.x = pack_bf16x2(acc.x, acc.y);
-      pk.y = pack_bf16x2(acc.z, acc.w);
-      *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(out) + static_cast<size_t>(m) * ldo + n) = pk;
-    }
-  }
-}
-
 template <int BN, int STAGES, bool SWAP, bool SPLIT>
-void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, dim3 grid,
+void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, dim3 grid, int splits,
                  cudaStream_t stream) {
   auto kern = gemm_tc_kernel<BN, STAGES, SWAP, SPLIT>;
   constexpr uint32_t smem = Smem<BN, STAGES>::kBytes;
@@ -288,77 +312,97 @@ void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (SPLIT) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     configured[dev & 63] = true;
   }
-  kern<<<grid, kThreads, smem, stream>>>(ta, tb, kp);
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = dim3(kThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attrs[2];
+  int n = 0;
+  attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attrs[n].val.programmaticStreamSerializationAllowed = 1;
+  ++n;
+  if (SPLIT) {
+    attrs[n].id = cudaLaunchAttributeClusterDimension;
+    attrs[n].val.clusterDim.x = 1;
+    attrs[n].val.clusterDim.y = 1;
+    attrs[n].val.clusterDim.z = static_cast<unsigned>(splits);
+    ++n;
+  }
+  cfg.attrs = attrs;
+  cfg.numAttrs = n;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, kp);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("minisgl.gemm launch failed: ") + cudaGetErrorString(e));
 }
 
 template <int BN, int STAGES, bool SWAP>
-void dispatch_split(bool split, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp,
-                    dim3 grid, cudaStream_t stream) {
-  if (split) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, stream);
-  else launch_tile<BN, STAGES, SWAP, false>(ta, tb, kp, grid, stream);
+void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, dim3 grid,
+                    cudaStream_t stream) {
+  if (splits > 1) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
+  else launch_tile<BN, STAGES, SWAP, false>(ta, tb, kp, grid, 1, stream);
 }
 
-constexpr int kNumSM = 148;
+constexpr int kMaxSplits = 8;
 
 struct Plan {
   bool swap;
   int bn;
-  int tiles;  // output tiles
+  int tiles;
   int splits;
   int kb_per_split;
 };
 
+int tiles_for(int M, int N, int bn, bool swap) {
+  return swap ? ((N + BM - 1) / BM) * ((M + bn - 1) / bn) : ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
+}
+
+// Tile plan: prefer enough CTAs to cover the SMs through smaller tiles; use
+// cluster split-K (<= 8 CTAs sharing a tile) only when tiles alone cannot.
 Plan make_plan(int M, int N, int K, int force_mode, int force_splits) {
   Plan pl;
   const int num_kb = (K + BK - 1) / BK;
   pl.swap = force_mode == 2 || (force_mode == 0 && M <= 128);
   if (pl.swap) {
     pl.bn = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
-    pl.tiles = ((N + BM - 1) / BM) * ((M + pl.bn - 1) / pl.bn);
   } else {
-    pl.bn = N >= 256 ? 256 : 128;
-    pl.tiles = ((M + BM - 1) / BM) * ((N + pl.bn - 1) / pl.bn);
+    pl.bn = 64;
+    for (int bn : {256, 128}) {
+      if (tiles_for(M, N, bn, false) >= 120) {
+        pl.bn = bn;
+        break;
+      }
+    }
   }
+  pl.tiles = tiles_for(M, N, pl.bn, pl.swap);
   int splits = 1;
   if (force_splits > 0) {
     splits = force_splits;
-  } else if (pl.tiles < kNumSM) {
-    // enough CTAs to cover the SMs, at least two k-blocks per split
-    splits = std::max(1, std::min(kNumSM / pl.tiles, num_kb / 2));
+  } else if (pl.tiles < 100) {
+    for (int s = 2; s <= kMaxSplits; s *= 2)
+      if (pl.tiles * s <= 160 && num_kb / s >= 2) splits = s;
   }
-  splits = std::max(1, std::min(splits, num_kb));
+  splits = std::max(1, std::min(splits, kMaxSplits));
+  while (splits > 1 && (splits > num_kb || (BM % splits) != 0)) splits /= 2;
   pl.kb_per_split = (num_kb + splits - 1) / splits;
-  pl.splits = (num_kb + pl.kb_per_split - 1) / pl.kb_per_split;  // no empty split
+  pl.splits = splits;
   return pl;
 }
 
 }  // namespace
 
-int64_t gemm_workspace_elems(int M, int N, int K) {
-  Plan pl = make_plan(M, N, K, 0, 0);
-  return pl.splits > 1 ? static_cast<int64_t>(pl.splits) * M * N : 0;
-}
+int64_t gemm_workspace_elems(int, int, int) { return 0; }
 
 void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0) return;
   if (a.K % 8 != 0 || a.ldx % 8 != 0 || a.ldw % 8 != 0)
     throw std::runtime_error("minisgl.gemm: K and row strides must be multiples of 8 elements");
   if (a.N % 4 != 0) throw std::runtime_error("minisgl.gemm: N must be a multiple of 4");
-  Plan pl = make_plan(a.M, a.N, a.K, a.force_mode, a.force_splits);
-  if (pl.splits > 1) {
-    const int64_t need = static_cast<int64_t>(pl.splits) * a.M * a.N;
-    if (a.workspace == nullptr || a.workspace_elems < need) {
-      // fall back to fewer splits that fit the workspace
-      int fit = a.workspace == nullptr ? 1 : static_cast<int>(a.workspace_elems / (static_cast<int64_t>(a.M) * a.N));
-      pl = make_plan(a.M, a.N, a.K, a.force_mode, std::max(1, fit));
-    }
-  }
-  const bool split = pl.splits > 1;
+  const Plan pl = make_plan(a.M, a.N, a.K, a.force_mode, a.force_splits);
   KParams kp;
   kp.out = a.out;
-  kp.ws = a.workspace;
   kp.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
   kp.M = a.M;
   kp.N = a.N;
@@ -367,30 +411,25 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   kp.num_kb = (a.K + BK - 1) / BK;
   kp.out_f32 = a.out_f32 ? 1 : 0;
   kp.err = ErrorSink{a.err};
-
   if (pl.swap) {
     CUtensorMap ta = make_tmap_bf16_2d_sw128(a.w, a.N, a.K, a.ldw, BM);
     CUtensorMap tb = make_tmap_bf16_2d_sw128(a.x, a.M, a.K, a.ldx, pl.bn);
     dim3 grid((a.M + pl.bn - 1) / pl.bn, (a.N + BM - 1) / BM, pl.splits);
     switch (pl.bn) {
-      case 16: dispatch_split<16, 8, true>(split, ta, tb, kp, grid, stream); break;
-      case 32: dispatch_split<32, 8, true>(split, ta, tb, kp, grid, stream); break;
-      case 64: dispatch_split<64, 8, true>(split, ta, tb, kp, grid, stream); break;
-      default: dispatch_split<128, 6, true>(split, ta, tb, kp, grid, stream); break;
+      case 16: dispatch_split<16, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 32: dispatch_split<32, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 64: dispatch_split<64, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      default: dispatch_split<128, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
     }
   } else {
     CUtensorMap ta = make_tmap_bf16_2d_sw128(a.x, a.M, a.K, a.ldx, BM);
     CUtensorMap tb = make_tmap_bf16_2d_sw128(a.w, a.N, a.K, a.ldw, pl.bn);
     dim3 grid((a.N + pl.bn - 1) / pl.bn, (a.M + BM - 1) / BM, pl.splits);
-    if (pl.bn == 256) dispatch_split<256, 4, false>(split, ta, tb, kp, grid, stream);
-    else dispatch_split<128, 6, false>(split, ta, tb, kp, grid, stream);
-  }
-  if (split) {
-    const size_t total = static_cast<size_t>(a.M) * (a.N / 4);
-    const int threads = 256;
-    const int blocks = static_cast<int>(std::min<size_t>((total + threads - 1) / threads, 148 * 8));
-    splitk_reduce_kernel<<<blocks, threads, 0, stream>>>(a.workspace, a.out, kp.bias, a.M, a.N,
-                                                         a.ldo, pl.splits, kp.out_f32);
+    switch (pl.bn) {
+      case 64: dispatch_split<64, 4, false>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 128: dispatch_split<128, 4, false>(pl.splits, ta, tb, kp, grid, stream); break;
+      default: dispatch_split<256, 4, false>(pl.splits, ta, tb, kp, grid, stream); break;
+    }
   }
 }
 

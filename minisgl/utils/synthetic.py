@@ -136,3 +136,56 @@ def make_model_dir(shape: str, folder: Optional[str] = None, overrides: Optional
             with open(os.path.join(folder, "config.json"), "w") as f:
                 json.dump(cfg, f, indent=1)
     return folder
+
+
+def write_random_checkpoint(folder: str, seed: int = 0, std: float = 0.02) -> str:
+    """Write HF-named random weights (``model.safetensors``) for the config
+    in ``folder``: separate q/k/v and gate/up projections, per-expert tensors,
+    exactly as a downloaded checkpoint is laid out."""
+    import torch
+    from safetensors.torch import save_file
+
+    with open(os.path.join(folder, "config.json")) as f:
+        c = json.load(f)
+    g = torch.Generator().manual_seed(seed)
+    dt = {"bfloat16": torch.bfloat16, "float16": torch.float16}.get(c.get("torch_dtype"), torch.float32)
+
+    def rnd(*shape):
+        return (torch.randn(*shape, generator=g) * std).to(dt)
+
+    H, V = c["hidden_size"], c["vocab_size"]
+    hq, hk = c["num_attention_heads"], c.get("num_key_value_heads", c["num_attention_heads"])
+    d = c.get("head_dim") or H // hq
+    W = {"model.embed_tokens.weight": rnd(V, H), "model.norm.weight": torch.ones(H, dtype=dt)}
+    if not c.get("tie_word_embeddings", False):
+        W["lm_head.weight"] = rnd(V, H)
+    moe = c.get("num_experts", 0) > 0
+    for i in range(c["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        W[p + "input_layernorm.weight"] = torch.ones(H, dtype=dt)
+        W[p + "post_attention_layernorm.weight"] = torch.ones(H, dtype=dt)
+        W[p + "self_attn.q_proj.weight"] = rnd(hq * d, H)
+        W[p + "self_attn.k_proj.weight"] = rnd(hk * d, H)
+        W[p + "self_attn.v_proj.weight"] = rnd(hk * d, H)
+        W[p + "self_attn.o_proj.weight"] = rnd(H, hq * d)
+        if c.get("model_type", "").startswith("qwen3"):
+            W[p + "self_attn.q_norm.weight"] = torch.ones(d, dtype=dt)
+            W[p + "self_attn.k_norm.weight"] = torch.ones(d, dtype=dt)
+        if c.get("model_type") == "qwen2":
+            for n, size in (("q", hq * d), ("k", hk * d), ("v", hk * d)):
+                W[p + f"self_attn.{n}_proj.bias"] = rnd(size)
+        if moe:
+            I = c["moe_intermediate_size"]
+            W[p + "mlp.gate.weight"] = rnd(c["num_experts"], H)
+            for e in range(c["num_experts"]):
+                q = p + f"mlp.experts.{e}."
+                W[q + "gate_proj.weight"] = rnd(I, H)
+                W[q + "up_proj.weight"] = rnd(I, H)
+                W[q + "down_proj.weight"] = rnd(H, I)
+        else:
+            I = c["intermediate_size"]
+            W[p + "mlp.gate_proj.weight"] = rnd(I, H)
+            W[p + "mlp.up_proj.weight"] = rnd(I, H)
+            W[p + "mlp.down_proj.weight"] = rnd(H, I)
+    save_file({k: v.contiguous() for k, v in W.items()}, os.path.join(folder, "model.safetensors"))
+    return folder

@@ -40,6 +40,9 @@ def _close(out, expect, atol, rtol):
         (1000, 1536, 1024),
         (4096, 4096, 1024),
         (3000, 1024, 72),
+        (256, 151936 // 16, 1024),
+        (129, 1024, 3072),
+        (250, 6144, 1024),
     ],
 )
 @pytest.mark.parametrize("bias", [False, True])
@@ -54,7 +57,7 @@ def test_gemm(M, N, K, bias):
     _close(out, expect, atol=2e-2 * math.sqrt(K / 1024), rtol=1e-2)
 
 
-@pytest.mark.parametrize("mode,splits", [(1, 1), (1, 3), (2, 1), (2, 4)])
+@pytest.mark.parametrize("mode,splits", [(1, 1), (1, 2), (1, 4), (2, 1), (2, 4), (2, 8)])
 def test_gemm_forced_paths(mode, splits):
     torch.manual_seed(0)
     M, N, K = 96, 2048, 2048
