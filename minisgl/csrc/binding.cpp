@@ -12,6 +12,7 @@
 
 namespace minisgl {
 int64_t compare_key_raw(const void* a, int64_t na, int ea, const void* b, int64_t nb, int eb);
+std::vector<int64_t> gemm_plan_desc(int64_t M, int64_t N, int64_t K);
 }
 
 using minisgl::DType;
@@ -56,7 +57,8 @@ cudaStream_t stream_of(const at::Tensor& t) {
 // ------------------------------------------------------------------- GEMM
 void gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w,
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& workspace,
-          int64_t force_splits, int64_t force_mode, const c10::optional<at::Tensor>& err) {
+          int64_t force_splits, int64_t force_mode, const c10::optional<at::Tensor>& err, int64_t force_bn,
+          const c10::optional<at::Tensor>& trace) {
   check_cuda(x, "x");
   check_cuda(w, "w");
   check_cuda(out, "out");
@@ -99,6 +101,12 @@ void gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w,
   a.out_f32 = out.scalar_type() == at::kFloat;
   a.force_splits = static_cast<int>(force_splits);
   a.force_mode = static_cast<int>(force_mode);
+  a.force_bn = static_cast<int>(force_bn);
+  a.trace = nullptr;
+  if (trace.has_value()) {
+    MSG_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous(), "trace must be CUDA int64");
+    a.trace = trace->data_ptr();
+  }
   a.err = err_ptr(err);
   const c10::cuda::CUDAGuard guard(x.device());
   minisgl::launch_gemm(a, stream_of(x));
@@ -388,7 +396,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "minisgl native kernels for NVIDIA B200 (sm_100a)";
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM: out = x @ w^T (+ bias)", py::arg("out"), py::arg("x"),
         py::arg("w"), py::arg("bias") = py::none(), py::arg("workspace") = py::none(),
-        py::arg("force_splits") = 0, py::arg("force_mode") = 0, py::arg("err") = py::none());
+        py::arg("force_splits") = 0, py::arg("force_mode") = 0, py::arg("err") = py::none(),
+        py::arg("force_bn") = 0, py::arg("trace") = py::none());
+  m.def("gemm_plan", [](int64_t M, int64_t N, int64_t K) { return minisgl::gemm_plan_desc(M, N, K); });
   m.def("gemm_workspace_elems", &gemm_workspace_elems);
   m.def("rmsnorm", &rmsnorm);
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);

@@ -292,17 +292,19 @@ __device__ __forceinline__ uint32_t map_shared_rank(uint32_t smem_addr, uint32_t
   asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr), "r"(rank));
   return out;
 }
+// Loads from peer shared memory. Volatile (kept in program order after the
+// cluster barrier) but without a memory clobber, so independent loads issue
+// back to back and are in flight together.
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
   return v;
 }
 __device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-               : "r"(addr)
-               : "memory");
+      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+      : "r"(addr));
   return v;
 }
 

@@ -32,6 +32,7 @@
 #include <algorithm>
 #include <stdexcept>
 #include <string>
+#include <vector>
 
 #include "common.cuh"
 #include "ops.h"
@@ -53,15 +54,29 @@ struct KParams {
   int num_kb;
   int out_f32;
   ErrorSink err;
+  // optional per-CTA phase timestamps (%globaltimer ns), 8 slots per CTA:
+  // 0 entry, 1 setup done, 2 producer past griddepcontrol.wait, 3 first
+  // stage consumed by the MMA thread, 4 accumulator ready, 5 exit
+  unsigned long long* trace;
 };
+
+__device__ __forceinline__ void trace_stamp(const KParams& p, int slot) {
+  if (p.trace != nullptr) {
+    const size_t cta = (static_cast<size_t>(blockIdx.z) * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x;
+    p.trace[cta * 8 + slot] = globaltimer_ns();
+  }
+}
 
 template <int BN, int STAGES>
 struct Smem {
   static constexpr uint32_t kA = BM * BK * 2;
   static constexpr uint32_t kB = BN * BK * 2;
   static constexpr uint32_t kPipe = STAGES * (kA + kB);
-  // split-K reduction tile: 128 rows x BN fp32, rows padded by 4 floats
-  static constexpr uint32_t kRed = BM * (BN + 4) * 4;
+  // split-K reduction tile, output-major: tokens x features fp32, each row
+  // padded by 4 floats (weight-major tiles: BN tokens x 128 features)
+  static constexpr uint32_t kRedLdSwap = BM + 4;
+  static constexpr uint32_t kRedLdTok = BN + 4;
+  static constexpr uint32_t kRed = (BN * kRedLdSwap > BM * kRedLdTok ? BN * kRedLdSwap : BM * kRedLdTok) * 4;
   static constexpr uint32_t kMain = kPipe > kRed ? kPipe : kRed;
   static constexpr uint32_t kBytes = kMain + 1024 /*align*/ + 256 /*barriers*/;
 };
@@ -105,6 +120,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int nkb = max(0, kb1 - kb0);
 
   pdl_launch_dependents();
+  if (threadIdx.x == 0) trace_stamp(p, 0);
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full[s], 1);
@@ -123,6 +139,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
+  if (threadIdx.x == 0) trace_stamp(p, 1);
 
   if (warp == 0) {
     if (lane == 0) {
@@ -141,6 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         tma_load_2d(sW + i * kW, tw, &full[i], (kb0 + i) * BK, w_row);
       }
       pdl_wait();
+      trace_stamp(p, 2);
       for (int i = 0; i < pre; ++i) tma_load_2d(sX + i * kX, tx, &full[i], (kb0 + i) * BK, x_row);
       for (int i = pre; i < nkb; ++i) {
         const int s = i % STAGES;
@@ -159,6 +177,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int s = i % STAGES;
         const uint32_t ph = (i / STAGES) & 1u;
         if (!mbar_wait(&full[s], ph, p.err, 102)) break;
+        if (i == 0) trace_stamp(p, 3);
         tc_fence_after();
         const uint32_t a_addr = smem_u32(sA + s * S::kA);
         const uint32_t b_addr = smem_u32(sB + s * S::kB);
@@ -177,11 +196,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   constexpr int CH = BN < 32 ? BN : 32;
   if (warp >= 2) {
     const bool ok = mbar_wait(done, 0, p.err, 103);
+    if (threadIdx.x == 64) trace_stamp(p, 4);
     tc_fence_after();
     const int sub = warp & 3;
     const int row = sub * 32 + lane;  // TMEM lane == tile row
     const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16);
-    float* red = reinterpret_cast<float*>(smem);  // split-K: [BM][BN + 4]
+    float* red = reinterpret_cast<float*>(smem);  // split-K parking tile (output-major)
 #pragma unroll 1
     for (int c = 0; c < BN; c += CH) {
       uint32_t r[32];
@@ -195,14 +215,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       tc_wait_ld();
       if constexpr (SPLIT) {
-        // park the partial tile (zeros if the pipeline failed or nkb == 0)
+        // park the partial tile output-major (zeros if the pipeline failed)
+        const bool have = ok && nkb > 0;
+        if constexpr (SWAP) {
 #pragma unroll
-        for (int j = 0; j < CH; j += 4) {
-          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (ok && nkb > 0)
-            v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
-                            __uint_as_float(r[j + 3]));
-          *reinterpret_cast<float4*>(red + row * (BN + 4) + c + j) = v;
+          for (int j = 0; j < CH; ++j)
+            red[(c + j) * S::kRedLdSwap + row] = have ? __uint_as_float(r[j]) : 0.f;
+        } else {
+#pragma unroll
+          for (int j = 0; j < CH; j += 4) {
+            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+            if (have)
+              v = make_float4(__uint_as_float(r[j]), __uint_as_float(r[j + 1]), __uint_as_float(r[j + 2]),
+                              __uint_as_float(r[j + 3]));
+            *reinterpret_cast<float4*>(red + row * S::kRedLdTok + c + j) = v;
+          }
         }
         continue;
       }
@@ -262,33 +289,50 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if constexpr (SPLIT) {
     __syncwarp();  // reconverge the producer / MMA warps before the aligned barrier
-    // sum the cluster's partial tiles through distributed shared memory; CTA
-    // rank r finalises rows [r * BM / S, (r + 1) * BM / S) of the tile
-    cluster_sync();
-    const uint32_t nsplit = gridDim.z;  // == cluster size along z
-    const uint32_t rank = cluster_ctarank();
-    const int rows_per = BM / static_cast<int>(nsplit);
-    const int r0 = static_cast<int>(rank) * rows_per;
+    // sum the cluster's partial tiles through distributed shared memory: CTA
+    // rank r finalises output rows [r * R / S, (r + 1) * R / S) of the tile
+    // (R = tokens in the tile), 4 consecutive features per thread and load
+    constexpr int kOutRows = SWAP ? BN : BM;
+    constexpr int kOutCols = SWAP ? BM : BN;
+    constexpr int kLd = SWAP ? S::kRedLdSwap : S::kRedLdTok;
+    constexpr int kMaxS = 16;
+    const int nsplit = static_cast<int>(gridDim.z);  // == cluster size along z
+    const int rank = static_cast<int>(cluster_ctarank());
+    const int rows_per = kOutRows / nsplit;
     const uint32_t red_base = smem_u32(smem);
-    const int total = rows_per * BN;
-    for (int e = threadIdx.x; e < total; e += kThreads) {
-      // consecutive threads walk the output's contiguous dimension
-      int tr, tc;
-      if constexpr (SWAP) {
-        tr = r0 + e % rows_per;  // tile row = feature
-        tc = e / rows_per;       // tile column = token
+    const int tok0 = SWAP ? b_row0 : a_row0;
+    const int feat0 = SWAP ? a_row0 : b_row0;
+    const int vecs = rows_per * (kOutCols / 4);
+    for (int e = threadIdx.x; e < vecs; e += kThreads) {
+      const int orow = rank * rows_per + e / (kOutCols / 4);
+      const int ocol = (e % (kOutCols / 4)) * 4;
+      const uint32_t off = static_cast<uint32_t>((orow * kLd + ocol) * 4);
+      float4 part[kMaxS];
+#pragma unroll
+      for (int q = 0; q < kMaxS; ++q)
+        if (q < nsplit) part[q] = ld_shared_cluster_v4(map_shared_rank(red_base + off, static_cast<uint32_t>(q)));
+      float4 acc = part[0];
+#pragma unroll
+      for (int q = 1; q < kMaxS; ++q)
+        if (q < nsplit) acc.x += part[q].x, acc.y += part[q].y, acc.z += part[q].z, acc.w += part[q].w;
+      const int m = tok0 + orow;
+      const int n = feat0 + ocol;
+      if (m >= p.M || n >= p.N) continue;
+      float v[4] = {acc.x, acc.y, acc.z, acc.w};
+      if (p.bias != nullptr)
+        for (int q = 0; q < 4; ++q) v[q] += n + q < p.N ? __bfloat162float(p.bias[n + q]) : 0.f;
+      if (n + 4 <= p.N && (p.ldo & 3) == 0) {
+        if (p.out_f32) {
+          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n) =
+              make_float4(v[0], v[1], v[2], v[3]);
+        } else {
+          uint2 pk;
+          pk.x = pack_bf16x2(v[0], v[1]);
+          pk.y = pack_bf16x2(v[2], v[3]);
+          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + n) = pk;
+        }
       } else {
-        tr = r0 + e / BN;        // tile row = token
-        tc = e % BN;             // tile column = feature
-      }
-      const uint32_t off = static_cast<uint32_t>((tr * (BN + 4) + tc) * 4);
-      float acc = 0.f;
-      for (uint32_t q = 0; q < nsplit; ++q) acc += ld_shared_cluster_f32(map_shared_rank(red_base + off, q));
-      const int m = SWAP ? b_row0 + tc : a_row0 + tr;
-      const int n = SWAP ? a_row0 + tr : b_row0 + tc;
-      if (m < p.M && n < p.N) {
-        if (p.bias != nullptr) acc += __bfloat162float(p.bias[n]);
-        store_out(p, m, n, acc);
+        for (int q = 0; q < 4 && n + q < p.N; ++q) store_out(p, m, n + q, v[q]);
       }
     }
     cluster_sync();  // peers may still be reading this CTA's tile
@@ -296,6 +340,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  if (threadIdx.x == 0) trace_stamp(p, 5);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, kCols);
@@ -345,11 +390,13 @@ void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, co
   else launch_tile<BN, STAGES, SWAP, false>(ta, tb, kp, grid, 1, stream);
 }
 
-constexpr int kMaxSplits = 8;
+constexpr int kMaxSplits = 16;
+constexpr int kTargetCtas = 148;
 
 struct Plan {
   bool swap;
   int bn;
+  int stages;
   int tiles;
   int splits;
   int kb_per_split;
@@ -359,33 +406,36 @@ int tiles_for(int M, int N, int bn, bool swap) {
   return swap ? ((N + BM - 1) / BM) * ((M + bn - 1) / bn) : ((M + BM - 1) / BM) * ((N + bn - 1) / bn);
 }
 
-// Tile plan: prefer enough CTAs to cover the SMs through smaller tiles; use
-// cluster split-K (<= 8 CTAs sharing a tile) only when tiles alone cannot.
-Plan make_plan(int M, int N, int K, int force_mode, int force_splits) {
+int stages_for(int bn) { return bn <= 64 ? 8 : 4; }
+
+// Default tile plan (autotuned plans from the Python side override it):
+//   * weight-major tiles for up to 128 tokens, 16 or 32 tokens per tile;
+//   * split K until each CTA's whole weight slice fits its stage ring (so it
+//     is prefetched under PDL before griddepcontrol.wait), then keep
+//     splitting while that still fits about one CTA per SM.
+Plan make_plan(int M, int N, int K, int force_mode, int force_splits, int force_bn = 0) {
   Plan pl;
   const int num_kb = (K + BK - 1) / BK;
   pl.swap = force_mode == 2 || (force_mode == 0 && M <= 128);
   if (pl.swap) {
-    pl.bn = M <= 16 ? 16 : (M <= 32 ? 32 : (M <= 64 ? 64 : 128));
+    pl.bn = M <= 16 ? 16 : 32;
   } else {
-    pl.bn = 64;
-    for (int bn : {256, 128}) {
-      if (tiles_for(M, N, bn, false) >= 120) {
-        pl.bn = bn;
-        break;
-      }
-    }
+    pl.bn = M >= 1024 ? 256 : 64;
+    if (M >= 1024 && tiles_for(M, N, 256, false) < 120) pl.bn = 128;
   }
+  if (force_bn > 0) pl.bn = force_bn;
+  pl.stages = stages_for(pl.bn);
   pl.tiles = tiles_for(M, N, pl.bn, pl.swap);
+  const int out_rows = pl.swap ? pl.bn : BM;
   int splits = 1;
   if (force_splits > 0) {
     splits = force_splits;
-  } else if (pl.tiles < 100) {
-    for (int s = 2; s <= kMaxSplits; s *= 2)
-      if (pl.tiles * s <= 160 && num_kb / s >= 2) splits = s;
+  } else if (M < 1024) {
+    while (splits < kMaxSplits && (num_kb + splits - 1) / splits > pl.stages) splits *= 2;
+    while (splits < kMaxSplits && pl.tiles * splits * 2 <= kTargetCtas && num_kb / (splits * 2) >= 2) splits *= 2;
   }
   splits = std::max(1, std::min(splits, kMaxSplits));
-  while (splits > 1 && (splits > num_kb || (BM % splits) != 0)) splits /= 2;
+  while (splits > 1 && (splits > num_kb || (out_rows % splits) != 0)) splits /= 2;
   pl.kb_per_split = (num_kb + splits - 1) / splits;
   pl.splits = splits;
   return pl;
@@ -395,12 +445,23 @@ Plan make_plan(int M, int N, int K, int force_mode, int force_splits) {
 
 int64_t gemm_workspace_elems(int, int, int) { return 0; }
 
+// (swap, bn, splits, grid CTAs) of the heuristic plan, for tests and tools.
+std::vector<int64_t> gemm_plan_desc(int64_t M, int64_t N, int64_t K) {
+  const Plan pl = make_plan(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K), 0, 0, 0);
+  return {pl.swap ? 1 : 0, pl.bn, pl.splits, static_cast<int64_t>(pl.tiles) * pl.splits, pl.stages};
+}
+
 void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0) return;
   if (a.K % 8 != 0 || a.ldx % 8 != 0 || a.ldw % 8 != 0)
     throw std::runtime_error("minisgl.gemm: K and row strides must be multiples of 8 elements");
   if (a.N % 4 != 0) throw std::runtime_error("minisgl.gemm: N must be a multiple of 4");
-  const Plan pl = make_plan(a.M, a.N, a.K, a.force_mode, a.force_splits);
+  if (a.force_bn != 0 && a.force_bn != 16 && a.force_bn != 32 && a.force_bn != 64 && a.force_bn != 128 &&
+      a.force_bn != 256)
+    throw std::runtime_error("minisgl.gemm: N tile must be 16, 32, 64, 128 or 256");
+  if (a.force_bn == 16 && a.force_mode == 1)
+    throw std::runtime_error("minisgl.gemm: token-major tiles need an N tile of at least 32");
+  const Plan pl = make_plan(a.M, a.N, a.K, a.force_mode, a.force_splits, a.force_bn);
   KParams kp;
   kp.out = a.out;
   kp.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
@@ -411,22 +472,25 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   kp.num_kb = (a.K + BK - 1) / BK;
   kp.out_f32 = a.out_f32 ? 1 : 0;
   kp.err = ErrorSink{a.err};
+  kp.trace = reinterpret_cast<unsigned long long*>(a.trace);
   if (pl.swap) {
     CUtensorMap ta = make_tmap_bf16_2d_sw128(a.w, a.N, a.K, a.ldw, BM);
     CUtensorMap tb = make_tmap_bf16_2d_sw128(a.x, a.M, a.K, a.ldx, pl.bn);
     dim3 grid((a.M + pl.bn - 1) / pl.bn, (a.N + BM - 1) / BM, pl.splits);
     switch (pl.bn) {
-      case 16: dispatch_split<16, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
-      case 32: dispatch_split<32, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
-      case 64: dispatch_split<64, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
-      default: dispatch_split<128, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 16: dispatch_split<16, 8, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 32: dispatch_split<32, 8, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 64: dispatch_split<64, 8, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 128: dispatch_split<128, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
+      default: dispatch_split<256, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
     }
   } else {
     CUtensorMap ta = make_tmap_bf16_2d_sw128(a.x, a.M, a.K, a.ldx, BM);
     CUtensorMap tb = make_tmap_bf16_2d_sw128(a.w, a.N, a.K, a.ldw, pl.bn);
     dim3 grid((a.N + pl.bn - 1) / pl.bn, (a.M + BM - 1) / BM, pl.splits);
     switch (pl.bn) {
-      case 64: dispatch_split<64, 4, false>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 32: dispatch_split<32, 8, false>(pl.splits, ta, tb, kp, grid, stream); break;
+      case 64: dispatch_split<64, 8, false>(pl.splits, ta, tb, kp, grid, stream); break;
       case 128: dispatch_split<128, 4, false>(pl.splits, ta, tb, kp, grid, stream); break;
       default: dispatch_split<256, 4, false>(pl.splits, ta, tb, kp, grid, stream); break;
     }

@@ -24,6 +24,8 @@ struct GemmArgs {
   bool out_f32;
   int force_splits;   // 0 = heuristic
   int force_mode;     // 0 = heuristic, 1 = token-major tiles, 2 = weight-major tiles (swap)
+  int force_bn;       // 0 = heuristic, else the N tile (16..256)
+  void* trace;        // optional uint64 [ctas * 8] phase timestamps (profiling)
   int* err;           // device error word (2 x int32) or nullptr
 };
 void launch_gemm(const GemmArgs& a, cudaStream_t stream);

@@ -47,6 +47,7 @@ class EngineConfig:
     dummy_weight_device: Optional[str] = None  # draw random weights here ("cpu" for bit-identical tests)
     hf_config_override: Optional[Dict[str, Any]] = field(default=None, hash=False, compare=False)
     distributed_port: Optional[int] = None
+    gemm_autotune: bool = True        # time GEMM tile plans for the decode batch sizes at start-up
 
     @cached_property
     def hf_config(self):

@@ -121,6 +121,9 @@ class Engine:
             ops.error_word(self.device)
             logger.info_rank0(f"Free memory after initialization: {mem_GB(self._sync_get_memory()[0])}")
 
+        if self.is_cuda and config.gemm_autotune:
+            self._tune_gemms(config)
+
         # ------------------------------------------------------ CUDA graphs
         self.dummy_req = Req(input_ids=torch.tensor([0], dtype=torch.int32), table_idx=config.max_running_req,
                              cached_len=0, output_len=1, uid=-1, sampling_params=None,  # type: ignore[arg-type]
@@ -138,6 +141,42 @@ class Engine:
         if mx is None:
             return min(config.max_running_req, 256)
         return min(mx, config.max_running_req)
+
+    def _gemm_shapes(self):
+        """(N, K) of every dense projection the decode graphs run."""
+        from minisgl.layers import BaseOP, OPList, ParallelLMHead
+        from minisgl.layers.linear import _Linear
+
+        shapes, stack = set(), [self.model]
+        while stack:
+            op = stack.pop()
+            if isinstance(op, OPList):
+                stack.extend(op.op_list)
+                continue
+            if isinstance(op, _Linear):
+                shapes.add(tuple(op.weight.shape))
+            elif isinstance(op, ParallelLMHead):
+                w = op._tied.weight if op._tied is not None else op.weight
+                shapes.add(tuple(w.shape))
+            for name, v in vars(op).items():
+                if isinstance(v, BaseOP) and not name.startswith("_"):
+                    stack.append(v)
+        return sorted(shapes)
+
+    def _tune_gemms(self, config: EngineConfig) -> None:
+        import time
+
+        from minisgl.ops import gemm_tune
+
+        from .graph import determine_cuda_graph_bs
+
+        bs = determine_cuda_graph_bs(config.cuda_graph_bs, self._graph_max_bs(config), 1 << 40)
+        if not bs:
+            return
+        t0 = time.perf_counter()
+        cache = os.environ.get("MINISGL_GEMM_TUNE_CACHE") or None
+        plans = gemm_tune.tune(self._gemm_shapes(), bs, self.device, cache)
+        logger.info_rank0(f"Tuned {len(plans)} GEMM plans in {time.perf_counter() - t0:.1f}s")
 
     def _init_communication(self, config: EngineConfig):
         import torch.distributed as dist

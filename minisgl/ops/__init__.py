@@ -89,17 +89,7 @@ def check_device_errors(device: torch.device) -> None:
 
 
 # ------------------------------------------------------------------- GEMM
-_GEMM_KERNELS: dict = {}
-
-
-def _gemm_kernels(M: int, N: int, K: int) -> int:
-    """1, or 2 when the split-K plan adds its reduction kernel."""
-    key = (M, N, K)
-    n = _GEMM_KERNELS.get(key)
-    if n is None:
-        n = 2 if native().gemm_workspace_elems(M, N, K) > 0 else 1
-        _GEMM_KERNELS[key] = n
-    return n
+from .gemm_tune import PLANS as _gemm_plans  # noqa: E402  (autotuned plans by (M, N, K))
 
 def gemm(
     x: torch.Tensor,
@@ -118,8 +108,13 @@ def gemm(
         return y
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
-    _count(_gemm_kernels(x.shape[0], w.shape[0], x.shape[1]))
-    native().gemm(out, x, w, bias, gemm_workspace(x.device), 0, 0, error_word(x.device))
+    _count()
+    plan = _gemm_plans.get((x.shape[0], w.shape[0], x.shape[1]))
+    if plan is None:
+        native().gemm(out, x, w, bias, None, 0, 0, error_word(x.device))
+    else:
+        mode, bn, splits = plan
+        native().gemm(out, x, w, bias, None, splits, mode, error_word(x.device), bn)
     return out
 
 
