@@ -283,28 +283,33 @@ __device__ __forceinline__ uint32_t cluster_ctarank() {
   asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
   return r;
 }
+// Cluster-wide barrier. All threads of every warp must reach it converged
+// (.aligned): kernels keep their role warps converged for this reason.
 __device__ __forceinline__ void cluster_sync() {
+  __syncwarp();
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 // Address of the same shared-memory location in CTA `rank` of the cluster.
 __device__ __forceinline__ uint32_t map_shared_rank(uint32_t smem_addr, uint32_t rank) {
   uint32_t out;
-  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr), "r"(rank));
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_addr), "r"(rank) : "memory");
   return out;
 }
-// Loads from peer shared memory. Volatile (kept in program order after the
-// cluster barrier) but without a memory clobber, so independent loads issue
-// back to back and are in flight together.
+// Loads from peer shared memory. The memory clobber keeps them after the
+// cluster barrier (without it the compiler may hoist them above the barrier
+// and read a peer's tile before the peer has written it); consecutive loads
+// still issue back to back because nothing waits on their results until use.
 __device__ __forceinline__ float ld_shared_cluster_f32(uint32_t addr) {
   float v;
-  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr));
+  asm volatile("ld.shared::cluster.f32 %0, [%1];" : "=f"(v) : "r"(addr) : "memory");
   return v;
 }
 __device__ __forceinline__ float4 ld_shared_cluster_v4(uint32_t addr) {
   float4 v;
   asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
-      : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-      : "r"(addr));
+               : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+               : "r"(addr)
+               : "memory");
   return v;
 }
 

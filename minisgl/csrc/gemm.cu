@@ -141,44 +141,55 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem = *tmem_slot;
   if (threadIdx.x == 0) trace_stamp(p, 1);
 
+  // The producer and MMA warps stay converged: every lane walks the loop and
+  // waits, lane 0 alone issues TMA / tcgen05 work (the cluster barrier of the
+  // split-K epilogue is .aligned and needs converged warps).
   if (warp == 0) {
+    // weights first: they do not depend on the previous kernel
+    const CUtensorMap* tw = SWAP ? &tmA : &tmB;
+    const CUtensorMap* tx = SWAP ? &tmB : &tmA;
+    const int w_row = SWAP ? a_row0 : b_row0;
+    const int x_row = SWAP ? b_row0 : a_row0;
+    uint8_t* sW = SWAP ? sA : sB;
+    uint8_t* sX = SWAP ? sB : sA;
+    constexpr uint32_t kW = SWAP ? S::kA : S::kB;
+    constexpr uint32_t kX = SWAP ? S::kB : S::kA;
+    const int pre = min(nkb, STAGES);
     if (lane == 0) {
-      // weights first: they do not depend on the previous kernel
-      const CUtensorMap* tw = SWAP ? &tmA : &tmB;
-      const CUtensorMap* tx = SWAP ? &tmB : &tmA;
-      const int w_row = SWAP ? a_row0 : b_row0;
-      const int x_row = SWAP ? b_row0 : a_row0;
-      uint8_t* sW = SWAP ? sA : sB;
-      uint8_t* sX = SWAP ? sB : sA;
-      constexpr uint32_t kW = SWAP ? S::kA : S::kB;
-      constexpr uint32_t kX = SWAP ? S::kB : S::kA;
-      const int pre = min(nkb, STAGES);
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], S::kA + S::kB);
         tma_load_2d(sW + i * kW, tw, &full[i], (kb0 + i) * BK, w_row);
       }
-      pdl_wait();
+    }
+    pdl_wait();
+    if (lane == 0) {
       trace_stamp(p, 2);
       for (int i = 0; i < pre; ++i) tma_load_2d(sX + i * kX, tx, &full[i], (kb0 + i) * BK, x_row);
-      for (int i = pre; i < nkb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, p.err, 101)) break;
+    }
+    __syncwarp();
+    for (int i = pre; i < nkb; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1u;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u, p.err, 101));
+      if (!ok) break;
+      if (lane == 0) {
         mbar_arrive_expect_tx(&full[s], S::kA + S::kB);
         const int kc = (kb0 + i) * BK;
         tma_load_2d(sW + s * kW, tw, &full[s], kc, w_row);
         tma_load_2d(sX + s * kX, tx, &full[s], kc, x_row);
       }
+      __syncwarp();
     }
   } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t idesc = make_idesc_bf16(BM, BN);
-      for (int i = 0; i < nkb; ++i) {
-        const int s = i % STAGES;
-        const uint32_t ph = (i / STAGES) & 1u;
-        if (!mbar_wait(&full[s], ph, p.err, 102)) break;
+    constexpr uint32_t idesc = make_idesc_bf16(BM, BN);
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % STAGES;
+      const uint32_t ph = (i / STAGES) & 1u;
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.err, 102));
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
         if (i == 0) trace_stamp(p, 3);
-        tc_fence_after();
         const uint32_t a_addr = smem_u32(sA + s * S::kA);
         const uint32_t b_addr = smem_u32(sB + s * S::kB);
 #pragma unroll
@@ -188,8 +199,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         tc_commit(&empty[s]);
       }
-      tc_commit(done);
+      __syncwarp();
     }
+    if (lane == 0) tc_commit(done);
+    __syncwarp();
   }
 
   // ------------------------------------------------------------ epilogue ----
@@ -288,7 +301,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if constexpr (SPLIT) {
-    __syncwarp();  // reconverge the producer / MMA warps before the aligned barrier
+    cluster_sync();  // every CTA of the cluster has parked its partial tile
     // sum the cluster's partial tiles through distributed shared memory: CTA
     // rank r finalises output rows [r * R / S, (r + 1) * R / S) of the tile
     // (R = tokens in the tile), 4 consecutive features per thread and load

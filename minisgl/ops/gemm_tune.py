@@ -24,20 +24,26 @@ Plan = Tuple[int, int, int]  # (mode: 1 token-major / 2 weight-major, n tile, sp
 PLANS: Dict[Tuple[int, int, int], Plan] = {}
 
 
-def candidates(M: int, K: int) -> List[Plan]:
+# batch sizes that are tuned; other sizes use the plan of the next tuned size
+TUNED_SIZES = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
+
+
+def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
+    """Plans worth timing for M tokens and reduction size K (``full`` adds
+    plans that are rarely the best, for exhaustive tests)."""
     num_kb = (K + 63) // 64
     out: List[Plan] = []
     top = 16
     while top < M and top < 256:
         top *= 2
     for bn in (16, 32, 64, 128, 256):
-        if bn > max(top, 16):
-            break
+        if bn > top or (not full and bn < top // 8):
+            continue
         for s in (1, 2, 4, 8, 16):
-            if s <= num_kb and bn % s == 0:
+            if s <= num_kb and bn % s == 0 and (full or s * 2 <= num_kb):
                 out.append((2, bn, s))
-    if M >= 32:
-        for bn in (32, 64, 128, 256):
+    if M >= (32 if full else 128):
+        for bn in (32, 64, 128, 256) if full else (64, 128, 256):
             for s in (1, 2, 4, 8):
                 if s <= num_kb:
                     out.append((1, bn, s))
@@ -80,7 +86,9 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
     key_dev = torch.cuda.get_device_name(device)
     cached = _load(cache_file, key_dev)
     shapes = sorted(set(shapes))
-    sizes = sorted(set(int(m) for m in batch_sizes if m > 0))
+    wanted = sorted(set(int(m) for m in batch_sizes if m > 0))
+    # tune representative sizes only; every wanted size maps to the next one
+    sizes = sorted({next((t for t in TUNED_SIZES if t >= m), m) for m in wanted})
     with torch.cuda.device(device):
         for N, K in shapes:
             w = torch.randn(N, K, device=device, dtype=torch.bfloat16) * 0.02
@@ -93,7 +101,7 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
                     continue
                 x, out = xmax[:M], omax[:M]
                 timed = []
-                for plan in candidates(M, K):
+                for plan in candidates(M, K, full=False):
                     try:
                         timed.append((_time_plan(native, out, x, w, plan), plan))
                     except RuntimeError:
@@ -104,6 +112,12 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
             del w, xmax, omax
     torch.cuda.synchronize(device)
     _save(cache_file, key_dev, cached)
+    # wanted sizes that were not tuned themselves borrow the next tuned plan
+    for N, K in shapes:
+        for m in wanted:
+            t = next((s for s in sizes if s >= m), None)
+            if t is not None and (t, N, K) in PLANS:
+                PLANS.setdefault((m, N, K), PLANS[(t, N, K)])
     return dict(PLANS)
 
 

@@ -70,6 +70,23 @@ def test_gemm_forced_paths(mode, splits):
     ops.check_device_errors(x.device)
 
 
+@pytest.mark.parametrize("M,N,K", [(1, 1024, 1024), (4, 256, 256), (64, 1024, 2048), (200, 512, 3072)])
+def test_gemm_every_plan(M, N, K):
+    """Every (tile orientation, N tile, cluster split) plan is numerically right."""
+    torch.manual_seed(M + N)
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) * 0.05).to(torch.bfloat16)
+    expect = ref.gemm(x, w, None, torch.float32).cpu()
+    from minisgl.ops.gemm_tune import candidates
+
+    for mode, bn, s in candidates(M, K):
+        out = torch.zeros(M, N, device=DEV, dtype=torch.float32)
+        ops.native().gemm(out, x, w, None, None, s, mode, None, bn)
+        torch.cuda.synchronize()
+        err = (out.cpu() - expect).abs().max().item()
+        assert err < 3e-2 * (K / 1024) ** 0.5 + 1e-2, (mode, bn, s, err)
+
+
 def test_gemm_strided_input_fp32_out():
     torch.manual_seed(1)
     big = torch.randn(50, 3072, device=DEV, dtype=torch.bfloat16)
