@@ -16,6 +16,8 @@
 // Softmax runs in the exp2 domain: q is pre-scaled by scale * log2(e).
 #include <algorithm>
 #include <stdexcept>
+#include <string>
+#include <utility>
 
 #include "common.cuh"
 #include "ops.h"
@@ -110,20 +112,39 @@ __device__ __forceinline__ void load_q_frags(uint32_t (&qa)[8][4], const __nv_bf
 }
 
 // ============================================================== decode ====
-// grid (max_splits, hk, B); 4 warps. Warp w handles keys [16w, 16w+16) of
-// each tile for all G = hq / hk query heads of this kv head; the four
-// partial softmax states are merged at the end.
-__global__ void __launch_bounds__(128, 2)
+// grid (max_splits, hk, B); 5 warps. Warps 0-3 consume: warp w handles keys
+// [16w, 16w+16) of each tile for all G = hq / hk query heads of this kv
+// head. Warp 4 produces: it streams 64-key K/V tiles through a 3-stage ring
+// (full barriers completed by TMA bytes, empty barriers by the 4 consumer
+// warps), so no CTA-wide barrier sits in the loop. The four partial softmax
+// states are merged at the end.
+constexpr int kConsumers = 4;
+constexpr int kDecodeThreads = (kConsumers + 1) * 32;
+constexpr int kMergeLd = kD + 4;  // padded row of the merge buffer (floats)
+
+__global__ void __launch_bounds__(kDecodeThreads, 2)
     decode_attn_kernel(const __grid_constant__ CUtensorMap tm, AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
+  uint64_t* empty = full + kStages;
   const ErrorSink err{a.err};
 
+  pdl_launch_dependents();
   const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int G = a.hq / a.hk;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], kConsumers);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tm);
+  }
+  // q, the KV of the current token and the metadata come from earlier kernels
+  pdl_wait();
   const int L = a.seq_lens[b];
   // chunk of keys for this split: a multiple of the tile, at least one tile
   int chunk = (L + a.max_splits - 1) / a.max_splits;
@@ -134,20 +155,7 @@ __global__ void __launch_bounds__(128, 2)
   const int k_end = min(L, k_begin + chunk);
   const int ntiles = k_end > k_begin ? (k_end - k_begin + kTile - 1) / kTile : 0;
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
-
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
-    fence_barrier_init();
-    prefetch_tmap(&tm);
-    for (int i = 0; i < kStages && i < ntiles; ++i)
-      issue_kv_tile(smem + i * kStageBytes, &bars[i], &tm, a, pt_row, L, k_begin + i * kTile, h);
-  }
   __syncthreads();
-
-  const __nv_bfloat16* qb =
-      reinterpret_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(b) * a.ld_q + h * G * kD;
-  uint32_t qa[8][4];
-  load_q_frags(qa, qb, kD, G, a.scale * kLog2e);
 
   const int g = lane >> 2, t = lane & 3;
   float m_lo = -INFINITY, m_hi = -INFINITY;  // running max for rows g and g+8
@@ -156,130 +164,140 @@ __global__ void __launch_bounds__(128, 2)
 #pragma unroll
   for (int n = 0; n < 16; ++n) o[n][0] = o[n][1] = o[n][2] = o[n][3] = 0.f;
 
-  bool ok = true;
-  for (int i = 0; i < ntiles; ++i) {
-    const int s = i % kStages;
-    if (ok) ok = mbar_wait(&bars[s], (i / kStages) & 1u, err, 201);
-    const uint32_t kbase = smem_u32(smem + s * kStageBytes);
-    const uint32_t vbase = kbase + kTileBytes;
+  if (warp == kConsumers) {
+    // ------------------------------------------------------- producer ----
+    if (lane == 0) {
+      for (int i = 0; i < ntiles; ++i) {
+        const int s = i % kStages;
+        if (i >= kStages && !mbar_wait(&empty[s], ((i / kStages) & 1u) ^ 1u, err, 200)) break;
+        issue_kv_tile(smem + s * kStageBytes, &full[s], &tm, a, pt_row, L, k_begin + i * kTile, h);
+      }
+    }
+  } else {
+    // ------------------------------------------------------- consumers ----
+    const __nv_bfloat16* qb =
+        reinterpret_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(b) * a.ld_q + h * G * kD;
+    uint32_t qa[8][4];
+    load_q_frags(qa, qb, kD, G, a.scale * kLog2e);
+    bool ok = true;
+    const int mi = lane >> 3, rr = lane & 7;
     const int tok0 = warp * 16;  // this warp's 16 keys inside the tile
-    // S = Q K^T for 16 rows x 16 keys
-    float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-    {
-      const int mi = lane >> 3, rr = lane & 7;
-      const int tok = tok0 + (mi >> 1) * 8 + rr;
+    for (int i = 0; i < ntiles; ++i) {
+      const int s = i % kStages;
+      if (ok) ok = mbar_wait(&full[s], (i / kStages) & 1u, err, 201);
+      const uint32_t kbase = smem_u32(smem + s * kStageBytes);
+      const uint32_t vbase = kbase + kTileBytes;
+      // S = Q K^T for 16 rows x 16 keys
+      float sc[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+      {
+        const int tok = tok0 + (mi >> 1) * 8 + rr;
 #pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4(kbase + tile_off(tok, ks * 2 + (mi & 1)), b0, b1, b2, b3);
-        mma_bf16(sc[0], qa[ks], b0, b1);
-        mma_bf16(sc[1], qa[ks], b2, b3);
+        for (int ks = 0; ks < 8; ++ks) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4(kbase + tile_off(tok, ks * 2 + (mi & 1)), b0, b1, b2, b3);
+          mma_bf16(sc[0], qa[ks], b0, b1);
+          mma_bf16(sc[1], qa[ks], b2, b3);
+        }
       }
-    }
-    // mask keys past the end of this split
-    const int pos0 = k_begin + i * kTile + tok0;
+      // mask keys past the end of this split
+      const int pos0 = k_begin + i * kTile + tok0;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
+      for (int nt = 0; nt < 2; ++nt) {
 #pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        const int pos = pos0 + nt * 8 + 2 * t + (e & 1);
-        if (pos >= k_end) sc[nt][e] = -INFINITY;
+        for (int e = 0; e < 4; ++e) {
+          const int pos = pos0 + nt * 8 + 2 * t + (e & 1);
+          if (pos >= k_end) sc[nt][e] = -INFINITY;
+        }
       }
-    }
-    // online softmax (rows g: elements 0,1 ; rows g+8: elements 2,3)
-    float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
-    float mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
-    mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
-    mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
-    const float new_lo = fmaxf(m_lo, mx_lo), new_hi = fmaxf(m_hi, mx_hi);
-    const float base_lo = new_lo == -INFINITY ? 0.f : new_lo;
-    const float base_hi = new_hi == -INFINITY ? 0.f : new_hi;
-    const float alpha_lo = exp2f(m_lo - base_lo), alpha_hi = exp2f(m_hi - base_hi);
-    m_lo = new_lo, m_hi = new_hi;
-    float p[2][4];
-    float sum_lo = 0.f, sum_hi = 0.f;
+      // online softmax (rows g: elements 0,1 ; rows g+8: elements 2,3)
+      float mx_lo = fmaxf(fmaxf(sc[0][0], sc[0][1]), fmaxf(sc[1][0], sc[1][1]));
+      float mx_hi = fmaxf(fmaxf(sc[0][2], sc[0][3]), fmaxf(sc[1][2], sc[1][3]));
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 1));
+      mx_lo = fmaxf(mx_lo, __shfl_xor_sync(0xffffffffu, mx_lo, 2));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 1));
+      mx_hi = fmaxf(mx_hi, __shfl_xor_sync(0xffffffffu, mx_hi, 2));
+      const float new_lo = fmaxf(m_lo, mx_lo), new_hi = fmaxf(m_hi, mx_hi);
+      const float base_lo = new_lo == -INFINITY ? 0.f : new_lo;
+      const float base_hi = new_hi == -INFINITY ? 0.f : new_hi;
+      const float alpha_lo = exp2f(m_lo - base_lo), alpha_hi = exp2f(m_hi - base_hi);
+      m_lo = new_lo, m_hi = new_hi;
+      float p[2][4];
+      float sum_lo = 0.f, sum_hi = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < 2; ++nt) {
-      p[nt][0] = exp2f(sc[nt][0] - base_lo);
-      p[nt][1] = exp2f(sc[nt][1] - base_lo);
-      p[nt][2] = exp2f(sc[nt][2] - base_hi);
-      p[nt][3] = exp2f(sc[nt][3] - base_hi);
-      sum_lo += p[nt][0] + p[nt][1];
-      sum_hi += p[nt][2] + p[nt][3];
-    }
-    l_lo = l_lo * alpha_lo + sum_lo;
-    l_hi = l_hi * alpha_hi + sum_hi;
-#pragma unroll
-    for (int n = 0; n < 16; ++n) {
-      o[n][0] *= alpha_lo, o[n][1] *= alpha_lo;
-      o[n][2] *= alpha_hi, o[n][3] *= alpha_hi;
-    }
-    uint32_t pa[4];
-    pa[0] = pack_bf16x2(p[0][0], p[0][1]);
-    pa[1] = pack_bf16x2(p[0][2], p[0][3]);
-    pa[2] = pack_bf16x2(p[1][0], p[1][1]);
-    pa[3] = pack_bf16x2(p[1][2], p[1][3]);
-    // O += P V   (V rows tok0..tok0+15, all 128 columns)
-    {
-      const int mi = lane >> 3, rr = lane & 7;
-      const int tok = tok0 + (mi & 1) * 8 + rr;
-#pragma unroll
-      for (int nd = 0; nd < 16; nd += 2) {
-        uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(vbase + tile_off(tok, nd + (mi >> 1)), b0, b1, b2, b3);
-        mma_bf16(o[nd], pa, b0, b1);
-        mma_bf16(o[nd + 1], pa, b2, b3);
+      for (int nt = 0; nt < 2; ++nt) {
+        p[nt][0] = exp2f(sc[nt][0] - base_lo);
+        p[nt][1] = exp2f(sc[nt][1] - base_lo);
+        p[nt][2] = exp2f(sc[nt][2] - base_hi);
+        p[nt][3] = exp2f(sc[nt][3] - base_hi);
+        sum_lo += p[nt][0] + p[nt][1];
+        sum_hi += p[nt][2] + p[nt][3];
       }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0 && i + kStages < ntiles) {
-      fence_proxy_async_smem();
-      issue_kv_tile(smem + s * kStageBytes, &bars[s], &tm, a, pt_row, L,
-                    k_begin + (i + kStages) * kTile, h);
+      l_lo = l_lo * alpha_lo + sum_lo;
+      l_hi = l_hi * alpha_hi + sum_hi;
+#pragma unroll
+      for (int n = 0; n < 16; ++n) {
+        o[n][0] *= alpha_lo, o[n][1] *= alpha_lo;
+        o[n][2] *= alpha_hi, o[n][3] *= alpha_hi;
+      }
+      uint32_t pa[4];
+      pa[0] = pack_bf16x2(p[0][0], p[0][1]);
+      pa[1] = pack_bf16x2(p[0][2], p[0][3]);
+      pa[2] = pack_bf16x2(p[1][0], p[1][1]);
+      pa[3] = pack_bf16x2(p[1][2], p[1][3]);
+      // O += P V   (V rows tok0..tok0+15, all 128 columns)
+      {
+        const int tok = tok0 + (mi & 1) * 8 + rr;
+#pragma unroll
+        for (int nd = 0; nd < 16; nd += 2) {
+          uint32_t b0, b1, b2, b3;
+          ldsm_x4_t(vbase + tile_off(tok, nd + (mi >> 1)), b0, b1, b2, b3);
+          mma_bf16(o[nd], pa, b0, b1);
+          mma_bf16(o[nd + 1], pa, b2, b3);
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);  // this warp is done with stage s
     }
   }
 
-  // ---- merge the four warps' partial states (rows < G) through shared memory
+  // ---- merge the four consumer warps' partial states (rows < G)
   l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 1);
   l_lo += __shfl_xor_sync(0xffffffffu, l_lo, 2);
   l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 1);
   l_hi += __shfl_xor_sync(0xffffffffu, l_hi, 2);
-  __syncthreads();  // pipeline buffers are free now
-  float* so = reinterpret_cast<float*>(smem);           // [4 warps][16 rows][128]
-  float* sm = so + 4 * 16 * kD;                          // [4][16]
-  float* sl = sm + 4 * 16;                               // [4][16]
+  __syncthreads();  // every tile consumed: the ring buffers are free now
+  float* so = reinterpret_cast<float*>(smem);           // [4 warps][16 rows][kMergeLd]
+  float* sm = so + kConsumers * 16 * kMergeLd;           // [4][16]
+  float* sl = sm + kConsumers * 16;                      // [4][16]
+  if (warp < kConsumers) {
 #pragma unroll
-  for (int n = 0; n < 16; ++n) {
-    const int col = n * 8 + 2 * t;
-    so[(warp * 16 + g) * kD + col] = o[n][0];
-    so[(warp * 16 + g) * kD + col + 1] = o[n][1];
-    so[(warp * 16 + g + 8) * kD + col] = o[n][2];
-    so[(warp * 16 + g + 8) * kD + col + 1] = o[n][3];
-  }
-  if (t == 0) {
-    sm[warp * 16 + g] = m_lo;
-    sm[warp * 16 + g + 8] = m_hi;
-    sl[warp * 16 + g] = l_lo;
-    sl[warp * 16 + g + 8] = l_hi;
+    for (int n = 0; n < 16; ++n) {
+      const int col = n * 8 + 2 * t;
+      *reinterpret_cast<float2*>(so + (warp * 16 + g) * kMergeLd + col) = make_float2(o[n][0], o[n][1]);
+      *reinterpret_cast<float2*>(so + (warp * 16 + g + 8) * kMergeLd + col) = make_float2(o[n][2], o[n][3]);
+    }
+    if (t == 0) {
+      sm[warp * 16 + g] = m_lo;
+      sm[warp * 16 + g + 8] = m_hi;
+      sl[warp * 16 + g] = l_lo;
+      sl[warp * 16 + g + 8] = l_hi;
+    }
   }
   __syncthreads();
-  // each warp finishes rows warp, warp+4, ... (< G); lane covers 4 columns
-  for (int r = warp; r < G; r += 4) {
+  // each consumer warp finishes rows warp, warp+4, ... (< G); lane covers 4 columns
+  for (int r = warp; r < G && warp < kConsumers; r += kConsumers) {
     float mx = -INFINITY;
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, sm[w * 16 + r]);
+    for (int w = 0; w < kConsumers; ++w) mx = fmaxf(mx, sm[w * 16 + r]);
     const float base = mx == -INFINITY ? 0.f : mx;
-    float lsum = 0.f, f[4];
-    for (int w = 0; w < 4; ++w) {
+    float lsum = 0.f, f[kConsumers];
+    for (int w = 0; w < kConsumers; ++w) {
       f[w] = exp2f(sm[w * 16 + r] - base);
       lsum += sl[w * 16 + r] * f[w];
     }
     float acc[4] = {0.f, 0.f, 0.f, 0.f};
-    for (int w = 0; w < 4; ++w) {
-      const float* src = so + (w * 16 + r) * kD + lane * 4;
-#pragma unroll
-      for (int c = 0; c < 4; ++c) acc[c] += src[c] * f[w];
+    for (int w = 0; w < kConsumers; ++w) {
+      const float4 v = *reinterpret_cast<const float4*>(so + (w * 16 + r) * kMergeLd + lane * 4);
+      acc[0] += v.x * f[w], acc[1] += v.y * f[w], acc[2] += v.z * f[w], acc[3] += v.w * f[w];
     }
     const float inv = lsum > 0.f ? 1.f / lsum : 0.f;
     const int qh = h * G + r;
@@ -303,6 +321,8 @@ __global__ void __launch_bounds__(128, 2)
 
 // Merge split-KV partials: grid (B), block = 32 * 4 threads, warp per head.
 __global__ void decode_combine_kernel(AttnArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int b = blockIdx.y;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int qh = blockIdx.x * 4 + warp;
@@ -344,6 +364,8 @@ __global__ void __launch_bounds__(128, 2)
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * kStageBytes);
   const ErrorSink err{a.err};
 
+  pdl_launch_dependents();
+  pdl_wait();
   const int qt = blockIdx.x, qh = blockIdx.y, b = blockIdx.z;
   const int q_begin = a.cu_q[b];
   const int q_len = a.cu_q[b + 1] - q_begin;
@@ -490,6 +512,27 @@ __global__ void __launch_bounds__(128, 2)
 }
 
 constexpr int kAttnSmem = kStages * kStageBytes + 1024 + 128;
+static_assert(kConsumers * 16 * kMergeLd * 4 + 2 * kConsumers * 16 * 4 <= kStages * kStageBytes,
+              "merge buffer must fit in the ring");
+
+// Launch with programmatic stream serialization (the kernel calls
+// griddepcontrol.wait before touching data produced upstream).
+template <typename... KArgs, typename... Args>
+void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("minisgl.attention launch failed: ") + cudaGetErrorString(e));
+}
 
 CUtensorMap pool_map(const AttnArgs& a) {
   const uint32_t box_rows = a.page_size < kTile ? a.page_size : kTile;
@@ -526,10 +569,10 @@ void launch_decode_attention(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tm = pool_map(a);
   set_smem_once<0>(decode_attn_kernel);
   dim3 grid(std::max(1, a.max_splits), a.hk, a.B);
-  decode_attn_kernel<<<grid, 128, kAttnSmem, s>>>(tm, a);
+  launch_pdl(decode_attn_kernel, grid, dim3(kDecodeThreads), kAttnSmem, s, tm, a);
   if (a.max_splits > 1) {
     dim3 g2((a.hq + 3) / 4, a.B);
-    decode_combine_kernel<<<g2, 128, 0, s>>>(a);
+    launch_pdl(decode_combine_kernel, g2, dim3(128), 0, s, a);
   }
 }
 
@@ -539,7 +582,7 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
   CUtensorMap tm = pool_map(a);
   set_smem_once<1>(prefill_attn_kernel);
   dim3 grid((a.max_q + 63) / 64, a.hq, a.B);
-  prefill_attn_kernel<<<grid, 128, kAttnSmem, s>>>(tm, a);
+  launch_pdl(prefill_attn_kernel, grid, dim3(128), kAttnSmem, s, tm, a);
 }
 
 }  // namespace minisgl

@@ -57,6 +57,7 @@ constexpr int kMaxVecs = 4;
 template <typename T>
 __global__ void rmsnorm_kernel(T* __restrict__ out, const T* __restrict__ x,
                                const T* __restrict__ w, int cols, int ld_x, int ld_out, float eps) {
+  pdl_launch_dependents();  // let a following PDL kernel start its prologue
   constexpr int V = Vec<T>::N;
   __shared__ float red[32];
   const int row = blockIdx.x;
@@ -90,6 +91,7 @@ __global__ void rmsnorm_kernel(T* __restrict__ out, const T* __restrict__ x,
 template <typename T>
 __global__ void fused_add_rmsnorm_kernel(T* __restrict__ x, T* __restrict__ res,
                                          const T* __restrict__ w, int cols, float eps) {
+  pdl_launch_dependents();  // let a following PDL kernel start its prologue
   constexpr int V = Vec<T>::N;
   __shared__ float red[32];
   const int row = blockIdx.x;
@@ -133,6 +135,7 @@ __device__ __forceinline__ float gelu(float x) { return 0.5f * x * (1.f + erff(x
 
 template <typename T, int ACT>
 __global__ void act_and_mul_kernel(T* __restrict__ out, const T* __restrict__ x, int rows, int d) {
+  pdl_launch_dependents();  // let a following PDL kernel start its prologue
   constexpr int V = Vec<T>::N;
   const int nvec = d / V;
   const int64_t total = static_cast<int64_t>(rows) * nvec;
@@ -152,6 +155,7 @@ __global__ void act_and_mul_kernel(T* __restrict__ out, const T* __restrict__ x,
 template <typename T>
 __global__ void embedding_kernel(T* __restrict__ out, const T* __restrict__ w,
                                  const int32_t* __restrict__ ids, int hidden, int lo, int n) {
+  pdl_launch_dependents();  // let a following PDL kernel start its prologue
   constexpr int V = Vec<T>::N;
   const int row = blockIdx.x;
   const int id = ids[row] - lo;

@@ -20,6 +20,7 @@ namespace {
 
 template <typename T, int D>
 __global__ void rope_store_kernel(RopeStoreArgs a) {
+  pdl_launch_dependents();  // let a following PDL kernel start its prologue
   constexpr int E = D / 32;  // elements per lane (contiguous)
   const int warps_per_block = blockDim.x >> 5;
   const int item = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
