@@ -13,9 +13,11 @@
 //     counts elements; for top-p it accumulates exp((l - max) / T) mass and
 //     stops at the bucket where the mass from the top reaches p * Z. Gumbel-max
 //     restricted to the kept set then draws the token.
-// Random numbers: a counter-based generator, the SplitMix64 finaliser of
-// Steele, Lea and Flood ("Fast splittable pseudorandom number generators",
-// OOPSLA 2014) applied to (seed, step, row, column).
+// Random numbers: counter based. A per-row key comes from the SplitMix64
+// finaliser (Steele, Lea and Flood, "Fast splittable pseudorandom number
+// generators", OOPSLA 2014) of (seed, step, row); each column's 24-bit
+// uniform is the 32-bit MurmurHash3 finaliser (Appleby) of key ^ (column *
+// golden ratio), two multiplies per element so the pass stays memory bound.
 #include <stdexcept>
 
 #include "common.cuh"
@@ -32,11 +34,23 @@ __device__ __forceinline__ uint64_t mix64(uint64_t z) {
   return z ^ (z >> 31);
 }
 
+__device__ __forceinline__ uint32_t row_key(uint64_t seed, uint64_t step, int row) {
+  return static_cast<uint32_t>(mix64(seed ^ mix64(step * 0x9e3779b97f4a7c15ull + static_cast<uint64_t>(row))));
+}
+
+__device__ __forceinline__ uint32_t fmix32(uint32_t h) {
+  h ^= h >> 16;
+  h *= 0x85ebca6bu;
+  h ^= h >> 13;
+  h *= 0xc2b2ae35u;
+  h ^= h >> 16;
+  return h;
+}
+
 // uniform in (0, 1)
-__device__ __forceinline__ float uniform(uint64_t seed, uint64_t step, int row, int col) {
-  const uint64_t key = mix64(seed ^ mix64(step * 0x9e3779b97f4a7c15ull + static_cast<uint64_t>(row)));
-  const uint64_t r = mix64(key + static_cast<uint64_t>(col) * 0x9e3779b97f4a7c15ull);
-  return (static_cast<float>(r >> 40) + 0.5f) * (1.0f / 16777216.0f);
+__device__ __forceinline__ float uniform(uint32_t key, int col) {
+  const uint32_t r = fmix32(key ^ (static_cast<uint32_t>(col) * 0x9e3779b9u));
+  return (static_cast<float>(r >> 8) + 0.5f) * (1.0f / 16777216.0f);
 }
 
 // order-preserving map of fp32 to uint32 (larger float -> larger key)
@@ -168,12 +182,27 @@ __global__ void sample_kernel(SampleArgs a) {
     }
   }
   ArgMax best{-INFINITY, 0x7fffffff};
-  for (int i = threadIdx.x; i < V; i += blockDim.x) {
-    const float l = row[i];
-    if (fkey(l) < floor_key) continue;
-    const float u = uniform(a.seed, step, r, i);
-    const float gumbel = -__logf(-__logf(u));
-    best = better(best, ArgMax{l * inv_t + gumbel, i});
+  const uint32_t key = row_key(a.seed, step, r);
+  if ((V & 3) == 0 && (a.ld & 3) == 0) {
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+    for (int i4 = threadIdx.x; i4 < V / 4; i4 += blockDim.x) {
+      const float4 l4 = row4[i4];
+      const float ls[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int i = i4 * 4 + q;
+        if (fkey(ls[q]) < floor_key) continue;
+        const float gumbel = -__logf(-__logf(uniform(key, i)));
+        best = better(best, ArgMax{ls[q] * inv_t + gumbel, i});
+      }
+    }
+  } else {
+    for (int i = threadIdx.x; i < V; i += blockDim.x) {
+      const float l = row[i];
+      if (fkey(l) < floor_key) continue;
+      const float gumbel = -__logf(-__logf(uniform(key, i)));
+      best = better(best, ArgMax{l * inv_t + gumbel, i});
+    }
   }
   best = block_argmax(best);
   if (threadIdx.x == 0) a.out[r] = best.i == 0x7fffffff ? 0 : best.i;
