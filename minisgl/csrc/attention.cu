@@ -15,11 +15,15 @@
 //
 // Softmax runs in the exp2 domain: q is pre-scaled by scale * log2(e).
 #include <algorithm>
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
 #include <stdexcept>
 #include <string>
 #include <utility>
 
 #include "common.cuh"
+#include "noalloc.h"
 #include "ops.h"
 #include "tma_host.h"
 
@@ -586,3 +590,205 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
 }
 
 }  // namespace minisgl
+
+// ====================================================== allocation-free ====
+// minisgl_decode_attention_noalloc (declared in noalloc.h): the split-KV
+// decode above with its scratch in a fixed device array instead of caller
+// buffers. Nothing here allocates: argument errors are reported through the
+// return code and a caller-owned message buffer, the tensor map is encoded on
+// the stack, and launches go straight to cudaLaunchKernelEx.
+
+namespace minisgl {
+namespace {
+
+constexpr size_t kNoAllocFloats = MINISGL_NOALLOC_SCRATCH_BYTES / sizeof(float);
+static_assert(MINISGL_NOALLOC_SCRATCH_BYTES % 256 == 0, "scratch size must keep 256-byte alignment");
+
+// Shared by every call on a device; see noalloc.h for the race rule.
+static __device__ __align__(256) float g_decode_scratch[kNoAllocFloats];
+
+constexpr int kNoAllocMaxDevices = 64;
+constexpr int kNoAllocMaxSplits = 16;
+
+struct NoAllocDeviceState {
+  float* scratch = nullptr;  // device address of g_decode_scratch
+  bool ready = false;
+};
+NoAllocDeviceState g_noalloc_state[kNoAllocMaxDevices];
+std::mutex g_noalloc_mu;
+PFN_cuTensorMapEncodeTiled_v12000 g_noalloc_encode = nullptr;
+
+int noalloc_fail(char* msg, size_t msg_len, int code, const char* fmt, ...) {
+  if (msg != nullptr && msg_len > 0) {
+    va_list ap;
+    va_start(ap, fmt);
+    std::vsnprintf(msg, msg_len, fmt, ap);
+    va_end(ap);
+  }
+  return code;
+}
+
+// Once per device, with that device current: look up the scratch array and
+// the tensor-map encoder, and raise the kernel's shared-memory limit.
+int noalloc_setup(int dev, float** scratch, char* msg, size_t msg_len) {
+  std::lock_guard<std::mutex> lock(g_noalloc_mu);
+  NoAllocDeviceState& st = g_noalloc_state[dev];
+  if (st.ready) {
+    *scratch = st.scratch;
+    return MINISGL_NOALLOC_OK;
+  }
+  if (g_noalloc_encode == nullptr) {
+    void* fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+    if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || fn == nullptr)
+      return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA,
+                          "minisgl_decode_attention_noalloc: cuTensorMapEncodeTiled unavailable (%s)",
+                          cudaGetErrorString(e));
+    g_noalloc_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  }
+  void* ptr = nullptr;
+  cudaError_t e = cudaGetSymbolAddress(&ptr, g_decode_scratch);
+  if (e != cudaSuccess || ptr == nullptr)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA,
+                        "minisgl_decode_attention_noalloc: cudaGetSymbolAddress failed on device %d: %s", dev,
+                        cudaGetErrorString(e));
+  if ((reinterpret_cast<uintptr_t>(ptr) & 255) != 0)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA,
+                        "minisgl_decode_attention_noalloc: scratch array is not 256-byte aligned");
+  e = cudaFuncSetAttribute(decode_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kAttnSmem);
+  if (e != cudaSuccess)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA,
+                        "minisgl_decode_attention_noalloc: cannot set shared memory limit: %s",
+                        cudaGetErrorString(e));
+  st.scratch = static_cast<float*>(ptr);
+  st.ready = true;
+  *scratch = st.scratch;
+  return MINISGL_NOALLOC_OK;
+}
+
+template <typename... KArgs, typename... Args>
+cudaError_t noalloc_launch(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                           Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr;
+  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr.val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = &attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
+}
+
+}  // namespace
+}  // namespace minisgl
+
+extern "C" __attribute__((visibility("default"))) int minisgl_decode_attention_noalloc(
+    void* out, const void* q, int ld_q, const void* kv_pool, int num_layers, int num_pages, int layer,
+    const int32_t* page_table, int ld_pt, const int32_t* req_rows, const int32_t* seq_lens, int B, int hq,
+    int hk, int d, int page_size, float scale, int max_splits, int* err, void* stream, char* msg,
+    size_t msg_len) {
+  using namespace minisgl;
+  constexpr const char* kName = "minisgl_decode_attention_noalloc";
+  if (msg != nullptr && msg_len > 0) msg[0] = '\0';
+  if (B <= 0) return MINISGL_NOALLOC_OK;
+  // ---- argument checks (the same rules as the regular entry point)
+  if (out == nullptr || q == nullptr || kv_pool == nullptr || page_table == nullptr || req_rows == nullptr ||
+      seq_lens == nullptr)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: a required pointer is NULL", kName);
+  if (d != kD) return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: head_dim must be 128 (got %d)", kName, d);
+  if (hk <= 0 || hq <= 0 || hq % hk != 0 || hq / hk > 16)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL,
+                        "%s: need hq %% hk == 0 and a GQA group of at most 16 (hq=%d hk=%d)", kName, hq, hk);
+  if (page_size < 16 || (page_size & (page_size - 1)) != 0)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: page_size must be a power of two >= 16 (got %d)",
+                        kName, page_size);
+  if (num_layers <= 0 || num_pages <= 0 || layer < 0 || layer >= num_layers)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: layer %d out of range for %d layers", kName, layer,
+                        num_layers);
+  if (max_splits < 1 || max_splits > kNoAllocMaxSplits)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: max_splits must be in [1, %d] (got %d)", kName,
+                        kNoAllocMaxSplits, max_splits);
+  if (ld_q < hq * d || (ld_q & 7) != 0)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: ld_q must be >= hq*d and a multiple of 8 (got %d)",
+                        kName, ld_q);
+  if (((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(out) | reinterpret_cast<uintptr_t>(kv_pool)) &
+       15) != 0)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: q, out and kv_pool must be 16-byte aligned", kName);
+  const int64_t rows_per_layer = static_cast<int64_t>(num_pages) * hk * page_size;
+  const int64_t pool_rows = 2 * static_cast<int64_t>(num_layers) * rows_per_layer;
+  if (pool_rows >= (int64_t(1) << 31))
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: KV pool too large for int32 rows", kName);
+  // ---- scratch size against the fixed array
+  const uint64_t lse_floats = static_cast<uint64_t>(B) * hq * max_splits;
+  const uint64_t o_floats = lse_floats * d;
+  const uint64_t o_padded = (o_floats + 63) / 64 * 64;  // part_lse starts on a 256-byte boundary
+  const uint64_t need = max_splits > 1 ? o_padded + lse_floats : 0;
+  if (need > kNoAllocFloats)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ETOOLARGE,
+                        "%s: split-KV scratch of %llu bytes exceeds the fixed %u-byte array "
+                        "(B=%d hq=%d max_splits=%d); lower max_splits or split the batch",
+                        kName, static_cast<unsigned long long>(need * sizeof(float)),
+                        static_cast<unsigned>(MINISGL_NOALLOC_SCRATCH_BYTES), B, hq, max_splits);
+  // ---- per-device set-up (first call on the device)
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA, "%s: cudaGetDevice failed: %s", kName,
+                        cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoAllocMaxDevices)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA, "%s: device index %d not supported", kName, dev);
+  float* scratch = nullptr;
+  const int rc = noalloc_setup(dev, &scratch, msg, msg_len);
+  if (rc != MINISGL_NOALLOC_OK) return rc;
+  // ---- tensor map over the whole pool, encoded on the stack (no cache)
+  CUtensorMap tm;
+  {
+    const uint32_t box_rows = page_size < kTile ? page_size : kTile;
+    cuuint64_t gdim[2] = {static_cast<cuuint64_t>(d), static_cast<cuuint64_t>(pool_rows)};
+    cuuint64_t gstride[1] = {static_cast<cuuint64_t>(d) * 2};
+    cuuint32_t bdim[2] = {64, box_rows};
+    cuuint32_t estride[2] = {1, 1};
+    const CUresult r = g_noalloc_encode(&tm, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(kv_pool), gdim,
+                                        gstride, bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                                        CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+      return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA, "%s: cuTensorMapEncodeTiled failed with code %d", kName,
+                          static_cast<int>(r));
+  }
+  AttnArgs a{};
+  a.q = q;
+  a.ld_q = ld_q;
+  a.out = out;
+  a.kv_pool = kv_pool;
+  a.pool_rows = pool_rows;
+  a.k_row0 = layer * rows_per_layer;
+  a.v_row0 = (static_cast<int64_t>(num_layers) + layer) * rows_per_layer;
+  a.page_table = page_table;
+  a.ld_pt = ld_pt;
+  a.req_rows = req_rows;
+  a.seq_lens = seq_lens;
+  a.cu_q = nullptr;
+  a.B = B;
+  a.hq = hq;
+  a.hk = hk;
+  a.d = d;
+  a.page_size = page_size;
+  a.max_q = 1;
+  a.scale = scale;
+  a.max_splits = max_splits;
+  a.part_o = max_splits > 1 ? scratch : nullptr;
+  a.part_lse = max_splits > 1 ? scratch + o_padded : nullptr;
+  a.err = err;
+  const cudaStream_t s = static_cast<cudaStream_t>(stream);
+  e = noalloc_launch(decode_attn_kernel, dim3(max_splits, hk, B), dim3(kDecodeThreads), kAttnSmem, s, tm, a);
+  if (e == cudaSuccess && max_splits > 1)
+    e = noalloc_launch(decode_combine_kernel, dim3((hq + 3) / 4, B), dim3(128), 0, s, a);
+  if (e != cudaSuccess)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_ECUDA, "%s: launch failed: %s", kName, cudaGetErrorString(e));
+  return MINISGL_NOALLOC_OK;
+}
