@@ -35,18 +35,9 @@ MAX_SPLITS = 16
 
 
 def decode_splits(batch_size: int, kv_heads: int) -> int:
-    """Splits per (request, kv head). The decode kernel runs two CTAs per SM,
-    so work is issued in waves of 2 * 148 CTAs; pick the split count whose
-    last wave is fullest (relative time ceil(waves) / splits), with a small
-    charge per extra split for the partial-result traffic and the combine."""
-    slots = 2 * NUM_SMS
-    n = max(1, batch_size * kv_heads)
-    best, best_cost = 1, float("inf")
-    for s in range(1, MAX_SPLITS + 1):
-        cost = math.ceil(n * s / slots) / s * (1.0 + 0.03 * (s - 1))
-        if cost < best_cost - 1e-9:
-            best, best_cost = s, cost
-    return best
+    """Splits per (request, kv head) so that about two CTAs run per SM."""
+    want = math.ceil(2 * NUM_SMS / max(1, batch_size * kv_heads))
+    return max(1, min(MAX_SPLITS, want))
 
 
 @dataclass

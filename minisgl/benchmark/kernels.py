@@ -68,6 +68,30 @@ def bench_decode_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) -
             "ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
 
 
+def bench_decode_attention_varlen(B: int, lo: int, hi: int, hq: int, hk: int, page: int, peaks) -> List[Dict]:
+    """Mixed lengths U[lo, hi], the serving mix (bytes: the keys that exist)."""
+    d = 128
+    g = random.Random(1)
+    lens = [g.randint(lo, hi) for _ in range(B)]
+    pool, pt, rows = _pool(lens, hk, d, page)
+    seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    q = torch.randn(B, hq * d, device="cuda", dtype=torch.bfloat16)
+    from minisgl.attention.native import MAX_SPLITS, decode_splits
+
+    splits = decode_splits(B, hk)
+    part_o = torch.empty(B * hq * MAX_SPLITS * d, device="cuda")
+    part_lse = torch.empty(B * hq * MAX_SPLITS, device="cuda")
+    nbytes = 2 * sum(lens) * hk * d * 2
+    out = []
+    ms = time_kernel(lambda: ops.decode_attention(q, pool, 0, pt, rows, seq, hq, hk, d, page, d ** -0.5,
+                                                  part_o, part_lse, splits))
+    gbs = nbytes / ms / 1e6
+    out.append({"kernel": "decode_attention_varlen", "B": B, "L": f"U[{lo},{hi}]", "hq": hq, "hk": hk,
+                "page": page, "splits": splits, "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)})
+    return out
+
+
 def bench_prefill_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) -> Dict:
     d = 128
     lens = [L] * B
@@ -136,6 +160,9 @@ def main() -> None:
     cases = []
     for B, L in [(256, 800), (128, 800), (32, 2000), (1, 4000)]:
         cases.append((f"decode_attention B={B} L={L}", lambda B=B, L=L: bench_decode_attention(B, L, 16, 8, 64, peaks)))
+    for B, lo, hi in [(256, 200, 2000), (64, 200, 2000), (8, 500, 4000), (1, 4000, 4000)]:
+        cases.append((f"decode_attention varlen B={B}",
+                      lambda B=B, lo=lo, hi=hi: bench_decode_attention_varlen(B, lo, hi, 16, 8, 64, peaks)))
     cases.append(("decode_attention qwen3-32b", lambda: bench_decode_attention(64, 2000, 64, 8, 64, peaks)))
     cases.append(("decode_attention qwen3-32b tp8", lambda: bench_decode_attention(64, 2000, 8, 1, 64, peaks)))
     cases.append(("prefill_attention", lambda: bench_prefill_attention(16, 1024, 16, 8, 64, peaks)))

@@ -23,6 +23,7 @@
 #include <utility>
 
 #include "common.cuh"
+#include "launch.h"
 #include "noalloc.h"
 #include "ops.h"
 #include "tma_host.h"
@@ -518,25 +519,6 @@ __global__ void __launch_bounds__(128, 2)
 constexpr int kAttnSmem = kStages * kStageBytes + 1024 + 128;
 static_assert(kConsumers * 16 * kMergeLd * 4 + 2 * kConsumers * 16 * 4 <= kStages * kStageBytes,
               "merge buffer must fit in the ring");
-
-// Launch with programmatic stream serialization (the kernel calls
-// griddepcontrol.wait before touching data produced upstream).
-template <typename... KArgs, typename... Args>
-void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
-                Args&&... args) {
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = grid;
-  cfg.blockDim = block;
-  cfg.dynamicSmemBytes = smem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr;
-  attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr.val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = &attr;
-  cfg.numAttrs = 1;
-  cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
-  if (e != cudaSuccess) throw std::runtime_error(std::string("minisgl.attention launch failed: ") + cudaGetErrorString(e));
-}
 
 CUtensorMap pool_map(const AttnArgs& a) {
   const uint32_t box_rows = a.page_size < kTile ? a.page_size : kTile;

@@ -12,6 +12,7 @@
 #include <stdexcept>
 
 #include "common.cuh"
+#include "launch.h"
 #include "ops.h"
 
 namespace minisgl {
@@ -58,6 +59,7 @@ template <typename T>
 __global__ void rmsnorm_kernel(T* __restrict__ out, const T* __restrict__ x,
                                const T* __restrict__ w, int cols, int ld_x, int ld_out, float eps) {
   pdl_launch_dependents();  // let a following PDL kernel start its prologue
+  pdl_wait();               // inputs come from the previous kernel
   constexpr int V = Vec<T>::N;
   __shared__ float red[32];
   const int row = blockIdx.x;
@@ -92,6 +94,7 @@ template <typename T>
 __global__ void fused_add_rmsnorm_kernel(T* __restrict__ x, T* __restrict__ res,
                                          const T* __restrict__ w, int cols, float eps) {
   pdl_launch_dependents();  // let a following PDL kernel start its prologue
+  pdl_wait();               // inputs come from the previous kernel
   constexpr int V = Vec<T>::N;
   __shared__ float red[32];
   const int row = blockIdx.x;
@@ -136,6 +139,7 @@ __device__ __forceinline__ float gelu(float x) { return 0.5f * x * (1.f + erff(x
 template <typename T, int ACT>
 __global__ void act_and_mul_kernel(T* __restrict__ out, const T* __restrict__ x, int rows, int d) {
   pdl_launch_dependents();  // let a following PDL kernel start its prologue
+  pdl_wait();               // inputs come from the previous kernel
   constexpr int V = Vec<T>::N;
   const int nvec = d / V;
   const int64_t total = static_cast<int64_t>(rows) * nvec;
@@ -156,6 +160,7 @@ template <typename T>
 __global__ void embedding_kernel(T* __restrict__ out, const T* __restrict__ w,
                                  const int32_t* __restrict__ ids, int hidden, int lo, int n) {
   pdl_launch_dependents();  // let a following PDL kernel start its prologue
+  pdl_wait();               // inputs come from the previous kernel
   constexpr int V = Vec<T>::N;
   const int row = blockIdx.x;
   const int id = ids[row] - lo;
@@ -193,8 +198,8 @@ void launch_rmsnorm(void* out, const void* x, const void* w, int rows, int cols,
     using T = decltype(tag);
     constexpr int V = Vec<T>::N;
     if (cols % V != 0 || cols > kMaxVecs * 1024 * V) throw std::runtime_error("minisgl.rmsnorm: unsupported width");
-    rmsnorm_kernel<T><<<rows, norm_threads(cols, V), 0, s>>>(
-        static_cast<T*>(out), static_cast<const T*>(x), static_cast<const T*>(w), cols, ld_x, ld_out, eps);
+    launch_pdl(rmsnorm_kernel<T>, dim3(rows), dim3(norm_threads(cols, V)), 0, s, static_cast<T*>(out),
+               static_cast<const T*>(x), static_cast<const T*>(w), cols, ld_x, ld_out, eps);
   });
 }
 
@@ -205,8 +210,8 @@ void launch_fused_add_rmsnorm(void* x, void* residual, const void* w, int rows, 
     using T = decltype(tag);
     constexpr int V = Vec<T>::N;
     if (cols % V != 0 || cols > kMaxVecs * 1024 * V) throw std::runtime_error("minisgl.rmsnorm: unsupported width");
-    fused_add_rmsnorm_kernel<T><<<rows, norm_threads(cols, V), 0, s>>>(
-        static_cast<T*>(x), static_cast<T*>(residual), static_cast<const T*>(w), cols, eps);
+    launch_pdl(fused_add_rmsnorm_kernel<T>, dim3(rows), dim3(norm_threads(cols, V)), 0, s, static_cast<T*>(x),
+               static_cast<T*>(residual), static_cast<const T*>(w), cols, eps);
   });
 }
 
@@ -221,9 +226,11 @@ void launch_act_and_mul(void* out, const void* x, int rows, int d, int act, DTyp
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, 148 * 16));
     if (act == 0)
-      act_and_mul_kernel<T, 0><<<blocks, threads, 0, s>>>(static_cast<T*>(out), static_cast<const T*>(x), rows, d);
+      launch_pdl(act_and_mul_kernel<T, 0>, dim3(blocks), dim3(threads), 0, s, static_cast<T*>(out),
+                 static_cast<const T*>(x), rows, d);
     else
-      act_and_mul_kernel<T, 1><<<blocks, threads, 0, s>>>(static_cast<T*>(out), static_cast<const T*>(x), rows, d);
+      launch_pdl(act_and_mul_kernel<T, 1>, dim3(blocks), dim3(threads), 0, s, static_cast<T*>(out),
+                 static_cast<const T*>(x), rows, d);
   });
 }
 
@@ -235,8 +242,8 @@ void launch_embedding(void* out, const void* w, const int32_t* ids, int num_toke
     constexpr int V = Vec<T>::N;
     if (hidden % V != 0) throw std::runtime_error("minisgl.embedding: hidden must be a multiple of 16 bytes");
     const int threads = std::min(256, std::max(32, (hidden / V + 31) / 32 * 32));
-    embedding_kernel<T><<<num_tokens, threads, 0, s>>>(static_cast<T*>(out), static_cast<const T*>(w), ids,
-                                                       hidden, vocab_lo, vocab_n);
+    launch_pdl(embedding_kernel<T>, dim3(num_tokens), dim3(threads), 0, s, static_cast<T*>(out),
+               static_cast<const T*>(w), ids, hidden, vocab_lo, vocab_n);
   });
 }
 

@@ -52,6 +52,7 @@ struct KParams {
   int ldo;
   int kb_per_split;
   int num_kb;
+  int stages;          // ring depth used by this launch (<= the template maximum)
   int out_f32;
   ErrorSink err;
   // optional per-CTA phase timestamps (%globaltimer ns), 8 slots per CTA:
@@ -79,6 +80,14 @@ struct Smem {
   static constexpr uint32_t kRed = (BN * kRedLdSwap > BM * kRedLdTok ? BN * kRedLdSwap : BM * kRedLdTok) * 4;
   static constexpr uint32_t kMain = kPipe > kRed ? kPipe : kRed;
   static constexpr uint32_t kBytes = kMain + 1024 /*align*/ + 256 /*barriers*/;
+  // bytes of a launch whose ring holds `stages` k-blocks: a CTA with fewer
+  // k-blocks than the template depth asks for less shared memory, so more
+  // CTAs (of this and of neighbouring kernels) stay resident together
+  __host__ __device__ static constexpr uint32_t main_bytes(int stages, bool split) {
+    const uint32_t pipe = static_cast<uint32_t>(stages) * (kA + kB);
+    return split && kRed > pipe ? kRed : pipe;
+  }
+  static constexpr uint32_t bytes(int stages, bool split) { return main_bytes(stages, split) + 1024 + 256; }
 };
 
 template <int N>
@@ -103,11 +112,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
+  const int stages = p.stages;
   uint8_t* sA = smem;
-  uint8_t* sB = smem + STAGES * S::kA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::kMain);
-  uint64_t* empty = full + STAGES;
-  uint64_t* done = empty + STAGES;
+  uint8_t* sB = smem + stages * S::kA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::main_bytes(stages, SPLIT));
+  uint64_t* empty = full + stages;
+  uint64_t* done = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   constexpr uint32_t kCols = TmemCols<BN>::value;
@@ -122,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   pdl_launch_dependents();
   if (threadIdx.x == 0) trace_stamp(p, 0);
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; ++s) {
+    for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
       mbar_init(&empty[s], 1);
     }
@@ -154,7 +164,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* sX = SWAP ? sB : sA;
     constexpr uint32_t kW = SWAP ? S::kA : S::kB;
     constexpr uint32_t kX = SWAP ? S::kB : S::kA;
-    const int pre = min(nkb, STAGES);
+    const int pre = min(nkb, stages);
     if (lane == 0) {
       for (int i = 0; i < pre; ++i) {
         mbar_arrive_expect_tx(&full[i], S::kA + S::kB);
@@ -168,8 +178,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     __syncwarp();
     for (int i = pre; i < nkb; ++i) {
-      const int s = i % STAGES;
-      const uint32_t ph = (i / STAGES) & 1u;
+      const int s = i % stages;
+      const uint32_t ph = (i / stages) & 1u;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u, p.err, 101));
       if (!ok) break;
       if (lane == 0) {
@@ -183,8 +193,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     constexpr uint32_t idesc = make_idesc_bf16(BM, BN);
     for (int i = 0; i < nkb; ++i) {
-      const int s = i % STAGES;
-      const uint32_t ph = (i / STAGES) & 1u;
+      const int s = i % stages;
+      const uint32_t ph = (i / stages) & 1u;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.err, 102));
       if (!ok) break;
       tc_fence_after();
@@ -364,12 +374,12 @@ template <int BN, int STAGES, bool SWAP, bool SPLIT>
 void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, dim3 grid, int splits,
                  cudaStream_t stream) {
   auto kern = gemm_tc_kernel<BN, STAGES, SWAP, SPLIT>;
-  constexpr uint32_t smem = Smem<BN, STAGES>::kBytes;
+  const uint32_t smem = Smem<BN, STAGES>::bytes(kp.stages, SPLIT);
   static bool configured[64] = {};  // one attribute call per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
   if (!configured[dev & 63]) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Smem<BN, STAGES>::kBytes);
     if (SPLIT) cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
     configured[dev & 63] = true;
   }
@@ -397,8 +407,9 @@ void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp
 }
 
 template <int BN, int STAGES, bool SWAP>
-void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, dim3 grid,
+void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, dim3 grid,
                     cudaStream_t stream) {
+  kp.stages = std::max(1, std::min(STAGES, kp.kb_per_split));
   if (splits > 1) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
   else launch_tile<BN, STAGES, SWAP, false>(ta, tb, kp, grid, 1, stream);
 }

@@ -10,6 +10,7 @@
 #include <stdexcept>
 
 #include "common.cuh"
+#include "launch.h"
 #include "ops.h"
 
 namespace minisgl {
@@ -27,6 +28,8 @@ __device__ __forceinline__ void warp_argmax(float& v, int& i) {
 }
 
 __global__ void moe_route_kernel(MoeRouteArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();  // router logits come from the previous kernel
   const int warps = blockDim.x >> 5;
   const int t = blockIdx.x * warps + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
@@ -152,7 +155,7 @@ void launch_moe_route(const MoeRouteArgs& a, cudaStream_t s) {
   if (a.E > 32 * kMaxPerLane || a.k > 32 || a.n_group > 64)
     throw std::runtime_error("minisgl.moe_route: too many experts");
   const int warps = 8;
-  moe_route_kernel<<<(a.T + warps - 1) / warps, warps * 32, 0, s>>>(a);
+  launch_pdl(moe_route_kernel, dim3((a.T + warps - 1) / warps), dim3(warps * 32), 0, s, a);
 }
 
 }  // namespace minisgl

@@ -13,6 +13,7 @@
 #include <stdexcept>
 
 #include "common.cuh"
+#include "launch.h"
 #include "ops.h"
 
 namespace minisgl {
@@ -21,6 +22,7 @@ namespace {
 template <typename T, int D>
 __global__ void rope_store_kernel(RopeStoreArgs a) {
   pdl_launch_dependents();  // let a following PDL kernel start its prologue
+  pdl_wait();               // qkv comes from the previous kernel
   constexpr int E = D / 32;  // elements per lane (contiguous)
   const int warps_per_block = blockDim.x >> 5;
   const int item = blockIdx.x * warps_per_block + (threadIdx.x >> 5);
@@ -96,9 +98,9 @@ void launch_typed(const RopeStoreArgs& a, cudaStream_t s) {
   const int warps = 4;
   const int blocks = (items + warps - 1) / warps;
   switch (a.d) {
-    case 64: rope_store_kernel<T, 64><<<blocks, warps * 32, 0, s>>>(a); break;
-    case 128: rope_store_kernel<T, 128><<<blocks, warps * 32, 0, s>>>(a); break;
-    case 256: rope_store_kernel<T, 256><<<blocks, warps * 32, 0, s>>>(a); break;
+    case 64: launch_pdl(rope_store_kernel<T, 64>, dim3(blocks), dim3(warps * 32), 0, s, a); break;
+    case 128: launch_pdl(rope_store_kernel<T, 128>, dim3(blocks), dim3(warps * 32), 0, s, a); break;
+    case 256: launch_pdl(rope_store_kernel<T, 256>, dim3(blocks), dim3(warps * 32), 0, s, a); break;
     default: throw std::runtime_error("minisgl.rope_store: head_dim must be 64, 128 or 256");
   }
 }

@@ -21,6 +21,7 @@
 #include <stdexcept>
 
 #include "common.cuh"
+#include "launch.h"
 #include "ops.h"
 
 namespace minisgl {
@@ -103,6 +104,8 @@ __device__ float block_reduce_sum(float v) {
 }
 
 __global__ void argmax_kernel(int32_t* out, const float* logits, int V, int ld) {
+  pdl_launch_dependents();
+  pdl_wait();
   const float* row = logits + static_cast<int64_t>(blockIdx.x) * ld;
   ArgMax best{-INFINITY, 0x7fffffff};
   for (int i = threadIdx.x; i < V; i += blockDim.x) best = better(best, ArgMax{row[i], i});
@@ -154,6 +157,8 @@ __device__ uint32_t radix_threshold(const float* row, int V, float target, uint3
 }
 
 __global__ void sample_kernel(SampleArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
   const int r = blockIdx.x;
   const float* row = a.logits + static_cast<int64_t>(r) * a.ld;
   const int V = a.V;
@@ -208,19 +213,23 @@ __global__ void sample_kernel(SampleArgs a) {
   if (threadIdx.x == 0) a.out[r] = best.i == 0x7fffffff ? 0 : best.i;
 }
 
-__global__ void bump_step_kernel(int64_t* step) { *step += 1; }
+__global__ void bump_step_kernel(int64_t* step) {
+  pdl_launch_dependents();
+  pdl_wait();  // the sampling kernel reads the counter first
+  *step += 1;
+}
 
 }  // namespace
 
 void launch_argmax(int32_t* out, const float* logits, int B, int V, int ld, cudaStream_t s) {
   if (B <= 0) return;
-  argmax_kernel<<<B, kThreads, 0, s>>>(out, logits, V, ld);
+  launch_pdl(argmax_kernel, dim3(B), dim3(kThreads), 0, s, out, logits, V, ld);
 }
 
 void launch_sample(const SampleArgs& a, cudaStream_t s) {
   if (a.B <= 0) return;
-  sample_kernel<<<a.B, kThreads, 0, s>>>(a);
-  if (a.step != nullptr) bump_step_kernel<<<1, 1, 0, s>>>(const_cast<int64_t*>(a.step));
+  launch_pdl(sample_kernel, dim3(a.B), dim3(kThreads), 0, s, a);
+  if (a.step != nullptr) launch_pdl(bump_step_kernel, dim3(1), dim3(1), 0, s, const_cast<int64_t*>(a.step));
 }
 
 }  // namespace minisgl

@@ -5,8 +5,9 @@ token-major tiles, N tile, cluster split-K factor) depends on (M, N, K) in
 ways a closed-form heuristic gets wrong by up to 4x. Before CUDA-graph
 capture the engine times every candidate plan for each (batch size, weight
 shape) it will replay, with each candidate captured in a CUDA graph of
-back-to-back launches (so launch overhead does not hide kernel time), and
-records the fastest. ``minisgl.ops.gemm`` then uses the recorded plan for
+back-to-back launches (so launch overhead does not hide kernel time) that
+cycle through copies of the weight larger than L2 in total (so weights
+come from HBM, as in a real step), and records the fastest. ``minisgl.ops.gemm`` then uses the recorded plan for
 exactly that shape and the built-in heuristic for everything else.
 
 Plans can be saved to / loaded from a JSON file keyed by the device name.
@@ -50,18 +51,24 @@ def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
     return out
 
 
-def _time_plan(native, out, x, w, plan: Plan, reps: int = 8) -> float:
-    mode, bn, s = plan
+# bytes of weight copies cycled through while timing: above the 126 MB L2, so
+# every launch streams its weights from HBM as in a real decode step
+_COLD_BYTES = 192 << 20
 
-    def run():
+
+def _time_plan(native, out, x, ws: List[torch.Tensor], plan: Plan, reps: int = 8) -> float:
+    mode, bn, s = plan
+    reps = max(reps, len(ws))
+
+    def run(w):
         native.gemm(out, x, w, None, None, s, mode, None, bn)
 
-    run()
+    run(ws[0])
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
     with torch.cuda.graph(g):
-        for _ in range(reps):
-            run()
+        for i in range(reps):
+            run(ws[i % len(ws)])
     g.replay()
     torch.cuda.synchronize()
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -83,7 +90,7 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
     from minisgl import ops
 
     native = ops.native()
-    key_dev = torch.cuda.get_device_name(device)
+    key_dev = torch.cuda.get_device_name(device) + "|cold-weights"
     cached = _load(cache_file, key_dev)
     shapes = sorted(set(shapes))
     wanted = sorted(set(int(m) for m in batch_sizes if m > 0))
@@ -92,6 +99,8 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
     with torch.cuda.device(device):
         for N, K in shapes:
             w = torch.randn(N, K, device=device, dtype=torch.bfloat16) * 0.02
+            copies = max(1, min(24, -(-_COLD_BYTES // w.nbytes)))
+            ws = [w] + [w.clone() for _ in range(copies - 1)]
             xmax = torch.randn(max(sizes), K, device=device, dtype=torch.bfloat16)
             omax = torch.empty(max(sizes), N, device=device, dtype=torch.bfloat16)
             for M in sizes:
@@ -103,13 +112,13 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
                 timed = []
                 for plan in candidates(M, K, full=False):
                     try:
-                        timed.append((_time_plan(native, out, x, w, plan), plan))
+                        timed.append((_time_plan(native, out, x, ws, plan), plan))
                     except RuntimeError:
                         continue
                 if timed:
                     PLANS[key] = min(timed)[1]
                     cached[key] = PLANS[key]
-            del w, xmax, omax
+            del w, ws, xmax, omax
     torch.cuda.synchronize(device)
     _save(cache_file, key_dev, cached)
     # wanted sizes that were not tuned themselves borrow the next tuned plan
