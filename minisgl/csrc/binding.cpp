@@ -112,41 +112,139 @@ void gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w,
   minisgl::launch_gemm(a, stream_of(x));
 }
 
+// out = epilogue(x @ w^T (+ bias)) with the fused decode epilogues (see
+// GemmEpilogue in ops.h); optional tensors are None when a kind is unused.
+void gemm_fused(at::Tensor out, const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                int64_t force_splits, int64_t force_bn, const c10::optional<at::Tensor>& err, int64_t kind,
+                double eps, const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& q_norm_w,
+                const c10::optional<at::Tensor>& k_norm_w, double head_eps,
+                const c10::optional<at::Tensor>& cos_sin, const c10::optional<at::Tensor>& positions,
+                const c10::optional<at::Tensor>& out_loc, const c10::optional<at::Tensor>& k_cache,
+                const c10::optional<at::Tensor>& v_cache, int64_t hq, int64_t hk, int64_t page_size) {
+  check_cuda(x, "x");
+  check_cuda(w, "w");
+  check_cuda(out, "out");
+  check_same_device(x, w);
+  check_same_device(x, out);
+  check_rowmajor(x, "x");
+  check_rowmajor(w, "w");
+  check_rowmajor(out, "out");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                out.scalar_type() == at::kBFloat16,
+            "fused gemm: bf16 x, w and out");
+  MSG_CHECK(x.size(1) == w.size(1), "gemm K mismatch: ", x.sizes(), " vs ", w.sizes());
+  const int64_t M = x.size(0), N = w.size(0);
+  MSG_CHECK(out.size(0) == M, "fused gemm: output rows");
+  if (kind & minisgl::kEpiSiluMul) {
+    MSG_CHECK(out.size(1) == N / 2, "silu epilogue: out must be [M, N / 2]");
+  } else if (kind & minisgl::kEpiRope) {
+    MSG_CHECK(out.size(1) >= hq * 128, "rope epilogue: out must hold the q heads");
+  } else {
+    MSG_CHECK(out.size(1) == N, "fused gemm: out must be [M, N]");
+  }
+  minisgl::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.bias = nullptr;
+  if (bias.has_value()) {
+    MSG_CHECK(bias->is_cuda() && bias->scalar_type() == at::kBFloat16 && bias->is_contiguous() && bias->numel() == N,
+              "bias must be a contiguous bf16 vector of N elements");
+    a.bias = bias->data_ptr();
+  }
+  a.out = out.data_ptr();
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(x.size(1));
+  a.ldx = static_cast<int>(x.stride(0));
+  a.ldw = static_cast<int>(w.stride(0));
+  a.ldo = static_cast<int>(out.stride(0));
+  a.out_f32 = false;
+  a.force_splits = static_cast<int>(force_splits);
+  a.force_mode = 2;
+  a.force_bn = static_cast<int>(force_bn);
+  a.err = err_ptr(err);
+  minisgl::GemmEpilogue& e = a.epi;
+  e.kind = static_cast<int>(kind);
+  e.eps = static_cast<float>(eps);
+  if (kind & minisgl::kEpiResidual) {
+    MSG_CHECK(residual.has_value() && residual->is_cuda() && residual->scalar_type() == at::kBFloat16 &&
+                  residual->dim() == 2 && residual->stride(1) == 1 && residual->size(0) == M &&
+                  residual->size(1) == N,
+              "residual epilogue: bf16 residual [M, N]");
+    e.residual = residual->data_ptr();
+    e.ld_res = static_cast<int>(residual->stride(0));
+  }
+  if (kind & minisgl::kEpiRope) {
+    MSG_CHECK(cos_sin.has_value() && cos_sin->scalar_type() == at::kFloat && cos_sin->is_contiguous() &&
+                  cos_sin->size(-1) == 128,
+              "rope epilogue: float32 cos_sin [max_pos, 128]");
+    MSG_CHECK(positions.has_value() && out_loc.has_value(), "rope epilogue: positions and out_loc");
+    check_i32(*positions, "positions");
+    check_i32(*out_loc, "out_loc");
+    MSG_CHECK(positions->numel() == M && out_loc->numel() == M, "rope epilogue: positions / out_loc size");
+    for (const auto* c : {&k_cache, &v_cache})
+      MSG_CHECK(c->has_value() && (*c)->is_cuda() && (*c)->scalar_type() == at::kBFloat16 && (*c)->is_contiguous(),
+                "rope epilogue: bf16 contiguous k / v cache");
+    for (const auto* nw : {&q_norm_w, &k_norm_w})
+      if (nw->has_value())
+        MSG_CHECK((*nw)->scalar_type() == at::kBFloat16 && (*nw)->is_contiguous() && (*nw)->numel() == 128,
+                  "rope epilogue: bf16 head norm weight of 128");
+    e.q_norm_w = q_norm_w.has_value() ? q_norm_w->data_ptr() : nullptr;
+    e.k_norm_w = k_norm_w.has_value() ? k_norm_w->data_ptr() : nullptr;
+    e.head_eps = static_cast<float>(head_eps);
+    e.cos_sin = cos_sin->data_ptr<float>();
+    e.positions = positions->data_ptr<int32_t>();
+    e.out_loc = out_loc->data_ptr<int32_t>();
+    e.k_cache = k_cache->data_ptr();
+    e.v_cache = v_cache->data_ptr();
+    e.hq = static_cast<int>(hq);
+    e.hk = static_cast<int>(hk);
+    e.page_size = static_cast<int>(page_size);
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_gemm(a, stream_of(x));
+}
+
 int64_t gemm_workspace_elems(int64_t M, int64_t N, int64_t K) {
   return minisgl::gemm_workspace_elems(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
 }
 
 // ------------------------------------------------------------ elementwise
-void rmsnorm(at::Tensor out, const at::Tensor& x, const at::Tensor& w, double eps) {
+// w = None: the plain normalisation (its weight folded into the next GEMM)
+void rmsnorm(at::Tensor out, const at::Tensor& x, const c10::optional<at::Tensor>& w, double eps) {
   check_cuda(x, "x");
   check_rowmajor(x, "x");
   check_rowmajor(out, "out");
-  MSG_CHECK(w.is_contiguous() && w.numel() == x.size(1), "rmsnorm weight shape");
-  MSG_CHECK(out.sizes() == x.sizes() && out.scalar_type() == x.scalar_type() &&
-                w.scalar_type() == x.scalar_type(),
-            "rmsnorm dtype/shape mismatch");
+  if (w.has_value())
+    MSG_CHECK(w->is_contiguous() && w->numel() == x.size(1) && w->scalar_type() == x.scalar_type(),
+              "rmsnorm weight shape / dtype");
+  MSG_CHECK(out.sizes() == x.sizes() && out.scalar_type() == x.scalar_type(), "rmsnorm dtype/shape mismatch");
   const c10::cuda::CUDAGuard guard(x.device());
-  minisgl::launch_rmsnorm(out.data_ptr(), x.data_ptr(), w.data_ptr(), static_cast<int>(x.size(0)),
+  minisgl::launch_rmsnorm(out.data_ptr(), x.data_ptr(), w.has_value() ? w->data_ptr() : nullptr,
+                          static_cast<int>(x.size(0)),
                           static_cast<int>(x.size(1)), static_cast<int>(x.stride(0)),
                           static_cast<int>(out.stride(0)), static_cast<float>(eps), dtype_of(x),
                           stream_of(x));
 }
 
-void fused_add_rmsnorm(at::Tensor x, at::Tensor residual, const at::Tensor& w, double eps) {
+void fused_add_rmsnorm(at::Tensor x, at::Tensor residual, const c10::optional<at::Tensor>& w, double eps) {
   check_cuda(x, "x");
   MSG_CHECK(x.is_contiguous() && residual.is_contiguous() && x.sizes() == residual.sizes() &&
                 x.dim() == 2,
             "fused_add_rmsnorm needs contiguous 2-D x and residual of equal shape");
-  MSG_CHECK(x.scalar_type() == residual.scalar_type() && w.scalar_type() == x.scalar_type() &&
-                w.numel() == x.size(1),
-            "fused_add_rmsnorm dtype/shape mismatch");
+  MSG_CHECK(x.scalar_type() == residual.scalar_type(), "fused_add_rmsnorm dtype mismatch");
+  if (w.has_value())
+    MSG_CHECK(w->scalar_type() == x.scalar_type() && w->numel() == x.size(1) && w->is_contiguous(),
+              "fused_add_rmsnorm weight shape / dtype");
   const c10::cuda::CUDAGuard guard(x.device());
-  minisgl::launch_fused_add_rmsnorm(x.data_ptr(), residual.data_ptr(), w.data_ptr(),
+  minisgl::launch_fused_add_rmsnorm(x.data_ptr(), residual.data_ptr(), w.has_value() ? w->data_ptr() : nullptr,
                                     static_cast<int>(x.size(0)), static_cast<int>(x.size(1)),
                                     static_cast<float>(eps), dtype_of(x), stream_of(x));
 }
 
-void act_and_mul(at::Tensor out, const at::Tensor& x, int64_t act) {
+// interleaved: gate|up columns alternate in blocks of 64 (the layout the
+// fused decode GEMM uses); otherwise all gate columns, then all up columns
+void act_and_mul(at::Tensor out, const at::Tensor& x, int64_t act, bool interleaved) {
   check_cuda(x, "x");
   MSG_CHECK(x.is_contiguous() && out.is_contiguous() && x.dim() == 2 && out.dim() == 2 &&
                 x.size(1) == 2 * out.size(1) && x.size(0) == out.size(0) &&
@@ -154,7 +252,7 @@ void act_and_mul(at::Tensor out, const at::Tensor& x, int64_t act) {
             "act_and_mul shape mismatch");
   const c10::cuda::CUDAGuard guard(x.device());
   minisgl::launch_act_and_mul(out.data_ptr(), x.data_ptr(), static_cast<int>(x.size(0)),
-                              static_cast<int>(out.size(1)), static_cast<int>(act), dtype_of(x),
+                              static_cast<int>(out.size(1)), static_cast<int>(act), interleaved, dtype_of(x),
                               stream_of(x));
 }
 
@@ -402,10 +500,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_workspace_elems", &gemm_workspace_elems);
   m.def("rmsnorm", &rmsnorm);
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
-  m.def("act_and_mul", &act_and_mul);
+  m.def("act_and_mul", &act_and_mul, py::arg("out"), py::arg("x"), py::arg("act"), py::arg("interleaved") = false);
   m.def("embedding", &embedding);
   m.def("rope_store", &rope_store);
   m.def("decode_attention", &decode_attention);
+  m.def("gemm_fused", &gemm_fused);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);
   m.def("sample", &sample);

@@ -82,7 +82,12 @@ __global__ void rmsnorm_kernel(T* __restrict__ out, const T* __restrict__ x,
     const int c = (k * blockDim.x + threadIdx.x) * V;
     if (c < cols) {
       float wv[V];
-      load_vec<T>(w + c, wv);
+      if (w != nullptr) {
+        load_vec<T>(w + c, wv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) wv[i] = 1.f;
+      }
 #pragma unroll
       for (int i = 0; i < V; ++i) v[k][i] = v[k][i] * inv * wv[i];
       store_vec<T>(orow + c, v[k]);
@@ -125,7 +130,12 @@ __global__ void fused_add_rmsnorm_kernel(T* __restrict__ x, T* __restrict__ res,
     const int c = (k * blockDim.x + threadIdx.x) * V;
     if (c < cols) {
       float wv[V];
-      load_vec<T>(w + c, wv);
+      if (w != nullptr) {
+        load_vec<T>(w + c, wv);
+      } else {
+#pragma unroll
+        for (int i = 0; i < V; ++i) wv[i] = 1.f;
+      }
 #pragma unroll
       for (int i = 0; i < V; ++i) v[k][i] = v[k][i] * inv * wv[i];
       store_vec<T>(xr + c, v[k]);
@@ -137,7 +147,7 @@ __device__ __forceinline__ float silu(float x) { return x / (1.f + __expf(-x)); 
 __device__ __forceinline__ float gelu(float x) { return 0.5f * x * (1.f + erff(x * 0.7071067811865476f)); }
 
 template <typename T, int ACT>
-__global__ void act_and_mul_kernel(T* __restrict__ out, const T* __restrict__ x, int rows, int d) {
+__global__ void act_and_mul_kernel(T* __restrict__ out, const T* __restrict__ x, int rows, int d, int interleaved) {
   pdl_launch_dependents();  // let a following PDL kernel start its prologue
   pdl_wait();               // inputs come from the previous kernel
   constexpr int V = Vec<T>::N;
@@ -148,8 +158,11 @@ __global__ void act_and_mul_kernel(T* __restrict__ out, const T* __restrict__ x,
     const int64_t r = i / nvec;
     const int c = static_cast<int>(i % nvec) * V;
     float g[V], u[V], o[V];
-    load_vec<T>(x + r * 2 * d + c, g);
-    load_vec<T>(x + r * 2 * d + d + c, u);
+    // interleaved rows: gate block c / 64 at column 128 * (c / 64), its up block 64 later
+    const int64_t gc = interleaved ? (c / 64) * 128 + c % 64 : c;
+    const int64_t uc = interleaved ? gc + 64 : d + c;
+    load_vec<T>(x + r * 2 * d + gc, g);
+    load_vec<T>(x + r * 2 * d + uc, u);
 #pragma unroll
     for (int k = 0; k < V; ++k) o[k] = (ACT == 0 ? silu(g[k]) : gelu(g[k])) * u[k];
     store_vec<T>(out + r * d + c, o);
@@ -215,22 +228,23 @@ void launch_fused_add_rmsnorm(void* x, void* residual, const void* w, int rows, 
   });
 }
 
-void launch_act_and_mul(void* out, const void* x, int rows, int d, int act, DType dt,
+void launch_act_and_mul(void* out, const void* x, int rows, int d, int act, bool interleaved, DType dt,
                         cudaStream_t s) {
   if (rows <= 0) return;
   by_dtype(dt, [&](auto tag) {
     using T = decltype(tag);
     constexpr int V = Vec<T>::N;
     if (d % V != 0) throw std::runtime_error("minisgl.act_and_mul: width must be a multiple of 16 bytes");
+    if (interleaved && d % 64 != 0) throw std::runtime_error("minisgl.act_and_mul: interleaved width must be a multiple of 64");
     const int64_t total = static_cast<int64_t>(rows) * (d / V);
     const int threads = 256;
     const int blocks = static_cast<int>(std::min<int64_t>((total + threads - 1) / threads, 148 * 16));
     if (act == 0)
       launch_pdl(act_and_mul_kernel<T, 0>, dim3(blocks), dim3(threads), 0, s, static_cast<T*>(out),
-                 static_cast<const T*>(x), rows, d);
+                 static_cast<const T*>(x), rows, d, interleaved ? 1 : 0);
     else
       launch_pdl(act_and_mul_kernel<T, 1>, dim3(blocks), dim3(threads), 0, s, static_cast<T*>(out),
-                 static_cast<const T*>(x), rows, d);
+                 static_cast<const T*>(x), rows, d, interleaved ? 1 : 0);
   });
 }
 

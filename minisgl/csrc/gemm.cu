@@ -53,7 +53,9 @@ struct KParams {
   int kb_per_split;
   int num_kb;
   int stages;          // ring depth used by this launch (<= the template maximum)
+  int K;               // reduction length (the RMSNorm mean of kEpiNorm)
   int out_f32;
+  GemmEpilogue epi;    // fused epilogue (weight-major split-K instantiations only)
   ErrorSink err;
   // optional per-CTA phase timestamps (%globaltimer ns), 8 slots per CTA:
   // 0 entry, 1 setup done, 2 producer past griddepcontrol.wait, 3 first
@@ -79,7 +81,7 @@ struct Smem {
   static constexpr uint32_t kRedLdTok = BN + 4;
   static constexpr uint32_t kRed = (BN * kRedLdSwap > BM * kRedLdTok ? BN * kRedLdSwap : BM * kRedLdTok) * 4;
   static constexpr uint32_t kMain = kPipe > kRed ? kPipe : kRed;
-  static constexpr uint32_t kBytes = kMain + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr uint32_t kBytes = kMain + 1024 /*align*/ + 256 /*barriers*/ + 2 * BN * 4;
   // bytes of a launch whose ring holds `stages` k-blocks: a CTA with fewer
   // k-blocks than the template depth asks for less shared memory, so more
   // CTAs (of this and of neighbouring kernels) stay resident together
@@ -87,7 +89,10 @@ struct Smem {
     const uint32_t pipe = static_cast<uint32_t>(stages) * (kA + kB);
     return split && kRed > pipe ? kRed : pipe;
   }
-  static constexpr uint32_t bytes(int stages, bool split) { return main_bytes(stages, split) + 1024 + 256; }
+  // + per-token sum of squares and rstd arrays (kEpiNorm) after the barriers
+  static constexpr uint32_t bytes(int stages, bool split) {
+    return main_bytes(stages, split) + 1024 + 256 + 2 * BN * 4;
+  }
 };
 
 template <int N>
@@ -101,6 +106,70 @@ __device__ __forceinline__ void store_out(const KParams& p, int m, int n, float 
   } else {
     reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(m) * p.ldo + n] = __float2bfloat16_rn(v);
   }
+}
+
+__device__ __forceinline__ float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+__device__ __forceinline__ void store4_bf16(__nv_bfloat16* dst, const float (&v)[4]) {
+  uint2 pk;
+  pk.x = pack_bf16x2(v[0], v[1]);
+  pk.y = pack_bf16x2(v[2], v[3]);
+  *reinterpret_cast<uint2*>(dst) = pk;
+}
+
+// Sum of the float4 at byte offset `addr` of every cluster CTA's parked tile.
+__device__ __forceinline__ float4 reduce_parts(uint32_t addr, int nsplit) {
+  constexpr int kMaxS = 16;
+  float4 part[kMaxS];
+#pragma unroll
+  for (int q = 0; q < kMaxS; ++q)
+    if (q < nsplit) part[q] = ld_shared_cluster_v4(map_shared_rank(addr, static_cast<uint32_t>(q)));
+  float4 acc = part[0];
+#pragma unroll
+  for (int q = 1; q < kMaxS; ++q)
+    if (q < nsplit) acc.x += part[q].x, acc.y += part[q].y, acc.z += part[q].z, acc.w += part[q].w;
+  return acc;
+}
+
+// kEpiRope for one token row of one 128-feature head; the calling warp holds
+// the whole row (lane l: features 4l..4l+3). Same steps and roundings as
+// the unfused rope_store kernel: bf16 GEMM output, per-head RMSNorm rounded
+// to bf16, NeoX rotation (feature j pairs with j + 64, held by lane l ^ 16).
+__device__ __forceinline__ void rope_epilogue(const KParams& p, int head, int m, int ocol, float (&v)[4]) {
+  const GemmEpilogue& e = p.epi;
+  const int lane = threadIdx.x & 31;
+  const bool is_q = head < e.hq;
+  const bool is_k = !is_q && head < e.hq + e.hk;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) v[q] = round_bf16(v[q]);
+  if (is_q || is_k) {
+    const __nv_bfloat16* nw = static_cast<const __nv_bfloat16*>(is_q ? e.q_norm_w : e.k_norm_w);
+    if (nw != nullptr) {
+      float ss = v[0] * v[0] + v[1] * v[1] + v[2] * v[2] + v[3] * v[3];
+      ss = warp_sum(ss);
+      const float inv = rsqrtf(ss / 128.f + e.head_eps);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) v[q] = round_bf16(v[q] * inv * __bfloat162float(nw[ocol + q]));
+    }
+    const float* cs = e.cos_sin + static_cast<int64_t>(e.positions[m]) * 128;
+    const bool first = lane < 16;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const float other = __shfl_xor_sync(0xffffffffu, v[q], 16);
+      const int j = (ocol + q) & 63;
+      const float c = cs[j], sn = cs[64 + j];
+      v[q] = first ? (v[q] * c - other * sn) : (v[q] * c + other * sn);
+    }
+  }
+  if (is_q) {
+    store4_bf16(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + head * 128 + ocol, v);
+    return;
+  }
+  const int kvh = is_k ? head - e.hq : head - e.hq - e.hk;
+  const int slot = e.out_loc[m];
+  const int page = slot / e.page_size, off = slot % e.page_size;
+  __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_k ? e.k_cache : e.v_cache);
+  store4_bf16(cache + ((static_cast<int64_t>(page) * e.hk + kvh) * e.page_size + off) * 128 + ocol, v);
 }
 
 // SWAP = weight-major tiles; SPLIT = cluster split-K (gridDim.z CTAs per tile).
@@ -119,6 +188,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
+  float* s_ss = reinterpret_cast<float*>(smem + S::main_bytes(stages, SPLIT) + 256);  // [BN]
+  float* s_rstd = s_ss + BN;                                                           // [BN]
+  // kEpiNorm: the epilogue warps read every x tile of the ring too, so a
+  // stage is free once the MMA commit and those four warps have released it
+  const bool do_norm = SWAP && SPLIT && (p.epi.kind & kEpiNorm) != 0;
 
   constexpr uint32_t kCols = TmemCols<BN>::value;
   const int warp = threadIdx.x >> 5;
@@ -134,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < stages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], do_norm ? 5 : 1);
     }
     mbar_init(done, 1);
     fence_barrier_init();
@@ -213,6 +287,53 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     if (lane == 0) tc_commit(done);
     __syncwarp();
+  }
+
+  // --------------------------------------- kEpiNorm: per-token sum of x^2 ----
+  if (do_norm && warp >= 2) {
+    // x tile of a stage: BN token rows of 128 bytes (64 bf16 of K); the
+    // 128-byte swizzle only permutes 16-byte chunks inside a row, so a row's
+    // sum is the sum over its 128-byte line. Thread et takes chunks et,
+    // et + 128, ...; the 8 lanes of a row combine by shuffles at the end.
+    constexpr int kChunks = BN * 8;
+    constexpr int kPer = (kChunks + 127) / 128;
+    const int et = threadIdx.x - 64;
+    float acc[kPer];
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
+    for (int i = 0; i < nkb; ++i) {
+      const int s = i % stages;
+      const uint32_t ph = (i / stages) & 1u;
+      if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.err, 104))) break;
+      const uint8_t* xs = sB + s * S::kB;
+#pragma unroll
+      for (int j = 0; j < kPer; ++j) {
+        const int idx = et + j * 128;
+        if (idx < kChunks) {
+          const uint4 raw = *reinterpret_cast<const uint4*>(xs + idx * 16);
+          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const float2 f = __bfloat1622float2(h[q]);
+            acc[j] += f.x * f.x + f.y * f.y;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&empty[s]);
+    }
+#pragma unroll
+    for (int j = 0; j < kPer; ++j) {
+      float v = acc[j];
+      v += __shfl_xor_sync(0xffffffffu, v, 1);
+      v += __shfl_xor_sync(0xffffffffu, v, 2);
+      v += __shfl_xor_sync(0xffffffffu, v, 4);
+      const int idx = et + j * 128;
+      if ((lane & 7) == 0 && idx < kChunks) s_ss[idx >> 3] = v;
+    }
+    // the parked split-K tile below overlaps the ring: no epilogue warp may
+    // write it while another still reads x tiles
+    asm volatile("bar.sync 2, 128;" ::: "memory");
   }
 
   // ------------------------------------------------------------ epilogue ----
@@ -318,44 +439,93 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kOutRows = SWAP ? BN : BM;
     constexpr int kOutCols = SWAP ? BM : BN;
     constexpr int kLd = SWAP ? S::kRedLdSwap : S::kRedLdTok;
-    constexpr int kMaxS = 16;
     const int nsplit = static_cast<int>(gridDim.z);  // == cluster size along z
     const int rank = static_cast<int>(cluster_ctarank());
     const int rows_per = kOutRows / nsplit;
     const uint32_t red_base = smem_u32(smem);
     const int tok0 = SWAP ? b_row0 : a_row0;
     const int feat0 = SWAP ? a_row0 : b_row0;
-    const int vecs = rows_per * (kOutCols / 4);
-    for (int e = threadIdx.x; e < vecs; e += kThreads) {
-      const int orow = rank * rows_per + e / (kOutCols / 4);
-      const int ocol = (e % (kOutCols / 4)) * 4;
-      const uint32_t off = static_cast<uint32_t>((orow * kLd + ocol) * 4);
-      float4 part[kMaxS];
-#pragma unroll
-      for (int q = 0; q < kMaxS; ++q)
-        if (q < nsplit) part[q] = ld_shared_cluster_v4(map_shared_rank(red_base + off, static_cast<uint32_t>(q)));
-      float4 acc = part[0];
-#pragma unroll
-      for (int q = 1; q < kMaxS; ++q)
-        if (q < nsplit) acc.x += part[q].x, acc.y += part[q].y, acc.z += part[q].z, acc.w += part[q].w;
-      const int m = tok0 + orow;
-      const int n = feat0 + ocol;
-      if (m >= p.M || n >= p.N) continue;
-      float v[4] = {acc.x, acc.y, acc.z, acc.w};
-      if (p.bias != nullptr)
-        for (int q = 0; q < 4; ++q) v[q] += n + q < p.N ? __bfloat162float(p.bias[n + q]) : 0.f;
-      if (n + 4 <= p.N && (p.ldo & 3) == 0) {
-        if (p.out_f32) {
-          *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n) =
-              make_float4(v[0], v[1], v[2], v[3]);
-        } else {
-          uint2 pk;
-          pk.x = pack_bf16x2(v[0], v[1]);
-          pk.y = pack_bf16x2(v[2], v[3]);
-          *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + n) = pk;
+    if (SWAP && do_norm) {
+      // rstd of this rank's rows from every CTA's partial sum of squares
+      for (int r = threadIdx.x; r < rows_per; r += kThreads) {
+        const int orow = rank * rows_per + r;
+        const uint32_t off = smem_u32(s_ss + orow);
+        float ss = 0.f;
+        for (int q = 0; q < nsplit; ++q) ss += ld_shared_cluster_f32(map_shared_rank(off, static_cast<uint32_t>(q)));
+        s_rstd[orow] = rsqrtf(ss / static_cast<float>(p.K) + p.epi.eps);
+      }
+      __syncthreads();
+    }
+    if (SWAP && (p.epi.kind & kEpiSiluMul) != 0) {
+      // gate features at tile columns [0, 64), the matching up features at
+      // [64, 128); output feature = feat0 / 2 + column
+      const int vecs = rows_per * 16;
+      for (int e = threadIdx.x; e < vecs; e += kThreads) {
+        const int orow = rank * rows_per + e / 16;
+        const int ocol = (e % 16) * 4;
+        const float4 g = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol) * 4), nsplit);
+        const float4 u = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol + 64) * 4), nsplit);
+        const int m = tok0 + orow;
+        if (m >= p.M || feat0 + ocol >= p.N) continue;
+        const float sc = do_norm ? s_rstd[orow] : 1.f;
+        float gv[4] = {g.x * sc, g.y * sc, g.z * sc, g.w * sc};
+        float uv[4] = {u.x * sc, u.y * sc, u.z * sc, u.w * sc};
+        if (p.bias != nullptr) {
+          for (int q = 0; q < 4; ++q) {
+            gv[q] += __bfloat162float(p.bias[feat0 + ocol + q]);
+            uv[q] += __bfloat162float(p.bias[feat0 + 64 + ocol + q]);
+          }
         }
-      } else {
-        for (int q = 0; q < 4 && n + q < p.N; ++q) store_out(p, m, n + q, v[q]);
+        float v[4];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          // the unfused path rounds the GEMM output to bf16 before the activation
+          const float gq = round_bf16(gv[q]), uq = round_bf16(uv[q]);
+          v[q] = gq / (1.f + __expf(-gq)) * uq;
+        }
+        store4_bf16(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + feat0 / 2 + ocol, v);
+      }
+    } else {
+      const int vecs = rows_per * (kOutCols / 4);
+      const bool rope = SWAP && (p.epi.kind & kEpiRope) != 0;
+      const int head = feat0 / BM;  // kEpiRope: one 128-feature head per tile
+      for (int e = threadIdx.x; e < vecs; e += kThreads) {
+        // kEpiRope relies on one warp covering one token row: kOutCols / 4
+        // == 32 vectors per row and kThreads is a multiple of 32
+        const int orow = rank * rows_per + e / (kOutCols / 4);
+        const int ocol = (e % (kOutCols / 4)) * 4;
+        const float4 acc = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol) * 4), nsplit);
+        const int m = tok0 + orow;
+        const int n = feat0 + ocol;
+        if (m >= p.M || n >= p.N) continue;  // uniform per warp for kEpiRope
+        const float sc = (SWAP && do_norm) ? s_rstd[orow] : 1.f;
+        float v[4] = {acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc};
+        if (p.bias != nullptr)
+          for (int q = 0; q < 4; ++q) v[q] += n + q < p.N ? __bfloat162float(p.bias[n + q]) : 0.f;
+        if (rope) {
+          rope_epilogue(p, head, m, ocol, v);
+          continue;
+        }
+        if ((p.epi.kind & kEpiResidual) != 0) {
+          const uint2 rr = *reinterpret_cast<const uint2*>(
+              reinterpret_cast<const __nv_bfloat16*>(p.epi.residual) + static_cast<size_t>(m) * p.epi.ld_res + n);
+          const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rr.x));
+          const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rr.y));
+          // the residual stream is kept in bf16: round the projection first,
+          // then the sum, as a separate add would
+          v[0] = round_bf16(v[0]) + r0.x, v[1] = round_bf16(v[1]) + r0.y;
+          v[2] = round_bf16(v[2]) + r1.x, v[3] = round_bf16(v[3]) + r1.y;
+        }
+        if (n + 4 <= p.N && (p.ldo & 3) == 0) {
+          if (p.out_f32) {
+            *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + n) =
+                make_float4(v[0], v[1], v[2], v[3]);
+          } else {
+            store4_bf16(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + n, v);
+          }
+        } else {
+          for (int q = 0; q < 4 && n + q < p.N; ++q) store_out(p, m, n + q, v[q]);
+        }
       }
     }
     cluster_sync();  // peers may still be reading this CTA's tile
@@ -410,7 +580,8 @@ template <int BN, int STAGES, bool SWAP>
 void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, dim3 grid,
                     cudaStream_t stream) {
   kp.stages = std::max(1, std::min(STAGES, kp.kb_per_split));
-  if (splits > 1) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
+  // fused epilogues live in the cluster (split-K) path; one split = a cluster of one
+  if (splits > 1 || kp.epi.kind != 0) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
   else launch_tile<BN, STAGES, SWAP, false>(ta, tb, kp, grid, 1, stream);
 }
 
@@ -485,7 +656,24 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     throw std::runtime_error("minisgl.gemm: N tile must be 16, 32, 64, 128 or 256");
   if (a.force_bn == 16 && a.force_mode == 1)
     throw std::runtime_error("minisgl.gemm: token-major tiles need an N tile of at least 32");
-  const Plan pl = make_plan(a.M, a.N, a.K, a.force_mode, a.force_splits, a.force_bn);
+  const int fused = a.epi.kind;
+  const bool needs_swap = (fused & (kEpiNorm | kEpiSiluMul | kEpiRope)) != 0;
+  if (fused != 0) {
+    if (a.out_f32) throw std::runtime_error("minisgl.gemm: fused epilogues write bf16");
+    if (needs_swap && a.force_mode == 1)
+      throw std::runtime_error("minisgl.gemm: norm / silu / rope epilogues need weight-major tiles");
+    if ((fused & kEpiResidual) != 0 && (a.epi.residual == nullptr || a.epi.ld_res % 4 != 0))
+      throw std::runtime_error("minisgl.gemm: residual epilogue needs a residual with row stride % 4 == 0");
+    if ((fused & kEpiSiluMul) != 0 && (a.N % 128 != 0 || (fused & (kEpiRope | kEpiResidual)) != 0))
+      throw std::runtime_error("minisgl.gemm: silu epilogue needs N % 128 == 0 and no rope / residual");
+    if ((fused & kEpiRope) != 0) {
+      if (a.N != (a.epi.hq + 2 * a.epi.hk) * 128 || a.epi.cos_sin == nullptr || a.epi.positions == nullptr ||
+          a.epi.out_loc == nullptr || a.epi.k_cache == nullptr || a.epi.v_cache == nullptr || a.epi.page_size <= 0 ||
+          (fused & kEpiResidual) != 0)
+        throw std::runtime_error("minisgl.gemm: rope epilogue needs head_dim 128 qkv weights and cache pointers");
+    }
+  }
+  const Plan pl = make_plan(a.M, a.N, a.K, needs_swap ? 2 : a.force_mode, a.force_splits, a.force_bn);
   KParams kp;
   kp.out = a.out;
   kp.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);
@@ -495,6 +683,8 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   kp.kb_per_split = pl.kb_per_split;
   kp.num_kb = (a.K + BK - 1) / BK;
   kp.out_f32 = a.out_f32 ? 1 : 0;
+  kp.K = a.K;
+  kp.epi = a.epi;
   kp.err = ErrorSink{a.err};
   kp.trace = reinterpret_cast<unsigned long long*>(a.trace);
   if (pl.swap) {

@@ -12,6 +12,37 @@ enum class DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 
 // ----------------------------------------------------------------- GEMM ----
 // out[M, N] = x[M, K] @ w[N, K]^T (+ bias[N]); bf16 inputs, fp32 accumulate.
+// Fused epilogues of the weight-major split-K GEMM (decode path). Flags:
+//   kEpiNorm     out rows scaled by rstd_t = rsqrt(mean_k x[t, k]^2 + eps):
+//                the RMSNorm of x whose weight was folded into w's columns
+//                (w' = w * diag(norm_weight)), so x is the raw residual
+//                stream; the sum of squares is taken from the x tiles the
+//                GEMM streams anyway.
+//   kEpiResidual out = acc + residual (out may alias residual).
+//   kEpiSiluMul  w rows interleaved in blocks of 64 (64 gate rows, then the
+//                64 matching up rows); out[t, j] = silu(gate) * up, N / 2
+//                output columns.
+//   kEpiRope     w is the fused qkv projection with head_dim 128: q/k heads
+//                get their per-head RMSNorm (if weights are given) and NeoX
+//                RoPE; q heads are written to out (the qkv row), k and v
+//                heads to the paged KV cache at out_loc (not to out).
+enum : int { kEpiNorm = 1, kEpiResidual = 2, kEpiSiluMul = 4, kEpiRope = 8 };
+struct GemmEpilogue {
+  int kind;
+  float eps;                  // kEpiNorm
+  const void* residual;       // kEpiResidual: bf16 [M, ld_res]
+  int ld_res;
+  const void* q_norm_w;       // kEpiRope: bf16 [128] or nullptr
+  const void* k_norm_w;
+  float head_eps;
+  const float* cos_sin;       // [max_pos, 128]: 64 cos then 64 sin
+  const int32_t* positions;   // [M]
+  const int32_t* out_loc;     // [M] token slots
+  void* k_cache;              // bf16 [pages, hk, page_size, 128] of this layer
+  void* v_cache;
+  int hq, hk, page_size;
+};
+
 struct GemmArgs {
   const void* x;      // bf16 [M, K], row stride ldx elements
   const void* w;      // bf16 [N, K], row stride ldw elements
@@ -27,6 +58,7 @@ struct GemmArgs {
   int force_bn;       // 0 = heuristic, else the N tile (16..256)
   void* trace;        // optional uint64 [ctas * 8] phase timestamps (profiling)
   int* err;           // device error word (2 x int32) or nullptr
+  GemmEpilogue epi;   // fused epilogue (kind 0: plain store)
 };
 void launch_gemm(const GemmArgs& a, cudaStream_t stream);
 // Number of fp32 workspace elements launch_gemm may need for this shape.
@@ -39,7 +71,7 @@ void launch_rmsnorm(void* out, const void* x, const void* w, int rows, int cols,
 void launch_fused_add_rmsnorm(void* x, void* residual, const void* w, int rows, int cols,
                               float eps, DType dt, cudaStream_t s);
 // out[t, :d] = act(x[t, :d]) * x[t, d:2d]; act 0 = silu, 1 = gelu(tanh)
-void launch_act_and_mul(void* out, const void* x, int rows, int d, int act, DType dt,
+void launch_act_and_mul(void* out, const void* x, int rows, int d, int act, bool interleaved, DType dt,
                         cudaStream_t s);
 // out[i, :] = (lo <= ids[i] < lo + n) ? w[ids[i] - lo, :] : 0
 void launch_embedding(void* out, const void* w, const int32_t* ids, int num_tokens, int hidden,

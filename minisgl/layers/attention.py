@@ -45,6 +45,30 @@ class AttentionLayer(StateLessOP):
         self._k_norm = k_norm
         self.eps = q_norm.eps if q_norm is not None else eps
 
+    def rope_args(self) -> dict:
+        """Arguments of the fused qkv-GEMM epilogue (q/k norm, RoPE, KV store)
+        for the current batch."""
+        ctx = get_global_ctx()
+        batch = ctx.batch
+        kv = ctx.kv_cache
+        return dict(
+            positions=batch.positions, cos_sin=self.rotary.cos_sin_cache, out_loc=batch.out_loc,
+            q_norm_w=None if self._q_norm is None else self._q_norm.weight,
+            k_norm_w=None if self._k_norm is None else self._k_norm.weight,
+            head_eps=self.eps, k_cache=kv.k_cache(self.layer_id), v_cache=kv.v_cache(self.layer_id),
+            hq=self.num_qo_heads, hk=self.num_kv_heads, page_size=ctx.page_size,
+        )
+
+    def attend(self, qkv: torch.Tensor) -> torch.Tensor:
+        """Attention over q heads already rotated in ``qkv`` (KV already stored)."""
+        ctx = get_global_ctx()
+        return ctx.attn_backend.forward(qkv, self.layer_id, ctx.batch)
+
+    @property
+    def fusable(self) -> bool:
+        """Whether the fused qkv epilogue can replace ``rope_store``."""
+        return self.head_dim == 128
+
     def forward(self, qkv: torch.Tensor) -> torch.Tensor:
         ctx = get_global_ctx()
         batch = ctx.batch

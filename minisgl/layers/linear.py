@@ -65,6 +65,17 @@ class LinearRowParallel(_Linear):
         y = ops.gemm(x, self.weight, self.bias)
         return self._comm.all_reduce(y) if self._tp > 1 else y
 
+    def forward_residual(self, x: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """residual + x @ w^T with the add fused into the GEMM epilogue. One
+        rank: written into ``residual`` in place. Several ranks: rank 0 adds
+        the residual to its partial product and the all-reduce sums the
+        partials, so every rank gets residual + the full product."""
+        if self._tp == 1:
+            return ops.gemm_fused(x, self.weight, bias=self.bias, residual=residual, out=residual)
+        first = get_tp_info().rank == 0
+        y = ops.gemm_fused(x, self.weight, bias=self.bias if first else None, residual=residual if first else None)
+        return self._comm.all_reduce(y)
+
 
 class LinearOProj(LinearRowParallel):
     """The attention output projection (row parallel)."""

@@ -25,14 +25,27 @@ class RMSNorm(BaseOP):
 
 class RMSNormFused(BaseOP):
     """First call (no residual yet): y = norm(x), residual = x. Later calls:
-    residual += x and x = norm(residual), in place."""
+    residual += x and x = norm(residual), in place.
+
+    ``folded`` (set by the owning layer after loading): the weight has been
+    multiplied into the columns of the projection that consumes this norm,
+    so the norm itself runs without a weight."""
 
     def __init__(self, size: int, eps: float) -> None:
         self.eps = eps
         self.weight = torch.empty(size)
+        self._folded = False
+
+    def fold(self) -> None:
+        self._folded = True
+
+    @property
+    def folded(self) -> bool:
+        return self._folded
 
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+        w = None if self._folded else self.weight
         if residual is None:
-            return ops.rmsnorm(x, self.weight, self.eps), x
-        ops.fused_add_rmsnorm(x, residual, self.weight, self.eps)
+            return ops.rmsnorm(x, w, self.eps), x
+        ops.fused_add_rmsnorm(x, residual, w, self.eps)
         return x, residual

@@ -19,6 +19,10 @@ def _rms(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     return x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w.float()
 
 
+def _ones_if(flag: bool, w: torch.Tensor) -> torch.Tensor:
+    return torch.ones_like(w) if flag else w
+
+
 def _rope_tables(cfg: ModelConfig, n: int):
     from minisgl.layers.rotary import RotaryEmbedding
 
@@ -39,8 +43,13 @@ def _rotate(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tens
 
 @torch.no_grad()
 def dense_logits(state: Dict[str, torch.Tensor], cfg: ModelConfig, tokens: List[int],
-                 qk_norm: bool = True) -> torch.Tensor:
-    """fp32 logits [len(tokens), vocab] for a dense (non-MoE, non-MLA) decoder."""
+                 qk_norm: bool = True, fused_layout: bool = False) -> torch.Tensor:
+    """fp32 logits [len(tokens), vocab] for a dense (non-MoE, non-MLA) decoder.
+
+    ``fused_layout``: the state comes from a model whose input / post-
+    attention norm weights are folded into qkv / gate_up and whose gate|up
+    rows alternate in 64-row blocks; the oracle then skips those norm weights
+    and reads gate and up from the interleaved rows."""
     W = {k: v.detach().float().cpu() for k, v in state.items()}
     n = len(tokens)
     ids = torch.tensor(tokens, dtype=torch.long)
@@ -51,7 +60,7 @@ def dense_logits(state: Dict[str, torch.Tensor], cfg: ModelConfig, tokens: List[
     eps = cfg.rms_norm_eps
     for i in range(cfg.num_layers):
         p = f"model.layers.{i}."
-        h = _rms(x, W[p + "input_layernorm.weight"], eps)
+        h = _rms(x, _ones_if(fused_layout, W[p + "input_layernorm.weight"]), eps)
         qkv = h @ W[p + "self_attn.qkv_proj.weight"].t()
         if (p + "self_attn.qkv_proj.bias") in W:
             qkv = qkv + W[p + "self_attn.qkv_proj.bias"]
@@ -68,10 +77,14 @@ def dense_logits(state: Dict[str, torch.Tensor], cfg: ModelConfig, tokens: List[
         s = s.masked_fill(~causal[None], float("-inf"))
         o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), v).reshape(n, hq * d)
         x = x + o @ W[p + "self_attn.o_proj.weight"].t()
-        h = _rms(x, W[p + "post_attention_layernorm.weight"], eps)
+        h = _rms(x, _ones_if(fused_layout, W[p + "post_attention_layernorm.weight"]), eps)
         gu = h @ W[p + "mlp.gate_up_proj.weight"].t()
         inter = gu.shape[-1] // 2
-        a = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
+        if fused_layout:
+            blocks = gu.view(n, inter // 64, 2, 64)
+            a = (torch.nn.functional.silu(blocks[:, :, 0]) * blocks[:, :, 1]).reshape(n, inter)
+        else:
+            a = torch.nn.functional.silu(gu[:, :inter]) * gu[:, inter:]
         x = x + a @ W[p + "mlp.down_proj.weight"].t()
     x = _rms(x, W["model.norm.weight"], eps)
     head = W.get("lm_head.weight", W["model.embed_tokens.weight"])
@@ -79,11 +92,11 @@ def dense_logits(state: Dict[str, torch.Tensor], cfg: ModelConfig, tokens: List[
 
 
 def greedy_generate(state: Dict[str, torch.Tensor], cfg: ModelConfig, prompt: List[int], steps: int,
-                    qk_norm: bool = True) -> List[int]:
+                    qk_norm: bool = True, fused_layout: bool = False) -> List[int]:
     seq = list(prompt)
     out = []
     for _ in range(steps):
-        nxt = int(dense_logits(state, cfg, seq, qk_norm)[-1].argmax())
+        nxt = int(dense_logits(state, cfg, seq, qk_norm, fused_layout)[-1].argmax())
         out.append(nxt)
         seq.append(nxt)
     return out

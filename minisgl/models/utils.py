@@ -4,6 +4,9 @@ from __future__ import annotations
 
 from typing import TYPE_CHECKING
 
+import torch
+
+from minisgl import ops
 from minisgl.layers import (
     AttentionLayer,
     BaseOP,
@@ -20,8 +23,6 @@ from minisgl.layers import (
 from minisgl.utils import nvtx_annotate
 
 if TYPE_CHECKING:
-    import torch
-
     from .config import ModelConfig
 
 _ACT = {"silu": silu_and_mul, "gelu": gelu_and_mul, "gelu_pytorch_tanh": gelu_and_mul}
@@ -36,12 +37,35 @@ class GatedMLP(BaseOP):
         if config.hidden_act not in _ACT:
             raise ValueError(f"unsupported activation {config.hidden_act}")
         self._act = _ACT[config.hidden_act]
+        self._silu = config.hidden_act == "silu"
+        self._interleaved = False
         self.down_proj = LinearRowParallel(inter, config.hidden_size, has_bias=False)
+
+    @property
+    def fusable(self) -> bool:
+        """SiLU MLPs whose local gate / up halves split into 64-row blocks can
+        run the gate_up GEMM with the activation in its epilogue."""
+        return self._silu and self.gate_up_proj.local_output_size % 128 == 0
+
+    def interleave(self) -> None:
+        """Reorder gate|up rows into alternating blocks of 64 (64 gate rows,
+        then the matching 64 up rows), the layout of the fused epilogue."""
+        w = self.gate_up_proj.weight
+        n = w.shape[0] // 2
+        self.gate_up_proj.weight = w.view(2, n // 64, 64, -1).transpose(0, 1).reshape(2 * n, -1).contiguous()
+        self._interleaved = True
 
     @nvtx_annotate("MLP")
     def forward(self, x: "torch.Tensor") -> "torch.Tensor":
         h = self.gate_up_proj.forward(x)
-        return self.down_proj.forward(self._act(h))
+        a = ops.silu_and_mul(h, interleaved=True) if self._interleaved else self._act(h)
+        return self.down_proj.forward(a)
+
+    def forward_fused(self, r: "torch.Tensor", norm_eps: float) -> "torch.Tensor":
+        """r + down(silu(gate) * up) of rmsnorm(r): two GEMMs, the norm and the
+        activation in the first one's epilogue, the add in the second's."""
+        h = ops.gemm_fused(r, self.gate_up_proj.weight, norm_eps=norm_eps, silu=True)
+        return self.down_proj.forward_residual(h, r)
 
 
 class MoEMLP(BaseOP):
@@ -73,6 +97,14 @@ class RopeAttn(BaseOP):
     @nvtx_annotate("MHA")
     def forward(self, x: "torch.Tensor") -> "torch.Tensor":
         return self.o_proj.forward(self.attn.forward(self.qkv_proj.forward(x)))
+
+    def forward_fused(self, r: "torch.Tensor", norm_eps: float) -> "torch.Tensor":
+        """r + o_proj(attention(rmsnorm(r))): the norm, q/k-norm, RoPE and
+        KV store in the qkv GEMM epilogue, the add in the o_proj epilogue."""
+        q = torch.empty(r.shape[0], self.attn.qo_attn_dim, dtype=r.dtype, device=r.device)
+        ops.gemm_fused(r, self.qkv_proj.weight, bias=self.qkv_proj.bias, norm_eps=norm_eps,
+                       rope=self.attn.rope_args(), out=q)
+        return self.o_proj.forward_residual(self.attn.attend(q), r)
 
 
 __all__ = ["GatedMLP", "MoEMLP", "RopeAttn"]

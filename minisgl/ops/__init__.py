@@ -119,7 +119,62 @@ def gemm(
 
 
 # ------------------------------------------------------------ elementwise
-def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+EPI_NORM, EPI_RESIDUAL, EPI_SILU, EPI_ROPE = 1, 2, 4, 8
+from .gemm_tune import SWAP_PLANS as _gemm_swap_plans  # noqa: E402  (best weight-major plans)
+
+
+def gemm_fused(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    *,
+    bias: Optional[torch.Tensor] = None,
+    norm_eps: Optional[float] = None,
+    residual: Optional[torch.Tensor] = None,
+    silu: bool = False,
+    rope: Optional[dict] = None,
+    out: Optional[torch.Tensor] = None,
+    plan: Optional[Tuple[int, int]] = None,
+) -> torch.Tensor:
+    """GEMM with a fused decode epilogue (weight-major tiles; ``plan`` =
+    (token tile, K splits) overrides the tuned / default tile plan):
+
+    * ``norm_eps``: rows of x are RMS-normalised (x is the raw residual
+      stream; the norm weight must already be folded into ``w``'s columns);
+    * ``silu``: ``w`` holds gate|up rows interleaved in blocks of 64 and the
+      result is silu(gate) * up, [M, N / 2];
+    * ``residual``: out = x @ w^T + residual (``out`` may be ``residual``);
+    * ``rope`` (dict: positions, cos_sin, q_norm_w, k_norm_w, head_eps,
+      k_cache, v_cache, out_loc, hq, hk, page_size): q/k head norm + NeoX
+      RoPE; q heads land in ``out`` (the qkv rows), k/v in the paged cache.
+    """
+    if not x.is_cuda:
+        y = ref.gemm_fused(x, w, bias, norm_eps, residual, silu, rope)
+        if out is not None:
+            out.copy_(y[:, : out.shape[1]])  # rope: out may hold only the q heads
+            return out
+        return y
+    M, N = x.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(M, N // 2 if silu else N, dtype=x.dtype, device=x.device)
+    kind = (EPI_NORM if norm_eps is not None else 0) | (EPI_RESIDUAL if residual is not None else 0)
+    kind |= (EPI_SILU if silu else 0) | (EPI_ROPE if rope is not None else 0)
+    if plan is not None:
+        bn, splits = plan
+    else:
+        tuned = _gemm_swap_plans.get((M, N, x.shape[1]))
+        splits, bn = (tuned[2], tuned[1]) if tuned is not None else (0, 0)
+    r = rope or {}
+    _count()
+    native().gemm_fused(
+        out, x, w, bias, splits, bn, error_word(x.device), kind, norm_eps or 0.0, residual,
+        r.get("q_norm_w"), r.get("k_norm_w"), r.get("head_eps", 0.0), r.get("cos_sin"), r.get("positions"),
+        r.get("out_loc"), r.get("k_cache"), r.get("v_cache"), r.get("hq", 0), r.get("hk", 0), r.get("page_size", 0),
+    )
+    return out
+
+
+def rmsnorm(x: torch.Tensor, w: Optional[torch.Tensor], eps: float, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """y = x / rms(x) * w (w None: no weight, e.g. folded into the next GEMM)."""
     if not x.is_cuda:
         y = ref.rmsnorm(x, w, eps)
         if out is not None:
@@ -133,7 +188,7 @@ def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float, out: Optional[torch.Te
     return out
 
 
-def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> None:
     if not x.is_cuda:
         ref.fused_add_rmsnorm(x, residual, w, eps)
         return
@@ -141,17 +196,22 @@ def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, 
     native().fused_add_rmsnorm(x, residual, w, eps)
 
 
-def silu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
-    return _act_and_mul(x, "silu", out)
+def silu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None, interleaved: bool = False) -> torch.Tensor:
+    """silu(gate) * up; ``interleaved``: gate|up columns alternate in blocks of 64."""
+    return _act_and_mul(x, "silu", out, interleaved)
 
 
 def gelu_and_mul(x: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
     return _act_and_mul(x, "gelu", out)
 
 
-def _act_and_mul(x: torch.Tensor, act: str, out: Optional[torch.Tensor]) -> torch.Tensor:
+def _act_and_mul(x: torch.Tensor, act: str, out: Optional[torch.Tensor], interleaved: bool = False) -> torch.Tensor:
     if not x.is_cuda:
-        y = ref.act_and_mul(x, act)
+        if interleaved:
+            assert act == "silu", "interleaved layout is used with SiLU only"
+            y = ref.silu_mul_interleaved(x)
+        else:
+            y = ref.act_and_mul(x, act)
         if out is not None:
             out.copy_(y)
             return out
@@ -159,7 +219,7 @@ def _act_and_mul(x: torch.Tensor, act: str, out: Optional[torch.Tensor]) -> torc
     if out is None:
         out = torch.empty(x.shape[0], x.shape[1] // 2, dtype=x.dtype, device=x.device)
     _count()
-    native().act_and_mul(out, x, 0 if act == "silu" else 1)
+    native().act_and_mul(out, x, 0 if act == "silu" else 1, interleaved)
     return out
 
 

@@ -23,6 +23,8 @@ import torch
 
 Plan = Tuple[int, int, int]  # (mode: 1 token-major / 2 weight-major, n tile, splits)
 PLANS: Dict[Tuple[int, int, int], Plan] = {}
+# best weight-major plan per shape: the fused-epilogue GEMMs need those tiles
+SWAP_PLANS: Dict[Tuple[int, int, int], Plan] = {}
 
 
 # batch sizes that are tuned; other sizes use the plan of the next tuned size
@@ -105,8 +107,10 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
             omax = torch.empty(max(sizes), N, device=device, dtype=torch.bfloat16)
             for M in sizes:
                 key = (M, N, K)
-                if key in cached:
+                skey = (-M, N, K)  # weight-major entry of the cache
+                if key in cached and skey in cached:
                     PLANS[key] = cached[key]
+                    SWAP_PLANS[key] = cached[skey]
                     continue
                 x, out = xmax[:M], omax[:M]
                 timed = []
@@ -118,6 +122,10 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
                 if timed:
                     PLANS[key] = min(timed)[1]
                     cached[key] = PLANS[key]
+                    swap = [t for t in timed if t[1][0] == 2]
+                    if swap:
+                        SWAP_PLANS[key] = min(swap)[1]
+                        cached[skey] = SWAP_PLANS[key]
             del w, ws, xmax, omax
     torch.cuda.synchronize(device)
     _save(cache_file, key_dev, cached)
@@ -127,6 +135,8 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
             t = next((s for s in sizes if s >= m), None)
             if t is not None and (t, N, K) in PLANS:
                 PLANS.setdefault((m, N, K), PLANS[(t, N, K)])
+            if t is not None and (t, N, K) in SWAP_PLANS:
+                SWAP_PLANS.setdefault((m, N, K), SWAP_PLANS[(t, N, K)])
     return dict(PLANS)
 
 
@@ -136,6 +146,7 @@ def lookup(M: int, N: int, K: int) -> Optional[Plan]:
 
 def clear() -> None:
     PLANS.clear()
+    SWAP_PLANS.clear()
 
 
 def _load(path: Optional[str], dev: str) -> Dict[Tuple[int, int, int], Plan]:

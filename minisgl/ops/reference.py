@@ -20,13 +20,52 @@ def gemm(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor], out_dty
     return y.to(out_dtype)
 
 
-def rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+def rmsnorm(x: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> torch.Tensor:
     xf = x.float()
     inv = torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)
-    return (xf * inv * w.float()).to(x.dtype)
+    y = xf * inv if w is None else xf * inv * w.float()
+    return y.to(x.dtype)
 
 
-def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: torch.Tensor, eps: float) -> None:
+def silu_mul_interleaved(h: torch.Tensor) -> torch.Tensor:
+    """silu(gate) * up for gate|up rows interleaved in blocks of 64 columns."""
+    M, N = h.shape
+    hv = h.float().view(M, N // 128, 2, 64)
+    g, u = hv[:, :, 0], hv[:, :, 1]
+    return (torch.nn.functional.silu(g) * u).reshape(M, N // 2).to(h.dtype)
+
+
+def gemm_fused(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    norm_eps: Optional[float],
+    residual: Optional[torch.Tensor],
+    silu: bool,
+    rope: Optional[dict],
+) -> torch.Tensor:
+    """The fused decode GEMM: optional row RMSNorm of x (weight folded into
+    w), bias, then one of silu(gate) * up (interleaved rows), residual add,
+    or q/k-norm + RoPE + KV store (returns the qkv rows, q heads rotated)."""
+    y = x.float() @ w.float().t()
+    if norm_eps is not None:
+        xf = x.float()
+        y = y * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + norm_eps)
+    if bias is not None:
+        y = y + bias.float()
+    y = y.to(x.dtype)
+    if silu:
+        return silu_mul_interleaved(y)
+    if residual is not None:
+        return (y.float() + residual.float()).to(x.dtype)
+    if rope is not None:
+        rope_store(y, rope["positions"], rope["cos_sin"], rope.get("q_norm_w"), rope.get("k_norm_w"),
+                   rope["k_cache"], rope["v_cache"], rope["out_loc"], rope["hq"], rope["hk"], 128,
+                   rope["page_size"], rope["head_eps"])
+    return y
+
+
+def fused_add_rmsnorm(x: torch.Tensor, residual: torch.Tensor, w: Optional[torch.Tensor], eps: float) -> None:
     s = (x.float() + residual.float()).to(x.dtype)
     residual.copy_(s)
     x.copy_(rmsnorm(s, w, eps))

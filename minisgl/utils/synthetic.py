@@ -138,10 +138,11 @@ def make_model_dir(shape: str, folder: Optional[str] = None, overrides: Optional
     return folder
 
 
-def write_random_checkpoint(folder: str, seed: int = 0, std: float = 0.02) -> str:
+def write_random_checkpoint(folder: str, seed: int = 0, std: float = 0.02, norm_std: float = 0.0) -> str:
     """Write HF-named random weights (``model.safetensors``) for the config
     in ``folder``: separate q/k/v and gate/up projections, per-expert tensors,
-    exactly as a downloaded checkpoint is laid out."""
+    exactly as a downloaded checkpoint is laid out. Norm weights are
+    1 + N(0, norm_std) (exactly one with the default 0)."""
     import torch
     from safetensors.torch import save_file
 
@@ -153,6 +154,9 @@ def write_random_checkpoint(folder: str, seed: int = 0, std: float = 0.02) -> st
     def rnd(*shape):
         return (torch.randn(*shape, generator=g) * std).to(dt)
 
+    def norm_w(n):
+        return (1.0 + torch.randn(n, generator=g) * norm_std).to(dt) if norm_std > 0 else torch.ones(n, dtype=dt)
+
     H, V = c["hidden_size"], c["vocab_size"]
     hq, hk = c["num_attention_heads"], c.get("num_key_value_heads", c["num_attention_heads"])
     d = c.get("head_dim") or H // hq
@@ -162,15 +166,15 @@ def write_random_checkpoint(folder: str, seed: int = 0, std: float = 0.02) -> st
     moe = c.get("num_experts", 0) > 0
     for i in range(c["num_hidden_layers"]):
         p = f"model.layers.{i}."
-        W[p + "input_layernorm.weight"] = torch.ones(H, dtype=dt)
-        W[p + "post_attention_layernorm.weight"] = torch.ones(H, dtype=dt)
+        W[p + "input_layernorm.weight"] = norm_w(H)
+        W[p + "post_attention_layernorm.weight"] = norm_w(H)
         W[p + "self_attn.q_proj.weight"] = rnd(hq * d, H)
         W[p + "self_attn.k_proj.weight"] = rnd(hk * d, H)
         W[p + "self_attn.v_proj.weight"] = rnd(hk * d, H)
         W[p + "self_attn.o_proj.weight"] = rnd(H, hq * d)
         if c.get("model_type", "").startswith("qwen3"):
-            W[p + "self_attn.q_norm.weight"] = torch.ones(d, dtype=dt)
-            W[p + "self_attn.k_norm.weight"] = torch.ones(d, dtype=dt)
+            W[p + "self_attn.q_norm.weight"] = norm_w(d)
+            W[p + "self_attn.k_norm.weight"] = norm_w(d)
         if c.get("model_type") == "qwen2":
             for n, size in (("q", hq * d), ("k", hk * d), ("v", hk * d)):
                 W[p + f"self_attn.{n}_proj.bias"] = rnd(size)

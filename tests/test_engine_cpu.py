@@ -22,7 +22,9 @@ def llm():
 
 
 def _oracle(llm, prompt, n):
-    return greedy_generate(llm.engine.model.state_dict(), llm.engine.model_config, prompt, n)
+    model = llm.engine.model
+    return greedy_generate(model.state_dict(), llm.engine.model_config, prompt, n,
+                           fused_layout=getattr(model, "fused_layout", False))
 
 
 def test_tiny_qwen3_matches_dense_oracle(llm):

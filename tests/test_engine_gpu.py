@@ -42,7 +42,8 @@ def test_gpu_engine_tracks_oracle():
         for p, o in zip(prompts, outs):
             toks = o["token_ids"]
             assert len(toks) == 12
-            logits = dense_logits(state, cfg, p + toks[:-1])[len(p) - 1 :]
+            logits = dense_logits(state, cfg, p + toks[:-1],
+                                  fused_layout=llm.engine.model.fused_layout)[len(p) - 1 :]
             for t, row in zip(toks, logits):
                 assert row[t] >= row.max() - 0.05 * row.abs().max(), (t, int(row.argmax()))
     finally:
