@@ -124,6 +124,95 @@ def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
             "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "frac_roofline": round(bound / ms, 3)}
 
 
+def bench_layer_chain(M: int, peaks, layers: int = 28) -> List[Dict]:
+    """The non-attention kernels of one Qwen3-0.6B decode layer (tp1) at M
+    tokens, per layer, over ``layers`` weight copies (~0.9 GB, so weights
+    stream from HBM), in a CUDA graph: the fused chain (4 GEMMs with norm /
+    RoPE / SiLU / residual epilogues) against the unfused one (norms, RoPE +
+    KV store and activation as separate kernels). Attention is left out; a
+    fixed tensor stands in for its output."""
+    from minisgl.ops import gemm_tune
+
+    H, I, hq, hk, d, page = 1024, 3072, 16, 8, 128, 64
+    dev = torch.device("cuda")
+    nqkv = (hq + 2 * hk) * d
+    gemm_tune.tune([(nqkv, H), (H, hq * d), (2 * I, H), (H, I)], [M], dev, fused={
+        (nqkv, H): (ops.EPI_NORM | ops.EPI_ROPE, hq, hk), (H, hq * d): (ops.EPI_RESIDUAL, hq, hk),
+        (2 * I, H): (ops.EPI_NORM | ops.EPI_SILU, hq, hk), (H, I): (ops.EPI_RESIDUAL, hq, hk)})
+    W = [dict(qkv=torch.randn(nqkv, H, device=dev, dtype=torch.bfloat16) * 0.02,
+              o=torch.randn(H, hq * d, device=dev, dtype=torch.bfloat16) * 0.02,
+              gu=torch.randn(2 * I, H, device=dev, dtype=torch.bfloat16) * 0.02,
+              down=torch.randn(H, I, device=dev, dtype=torch.bfloat16) * 0.02) for _ in range(layers)]
+    r = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+    x = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+    attn = torch.randn(M, hq * d, device=dev, dtype=torch.bfloat16)
+    pages = (M + page - 1) // page + 1
+    kc = torch.zeros(pages, hk, page, d, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    positions = torch.arange(M, device=dev, dtype=torch.int32)
+    out_loc = torch.arange(M, device=dev, dtype=torch.int32)
+    ang = torch.rand(4096, 64, device=dev) * 6
+    cos_sin = torch.cat([ang.cos(), ang.sin()], dim=1).contiguous()
+    rope = dict(positions=positions, cos_sin=cos_sin, out_loc=out_loc, q_norm_w=None, k_norm_w=None,
+                head_eps=1e-6, k_cache=kc, v_cache=vc, hq=hq, hk=hk, page_size=page)
+    q = torch.empty(M, hq * d, device=dev, dtype=torch.bfloat16)
+    h = torch.empty(M, I, device=dev, dtype=torch.bfloat16)
+
+    def fused():
+        for w in W:
+            ops.gemm_fused(r, w["qkv"], norm_eps=1e-6, rope=rope, out=q)
+            ops.gemm_fused(attn, w["o"], residual=r, out=r)
+            ops.gemm_fused(r, w["gu"], norm_eps=1e-6, silu=True, out=h)
+            ops.gemm_fused(h, w["down"], residual=r, out=r)
+
+    def unfused():
+        y = x
+        for w in W:
+            ops.fused_add_rmsnorm(y, r, None, 1e-6)
+            qkv = ops.gemm(y, w["qkv"])
+            ops.rope_store(qkv, positions, cos_sin, None, None, kc, vc, out_loc, hq, hk, d, page, 1e-6)
+            o = ops.gemm(attn, w["o"])
+            ops.fused_add_rmsnorm(o, r, None, 1e-6)
+            a = ops.silu_and_mul(ops.gemm(o, w["gu"]), interleaved=True)
+            y = ops.gemm(a, w["down"])
+
+    out = []
+    wbytes = sum(t.numel() * 2 for t in W[0].values())
+    for name, fn in (("fused", fused), ("unfused", unfused)):
+        ms = time_graph(fn, iters=3) / layers
+        out.append({"kernel": f"layer_chain[{name}]", "M": M, "us_per_layer": round(ms * 1000, 2),
+                    "weight_GB/s": round(wbytes / ms / 1e6, 1), "frac_hbm": round(wbytes / ms / 1e6 / peaks["hbm_gbs"], 3),
+                    "fused_plans": [gemm_tune.FUSED_PLANS.get((M, n, k)) for n, k in
+                                    ((nqkv, H), (H, hq * d), (2 * I, H), (H, I))] if name == "fused" else
+                    [gemm_tune.PLANS.get((M, n, k)) for n, k in ((nqkv, H), (H, hq * d), (2 * I, H), (H, I))]})
+    return out
+
+
+def bench_row_kernels(M: int, peaks) -> List[Dict]:
+    """The decode-sized row kernels (M tokens of Qwen3-0.6B) back to back in a
+    CUDA graph: what one launch costs inside a chain."""
+    H, I, hq, hk, d, page = 1024, 3072, 16, 8, 128, 64
+    dev = torch.device("cuda")
+    x = torch.randn(M, H, device=dev, dtype=torch.bfloat16)
+    r = torch.randn_like(x)
+    gu = torch.randn(M, 2 * I, device=dev, dtype=torch.bfloat16)
+    qkv = torch.randn(M, (hq + 2 * hk) * d, device=dev, dtype=torch.bfloat16)
+    kc = torch.zeros((M + page - 1) // page + 1, hk, page, d, device=dev, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    pos = torch.arange(M, device=dev, dtype=torch.int32)
+    ang = torch.rand(4096, 64, device=dev) * 6
+    cs = torch.cat([ang.cos(), ang.sin()], 1).contiguous()
+    out = []
+    for name, fn in (("fused_add_rmsnorm", lambda: ops.fused_add_rmsnorm(x, r, None, 1e-6)),
+                     ("rmsnorm", lambda: ops.rmsnorm(x, None, 1e-6)),
+                     ("silu_and_mul", lambda: ops.silu_and_mul(gu, interleaved=True)),
+                     ("rope_store", lambda: ops.rope_store(qkv, pos, cs, None, None, kc, vc, pos, hq, hk, d, page,
+                                                           1e-6))):
+        ms = time_graph(fn, iters=200)
+        out.append({"kernel": f"chain[{name}]", "M": M, "us": round(ms * 1000, 2)})
+    return out
+
+
 def bench_elementwise(peaks) -> List[Dict]:
     out = []
     T, H = 16384, 1024
@@ -175,6 +264,9 @@ def main() -> None:
     cases.append(("gemm[gate_up prefill]", lambda: bench_gemm(16384, 2 * I, H, peaks, "gate_up prefill")))
     cases.append(("gemm[square 8192]", lambda: bench_gemm(8192, 8192, 8192, peaks, "square 8192")))
     cases.append(("elementwise", lambda: bench_elementwise(peaks)))
+    for M in (1, 8, 32, 64, 128, 192, 256):
+        cases.append((f"layer_chain M={M};", lambda M=M: bench_layer_chain(M, peaks)))
+    cases.append(("rowkernels M=256", lambda: bench_row_kernels(256, peaks)))
     rows: List[Dict] = []
     for label, fn in cases:
         if args.only and args.only not in label:

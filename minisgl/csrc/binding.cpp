@@ -115,7 +115,8 @@ void gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w,
 // out = epilogue(x @ w^T (+ bias)) with the fused decode epilogues (see
 // GemmEpilogue in ops.h); optional tensors are None when a kind is unused.
 void gemm_fused(at::Tensor out, const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
-                int64_t force_splits, int64_t force_bn, const c10::optional<at::Tensor>& err, int64_t kind,
+                int64_t force_mode, int64_t force_splits, int64_t force_bn, const c10::optional<at::Tensor>& err,
+                int64_t kind,
                 double eps, const c10::optional<at::Tensor>& residual, const c10::optional<at::Tensor>& q_norm_w,
                 const c10::optional<at::Tensor>& k_norm_w, double head_eps,
                 const c10::optional<at::Tensor>& cos_sin, const c10::optional<at::Tensor>& positions,
@@ -160,7 +161,7 @@ void gemm_fused(at::Tensor out, const at::Tensor& x, const at::Tensor& w, const 
   a.ldo = static_cast<int>(out.stride(0));
   a.out_f32 = false;
   a.force_splits = static_cast<int>(force_splits);
-  a.force_mode = 2;
+  a.force_mode = static_cast<int>(force_mode);
   a.force_bn = static_cast<int>(force_bn);
   a.err = err_ptr(err);
   minisgl::GemmEpilogue& e = a.epi;

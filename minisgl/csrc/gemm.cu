@@ -35,6 +35,7 @@
 #include <vector>
 
 #include "common.cuh"
+#include "launch.h"
 #include "ops.h"
 #include "tma_host.h"
 
@@ -81,7 +82,7 @@ struct Smem {
   static constexpr uint32_t kRedLdTok = BN + 4;
   static constexpr uint32_t kRed = (BN * kRedLdSwap > BM * kRedLdTok ? BN * kRedLdSwap : BM * kRedLdTok) * 4;
   static constexpr uint32_t kMain = kPipe > kRed ? kPipe : kRed;
-  static constexpr uint32_t kBytes = kMain + 1024 /*align*/ + 256 /*barriers*/ + 2 * BN * 4;
+  static constexpr uint32_t kBytes = kMain + 1024 /*align*/ + 256 /*barriers*/ + 2 * (BN > BM ? BN : BM) * 4;
   // bytes of a launch whose ring holds `stages` k-blocks: a CTA with fewer
   // k-blocks than the template depth asks for less shared memory, so more
   // CTAs (of this and of neighbouring kernels) stay resident together
@@ -90,8 +91,9 @@ struct Smem {
     return split && kRed > pipe ? kRed : pipe;
   }
   // + per-token sum of squares and rstd arrays (kEpiNorm) after the barriers
+  static constexpr int kRows = BN > BM ? BN : BM;
   static constexpr uint32_t bytes(int stages, bool split) {
-    return main_bytes(stages, split) + 1024 + 256 + 2 * BN * 4;
+    return main_bytes(stages, split) + 1024 + 256 + 2 * kRows * 4;
   }
 };
 
@@ -172,6 +174,146 @@ __device__ __forceinline__ void rope_epilogue(const KParams& p, int head, int m,
   store4_bf16(cache + ((static_cast<int64_t>(page) * e.hk + kvh) * e.page_size + off) * 128 + ocol, v);
 }
 
+// Fused epilogue of a token-major tile without split-K, straight from TMEM:
+// this thread owns token row m (its TMEM lane) and the tile's BN features
+// [feat0, feat0 + BN). tcgen05.ld is warp-collective, so every lane loads
+// and only `valid` lanes (row inside M, pipeline healthy) read or write
+// global memory. Same arithmetic and roundings as the split-K path.
+template <int BN>
+__device__ __forceinline__ void rows_epilogue(const KParams& p, uint32_t taddr, int m, int feat0, float rstd,
+                                              bool valid) {
+  const GemmEpilogue& e = p.epi;
+  const __nv_bfloat16* bias = p.bias;
+  auto col = [&](const uint32_t (&r)[32], int j, int n) {
+    float x = __uint_as_float(r[j]) * rstd;
+    if (bias != nullptr) x += __bfloat162float(bias[n]);
+    return x;
+  };
+  if ((e.kind & kEpiSiluMul) != 0) {
+#pragma unroll 1
+    for (int blk = 0; blk < BN / 128; ++blk) {
+#pragma unroll 1
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t g[32], u[32];
+        tmem_ld_32x32b_x32(taddr + blk * 128 + c, g);
+        tmem_ld_32x32b_x32(taddr + blk * 128 + 64 + c, u);
+        tc_wait_ld();
+        if (!valid) continue;
+        const int n = feat0 + blk * 128 + c;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          const float gq = round_bf16(col(g, j, n + j)), uq = round_bf16(col(u, j, n + 64 + j));
+          v[j] = gq / (1.f + __expf(-gq)) * uq;
+        }
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + feat0 / 2 +
+                             blk * 64 + c;
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) store4_bf16(dst + j, {v[j], v[j + 1], v[j + 2], v[j + 3]});
+      }
+    }
+    return;
+  }
+  if ((e.kind & kEpiRope) != 0) {
+    const float* cs = e.cos_sin + static_cast<int64_t>(valid ? e.positions[m] : 0) * 128;
+#pragma unroll 1
+    for (int hb = 0; hb < BN / 128; ++hb) {
+      const int head = (feat0 + hb * 128) / 128;
+      const bool is_q = head < e.hq, is_k = !is_q && head < e.hq + e.hk;
+      const __nv_bfloat16* nw =
+          static_cast<const __nv_bfloat16*>(is_q ? e.q_norm_w : (is_k ? e.k_norm_w : nullptr));
+      const uint32_t ta = taddr + hb * 128;
+      const int n0 = head * 128;
+      // pass 1: per-head RMS of the bf16-rounded projection
+      float inv = 1.f;
+      if (nw != nullptr) {
+        float ss = 0.f;
+#pragma unroll 1
+        for (int c = 0; c < 128; c += 32) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(ta + c, r);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float x = round_bf16(col(r, j, n0 + c + j));
+            ss += x * x;
+          }
+        }
+        inv = rsqrtf(ss / 128.f + e.head_eps);
+      }
+      // pass 2: feature j (< 64) and its NeoX partner j + 64 together
+      __nv_bfloat16* dst;
+      if (is_q) {
+        dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + n0;
+      } else {
+        const int kvh = is_k ? head - e.hq : head - e.hq - e.hk;
+        const int slot = valid ? e.out_loc[m] : 0;
+        const int page = slot / e.page_size, off = slot % e.page_size;
+        dst = static_cast<__nv_bfloat16*>(is_k ? e.k_cache : e.v_cache) +
+              ((static_cast<int64_t>(page) * e.hk + kvh) * e.page_size + off) * 128;
+      }
+#pragma unroll 1
+      for (int c = 0; c < 64; c += 32) {
+        uint32_t lo[32], hi[32];
+        tmem_ld_32x32b_x32(ta + c, lo);
+        tmem_ld_32x32b_x32(ta + 64 + c, hi);
+        tc_wait_ld();
+        if (!valid) continue;
+        float a[32], b[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float xl = round_bf16(col(lo, j, n0 + c + j)), xh = round_bf16(col(hi, j, n0 + 64 + c + j));
+          if (nw != nullptr) {
+            xl = round_bf16(xl * inv * __bfloat162float(nw[c + j]));
+            xh = round_bf16(xh * inv * __bfloat162float(nw[64 + c + j]));
+          }
+          if (is_q || is_k) {
+            const float cj = cs[c + j], sj = cs[64 + c + j];
+            a[j] = xl * cj - xh * sj;
+            b[j] = xh * cj + xl * sj;
+          } else {
+            a[j] = xl, b[j] = xh;
+          }
+        }
+#pragma unroll
+        for (int j = 0; j < 32; j += 4) {
+          store4_bf16(dst + c + j, {a[j], a[j + 1], a[j + 2], a[j + 3]});
+          store4_bf16(dst + 64 + c + j, {b[j], b[j + 1], b[j + 2], b[j + 3]});
+        }
+      }
+    }
+    return;
+  }
+#pragma unroll 1
+  for (int c = 0; c < BN; c += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + c, r);
+    tc_wait_ld();
+    if (!valid) continue;
+    const int n = feat0 + c;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) v[j] = col(r, j, n + j);
+    if ((e.kind & kEpiResidual) != 0) {
+      const __nv_bfloat16* res = static_cast<const __nv_bfloat16*>(e.residual) + static_cast<size_t>(m) * e.ld_res + n;
+#pragma unroll
+      for (int j = 0; j < 32; j += 8) {
+        const uint4 raw = *reinterpret_cast<const uint4*>(res + j);
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          v[j + 2 * q] = round_bf16(v[j + 2 * q]) + f.x;
+          v[j + 2 * q + 1] = round_bf16(v[j + 2 * q + 1]) + f.y;
+        }
+      }
+    }
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + n;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) store4_bf16(dst + j, {v[j], v[j + 1], v[j + 2], v[j + 3]});
+  }
+}
+
 // SWAP = weight-major tiles; SPLIT = cluster split-K (gridDim.z CTAs per tile).
 template <int BN, int STAGES, bool SWAP, bool SPLIT>
 __global__ void __launch_bounds__(kThreads, 1)
@@ -188,11 +330,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  float* s_ss = reinterpret_cast<float*>(smem + S::main_bytes(stages, SPLIT) + 256);  // [BN]
-  float* s_rstd = s_ss + BN;                                                           // [BN]
+  float* s_ss = reinterpret_cast<float*>(smem + S::main_bytes(stages, SPLIT) + 256);  // [token rows]
+  float* s_rstd = s_ss + S::kRows;                                                     // [token rows]
   // kEpiNorm: the epilogue warps read every x tile of the ring too, so a
   // stage is free once the MMA commit and those four warps have released it
-  const bool do_norm = SWAP && SPLIT && (p.epi.kind & kEpiNorm) != 0;
+  const bool do_norm = (SPLIT || !SWAP) && (p.epi.kind & kEpiNorm) != 0;
 
   constexpr uint32_t kCols = TmemCols<BN>::value;
   const int warp = threadIdx.x >> 5;
@@ -291,11 +433,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // --------------------------------------- kEpiNorm: per-token sum of x^2 ----
   if (do_norm && warp >= 2) {
-    // x tile of a stage: BN token rows of 128 bytes (64 bf16 of K); the
-    // 128-byte swizzle only permutes 16-byte chunks inside a row, so a row's
-    // sum is the sum over its 128-byte line. Thread et takes chunks et,
-    // et + 128, ...; the 8 lanes of a row combine by shuffles at the end.
-    constexpr int kChunks = BN * 8;
+    // x tile of a stage: token rows of 128 bytes (64 bf16 of K), BN of them
+    // in weight-major tiles (operand B), BM in token-major ones (operand A);
+    // the 128-byte swizzle only permutes 16-byte chunks inside a row, so a
+    // row's sum is the sum over its 128-byte line. Thread et takes chunks
+    // et, et + 128, ...; the 8 lanes of a row combine by shuffles at the end.
+    constexpr int kChunks = (SWAP ? BN : BM) * 8;
     constexpr int kPer = (kChunks + 127) / 128;
     const int et = threadIdx.x - 64;
     float acc[kPer];
@@ -305,7 +448,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int s = i % stages;
       const uint32_t ph = (i / stages) & 1u;
       if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.err, 104))) break;
-      const uint8_t* xs = sB + s * S::kB;
+      const uint8_t* xs = SWAP ? sB + s * S::kB : sA + s * S::kA;
 #pragma unroll
       for (int j = 0; j < kPer; ++j) {
         const int idx = et + j * 128;
@@ -345,9 +488,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sub = warp & 3;
     const int row = sub * 32 + lane;  // TMEM lane == tile row
     const uint32_t taddr = tmem + (static_cast<uint32_t>(sub * 32) << 16);
+    bool fused_done = false;
+    if constexpr (!SWAP && !SPLIT && BN >= 32) {
+      if (p.epi.kind != 0) {
+        const int m = a_row0 + row;
+        const bool valid = ok && m < p.M;
+        const float rstd = do_norm ? rsqrtf(s_ss[row] / static_cast<float>(p.K) + p.epi.eps) : 1.f;
+        rows_epilogue<BN>(p, taddr, m, b_row0, rstd, valid);
+        fused_done = true;
+      }
+    }
     float* red = reinterpret_cast<float*>(smem);  // split-K parking tile (output-major)
 #pragma unroll 1
-    for (int c = 0; c < BN; c += CH) {
+    for (int c = 0; c < BN && !fused_done; c += CH) {
       uint32_t r[32];
       if constexpr (CH == 32) {
         tmem_ld_32x32b_x32(taddr + c, r);
@@ -445,7 +598,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const uint32_t red_base = smem_u32(smem);
     const int tok0 = SWAP ? b_row0 : a_row0;
     const int feat0 = SWAP ? a_row0 : b_row0;
-    if (SWAP && do_norm) {
+    if (do_norm) {
       // rstd of this rank's rows from every CTA's partial sum of squares
       for (int r = threadIdx.x; r < rows_per; r += kThreads) {
         const int orow = rank * rows_per + r;
@@ -456,13 +609,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       __syncthreads();
     }
-    if (SWAP && (p.epi.kind & kEpiSiluMul) != 0) {
-      // gate features at tile columns [0, 64), the matching up features at
-      // [64, 128); output feature = feat0 / 2 + column
-      const int vecs = rows_per * 16;
+    if ((p.epi.kind & kEpiSiluMul) != 0) {
+      // every 128 tile columns hold 64 gate features, then the matching 64 up
+      // features; output feature = feat0 / 2 + block * 64 + column
+      constexpr int kBlocks = kOutCols / 128;
+      const int vecs = rows_per * kBlocks * 16;
       for (int e = threadIdx.x; e < vecs; e += kThreads) {
-        const int orow = rank * rows_per + e / 16;
-        const int ocol = (e % 16) * 4;
+        const int orow = rank * rows_per + e / (kBlocks * 16);
+        const int blk = (e % (kBlocks * 16)) / 16;
+        const int ocol = blk * 128 + (e % 16) * 4;
         const float4 g = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol) * 4), nsplit);
         const float4 u = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol + 64) * 4), nsplit);
         const int m = tok0 + orow;
@@ -483,27 +638,29 @@ __global__ void __launch_bounds__(kThreads, 1)
           const float gq = round_bf16(gv[q]), uq = round_bf16(uv[q]);
           v[q] = gq / (1.f + __expf(-gq)) * uq;
         }
-        store4_bf16(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + feat0 / 2 + ocol, v);
+        store4_bf16(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + feat0 / 2 + blk * 64 +
+                        (e % 16) * 4,
+                    v);
       }
     } else {
       const int vecs = rows_per * (kOutCols / 4);
-      const bool rope = SWAP && (p.epi.kind & kEpiRope) != 0;
-      const int head = feat0 / BM;  // kEpiRope: one 128-feature head per tile
+      const bool rope = (p.epi.kind & kEpiRope) != 0;
       for (int e = threadIdx.x; e < vecs; e += kThreads) {
-        // kEpiRope relies on one warp covering one token row: kOutCols / 4
-        // == 32 vectors per row and kThreads is a multiple of 32
+        // kEpiRope relies on one warp covering one 128-feature head of one
+        // token row: kOutCols / 4 is a multiple of 32 vectors per row and
+        // kThreads a multiple of 32 (the host asks for N tiles of >= 128)
         const int orow = rank * rows_per + e / (kOutCols / 4);
         const int ocol = (e % (kOutCols / 4)) * 4;
         const float4 acc = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol) * 4), nsplit);
         const int m = tok0 + orow;
         const int n = feat0 + ocol;
         if (m >= p.M || n >= p.N) continue;  // uniform per warp for kEpiRope
-        const float sc = (SWAP && do_norm) ? s_rstd[orow] : 1.f;
+        const float sc = do_norm ? s_rstd[orow] : 1.f;
         float v[4] = {acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc};
         if (p.bias != nullptr)
           for (int q = 0; q < 4; ++q) v[q] += n + q < p.N ? __bfloat162float(p.bias[n + q]) : 0.f;
         if (rope) {
-          rope_epilogue(p, head, m, ocol, v);
+          rope_epilogue(p, n / 128, m, n % 128, v);
           continue;
         }
         if ((p.epi.kind & kEpiResidual) != 0) {
@@ -560,9 +717,11 @@ void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp
   cfg.stream = stream;
   cudaLaunchAttribute attrs[2];
   int n = 0;
-  attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attrs[n].val.programmaticStreamSerializationAllowed = 1;
-  ++n;
+  if (pdl_enabled()) {
+    attrs[n].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attrs[n].val.programmaticStreamSerializationAllowed = 1;
+    ++n;
+  }
   if (SPLIT) {
     attrs[n].id = cudaLaunchAttributeClusterDimension;
     attrs[n].val.clusterDim.x = 1;
@@ -580,8 +739,10 @@ template <int BN, int STAGES, bool SWAP>
 void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, dim3 grid,
                     cudaStream_t stream) {
   kp.stages = std::max(1, std::min(STAGES, kp.kb_per_split));
-  // fused epilogues live in the cluster (split-K) path; one split = a cluster of one
-  if (splits > 1 || kp.epi.kind != 0) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
+  // fused epilogues of weight-major tiles live in the cluster (split-K) path
+  // (one split = a cluster of one); token-major tiles without split-K apply
+  // them straight from TMEM
+  if (splits > 1 || (SWAP && kp.epi.kind != 0)) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
   else launch_tile<BN, STAGES, SWAP, false>(ta, tb, kp, grid, 1, stream);
 }
 
@@ -657,11 +818,12 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   if (a.force_bn == 16 && a.force_mode == 1)
     throw std::runtime_error("minisgl.gemm: token-major tiles need an N tile of at least 32");
   const int fused = a.epi.kind;
-  const bool needs_swap = (fused & (kEpiNorm | kEpiSiluMul | kEpiRope)) != 0;
   if (fused != 0) {
     if (a.out_f32) throw std::runtime_error("minisgl.gemm: fused epilogues write bf16");
-    if (needs_swap && a.force_mode == 1)
-      throw std::runtime_error("minisgl.gemm: norm / silu / rope epilogues need weight-major tiles");
+    // token-major tiles hold whole 128-feature heads / gate|up blocks only
+    // when their N tile is a multiple of 128
+    if ((fused & (kEpiSiluMul | kEpiRope)) != 0 && a.force_mode == 1 && a.force_bn % 128 != 0)
+      throw std::runtime_error("minisgl.gemm: token-major silu / rope epilogues need an N tile of 128 or 256");
     if ((fused & kEpiResidual) != 0 && (a.epi.residual == nullptr || a.epi.ld_res % 4 != 0))
       throw std::runtime_error("minisgl.gemm: residual epilogue needs a residual with row stride % 4 == 0");
     if ((fused & kEpiSiluMul) != 0 && (a.N % 128 != 0 || (fused & (kEpiRope | kEpiResidual)) != 0))
@@ -673,7 +835,8 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
         throw std::runtime_error("minisgl.gemm: rope epilogue needs head_dim 128 qkv weights and cache pointers");
     }
   }
-  const Plan pl = make_plan(a.M, a.N, a.K, needs_swap ? 2 : a.force_mode, a.force_splits, a.force_bn);
+  const bool default_swap = fused != 0 && a.force_mode == 0;  // fused calls default to weight-major tiles
+  const Plan pl = make_plan(a.M, a.N, a.K, default_swap ? 2 : a.force_mode, a.force_splits, a.force_bn);
   KParams kp;
   kp.out = a.out;
   kp.bias = reinterpret_cast<const __nv_bfloat16*>(a.bias);

@@ -12,11 +12,23 @@
 
 #include <cuda_runtime.h>
 
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 #include <utility>
 
 namespace minisgl {
+
+// MINISGL_NO_PDL=1 launches everything with plain stream order (a debugging
+// and measurement switch; the kernels' griddepcontrol instructions are then
+// no-ops).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("MINISGL_NO_PDL");
+    return v == nullptr || v[0] == '\0' || v[0] == '0';
+  }();
+  return on;
+}
 
 template <typename... KArgs, typename... Args>
 void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
@@ -30,7 +42,7 @@ void launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cuda
   attr.id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr.val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = &attr;
-  cfg.numAttrs = 1;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
   if (e != cudaSuccess) throw std::runtime_error(std::string("minisgl: kernel launch failed: ") + cudaGetErrorString(e));
 }

@@ -175,7 +175,8 @@ class Engine:
             return
         t0 = time.perf_counter()
         cache = os.environ.get("MINISGL_GEMM_TUNE_CACHE") or None
-        plans = gemm_tune.tune(self._gemm_shapes(), bs, self.device, cache)
+        kinds = self.model.fused_gemm_kinds() if hasattr(self.model, "fused_gemm_kinds") else {}
+        plans = gemm_tune.tune(self._gemm_shapes(), bs, self.device, cache, fused=kinds, prefill=True)
         logger.info_rank0(f"Tuned {len(plans)} GEMM plans in {time.perf_counter() - t0:.1f}s")
 
     def _init_communication(self, config: EngineConfig):

@@ -4,7 +4,7 @@ head. Family differences are constructor flags (qkv bias, q/k norm, MoE)."""
 
 from __future__ import annotations
 
-from typing import TYPE_CHECKING, Optional, Tuple
+from typing import TYPE_CHECKING, Dict, Optional, Tuple
 
 import torch
 
@@ -128,6 +128,22 @@ class DecoderForCausalLM(BaseLLMModel):
         """True when norm weights are folded into qkv / gate_up and gate|up
         rows are interleaved (what ``state_dict`` then returns)."""
         return any(l.input_layernorm.folded for l in self.model.layers.op_list)
+
+    def fused_gemm_kinds(self) -> Dict[Tuple[int, int], Tuple[int, int, int]]:
+        """(N, K) of each projection the fused decode path runs -> (epilogue
+        kind, local q heads, local kv heads), for the GEMM autotuner."""
+        out: Dict[Tuple[int, int], Tuple[int, int, int]] = {}
+        if not self.model.fusable:
+            return out
+        for layer in self.model.layers.op_list:
+            attn = layer.self_attn
+            hq, hk = attn.attn.num_qo_heads, attn.attn.num_kv_heads
+            out[tuple(attn.qkv_proj.weight.shape)] = (ops.EPI_NORM | ops.EPI_ROPE, hq, hk)
+            out[tuple(attn.o_proj.weight.shape)] = (ops.EPI_RESIDUAL, hq, hk)
+            if layer._fused_mlp:
+                out[tuple(layer.mlp.gate_up_proj.weight.shape)] = (ops.EPI_NORM | ops.EPI_SILU, hq, hk)
+                out[tuple(layer.mlp.down_proj.weight.shape)] = (ops.EPI_RESIDUAL, hq, hk)
+        return out
 
     def forward(self) -> torch.Tensor:
         hidden = self.model.forward(get_global_ctx().batch.input_ids)

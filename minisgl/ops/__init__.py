@@ -89,7 +89,7 @@ def check_device_errors(device: torch.device) -> None:
 
 
 # ------------------------------------------------------------------- GEMM
-from .gemm_tune import PLANS as _gemm_plans  # noqa: E402  (autotuned plans by (M, N, K))
+from .gemm_tune import lookup as _gemm_lookup  # noqa: E402  (autotuned plans by (M, N, K))
 
 def gemm(
     x: torch.Tensor,
@@ -108,9 +108,18 @@ def gemm(
         return y
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
+    plan = _gemm_lookup(x.shape[0], w.shape[0], x.shape[1])
+    if plan is not None and plan[0] == 3 and (bias is None or out.dtype == x.dtype):
+        # library GEMM: tuned faster than every tcgen05 plan for this shape
+        if out.dtype != x.dtype:
+            torch.mm(x, w.t(), out_dtype=out.dtype, out=out)  # e.g. bf16 x bf16 -> fp32 logits
+        elif bias is None:
+            torch.matmul(x, w.t(), out=out)
+        else:
+            torch.addmm(bias, x, w.t(), out=out)
+        return out
     _count()
-    plan = _gemm_plans.get((x.shape[0], w.shape[0], x.shape[1]))
-    if plan is None:
+    if plan is None or plan[0] == 3:
         native().gemm(out, x, w, bias, None, 0, 0, error_word(x.device))
     else:
         mode, bn, splits = plan
@@ -120,7 +129,7 @@ def gemm(
 
 # ------------------------------------------------------------ elementwise
 EPI_NORM, EPI_RESIDUAL, EPI_SILU, EPI_ROPE = 1, 2, 4, 8
-from .gemm_tune import SWAP_PLANS as _gemm_swap_plans  # noqa: E402  (best weight-major plans)
+from .gemm_tune import FUSED_PLANS as _gemm_fused_plans  # noqa: E402  (best plans fused epilogues accept)
 
 
 def gemm_fused(
@@ -133,10 +142,11 @@ def gemm_fused(
     silu: bool = False,
     rope: Optional[dict] = None,
     out: Optional[torch.Tensor] = None,
-    plan: Optional[Tuple[int, int]] = None,
+    plan: Optional[Tuple[int, int, int]] = None,
 ) -> torch.Tensor:
-    """GEMM with a fused decode epilogue (weight-major tiles; ``plan`` =
-    (token tile, K splits) overrides the tuned / default tile plan):
+    """GEMM with a fused epilogue (``plan`` = (mode: 1 token-major / 2
+    weight-major tiles, N tile, K splits) overrides the tuned / default
+    plan; token-major tiles need an N tile of 128 or 256 for silu / rope):
 
     * ``norm_eps``: rows of x are RMS-normalised (x is the raw residual
       stream; the norm weight must already be folded into ``w``'s columns);
@@ -158,15 +168,13 @@ def gemm_fused(
         out = torch.empty(M, N // 2 if silu else N, dtype=x.dtype, device=x.device)
     kind = (EPI_NORM if norm_eps is not None else 0) | (EPI_RESIDUAL if residual is not None else 0)
     kind |= (EPI_SILU if silu else 0) | (EPI_ROPE if rope is not None else 0)
-    if plan is not None:
-        bn, splits = plan
-    else:
-        tuned = _gemm_swap_plans.get((M, N, x.shape[1]))
-        splits, bn = (tuned[2], tuned[1]) if tuned is not None else (0, 0)
+    if plan is None:
+        plan = _gemm_fused_plans.get((M, N, x.shape[1]), (0, 0, 0))
+    mode, bn, splits = plan
     r = rope or {}
     _count()
     native().gemm_fused(
-        out, x, w, bias, splits, bn, error_word(x.device), kind, norm_eps or 0.0, residual,
+        out, x, w, bias, mode, splits, bn, error_word(x.device), kind, norm_eps or 0.0, residual,
         r.get("q_norm_w"), r.get("k_norm_w"), r.get("head_eps", 0.0), r.get("cos_sin"), r.get("positions"),
         r.get("out_loc"), r.get("k_cache"), r.get("v_cache"), r.get("hq", 0), r.get("hk", 0), r.get("page_size", 0),
     )

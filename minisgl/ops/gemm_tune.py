@@ -23,12 +23,20 @@ import torch
 
 Plan = Tuple[int, int, int]  # (mode: 1 token-major / 2 weight-major, n tile, splits)
 PLANS: Dict[Tuple[int, int, int], Plan] = {}
-# best weight-major plan per shape: the fused-epilogue GEMMs need those tiles
-SWAP_PLANS: Dict[Tuple[int, int, int], Plan] = {}
+# best plan per shape among those the fused epilogues accept (weight-major
+# tiles, or token-major tiles with an N tile of 128 / 256)
+FUSED_PLANS: Dict[Tuple[int, int, int], Plan] = {}
 
 
 # batch sizes that are tuned; other sizes use the plan of the next tuned size
 TUNED_SIZES = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
+# prefill chunk sizes that are tuned; longer chunks use the plan of the next
+# one (or of the largest)
+PREFILL_SIZES = (512, 2048, 8192)
+# mode 3: the cuBLAS GEMM (through torch). Plain GEMMs (no fused epilogue,
+# bf16 out) use it for the shapes where it times faster than every tcgen05
+# plan; fused-epilogue GEMMs always run the tcgen05 kernel.
+LIBRARY: Plan = (3, 0, 0)
 
 
 def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
@@ -58,13 +66,10 @@ def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
 _COLD_BYTES = 192 << 20
 
 
-def _time_plan(native, out, x, ws: List[torch.Tensor], plan: Plan, reps: int = 8) -> float:
-    mode, bn, s = plan
+def _time_runs(run, ws: List[torch.Tensor], reps: int = 8) -> float:
+    """Mean ms of ``run(w)`` over back-to-back launches in a CUDA graph that
+    cycles through the weight copies ``ws``; best of three replays."""
     reps = max(reps, len(ws))
-
-    def run(w):
-        native.gemm(out, x, w, None, None, s, mode, None, bn)
-
     run(ws[0])
     torch.cuda.synchronize()
     g = torch.cuda.CUDAGraph()
@@ -85,16 +90,66 @@ def _time_plan(native, out, x, ws: List[torch.Tensor], plan: Plan, reps: int = 8
     return best
 
 
+def _fused_candidates(M: int, K: int, kind: int) -> List[Plan]:
+    """Plans a fused-epilogue GEMM of this kind accepts: weight-major tiles,
+    token-major tiles (with whole 128-feature heads / gate|up blocks when the
+    epilogue needs them)."""
+    from minisgl import ops
+
+    num_kb = (K + 63) // 64
+    out = [p for p in candidates(M, K, full=False) if p[0] == 2]
+    if M >= 64:
+        whole = (kind & (ops.EPI_ROPE | ops.EPI_SILU)) != 0
+        for bn in (128, 256) if whole else (64, 128, 256):
+            for s in (1, 2, 4, 8):
+                if s <= num_kb:
+                    out.append((1, bn, s))
+    return out
+
+
+class _FusedBench:
+    """Dummy epilogue operands for timing a fused GEMM of one kind."""
+
+    def __init__(self, kind: int, hq: int, hk: int, M: int, N: int, device: torch.device) -> None:
+        from minisgl import ops
+
+        self.kw: dict = {}
+        self.out = torch.empty(M, N // 2 if kind & ops.EPI_SILU else N, dtype=torch.bfloat16, device=device)
+        if kind & ops.EPI_NORM:
+            self.kw["norm_eps"] = 1e-6
+        if kind & ops.EPI_SILU:
+            self.kw["silu"] = True
+        if kind & ops.EPI_RESIDUAL:
+            self.kw["residual"] = self.out
+        if kind & ops.EPI_ROPE:
+            page = 64
+            pages = (M + page - 1) // page + 1
+            cache = torch.zeros(pages, hk, page, 128, dtype=torch.bfloat16, device=device)
+            ang = torch.rand(64, 64, device=device)
+            self.kw["rope"] = dict(
+                positions=torch.zeros(M, dtype=torch.int32, device=device),
+                cos_sin=torch.cat([ang.cos(), ang.sin()], 1).contiguous(),
+                out_loc=torch.arange(M, dtype=torch.int32, device=device), q_norm_w=None, k_norm_w=None,
+                head_eps=1e-6, k_cache=cache, v_cache=torch.zeros_like(cache), hq=hq, hk=hk, page_size=page)
+
+
 def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: torch.device,
-         cache_file: Optional[str] = None) -> Dict[Tuple[int, int, int], Plan]:
+         cache_file: Optional[str] = None,
+         fused: Optional[Dict[Tuple[int, int], Tuple[int, int, int]]] = None,
+         prefill: bool = False) -> Dict[Tuple[int, int, int], Plan]:
     """Find the fastest plan for every (M, N, K); M from ``batch_sizes``,
-    (N, K) from ``shapes``. Returns (and installs) the plan table."""
+    (N, K) from ``shapes``. ``fused`` maps (N, K) to (epilogue kind, q heads,
+    kv heads) for the projections the fused decode layers run: those get a
+    plan of their own (FUSED_PLANS), timed with that epilogue. ``prefill``
+    also tunes the chunk sizes of PREFILL_SIZES. Returns (and installs) the
+    plain plan table."""
     from minisgl import ops
 
     native = ops.native()
-    key_dev = torch.cuda.get_device_name(device) + "|cold-weights"
+    fused = dict(fused or {})
+    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds"
     cached = _load(cache_file, key_dev)
-    shapes = sorted(set(shapes))
+    shapes = sorted(set(shapes) | set(fused))
     wanted = sorted(set(int(m) for m in batch_sizes if m > 0))
     # tune representative sizes only; every wanted size maps to the next one
     sizes = sorted({next((t for t in TUNED_SIZES if t >= m), m) for m in wanted})
@@ -107,26 +162,43 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
             omax = torch.empty(max(sizes), N, device=device, dtype=torch.bfloat16)
             for M in sizes:
                 key = (M, N, K)
-                skey = (-M, N, K)  # weight-major entry of the cache
-                if key in cached and skey in cached:
-                    PLANS[key] = cached[key]
-                    SWAP_PLANS[key] = cached[skey]
-                    continue
+                skey = (-M, N, K)  # fused-epilogue entry of the cache
                 x, out = xmax[:M], omax[:M]
+                if key in cached:
+                    PLANS[key] = cached[key]
+                else:
+                    timed = []
+                    for plan in candidates(M, K, full=False) + [LIBRARY]:
+                        mode, bn, s = plan
+                        try:
+                            if plan == LIBRARY:
+                                timed.append((_time_runs(lambda w_: torch.matmul(x, w_.t(), out=out), ws), plan))
+                            else:
+                                timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
+                                    out, x, w_, None, None, sp, m, None, b), ws), plan))
+                        except RuntimeError:
+                            continue
+                    if timed:
+                        PLANS[key] = cached[key] = min(timed)[1]
+                if (N, K) not in fused:
+                    continue
+                if skey in cached:
+                    FUSED_PLANS[key] = cached[skey]
+                    continue
+                kind, hq, hk = fused[(N, K)]
+                fb = _FusedBench(kind, hq, hk, M, N, device)
                 timed = []
-                for plan in candidates(M, K, full=False):
+                for plan in _fused_candidates(M, K, kind):
                     try:
-                        timed.append((_time_plan(native, out, x, ws, plan), plan))
+                        timed.append((_time_runs(lambda w_, p_=plan: ops.gemm_fused(
+                            x, w_, out=fb.out, plan=p_, **fb.kw), ws), plan))
                     except RuntimeError:
                         continue
                 if timed:
-                    PLANS[key] = min(timed)[1]
-                    cached[key] = PLANS[key]
-                    swap = [t for t in timed if t[1][0] == 2]
-                    if swap:
-                        SWAP_PLANS[key] = min(swap)[1]
-                        cached[skey] = SWAP_PLANS[key]
+                    FUSED_PLANS[key] = cached[skey] = min(timed)[1]
             del w, ws, xmax, omax
+    if prefill:
+        _tune_prefill(native, shapes, device, cached)
     torch.cuda.synchronize(device)
     _save(cache_file, key_dev, cached)
     # wanted sizes that were not tuned themselves borrow the next tuned plan
@@ -135,18 +207,51 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
             t = next((s for s in sizes if s >= m), None)
             if t is not None and (t, N, K) in PLANS:
                 PLANS.setdefault((m, N, K), PLANS[(t, N, K)])
-            if t is not None and (t, N, K) in SWAP_PLANS:
-                SWAP_PLANS.setdefault((m, N, K), SWAP_PLANS[(t, N, K)])
+            if t is not None and (t, N, K) in FUSED_PLANS:
+                FUSED_PLANS.setdefault((m, N, K), FUSED_PLANS[(t, N, K)])
     return dict(PLANS)
 
 
+def _tune_prefill(native, shapes, device: torch.device, cached: Dict[Tuple[int, int, int], Plan]) -> None:
+    """Plain plans for long prefill chunks: the default token-major tiles
+    against the library GEMM (the weight-major and split-K plans only pay
+    off for short batches)."""
+    for N, K in shapes:
+        for M in PREFILL_SIZES:
+            key = (M, N, K)
+            if M * N * 2 > (256 << 20):  # e.g. the LM head: prefill computes only last-token logits
+                continue
+            if key in cached:
+                PLANS[key] = cached[key]
+                continue
+            x = torch.randn(M, K, device=device, dtype=torch.bfloat16)
+            out = torch.empty(M, N, device=device, dtype=torch.bfloat16)
+            w = torch.randn(N, K, device=device, dtype=torch.bfloat16) * 0.02
+            timed = []
+            for plan in ((1, 256, 1), (1, 128, 1), LIBRARY):
+                mode, bn, s = plan
+                if plan == LIBRARY:
+                    timed.append((_time_runs(lambda w_: torch.matmul(x, w_.t(), out=out), [w], reps=4), plan))
+                else:
+                    timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
+                        out, x, w_, None, None, sp, m, None, b), [w], reps=4), plan))
+            PLANS[key] = cached[key] = min(timed)[1]
+            del x, out, w
+
+
 def lookup(M: int, N: int, K: int) -> Optional[Plan]:
-    return PLANS.get((M, N, K))
+    """The plan for (M, N, K): tuned for M itself, or for the next tuned
+    prefill size (the largest one beyond it)."""
+    plan = PLANS.get((M, N, K))
+    if plan is not None or M <= TUNED_SIZES[-1]:
+        return plan
+    size = next((p for p in PREFILL_SIZES if p >= M), PREFILL_SIZES[-1])
+    return PLANS.get((size, N, K))
 
 
 def clear() -> None:
     PLANS.clear()
-    SWAP_PLANS.clear()
+    FUSED_PLANS.clear()
 
 
 def _load(path: Optional[str], dev: str) -> Dict[Tuple[int, int, int], Plan]:
