@@ -109,17 +109,8 @@ def gemm(
     if out is None:
         out = torch.empty(x.shape[0], w.shape[0], dtype=out_dtype, device=x.device)
     plan = _gemm_lookup(x.shape[0], w.shape[0], x.shape[1])
-    if plan is not None and plan[0] == 3 and (bias is None or out.dtype == x.dtype):
-        # library GEMM: tuned faster than every tcgen05 plan for this shape
-        if out.dtype != x.dtype:
-            torch.mm(x, w.t(), out_dtype=out.dtype, out=out)  # e.g. bf16 x bf16 -> fp32 logits
-        elif bias is None:
-            torch.matmul(x, w.t(), out=out)
-        else:
-            torch.addmm(bias, x, w.t(), out=out)
-        return out
     _count()
-    if plan is None or plan[0] == 3:
+    if plan is None:
         native().gemm(out, x, w, bias, None, 0, 0, error_word(x.device))
     else:
         mode, bn, splits = plan

@@ -33,10 +33,7 @@ TUNED_SIZES = (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 160, 192, 224, 256)
 # prefill chunk sizes that are tuned; longer chunks use the plan of the next
 # one (or of the largest)
 PREFILL_SIZES = (512, 2048, 8192)
-# mode 3: the cuBLAS GEMM (through torch). Plain GEMMs (no fused epilogue,
-# bf16 out) use it for the shapes where it times faster than every tcgen05
-# plan; fused-epilogue GEMMs always run the tcgen05 kernel.
-LIBRARY: Plan = (3, 0, 0)
+
 
 
 def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
@@ -147,7 +144,7 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
 
     native = ops.native()
     fused = dict(fused or {})
-    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds"
+    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only"
     cached = _load(cache_file, key_dev)
     shapes = sorted(set(shapes) | set(fused))
     wanted = sorted(set(int(m) for m in batch_sizes if m > 0))
@@ -168,14 +165,11 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
                     PLANS[key] = cached[key]
                 else:
                     timed = []
-                    for plan in candidates(M, K, full=False) + [LIBRARY]:
+                    for plan in candidates(M, K, full=False):
                         mode, bn, s = plan
                         try:
-                            if plan == LIBRARY:
-                                timed.append((_time_runs(lambda w_: torch.matmul(x, w_.t(), out=out), ws), plan))
-                            else:
-                                timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
-                                    out, x, w_, None, None, sp, m, None, b), ws), plan))
+                            timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
+                                out, x, w_, None, None, sp, m, None, b), ws), plan))
                         except RuntimeError:
                             continue
                     if timed:
@@ -213,9 +207,9 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
 
 
 def _tune_prefill(native, shapes, device: torch.device, cached: Dict[Tuple[int, int, int], Plan]) -> None:
-    """Plain plans for long prefill chunks: the default token-major tiles
-    against the library GEMM (the weight-major and split-K plans only pay
-    off for short batches)."""
+    """Plain plans for long prefill chunks: token-major tiles of 128 or 256
+    features (the weight-major and split-K plans only pay off for short
+    batches)."""
     for N, K in shapes:
         for M in PREFILL_SIZES:
             key = (M, N, K)
@@ -228,13 +222,10 @@ def _tune_prefill(native, shapes, device: torch.device, cached: Dict[Tuple[int, 
             out = torch.empty(M, N, device=device, dtype=torch.bfloat16)
             w = torch.randn(N, K, device=device, dtype=torch.bfloat16) * 0.02
             timed = []
-            for plan in ((1, 256, 1), (1, 128, 1), LIBRARY):
+            for plan in ((1, 256, 1), (1, 128, 1)):
                 mode, bn, s = plan
-                if plan == LIBRARY:
-                    timed.append((_time_runs(lambda w_: torch.matmul(x, w_.t(), out=out), [w], reps=4), plan))
-                else:
-                    timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
-                        out, x, w_, None, None, sp, m, None, b), [w], reps=4), plan))
+                timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
+                    out, x, w_, None, None, sp, m, None, b), [w], reps=4), plan))
             PLANS[key] = cached[key] = min(timed)[1]
             del x, out, w
 
