@@ -58,7 +58,7 @@ cudaStream_t stream_of(const at::Tensor& t) {
 void gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w,
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& workspace,
           int64_t force_splits, int64_t force_mode, const c10::optional<at::Tensor>& err, int64_t force_bn,
-          const c10::optional<at::Tensor>& trace) {
+          const c10::optional<at::Tensor>& trace, int64_t force_kps) {
   check_cuda(x, "x");
   check_cuda(w, "w");
   check_cuda(out, "out");
@@ -102,6 +102,7 @@ void gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w,
   a.force_splits = static_cast<int>(force_splits);
   a.force_mode = static_cast<int>(force_mode);
   a.force_bn = static_cast<int>(force_bn);
+  a.force_kps = static_cast<int>(force_kps);
   a.trace = nullptr;
   if (trace.has_value()) {
     MSG_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous(), "trace must be CUDA int64");
@@ -496,7 +497,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm, "tcgen05 bf16 GEMM: out = x @ w^T (+ bias)", py::arg("out"), py::arg("x"),
         py::arg("w"), py::arg("bias") = py::none(), py::arg("workspace") = py::none(),
         py::arg("force_splits") = 0, py::arg("force_mode") = 0, py::arg("err") = py::none(),
-        py::arg("force_bn") = 0, py::arg("trace") = py::none());
+        py::arg("force_bn") = 0, py::arg("trace") = py::none(), py::arg("force_kps") = 0);
   m.def("gemm_plan", [](int64_t M, int64_t N, int64_t K) { return minisgl::gemm_plan_desc(M, N, K); });
   m.def("gemm_workspace_elems", &gemm_workspace_elems);
   m.def("rmsnorm", &rmsnorm);

@@ -54,6 +54,7 @@ struct KParams {
   int kb_per_split;
   int num_kb;
   int stages;          // ring depth used by this launch (<= the template maximum)
+  int kps;             // k-blocks per stage: >1 loads them with one 3-D TMA box per operand
   int K;               // reduction length (the RMSNorm mean of kEpiNorm)
   int out_f32;
   GemmEpilogue epi;    // fused epilogue (weight-major split-K instantiations only)
@@ -86,14 +87,14 @@ struct Smem {
   // bytes of a launch whose ring holds `stages` k-blocks: a CTA with fewer
   // k-blocks than the template depth asks for less shared memory, so more
   // CTAs (of this and of neighbouring kernels) stay resident together
-  __host__ __device__ static constexpr uint32_t main_bytes(int stages, bool split) {
-    const uint32_t pipe = static_cast<uint32_t>(stages) * (kA + kB);
+  __host__ __device__ static constexpr uint32_t main_bytes(int stages, bool split, int kps = 1) {
+    const uint32_t pipe = static_cast<uint32_t>(stages * kps) * (kA + kB);
     return split && kRed > pipe ? kRed : pipe;
   }
   // + per-token sum of squares and rstd arrays (kEpiNorm) after the barriers
   static constexpr int kRows = BN > BM ? BN : BM;
-  static constexpr uint32_t bytes(int stages, bool split) {
-    return main_bytes(stages, split) + 1024 + 256 + 2 * kRows * 4;
+  static constexpr uint32_t bytes(int stages, bool split, int kps = 1) {
+    return main_bytes(stages, split, kps) + 1024 + 256 + 2 * kRows * 4;
   }
 };
 
@@ -324,13 +325,15 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   const int stages = p.stages;
+  const int kps = p.kps;
+  const uint32_t stA = kps * S::kA, stB = kps * S::kB;  // bytes of one stage per operand
   uint8_t* sA = smem;
-  uint8_t* sB = smem + stages * S::kA;
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::main_bytes(stages, SPLIT));
+  uint8_t* sB = smem + stages * stA;
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + S::main_bytes(stages, SPLIT, kps));
   uint64_t* empty = full + stages;
   uint64_t* done = empty + stages;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
-  float* s_ss = reinterpret_cast<float*>(smem + S::main_bytes(stages, SPLIT) + 256);  // [token rows]
+  float* s_ss = reinterpret_cast<float*>(smem + S::main_bytes(stages, SPLIT, kps) + 256);  // [token rows]
   float* s_rstd = s_ss + S::kRows;                                                     // [token rows]
   // kEpiNorm: the epilogue warps read every x tile of the ring too, so a
   // stage is free once the MMA commit and those four warps have released it
@@ -378,37 +381,45 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int x_row = SWAP ? b_row0 : a_row0;
     uint8_t* sW = SWAP ? sA : sB;
     uint8_t* sX = SWAP ? sB : sA;
-    constexpr uint32_t kW = SWAP ? S::kA : S::kB;
-    constexpr uint32_t kX = SWAP ? S::kB : S::kA;
-    const int pre = min(nkb, stages);
+    const uint32_t sw = SWAP ? stA : stB;
+    const uint32_t sx = SWAP ? stB : stA;
+    const uint32_t stage_bytes = stA + stB;
+    const int nst = (nkb + kps - 1) / kps;  // stages of this CTA's K range
+    // stage i holds k-blocks [kb0 + i * kps, + kps): one 2-D box per operand,
+    // or one 3-D box of kps k-blocks
+    auto load = [&](const CUtensorMap* tm, uint8_t* dst, int i, int row, uint64_t* bar) {
+      if (kps == 1) tma_load_2d(dst, tm, bar, (kb0 + i) * BK, row);
+      else tma_load_3d(dst, tm, bar, 0, row, kb0 + i * kps);
+    };
+    const int pre = min(nst, stages);
     if (lane == 0) {
       for (int i = 0; i < pre; ++i) {
-        mbar_arrive_expect_tx(&full[i], S::kA + S::kB);
-        tma_load_2d(sW + i * kW, tw, &full[i], (kb0 + i) * BK, w_row);
+        mbar_arrive_expect_tx(&full[i], stage_bytes);
+        load(tw, sW + i * sw, i, w_row, &full[i]);
       }
     }
     pdl_wait();
     if (lane == 0) {
       trace_stamp(p, 2);
-      for (int i = 0; i < pre; ++i) tma_load_2d(sX + i * kX, tx, &full[i], (kb0 + i) * BK, x_row);
+      for (int i = 0; i < pre; ++i) load(tx, sX + i * sx, i, x_row, &full[i]);
     }
     __syncwarp();
-    for (int i = pre; i < nkb; ++i) {
+    for (int i = pre; i < nst; ++i) {
       const int s = i % stages;
       const uint32_t ph = (i / stages) & 1u;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u, p.err, 101));
       if (!ok) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], S::kA + S::kB);
-        const int kc = (kb0 + i) * BK;
-        tma_load_2d(sW + s * kW, tw, &full[s], kc, w_row);
-        tma_load_2d(sX + s * kX, tx, &full[s], kc, x_row);
+        mbar_arrive_expect_tx(&full[s], stage_bytes);
+        load(tw, sW + s * sw, i, w_row, &full[s]);
+        load(tx, sX + s * sx, i, x_row, &full[s]);
       }
       __syncwarp();
     }
   } else if (warp == 1) {
     constexpr uint32_t idesc = make_idesc_bf16(BM, BN);
-    for (int i = 0; i < nkb; ++i) {
+    const int nst = (nkb + kps - 1) / kps;
+    for (int i = 0; i < nst; ++i) {
       const int s = i % stages;
       const uint32_t ph = (i / stages) & 1u;
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.err, 102));
@@ -416,12 +427,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       if (lane == 0) {
         if (i == 0) trace_stamp(p, 3);
-        const uint32_t a_addr = smem_u32(sA + s * S::kA);
-        const uint32_t b_addr = smem_u32(sB + s * S::kB);
+        const int nj = min(kps, nkb - i * kps);
+        for (int j = 0; j < nj; ++j) {
+          const uint32_t a_addr = smem_u32(sA + s * stA + j * S::kA);
+          const uint32_t b_addr = smem_u32(sB + s * stB + j * S::kB);
 #pragma unroll
-        for (int k = 0; k < BK / 16; ++k) {
-          tc_mma_f16(tmem, make_sdesc_k_sw128(a_addr + k * 32), make_sdesc_k_sw128(b_addr + k * 32),
-                     idesc, (i > 0 || k > 0) ? 1u : 0u);
+          for (int k = 0; k < BK / 16; ++k) {
+            tc_mma_f16(tmem, make_sdesc_k_sw128(a_addr + k * 32), make_sdesc_k_sw128(b_addr + k * 32),
+                       idesc, (i > 0 || j > 0 || k > 0) ? 1u : 0u);
+          }
         }
         tc_commit(&empty[s]);
       }
@@ -444,21 +458,25 @@ __global__ void __launch_bounds__(kThreads, 1)
     float acc[kPer];
 #pragma unroll
     for (int j = 0; j < kPer; ++j) acc[j] = 0.f;
-    for (int i = 0; i < nkb; ++i) {
+    const int nst = (nkb + kps - 1) / kps;
+    for (int i = 0; i < nst; ++i) {
       const int s = i % stages;
       const uint32_t ph = (i / stages) & 1u;
       if (!__all_sync(0xffffffffu, mbar_wait(&full[s], ph, p.err, 104))) break;
-      const uint8_t* xs = SWAP ? sB + s * S::kB : sA + s * S::kA;
+      const int nj = min(kps, nkb - i * kps);
+      for (int kb = 0; kb < nj; ++kb) {
+        const uint8_t* xs = SWAP ? sB + s * stB + kb * S::kB : sA + s * stA + kb * S::kA;
 #pragma unroll
-      for (int j = 0; j < kPer; ++j) {
-        const int idx = et + j * 128;
-        if (idx < kChunks) {
-          const uint4 raw = *reinterpret_cast<const uint4*>(xs + idx * 16);
-          const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        for (int j = 0; j < kPer; ++j) {
+          const int idx = et + j * 128;
+          if (idx < kChunks) {
+            const uint4 raw = *reinterpret_cast<const uint4*>(xs + idx * 16);
+            const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll
-          for (int q = 0; q < 4; ++q) {
-            const float2 f = __bfloat1622float2(h[q]);
-            acc[j] += f.x * f.x + f.y * f.y;
+            for (int q = 0; q < 4; ++q) {
+              const float2 f = __bfloat1622float2(h[q]);
+              acc[j] += f.x * f.x + f.y * f.y;
+            }
           }
         }
       }
@@ -701,7 +719,7 @@ template <int BN, int STAGES, bool SWAP, bool SPLIT>
 void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, dim3 grid, int splits,
                  cudaStream_t stream) {
   auto kern = gemm_tc_kernel<BN, STAGES, SWAP, SPLIT>;
-  const uint32_t smem = Smem<BN, STAGES>::bytes(kp.stages, SPLIT);
+  const uint32_t smem = Smem<BN, STAGES>::bytes(kp.stages, SPLIT, kp.kps);
   static bool configured[64] = {};  // one attribute call per instantiation and device
   int dev = 0;
   cudaGetDevice(&dev);
@@ -738,7 +756,8 @@ void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp
 template <int BN, int STAGES, bool SWAP>
 void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, KParams kp, dim3 grid,
                     cudaStream_t stream) {
-  kp.stages = std::max(1, std::min(STAGES, kp.kb_per_split));
+  // the ring keeps its byte budget: STAGES k-blocks in stages of kps
+  kp.stages = std::max(1, std::min(STAGES / kp.kps, (kp.kb_per_split + kp.kps - 1) / kp.kps));
   // fused epilogues of weight-major tiles live in the cluster (split-K) path
   // (one split = a cluster of one); token-major tiles without split-K apply
   // them straight from TMEM
@@ -845,14 +864,35 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   kp.ldo = a.ldo;
   kp.kb_per_split = pl.kb_per_split;
   kp.num_kb = (a.K + BK - 1) / BK;
+  // k-blocks per stage: one 3-D TMA box per operand moves kps k-blocks (a
+  // TMA box costs about the same whatever its size, so bigger boxes stream
+  // faster); needs whole k-blocks everywhere and at least two stages
+  {
+    const int max_stages = pl.bn >= 128 ? 4 : 8;
+    const bool ok_k = a.K % BK == 0;
+    auto fits = [&](int c) {
+      return ok_k && kp.num_kb % c == 0 && kp.kb_per_split % c == 0 && max_stages / c >= 2;
+    };
+    if (a.force_kps > 0) {
+      if (a.force_kps != 1 && !fits(a.force_kps))
+        throw std::runtime_error("minisgl.gemm: k-blocks per stage must divide the K range of every split");
+      kp.kps = a.force_kps;
+    } else {
+      kp.kps = fits(4) ? 4 : (fits(2) ? 2 : 1);
+    }
+  }
   kp.out_f32 = a.out_f32 ? 1 : 0;
   kp.K = a.K;
   kp.epi = a.epi;
   kp.err = ErrorSink{a.err};
   kp.trace = reinterpret_cast<unsigned long long*>(a.trace);
+  auto tmap = [&](const void* base, int rows, int ld, int box_rows) {
+    return kp.kps > 1 ? make_tmap_bf16_kblocks(base, rows, a.K, ld, box_rows, kp.kps)
+                      : make_tmap_bf16_2d_sw128(base, rows, a.K, ld, box_rows);
+  };
   if (pl.swap) {
-    CUtensorMap ta = make_tmap_bf16_2d_sw128(a.w, a.N, a.K, a.ldw, BM);
-    CUtensorMap tb = make_tmap_bf16_2d_sw128(a.x, a.M, a.K, a.ldx, pl.bn);
+    CUtensorMap ta = tmap(a.w, a.N, a.ldw, BM);
+    CUtensorMap tb = tmap(a.x, a.M, a.ldx, pl.bn);
     dim3 grid((a.M + pl.bn - 1) / pl.bn, (a.N + BM - 1) / BM, pl.splits);
     switch (pl.bn) {
       case 16: dispatch_split<16, 8, true>(pl.splits, ta, tb, kp, grid, stream); break;
@@ -862,8 +902,8 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
       default: dispatch_split<256, 4, true>(pl.splits, ta, tb, kp, grid, stream); break;
     }
   } else {
-    CUtensorMap ta = make_tmap_bf16_2d_sw128(a.x, a.M, a.K, a.ldx, BM);
-    CUtensorMap tb = make_tmap_bf16_2d_sw128(a.w, a.N, a.K, a.ldw, pl.bn);
+    CUtensorMap ta = tmap(a.x, a.M, a.ldx, BM);
+    CUtensorMap tb = tmap(a.w, a.N, a.ldw, pl.bn);
     dim3 grid((a.N + pl.bn - 1) / pl.bn, (a.M + BM - 1) / BM, pl.splits);
     switch (pl.bn) {
       case 32: dispatch_split<32, 8, false>(pl.splits, ta, tb, kp, grid, stream); break;

@@ -56,6 +56,7 @@ struct GemmArgs {
   int force_splits;   // 0 = heuristic
   int force_mode;     // 0 = heuristic, 1 = token-major tiles, 2 = weight-major tiles (swap)
   int force_bn;       // 0 = heuristic, else the N tile (16..256)
+  int force_kps;      // 0 = heuristic, else k-blocks per pipeline stage (1, 2 or 4)
   void* trace;        // optional uint64 [ctas * 8] phase timestamps (profiling)
   int* err;           // device error word (2 x int32) or nullptr
   GemmEpilogue epi;   // fused epilogue (kind 0: plain store)

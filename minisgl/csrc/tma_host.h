@@ -107,4 +107,17 @@ inline CUtensorMap make_tmap_bf16_2d_sw128(const void* base, uint64_t rows, uint
                    CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// 3-D bf16 map that moves `kps` consecutive 64-column k-blocks of box_rows
+// rows in one TMA instruction: dims {64, rows, cols / 64} with strides
+// {ld * 2, 128} bytes, box {64, box_rows, kps}. The box lands in shared
+// memory as kps back-to-back [box_rows][128 B] sub-tiles, each with the same
+// 128-byte swizzle as the 2-D map (cols must be a multiple of 64).
+inline CUtensorMap make_tmap_bf16_kblocks(const void* base, uint64_t rows, uint64_t cols, uint64_t ld,
+                                          uint32_t box_rows, uint32_t kps) {
+  uint64_t dims[3] = {64, rows, cols / 64};
+  uint64_t strides[2] = {ld * 2, 128};
+  uint32_t box[3] = {64, box_rows, kps};
+  return make_tmap(base, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
 }  // namespace minisgl
