@@ -120,8 +120,17 @@ __device__ __forceinline__ void store4_bf16(__nv_bfloat16* dst, const float (&v)
   *reinterpret_cast<uint2*>(dst) = pk;
 }
 
-// Sum of the float4 at byte offset `addr` of every cluster CTA's parked tile.
+// Sum of the float4 at byte offset `addr` of every cluster CTA's parked tile
+// (one split: this CTA's own tile, read with a plain shared load).
 __device__ __forceinline__ float4 reduce_parts(uint32_t addr, int nsplit) {
+  if (nsplit == 1) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];"
+                 : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
+                 : "r"(addr)
+                 : "memory");
+    return v;
+  }
   constexpr int kMaxS = 16;
   float4 part[kMaxS];
 #pragma unroll
@@ -603,7 +612,10 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 
   if constexpr (SPLIT) {
-    cluster_sync();  // every CTA of the cluster has parked its partial tile
+    // one split (a fused epilogue without split-K) runs without a cluster
+    const bool clustered = gridDim.z > 1;
+    if (clustered) cluster_sync();  // every CTA of the cluster has parked its partial tile
+    else __syncthreads();
     // sum the cluster's partial tiles through distributed shared memory: CTA
     // rank r finalises output rows [r * R / S, (r + 1) * R / S) of the tile
     // (R = tokens in the tile), 4 consecutive features per thread and load
@@ -622,7 +634,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int orow = rank * rows_per + r;
         const uint32_t off = smem_u32(s_ss + orow);
         float ss = 0.f;
-        for (int q = 0; q < nsplit; ++q) ss += ld_shared_cluster_f32(map_shared_rank(off, static_cast<uint32_t>(q)));
+        if (nsplit == 1) ss = s_ss[orow];
+        else
+          for (int q = 0; q < nsplit; ++q) ss += ld_shared_cluster_f32(map_shared_rank(off, static_cast<uint32_t>(q)));
         s_rstd[orow] = rsqrtf(ss / static_cast<float>(p.K) + p.epi.eps);
       }
       __syncthreads();
@@ -703,7 +717,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       }
     }
-    cluster_sync();  // peers may still be reading this CTA's tile
+    if (clustered) cluster_sync();  // peers may still be reading this CTA's tile
   }
 
   tc_fence_before();
@@ -740,7 +754,7 @@ void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp
     attrs[n].val.programmaticStreamSerializationAllowed = 1;
     ++n;
   }
-  if (SPLIT) {
+  if (SPLIT && splits > 1) {
     attrs[n].id = cudaLaunchAttributeClusterDimension;
     attrs[n].val.clusterDim.x = 1;
     attrs[n].val.clusterDim.y = 1;

@@ -19,11 +19,11 @@ from .utils import GatedMLP, MoEMLP, RopeAttn
 if TYPE_CHECKING:
     from .config import ModelConfig
 
-# batches of up to this many tokens take the fused-epilogue path (fewer,
-# weight-major GEMMs: 10-14% faster decode steps at 8-64 requests on a B200);
-# larger batches the token-major GEMMs plus separate norm / RoPE / activation
-# kernels, which measured faster from about 192 requests up
-FUSED_MAX_TOKENS = 160
+# batches of up to this many tokens (every CUDA-graph decode batch) take the
+# fused-epilogue path: 4 GEMMs per layer instead of 4 GEMMs + 4 row kernels
+# (per-layer chain on a B200: 14-22% faster at 1-128 tokens, even at 256);
+# longer prefill chunks take the token-major GEMMs plus separate kernels
+FUSED_MAX_TOKENS = 256
 
 
 class DecoderLayer(BaseOP):
