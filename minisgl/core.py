@@ -128,6 +128,18 @@ class Batch:
 
 
 @dataclass
+class FusedSample:
+    """Sampling fused into the LM head: per-row temperatures (None: greedy),
+    the sampler's seed and device step counter, and an optional output
+    buffer for the tokens."""
+
+    temperatures: Optional[torch.Tensor]
+    seed: int
+    step: torch.Tensor
+    out: Optional[torch.Tensor] = None
+
+
+@dataclass
 class Context:
     """Per-process forward context: the page table (token slots per request
     row), the KV pool, the attention / MoE backends and the active batch."""
@@ -139,6 +151,9 @@ class Context:
     kv_cache: "BaseKVCachePool" = field(init=False)
     extras: dict = field(default_factory=dict)
     _batch: Optional[Batch] = field(default=None, init=False)
+    # set around a forward whose LM head should return sampled tokens instead
+    # of logits (engine / CUDA-graph capture; see FusedSample)
+    fused_sample: Optional["FusedSample"] = field(default=None, init=False)
 
     @property
     def batch(self) -> Batch:

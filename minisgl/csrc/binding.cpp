@@ -207,6 +207,69 @@ void gemm_fused(at::Tensor out, const at::Tensor& x, const at::Tensor& w, const 
   minisgl::launch_gemm(a, stream_of(x));
 }
 
+// Sampled tokens of the LM head without materialising logits: the GEMM's
+// epilogue writes per-vocabulary-tile (best score, index) partials, a second
+// kernel reduces them to one token per row (and advances the step counter
+// when a row sampled with a temperature). temps = None: greedy argmax.
+void gemm_sample(at::Tensor out_tokens, const at::Tensor& x, const at::Tensor& w, const c10::optional<at::Tensor>& bias,
+                 const c10::optional<at::Tensor>& temps, int64_t seed, at::Tensor step, at::Tensor part_val,
+                 at::Tensor part_idx, int64_t force_splits, int64_t force_bn, const c10::optional<at::Tensor>& err) {
+  check_cuda(x, "x");
+  check_cuda(w, "w");
+  check_same_device(x, w);
+  check_rowmajor(x, "x");
+  check_rowmajor(w, "w");
+  check_i32(out_tokens, "out_tokens");
+  check_i32(part_idx, "part_idx");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16, "gemm_sample: bf16 x and w");
+  MSG_CHECK(x.size(1) == w.size(1), "gemm K mismatch");
+  const int64_t M = x.size(0), N = w.size(0);
+  const int64_t ntiles = (N + 127) / 128;
+  MSG_CHECK(out_tokens.numel() == M, "gemm_sample: one token per row");
+  MSG_CHECK(part_val.is_cuda() && part_val.scalar_type() == at::kFloat && part_val.is_contiguous() &&
+                part_val.numel() >= M * ntiles && part_idx.numel() >= M * ntiles,
+            "gemm_sample: partial buffers of M * ceil(N / 128) entries");
+  MSG_CHECK(step.is_cuda() && step.scalar_type() == at::kLong && step.numel() == 1, "gemm_sample: int64 step counter");
+  minisgl::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.bias = nullptr;
+  if (bias.has_value()) {
+    MSG_CHECK(bias->is_cuda() && bias->scalar_type() == at::kBFloat16 && bias->is_contiguous() && bias->numel() == N,
+              "bias must be a contiguous bf16 vector of N elements");
+    a.bias = bias->data_ptr();
+  }
+  a.out = part_val.data_ptr();
+  a.M = static_cast<int>(M);
+  a.N = static_cast<int>(N);
+  a.K = static_cast<int>(x.size(1));
+  a.ldx = static_cast<int>(x.stride(0));
+  a.ldw = static_cast<int>(w.stride(0));
+  a.ldo = static_cast<int>(ntiles);
+  a.force_splits = static_cast<int>(force_splits);
+  a.force_mode = 2;
+  a.force_bn = static_cast<int>(force_bn);
+  a.err = err_ptr(err);
+  minisgl::GemmEpilogue& e = a.epi;
+  e.kind = minisgl::kEpiSample;
+  const float* tp = nullptr;
+  if (temps.has_value()) {
+    MSG_CHECK(temps->is_cuda() && temps->scalar_type() == at::kFloat && temps->is_contiguous() && temps->numel() >= M,
+              "gemm_sample: float32 temperatures per row");
+    tp = temps->data_ptr<float>();
+  }
+  e.temps = tp;
+  e.seed = static_cast<uint64_t>(seed);
+  e.step = step.data_ptr<int64_t>();
+  e.part_val = part_val.data_ptr<float>();
+  e.part_idx = part_idx.data_ptr<int32_t>();
+  e.ntiles = static_cast<int>(ntiles);
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_gemm(a, stream_of(x));
+  minisgl::launch_lm_sample_reduce(out_tokens.data_ptr<int32_t>(), e.part_val, e.part_idx, e.ntiles,
+                                   static_cast<int>(M), tp, step.data_ptr<int64_t>(), stream_of(x));
+}
+
 int64_t gemm_workspace_elems(int64_t M, int64_t N, int64_t K) {
   return minisgl::gemm_workspace_elems(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
 }
@@ -507,6 +570,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_store", &rope_store);
   m.def("decode_attention", &decode_attention);
   m.def("gemm_fused", &gemm_fused);
+  m.def("gemm_sample", &gemm_sample);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);
   m.def("sample", &sample);

@@ -37,6 +37,7 @@
 #include "common.cuh"
 #include "launch.h"
 #include "ops.h"
+#include "sampling_rng.cuh"
 #include "tma_host.h"
 
 namespace minisgl {
@@ -182,6 +183,42 @@ __device__ __forceinline__ void rope_epilogue(const KParams& p, int head, int m,
   const int page = slot / e.page_size, off = slot % e.page_size;
   __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_k ? e.k_cache : e.v_cache);
   store4_bf16(cache + ((static_cast<int64_t>(page) * e.hk + kvh) * e.page_size + off) * 128 + ocol, v);
+}
+
+// kEpiSample for one token row m of one 128-row vocabulary tile; the calling
+// warp holds the row (lane l: vocabulary entries n .. n + 3, n = tile base +
+// 4 l). Score and tie rule are the sampling kernel's: score = logit / max(T,
+// 1e-6) + Gumbel(row_key(seed, step, m), index) when T > 0, else the logit;
+// the larger score wins, ties go to the smaller index.
+__device__ __forceinline__ void sample_epilogue(const KParams& p, int m, int n, float4 acc) {
+  const GemmEpilogue& e = p.epi;
+  const float T = e.temps != nullptr ? e.temps[m] : 0.f;
+  const bool hot = T > 0.f;
+  const float inv = 1.f / fmaxf(T, 1e-6f);
+  const uint32_t key = hot ? row_key(e.seed, static_cast<uint64_t>(*e.step), m) : 0u;
+  const float v[4] = {acc.x, acc.y, acc.z, acc.w};
+  float bv = -INFINITY;
+  int bi = 0x7fffffff;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int idx = n + q;
+    if (idx >= p.N) break;
+    float l = v[q];
+    if (p.bias != nullptr) l += __bfloat162float(p.bias[idx]);
+    const float sc = hot ? l * inv + gumbel(key, idx) : l;
+    if (sc > bv || (sc == bv && idx < bi)) bv = sc, bi = idx;
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+    const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+    if (ov > bv || (ov == bv && oi < bi)) bv = ov, bi = oi;
+  }
+  if ((threadIdx.x & 31) == 0) {
+    const int64_t o = static_cast<int64_t>(m) * e.ntiles + n / 128;
+    e.part_val[o] = bv;
+    e.part_idx[o] = bi;
+  }
 }
 
 // Fused epilogue of a token-major tile without split-K, straight from TMEM:
@@ -686,6 +723,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float4 acc = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol) * 4), nsplit);
         const int m = tok0 + orow;
         const int n = feat0 + ocol;
+        if (SWAP && (p.epi.kind & kEpiSample) != 0) {
+          if (m < p.M) sample_epilogue(p, m, n, acc);  // m is uniform per warp
+          continue;
+        }
         if (m >= p.M || n >= p.N) continue;  // uniform per warp for kEpiRope
         const float sc = do_norm ? s_rstd[orow] : 1.f;
         float v[4] = {acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc};
@@ -861,6 +902,11 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
       throw std::runtime_error("minisgl.gemm: residual epilogue needs a residual with row stride % 4 == 0");
     if ((fused & kEpiSiluMul) != 0 && (a.N % 128 != 0 || (fused & (kEpiRope | kEpiResidual)) != 0))
       throw std::runtime_error("minisgl.gemm: silu epilogue needs N % 128 == 0 and no rope / residual");
+    if ((fused & kEpiSample) != 0) {
+      if (fused != kEpiSample || a.force_mode == 1 || a.epi.part_val == nullptr || a.epi.part_idx == nullptr ||
+          a.epi.step == nullptr || a.epi.ntiles != (a.N + 127) / 128)
+        throw std::runtime_error("minisgl.gemm: the sampling epilogue runs alone on weight-major tiles");
+    }
     if ((fused & kEpiRope) != 0) {
       if (a.N != (a.epi.hq + 2 * a.epi.hk) * 128 || a.epi.cos_sin == nullptr || a.epi.positions == nullptr ||
           a.epi.out_loc == nullptr || a.epi.k_cache == nullptr || a.epi.v_cache == nullptr || a.epi.page_size <= 0 ||

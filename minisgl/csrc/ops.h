@@ -26,7 +26,12 @@ enum class DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 //                get their per-head RMSNorm (if weights are given) and NeoX
 //                RoPE; q heads are written to out (the qkv row), k and v
 //                heads to the paged KV cache at out_loc (not to out).
-enum : int { kEpiNorm = 1, kEpiResidual = 2, kEpiSiluMul = 4, kEpiRope = 8 };
+//   kEpiSample   the LM head (weight-major tiles): instead of logits, each
+//                (token, 128-row vocabulary tile) writes its best score and
+//                index, score = logit / T + Gumbel noise of the sampler's
+//                counter-based stream (T <= 0: the plain logit, argmax);
+//                launch_lm_sample_reduce turns the partials into tokens.
+enum : int { kEpiNorm = 1, kEpiResidual = 2, kEpiSiluMul = 4, kEpiRope = 8, kEpiSample = 16 };
 struct GemmEpilogue {
   int kind;
   float eps;                  // kEpiNorm
@@ -41,6 +46,12 @@ struct GemmEpilogue {
   void* k_cache;              // bf16 [pages, hk, page_size, 128] of this layer
   void* v_cache;
   int hq, hk, page_size;
+  const float* temps;         // kEpiSample: [M] temperatures (nullptr: all greedy)
+  uint64_t seed;
+  const int64_t* step;        // device step counter (read only here)
+  float* part_val;            // [M, ntiles]
+  int32_t* part_idx;
+  int ntiles;                 // ceil(N / 128)
 };
 
 struct GemmArgs {
@@ -138,6 +149,8 @@ struct SampleArgs {
   const int64_t* step;       // device counter mixed into the random stream (may be nullptr)
 };
 void launch_sample(const SampleArgs& a, cudaStream_t s);
+void launch_lm_sample_reduce(int32_t* out, const float* part_val, const int32_t* part_idx, int ntiles, int B,
+                             const float* temps, int64_t* step, cudaStream_t s);
 
 // ------------------------------------------------------------------- MoE ----
 struct MoeRouteArgs {

@@ -23,36 +23,12 @@
 #include "common.cuh"
 #include "launch.h"
 #include "ops.h"
+#include "sampling_rng.cuh"
 
 namespace minisgl {
 namespace {
 
 constexpr int kThreads = 1024;
-
-__device__ __forceinline__ uint64_t mix64(uint64_t z) {
-  z = (z ^ (z >> 30)) * 0xbf58476d1ce4e5b9ull;
-  z = (z ^ (z >> 27)) * 0x94d049bb133111ebull;
-  return z ^ (z >> 31);
-}
-
-__device__ __forceinline__ uint32_t row_key(uint64_t seed, uint64_t step, int row) {
-  return static_cast<uint32_t>(mix64(seed ^ mix64(step * 0x9e3779b97f4a7c15ull + static_cast<uint64_t>(row))));
-}
-
-__device__ __forceinline__ uint32_t fmix32(uint32_t h) {
-  h ^= h >> 16;
-  h *= 0x85ebca6bu;
-  h ^= h >> 13;
-  h *= 0xc2b2ae35u;
-  h ^= h >> 16;
-  return h;
-}
-
-// uniform in (0, 1)
-__device__ __forceinline__ float uniform(uint32_t key, int col) {
-  const uint32_t r = fmix32(key ^ (static_cast<uint32_t>(col) * 0x9e3779b9u));
-  return (static_cast<float>(r >> 8) + 0.5f) * (1.0f / 16777216.0f);
-}
 
 // order-preserving map of fp32 to uint32 (larger float -> larger key)
 __device__ __forceinline__ uint32_t fkey(float f) {
@@ -197,20 +173,43 @@ __global__ void sample_kernel(SampleArgs a) {
       for (int q = 0; q < 4; ++q) {
         const int i = i4 * 4 + q;
         if (fkey(ls[q]) < floor_key) continue;
-        const float gumbel = -__logf(-__logf(uniform(key, i)));
-        best = better(best, ArgMax{ls[q] * inv_t + gumbel, i});
+        best = better(best, ArgMax{ls[q] * inv_t + gumbel(key, i), i});
       }
     }
   } else {
     for (int i = threadIdx.x; i < V; i += blockDim.x) {
       const float l = row[i];
       if (fkey(l) < floor_key) continue;
-      const float gumbel = -__logf(-__logf(uniform(key, i)));
-      best = better(best, ArgMax{l * inv_t + gumbel, i});
+      best = better(best, ArgMax{l * inv_t + gumbel(key, i), i});
     }
   }
   best = block_argmax(best);
   if (threadIdx.x == 0) a.out[r] = best.i == 0x7fffffff ? 0 : best.i;
+}
+
+// Token of each row from the LM-head epilogue's per-vocab-tile partials
+// (best score, its vocabulary index): the same argmax (ties to the smaller
+// index) the sampling kernel takes over the whole row. CTA 0 then advances
+// the step counter when any row sampled with a temperature, as the sampling
+// kernel does; every reader of the counter (the GEMM) finished before this
+// kernel passed griddepcontrol.wait.
+__global__ void lm_sample_reduce_kernel(int32_t* out, const float* part_val, const int32_t* part_idx, int ntiles,
+                                        int B, const float* temps, int64_t* step) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x;
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int t = threadIdx.x; t < ntiles; t += blockDim.x) {
+    const int64_t o = static_cast<int64_t>(r) * ntiles + t;
+    best = better(best, ArgMax{part_val[o], part_idx[o]});
+  }
+  best = block_argmax(best);
+  if (threadIdx.x == 0) out[r] = best.i == 0x7fffffff ? 0 : best.i;
+  if (r == 0 && step != nullptr && temps != nullptr) {
+    int any = 0;
+    for (int i = threadIdx.x; i < B; i += blockDim.x) any |= temps[i] > 0.f;
+    if (__syncthreads_or(any) && threadIdx.x == 0) *step += 1;
+  }
 }
 
 __global__ void bump_step_kernel(int64_t* step) {
@@ -224,6 +223,12 @@ __global__ void bump_step_kernel(int64_t* step) {
 void launch_argmax(int32_t* out, const float* logits, int B, int V, int ld, cudaStream_t s) {
   if (B <= 0) return;
   launch_pdl(argmax_kernel, dim3(B), dim3(kThreads), 0, s, out, logits, V, ld);
+}
+
+void launch_lm_sample_reduce(int32_t* out, const float* part_val, const int32_t* part_idx, int ntiles, int B,
+                             const float* temps, int64_t* step, cudaStream_t s) {
+  if (B <= 0) return;
+  launch_pdl(lm_sample_reduce_kernel, dim3(B), dim3(256), 0, s, out, part_val, part_idx, ntiles, B, temps, step);
 }
 
 void launch_sample(const SampleArgs& a, cudaStream_t s) {

@@ -18,8 +18,10 @@ from typing import Dict, NamedTuple, Optional, Tuple
 
 import torch
 
+from minisgl.env import ENV
+
 from minisgl.attention import create_attention_backend
-from minisgl.core import Batch, Context, Req, reset_global_ctx, set_global_ctx
+from minisgl.core import FusedSample, Batch, Context, Req, reset_global_ctx, set_global_ctx
 from minisgl.kvcache import create_kvcache_pool
 from minisgl.layers import set_rope_device
 from minisgl.models import create_model, load_weight, random_weights
@@ -131,7 +133,8 @@ class Engine:
         self.page_table[self.dummy_req.table_idx].fill_(num_tokens)  # -> the spare page
         self.graph_runner = GraphRunner(
             self.stream, self.device, self.model, self.attn_backend, config.cuda_graph_bs,
-            self._graph_max_bs(config), init_free, width, mcfg.vocab_size, self.dummy_req)
+            self._graph_max_bs(config), init_free, width, mcfg.vocab_size, self.dummy_req,
+            sampler=None if ENV.NO_FUSED_SAMPLING.value else self.sampler)
 
     # ---------------------------------------------------------------- setup
     def _graph_max_bs(self, config: EngineConfig) -> Optional[int]:
@@ -172,7 +175,9 @@ class Engine:
 
         bs = determine_cuda_graph_bs(config.cuda_graph_bs, self._graph_max_bs(config), 1 << 40)
         if not bs:
-            return
+            # no graphs: eager decode batches still get tuned plans (the same
+            # ones a graph engine would use, so both compute the same logits)
+            bs = list(range(1, min(config.max_running_req, 256) + 1))
         t0 = time.perf_counter()
         cache = os.environ.get("MINISGL_GEMM_TUNE_CACHE") or None
         kinds = self.model.fused_gemm_kinds() if hasattr(self.model, "fused_gemm_kinds") else {}
@@ -255,14 +260,27 @@ class Engine:
 
     # -------------------------------------------------------------- forward
     def forward_batch(self, batch: Batch, args: BatchSamplingArgs) -> ForwardOutput:
+        # greedy / temperature batches sample inside the LM-head GEMM (no
+        # logits in memory); top-k / top-p batches sample from the logits
+        fused = self.sampler.fusable(args, batch.size) and getattr(self.model, "samples_in_lm_head", False)
+        tokens = None
         with self.ctx.forward_batch(batch):
             if self.graph_runner.can_use_cuda_graph(batch):
-                logits = self.graph_runner.replay(batch)
+                if fused and self.graph_runner.can_sample(batch):
+                    tokens = self.graph_runner.replay_sample(batch, args.temperatures)
+                else:
+                    logits = self.graph_runner.replay(batch)
+            elif fused:
+                self.ctx.fused_sample = FusedSample(args.temperatures, self.sampler.seed, self.sampler.step)
+                try:
+                    tokens = self.model.forward()
+                finally:
+                    self.ctx.fused_sample = None
             else:
                 logits = self.model.forward()
         for r in batch.reqs:
             r.complete_one()
-        next_gpu = self.sampler.sample(logits[: batch.size], args)
+        next_gpu = tokens[: batch.size] if tokens is not None else self.sampler.sample(logits[: batch.size], args)
         if not self.is_cuda:
             return ForwardOutput(next_gpu, next_gpu, _Done())
         next_cpu = torch.empty(next_gpu.shape, dtype=next_gpu.dtype, pin_memory=True)

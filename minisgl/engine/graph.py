@@ -18,12 +18,14 @@ from typing import TYPE_CHECKING, Dict, List, Optional
 import torch
 
 from minisgl import ops
-from minisgl.core import Batch, Req, get_global_ctx
+from minisgl.core import Batch, FusedSample, Req, get_global_ctx
 from minisgl.utils import init_logger
 
 if TYPE_CHECKING:
     from minisgl.attention import BaseAttnBackend
     from minisgl.models import BaseLLMModel
+
+    from .sample import Sampler
 
 logger = init_logger(__name__)
 
@@ -50,8 +52,13 @@ class GraphRunner:
     def __init__(self, stream: Optional[torch.cuda.Stream], device: torch.device, model: "BaseLLMModel",
                  attn_backend: "BaseAttnBackend", cuda_graph_bs: Optional[List[int]],
                  cuda_graph_max_bs: Optional[int], free_memory: int, max_seq_len: int, vocab_size: int,
-                 dummy_req: Req) -> None:
+                 dummy_req: Req, sampler: Optional["Sampler"] = None) -> None:
         self.stream = stream
+        self.sampler = sampler
+        # graphs that sample inside the LM head (greedy / temperature batches)
+        self.sample_graph_map: Dict[int, torch.cuda.CUDAGraph] = {}
+        self.logits_out: Dict[int, torch.Tensor] = {}
+        self.tokens_out: Dict[int, torch.Tensor] = {}
         self.device = device
         self.attn_backend = attn_backend
         self.dummy_req = dummy_req
@@ -70,7 +77,7 @@ class GraphRunner:
         self.input_ids = torch.zeros(n, dtype=torch.int32, device=self.device)
         self.positions = torch.zeros(n, dtype=torch.int32, device=self.device)
         self.out_loc = torch.zeros(n, dtype=torch.int32, device=self.device)
-        self.logits = torch.empty(n, vocab_size, dtype=torch.float32, device=self.device)
+        self.temps = torch.zeros(n, dtype=torch.float32, device=self.device)
         self.attn_backend.init_capture_graph(max_seq_len, self.graph_bs_list)
         torch.cuda.synchronize(self.device)
         logger.info_rank0(f"Capturing CUDA graphs for batch sizes {self.graph_bs_list}; "
@@ -86,15 +93,31 @@ class GraphRunner:
             self.attn_backend.prepare_for_capture(batch)
             graph = torch.cuda.CUDAGraph()
             with ctx.forward_batch(batch):
-                self.logits[:bs] = model.forward()  # warm-up outside the capture
+                model.forward()  # warm-up outside the capture
                 before = ops.LAUNCHES[0]
                 with torch.cuda.graph(graph, pool=pool, stream=self.stream):
-                    self.logits[:bs] = model.forward()
+                    # the graph's own output tensor is the static logits buffer
+                    self.logits_out[bs] = model.forward()
                 self.graph_launches[bs] = ops.LAUNCHES[0] - before
                 ops.LAUNCHES[0] = before
             if pool is None:
                 pool = graph.pool()
             self.graph_map[bs] = graph
+            if (self.sampler is not None and getattr(model, "samples_in_lm_head", False)
+                    and bs <= self.sampler.FUSED_MAX_ROWS):
+                sgraph = torch.cuda.CUDAGraph()
+                ctx.fused_sample = FusedSample(self.temps[:bs], self.sampler.seed, self.sampler.step)
+                try:
+                    with ctx.forward_batch(batch):
+                        model.forward()  # warm-up (zero temperatures: greedy, the counter stays)
+                        before = ops.LAUNCHES[0]
+                        with torch.cuda.graph(sgraph, pool=pool, stream=self.stream):
+                            self.tokens_out[bs] = model.forward()
+                        self.graph_launches[-bs] = ops.LAUNCHES[0] - before
+                        ops.LAUNCHES[0] = before
+                finally:
+                    ctx.fused_sample = None
+                self.sample_graph_map[bs] = sgraph
         torch.cuda.synchronize(self.device)
         logger.info_rank0(f"CUDA graphs ready; free memory {mem_GB(get_free_memory(self.device))}")
 
@@ -107,18 +130,41 @@ class GraphRunner:
             size = next(b for b in self.graph_bs_list if b >= batch.size)
         batch.padded_reqs = batch.reqs + [self.dummy_req] * (size - batch.size)
 
-    def replay(self, batch: Batch) -> torch.Tensor:
+    def _load_inputs(self, batch: Batch) -> int:
         bs = batch.padded_size
         self.input_ids[:bs].copy_(batch.input_ids)
         self.positions[:bs].copy_(batch.positions)
         self.out_loc[:bs].copy_(batch.out_loc)
         self.attn_backend.prepare_for_replay(batch)
+        return bs
+
+    def replay(self, batch: Batch) -> torch.Tensor:
+        bs = self._load_inputs(batch)
         self.graph_map[bs].replay()
         ops.LAUNCHES[0] += self.graph_launches[bs]
-        return self.logits[: batch.size]
+        return self.logits_out[bs][: batch.size]
+
+    def can_sample(self, batch: Batch) -> bool:
+        return batch.padded_size in self.sample_graph_map
+
+    def replay_sample(self, batch: Batch, temperatures: Optional[torch.Tensor]) -> torch.Tensor:
+        """Replay the graph that samples in the LM head; padded rows are greedy."""
+        bs = self._load_inputs(batch)
+        if temperatures is None:
+            self.temps[:bs].zero_()
+        else:
+            self.temps[: batch.size].copy_(temperatures)
+            if bs > batch.size:
+                self.temps[batch.size : bs].zero_()
+        self.sample_graph_map[bs].replay()
+        ops.LAUNCHES[0] += self.graph_launches[-bs]
+        return self.tokens_out[bs][: batch.size]
 
     def destroy_cuda_graphs(self) -> None:
         """Release graphs first: graphs holding collectives must go before
         the communicators they captured."""
         self.graph_map.clear()
+        self.sample_graph_map.clear()
+        self.logits_out.clear()
+        self.tokens_out.clear()
         gc.collect()

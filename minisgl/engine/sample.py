@@ -52,6 +52,19 @@ class Sampler:
         p = torch.tensor(ps, dtype=torch.float32, pin_memory=pin).to(self.device, non_blocking=True) if use_p else None
         return BatchSamplingArgs(t, k, p)
 
+    # rows up to which sampling inside the LM-head GEMM is faster than GEMM +
+    # sampling kernel on a B200 (Qwen3 vocabulary: 120 vs 140 us at 32 rows;
+    # at 256 rows the epilogue's noise work, serial behind each tile's
+    # mainloop at one CTA per SM, makes it 2x slower)
+    FUSED_MAX_ROWS = 64
+
+    def fusable(self, args: BatchSamplingArgs, rows: int) -> bool:
+        """Greedy and temperature-only batches of at most FUSED_MAX_ROWS rows
+        are sampled inside the LM-head GEMM (same random stream, same
+        tokens); top-k / top-p batches need the logits."""
+        return (self.device.type == "cuda" and rows <= self.FUSED_MAX_ROWS and args.top_k is None
+                and args.top_p is None and not ENV.NO_FUSED_SAMPLING.value)
+
     @nvtx_annotate("Sampler")
     def sample(self, logits: torch.Tensor, args: BatchSamplingArgs) -> torch.Tensor:
         if args.temperatures is None:

@@ -83,6 +83,7 @@ class _Env:
     DEBUG_CHECK_ERRORS = _bool(False)   # read the kernel error word after every step
     STATS_INTERVAL = _int(0)            # log a stats line every N steps (0 = off)
     SAMPLING_SEED = _int(0)
+    NO_FUSED_SAMPLING = _bool(False)    # sample from materialised logits even when the LM head could
 
     def __init__(self) -> None:
         self.reload()

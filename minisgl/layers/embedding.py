@@ -68,6 +68,11 @@ class ParallelLMHead(VocabParallelEmbedding):
         if batch.is_prefill:
             x = x.index_select(0, batch.attn_metadata.get_last_indices(bs))
         w = self._tied.weight if self._tied is not None else self.weight
+        fs = get_global_ctx().fused_sample
+        if fs is not None and self.tp_size == 1:
+            # tokens straight from the GEMM epilogue (no logits in memory)
+            return ops.lm_head_sample(x, w, self.bias.to(w.dtype) if self.bias is not None else None,
+                                      fs.temperatures, fs.seed, fs.step, out=fs.out)
         logits = ops.gemm(x, w, self.bias.to(w.dtype) if self.bias is not None else None, out_dtype=torch.float32)
         if self.tp_size == 1:
             return logits

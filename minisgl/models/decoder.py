@@ -124,6 +124,11 @@ class DecoderForCausalLM(BaseLLMModel):
                                       tied_embedding=self.model.embed_tokens if tied else None)
 
     @property
+    def samples_in_lm_head(self) -> bool:
+        """The LM head can return sampled tokens (one rank holds the whole vocabulary)."""
+        return self.lm_head.tp_size == 1
+
+    @property
     def fused_layout(self) -> bool:
         """True when norm weights are folded into qkv / gate_up and gate|up
         rows are interleaved (what ``state_dict`` then returns)."""
@@ -143,6 +148,9 @@ class DecoderForCausalLM(BaseLLMModel):
             if layer._fused_mlp:
                 out[tuple(layer.mlp.gate_up_proj.weight.shape)] = (ops.EPI_NORM | ops.EPI_SILU, hq, hk)
                 out[tuple(layer.mlp.down_proj.weight.shape)] = (ops.EPI_RESIDUAL, hq, hk)
+        if self.samples_in_lm_head:
+            head = self.lm_head._tied.weight if self.lm_head._tied is not None else self.lm_head.weight
+            out[tuple(head.shape)] = (ops.EPI_SAMPLE, 0, 0)
         return out
 
     def forward(self) -> torch.Tensor:

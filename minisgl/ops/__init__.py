@@ -119,7 +119,7 @@ def gemm(
 
 
 # ------------------------------------------------------------ elementwise
-EPI_NORM, EPI_RESIDUAL, EPI_SILU, EPI_ROPE = 1, 2, 4, 8
+EPI_NORM, EPI_RESIDUAL, EPI_SILU, EPI_ROPE, EPI_SAMPLE = 1, 2, 4, 8, 16
 from .gemm_tune import FUSED_PLANS as _gemm_fused_plans  # noqa: E402  (best plans fused epilogues accept)
 
 
@@ -365,6 +365,54 @@ def sample(
     lf = logits if logits.dtype == torch.float32 else logits.float()
     _count(2 if step is not None else 1)
     native().sample(out, lf, temperature, top_k, top_p, seed, step)
+    return out
+
+
+_SAMPLE_PARTS: dict = {}
+
+
+def lm_head_sample(
+    x: torch.Tensor,
+    w: torch.Tensor,
+    bias: Optional[torch.Tensor],
+    temperature: Optional[torch.Tensor],
+    seed: int,
+    step: torch.Tensor,
+    out: Optional[torch.Tensor] = None,
+    plan: Optional[Tuple[int, int]] = None,
+    generator: Optional[torch.Generator] = None,
+) -> torch.Tensor:
+    """Tokens sampled from x @ w^T (+ bias) without materialising the logits:
+    the LM-head GEMM's epilogue keeps, per 128-row vocabulary tile, the best
+    Gumbel-perturbed score (temperature None: the plain logit, i.e. greedy),
+    and a small kernel reduces the tiles. Draws the same random numbers as
+    ``sample`` for the same (seed, step), so both paths give the same tokens
+    for the same logits. ``plan`` = (token tile, K splits) for tests."""
+    M, N = x.shape[0], w.shape[0]
+    if not x.is_cuda:
+        logits = ref.gemm(x, w, bias, torch.float32)
+        y = ref.argmax(logits) if temperature is None else ref.sample(logits, temperature, None, None, generator)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(M, dtype=torch.int32, device=x.device)
+    ntiles = (N + 127) // 128
+    key = (x.device.index, N)
+    buf = _SAMPLE_PARTS.get(key)
+    if buf is None or buf[0].numel() < M * ntiles or torch.cuda.is_current_stream_capturing():
+        buf = (torch.empty(M * ntiles, dtype=torch.float32, device=x.device),
+               torch.empty(M * ntiles, dtype=torch.int32, device=x.device))
+        if not torch.cuda.is_current_stream_capturing():
+            _SAMPLE_PARTS[key] = buf
+    if plan is None:
+        tuned = _gemm_fused_plans.get((M, N, x.shape[1]))
+        splits, bn = (tuned[2], tuned[1]) if tuned is not None and tuned[0] == 2 else (0, 0)
+    else:
+        bn, splits = plan
+    _count(2)
+    native().gemm_sample(out, x, w, bias, temperature, seed, step, buf[0], buf[1], splits, bn, error_word(x.device))
     return out
 
 

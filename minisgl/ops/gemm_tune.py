@@ -95,6 +95,8 @@ def _fused_candidates(M: int, K: int, kind: int) -> List[Plan]:
 
     num_kb = (K + 63) // 64
     out = [p for p in candidates(M, K, full=False) if p[0] == 2]
+    if kind == ops.EPI_SAMPLE:  # the sampling epilogue needs weight-major tiles
+        return out
     if M >= 64:
         whole = (kind & (ops.EPI_ROPE | ops.EPI_SILU)) != 0
         for bn in (128, 256) if whole else (64, 128, 256):
@@ -144,7 +146,7 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
 
     native = ops.native()
     fused = dict(fused or {})
-    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only"
+    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only|sample"
     cached = _load(cache_file, key_dev)
     shapes = sorted(set(shapes) | set(fused))
     wanted = sorted(set(int(m) for m in batch_sizes if m > 0))
@@ -180,14 +182,25 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
                     FUSED_PLANS[key] = cached[skey]
                     continue
                 kind, hq, hk = fused[(N, K)]
-                fb = _FusedBench(kind, hq, hk, M, N, device)
                 timed = []
-                for plan in _fused_candidates(M, K, kind):
-                    try:
-                        timed.append((_time_runs(lambda w_, p_=plan: ops.gemm_fused(
-                            x, w_, out=fb.out, plan=p_, **fb.kw), ws), plan))
-                    except RuntimeError:
-                        continue
+                if kind == ops.EPI_SAMPLE:
+                    temps = torch.full((M,), 0.7, device=device)
+                    step = torch.zeros((), dtype=torch.int64, device=device)
+                    toks = torch.empty(M, dtype=torch.int32, device=device)
+                    for plan in _fused_candidates(M, K, kind):
+                        try:
+                            timed.append((_time_runs(lambda w_, p_=plan: ops.lm_head_sample(
+                                x, w_, None, temps, 0, step, out=toks, plan=(p_[1], p_[2])), ws), plan))
+                        except RuntimeError:
+                            continue
+                else:
+                    fb = _FusedBench(kind, hq, hk, M, N, device)
+                    for plan in _fused_candidates(M, K, kind):
+                        try:
+                            timed.append((_time_runs(lambda w_, p_=plan: ops.gemm_fused(
+                                x, w_, out=fb.out, plan=p_, **fb.kw), ws), plan))
+                        except RuntimeError:
+                            continue
                 if timed:
                     FUSED_PLANS[key] = cached[skey] = min(timed)[1]
             del w, ws, xmax, omax

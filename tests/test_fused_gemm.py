@@ -98,3 +98,32 @@ def test_norm_rope_store(M, plan, qk_norm):
     _close(qkv[:, : hq * 128], expect[:, : hq * 128])
     _close(kcd, kc)
     _close(vcd, vc)
+
+
+@pytest.mark.parametrize("M", [1, 7, 64, 256])
+@pytest.mark.parametrize("plan", [(16, 1), (32, 2), (64, 1), (256, 1), (32, 8)])
+@pytest.mark.parametrize("temps", ["greedy", "mixed"])
+def test_lm_head_sample_matches_logit_sampler(M, plan, temps):
+    """Sampling inside the LM-head GEMM draws the same tokens as the sampling
+    kernel run on the materialised fp32 logits of the same tile plan."""
+    N, K = 5000, 1024  # a vocabulary that does not fill its last 128-row tile
+    g = torch.Generator().manual_seed(M)
+    x = torch.randn(M, K, generator=g).to(torch.bfloat16).to(DEV)
+    w = (torch.randn(N, K, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    logits = torch.empty(M, N, device=DEV, dtype=torch.float32)
+    ops.native().gemm(logits, x, w, None, None, plan[1], 2, None, plan[0])
+    step_a = torch.full((), 5, dtype=torch.int64, device=DEV)
+    step_b = step_a.clone()
+    if temps == "greedy":
+        expect = ops.argmax(logits)
+        got = ops.lm_head_sample(x, w, None, None, 123, step_b, plan=plan)
+    else:
+        t = torch.rand(M, generator=g) * 1.5
+        t[::3] = 1e-6  # greedy rows of a mixed batch
+        t = t.to(DEV)
+        expect = ops.sample(logits, t, None, None, 123, step_a)
+        got = ops.lm_head_sample(x, w, None, t, 123, step_b, plan=plan)
+    torch.cuda.synchronize()
+    ops.check_device_errors(torch.device(DEV))
+    assert torch.equal(got.cpu(), expect.cpu())
+    assert step_a.item() == step_b.item()  # both paths advance the counter alike
