@@ -270,6 +270,78 @@ void gemm_sample(at::Tensor out_tokens, const at::Tensor& x, const at::Tensor& w
                                    static_cast<int>(M), tp, step.data_ptr<int64_t>(), stream_of(x));
 }
 
+// Routed experts on the expert-sorted layout: align -> gather -> grouped
+// gate_up GEMM with SiLU x up in its epilogue (w1 rows interleaved in 64-row
+// gate / up blocks per expert) -> grouped down GEMM -> weighted combine.
+// Scratch tensors come from the caller (static shapes for CUDA graphs):
+// P = T * k + E * (tile - 1) rows.
+void moe_experts(at::Tensor out, const at::Tensor& x, const at::Tensor& w1, const at::Tensor& w2,
+                 const at::Tensor& topk_w, const at::Tensor& topk_ids, int64_t tile, at::Tensor xs, at::Tensor h,
+                 at::Tensor ys, at::Tensor sorted_pair, at::Tensor pair_pos, at::Tensor tile_expert,
+                 at::Tensor tile_row, at::Tensor num_tiles, const c10::optional<at::Tensor>& err) {
+  check_cuda(x, "x");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && w1.scalar_type() == at::kBFloat16 && w2.scalar_type() == at::kBFloat16,
+            "moe_experts: bf16 activations and expert weights");
+  MSG_CHECK(x.is_contiguous() && w1.is_contiguous() && w2.is_contiguous() && out.is_contiguous(),
+            "moe_experts: contiguous tensors");
+  MSG_CHECK(w1.dim() == 3 && w2.dim() == 3 && w1.size(0) == w2.size(0) && w1.size(2) == x.size(1) &&
+                w2.size(1) == x.size(1) && w1.size(1) == 2 * w2.size(2),
+            "moe_experts: w1 [E, 2I, H], w2 [E, H, I]");
+  const int64_t T = x.size(0), H = x.size(1), E = w1.size(0), I = w2.size(2), k = topk_ids.size(1);
+  MSG_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous() && topk_ids.size(0) == T,
+            "moe_experts: int32 topk_ids [T, k]");
+  MSG_CHECK(topk_w.scalar_type() == at::kFloat && topk_w.is_contiguous() && topk_w.numel() == T * k,
+            "moe_experts: float32 topk_w [T, k]");
+  MSG_CHECK(I % 64 == 0 && H % 128 == 0, "moe_experts: I % 64 == 0 and H % 128 == 0");
+  MSG_CHECK(tile == 16 || tile == 32 || tile == 64 || tile == 128, "moe_experts: tile of 16, 32, 64 or 128");
+  const int64_t P = T * k + E * (tile - 1);
+  MSG_CHECK(xs.numel() >= P * H && h.numel() >= P * I && ys.numel() >= P * H && sorted_pair.numel() >= P &&
+                pair_pos.numel() >= T * k && tile_expert.numel() >= P / tile && tile_row.numel() >= P / tile &&
+                num_tiles.numel() >= 1,
+            "moe_experts: scratch too small");
+  MSG_CHECK(out.numel() == T * H && out.scalar_type() == at::kBFloat16, "moe_experts: out [T, H] bf16");
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = stream_of(x);
+  minisgl::MoeAlignArgs al{};
+  al.topk_ids = topk_ids.data_ptr<int32_t>();
+  al.T = static_cast<int>(T);
+  al.k = static_cast<int>(k);
+  al.E = static_cast<int>(E);
+  al.tile = static_cast<int>(tile);
+  al.sorted_pair = sorted_pair.data_ptr<int32_t>();
+  al.pair_pos = pair_pos.data_ptr<int32_t>();
+  al.tile_expert = tile_expert.data_ptr<int32_t>();
+  al.tile_row = tile_row.data_ptr<int32_t>();
+  al.num_tiles = num_tiles.data_ptr<int32_t>();
+  minisgl::launch_moe_align(al, st);
+  minisgl::launch_moe_gather(xs.data_ptr(), x.data_ptr(), al.sorted_pair, static_cast<int>(P), static_cast<int>(k),
+                             static_cast<int>(H), st);
+  for (int pass = 0; pass < 2; ++pass) {
+    minisgl::GemmArgs a{};
+    a.x = pass == 0 ? xs.data_ptr() : h.data_ptr();
+    a.w = pass == 0 ? w1.data_ptr() : w2.data_ptr();
+    a.out = pass == 0 ? h.data_ptr() : ys.data_ptr();
+    a.M = static_cast<int>(P);
+    a.N = static_cast<int>(pass == 0 ? 2 * I : H);
+    a.K = static_cast<int>(pass == 0 ? H : I);
+    a.ldx = a.K;
+    a.ldw = a.K;
+    a.ldo = static_cast<int>(pass == 0 ? I : H);
+    a.force_mode = 2;
+    a.force_bn = static_cast<int>(tile);
+    a.force_splits = 1;
+    a.err = err_ptr(err);
+    if (pass == 0) a.epi.kind = minisgl::kEpiSiluMul;
+    a.g_tile_expert = al.tile_expert;
+    a.g_tile_row = al.tile_row;
+    a.g_num_tiles = al.num_tiles;
+    a.g_experts = static_cast<int>(E);
+    minisgl::launch_gemm(a, st);
+  }
+  minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), al.pair_pos,
+                              static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
+}
+
 int64_t gemm_workspace_elems(int64_t M, int64_t N, int64_t K) {
   return minisgl::gemm_workspace_elems(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
 }
@@ -571,6 +643,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &decode_attention);
   m.def("gemm_fused", &gemm_fused);
   m.def("gemm_sample", &gemm_sample);
+  m.def("moe_experts", &moe_experts);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);
   m.def("sample", &sample);

@@ -57,6 +57,11 @@ struct KParams {
   int stages;          // ring depth used by this launch (<= the template maximum)
   int kps;             // k-blocks per stage: >1 loads them with one 3-D TMA box per operand
   int K;               // reduction length (the RMSNorm mean of kEpiNorm)
+  // grouped weight-major GEMM (MoE experts): w holds the experts' [N, K]
+  // matrices back to back; token tile i is rows [g_tile_row[i], + BN) of x
+  const int32_t* g_tile_expert;
+  const int32_t* g_tile_row;
+  const int32_t* g_num_tiles;  // nullptr: plain GEMM
   int out_f32;
   GemmEpilogue epi;    // fused epilogue (weight-major split-K instantiations only)
   ErrorSink err;
@@ -389,10 +394,21 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int a_row0 = blockIdx.y * BM;
-  const int b_row0 = blockIdx.x * BN;
+  int b_row0 = blockIdx.x * BN;
   const int kb0 = blockIdx.z * p.kb_per_split;
   const int kb1 = min(p.num_kb, kb0 + p.kb_per_split);
   const int nkb = max(0, kb1 - kb0);
+  // grouped (MoE) weight-major GEMM: token tile i of the expert-sorted rows
+  // belongs to expert g_tile_expert[i]; the table comes from the previous
+  // kernel, and tiles past the live count leave before any set-up
+  int w_off = 0;
+  if (SWAP && p.g_num_tiles != nullptr) {
+    pdl_launch_dependents();
+    pdl_wait();
+    if (static_cast<int>(blockIdx.x) >= *p.g_num_tiles) return;
+    b_row0 = p.g_tile_row[blockIdx.x];
+    w_off = p.g_tile_expert[blockIdx.x] * p.N;
+  }
 
   pdl_launch_dependents();
   if (threadIdx.x == 0) trace_stamp(p, 0);
@@ -423,7 +439,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // weights first: they do not depend on the previous kernel
     const CUtensorMap* tw = SWAP ? &tmA : &tmB;
     const CUtensorMap* tx = SWAP ? &tmB : &tmA;
-    const int w_row = SWAP ? a_row0 : b_row0;
+    const int w_row = (SWAP ? a_row0 : b_row0) + w_off;
     const int x_row = SWAP ? b_row0 : a_row0;
     uint8_t* sW = SWAP ? sA : sB;
     uint8_t* sX = SWAP ? sB : sA;
@@ -891,6 +907,11 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     throw std::runtime_error("minisgl.gemm: N tile must be 16, 32, 64, 128 or 256");
   if (a.force_bn == 16 && a.force_mode == 1)
     throw std::runtime_error("minisgl.gemm: token-major tiles need an N tile of at least 32");
+  if (a.g_num_tiles != nullptr) {
+    if (a.force_mode == 1 || a.force_bn <= 0 || a.force_splits > 1 || a.g_experts <= 0 || a.N % BM != 0)
+      throw std::runtime_error("minisgl.gemm: grouped GEMMs use weight-major tiles of the align tile, no split-K, "
+                               "and expert matrices of a multiple of 128 rows");
+  }
   const int fused = a.epi.kind;
   if (fused != 0) {
     if (a.out_f32) throw std::runtime_error("minisgl.gemm: fused epilogues write bf16");
@@ -914,7 +935,8 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
         throw std::runtime_error("minisgl.gemm: rope epilogue needs head_dim 128 qkv weights and cache pointers");
     }
   }
-  const bool default_swap = fused != 0 && a.force_mode == 0;  // fused calls default to weight-major tiles
+  // fused and grouped calls default to weight-major tiles
+  const bool default_swap = (fused != 0 || a.g_num_tiles != nullptr) && a.force_mode == 0;
   const Plan pl = make_plan(a.M, a.N, a.K, default_swap ? 2 : a.force_mode, a.force_splits, a.force_bn);
   KParams kp;
   kp.out = a.out;
@@ -944,6 +966,9 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   kp.out_f32 = a.out_f32 ? 1 : 0;
   kp.K = a.K;
   kp.epi = a.epi;
+  kp.g_tile_expert = a.g_tile_expert;
+  kp.g_tile_row = a.g_tile_row;
+  kp.g_num_tiles = a.g_num_tiles;
   kp.err = ErrorSink{a.err};
   kp.trace = reinterpret_cast<unsigned long long*>(a.trace);
   auto tmap = [&](const void* base, int rows, int ld, int box_rows) {
@@ -951,7 +976,7 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
                       : make_tmap_bf16_2d_sw128(base, rows, a.K, ld, box_rows);
   };
   if (pl.swap) {
-    CUtensorMap ta = tmap(a.w, a.N, a.ldw, BM);
+    CUtensorMap ta = tmap(a.w, a.g_num_tiles != nullptr ? a.N * a.g_experts : a.N, a.ldw, BM);
     CUtensorMap tb = tmap(a.x, a.M, a.ldx, pl.bn);
     dim3 grid((a.M + pl.bn - 1) / pl.bn, (a.N + BM - 1) / BM, pl.splits);
     switch (pl.bn) {

@@ -71,6 +71,12 @@ struct GemmArgs {
   void* trace;        // optional uint64 [ctas * 8] phase timestamps (profiling)
   int* err;           // device error word (2 x int32) or nullptr
   GemmEpilogue epi;   // fused epilogue (kind 0: plain store)
+  // grouped (MoE) GEMM: w = g_experts matrices of [N, K]; x rows are expert-
+  // sorted and padded to the token tile (force_bn); see MoeAlignArgs
+  const int32_t* g_tile_expert;
+  const int32_t* g_tile_row;
+  const int32_t* g_num_tiles;  // nullptr: plain GEMM
+  int g_experts;
 };
 void launch_gemm(const GemmArgs& a, cudaStream_t stream);
 // Number of fp32 workspace elements launch_gemm may need for this shape.
@@ -165,5 +171,24 @@ struct MoeRouteArgs {
   float routed_scale;
 };
 void launch_moe_route(const MoeRouteArgs& a, cudaStream_t s);
+
+// Expert-sorted layout of the T * k (token, slot) pairs for the grouped
+// expert GEMMs. Every expert's segment is padded to a multiple of `tile`
+// rows; capacity P = T * k + E * (tile - 1) rows, P / tile tiles.
+struct MoeAlignArgs {
+  const int32_t* topk_ids;   // [T * k]
+  int T, k, E, tile;
+  int32_t* sorted_pair;      // [P]: pair index t * k + j, or -1 for padding rows
+  int32_t* pair_pos;         // [T * k]: row of each pair in the sorted layout
+  int32_t* tile_expert;      // [P / tile]: expert of each tile
+  int32_t* tile_row;         // [P / tile]: first sorted row of each tile
+  int32_t* num_tiles;        // [1]: tiles in use
+};
+void launch_moe_align(const MoeAlignArgs& a, cudaStream_t s);
+// xs[r] = x[sorted_pair[r] / k] (zeros for padding rows); bf16 rows of H
+void launch_moe_gather(void* xs, const void* x, const int32_t* sorted_pair, int P, int k, int H, cudaStream_t s);
+// out[t] = sum_j topk_w[t, j] * ys[pair_pos[t * k + j]] (fixed j order), bf16 rows of H
+void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* pair_pos, int T, int k, int H,
+                        cudaStream_t s);
 
 }  // namespace minisgl

@@ -11,5 +11,6 @@ class BaseMoeBackend(ABC):
     def forward(self, hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, gating_output: torch.Tensor,
                 topk: int, renormalize: bool, activation: str = "silu", scoring: str = "softmax",
                 correction_bias: Optional[torch.Tensor] = None, n_group: int = 1, topk_group: int = 1,
-                routed_scale: float = 1.0) -> torch.Tensor:
-        """sum_k w[t, k] * down_e(act(gate_up_e(x_t))) for the k routed experts."""
+                routed_scale: float = 1.0, interleaved: bool = False) -> torch.Tensor:
+        """sum_k w[t, k] * down_e(act(gate_up_e(x_t))) for the k routed experts.
+        ``interleaved``: each expert's gate|up rows alternate in 64-row blocks."""

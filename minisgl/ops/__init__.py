@@ -417,6 +417,41 @@ def lm_head_sample(
 
 
 # -------------------------------------------------------------------- MoE
+def moe_tile(tokens: int, k: int, experts: int) -> int:
+    """Token tile of the grouped expert GEMMs: about the average number of
+    rows an expert receives (padding per expert is below one tile)."""
+    avg = tokens * k / max(1, experts)
+    return 16 if avg <= 16 else 32 if avg <= 48 else 64 if avg <= 160 else 128
+
+
+def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_w: torch.Tensor,
+                topk_ids: torch.Tensor, tile: int = 0) -> torch.Tensor:
+    """sum_j topk_w[t, j] * w2_e (silu(gate) * up)(w1_e x_t) over the k routed
+    experts e = topk_ids[t, j]; w1 [E, 2I, H] with gate|up rows interleaved in
+    64-row blocks per expert, w2 [E, H, I]. Expert-sorted grouped tcgen05
+    GEMMs (align, gather, gate_up with SiLU epilogue, down, combine)."""
+    T, H = x.shape
+    E, I, k = w1.shape[0], w2.shape[2], topk_ids.shape[1]
+    out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    tile = tile or moe_tile(T, k, E)
+    P = T * k + E * (tile - 1)
+    dev, i32 = x.device, torch.int32
+    xs = torch.empty(P, H, dtype=x.dtype, device=dev)
+    h = torch.empty(P, I, dtype=x.dtype, device=dev)
+    ys = torch.empty(P, H, dtype=x.dtype, device=dev)
+    sorted_pair = torch.empty(P, dtype=i32, device=dev)
+    pair_pos = torch.empty(T * k, dtype=i32, device=dev)
+    tile_expert = torch.empty(P // tile, dtype=i32, device=dev)
+    tile_row = torch.empty(P // tile, dtype=i32, device=dev)
+    num_tiles = torch.empty(1, dtype=i32, device=dev)
+    _count(6)
+    native().moe_experts(out, x.contiguous(), w1, w2, topk_w.float().contiguous(), topk_ids.to(i32).contiguous(),
+                         tile, xs, h, ys, sorted_pair, pair_pos, tile_expert, tile_row, num_tiles, error_word(dev))
+    return out
+
+
 def moe_route(
     logits: torch.Tensor,
     k: int,
