@@ -4,6 +4,7 @@
 // tensor arguments on the host (the role of the reference's TensorMatcher,
 // python/minisgl/kernel/csrc/include/minisgl/tensor.h) and then calls the
 // plain launchers declared in ops.h on the current CUDA stream.
+#include <cstring>
 #include <ATen/cuda/CUDAContext.h>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -342,6 +343,65 @@ void moe_experts(at::Tensor out, const at::Tensor& x, const at::Tensor& w1, cons
                               static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
 }
 
+// ------------------------------------------------- symmetric heap (IPC) ----
+// Allocate a heap of `bytes` on the current device with zeroed signal slots;
+// returns (device address, CUDA IPC handle bytes) for the other ranks.
+py::tuple symm_create(int64_t bytes) {
+  MSG_CHECK(bytes > minisgl::kSymmSignalBytes, "symm_create: heap too small");
+  void* p = nullptr;
+  cudaError_t e = cudaMalloc(&p, static_cast<size_t>(bytes));
+  MSG_CHECK(e == cudaSuccess, "symm_create: cudaMalloc failed: ", cudaGetErrorString(e));
+  e = cudaMemset(p, 0, static_cast<size_t>(minisgl::kSymmSignalBytes));
+  MSG_CHECK(e == cudaSuccess, "symm_create: cudaMemset failed: ", cudaGetErrorString(e));
+  cudaIpcMemHandle_t h;
+  e = cudaIpcGetMemHandle(&h, p);
+  MSG_CHECK(e == cudaSuccess, "symm_create: cudaIpcGetMemHandle failed: ", cudaGetErrorString(e));
+  return py::make_tuple(reinterpret_cast<int64_t>(p),
+                        py::bytes(reinterpret_cast<const char*>(&h), sizeof(cudaIpcMemHandle_t)));
+}
+
+// Map a peer's heap (same node, P2P over NVLink); returns its device address here.
+int64_t symm_open(py::bytes handle) {
+  const std::string raw = handle;
+  MSG_CHECK(raw.size() == sizeof(cudaIpcMemHandle_t), "symm_open: bad handle");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, raw.data(), sizeof(h));
+  void* p = nullptr;
+  const cudaError_t e = cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess);
+  MSG_CHECK(e == cudaSuccess, "symm_open: cudaIpcOpenMemHandle failed: ", cudaGetErrorString(e));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void symm_close(int64_t ptr) { cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)); }
+void symm_free(int64_t ptr) { cudaFree(reinterpret_cast<void*>(ptr)); }
+
+// kind 0: out = sum over ranks of the partials (+ residual); kind 1:
+// out = concatenation of every rank's rows. bases: int64 CUDA tensor of the
+// heap addresses of all ranks (in this process's address space).
+void symm_collective(int64_t kind, at::Tensor out, const c10::optional<at::Tensor>& residual, const at::Tensor& bases,
+                     at::Tensor epoch, int64_t rank, int64_t world, int64_t n_elems, int64_t rows_per_rank,
+                     int64_t row_elems, const c10::optional<at::Tensor>& err) {
+  check_cuda(out, "out");
+  MSG_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous(),
+            "symm_collective: contiguous bf16 out (other dtypes as bf16 views)");
+  MSG_CHECK(bases.is_cuda() && bases.scalar_type() == at::kLong && bases.numel() == world, "symm_collective: bases");
+  MSG_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() == 1, "symm_collective: epoch");
+  const void* res = nullptr;
+  if (residual.has_value()) {
+    MSG_CHECK(residual->scalar_type() == at::kBFloat16 && residual->is_contiguous() && residual->numel() == n_elems,
+              "symm_collective: residual");
+    res = residual->data_ptr();
+  }
+  MSG_CHECK(kind == 0 ? out.numel() == n_elems : out.numel() == world * rows_per_rank * row_elems,
+            "symm_collective: output size");
+  const c10::cuda::CUDAGuard guard(out.device());
+  minisgl::launch_symm_collective(static_cast<int>(kind), bases.data_ptr<int64_t>(),
+                                  reinterpret_cast<uint32_t*>(epoch.data_ptr<int32_t>()), static_cast<int>(rank),
+                                  static_cast<int>(world), n_elems, out.data_ptr(), res,
+                                  static_cast<int>(rows_per_rank), static_cast<int>(row_elems), err_ptr(err),
+                                  stream_of(out));
+}
+
 int64_t gemm_workspace_elems(int64_t M, int64_t N, int64_t K) {
   return minisgl::gemm_workspace_elems(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
 }
@@ -644,6 +704,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fused", &gemm_fused);
   m.def("gemm_sample", &gemm_sample);
   m.def("moe_experts", &moe_experts);
+  m.def("symm_create", &symm_create);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_free", &symm_free);
+  m.def("symm_collective", &symm_collective);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);
   m.def("sample", &sample);

@@ -191,4 +191,15 @@ void launch_moe_gather(void* xs, const void* x, const int32_t* sorted_pair, int 
 void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* pair_pos, int T, int k, int H,
                         cudaStream_t s);
 
+// ------------------------------------------------------- NVLink collectives ----
+// kind 0: all-reduce of every rank's partial (bf16, n_elems, at the data
+// offset of each heap) into out (+ residual); kind 1: all-gather of
+// rows_per_rank rows of row_elems from every heap into out. bases: device
+// int64 [world] heap bases (own one included), epoch: this rank's uint32
+// call counter. See symm.cu for the protocol.
+void launch_symm_collective(int kind, const int64_t* bases, uint32_t* epoch, int rank, int world, int64_t n_elems,
+                            void* out, const void* residual, int rows_per_rank, int row_elems, int* err,
+                            cudaStream_t s);
+constexpr int64_t kSymmSignalBytes = 4096;
+
 }  // namespace minisgl

@@ -1,0 +1,204 @@
+// Tensor-parallel collectives over NVLink peer memory, issued from our own
+// kernels (no NCCL on this path).
+//
+// Symmetric heap: every rank allocates the same-sized device buffer, exports a
+// CUDA IPC handle, and maps every peer's buffer (handles are exchanged over
+// the CPU process group by minisgl/parallel/symm.py). Layout of each heap:
+//
+//   [0, 4 KB)       uint32 slots: entry[src] at 0, exit[src] at 16,
+//                   done-CTA counter at 32 (local)
+//   [4 KB, 4 KB+C)  data: this rank's partial, written before the call
+//
+// A call with epoch e (a device counter, so CUDA-graph replays advance it):
+//   1. entry barrier: CTA 0 stores e into entry[rank] of every peer
+//      (system-scope release) and every CTA waits until its own entry slots
+//      of all ranks reach e: all partials are complete;
+//   2. every rank reads all partials over NVLink in rank order 0..R-1 (the
+//      same order everywhere, so all ranks produce the same bits);
+//   3. exit barrier: the last CTA of the rank to finish stores e into
+//      exit[rank] of every peer and waits for all exit slots: no peer still
+//      reads this rank's data once the kernel has completed, so the next
+//      producer (which starts after griddepcontrol.wait) may overwrite it.
+// Waits give up after two seconds, record kErrPeerTimeout in the error word
+// and let the kernel finish (the result is then undefined but the GPU keeps
+// running). No NVLS / multicast objects are created.
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "launch.h"
+#include "ops.h"
+
+namespace minisgl {
+namespace {
+
+constexpr int kMaxRanks = 8;
+constexpr int64_t kSignalBytes = 4096;
+constexpr int kEntry = 0, kExit = 16, kDone = 32;  // uint32 slot offsets
+
+struct SymmArgs {
+  const int64_t* bases;  // [world] heap base of every rank (own one included)
+  const uint32_t* epoch; // this rank's call counter (the call uses epoch + 1)
+  int rank, world;
+  int n8;                // elements / 8 (16-byte vectors)
+  __nv_bfloat16* out;
+  const __nv_bfloat16* residual;  // all-reduce: added after the sum (may be nullptr)
+  int rows_per_rank;     // all-gather: rows of each rank's slice
+  int row_vecs;          // all-gather: 16-byte vectors per row
+  ErrorSink err;
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Threads 0..world-1: store e into slot `which` + rank of every peer.
+__device__ __forceinline__ void signal_peers(const SymmArgs& a, int which, uint32_t e) {
+  if (threadIdx.x < a.world) {
+    __threadfence_system();  // data written before the signal is visible to the peers
+    st_release_sys(reinterpret_cast<uint32_t*>(a.bases[threadIdx.x]) + which + a.rank, e);
+  }
+}
+
+// Threads 0..world-1 wait (bounded) until slot `which` + t of this rank
+// reaches e.
+__device__ __forceinline__ void wait_peers(const SymmArgs& a, int which, uint32_t e, int site) {
+  if (threadIdx.x < a.world) {
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(a.bases[a.rank]) + which + threadIdx.x;
+    const uint64_t t0 = globaltimer_ns();
+    uint32_t it = 0;
+    while (static_cast<int32_t>(ld_acquire_sys(mine) - e) < 0) {
+      if (((++it) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
+        a.err.report(kErrPeerTimeout, site + static_cast<int>(threadIdx.x));
+        break;
+      }
+    }
+  }
+}
+
+// Entry barrier; returns the epoch of this call.
+__device__ uint32_t symm_enter(const SymmArgs& a) {
+  const uint32_t e = *a.epoch + 1;
+  if (blockIdx.x == 0) signal_peers(a, kEntry, e);
+  wait_peers(a, kEntry, e, 300);
+  __syncthreads();
+  return e;
+}
+
+// Exit barrier, run by the last CTA of this rank to finish reading.
+__device__ void symm_exit(const SymmArgs& a, uint32_t e) {
+  __shared__ bool last;
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    __threadfence();
+    uint32_t* done = reinterpret_cast<uint32_t*>(a.bases[a.rank]) + kDone;
+    last = atomicAdd(done, 1u) == gridDim.x - 1;
+    if (last) *done = 0;  // ready for the next call (which starts after this kernel)
+  }
+  __syncthreads();
+  if (!last) return;
+  signal_peers(a, kExit, e);
+  wait_peers(a, kExit, e, 310);
+}
+
+__device__ __forceinline__ const uint4* data_ptr(const SymmArgs& a, int r) {
+  return reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.bases[r]) + kSignalBytes);
+}
+
+__global__ void symm_all_reduce_kernel(SymmArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t e = symm_enter(a);
+  const uint4* src[kMaxRanks];
+#pragma unroll
+  for (int r = 0; r < kMaxRanks; ++r) src[r] = r < a.world ? data_ptr(a, r) : nullptr;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.n8; i += gridDim.x * blockDim.x) {
+    float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int r = 0; r < kMaxRanks; ++r) {
+      if (r >= a.world) break;
+      const uint4 raw = src[r][i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h[q]);
+        acc[2 * q] += f.x;
+        acc[2 * q + 1] += f.y;
+      }
+    }
+    if (a.residual != nullptr) {
+      // the sum as a bf16 all-reduce would return it, then the residual add
+      const uint4 rr = reinterpret_cast<const uint4*>(a.residual)[i];
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h[q]);
+        acc[2 * q] = __bfloat162float(__float2bfloat16_rn(acc[2 * q])) + f.x;
+        acc[2 * q + 1] = __bfloat162float(__float2bfloat16_rn(acc[2 * q + 1])) + f.y;
+      }
+    }
+    uint4 pk;
+    pk.x = pack_bf16x2(acc[0], acc[1]);
+    pk.y = pack_bf16x2(acc[2], acc[3]);
+    pk.z = pack_bf16x2(acc[4], acc[5]);
+    pk.w = pack_bf16x2(acc[6], acc[7]);
+    reinterpret_cast<uint4*>(a.out)[i] = pk;
+  }
+  symm_exit(a, e);
+}
+
+// out [world * rows_per_rank, row] = concatenation of every rank's slice
+__global__ void symm_all_gather_kernel(SymmArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t e = symm_enter(a);
+  const int per_rank = a.rows_per_rank * a.row_vecs;
+  const int total = per_rank * a.world;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < total; i += gridDim.x * blockDim.x) {
+    const int r = i / per_rank;
+    reinterpret_cast<uint4*>(a.out)[i] = data_ptr(a, r)[i - r * per_rank];
+  }
+  symm_exit(a, e);
+}
+
+__global__ void symm_bump_kernel(uint32_t* epoch) {
+  pdl_launch_dependents();
+  pdl_wait();  // every CTA of the collective has read the old value
+  *epoch += 1;
+}
+
+}  // namespace
+
+void launch_symm_collective(int kind, const int64_t* bases, uint32_t* epoch, int rank, int world, int64_t n_elems,
+                            void* out, const void* residual, int rows_per_rank, int row_elems, int* err,
+                            cudaStream_t s) {
+  if (world < 1 || world > kMaxRanks) throw std::runtime_error("minisgl.symm: 1..8 ranks");
+  if (n_elems % 8 != 0) throw std::runtime_error("minisgl.symm: element count must be a multiple of 8");
+  SymmArgs a{};
+  a.bases = bases;
+  a.epoch = epoch;
+  a.rank = rank;
+  a.world = world;
+  a.n8 = static_cast<int>(n_elems / 8);
+  a.out = static_cast<__nv_bfloat16*>(out);
+  a.residual = static_cast<const __nv_bfloat16*>(residual);
+  a.rows_per_rank = rows_per_rank;
+  a.row_vecs = row_elems / 8;
+  a.err = ErrorSink{err};
+  const int threads = 512;
+  const int64_t work = kind == 0 ? a.n8 : static_cast<int64_t>(a.n8) * world;
+  const int blocks = static_cast<int>(std::max<int64_t>(1, std::min<int64_t>((work + threads - 1) / threads, 148 * 2)));
+  if (kind == 0) launch_pdl(symm_all_reduce_kernel, dim3(blocks), dim3(threads), 0, s, a);
+  else launch_pdl(symm_all_gather_kernel, dim3(blocks), dim3(threads), 0, s, a);
+  launch_pdl(symm_bump_kernel, dim3(1), dim3(1), 0, s, epoch);
+}
+
+}  // namespace minisgl

@@ -73,6 +73,13 @@ class LinearRowParallel(_Linear):
         if self._tp == 1:
             return ops.gemm_fused(x, self.weight, bias=self.bias, residual=residual, out=residual)
         first = get_tp_info().rank == 0
+        plugin = DistributedCommunicator.plugins[-1]
+        if hasattr(plugin, "partial_buffer"):
+            # NVLink collectives: the GEMM writes its partial into the symmetric
+            # heap and one kernel sums all ranks' partials into the residual
+            part = plugin.partial_buffer(x.shape[0], self.weight.shape[0])
+            ops.gemm_fused(x, self.weight, bias=self.bias if first else None, out=part)
+            return plugin.reduce_into(part, residual)
         y = ops.gemm_fused(x, self.weight, bias=self.bias if first else None, residual=residual if first else None)
         return self._comm.all_reduce(y)
 

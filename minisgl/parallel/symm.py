@@ -1,0 +1,136 @@
+"""Tensor-parallel collectives from our own kernels over NVLink peer memory.
+
+``--comm fused`` registers ``SymmMemImpl`` as the communicator plugin. Each
+rank allocates a symmetric heap (same size on every rank, CUDA IPC handles
+exchanged over a gloo group, every peer's heap mapped into this process) and
+the collectives are one kernel each (``minisgl/csrc/symm.cu``): a one-shot
+all-reduce that sums every rank's partial over NVLink in rank order, with the
+residual add fused, and an all-gather; both synchronise through flags in the
+heaps with bounded waits. No NCCL call and no NVLS multicast object is used
+on this path.
+
+The row-parallel projections (o_proj, down_proj) write their GEMM output
+straight into the heap (``partial_buffer``), so the reduction reads the
+partials where the tensor cores left them: one GEMM kernel and one
+collective kernel per projection, chained with programmatic dependent launch.
+
+The reference's counterpart is the PyNCCL plugin over NCCL symmetric windows
+(python/minisgl/kernel/pynccl.py, src/pynccl.cu:72-188).
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from minisgl import ops
+
+from .comm import DistributedImpl, register_plugin
+
+SIGNAL_BYTES = 4096
+
+
+class _DeviceBuffer:
+    """Exposes a raw device address as a torch tensor (CUDA array interface)."""
+
+    def __init__(self, ptr: int, nbytes: int) -> None:
+        self.__cuda_array_interface__ = {"shape": (nbytes,), "typestr": "|u1", "data": (ptr, False), "version": 3}
+
+
+class SymmMemImpl(DistributedImpl):
+    def __init__(self, device: torch.device, capacity_bytes: int, group: Optional[dist.ProcessGroup] = None) -> None:
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        if self.world > 8:
+            raise ValueError("the NVLink collectives support up to 8 ranks")
+        self.device = device
+        self.capacity = (max(capacity_bytes, 1 << 20) + 255) // 256 * 256
+        native = ops.native()
+        ranks = dist.get_process_group_ranks(group) if group is not None else list(range(self.world))
+        self._cpu_group = dist.new_group(ranks=ranks, backend="gloo")
+        with torch.cuda.device(device):
+            own, handle = native.symm_create(SIGNAL_BYTES + self.capacity)
+        handles: List[Optional[bytes]] = [None] * self.world
+        dist.all_gather_object(handles, handle, group=self._cpu_group)
+        bases: List[int] = []
+        self._opened: List[int] = []
+        with torch.cuda.device(device):
+            for r in range(self.world):
+                if r == self.rank:
+                    bases.append(own)
+                else:
+                    p = native.symm_open(handles[r])
+                    self._opened.append(p)
+                    bases.append(p)
+        self._own = own
+        self.bases = torch.tensor(bases, dtype=torch.int64, device=device)
+        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
+        self.data = torch.as_tensor(_DeviceBuffer(own + SIGNAL_BYTES, self.capacity), device=device)
+        dist.barrier(group=self._cpu_group)  # every heap is mapped before the first collective
+
+    # -------------------------------------------------------------- buffers
+    def partial_buffer(self, rows: int, cols: int, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
+        """This rank's heap data region viewed as [rows, cols]: a GEMM writes
+        its partial product here and ``reduce_into`` sums the partials."""
+        n = rows * cols * torch.finfo(dtype).bits // 8
+        if n > self.capacity:
+            raise RuntimeError(f"symmetric heap too small: {n} > {self.capacity} bytes")
+        return self.data[:n].view(dtype).view(rows, cols)
+
+    def _collective(self, kind: int, out: torch.Tensor, n_elems: int, residual: Optional[torch.Tensor] = None,
+                    rows: int = 0, row_elems: int = 0) -> None:
+        ops._count(2)
+        ops.native().symm_collective(kind, out, residual, self.bases, self.epoch, self.rank, self.world, n_elems, rows,
+                                     row_elems, ops.error_word(out.device))
+
+    # ---------------------------------------------------------- collectives
+    def reduce_into(self, partial: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
+        """residual += sum of every rank's ``partial`` (a ``partial_buffer``),
+        in place."""
+        self._collective(0, residual, partial.numel(), residual=residual)
+        return residual
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        if x.dtype != torch.bfloat16 or x.numel() % 8 != 0 or 2 * x.numel() > self.capacity:
+            dist.all_reduce(x, group=self.group)  # outside the kernel's domain: library collective
+            return x
+        buf = self.partial_buffer(x.numel(), 1).view(x.shape)
+        buf.copy_(x)
+        self._collective(0, x, x.numel())
+        return x
+
+    def all_gather(self, x: torch.Tensor) -> torch.Tensor:
+        """Rows of every rank concatenated; a byte copy, so 16- and 32-bit
+        tensors both go through the kernel (as bf16 units)."""
+        rows = x.shape[0]
+        out = x.new_empty((rows * self.world,) + tuple(x.shape[1:]))
+        units = x.contiguous().view(-1).view(torch.bfloat16) if x.element_size() in (2, 4) else None
+        row = units.numel() // max(rows, 1) if units is not None else 0
+        if units is None or rows == 0 or row % 8 != 0 or 2 * units.numel() > self.capacity:
+            dist.all_gather_into_tensor(out, x.contiguous(), group=self.group)
+            return out
+        self.partial_buffer(units.numel(), 1).view(-1).copy_(units)
+        self._collective(1, out.view(-1).view(torch.bfloat16), units.numel(), rows=rows, row_elems=row)
+        return out
+
+    def shutdown(self) -> None:
+        native = ops.native()
+        torch.cuda.synchronize(self.device)
+        if self._cpu_group is not None:
+            dist.barrier(group=self._cpu_group)  # no peer reads this heap any more
+        for p in self._opened:
+            native.symm_close(p)
+        self._opened = []
+        if self._own:
+            native.symm_free(self._own)
+            self._own = 0
+
+
+def enable_symm_comm(device: torch.device, capacity_bytes: int) -> SymmMemImpl:
+    """Register the NVLink collectives as the tensor-parallel communicator."""
+    impl = SymmMemImpl(device, capacity_bytes)
+    register_plugin(impl)
+    return impl

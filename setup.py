@@ -30,6 +30,7 @@ SOURCES = [
     "minisgl/csrc/rope_store.cu",
     "minisgl/csrc/sampling.cu",
     "minisgl/csrc/moe.cu",
+    "minisgl/csrc/symm.cu",
 ]
 
 

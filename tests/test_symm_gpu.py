@@ -1,0 +1,159 @@
+"""NVLink collectives from our own kernels (``--comm fused``) on 2 GPUs: the
+one-shot all-reduce (plain and with the residual add fused), the all-gather
+and a CUDA-graph replay against NCCL, and a TP=2 engine with the fused
+communicator against one with NCCL. Ranks are child processes; NCCL's NVLS
+is off and no multicast object is created."""
+
+import os
+import socket
+from datetime import timedelta
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _need_two_gpus():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+
+
+def _close(a, b, tol=2e-2):
+    return (a.float() - b.float()).abs().max().item() <= tol * max(1.0, b.float().abs().max().item())
+
+
+def _collectives(rank, world, port, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    impl = None
+    msgs = []
+    try:
+        from minisgl import ops
+        from minisgl.parallel.symm import SymmMemImpl
+
+        impl = SymmMemImpl(dev, 8 << 20)
+        g = torch.Generator(device=dev).manual_seed(rank + 1)
+        for n in (8, 8192, 262144):
+            x = torch.randn(n, device=dev, generator=g).to(torch.bfloat16)
+            ref = x.float().clone()
+            dist.all_reduce(ref)
+            out = impl.all_reduce(x.clone())
+            if not _close(out, ref):
+                msgs.append(f"all_reduce n={n}")
+            # every rank must produce the same bits
+            outs = [torch.empty_like(out) for _ in range(world)]
+            dist.all_gather(outs, out)
+            if not all(torch.equal(o, outs[0]) for o in outs):
+                msgs.append(f"ranks differ n={n}")
+        # GEMM partial written into the heap, reduced into the residual in place
+        part = impl.partial_buffer(64, 1024)
+        part.copy_(torch.randn(64, 1024, device=dev, generator=g).to(torch.bfloat16))
+        res = torch.randn(64, 1024, device=dev, generator=g).to(torch.bfloat16)
+        total = part.float().clone()
+        dist.all_reduce(total)
+        expect = (total.to(torch.bfloat16).float() + res.float())
+        got = impl.reduce_into(part, res.clone())
+        if not _close(got, expect):
+            msgs.append("reduce_into")
+        for dt in (torch.bfloat16, torch.float32):
+            x = torch.randn(5, 256, device=dev, generator=g).to(dt)
+            out = impl.all_gather(x)
+            ref = torch.empty_like(out)
+            dist.all_gather_into_tensor(ref, x)
+            if not torch.equal(out, ref):
+                msgs.append(f"all_gather {dt}")
+        # CUDA graph: the device epoch advances on every replay
+        buf = torch.zeros(4096, device=dev, dtype=torch.bfloat16)
+        stream = torch.cuda.Stream(dev)
+        stream.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(stream):
+            impl.all_reduce(buf)
+        torch.cuda.current_stream(dev).wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph, stream=stream):
+            impl.all_reduce(buf)
+        for it in range(3):
+            buf.fill_(float(rank + it))
+            graph.replay()
+            torch.cuda.synchronize(dev)
+            want = float(sum(r + it for r in range(world)))
+            if not torch.all(buf.float() == want):
+                msgs.append(f"graph replay {it}")
+        del graph
+        torch.cuda.synchronize(dev)
+        code, _ = ops.error_word(dev).tolist()
+        if code != 0:
+            msgs.append(f"device error {code}")
+    except Exception as e:  # reported to the parent
+        msgs.append(repr(e))
+    finally:
+        if impl is not None:
+            impl.shutdown()
+        dist.destroy_process_group()
+    q.put((rank, msgs))
+
+
+def _spawn(target, world, *args):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, q) + args) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=400) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return results
+
+
+def test_nvlink_collectives_match_nccl():
+    _need_two_gpus()
+    results = _spawn(_collectives, 2)
+    assert results == {0: [], 1: []}, results
+
+
+def _engine(rank, world, port, q, comm):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from minisgl.core import SamplingParams
+    from minisgl.llm import LLM
+    from minisgl.parallel import DistributedInfo
+    from minisgl.utils.synthetic import make_model_dir
+
+    torch.cuda.set_device(rank)
+    llm = LLM(make_model_dir("small-qwen3"), dtype=torch.bfloat16, device=f"cuda:{rank}", use_dummy_weight=True,
+              tp_info=DistributedInfo(rank, world), page_size=64, num_page_override=128, max_running_req=8,
+              max_seq_len_override=1024, max_extend_tokens=512, cuda_graph_max_bs=8, distributed_port=port,
+              comm=comm)
+    prompts = [[(7 * i + 3 * j) % 4000 for j in range(40 + 9 * i)] for i in range(4)]
+    outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
+    q.put((rank, [o["token_ids"] for o in outs]))
+    llm.shutdown()
+
+
+def test_tp2_engine_fused_comm_matches_nccl():
+    _need_two_gpus()
+    fused = _spawn(_engine, 2, "fused")
+    nccl = _spawn(_engine, 2, "nccl")
+    assert fused[0] == fused[1]
+    # the two reductions round differently (fp32 sum then residual add, vs a
+    # bf16 NCCL sum of partial + residual), so a near-tie of the random-init
+    # logits may flip and the sequence then diverges; a wrong reduction would
+    # scramble nearly every token
+    a, b = fused[0], nccl[0]
+    same = sum(p == q for x, y in zip(a, b) for p, q in zip(x, y))
+    firsts = sum(x[0] == y[0] for x, y in zip(a, b))
+    assert firsts >= 3 and same >= 0.6 * sum(len(x) for x in a), (a, b)
