@@ -402,6 +402,43 @@ void symm_collective(int64_t kind, at::Tensor out, const c10::optional<at::Tenso
                                   stream_of(out));
 }
 
+// residual += all-reduce over ranks of x @ w^T (+ bias on the caller's rank
+// 0): one fused kernel when the grid is resident (see gemm.cu). epoch: int32
+// [2] device counters (fused GEMM, collective kernel).
+void gemm_allreduce(at::Tensor residual, const at::Tensor& x, const at::Tensor& w,
+                    const c10::optional<at::Tensor>& bias, const at::Tensor& bases, at::Tensor epoch,
+                    int64_t own_base, int64_t rank, int64_t world, int64_t half_bytes, int64_t force_mode,
+                    int64_t force_splits, int64_t force_bn, const c10::optional<at::Tensor>& err) {
+  check_cuda(x, "x");
+  check_rowmajor(x, "x");
+  check_rowmajor(w, "w");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 &&
+                residual.scalar_type() == at::kBFloat16 && residual.is_contiguous(),
+            "gemm_allreduce: bf16 x, w and contiguous residual");
+  MSG_CHECK(x.size(1) == w.size(1) && residual.size(0) == x.size(0) && residual.size(1) == w.size(0),
+            "gemm_allreduce: shapes");
+  MSG_CHECK(bases.is_cuda() && bases.scalar_type() == at::kLong && bases.numel() == world, "gemm_allreduce: bases");
+  MSG_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() == 2, "gemm_allreduce: epoch [2]");
+  minisgl::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.bias = bias.has_value() ? bias->data_ptr() : nullptr;
+  a.M = static_cast<int>(x.size(0));
+  a.N = static_cast<int>(w.size(0));
+  a.K = static_cast<int>(x.size(1));
+  a.ldx = static_cast<int>(x.stride(0));
+  a.ldw = static_cast<int>(w.stride(0));
+  a.ldo = a.N;
+  a.force_mode = static_cast<int>(force_mode);
+  a.force_splits = static_cast<int>(force_splits);
+  a.force_bn = static_cast<int>(force_bn);
+  a.err = err_ptr(err);
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_gemm_allreduce(a, bases.data_ptr<int64_t>(), reinterpret_cast<uint32_t*>(epoch.data_ptr<int32_t>()),
+                                 own_base, static_cast<int>(rank), static_cast<int>(world), half_bytes,
+                                 residual.data_ptr(), stream_of(x));
+}
+
 int64_t gemm_workspace_elems(int64_t M, int64_t N, int64_t K) {
   return minisgl::gemm_workspace_elems(static_cast<int>(M), static_cast<int>(N), static_cast<int>(K));
 }
@@ -709,6 +746,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("symm_collective", &symm_collective);
+  m.def("gemm_allreduce", &gemm_allreduce);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);
   m.def("sample", &sample);

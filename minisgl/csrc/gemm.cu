@@ -190,6 +190,34 @@ __device__ __forceinline__ void rope_epilogue(const KParams& p, int head, int m,
   store4_bf16(cache + ((static_cast<int64_t>(page) * e.hk + kvh) * e.page_size + off) * 128 + ocol, v);
 }
 
+// kEpiAllReduce heap addressing: [signal 4 KB][flags 16 KB][collective data
+// C][half 0 C][half 1 C], C = ar_half_bytes.
+__device__ __forceinline__ __nv_bfloat16* ar_half(const KParams& p, int r, uint32_t e) {
+  uint8_t* base = reinterpret_cast<uint8_t*>(p.epi.ar_bases[r]);
+  return reinterpret_cast<__nv_bfloat16*>(base + kSymmSignalBytes + kSymmFlagBytes +
+                                          (1 + (e & 1u)) * p.epi.ar_half_bytes);
+}
+__device__ __forceinline__ uint32_t* ar_flag(const KParams& p, int r, int cta) {
+  return reinterpret_cast<uint32_t*>(reinterpret_cast<uint8_t*>(p.epi.ar_bases[r]) + kSymmSignalBytes) + cta;
+}
+__device__ __forceinline__ void ar_store_release(uint32_t* f, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(f), "r"(v) : "memory");
+}
+// bounded wait until a peer's flag reaches e (kErrPeerTimeout after 2 s)
+__device__ __forceinline__ void ar_wait(const KParams& p, const uint32_t* f, uint32_t e) {
+  const uint64_t t0 = globaltimer_ns();
+  uint32_t it = 0;
+  while (true) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(f) : "memory");
+    if (static_cast<int32_t>(v - e) >= 0) return;
+    if (((++it) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
+      p.err.report(kErrPeerTimeout, 320);
+      return;
+    }
+  }
+}
+
 // kEpiSample for one token row m of one 128-row vocabulary tile; the calling
 // warp holds the row (lane l: vocabulary entries n .. n + 3, n = tile base +
 // 4 l). Score and tie rule are the sampling kernel's: score = logit / max(T,
@@ -730,6 +758,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     } else {
       const int vecs = rows_per * (kOutCols / 4);
       const bool rope = (p.epi.kind & kEpiRope) != 0;
+      const bool allreduce = (p.epi.kind & kEpiAllReduce) != 0;
+      const uint32_t ar_e = allreduce ? *p.epi.ar_epoch + 1 : 0u;  // after griddepcontrol.wait (see below)
       for (int e = threadIdx.x; e < vecs; e += kThreads) {
         // kEpiRope relies on one warp covering one 128-feature head of one
         // token row: kOutCols / 4 is a multiple of 32 vectors per row and
@@ -748,6 +778,11 @@ __global__ void __launch_bounds__(kThreads, 1)
         float v[4] = {acc.x * sc, acc.y * sc, acc.z * sc, acc.w * sc};
         if (p.bias != nullptr)
           for (int q = 0; q < 4; ++q) v[q] += n + q < p.N ? __bfloat162float(p.bias[n + q]) : 0.f;
+        if (allreduce) {
+          // this rank's partial, rounded as a bf16 GEMM output would be
+          store4_bf16(ar_half(p, p.epi.ar_rank, ar_e) + static_cast<size_t>(m) * p.N + n, v);
+          continue;
+        }
         if (rope) {
           rope_epilogue(p, n / 128, m, n % 128, v);
           continue;
@@ -773,6 +808,43 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int q = 0; q < 4 && n + q < p.N; ++q) store_out(p, m, n + q, v[q]);
         }
       }
+      if (allreduce) {
+        // Exchange with the other ranks: every rank runs the same plan, so
+        // CTA `cta` covers the same output elements everywhere. The epoch was
+        // read after this CTA's producer passed griddepcontrol.wait, i.e.
+        // after the previous call's counter bump completed.
+        const int cta = static_cast<int>((blockIdx.z * gridDim.y + blockIdx.y) * gridDim.x + blockIdx.x);
+        __syncthreads();
+        if (threadIdx.x == 0) {
+          __threadfence_system();
+          ar_store_release(ar_flag(p, p.epi.ar_rank, cta), ar_e);
+        }
+        if (threadIdx.x < p.epi.ar_world) ar_wait(p, ar_flag(p, threadIdx.x, cta), ar_e);
+        __syncthreads();
+        for (int e = threadIdx.x; e < vecs; e += kThreads) {
+          const int orow = rank * rows_per + e / (kOutCols / 4);
+          const int ocol = (e % (kOutCols / 4)) * 4;
+          const int m = tok0 + orow;
+          const int n = feat0 + ocol;
+          if (m >= p.M || n >= p.N) continue;
+          float v[4] = {0.f, 0.f, 0.f, 0.f};
+          for (int r = 0; r < p.epi.ar_world; ++r) {  // rank order: the same bits on every rank
+            const uint2 raw = *reinterpret_cast<const uint2*>(ar_half(p, r, ar_e) + static_cast<size_t>(m) * p.N + n);
+            const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.x));
+            const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&raw.y));
+            v[0] += a.x, v[1] += a.y, v[2] += b.x, v[3] += b.y;
+          }
+          if ((p.epi.kind & kEpiResidual) != 0) {
+            const uint2 rr = *reinterpret_cast<const uint2*>(
+                reinterpret_cast<const __nv_bfloat16*>(p.epi.residual) + static_cast<size_t>(m) * p.epi.ld_res + n);
+            const float2 r0 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rr.x));
+            const float2 r1 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&rr.y));
+            v[0] = round_bf16(v[0]) + r0.x, v[1] = round_bf16(v[1]) + r0.y;
+            v[2] = round_bf16(v[2]) + r1.x, v[3] = round_bf16(v[3]) + r1.y;
+          }
+          store4_bf16(reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + n, v);
+        }
+      }
     }
     if (clustered) cluster_sync();  // peers may still be reading this CTA's tile
   }
@@ -785,6 +857,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_dealloc(tmem, kCols);
   }
 }
+
+// When set, launch_tile reports grid residency here instead of launching.
+thread_local int* g_resident_query = nullptr;
 
 template <int BN, int STAGES, bool SWAP, bool SPLIT>
 void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp, dim3 grid, int splits,
@@ -820,6 +895,23 @@ void launch_tile(const CUtensorMap& ta, const CUtensorMap& tb, const KParams& kp
   }
   cfg.attrs = attrs;
   cfg.numAttrs = n;
+  if (g_resident_query != nullptr) {
+    // query only: can every CTA (cluster) of this grid be resident at once?
+    int sms = 0;
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int64_t ctas = static_cast<int64_t>(grid.x) * grid.y * grid.z;
+    if (SPLIT && splits > 1) {
+      int clusters = 0;
+      const cudaError_t q = cudaOccupancyMaxActiveClusters(&clusters, kern, &cfg);
+      *g_resident_query = q == cudaSuccess && static_cast<int64_t>(clusters) * splits >= ctas;
+    } else {
+      int per_sm = 0;
+      const cudaError_t q = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kern, kThreads, smem);
+      *g_resident_query = q == cudaSuccess && static_cast<int64_t>(per_sm) * sms >= ctas;
+    }
+    if (ctas > kSymmFlagBytes / 4) *g_resident_query = 0;  // one flag slot per CTA
+    return;
+  }
   cudaError_t e = cudaLaunchKernelEx(&cfg, kern, ta, tb, kp);
   if (e != cudaSuccess) throw std::runtime_error(std::string("minisgl.gemm launch failed: ") + cudaGetErrorString(e));
 }
@@ -832,7 +924,8 @@ void dispatch_split(int splits, const CUtensorMap& ta, const CUtensorMap& tb, KP
   // fused epilogues of weight-major tiles live in the cluster (split-K) path
   // (one split = a cluster of one); token-major tiles without split-K apply
   // them straight from TMEM
-  if (splits > 1 || (SWAP && kp.epi.kind != 0)) launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
+  if (splits > 1 || (SWAP && kp.epi.kind != 0) || (kp.epi.kind & kEpiAllReduce) != 0)
+    launch_tile<BN, STAGES, SWAP, true>(ta, tb, kp, grid, splits, stream);
   else launch_tile<BN, STAGES, SWAP, false>(ta, tb, kp, grid, 1, stream);
 }
 
@@ -997,6 +1090,50 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
       default: dispatch_split<256, 4, false>(pl.splits, ta, tb, kp, grid, stream); break;
     }
   }
+}
+
+// Row-parallel GEMM with the tensor-parallel all-reduce. When every CTA of
+// the planned grid can be resident at once, one kernel computes, exchanges
+// and reduces (kEpiAllReduce; CTAs wait on the same CTA of the other ranks,
+// which is only deadlock-free if none of them waits for a slot). Otherwise
+// the GEMM writes its partial into the heap's collective region and the
+// collective kernel reduces it.
+void launch_gemm_allreduce(const GemmArgs& a, const int64_t* bases, uint32_t* epoch, int64_t own_base, int rank,
+                           int world, int64_t half_bytes, void* residual_out, cudaStream_t s) {
+  if (static_cast<int64_t>(a.M) * a.N * 2 > half_bytes)
+    throw std::runtime_error("minisgl.gemm_allreduce: output larger than the heap half");
+  GemmArgs b = a;
+  b.out = residual_out;
+  b.ldo = a.N;
+  b.epi.kind = kEpiAllReduce | kEpiResidual;
+  b.epi.residual = residual_out;
+  b.epi.ld_res = a.N;
+  b.epi.ar_bases = bases;
+  b.epi.ar_epoch = epoch;
+  b.epi.ar_rank = rank;
+  b.epi.ar_world = world;
+  b.epi.ar_half_bytes = half_bytes;
+  int resident = 0;
+  g_resident_query = &resident;
+  try {
+    launch_gemm(b, s);
+  } catch (...) {
+    g_resident_query = nullptr;
+    throw;
+  }
+  g_resident_query = nullptr;
+  if (resident) {
+    launch_gemm(b, s);
+    launch_epoch_bump(epoch, s);
+    return;
+  }
+  GemmArgs c = a;  // the partial into the collective region, then the collective kernel
+  c.out = reinterpret_cast<void*>(own_base + kSymmSignalBytes + kSymmFlagBytes);
+  c.ldo = a.N;
+  c.epi.kind = 0;
+  launch_gemm(c, s);
+  launch_symm_collective(0, bases, epoch + 1, rank, world, static_cast<int64_t>(a.M) * a.N, residual_out,
+                         residual_out, 0, 0, a.err, s);
 }
 
 }  // namespace minisgl

@@ -31,7 +31,14 @@ enum class DType : int { kF32 = 0, kBF16 = 1, kF16 = 2 };
 //                index, score = logit / T + Gumbel noise of the sampler's
 //                counter-based stream (T <= 0: the plain logit, argmax);
 //                launch_lm_sample_reduce turns the partials into tokens.
-enum : int { kEpiNorm = 1, kEpiResidual = 2, kEpiSiluMul = 4, kEpiRope = 8, kEpiSample = 16 };
+//   kEpiAllReduce tensor-parallel row-parallel GEMM: the CTA writes its
+//                rounded partial tile into its symmetric heap (half epoch & 1),
+//                flags it, waits for the same CTA's flag on every peer, and
+//                stores sum over ranks (rank order) of the partials (+ residual
+//                with kEpiResidual) into out. Needs every CTA of the grid
+//                resident at once (checked; otherwise the host runs the GEMM
+//                into the heap and the separate collective kernel).
+enum : int { kEpiNorm = 1, kEpiResidual = 2, kEpiSiluMul = 4, kEpiRope = 8, kEpiSample = 16, kEpiAllReduce = 32 };
 struct GemmEpilogue {
   int kind;
   float eps;                  // kEpiNorm
@@ -52,6 +59,10 @@ struct GemmEpilogue {
   float* part_val;            // [M, ntiles]
   int32_t* part_idx;
   int ntiles;                 // ceil(N / 128)
+  const int64_t* ar_bases;    // kEpiAllReduce: [world] heap bases (own included)
+  const uint32_t* ar_epoch;   // this rank's call counter (the call uses epoch + 1)
+  int ar_rank, ar_world;
+  int64_t ar_half_bytes;      // bytes of one data half of the heap
 };
 
 struct GemmArgs {
@@ -201,5 +212,13 @@ void launch_symm_collective(int kind, const int64_t* bases, uint32_t* epoch, int
                             void* out, const void* residual, int rows_per_rank, int row_elems, int* err,
                             cudaStream_t s);
 constexpr int64_t kSymmSignalBytes = 4096;
+// GEMM with the all-reduce fused (kEpiAllReduce) when the grid is resident,
+// otherwise GEMM into the heap data region + launch_symm_collective. Heap
+// layout for the fused kind: [signal 4 KB][flags 16 KB][half 0][half 1].
+constexpr int64_t kSymmFlagBytes = 16384;
+// advance a uint32 call counter after every CTA of the previous kernel read it
+void launch_epoch_bump(uint32_t* epoch, cudaStream_t s);
+void launch_gemm_allreduce(const GemmArgs& a, const int64_t* bases, uint32_t* epoch, int64_t own_base, int rank,
+                           int world, int64_t half_bytes, void* residual_out, cudaStream_t s);
 
 }  // namespace minisgl

@@ -5,9 +5,13 @@
 // CUDA IPC handle, and maps every peer's buffer (handles are exchanged over
 // the CPU process group by minisgl/parallel/symm.py). Layout of each heap:
 //
-//   [0, 4 KB)       uint32 slots: entry[src] at 0, exit[src] at 16,
-//                   done-CTA counter at 32 (local)
-//   [4 KB, 4 KB+C)  data: this rank's partial, written before the call
+//   [0, 4 KB)        uint32 slots: entry[src] at 0, exit[src] at 16,
+//                    done-CTA counter at 32 (local)
+//   [4 KB, 20 KB)    per-CTA flags of the GEMM with the all-reduce fused
+//                    (gemm.cu, kEpiAllReduce)
+//   [20 KB, +C)      collective data: this rank's partial, written before
+//                    the call
+//   [+C, +3C)        the fused GEMM's two partial halves (gemm.cu)
 //
 // A call with epoch e (a device counter, so CUDA-graph replays advance it):
 //   1. entry barrier: CTA 0 stores e into entry[rank] of every peer
@@ -110,7 +114,8 @@ __device__ void symm_exit(const SymmArgs& a, uint32_t e) {
 }
 
 __device__ __forceinline__ const uint4* data_ptr(const SymmArgs& a, int r) {
-  return reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.bases[r]) + kSignalBytes);
+  return reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.bases[r]) + kSignalBytes +
+                                        kSymmFlagBytes);
 }
 
 __global__ void symm_all_reduce_kernel(SymmArgs a) {
@@ -176,6 +181,10 @@ __global__ void symm_bump_kernel(uint32_t* epoch) {
 }
 
 }  // namespace
+
+void launch_epoch_bump(uint32_t* epoch, cudaStream_t s) {
+  launch_pdl(symm_bump_kernel, dim3(1), dim3(1), 0, s, epoch);
+}
 
 void launch_symm_collective(int kind, const int64_t* bases, uint32_t* epoch, int rank, int world, int64_t n_elems,
                             void* out, const void* residual, int rows_per_rank, int row_elems, int* err,

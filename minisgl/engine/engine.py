@@ -182,6 +182,17 @@ class Engine:
         cache = os.environ.get("MINISGL_GEMM_TUNE_CACHE") or None
         kinds = self.model.fused_gemm_kinds() if hasattr(self.model, "fused_gemm_kinds") else {}
         plans = gemm_tune.tune(self._gemm_shapes(), bs, self.device, cache, fused=kinds, prefill=True)
+        if self.tp_cpu_group is not None:
+            # every rank must run the same tile plans: the kernels with the
+            # all-reduce fused pair CTA i of one rank with CTA i of the others
+            import torch.distributed as dist
+
+            tables = [dict(gemm_tune.PLANS), dict(gemm_tune.FUSED_PLANS)]
+            dist.broadcast_object_list(tables, src=0, group=self.tp_cpu_group, device=torch.device("cpu"))
+            gemm_tune.PLANS.clear()
+            gemm_tune.PLANS.update(tables[0])
+            gemm_tune.FUSED_PLANS.clear()
+            gemm_tune.FUSED_PLANS.update(tables[1])
         logger.info_rank0(f"Tuned {len(plans)} GEMM plans in {time.perf_counter() - t0:.1f}s")
 
     def _init_communication(self, config: EngineConfig):

@@ -74,12 +74,10 @@ class LinearRowParallel(_Linear):
             return ops.gemm_fused(x, self.weight, bias=self.bias, residual=residual, out=residual)
         first = get_tp_info().rank == 0
         plugin = DistributedCommunicator.plugins[-1]
-        if hasattr(plugin, "partial_buffer"):
-            # NVLink collectives: the GEMM writes its partial into the symmetric
-            # heap and one kernel sums all ranks' partials into the residual
-            part = plugin.partial_buffer(x.shape[0], self.weight.shape[0])
-            ops.gemm_fused(x, self.weight, bias=self.bias if first else None, out=part)
-            return plugin.reduce_into(part, residual)
+        if hasattr(plugin, "gemm_reduce_into") and x.is_cuda:
+            # NVLink collectives: the GEMM exchanges its output tiles with the
+            # other ranks and adds the residual in one kernel
+            return plugin.gemm_reduce_into(x, self.weight, self.bias, residual)
         y = ops.gemm_fused(x, self.weight, bias=self.bias if first else None, residual=residual if first else None)
         return self._comm.all_reduce(y)
 

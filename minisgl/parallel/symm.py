@@ -9,10 +9,11 @@ residual add fused, and an all-gather; both synchronise through flags in the
 heaps with bounded waits. No NCCL call and no NVLS multicast object is used
 on this path.
 
-The row-parallel projections (o_proj, down_proj) write their GEMM output
-straight into the heap (``partial_buffer``), so the reduction reads the
-partials where the tensor cores left them: one GEMM kernel and one
-collective kernel per projection, chained with programmatic dependent launch.
+The row-parallel projections (o_proj, down_proj) run one kernel each
+(``gemm_reduce_into``): every output tile is computed, written into this
+rank's heap, exchanged with the same tile of the other ranks over NVLink and
+summed with the residual in the GEMM's epilogue, tile by tile, so the
+transfer of one tile overlaps the math of the others.
 
 The reference's counterpart is the PyNCCL plugin over NCCL symmetric windows
 (python/minisgl/kernel/pynccl.py, src/pynccl.cu:72-188).
@@ -30,6 +31,8 @@ from minisgl import ops
 from .comm import DistributedImpl, register_plugin
 
 SIGNAL_BYTES = 4096
+FLAG_BYTES = 16384  # per-CTA flags of the GEMM with the all-reduce fused
+DATA_OFFSET = SIGNAL_BYTES + FLAG_BYTES
 
 
 class _DeviceBuffer:
@@ -52,7 +55,8 @@ class SymmMemImpl(DistributedImpl):
         ranks = dist.get_process_group_ranks(group) if group is not None else list(range(self.world))
         self._cpu_group = dist.new_group(ranks=ranks, backend="gloo")
         with torch.cuda.device(device):
-            own, handle = native.symm_create(SIGNAL_BYTES + self.capacity)
+            # [signals][GEMM flags][collective data][two GEMM partial halves]
+            own, handle = native.symm_create(DATA_OFFSET + 3 * self.capacity)
         handles: List[Optional[bytes]] = [None] * self.world
         dist.all_gather_object(handles, handle, group=self._cpu_group)
         bases: List[int] = []
@@ -67,8 +71,9 @@ class SymmMemImpl(DistributedImpl):
                     bases.append(p)
         self._own = own
         self.bases = torch.tensor(bases, dtype=torch.int64, device=device)
-        self.epoch = torch.zeros(1, dtype=torch.int32, device=device)
-        self.data = torch.as_tensor(_DeviceBuffer(own + SIGNAL_BYTES, self.capacity), device=device)
+        # call counters: [0] the fused GEMM + all-reduce, [1] the collective kernels
+        self.epoch = torch.zeros(2, dtype=torch.int32, device=device)
+        self.data = torch.as_tensor(_DeviceBuffer(own + DATA_OFFSET, self.capacity), device=device)
         dist.barrier(group=self._cpu_group)  # every heap is mapped before the first collective
 
     # -------------------------------------------------------------- buffers
@@ -83,10 +88,25 @@ class SymmMemImpl(DistributedImpl):
     def _collective(self, kind: int, out: torch.Tensor, n_elems: int, residual: Optional[torch.Tensor] = None,
                     rows: int = 0, row_elems: int = 0) -> None:
         ops._count(2)
-        ops.native().symm_collective(kind, out, residual, self.bases, self.epoch, self.rank, self.world, n_elems, rows,
-                                     row_elems, ops.error_word(out.device))
+        ops.native().symm_collective(kind, out, residual, self.bases, self.epoch[1:], self.rank, self.world, n_elems,
+                                     rows, row_elems, ops.error_word(out.device))
 
     # ---------------------------------------------------------- collectives
+    def gemm_reduce_into(self, x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],
+                         residual: torch.Tensor) -> torch.Tensor:
+        """residual += all-reduce over ranks of x @ w^T (+ bias, added by rank
+        0): one kernel computes each output tile, exchanges it with the other
+        ranks over NVLink and adds the residual, when the whole grid fits on
+        the GPU at once; otherwise the GEMM writes into the heap and the
+        collective kernel reduces. Plans are the tuned fused-epilogue plans,
+        which the engine keeps identical on every rank."""
+        plan = ops._gemm_fused_plans.get((x.shape[0], w.shape[0], x.shape[1]), (0, 0, 0))
+        ops._count(2)
+        ops.native().gemm_allreduce(residual, x, w, bias if self.rank == 0 else None, self.bases, self.epoch,
+                                    self._own, self.rank, self.world, self.capacity, plan[0], plan[2], plan[1],
+                                    ops.error_word(x.device))
+        return residual
+
     def reduce_into(self, partial: torch.Tensor, residual: torch.Tensor) -> torch.Tensor:
         """residual += sum of every rank's ``partial`` (a ``partial_buffer``),
         in place."""

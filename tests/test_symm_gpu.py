@@ -44,7 +44,7 @@ def _collectives(rank, world, port, q):
         from minisgl import ops
         from minisgl.parallel.symm import SymmMemImpl
 
-        impl = SymmMemImpl(dev, 8 << 20)
+        impl = SymmMemImpl(dev, 16 << 20)
         g = torch.Generator(device=dev).manual_seed(rank + 1)
         for n in (8, 8192, 262144):
             x = torch.randn(n, device=dev, generator=g).to(torch.bfloat16)
@@ -75,6 +75,24 @@ def _collectives(rank, world, port, q):
             dist.all_gather_into_tensor(ref, x)
             if not torch.equal(out, ref):
                 msgs.append(f"all_gather {dt}")
+        # GEMM with the all-reduce fused (small M: one kernel) and the
+        # fallback (large M: GEMM into the heap + collective kernel)
+        for M in (16, 256, 4096):
+            K, N = 512, 1024
+            x = torch.randn(M, K, device=dev, generator=g).to(torch.bfloat16)
+            w = (torch.randn(N, K, device=dev, generator=g) * 0.05).to(torch.bfloat16)
+            shared = torch.Generator(device=dev).manual_seed(1000 + M)  # the residual stream is replicated
+            res = torch.randn(M, N, device=dev, generator=shared).to(torch.bfloat16)
+            part = (x.float() @ w.float().t()).to(torch.bfloat16).float()
+            dist.all_reduce(part)
+            expect = part.to(torch.bfloat16).float() + res.float()
+            got = impl.gemm_reduce_into(x, w, None, res.clone())
+            if not _close(got, expect, 3e-2):
+                msgs.append(f"gemm_reduce_into M={M}")
+            outs = [torch.empty_like(got) for _ in range(world)]
+            dist.all_gather(outs, got)
+            if not all(torch.equal(o, outs[0]) for o in outs):
+                msgs.append(f"gemm_reduce_into ranks differ M={M}")
         # CUDA graph: the device epoch advances on every replay
         buf = torch.zeros(4096, device=dev, dtype=torch.bfloat16)
         stream = torch.cuda.Stream(dev)
