@@ -9,11 +9,13 @@ residual add fused, and an all-gather; both synchronise through flags in the
 heaps with bounded waits. No NCCL call and no NVLS multicast object is used
 on this path.
 
-The row-parallel projections (o_proj, down_proj) run one kernel each
-(``gemm_reduce_into``): every output tile is computed, written into this
-rank's heap, exchanged with the same tile of the other ranks over NVLink and
-summed with the residual in the GEMM's epilogue, tile by tile, so the
-transfer of one tile overlaps the math of the others.
+The row-parallel projections (o_proj, down_proj) go through
+``gemm_reduce_into``. For a few rows it is one kernel: every output tile is
+computed, written into this rank's heap, exchanged with the same tile of the
+other ranks over NVLink and summed with the residual in the GEMM's epilogue,
+tile by tile, so the transfer of one tile overlaps the math of the others.
+For more rows the tuned plain GEMM writes its partial into the heap and one
+NVLink kernel reduces it (faster there: no split-path parking).
 
 The reference's counterpart is the PyNCCL plugin over NCCL symmetric windows
 (python/minisgl/kernel/pynccl.py, src/pynccl.cu:72-188).
@@ -43,6 +45,11 @@ class _DeviceBuffer:
 
 
 class SymmMemImpl(DistributedImpl):
+    # rows up to which the row-parallel GEMM with the all-reduce in one kernel
+    # is used (Qwen3-32B TP2 on B200: 44.0 vs 47.1 us for NCCL at 1 row of
+    # down_proj; from 64 rows the GEMM + NVLink-kernel pair is faster)
+    ONE_KERNEL_MAX_ROWS = 16
+
     def __init__(self, device: torch.device, capacity_bytes: int, group: Optional[dist.ProcessGroup] = None) -> None:
         self.group = group
         self.rank = dist.get_rank(group)
@@ -100,7 +107,14 @@ class SymmMemImpl(DistributedImpl):
         the GPU at once; otherwise the GEMM writes into the heap and the
         collective kernel reduces. Plans are the tuned fused-epilogue plans,
         which the engine keeps identical on every rank."""
-        plan = ops._gemm_fused_plans.get((x.shape[0], w.shape[0], x.shape[1]), (0, 0, 0))
+        M = x.shape[0]
+        if M > self.ONE_KERNEL_MAX_ROWS:
+            # measured faster beyond a few rows: the tuned plain GEMM (no cluster
+            # parking) into the heap, then the NVLink all-reduce kernel
+            part = self.partial_buffer(M, w.shape[0])
+            ops.gemm(x, w, bias if self.rank == 0 else None, out=part)
+            return self.reduce_into(part, residual)
+        plan = ops._gemm_fused_plans.get((M, w.shape[0], x.shape[1]), (0, 0, 0))
         ops._count(2)
         ops.native().gemm_allreduce(residual, x, w, bias if self.rank == 0 else None, self.bases, self.epoch,
                                     self._own, self.rank, self.world, self.capacity, plan[0], plan[2], plan[1],
