@@ -30,7 +30,7 @@ import torch
 from minisgl.parallel import get_tp_info
 from minisgl.utils import cached_load_hf_config, div_ceil, download_hf_weight
 
-_SPLIT_ROWS = (".q_proj", ".k_proj", ".v_proj", ".gate_proj", ".up_proj")
+_SPLIT_ROWS = (".q_proj", ".k_proj", ".v_proj", ".gate_proj", ".up_proj", ".q_b_proj", ".kv_b_proj")
 _SPLIT_COLS = (".o_proj", ".down_proj")
 _MERGE = {
     ".q_proj": (".qkv_proj", "q", ("q", "k", "v")),

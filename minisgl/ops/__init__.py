@@ -294,6 +294,65 @@ def decode_attention(
     return out
 
 
+def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, kv_b: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
+                page_size: int) -> torch.Tensor:
+    """MLA before attention: the normalised, rotated latent rows go into the
+    cache and the queries are absorbed into the latent space (see
+    ``reference.mla_prepare``)."""
+    if not q.is_cuda:
+        return ref.mla_prepare(q, kv_a, kv_b, norm_w, eps, positions, cos_sin, latent, out_loc, page_size)
+    nat = native()
+    if not hasattr(nat, "mla_prepare"):
+        raise RuntimeError("minisgl: the sm_100a MLA kernels are not part of this build")
+    T, H, _ = q.shape
+    out = torch.empty(T, H, kv_b.shape[2] + kv_a.shape[1] - kv_b.shape[2], dtype=q.dtype, device=q.device)
+    _count(3)
+    nat.mla_prepare(out, q, kv_a, kv_b, norm_w, eps, positions, cos_sin, latent, out_loc, page_size,
+                    error_word(q.device))
+    return out
+
+
+def mla_output(o_lat: torch.Tensor, kv_b: torch.Tensor, nope: int) -> torch.Tensor:
+    """[T, H, kv_lora] latent attention output -> [T, H * v] through W_UV."""
+    if not o_lat.is_cuda:
+        return ref.mla_output(o_lat, kv_b, nope)
+    nat = native()
+    if not hasattr(nat, "mla_output"):
+        raise RuntimeError("minisgl: the sm_100a MLA kernels are not part of this build")
+    T, H, _ = o_lat.shape
+    out = torch.empty(T, H * (kv_b.shape[1] - nope), dtype=o_lat.dtype, device=o_lat.device)
+    _count(2)
+    nat.mla_output(out, o_lat, kv_b, nope, error_word(o_lat.device))
+    return out
+
+
+def mla_attention(
+    q: torch.Tensor,
+    latent: torch.Tensor,
+    page_table: torch.Tensor,
+    req_rows: torch.Tensor,
+    seq_lens: torch.Tensor,
+    cu_q: torch.Tensor,
+    max_q: int,
+    kv_lora: int,
+    page_size: int,
+    scale: float,
+) -> torch.Tensor:
+    """Causal absorbed MLA over the paged latent cache of one layer: q [T, H,
+    kv_lora + rope] -> [T, H, kv_lora] (decode: one query per request)."""
+    if not q.is_cuda:
+        return ref.mla_attention(q, latent, page_table, req_rows, seq_lens, cu_q, kv_lora, page_size, scale)
+    nat = native()
+    if not hasattr(nat, "mla_attention"):
+        raise RuntimeError("minisgl: the sm_100a MLA attention kernel is not part of this build")
+    out = torch.empty(q.shape[0], q.shape[1], kv_lora, dtype=q.dtype, device=q.device)
+    _count()
+    nat.mla_attention(out, q, latent, page_table, req_rows, seq_lens, cu_q, max_q, kv_lora, page_size, scale,
+                      error_word(q.device))
+    return out
+
+
 def prefill_attention(
     q: torch.Tensor,
     kv_pool: torch.Tensor,

@@ -182,6 +182,81 @@ def attention(
     return out
 
 
+def rope_interleaved(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+    """DeepSeek (GPT-J) rotary embedding: pairs (2i, 2i + 1) rotate by
+    frequency i. x [T, ..., d]; cos_sin [max_pos, d] = d/2 cos then d/2 sin."""
+    d = x.shape[-1]
+    cs = cos_sin[positions.long()].float()
+    shape = (x.shape[0],) + (1,) * (x.dim() - 2) + (d // 2,)
+    c, s = cs[:, : d // 2].reshape(shape), cs[:, d // 2 :].reshape(shape)
+    xf = x.float()
+    even, odd = xf[..., 0::2], xf[..., 1::2]
+    out = torch.empty_like(xf)
+    out[..., 0::2] = even * c - odd * s
+    out[..., 1::2] = odd * c + even * s
+    return out.to(x.dtype)
+
+
+def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, kv_b: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
+                page_size: int) -> torch.Tensor:
+    """Latent row [rmsnorm(c_kv) | rope(k_pe)] of every token into the paged
+    cache; returns the absorbed queries [T, H, kv_lora + rope] = [q_nope
+    W_UK | rope(q_pe)], W_UK = kv_b[:, :nope, :]."""
+    T, H, qk = q.shape
+    kv_lora = kv_b.shape[2]
+    rope = kv_a.shape[1] - kv_lora
+    nope = qk - rope
+    c = rmsnorm(kv_a[:, :kv_lora], norm_w, eps)
+    k_pe = rope_interleaved(kv_a[:, kv_lora:], positions, cos_sin)
+    loc = out_loc.long()
+    latent[loc // page_size, loc % page_size] = torch.cat([c, k_pe], dim=-1).to(latent.dtype)
+    q_pe = rope_interleaved(q[..., nope:], positions, cos_sin)
+    q_lat = torch.einsum("thn,hnc->thc", q[..., :nope].float(), kv_b[:, :nope, :].float()).to(q.dtype)
+    return torch.cat([q_lat, q_pe], dim=-1)
+
+
+def mla_output(o_lat: torch.Tensor, kv_b: torch.Tensor, nope: int) -> torch.Tensor:
+    """Latent attention output back to heads: [T, H, kv_lora] x W_UV
+    (kv_b[:, nope:, :]) -> [T, H * v]."""
+    o = torch.einsum("thc,hvc->thv", o_lat.float(), kv_b[:, nope:, :].float())
+    return o.reshape(o.shape[0], -1).to(o_lat.dtype)
+
+
+def mla_attention(
+    q: torch.Tensor,  # [T, H, kv_lora + rope]: absorbed queries
+    latent: torch.Tensor,  # [pages, page_size, kv_lora + rope] of one layer
+    page_table: torch.Tensor,
+    req_rows: torch.Tensor,
+    seq_lens: torch.Tensor,
+    cu_q: torch.Tensor,
+    kv_lora: int,
+    page_size: int,
+    scale: float,
+) -> torch.Tensor:
+    """Causal absorbed multi-head latent attention over the paged latent
+    cache: scores = q . [c_kv | k_pe], output = softmax(scores) @ c_kv
+    ([T, H, kv_lora], fp32 math, input dtype out)."""
+    T, H, D = q.shape
+    out = torch.zeros(T, H, kv_lora, dtype=q.dtype, device=q.device)
+    rows, lens, cu = req_rows.tolist(), seq_lens.tolist(), cu_q.tolist()
+    for b, (row, L) in enumerate(zip(rows, lens)):
+        s, e = cu[b], cu[b + 1]
+        n = e - s
+        if n == 0 or L <= 0:
+            continue
+        slots = page_table[row, :L].long()
+        kv = latent.reshape(-1, D)[slots].float()  # [L, D]
+        qb = q[s:e].float()  # [n, H, D]
+        scores = torch.einsum("nhd,ld->hnl", qb, kv) * scale
+        qpos = torch.arange(L - n, L, device=q.device)
+        mask = torch.arange(L, device=q.device)[None, :] > qpos[:, None]
+        scores = scores.masked_fill(mask[None], float("-inf"))
+        p = torch.softmax(scores, dim=-1)
+        out[s:e] = torch.einsum("hnl,lc->nhc", p, kv[:, :kv_lora]).to(q.dtype)
+    return out
+
+
 def argmax(logits: torch.Tensor) -> torch.Tensor:
     return torch.argmax(logits.float(), dim=-1).to(torch.int32)
 

@@ -16,7 +16,13 @@ from typing import Any
 def load_tokenizer(model_path: str):
     from transformers import AutoTokenizer
 
-    tok = AutoTokenizer.from_pretrained(model_path)
+    try:
+        tok = AutoTokenizer.from_pretrained(model_path)
+    except (ValueError, AttributeError, KeyError):
+        # an unknown model type in config.json: the fast tokenizer file alone
+        from transformers import PreTrainedTokenizerFast
+
+        tok = PreTrainedTokenizerFast.from_pretrained(model_path)
     if not getattr(tok, "chat_template", None):
         # some checkpoints (e.g. Mistral) keep the template in its own file
         path = os.path.join(model_path, "chat_template.json")
@@ -37,7 +43,27 @@ def load_tokenizer(model_path: str):
 def _load_config(model_path: str) -> Any:
     from transformers import AutoConfig
 
-    return AutoConfig.from_pretrained(model_path)
+    try:
+        return AutoConfig.from_pretrained(model_path)
+    except ValueError:
+        # model types transformers ships no class for (e.g. kimi_k2, whose
+        # checkpoints rely on remote code): the fields of config.json as is
+        path = os.path.join(model_path, "config.json")
+        if not os.path.isfile(path):
+            raise
+        with open(path, encoding="utf-8") as f:
+            return PlainConfig(**json.load(f))
+
+
+class PlainConfig:
+    """config.json fields as attributes (for model types without a
+    transformers config class)."""
+
+    def __init__(self, **fields: Any) -> None:
+        self.__dict__.update(fields)
+
+    def to_dict(self) -> dict:
+        return dict(self.__dict__)
 
 
 def cached_load_hf_config(model_path: str):
