@@ -1,10 +1,10 @@
 """Attention backend for multi-head latent attention (DeepSeek-V3 / Kimi-K2).
 
-The model hands over absorbed queries (q_nope multiplied into the latent
-space by W_UK, followed by the rotated q_pe), [T, heads, kv_lora + rope];
-the backend attends over the paged latent cache (every head reads the same
-latent rows) and returns the latent output [T, heads, kv_lora], which the
-model maps back to heads with W_UV. Metadata per batch is the GQA backend's:
+The model hands over absorbed queries: q_nope multiplied into the latent
+space by W_UK, head-major [heads, T_pad, kv_lora], and the rotated q_pe
+[T, heads, rope]. The backend attends over the paged latent cache (every
+head reads the same latent rows) and returns the latent output, head-major
+[heads, T_pad, kv_lora], which the model maps back to heads with W_UV. Metadata per batch is the GQA backend's:
 each request's page-table row, key count and query offset, in one pinned
 upload. The reference has no MLA (no DeepSeek-V3 architecture).
 """
@@ -67,10 +67,15 @@ class MLAAttnBackend(BaseAttnBackend):
         self.capture: Optional[Dict[str, torch.Tensor]] = None
 
     def forward(self, q: torch.Tensor, layer_id: int, batch: Batch) -> torch.Tensor:
+        raise TypeError("the MLA backend takes (q_lat, q_pe): call forward_mla")
+
+    def forward_mla(self, q_lat: torch.Tensor, q_pe: torch.Tensor, layer_id: int, batch: Batch) -> torch.Tensor:
+        """q_lat [H, T_pad, kv_lora] head-major, q_pe [T, H, rope] ->
+        latent output [H, T_pad, kv_lora]."""
         md = batch.attn_metadata
         assert isinstance(md, MLAAttnMetadata)
-        return ops.mla_attention(q, self.kv.latent(layer_id), get_global_ctx().page_table, md.req_rows, md.seq_lens,
-                                 md.cu_q, md.max_q, self.kv_lora, self.page_size, self.scale)
+        return ops.mla_attention(q_lat, q_pe, self.kv.latent(layer_id), get_global_ctx().page_table, md.req_rows,
+                                 md.seq_lens, md.cu_q, self.page_size, self.scale)
 
     def prepare_metadata(self, batch: Batch) -> None:
         reqs = batch.padded_reqs

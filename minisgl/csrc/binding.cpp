@@ -343,6 +343,153 @@ void moe_experts(at::Tensor out, const at::Tensor& x, const at::Tensor& w1, cons
                               static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
 }
 
+// ---------------------------------------------------------------- MLA ----
+// Grouped GEMM over G uniform groups: out[g] = x[g] @ w[g]^T with x rows of
+// group g at [g * rows_pad, + rows_pad) and w [G, N, K]; the tile tables map
+// each token tile to its group (weight-major tiles of `tile` rows).
+void grouped_gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w, int64_t tile,
+                  const at::Tensor& tile_expert, const at::Tensor& tile_row, const at::Tensor& num_tiles,
+                  const c10::optional<at::Tensor>& err) {
+  check_cuda(x, "x");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16 && out.scalar_type() == at::kBFloat16,
+            "grouped_gemm: bf16 tensors");
+  MSG_CHECK(x.dim() == 2 && out.dim() == 2 && w.dim() == 3 && x.is_contiguous() && w.is_contiguous() &&
+                out.is_contiguous() && w.size(2) == x.size(1) && out.size(0) == x.size(0) && out.size(1) == w.size(1),
+            "grouped_gemm: x [R, K], w [G, N, K], out [R, N] contiguous");
+  MSG_CHECK(tile == 16 || tile == 32 || tile == 64 || tile == 128, "grouped_gemm: tile of 16, 32, 64 or 128");
+  check_i32(tile_expert, "tile_expert");
+  check_i32(tile_row, "tile_row");
+  check_i32(num_tiles, "num_tiles");
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::GemmArgs a{};
+  a.x = x.data_ptr();
+  a.w = w.data_ptr();
+  a.out = out.data_ptr();
+  a.M = static_cast<int>(x.size(0));
+  a.N = static_cast<int>(w.size(1));
+  a.K = static_cast<int>(w.size(2));
+  a.ldx = a.K;
+  a.ldw = a.K;
+  a.ldo = a.N;
+  a.force_mode = 2;
+  a.force_bn = static_cast<int>(tile);
+  a.force_splits = 1;
+  a.err = err_ptr(err);
+  a.g_tile_expert = tile_expert.data_ptr<int32_t>();
+  a.g_tile_row = tile_row.data_ptr<int32_t>();
+  a.g_num_tiles = num_tiles.data_ptr<int32_t>();
+  a.g_experts = static_cast<int>(w.size(0));
+  minisgl::launch_gemm(a, stream_of(x));
+}
+
+void mla_prepare(at::Tensor q_pe, at::Tensor xs, const at::Tensor& q, const at::Tensor& kv_a, const at::Tensor& norm_w,
+                 double eps, const at::Tensor& positions, const at::Tensor& cos_sin, at::Tensor latent,
+                 const at::Tensor& out_loc, int64_t T_pad, const c10::optional<at::Tensor>& err) {
+  check_cuda(q, "q");
+  MSG_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2) && q.scalar_type() == at::kBFloat16,
+            "mla_prepare: q [T, H, nope + rope] bf16 with packed heads");
+  const int64_t T = q.size(0), H = q.size(1);
+  MSG_CHECK(kv_a.dim() == 2 && kv_a.stride(1) == 1 && kv_a.size(0) == T && kv_a.scalar_type() == at::kBFloat16,
+            "mla_prepare: kv_a [T, kv_lora + rope] bf16");
+  MSG_CHECK(latent.dim() == 3 && latent.is_contiguous() && latent.size(2) == kv_a.size(1) &&
+                latent.scalar_type() == at::kBFloat16,
+            "mla_prepare: latent [pages, page, kv_lora + rope] bf16 contiguous");
+  const int64_t rope = q_pe.size(2), kv_lora = kv_a.size(1) - rope, nope = q.size(2) - rope;
+  MSG_CHECK(q_pe.is_contiguous() && q_pe.size(0) == T && q_pe.size(1) == H, "mla_prepare: q_pe [T, H, rope]");
+  MSG_CHECK(xs.is_contiguous() && xs.numel() >= H * T_pad * nope && T_pad >= T, "mla_prepare: xs [H, T_pad, nope]");
+  MSG_CHECK(norm_w.numel() == kv_lora && norm_w.scalar_type() == at::kBFloat16, "mla_prepare: bf16 norm weight");
+  MSG_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == rope,
+            "mla_prepare: fp32 cos_sin [max_pos, rope]");
+  check_i32(positions, "positions");
+  check_i32(out_loc, "out_loc");
+  MSG_CHECK(positions.numel() >= T && out_loc.numel() >= T, "mla_prepare: positions / out_loc of T tokens");
+  const c10::cuda::CUDAGuard guard(q.device());
+  minisgl::MlaPrepareArgs a{};
+  a.q = q.data_ptr();
+  a.ld_q = static_cast<int>(q.stride(0));
+  a.kv_a = kv_a.data_ptr();
+  a.ld_kv_a = static_cast<int>(kv_a.stride(0));
+  a.norm_w = norm_w.data_ptr();
+  a.eps = static_cast<float>(eps);
+  a.positions = positions.data_ptr<int32_t>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.latent = latent.data_ptr();
+  a.out_loc = out_loc.data_ptr<int32_t>();
+  a.q_pe = q_pe.data_ptr();
+  a.xs = xs.data_ptr();
+  a.T = static_cast<int>(T);
+  a.T_pad = static_cast<int>(T_pad);
+  a.H = static_cast<int>(H);
+  a.nope = static_cast<int>(nope);
+  a.kv_lora = static_cast<int>(kv_lora);
+  a.rope = static_cast<int>(rope);
+  a.err = err_ptr(err);
+  minisgl::launch_mla_prepare(a, stream_of(q));
+}
+
+void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& latent,
+                   const at::Tensor& page_table, const at::Tensor& req_rows, const at::Tensor& seq_lens,
+                   const at::Tensor& cu_q, int64_t page_size, double scale, int64_t splits,
+                   const c10::optional<at::Tensor>& part_o, const c10::optional<at::Tensor>& part_lse,
+                   const c10::optional<at::Tensor>& err) {
+  check_cuda(q_lat, "q_lat");
+  MSG_CHECK(q_lat.dim() == 3 && q_lat.is_contiguous() && q_lat.scalar_type() == at::kBFloat16,
+            "mla_attention: q_lat [H, T_pad, kv_lora] bf16 contiguous");
+  MSG_CHECK(q_pe.dim() == 3 && q_pe.is_contiguous() && q_pe.scalar_type() == at::kBFloat16,
+            "mla_attention: q_pe [T, H, rope] bf16 contiguous");
+  const int64_t H = q_lat.size(0), T_pad = q_lat.size(1), T = q_pe.size(0);
+  MSG_CHECK(q_pe.size(1) == H && out.sizes() == q_lat.sizes() && out.scalar_type() == at::kBFloat16 &&
+                out.is_contiguous(),
+            "mla_attention: out like q_lat");
+  MSG_CHECK(latent.dim() == 3 && latent.is_contiguous() && latent.size(1) == page_size &&
+                latent.size(2) == q_lat.size(2) + q_pe.size(2),
+            "mla_attention: latent [pages, page_size, kv_lora + rope] contiguous");
+  check_i32(req_rows, "req_rows");
+  check_i32(seq_lens, "seq_lens");
+  check_i32(cu_q, "cu_q");
+  MSG_CHECK(page_table.scalar_type() == at::kInt && page_table.dim() == 2 && page_table.stride(1) == 1,
+            "mla_attention: int32 page table");
+  const c10::cuda::CUDAGuard guard(q_lat.device());
+  minisgl::MlaAttnArgs a{};
+  a.q_lat = q_lat.data_ptr();
+  a.q_pe = q_pe.data_ptr();
+  a.latent = latent.data_ptr();
+  a.num_slots = latent.size(0) * latent.size(1);
+  a.page_table = page_table.data_ptr<int32_t>();
+  a.ld_pt = static_cast<int>(page_table.stride(0));
+  a.req_rows = req_rows.data_ptr<int32_t>();
+  a.seq_lens = seq_lens.data_ptr<int32_t>();
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.out = out.data_ptr();
+  a.B = static_cast<int>(req_rows.numel());
+  a.T = static_cast<int>(T);
+  a.T_pad = static_cast<int>(T_pad);
+  a.H = static_cast<int>(H);
+  a.page_size = static_cast<int>(page_size);
+  a.splits = static_cast<int>(splits);
+  a.scale = static_cast<float>(scale);
+  if (splits > 1) {
+    MSG_CHECK(part_o.has_value() && part_lse.has_value() && part_o->scalar_type() == at::kFloat &&
+                  part_lse->scalar_type() == at::kFloat && part_o->numel() >= splits * T * H * q_lat.size(2) &&
+                  part_lse->numel() >= splits * T * H,
+              "mla_attention: fp32 split-KV scratch too small");
+    a.part_o = part_o->data_ptr<float>();
+    a.part_lse = part_lse->data_ptr<float>();
+  }
+  a.err = err_ptr(err);
+  minisgl::launch_mla_attention(a, stream_of(q_lat));
+}
+
+void mla_heads_to_rows(at::Tensor out, const at::Tensor& in, int64_t T) {
+  check_cuda(in, "in");
+  MSG_CHECK(in.dim() == 3 && in.is_contiguous() && in.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
+                out.scalar_type() == at::kBFloat16 && out.numel() == T * in.size(0) * in.size(2) && in.size(1) >= T,
+            "mla_heads_to_rows: in [H, T_pad, v] -> out [T, H * v] bf16");
+  const c10::cuda::CUDAGuard guard(in.device());
+  minisgl::launch_mla_heads_to_rows(out.data_ptr(), in.data_ptr(), static_cast<int>(T), static_cast<int>(in.size(1)),
+                                    static_cast<int>(in.size(0)), static_cast<int>(in.size(2)), stream_of(in));
+}
+
 // ------------------------------------------------- symmetric heap (IPC) ----
 // Allocate a heap of `bytes` on the current device with zeroed signal slots;
 // returns (device address, CUDA IPC handle bytes) for the other ranks.
@@ -741,6 +888,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_fused", &gemm_fused);
   m.def("gemm_sample", &gemm_sample);
   m.def("moe_experts", &moe_experts);
+  m.def("grouped_gemm", &grouped_gemm);
+  m.def("mla_prepare", &mla_prepare);
+  m.def("mla_attention", &mla_attention);
+  m.def("mla_heads_to_rows", &mla_heads_to_rows);
+  m.def("mla_num_splits", [](int64_t T, int64_t H) { return minisgl::mla_num_splits(static_cast<int>(T), static_cast<int>(H)); });
   m.def("symm_create", &symm_create);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);

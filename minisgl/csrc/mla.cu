@@ -1,0 +1,519 @@
+// Multi-head latent attention (DeepSeek-V3 / Kimi-K2) for sm_100a.
+//
+// The reference has no MLA (its attention backends are MHA/GQA only:
+// python/minisgl/attention/fi.py, trtllm.py). Layout of the absorbed form:
+//
+//   latent cache   [slots, 576] bf16: rmsnorm(c_kv) (512) | rope(k_pe) (64)
+//   q_lat          [H, T_pad, 512]: q_nope absorbed through W_UK (a grouped
+//                  GEMM with heads as groups, written head-major so each
+//                  head's tokens are contiguous rows of the GEMM)
+//   q_pe           [T, H, 64]: rotated positional part of the queries
+//   o_lat          [H, T_pad, 512]: attention output in the latent space,
+//                  head-major again so W_UV is another grouped GEMM
+//
+// mla_attn_kernel is a tcgen05 kernel. One CTA handles one query token, 64
+// heads and a range of 64-key tiles. With M = 64 rows the accumulator fills
+// half of each TMEM lane quadrant (rows 16q..16q+15 in lanes 32q..32q+15), so
+// the 64 x 512 fp32 output is kept whole in TMEM: dims 0-255 in the lower
+// half-quadrants and dims 256-511 in the upper ones (lane offset 16), both
+// in columns 0-255; scores S (64 heads x 64 keys, two buffers) sit in
+// columns 256-383 of the lower halves.
+//
+//   S = Q . K^T   A = Q (K-major, 9 chunks of 64 dims), B = latent tile
+//                 (K-major), M = 64 heads, N = 64 keys, K = 576
+//   O += P . V    A = P (K-major, written by the softmax warps), B = the
+//                 first 512 dims of the same latent tile read MN-major,
+//                 N = 256 per MMA (two MMAs for the two output halves)
+//
+// Warps 0-3 run the softmax (warp q owns heads 16q..16q+15 in lanes 0-15;
+// lanes 16-31 own the upper output half of the same heads), warp 4 issues
+// TMA, warp 5 issues tcgen05.mma. Softmax is in the exp2 domain with a
+// lazy rescale: O and l are only rescaled when a row's running max grows
+// by more than 8 (a factor of 256), which keeps P below 256 in bf16.
+#include <algorithm>
+#include <stdexcept>
+#include <string>
+
+#include "common.cuh"
+#include "launch.h"
+#include "ops.h"
+#include "tma_host.h"
+
+namespace minisgl {
+namespace {
+
+constexpr int kLora = 512;
+constexpr int kRope = 64;
+constexpr int kLat = kLora + kRope;          // 576
+constexpr int kChunks = kLat / 64;           // 9 chunks of 64 dims
+constexpr int kKeys = 64;                    // keys per tile
+constexpr int kHeadsCta = 64;                // heads per CTA (MMA M)
+constexpr int kChunkBytes = 64 * 128;        // 64 rows x 128 bytes
+constexpr int kQBytes = kChunks * kChunkBytes;
+constexpr int kKvBytes = kChunks * kChunkBytes;
+constexpr int kPBytes = kChunkBytes;
+constexpr int kStages = 2;
+constexpr int kSCol = 256;                   // first TMEM column of the score buffers
+constexpr int kMlaThreads = 192;
+constexpr int kMlaSmem = 1024 + kQBytes + kStages * kKvBytes + kPBytes + 256;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kRescaleLog2 = 8.f;
+
+// ------------------------------------------------------------ prepare ----
+// One CTA per token: the latent row [rmsnorm(c_kv) * w | rope(k_pe)] into
+// the cache slot, rope(q_pe) into q_pe [T, H, 64] and q_nope into the
+// head-major GEMM input xs [H, T_pad, nope]. Interleaved (GPT-J) rotation:
+// pairs (2i, 2i + 1) turn by frequency i; cos_sin [pos, 64] = 32 cos | 32 sin.
+__global__ void __launch_bounds__(256) mla_prepare_kernel(MlaPrepareArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int tid = threadIdx.x;
+  __shared__ float red[8];
+  const __nv_bfloat16* kva = reinterpret_cast<const __nv_bfloat16*>(a.kv_a) + static_cast<int64_t>(t) * a.ld_kv_a;
+  // rmsnorm over kv_lora (512): two values per thread
+  float v0 = __bfloat162float(kva[2 * tid]), v1 = __bfloat162float(kva[2 * tid + 1]);
+  float ss = warp_sum(v0 * v0 + v1 * v1);
+  if ((tid & 31) == 0) red[tid >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) tot += red[i];
+  const float rstd = rsqrtf(tot / kLora + a.eps);
+  const int64_t slot = a.out_loc[t];
+  __nv_bfloat16* lat = reinterpret_cast<__nv_bfloat16*>(a.latent) + slot * kLat;
+  const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+  {
+    __nv_bfloat162 o;  // x * rstd * w in fp32, one rounding
+    o.x = __float2bfloat16_rn(v0 * rstd * __bfloat162float(nw[2 * tid]));
+    o.y = __float2bfloat16_rn(v1 * rstd * __bfloat162float(nw[2 * tid + 1]));
+    *reinterpret_cast<__nv_bfloat162*>(lat + 2 * tid) = o;
+  }
+  const float* cs = a.cos_sin + static_cast<int64_t>(a.positions[t]) * kRope;
+  if (tid < kRope / 2) {
+    const float c = cs[tid], s = cs[kRope / 2 + tid];
+    const float x0 = __bfloat162float(kva[kLora + 2 * tid]), x1 = __bfloat162float(kva[kLora + 2 * tid + 1]);
+    __nv_bfloat162 o;
+    o.x = __float2bfloat16_rn(x0 * c - x1 * s);
+    o.y = __float2bfloat16_rn(x1 * c + x0 * s);
+    *reinterpret_cast<__nv_bfloat162*>(lat + kLora + 2 * tid) = o;
+  }
+  // queries: H heads of (nope + 64) values
+  const int qk = a.nope + kRope;
+  const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(t) * a.ld_q;
+  __nv_bfloat16* qpe = reinterpret_cast<__nv_bfloat16*>(a.q_pe) + static_cast<int64_t>(t) * a.H * kRope;
+  __nv_bfloat16* xs = reinterpret_cast<__nv_bfloat16*>(a.xs);
+  const int pairs = a.H * (qk / 2);
+  for (int i = tid; i < pairs; i += blockDim.x) {
+    const int h = i / (qk / 2);
+    const int j = 2 * (i - h * (qk / 2));  // even column inside the head
+    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(q + h * qk + j);
+    if (j < a.nope) {
+      *reinterpret_cast<__nv_bfloat162*>(xs + (static_cast<int64_t>(h) * a.T_pad + t) * a.nope + j) = v;
+    } else {
+      const int r = (j - a.nope) / 2;
+      const float c = cs[r], s = cs[kRope / 2 + r];
+      const float x0 = __bfloat162float(v.x), x1 = __bfloat162float(v.y);
+      __nv_bfloat162 o;
+      o.x = __float2bfloat16_rn(x0 * c - x1 * s);
+      o.y = __float2bfloat16_rn(x1 * c + x0 * s);
+      *reinterpret_cast<__nv_bfloat162*>(qpe + h * kRope + (j - a.nope)) = o;
+    }
+  }
+}
+
+// [H, T_pad, v] (the W_UV grouped GEMM output) -> [T, H * v] rows for o_proj.
+__global__ void __launch_bounds__(128) mla_heads_to_rows_kernel(__nv_bfloat16* out, const __nv_bfloat16* in, int T,
+                                                               int T_pad, int H, int v) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x;
+  const int n8 = H * v / 8;
+  for (int i = threadIdx.x; i < n8; i += blockDim.x) {
+    const int h = (i * 8) / v, c = i * 8 - h * v;
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * H * v + h * v + c) =
+        *reinterpret_cast<const uint4*>(in + (static_cast<int64_t>(h) * T_pad + t) * v + c);
+  }
+}
+
+// ---------------------------------------------------------- attention ----
+__device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
+__device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+
+// The request and causal key count of query token t: the last query token
+// of a request sees all seq_lens[b] keys, the one before it one fewer.
+__device__ __forceinline__ void mla_token(const MlaAttnArgs& a, int t, int& row, int& len) {
+  int lo = 0, hi = a.B - 1;
+  while (lo < hi) {  // largest b with cu_q[b] <= t
+    const int mid = (lo + hi + 1) >> 1;
+    if (a.cu_q[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  row = a.req_rows[lo];
+  len = a.seq_lens[lo] - (a.cu_q[lo + 1] - 1 - t);
+}
+
+// grid (splits, T, head groups of 64); 192 threads.
+__global__ void __launch_bounds__(kMlaThreads, 1)
+    mla_attn_kernel(const __grid_constant__ CUtensorMap tm_qlat, const __grid_constant__ CUtensorMap tm_qpe,
+                    const __grid_constant__ CUtensorMap tm_lat, const MlaAttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + kQBytes;
+  uint8_t* sP = sKV + kStages * kKvBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;       // [2]
+  uint64_t* kv_empty = bars + 3;      // [2]
+  uint64_t* s_full = bars + 5;        // [2]
+  uint64_t* s_free = bars + 7;        // [2]
+  uint64_t* p_full = bars + 9;
+  uint64_t* o_done = bars + 10;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  int* s_abort = reinterpret_cast<int*>(bars + 13);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int split = blockIdx.x, t = blockIdx.y, g = blockIdx.z;
+  pdl_launch_dependents();
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+    }
+    mbar_init(p_full, 4);
+    mbar_init(o_done, 1);
+    *s_abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tm_qlat);
+    prefetch_tmap(&tm_qpe);
+    prefetch_tmap(&tm_lat);
+  }
+  // queries, cache rows and metadata come from earlier kernels; TMEM is
+  // taken only after them, so an earlier kernel still waiting to allocate on
+  // this SM is never blocked by this CTA
+  pdl_wait();
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  int row = 0, len = 0;
+  mla_token(a, t, row, len);
+  const int ntiles_all = (max(len, 0) + kKeys - 1) / kKeys;
+  const int per = (ntiles_all + a.splits - 1) / a.splits;
+  const int tile0 = split * per;
+  const int n = max(0, min(ntiles_all, tile0 + per) - tile0);
+  const ErrorSink err{a.err};
+  int issued = 0;  // latent tiles whose copies the producer started
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA ----
+    if (lane == 0 && n > 0) {
+      mbar_arrive_expect_tx(q_full, kQBytes);
+      for (int c = 0; c < kLora / 64; ++c) tma_load_3d(sQ + c * kChunkBytes, &tm_qlat, q_full, c * 64, t, g * kHeadsCta);
+      tma_load_2d(sQ + (kChunks - 1) * kChunkBytes, &tm_qpe, q_full, 0, t * a.H + g * kHeadsCta);
+      const int32_t* pt = a.page_table + static_cast<int64_t>(row) * a.ld_pt;
+      const int P = a.page_size;
+      const int seg = P < kKeys ? P : kKeys;
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kStages;
+        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, err, 201)) {
+          atomicExch(s_abort, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(s_abort)) break;
+        ++issued;
+        uint8_t* st = sKV + s * kKvBytes;
+        mbar_arrive_expect_tx(&kv_full[s], kKvBytes);
+        const int p0 = (tile0 + j) * kKeys;
+        for (int jj = 0; jj < kKeys; jj += seg) {
+          const int pos = p0 + jj;
+          const int page = pos < len ? pt[pos] / P : 0;  // past the end: page 0, masked in the softmax
+          const int r = page * P + (P < kKeys ? 0 : p0 % P);
+          for (int c = 0; c < kChunks; ++c) tma_load_2d(st + c * kChunkBytes + jj * 128, &tm_lat, &kv_full[s], c * 64, r);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA ----
+    constexpr uint32_t idesc_qk = make_idesc_bf16(64, kKeys);
+    constexpr uint32_t idesc_pv = make_idesc_bf16(64, 256, false, true);
+    const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV), p_addr = smem_u32(sP);
+    bool ok = n > 0 && __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, 202));
+    auto qk = [&](int j) {  // S[j % 2] = Q . K_j^T
+      const uint32_t st = kv_addr + (j % kStages) * kKvBytes;
+      const uint32_t d = tmem + kSCol + (j % 2) * kKeys;
+      for (int c = 0; c < kChunks; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f16(d, make_sdesc_k_sw128(q_addr + c * kChunkBytes + k * 32),
+                     make_sdesc_k_sw128(st + c * kChunkBytes + k * 32), idesc_qk, (c | k) != 0 ? 1u : 0u);
+      tc_commit(&s_full[j % 2]);
+    };
+    if (ok) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&kv_full[0], 0, err, 203));
+      tc_fence_after();
+      if (ok && lane == 0) qk(0);
+      __syncwarp();
+    }
+    for (int i = 0; ok && i < n; ++i) {
+      const int j = i + 1;
+      if (j < n) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, err, 204));
+        if (ok && j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&s_free[j % 2], ((j / 2) - 1) & 1, err, 205));
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) qk(j);
+        __syncwarp();
+      }
+      ok = __all_sync(0xffffffffu, mbar_wait(p_full, i & 1, err, 206));
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        const uint32_t st = kv_addr + (i % kStages) * kKvBytes;
+#pragma unroll
+        for (int kk = 0; kk < kKeys / 16; ++kk) {
+          const uint64_t pa = make_sdesc_k_sw128(p_addr + kk * 32);
+          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+          tc_mma_f16(tmem, pa, make_sdesc_mn_sw128(st + kk * 2048, kChunkBytes), idesc_pv, acc);
+          tc_mma_f16(tmem + (16u << 16), pa, make_sdesc_mn_sw128(st + 4 * kChunkBytes + kk * 2048, kChunkBytes),
+                     idesc_pv, acc);
+        }
+        tc_commit(&kv_empty[i % kStages]);
+        tc_commit(o_done);
+      }
+      __syncwarp();
+    }
+    if (!ok && lane == 0) atomicExch(s_abort, 1);
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------- softmax ----
+    const int r = 16 * warp + (lane & 15);  // head row of this lane (both halves)
+    const bool lower = lane < 16;
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    const float sl2 = a.scale * kLog2e;
+    float m_run = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      const int b = i % 2;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (i / 2) & 1, err, 211));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[64];
+      {
+        uint32_t (&lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
+        uint32_t (&hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
+        tmem_ld_32x32b_x32(lane_base + kSCol + b * kKeys, lo);
+        tmem_ld_32x32b_x32(lane_base + kSCol + b * kKeys + 32, hi);
+      }
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[b]);
+      const int p0 = (tile0 + i) * kKeys;
+      const int valid = min(kKeys, len - p0);
+      float mt = -INFINITY;
+#pragma unroll
+      for (int j = 0; j < 64; ++j) {
+        const float x = j < valid ? u2f(sv[j]) * sl2 : -INFINITY;
+        sv[j] = f2u(x);
+        mt = fmaxf(mt, x);
+      }
+      // lazy rescale: only when the running max grows by more than 2^8
+      const bool grow = lower && mt > m_run + kRescaleLog2;
+      float alpha = 1.f;
+      if (grow) {
+        alpha = exp2f(m_run - mt);  // 0 on the first tile (m_run = -inf)
+        l_sum *= alpha;
+        m_run = mt;
+      }
+      const bool any_grow = __any_sync(0xffffffffu, grow) && i > 0;
+      const float alpha_row = __shfl_sync(0xffffffffu, alpha, lane & 15);
+      if (i > 0) {
+        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (i - 1) & 1, err, 212));
+        if (!ok) break;
+        tc_fence_after();
+      }
+      if (any_grow) {
+        // O rows of this warp: lanes 0-15 the low 256 dims, 16-31 the high
+#pragma unroll 1
+        for (int c = 0; c < 8; ++c) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(lane_base + c * 32, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] = f2u(u2f(ov[j]) * alpha_row);
+          tmem_st_32x32b_x32(lane_base + c * 32, ov);
+        }
+        tc_wait_st();
+      }
+      if (lower) {
+        // P row r (bf16) in the 128-byte-swizzled K-major layout of operand A
+        float ps = 0.f;
+        uint8_t* prow = sP + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint32_t pk[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const __nv_bfloat16 lo = __float2bfloat16_rn(exp2f(u2f(sv[c * 8 + 2 * e]) - m_run));
+            const __nv_bfloat16 hi = __float2bfloat16_rn(exp2f(u2f(sv[c * 8 + 2 * e + 1]) - m_run));
+            ps += __bfloat162float(lo) + __bfloat162float(hi);
+            pk[e] = static_cast<uint32_t>(__bfloat16_as_ushort(lo)) |
+                    (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
+          }
+          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        }
+        l_sum += ps;
+      }
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(p_full);
+    }
+    // ------------------------------------------------------- epilogue ----
+    if (!ok && lane == 0) atomicExch(s_abort, 1);
+    if (ok && n > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n - 1) & 1, err, 213));
+    tc_fence_after();
+    const float l_row = __shfl_sync(0xffffffffu, l_sum, lane & 15);
+    const float m_row = __shfl_sync(0xffffffffu, m_run, lane & 15);
+    const int h = g * kHeadsCta + r;
+    const int half = lower ? 0 : 1;
+    const bool live = ok && n > 0;
+    const float inv = live && l_row > 0.f ? 1.f / l_row : 0.f;
+#pragma unroll 1
+    for (int c = 0; c < 8; ++c) {
+      uint32_t ov[32];
+      if (live) {
+        tmem_ld_32x32b_x32(lane_base + c * 32, ov);
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ov[j] = 0u;
+      }
+      if (h >= a.H) continue;
+      const int d0 = half * 256 + c * 32;
+      if (a.splits == 1) {
+        __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (static_cast<int64_t>(h) * a.T_pad + t) * kLora + d0;
+#pragma unroll
+        for (int q4 = 0; q4 < 4; ++q4) {
+          uint4 v;
+          v.x = pack_bf16x2(u2f(ov[q4 * 8 + 0]) * inv, u2f(ov[q4 * 8 + 1]) * inv);
+          v.y = pack_bf16x2(u2f(ov[q4 * 8 + 2]) * inv, u2f(ov[q4 * 8 + 3]) * inv);
+          v.z = pack_bf16x2(u2f(ov[q4 * 8 + 4]) * inv, u2f(ov[q4 * 8 + 5]) * inv);
+          v.w = pack_bf16x2(u2f(ov[q4 * 8 + 6]) * inv, u2f(ov[q4 * 8 + 7]) * inv);
+          *reinterpret_cast<uint4*>(dst + q4 * 8) = v;
+        }
+      } else {
+        float* dst = a.part_o + ((static_cast<int64_t>(split) * a.T + t) * a.H + h) * kLora + d0;
+#pragma unroll
+        for (int q4 = 0; q4 < 8; ++q4)
+          *reinterpret_cast<float4*>(dst + q4 * 4) = make_float4(u2f(ov[q4 * 4]) * inv, u2f(ov[q4 * 4 + 1]) * inv,
+                                                                 u2f(ov[q4 * 4 + 2]) * inv, u2f(ov[q4 * 4 + 3]) * inv);
+      }
+    }
+    if (a.splits > 1 && lower && h < a.H)
+      a.part_lse[(static_cast<int64_t>(split) * a.T + t) * a.H + h] = live && l_row > 0.f ? m_row + log2f(l_row) : -INFINITY;
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4 && lane == 0 && n > 0 && *reinterpret_cast<volatile int*>(s_abort)) {
+    // after an abort, let the copies still in flight land before the CTA
+    // leaves (bounded waits; the normal path never gets here)
+    mbar_wait(q_full, 0, err, 207);
+    for (int j = max(0, issued - kStages); j < issued; ++j)
+      mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, err, 208);
+  }
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
+// Merge the split-KV partials: grid (T, H), 128 threads x 4 dims.
+__global__ void __launch_bounds__(128) mla_combine_kernel(MlaAttnArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int t = blockIdx.x, h = blockIdx.y;
+  float mx = -INFINITY;
+  for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, a.part_lse[(static_cast<int64_t>(s) * a.T + t) * a.H + h]);
+  float acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float wsum = 0.f;
+  for (int s = 0; s < a.splits; ++s) {
+    const float lse = a.part_lse[(static_cast<int64_t>(s) * a.T + t) * a.H + h];
+    if (lse == -INFINITY) continue;
+    const float w = exp2f(lse - mx);
+    wsum += w;
+    const float4 v = *reinterpret_cast<const float4*>(a.part_o + ((static_cast<int64_t>(s) * a.T + t) * a.H + h) * kLora +
+                                                      threadIdx.x * 4);
+    acc[0] += w * v.x, acc[1] += w * v.y, acc[2] += w * v.z, acc[3] += w * v.w;
+  }
+  const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (static_cast<int64_t>(h) * a.T_pad + t) * kLora +
+                       threadIdx.x * 4;
+  uint2 o;
+  o.x = pack_bf16x2(acc[0] * inv, acc[1] * inv);
+  o.y = pack_bf16x2(acc[2] * inv, acc[3] * inv);
+  *reinterpret_cast<uint2*>(dst) = o;
+}
+
+}  // namespace
+
+// ---------------------------------------------------------------- host ----
+void launch_mla_prepare(const MlaPrepareArgs& a, cudaStream_t s) {
+  if (a.T <= 0) return;
+  if (a.kv_lora != kLora || a.rope != kRope)
+    throw std::runtime_error("minisgl.mla_prepare: the sm_100a kernels take kv_lora_rank 512 and qk_rope_head_dim 64");
+  if (a.nope % 2 != 0 || a.T_pad < a.T || a.H <= 0)
+    throw std::runtime_error("minisgl.mla_prepare: bad head layout");
+  launch_pdl(mla_prepare_kernel, dim3(a.T), dim3(256), 0, s, a);
+}
+
+void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, cudaStream_t s) {
+  if (T <= 0) return;
+  if ((H * v) % 8 != 0 || v % 8 != 0) throw std::runtime_error("minisgl.mla_output: v must be a multiple of 8");
+  launch_pdl(mla_heads_to_rows_kernel, dim3(T), dim3(128), 0, s, static_cast<__nv_bfloat16*>(out),
+             static_cast<const __nv_bfloat16*>(in), T, T_pad, H, v);
+}
+
+int mla_num_splits(int T, int H) {
+  const int ctas = T * ((H + kHeadsCta - 1) / kHeadsCta);
+  return std::max(1, std::min(16, 148 / std::max(1, ctas)));
+}
+
+void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s) {
+  if (a.T <= 0) return;
+  const int P = a.page_size;
+  if (!(P == 8 || P == 16 || P == 32 || (P > 0 && P % 64 == 0)))
+    throw std::runtime_error("minisgl.mla_attention: page_size must be 8, 16, 32 or a multiple of 64");
+  if (a.splits < 1 || a.splits > 16 || (a.splits > 1 && (a.part_o == nullptr || a.part_lse == nullptr)))
+    throw std::runtime_error("minisgl.mla_attention: splits in [1, 16] with partial buffers");
+  if (a.T_pad < a.T || a.B <= 0 || a.H <= 0) throw std::runtime_error("minisgl.mla_attention: bad shapes");
+  static bool smem_set = false;
+  if (!smem_set) {
+    cudaFuncSetAttribute(mla_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMlaSmem);
+    smem_set = true;
+  }
+  uint64_t qd[3] = {static_cast<uint64_t>(kLora), static_cast<uint64_t>(a.T_pad), static_cast<uint64_t>(a.H)};
+  uint64_t qs[2] = {kLora * 2ull, static_cast<uint64_t>(a.T_pad) * kLora * 2ull};
+  uint32_t qb[3] = {64, 1, kHeadsCta};
+  CUtensorMap tq = make_tmap(a.q_lat, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, qd, qs, qb, CU_TENSOR_MAP_SWIZZLE_128B);
+  CUtensorMap tp = make_tmap_bf16_2d_sw128(a.q_pe, static_cast<uint64_t>(a.T) * a.H, kRope, kRope, kHeadsCta);
+  const int seg = P < kKeys ? P : kKeys;
+  CUtensorMap tl = make_tmap_bf16_2d_sw128(a.latent, static_cast<uint64_t>(a.num_slots), kLat, kLat, seg);
+  dim3 grid(a.splits, a.T, (a.H + kHeadsCta - 1) / kHeadsCta);
+  launch_pdl(mla_attn_kernel, grid, dim3(kMlaThreads), kMlaSmem, s, tq, tp, tl, a);
+  if (a.splits > 1) launch_pdl(mla_combine_kernel, dim3(a.T, a.H), dim3(128), 0, s, a);
+}
+
+}  // namespace minisgl

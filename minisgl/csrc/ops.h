@@ -152,6 +152,45 @@ struct AttnArgs {
 void launch_decode_attention(const AttnArgs& a, cudaStream_t s);
 void launch_prefill_attention(const AttnArgs& a, cudaStream_t s);
 
+// ------------------------------------------------------------------ MLA ----
+struct MlaPrepareArgs {
+  const void* q;          // [T, H, nope + rope] (token stride ld_q)
+  int ld_q;
+  const void* kv_a;       // [T, kv_lora + rope] (token stride ld_kv_a)
+  int ld_kv_a;
+  const void* norm_w;     // [kv_lora] kv_a_layernorm weight
+  float eps;
+  const int32_t* positions;
+  const float* cos_sin;   // [max_pos, rope]: rope / 2 cos then rope / 2 sin
+  void* latent;           // [slots, kv_lora + rope] of this layer
+  const int32_t* out_loc; // [T] cache slots
+  void* q_pe;             // out: [T, H, rope]
+  void* xs;               // out: [H, T_pad, nope] (grouped GEMM input)
+  int T, T_pad, H, nope, kv_lora, rope;
+  int* err;
+};
+struct MlaAttnArgs {
+  const void* q_lat;      // [H, T_pad, kv_lora]
+  const void* q_pe;       // [T, H, rope]
+  const void* latent;     // [num_slots, kv_lora + rope] of this layer
+  int64_t num_slots;
+  const int32_t* page_table;  // [rows, ld_pt] token slots
+  int ld_pt;
+  const int32_t* req_rows;    // [B]
+  const int32_t* seq_lens;    // [B] keys per request
+  const int32_t* cu_q;        // [B + 1] query offsets
+  void* out;                  // [H, T_pad, kv_lora]
+  float* part_o;              // [splits, T, H, kv_lora] (splits > 1)
+  float* part_lse;            // [splits, T, H]
+  int B, T, T_pad, H, page_size, splits;
+  float scale;
+  int* err;
+};
+void launch_mla_prepare(const MlaPrepareArgs& a, cudaStream_t s);
+void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s);
+void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, cudaStream_t s);
+int mla_num_splits(int T, int H);
+
 // -------------------------------------------------------------- sampling ----
 // logits fp32 [B, V] (row stride ld); writes int32 token ids.
 void launch_argmax(int32_t* out, const float* logits, int B, int V, int ld, cudaStream_t s);

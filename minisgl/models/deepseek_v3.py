@@ -78,8 +78,13 @@ class MLAAttention(BaseOP):
         self._layer_id = layer_id
         self._q_lora = config.q_lora_rank > 0
 
-    def _kv_b(self) -> torch.Tensor:
-        return self.kv_b_proj.weight.view(self.heads, self.nope + self.v_dim, self.kv_lora)
+    def post_load(self) -> None:
+        super().post_load()
+        # per-head W_UK^T [H, kv_lora, nope] and W_UV [H, v, kv_lora], each
+        # contiguous: the weights of the two head-grouped GEMMs
+        kv_b = self.kv_b_proj.weight.view(self.heads, self.nope + self.v_dim, self.kv_lora)
+        self._w_uk_t = kv_b[:, : self.nope, :].transpose(1, 2).contiguous()
+        self._w_uv = kv_b[:, self.nope :, :].contiguous()
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         ctx = get_global_ctx()
@@ -90,12 +95,12 @@ class MLAAttention(BaseOP):
         else:
             q = self.q_proj.forward(x)
         kv_a = self.kv_a_proj_with_mqa.forward(x)
-        q_abs = ops.mla_prepare(q.view(T, self.heads, self.nope + self.rope_dim), kv_a, self._kv_b(),
-                                self.kv_a_layernorm.weight, self.eps, batch.positions, self._rotary.cos_sin_cache,
-                                ctx.kv_cache.latent(self._layer_id), batch.out_loc, ctx.page_size)
-        o_lat = ctx.attn_backend.forward(q_abs, self._layer_id, batch)
-        o = ops.mla_output(o_lat, self._kv_b(), self.nope)
-        return self.o_proj.forward(o)
+        q_lat, q_pe = ops.mla_prepare(q.view(T, self.heads, self.nope + self.rope_dim), kv_a, self._w_uk_t,
+                                      self.kv_a_layernorm.weight, self.eps, batch.positions,
+                                      self._rotary.cos_sin_cache, ctx.kv_cache.latent(self._layer_id),
+                                      batch.out_loc, ctx.page_size)
+        o_lat = ctx.attn_backend.forward_mla(q_lat, q_pe, self._layer_id, batch)
+        return self.o_proj.forward(ops.mla_output(o_lat, self._w_uv, T))
 
 
 class DeepseekGate(BaseOP):

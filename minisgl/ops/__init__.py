@@ -294,62 +294,124 @@ def decode_attention(
     return out
 
 
-def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, kv_b: torch.Tensor, norm_w: torch.Tensor, eps: float,
+def _group_tile(T: int) -> int:
+    """Token tile of the head-grouped MLA GEMMs (rows of one head per tile)."""
+    return 16 if T <= 16 else 32 if T <= 32 else 64 if T <= 64 else 128
+
+
+_GROUP_TABLES: dict = {}
+
+
+def _group_tables(groups: int, tiles_per_group: int, tile: int, device: torch.device):
+    """Tile tables of a grouped GEMM whose G groups all have tiles_per_group
+    tiles: tile i belongs to group i // tiles_per_group and starts at row
+    i * tile (group g owns rows [g * T_pad, (g + 1) * T_pad))."""
+    key = (groups, tiles_per_group, tile, device)
+    t = _GROUP_TABLES.get(key)
+    if t is None:
+        n = groups * tiles_per_group
+        idx = torch.arange(n, dtype=torch.int32)
+        t = ((idx // tiles_per_group).to(device), (idx * tile).to(device),
+             torch.tensor([n], dtype=torch.int32).to(device))
+        _GROUP_TABLES[key] = t
+    return t
+
+
+def grouped_gemm(x: torch.Tensor, w: torch.Tensor, tile: int, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out[g] = x[g] @ w[g]^T for G uniform groups: x [G, R, K] (R a multiple
+    of ``tile``), w [G, N, K] -> [G, R, N]; one tcgen05 launch (weight-major
+    tiles, heads or experts as groups)."""
+    G, R, K = x.shape
+    N = w.shape[1]
+    if not x.is_cuda:
+        y = torch.einsum("grk,gnk->grn", x.float(), w.float()).to(x.dtype)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(G, R, N, dtype=x.dtype, device=x.device)
+    te, tr, nt = _group_tables(G, R // tile, tile, x.device)
+    _count()
+    native().grouped_gemm(out.view(G * R, N), x.view(G * R, K), w, tile, te, tr, nt, error_word(x.device))
+    return out
+
+
+def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_w: torch.Tensor, eps: float,
                 positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
-                page_size: int) -> torch.Tensor:
+                page_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """MLA before attention: the normalised, rotated latent rows go into the
-    cache and the queries are absorbed into the latent space (see
-    ``reference.mla_prepare``)."""
+    cache; returns (q_lat [H, T_pad, kv_lora] head-major, q_pe [T, H, rope]).
+    On the GPU one kernel writes the cache row, the rotated q_pe and q_nope
+    head-major, then a grouped GEMM (heads as groups) absorbs q_nope through
+    W_UK; rows past T of q_lat are padding."""
     if not q.is_cuda:
-        return ref.mla_prepare(q, kv_a, kv_b, norm_w, eps, positions, cos_sin, latent, out_loc, page_size)
-    nat = native()
-    if not hasattr(nat, "mla_prepare"):
-        raise RuntimeError("minisgl: the sm_100a MLA kernels are not part of this build")
-    T, H, _ = q.shape
-    out = torch.empty(T, H, kv_b.shape[2] + kv_a.shape[1] - kv_b.shape[2], dtype=q.dtype, device=q.device)
-    _count(3)
-    nat.mla_prepare(out, q, kv_a, kv_b, norm_w, eps, positions, cos_sin, latent, out_loc, page_size,
-                    error_word(q.device))
-    return out
+        return ref.mla_prepare(q, kv_a, w_uk_t, norm_w, eps, positions, cos_sin, latent, out_loc, page_size)
+    T, H, qk = q.shape
+    kv_lora, nope = w_uk_t.shape[1], w_uk_t.shape[2]
+    rope = qk - nope
+    tile = _group_tile(T)
+    T_pad = (T + tile - 1) // tile * tile
+    xs = torch.empty(H, T_pad, nope, dtype=q.dtype, device=q.device)
+    q_pe = torch.empty(T, H, rope, dtype=q.dtype, device=q.device)
+    _count()
+    native().mla_prepare(q_pe, xs, q, kv_a, norm_w, eps, positions, cos_sin, latent, out_loc, T_pad,
+                         error_word(q.device))
+    return grouped_gemm(xs, w_uk_t, tile), q_pe
 
 
-def mla_output(o_lat: torch.Tensor, kv_b: torch.Tensor, nope: int) -> torch.Tensor:
-    """[T, H, kv_lora] latent attention output -> [T, H * v] through W_UV."""
+def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int) -> torch.Tensor:
+    """[H, T_pad, kv_lora] latent attention output -> [T, H * v] through W_UV
+    (a grouped GEMM with heads as groups, then a head-major -> row-major
+    copy for o_proj)."""
     if not o_lat.is_cuda:
-        return ref.mla_output(o_lat, kv_b, nope)
-    nat = native()
-    if not hasattr(nat, "mla_output"):
-        raise RuntimeError("minisgl: the sm_100a MLA kernels are not part of this build")
-    T, H, _ = o_lat.shape
-    out = torch.empty(T, H * (kv_b.shape[1] - nope), dtype=o_lat.dtype, device=o_lat.device)
-    _count(2)
-    nat.mla_output(out, o_lat, kv_b, nope, error_word(o_lat.device))
+        return ref.mla_output(o_lat, w_uv, T)
+    H, T_pad, _ = o_lat.shape
+    ys = grouped_gemm(o_lat, w_uv, _group_tile(T))
+    out = torch.empty(T, H * w_uv.shape[1], dtype=o_lat.dtype, device=o_lat.device)
+    _count()
+    native().mla_heads_to_rows(out, ys, T)
     return out
+
+
+_MLA_SCRATCH: dict = {}
 
 
 def mla_attention(
-    q: torch.Tensor,
+    q_lat: torch.Tensor,
+    q_pe: torch.Tensor,
     latent: torch.Tensor,
     page_table: torch.Tensor,
     req_rows: torch.Tensor,
     seq_lens: torch.Tensor,
     cu_q: torch.Tensor,
-    max_q: int,
-    kv_lora: int,
     page_size: int,
     scale: float,
+    splits: int = 0,
 ) -> torch.Tensor:
-    """Causal absorbed MLA over the paged latent cache of one layer: q [T, H,
-    kv_lora + rope] -> [T, H, kv_lora] (decode: one query per request)."""
-    if not q.is_cuda:
-        return ref.mla_attention(q, latent, page_table, req_rows, seq_lens, cu_q, kv_lora, page_size, scale)
+    """Causal absorbed MLA over the paged latent cache of one layer:
+    q_lat [H, T_pad, kv_lora] + q_pe [T, H, rope] -> [H, T_pad, kv_lora]
+    (one CTA per query token and 64 heads; split-KV when there are few
+    tokens)."""
+    if not q_lat.is_cuda:
+        return ref.mla_attention(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale)
+    H, T_pad, kv_lora = q_lat.shape
+    T = q_pe.shape[0]
     nat = native()
-    if not hasattr(nat, "mla_attention"):
-        raise RuntimeError("minisgl: the sm_100a MLA attention kernel is not part of this build")
-    out = torch.empty(q.shape[0], q.shape[1], kv_lora, dtype=q.dtype, device=q.device)
-    _count()
-    nat.mla_attention(out, q, latent, page_table, req_rows, seq_lens, cu_q, max_q, kv_lora, page_size, scale,
-                      error_word(q.device))
+    splits = splits or nat.mla_num_splits(T, H)
+    out = torch.empty_like(q_lat)
+    part_o = part_lse = None
+    if splits > 1:
+        need = splits * T * H * (kv_lora + 1)
+        buf = _MLA_SCRATCH.get(q_lat.device)
+        if buf is None or buf.numel() < need:
+            buf = torch.empty(max(need, 148 * 64 * (kv_lora + 1)), dtype=torch.float32, device=q_lat.device)
+            _MLA_SCRATCH[q_lat.device] = buf
+        part_o = buf[: splits * T * H * kv_lora]
+        part_lse = buf[splits * T * H * kv_lora: need]
+    _count(2 if splits > 1 else 1)
+    nat.mla_attention(out, q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits,
+                      part_o, part_lse, error_word(q_lat.device))
     return out
 
 

@@ -197,47 +197,51 @@ def rope_interleaved(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
     return out.to(x.dtype)
 
 
-def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, kv_b: torch.Tensor, norm_w: torch.Tensor, eps: float,
+def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_w: torch.Tensor, eps: float,
                 positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
-                page_size: int) -> torch.Tensor:
+                page_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
     """Latent row [rmsnorm(c_kv) | rope(k_pe)] of every token into the paged
-    cache; returns the absorbed queries [T, H, kv_lora + rope] = [q_nope
-    W_UK | rope(q_pe)], W_UK = kv_b[:, :nope, :]."""
+    cache; returns the absorbed queries as (q_lat [H, T, kv_lora] = q_nope
+    W_UK per head, head-major; q_pe [T, H, rope] rotated). w_uk_t is
+    [H, kv_lora, nope] (W_UK of each head, transposed)."""
     T, H, qk = q.shape
-    kv_lora = kv_b.shape[2]
+    kv_lora = w_uk_t.shape[1]
     rope = kv_a.shape[1] - kv_lora
     nope = qk - rope
     c = rmsnorm(kv_a[:, :kv_lora], norm_w, eps)
     k_pe = rope_interleaved(kv_a[:, kv_lora:], positions, cos_sin)
     loc = out_loc.long()
     latent[loc // page_size, loc % page_size] = torch.cat([c, k_pe], dim=-1).to(latent.dtype)
-    q_pe = rope_interleaved(q[..., nope:], positions, cos_sin)
-    q_lat = torch.einsum("thn,hnc->thc", q[..., :nope].float(), kv_b[:, :nope, :].float()).to(q.dtype)
-    return torch.cat([q_lat, q_pe], dim=-1)
+    q_pe = rope_interleaved(q[..., nope:], positions, cos_sin).contiguous()
+    q_lat = torch.einsum("thn,hcn->htc", q[..., :nope].float(), w_uk_t.float()).to(q.dtype)
+    return q_lat, q_pe
 
 
-def mla_output(o_lat: torch.Tensor, kv_b: torch.Tensor, nope: int) -> torch.Tensor:
-    """Latent attention output back to heads: [T, H, kv_lora] x W_UV
-    (kv_b[:, nope:, :]) -> [T, H * v]."""
-    o = torch.einsum("thc,hvc->thv", o_lat.float(), kv_b[:, nope:, :].float())
-    return o.reshape(o.shape[0], -1).to(o_lat.dtype)
+def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int) -> torch.Tensor:
+    """Latent attention output back to heads: o_lat [H, >= T, kv_lora] x
+    W_UV [H, v, kv_lora] -> [T, H * v]."""
+    o = torch.einsum("htc,hvc->thv", o_lat[:, :T].float(), w_uv.float())
+    return o.reshape(T, -1).to(o_lat.dtype)
 
 
 def mla_attention(
-    q: torch.Tensor,  # [T, H, kv_lora + rope]: absorbed queries
+    q_lat: torch.Tensor,  # [H, >= T, kv_lora]: absorbed queries, head-major
+    q_pe: torch.Tensor,  # [T, H, rope]
     latent: torch.Tensor,  # [pages, page_size, kv_lora + rope] of one layer
     page_table: torch.Tensor,
     req_rows: torch.Tensor,
     seq_lens: torch.Tensor,
     cu_q: torch.Tensor,
-    kv_lora: int,
     page_size: int,
     scale: float,
 ) -> torch.Tensor:
     """Causal absorbed multi-head latent attention over the paged latent
-    cache: scores = q . [c_kv | k_pe], output = softmax(scores) @ c_kv
-    ([T, H, kv_lora], fp32 math, input dtype out)."""
-    T, H, D = q.shape
+    cache: scores = [q_lat | q_pe] . [c_kv | k_pe], output = softmax(scores)
+    @ c_kv, returned head-major like q_lat ([H, T, kv_lora], fp32 math)."""
+    T, H, _ = q_pe.shape
+    kv_lora = q_lat.shape[2]
+    q = torch.cat([q_lat[:, :T].transpose(0, 1), q_pe], dim=-1)
+    D = q.shape[-1]
     out = torch.zeros(T, H, kv_lora, dtype=q.dtype, device=q.device)
     rows, lens, cu = req_rows.tolist(), seq_lens.tolist(), cu_q.tolist()
     for b, (row, L) in enumerate(zip(rows, lens)):
@@ -254,7 +258,7 @@ def mla_attention(
         scores = scores.masked_fill(mask[None], float("-inf"))
         p = torch.softmax(scores, dim=-1)
         out[s:e] = torch.einsum("hnl,lc->nhc", p, kv[:, :kv_lora]).to(q.dtype)
-    return out
+    return out.transpose(0, 1).contiguous()
 
 
 def argmax(logits: torch.Tensor) -> torch.Tensor:

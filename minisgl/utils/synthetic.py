@@ -89,6 +89,13 @@ SHAPES["tiny-kimi"] = dict(copy.deepcopy(SHAPES["kimi-k2"]), num_hidden_layers=2
                            q_lora_rank=96, kv_lora_rank=64, qk_nope_head_dim=32, qk_rope_head_dim=16,
                            v_head_dim=32, vocab_size=1024, torch_dtype="float32", max_position_embeddings=4096)
 
+# GPU tests: the Kimi-K2 latent dims (kv_lora 512, rope 64) that the sm_100a
+# MLA kernels take, on a 2-layer model (layer 0 dense, layer 1 MoE)
+SHAPES["small-kimi"] = dict(copy.deepcopy(SHAPES["kimi-k2"]), num_hidden_layers=2, hidden_size=1024,
+                            num_attention_heads=16, num_key_value_heads=16, intermediate_size=2048,
+                            moe_intermediate_size=256, n_routed_experts=8, num_experts_per_tok=2,
+                            q_lora_rank=384, vocab_size=4096, max_position_embeddings=8192)
+
 _CHAT_TEMPLATE = (
     "{% for m in messages %}<|{{ m['role'] }}|>{{ m['content'] }}<|end|>{% endfor %}"
     "{% if add_generation_prompt %}<|assistant|>{% endif %}"

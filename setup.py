@@ -31,6 +31,7 @@ SOURCES = [
     "minisgl/csrc/sampling.cu",
     "minisgl/csrc/moe.cu",
     "minisgl/csrc/symm.cu",
+    "minisgl/csrc/mla.cu",
 ]
 
 
