@@ -107,6 +107,35 @@ def bench_prefill_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) 
             "TFLOP/s": round(tf, 1), "frac_tensor": round(tf / peaks["tflops"], 3)}
 
 
+def bench_mla_decode(B: int, L: int, H: int, page: int, peaks) -> Dict:
+    """Absorbed MLA decode over a paged latent cache (576 bf16 per token).
+    Bytes: every latent row once (head groups of 64 re-read it from L2);
+    FLOPs: 2 * H * L * (576 + 512) per request."""
+    lens = [L] * B
+    pages_per = (L + page - 1) // page
+    num_pages = B * pages_per + 1
+    latent = torch.randn(num_pages, page, 576, device="cuda", dtype=torch.bfloat16) * 0.5
+    perm = torch.randperm(num_pages - 1)
+    pos = torch.arange(pages_per * page)
+    pt = (perm[: B * pages_per].view(B, pages_per)[:, pos // page] * page + pos % page).to(torch.int32).cuda()
+    rows = torch.arange(B, dtype=torch.int32, device="cuda")
+    seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    cu = torch.arange(B + 1, dtype=torch.int32, device="cuda")
+    tile = ops._group_tile(B)
+    T_pad = (B + tile - 1) // tile * tile
+    q_lat = torch.randn(H, T_pad, 512, device="cuda", dtype=torch.bfloat16) * 0.5
+    q_pe = torch.randn(B, H, 64, device="cuda", dtype=torch.bfloat16) * 0.5
+    splits = ops.native().mla_num_splits(B, H)
+    ms = time_kernel(lambda: ops.mla_attention(q_lat, q_pe, latent, pt, rows, seq, cu, page, 192 ** -0.5))
+    nbytes = B * L * 576 * 2
+    flops = 2.0 * B * H * L * (576 + 512)
+    gbs = nbytes / ms / 1e6
+    tf = flops / ms / 1e9
+    return {"kernel": "mla_decode", "B": B, "L": L, "heads": H, "page": page, "splits": splits, "ms": round(ms, 4),
+            "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "TFLOP/s": round(tf, 1),
+            "frac_tensor": round(tf / peaks["tflops"], 3)}
+
+
 def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
     x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
@@ -255,6 +284,10 @@ def main() -> None:
     cases.append(("decode_attention qwen3-32b", lambda: bench_decode_attention(64, 2000, 64, 8, 64, peaks)))
     cases.append(("decode_attention qwen3-32b tp8", lambda: bench_decode_attention(64, 2000, 8, 1, 64, peaks)))
     cases.append(("prefill_attention", lambda: bench_prefill_attention(16, 1024, 16, 8, 64, peaks)))
+    for B, L, Hh in [(256, 1024, 64), (128, 2048, 64), (64, 4096, 64), (8, 4096, 64), (1, 8192, 64), (32, 4096, 16),
+                     (64, 2048, 128)]:
+        cases.append((f"mla_decode B={B} L={L} H={Hh}",
+                      lambda B=B, L=L, Hh=Hh: bench_mla_decode(B, L, Hh, 64, peaks)))
     H, I, V = 1024, 3072, 151936
     for M in (1, 64, 256):
         for lab, N, K in (("qkv", 4096, H), ("o", H, 2048), ("gate_up", 2 * I, H), ("down", H, I)):

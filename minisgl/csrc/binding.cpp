@@ -431,7 +431,7 @@ void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_
                    const at::Tensor& page_table, const at::Tensor& req_rows, const at::Tensor& seq_lens,
                    const at::Tensor& cu_q, int64_t page_size, double scale, int64_t splits,
                    const c10::optional<at::Tensor>& part_o, const c10::optional<at::Tensor>& part_lse,
-                   const c10::optional<at::Tensor>& err) {
+                   const c10::optional<at::Tensor>& err, const c10::optional<at::Tensor>& trace) {
   check_cuda(q_lat, "q_lat");
   MSG_CHECK(q_lat.dim() == 3 && q_lat.is_contiguous() && q_lat.scalar_type() == at::kBFloat16,
             "mla_attention: q_lat [H, T_pad, kv_lora] bf16 contiguous");
@@ -477,6 +477,11 @@ void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_
     a.part_lse = part_lse->data_ptr<float>();
   }
   a.err = err_ptr(err);
+  if (trace.has_value()) {
+    MSG_CHECK(trace->scalar_type() == at::kLong && trace->is_cuda() && trace->numel() >= 64 * 8,
+              "mla_attention: trace must be a CUDA int64 tensor of 512 slots");
+    a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   minisgl::launch_mla_attention(a, stream_of(q_lat));
 }
 
@@ -890,7 +895,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_experts", &moe_experts);
   m.def("grouped_gemm", &grouped_gemm);
   m.def("mla_prepare", &mla_prepare);
-  m.def("mla_attention", &mla_attention);
+  m.def("mla_attention", &mla_attention, py::arg("out"), py::arg("q_lat"), py::arg("q_pe"), py::arg("latent"),
+        py::arg("page_table"), py::arg("req_rows"), py::arg("seq_lens"), py::arg("cu_q"), py::arg("page_size"),
+        py::arg("scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("err"),
+        py::arg("trace") = py::none());
   m.def("mla_heads_to_rows", &mla_heads_to_rows);
   m.def("mla_num_splits", [](int64_t T, int64_t H) { return minisgl::mla_num_splits(static_cast<int>(T), static_cast<int>(H)); });
   m.def("symm_create", &symm_create);

@@ -12,18 +12,20 @@
 //                  head-major again so W_UV is another grouped GEMM
 //
 // mla_attn_kernel is a tcgen05 kernel. One CTA handles one query token, 64
-// heads and a range of 64-key tiles. With M = 64 rows the accumulator fills
-// half of each TMEM lane quadrant (rows 16q..16q+15 in lanes 32q..32q+15), so
-// the 64 x 512 fp32 output is kept whole in TMEM: dims 0-255 in the lower
-// half-quadrants and dims 256-511 in the upper ones (lane offset 16), both
-// in columns 0-255; scores S (64 heads x 64 keys, two buffers) sit in
-// columns 256-383 of the lower halves.
+// heads and a range of 32-key tiles streamed through a 4-stage ring. With
+// M = 64 rows the accumulator fills half of each TMEM lane quadrant (rows
+// 16q..16q+15 in lanes 32q..32q+15), so the 64 x 512 fp32 output is kept
+// whole in TMEM: dims 0-255 in the lower half-quadrants and dims 256-511 in
+// the upper ones (lane offset 16), both in columns 0-255; scores S (64 heads
+// x 32 keys, two buffers) sit in columns 256-319 of the lower halves.
 //
 //   S = Q . K^T   A = Q (K-major, 9 chunks of 64 dims), B = latent tile
-//                 (K-major), M = 64 heads, N = 64 keys, K = 576
-//   O += P . V    A = P (K-major, written by the softmax warps), B = the
-//                 first 512 dims of the same latent tile read MN-major,
-//                 N = 256 per MMA (two MMAs for the two output halves)
+//                 (K-major), M = 64 heads, N = 32 keys, K = 576
+//   O += P . V    A = P (K-major, written by the softmax warps; tile j uses
+//                 keys 32 (j % 2).. of a 64-key buffer, so consecutive
+//                 tiles never share a half), B = the first 512 dims of the
+//                 same latent tile read MN-major, N = 256 per MMA (two MMAs
+//                 for the two output halves)
 //
 // Warps 0-3 run the softmax (warp q owns heads 16q..16q+15 in lanes 0-15;
 // lanes 16-31 own the upper output half of the same heads), warp 4 issues
@@ -46,12 +48,14 @@ constexpr int kLora = 512;
 constexpr int kRope = 64;
 constexpr int kLat = kLora + kRope;          // 576
 constexpr int kChunks = kLat / 64;           // 9 chunks of 64 dims
-constexpr int kKeys = 64;                    // keys per tile
+constexpr int kKeys = 64;                    // keys per tile (N of QK; smaller N runs the tensor pipe at a loss)
 constexpr int kHeadsCta = 64;                // heads per CTA (MMA M)
-constexpr int kChunkBytes = 64 * 128;        // 64 rows x 128 bytes
-constexpr int kQBytes = kChunks * kChunkBytes;
-constexpr int kKvBytes = kChunks * kChunkBytes;
-constexpr int kPBytes = kChunkBytes;
+constexpr int kQChunk = 64 * 128;            // one 64-dim chunk of Q: 64 heads x 128 bytes
+constexpr int kKvChunk = kKeys * 128;        // one 64-dim chunk of a latent tile
+constexpr int kQBytes = kChunks * kQChunk;
+constexpr int kKvBytes = kChunks * kKvChunk;
+constexpr int kPBytes = 64 * 128;            // P: 64 heads x 64 keys
+constexpr int kPHalves = 64 / kKeys;         // tiles whose P the buffer holds at once
 constexpr int kStages = 2;
 constexpr int kSCol = 256;                   // first TMEM column of the score buffers
 constexpr int kMlaThreads = 192;
@@ -139,6 +143,13 @@ __global__ void __launch_bounds__(128) mla_heads_to_rows_kernel(__nv_bfloat16* o
 // ---------------------------------------------------------- attention ----
 __device__ __forceinline__ uint32_t f2u(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ float u2f(uint32_t u) { return __uint_as_float(u); }
+// 2^x on the special-function unit (PTX ex2.approx.ftz: relative error of a
+// few ulp, ex2(-inf) = +0), which is what a softmax needs.
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 // The request and causal key count of query token t: the last query token
 // of a request sees all seq_lens[b] keys, the one before it one fewer.
@@ -165,14 +176,14 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   uint8_t* sP = sKV + kStages * kKvBytes;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sP + kPBytes);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;       // [2]
-  uint64_t* kv_empty = bars + 3;      // [2]
-  uint64_t* s_full = bars + 5;        // [2]
-  uint64_t* s_free = bars + 7;        // [2]
-  uint64_t* p_full = bars + 9;
-  uint64_t* o_done = bars + 10;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
-  int* s_abort = reinterpret_cast<int*>(bars + 13);
+  uint64_t* kv_full = bars + 1;              // [kStages]
+  uint64_t* kv_empty = kv_full + kStages;    // [kStages]
+  uint64_t* s_full = kv_empty + kStages;     // [2] score buffers
+  uint64_t* s_free = s_full + 2;             // [2]
+  uint64_t* p_full = s_free + 2;             // [2] P of tiles with j % 2 == h written
+  uint64_t* o_done = p_full + 2;             // [2] PV of tiles with j % 2 == h complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  int* s_abort = reinterpret_cast<int*>(o_done + 3);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int split = blockIdx.x, t = blockIdx.y, g = blockIdx.z;
@@ -182,11 +193,13 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     for (int i = 0; i < kStages; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
       mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
     }
-    mbar_init(p_full, 4);
-    mbar_init(o_done, 1);
     *s_abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tm_qlat);
@@ -213,33 +226,67 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   const int tile0 = split * per;
   const int n = max(0, min(ntiles_all, tile0 + per) - tile0);
   const ErrorSink err{a.err};
+  const bool traced = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   int issued = 0;  // latent tiles whose copies the producer started
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA ----
-    if (lane == 0 && n > 0) {
-      mbar_arrive_expect_tx(q_full, kQBytes);
-      for (int c = 0; c < kLora / 64; ++c) tma_load_3d(sQ + c * kChunkBytes, &tm_qlat, q_full, c * 64, t, g * kHeadsCta);
-      tma_load_2d(sQ + (kChunks - 1) * kChunkBytes, &tm_qpe, q_full, 0, t * a.H + g * kHeadsCta);
+    // The whole warp walks the loop: lane 0 waits and issues copies, and the
+    // 32 lanes keep the page ids of the next 32 key segments in registers,
+    // read one window ahead, so no copy waits on a page-table load.
+    if (n > 0) {
+      if (lane == 0) {
+        mbar_arrive_expect_tx(q_full, kQBytes);
+        for (int c = 0; c < kLora / 64; ++c)
+          tma_load_3d(sQ + c * kQChunk, &tm_qlat, q_full, c * 64, t, g * kHeadsCta);
+        tma_load_2d(sQ + (kChunks - 1) * kQChunk, &tm_qpe, q_full, 0, t * a.H + g * kHeadsCta);
+      }
       const int32_t* pt = a.page_table + static_cast<int64_t>(row) * a.ld_pt;
       const int P = a.page_size;
       const int seg = P < kKeys ? P : kKeys;
+      const int segs = kKeys / seg;  // segments per tile
+      const int pos0 = tile0 * kKeys;
+      auto page_of = [&](int k) {  // page id of segment k (positions past the end: page 0, masked later)
+        const int pos = pos0 + k * seg;
+        return pos < len ? pt[pos] / P : 0;
+      };
+      int base = 0;
+      int cur = page_of(lane), nxt = page_of(32 + lane);
       for (int j = 0; j < n; ++j) {
         const int s = j % kStages;
-        if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, err, 201)) {
-          atomicExch(s_abort, 1);
-          break;
+        int go = 1;
+        if (lane == 0) {
+          if (j >= kStages && !mbar_wait(&kv_empty[s], ((j / kStages) - 1) & 1, err, 201)) {
+            atomicExch(s_abort, 1);
+            go = 0;
+          }
+          if (*reinterpret_cast<volatile int*>(s_abort)) go = 0;
         }
-        if (*reinterpret_cast<volatile int*>(s_abort)) break;
-        ++issued;
+        if (!__shfl_sync(0xffffffffu, go, 0)) break;
+        if (lane == 0) {
+          ++issued;
+          mbar_arrive_expect_tx(&kv_full[s], kKvBytes);
+          if (traced && j < 64) a.trace[j * 8 + 0] = globaltimer_ns();
+        }
         uint8_t* st = sKV + s * kKvBytes;
-        mbar_arrive_expect_tx(&kv_full[s], kKvBytes);
         const int p0 = (tile0 + j) * kKeys;
-        for (int jj = 0; jj < kKeys; jj += seg) {
-          const int pos = p0 + jj;
-          const int page = pos < len ? pt[pos] / P : 0;  // past the end: page 0, masked in the softmax
-          const int r = page * P + (P < kKeys ? 0 : p0 % P);
-          for (int c = 0; c < kChunks; ++c) tma_load_2d(st + c * kChunkBytes + jj * 128, &tm_lat, &kv_full[s], c * 64, r);
+        for (int q = 0; q < segs; ++q) {
+          const int k = j * segs + q;
+          if (k >= base + 32) {  // slide the window (warp-uniform)
+            base += 32;
+            cur = nxt;
+            nxt = page_of(base + 32 + lane);
+          }
+          const int page = __shfl_sync(0xffffffffu, cur, k - base);
+          if (lane == 0) {
+            const int r = page * P + (P < kKeys ? 0 : p0 % P);
+            if (seg == kKeys) {
+              tma_load_3d(st, &tm_lat, &kv_full[s], 0, r, 0);  // all 9 chunks in one box
+            } else {
+              for (int c = 0; c < kChunks; ++c)
+                tma_load_2d(st + c * kKvChunk + q * seg * 128, &tm_lat, &kv_full[s], c * 64, r);
+            }
+          }
         }
       }
     }
@@ -256,43 +303,66 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       for (int c = 0; c < kChunks; ++c)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc_mma_f16(d, make_sdesc_k_sw128(q_addr + c * kChunkBytes + k * 32),
-                     make_sdesc_k_sw128(st + c * kChunkBytes + k * 32), idesc_qk, (c | k) != 0 ? 1u : 0u);
+          tc_mma_f16(d, make_sdesc_k_sw128(q_addr + c * kQChunk + k * 32),
+                     make_sdesc_k_sw128(st + c * kKvChunk + k * 32), idesc_qk, (c | k) != 0 ? 1u : 0u);
       tc_commit(&s_full[j % 2]);
     };
-    if (ok) {
-      ok = __all_sync(0xffffffffu, mbar_wait(&kv_full[0], 0, err, 203));
-      tc_fence_after();
-      if (ok && lane == 0) qk(0);
-      __syncwarp();
-    }
-    for (int i = 0; ok && i < n; ++i) {
-      const int j = i + 1;
-      if (j < n) {
-        ok = __all_sync(0xffffffffu, mbar_wait(&kv_full[j % kStages], (j / kStages) & 1, err, 204));
-        if (ok && j >= 2) ok = __all_sync(0xffffffffu, mbar_wait(&s_free[j % 2], ((j / 2) - 1) & 1, err, 205));
-        if (!ok) break;
-        tc_fence_after();
-        if (lane == 0) qk(j);
-        __syncwarp();
-      }
-      ok = __all_sync(0xffffffffu, mbar_wait(p_full, i & 1, err, 206));
-      if (!ok) break;
-      tc_fence_after();
-      if (lane == 0) {
-        const uint32_t st = kv_addr + (i % kStages) * kKvBytes;
+    auto pv = [&](int i) {  // O += P_i . V_i (two N = 256 halves)
+      const uint32_t st = kv_addr + (i % kStages) * kKvBytes;
 #pragma unroll
-        for (int kk = 0; kk < kKeys / 16; ++kk) {
-          const uint64_t pa = make_sdesc_k_sw128(p_addr + kk * 32);
-          const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
-          tc_mma_f16(tmem, pa, make_sdesc_mn_sw128(st + kk * 2048, kChunkBytes), idesc_pv, acc);
-          tc_mma_f16(tmem + (16u << 16), pa, make_sdesc_mn_sw128(st + 4 * kChunkBytes + kk * 2048, kChunkBytes),
-                     idesc_pv, acc);
-        }
-        tc_commit(&kv_empty[i % kStages]);
-        tc_commit(o_done);
+      for (int kk = 0; kk < kKeys / 16; ++kk) {
+        const uint64_t pa = make_sdesc_k_sw128(p_addr + ((i % kPHalves) * (kKeys / 16) + kk) * 32);
+        const uint32_t acc = (i > 0 || kk > 0) ? 1u : 0u;
+        tc_mma_f16(tmem, pa, make_sdesc_mn_sw128(st + kk * 2048, kKvChunk), idesc_pv, acc);
+        tc_mma_f16(tmem + (16u << 16), pa, make_sdesc_mn_sw128(st + 4 * kKvChunk + kk * 2048, kKvChunk),
+                   idesc_pv, acc);
       }
-      __syncwarp();
+      tc_commit(&kv_empty[i % kStages]);
+      tc_commit(&o_done[i % 2]);
+    };
+    // Issue QK(j) and PV(i) in whichever order their inputs arrive: QK(j)
+    // needs latent tile j and a free score buffer (the softmax of tile j - 2
+    // has read it), PV(i) needs P_i. Waiting for tile j before PV(i) would
+    // chain every copy's latency into the loop.
+    int qn = 0, pn = 0;  // next QK, next PV
+    uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (ok && pn < n) {
+      // lane 0 polls and decides; the warp follows its choice
+      int choice = 0;
+      if (lane == 0) {
+        if (pn < qn && mbar_try_wait(&p_full[pn % 2], (pn / 2) & 1)) choice = 1;
+        else if (qn < n && qn <= pn + 1 && mbar_try_wait(&kv_full[qn % kStages], (qn / kStages) & 1) &&
+                 (qn < 2 || mbar_try_wait(&s_free[qn % 2], ((qn / 2) - 1) & 1)))
+          choice = 2;
+        else if (((++spins) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs)
+          choice = 3;
+      }
+      choice = __shfl_sync(0xffffffffu, choice, 0);
+      if (choice == 3) {
+        if (lane == 0) err.report(kErrMbarTimeout, 206);
+        ok = false;
+      } else if (choice != 0) {
+        tc_fence_after();
+        if (choice == 1) {
+          if (lane == 0) {
+            pv(pn);
+            if (traced && pn < 64) a.trace[pn * 8 + 4] = globaltimer_ns();
+          }
+          ++pn;
+        } else {
+          if (lane == 0) {
+            qk(qn);
+            if (traced && qn < 64) a.trace[qn * 8 + 1] = globaltimer_ns();
+          }
+          ++qn;
+        }
+        __syncwarp();
+        if (lane == 0) {
+          t0 = globaltimer_ns();
+          spins = 0;
+        }
+      }
     }
     if (!ok && lane == 0) atomicExch(s_abort, 1);
     __syncwarp();
@@ -309,42 +379,65 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[b], (i / 2) & 1, err, 211));
       if (!ok) break;
       tc_fence_after();
-      uint32_t sv[64];
-      {
-        uint32_t (&lo)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[0]);
-        uint32_t (&hi)[32] = *reinterpret_cast<uint32_t(*)[32]>(&sv[32]);
-        tmem_ld_32x32b_x32(lane_base + kSCol + b * kKeys, lo);
-        tmem_ld_32x32b_x32(lane_base + kSCol + b * kKeys + 32, hi);
-      }
+      const bool tr = traced && threadIdx.x == 0 && i < 64;
+      if (tr) a.trace[i * 8 + 2] = globaltimer_ns();
+      uint32_t sv[kKeys];
+#pragma unroll
+      for (int c = 0; c < kKeys / 32; ++c)
+        tmem_ld_32x32b_x32(lane_base + kSCol + b * kKeys + 32 * c, *reinterpret_cast<uint32_t(*)[32]>(&sv[32 * c]));
       tc_wait_ld();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);
       const int p0 = (tile0 + i) * kKeys;
       const int valid = min(kKeys, len - p0);
-      float mt = -INFINITY;
+      if (valid < kKeys) {
 #pragma unroll
-      for (int j = 0; j < 64; ++j) {
-        const float x = j < valid ? u2f(sv[j]) * sl2 : -INFINITY;
-        sv[j] = f2u(x);
-        mt = fmaxf(mt, x);
+        for (int j = 0; j < kKeys; ++j)
+          if (j >= valid) sv[j] = f2u(-INFINITY);
       }
+      float mr = u2f(sv[0]);
+#pragma unroll
+      for (int j = 1; j < kKeys; ++j) mr = fmaxf(mr, u2f(sv[j]));
+      const float mt = mr * sl2;  // the scale is positive: max commutes with it
       // lazy rescale: only when the running max grows by more than 2^8
       const bool grow = lower && mt > m_run + kRescaleLog2;
       float alpha = 1.f;
       if (grow) {
-        alpha = exp2f(m_run - mt);  // 0 on the first tile (m_run = -inf)
+        alpha = fast_exp2(m_run - mt);  // 0 on the first tile (m_run = -inf)
         l_sum *= alpha;
         m_run = mt;
       }
       const bool any_grow = __any_sync(0xffffffffu, grow) && i > 0;
       const float alpha_row = __shfl_sync(0xffffffffu, alpha, lane & 15);
-      if (i > 0) {
-        ok = __all_sync(0xffffffffu, mbar_wait(o_done, (i - 1) & 1, err, 212));
+      // P = 2^(s * scale * log2 e - m) packed to bf16 pairs, computed while
+      // earlier P . V products may still be running
+      uint32_t pk[kKeys / 2];
+      if (lower) {
+        float ps = 0.f;
+#pragma unroll
+        for (int e = 0; e < kKeys / 2; ++e) {
+          const float lo = fast_exp2(fmaf(u2f(sv[2 * e]), sl2, -m_run));
+          const float hi = fast_exp2(fmaf(u2f(sv[2 * e + 1]), sl2, -m_run));
+          ps += lo + hi;
+          const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+          pk[e] = *reinterpret_cast<const uint32_t*>(&b2);
+        }
+        l_sum += ps;
+      }
+      // this part of P was last read by PV(i - kPHalves); a rescale of O
+      // needs PV(i - 1) finished as well
+      if (i >= kPHalves) {
+        const int prev = i - kPHalves;
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[prev % 2], (prev / 2) & 1, err, 212));
         if (!ok) break;
-        tc_fence_after();
       }
       if (any_grow) {
+        if (kPHalves > 1) {
+          ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(i - 1) % 2], ((i - 1) / 2) & 1, err, 214));
+          if (!ok) break;
+        }
+        tc_fence_after();
         // O rows of this warp: lanes 0-15 the low 256 dims, 16-31 the high
 #pragma unroll 1
         for (int c = 0; c < 8; ++c) {
@@ -357,33 +450,26 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
         }
         tc_wait_st();
       }
+      if (tr && i >= 1) a.trace[(i - 1) * 8 + 5] = globaltimer_ns();
       if (lower) {
-        // P row r (bf16) in the 128-byte-swizzled K-major layout of operand A
-        float ps = 0.f;
+        // keys 32 (i % 2).. of row r of P, 128-byte-swizzled K-major layout
         uint8_t* prow = sP + r * 128;
 #pragma unroll
-        for (int c = 0; c < 8; ++c) {
-          uint32_t pk[4];
-#pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            const __nv_bfloat16 lo = __float2bfloat16_rn(exp2f(u2f(sv[c * 8 + 2 * e]) - m_run));
-            const __nv_bfloat16 hi = __float2bfloat16_rn(exp2f(u2f(sv[c * 8 + 2 * e + 1]) - m_run));
-            ps += __bfloat162float(lo) + __bfloat162float(hi);
-            pk[e] = static_cast<uint32_t>(__bfloat16_as_ushort(lo)) |
-                    (static_cast<uint32_t>(__bfloat16_as_ushort(hi)) << 16);
-          }
-          *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        for (int c = 0; c < kKeys / 8; ++c) {
+          const int chunk = (i % kPHalves) * (kKeys / 8) + c;
+          *reinterpret_cast<uint4*>(prow + ((chunk ^ (r & 7)) << 4)) =
+              make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
         }
-        l_sum += ps;
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(p_full);
+      if (lane == 0) mbar_arrive(&p_full[i % 2]);
+      if (tr) a.trace[i * 8 + 3] = globaltimer_ns();
     }
     // ------------------------------------------------------- epilogue ----
     if (!ok && lane == 0) atomicExch(s_abort, 1);
-    if (ok && n > 0) ok = __all_sync(0xffffffffu, mbar_wait(o_done, (n - 1) & 1, err, 213));
+    if (ok && n > 0) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(n - 1) % 2], ((n - 1) / 2) & 1, err, 213));
     tc_fence_after();
     const float l_row = __shfl_sync(0xffffffffu, l_sum, lane & 15);
     const float m_row = __shfl_sync(0xffffffffu, m_run, lane & 15);
@@ -494,8 +580,8 @@ int mla_num_splits(int T, int H) {
 void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s) {
   if (a.T <= 0) return;
   const int P = a.page_size;
-  if (!(P == 8 || P == 16 || P == 32 || (P > 0 && P % 64 == 0)))
-    throw std::runtime_error("minisgl.mla_attention: page_size must be 8, 16, 32 or a multiple of 64");
+  if (!(P == 8 || P == 16 || (P > 0 && P % 32 == 0)))
+    throw std::runtime_error("minisgl.mla_attention: page_size must be 8, 16 or a multiple of 32");
   if (a.splits < 1 || a.splits > 16 || (a.splits > 1 && (a.part_o == nullptr || a.part_lse == nullptr)))
     throw std::runtime_error("minisgl.mla_attention: splits in [1, 16] with partial buffers");
   if (a.T_pad < a.T || a.B <= 0 || a.H <= 0) throw std::runtime_error("minisgl.mla_attention: bad shapes");
@@ -510,7 +596,12 @@ void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s) {
   CUtensorMap tq = make_tmap(a.q_lat, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3, qd, qs, qb, CU_TENSOR_MAP_SWIZZLE_128B);
   CUtensorMap tp = make_tmap_bf16_2d_sw128(a.q_pe, static_cast<uint64_t>(a.T) * a.H, kRope, kRope, kHeadsCta);
   const int seg = P < kKeys ? P : kKeys;
-  CUtensorMap tl = make_tmap_bf16_2d_sw128(a.latent, static_cast<uint64_t>(a.num_slots), kLat, kLat, seg);
+  // pages of >= 32 keys: one 3-D box {64 dims, 32 keys, 9 chunks} per tile,
+  // landing chunk-major as [9][32 keys][128 B]; smaller pages: 2-D boxes of
+  // one page segment per chunk
+  CUtensorMap tl = seg == kKeys ? make_tmap_bf16_kblocks(a.latent, static_cast<uint64_t>(a.num_slots), kLat, kLat,
+                                                         kKeys, kChunks)
+                                : make_tmap_bf16_2d_sw128(a.latent, static_cast<uint64_t>(a.num_slots), kLat, kLat, seg);
   dim3 grid(a.splits, a.T, (a.H + kHeadsCta - 1) / kHeadsCta);
   launch_pdl(mla_attn_kernel, grid, dim3(kMlaThreads), kMlaSmem, s, tq, tp, tl, a);
   if (a.splits > 1) launch_pdl(mla_combine_kernel, dim3(a.T, a.H), dim3(128), 0, s, a);

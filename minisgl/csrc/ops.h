@@ -185,6 +185,10 @@ struct MlaAttnArgs {
   int B, T, T_pad, H, page_size, splits;
   float scale;
   int* err;
+  // optional per-tile timestamps (%globaltimer ns) of CTA (0, 0, 0), 8 slots
+  // per tile: 0 copy issued, 1 QK issued, 2 scores seen, 3 P written,
+  // 4 PV issued, 5 PV seen complete
+  unsigned long long* trace;
 };
 void launch_mla_prepare(const MlaPrepareArgs& a, cudaStream_t s);
 void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s);

@@ -388,11 +388,14 @@ def mla_attention(
     page_size: int,
     scale: float,
     splits: int = 0,
+    trace: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
     """Causal absorbed MLA over the paged latent cache of one layer:
     q_lat [H, T_pad, kv_lora] + q_pe [T, H, rope] -> [H, T_pad, kv_lora]
     (one CTA per query token and 64 heads; split-KV when there are few
-    tokens)."""
+    tokens). ``trace``: optional int64 [512] device tensor that receives
+    per-tile phase timestamps of the first CTA (copy issued, QK issued,
+    scores seen, P written, PV issued, PV seen complete; 8 slots a tile)."""
     if not q_lat.is_cuda:
         return ref.mla_attention(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale)
     H, T_pad, kv_lora = q_lat.shape
@@ -411,7 +414,7 @@ def mla_attention(
         part_lse = buf[splits * T * H * kv_lora: need]
     _count(2 if splits > 1 else 1)
     nat.mla_attention(out, q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits,
-                      part_o, part_lse, error_word(q_lat.device))
+                      part_o, part_lse, error_word(q_lat.device), trace)
     return out
 
 
