@@ -148,9 +148,17 @@ def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
     nbytes = 2 * (M * K + N * K + M * N)
     tf, gbs = flops / ms / 1e9, nbytes / ms / 1e6
     bound = max(flops / (peaks["tflops"] * 1e9), nbytes / (peaks["hbm_gbs"] * 1e6))  # roofline ms
-    return {"kernel": f"gemm[{label}]", "M": M, "N": N, "K": K, "ms": round(ms, 4), "cublas_ms": round(ms_cublas, 4),
-            "graph_ms": round(ms_graph, 4), "cublas_graph_ms": round(ms_cublas_graph, 4),
-            "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "frac_roofline": round(bound / ms, 3)}
+    row = {"kernel": f"gemm[{label}]", "M": M, "N": N, "K": K, "ms": round(ms, 4), "cublas_ms": round(ms_cublas, 4),
+           "graph_ms": round(ms_graph, 4), "cublas_graph_ms": round(ms_cublas_graph, 4),
+           "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "frac_roofline": round(bound / ms, 3)}
+    if M >= 512 and K % 64 == 0:
+        # persistent tiles (plan mode 3), both N tiles
+        nat = ops.native()
+        for bn in (256, 128):
+            t = time_kernel(lambda bn=bn: nat.gemm(out, x, w, None, None, 1, 3, None, bn))
+            row[f"persistent{bn}_ms"] = round(t, 4)
+            row[f"persistent{bn}_frac_roofline"] = round(bound / t, 3)
+    return row
 
 
 def bench_layer_chain(M: int, peaks, layers: int = 28) -> List[Dict]:
@@ -296,6 +304,9 @@ def main() -> None:
     cases.append(("gemm[lm_head M=256]", lambda: bench_gemm(256, V, H, peaks, "lm_head M=256")))
     cases.append(("gemm[gate_up prefill]", lambda: bench_gemm(16384, 2 * I, H, peaks, "gate_up prefill")))
     cases.append(("gemm[square 8192]", lambda: bench_gemm(8192, 8192, 8192, peaks, "square 8192")))
+    for lab, N, K in (("qkv", 4096, H), ("o", H, 2048), ("down", H, I)):
+        cases.append((f"gemm[{lab} prefill]", lambda N=N, K=K, lab=lab: bench_gemm(16384, N, K, peaks,
+                                                                                 f"{lab} prefill")))
     cases.append(("elementwise", lambda: bench_elementwise(peaks)))
     for M in (1, 8, 32, 64, 128, 192, 256):
         cases.append((f"layer_chain M={M};", lambda M=M: bench_layer_chain(M, peaks)))

@@ -90,6 +90,10 @@ struct GemmArgs {
   int g_experts;
 };
 void launch_gemm(const GemmArgs& a, cudaStream_t stream);
+// Persistent 128 x {128, 256} tiles with double-buffered TMEM accumulators
+// (force_mode 3): plain GEMMs (no fused epilogue) with K % 64 == 0.
+bool gemm_persistent_supported(const GemmArgs& a);
+void launch_gemm_persistent(const GemmArgs& a, cudaStream_t stream);
 // Number of fp32 workspace elements launch_gemm may need for this shape.
 int64_t gemm_workspace_elems(int M, int N, int K);
 

@@ -21,7 +21,7 @@ from typing import Dict, Iterable, List, Optional, Tuple
 
 import torch
 
-Plan = Tuple[int, int, int]  # (mode: 1 token-major / 2 weight-major, n tile, splits)
+Plan = Tuple[int, int, int]  # (mode: 1 token-major / 2 weight-major / 3 persistent, n tile, splits)
 PLANS: Dict[Tuple[int, int, int], Plan] = {}
 # best plan per shape among those the fused epilogues accept (weight-major
 # tiles, or token-major tiles with an N tile of 128 / 256)
@@ -220,9 +220,9 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
 
 
 def _tune_prefill(native, shapes, device: torch.device, cached: Dict[Tuple[int, int, int], Plan]) -> None:
-    """Plain plans for long prefill chunks: token-major tiles of 128 or 256
-    features (the weight-major and split-K plans only pay off for short
-    batches)."""
+    """Plain plans for long prefill chunks: persistent or one-tile-per-CTA
+    token-major tiles of 128 or 256 features (the weight-major and split-K
+    plans only pay off for short batches)."""
     for N, K in shapes:
         for M in PREFILL_SIZES:
             key = (M, N, K)
@@ -235,7 +235,7 @@ def _tune_prefill(native, shapes, device: torch.device, cached: Dict[Tuple[int, 
             out = torch.empty(M, N, device=device, dtype=torch.bfloat16)
             w = torch.randn(N, K, device=device, dtype=torch.bfloat16) * 0.02
             timed = []
-            for plan in ((1, 256, 1), (1, 128, 1)):
+            for plan in ((3, 256, 1), (3, 128, 1), (1, 256, 1), (1, 128, 1)):
                 mode, bn, s = plan
                 timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
                     out, x, w_, None, None, sp, m, None, b), [w], reps=4), plan))

@@ -25,6 +25,7 @@ SOURCES = [
     "minisgl/csrc/binding.cpp",
     "minisgl/csrc/radix.cpp",
     "minisgl/csrc/gemm.cu",
+    "minisgl/csrc/gemm_persistent.cu",
     "minisgl/csrc/attention.cu",
     "minisgl/csrc/elementwise.cu",
     "minisgl/csrc/rope_store.cu",

@@ -87,6 +87,22 @@ def test_gemm_every_plan(M, N, K):
         assert err < 3e-2 * (K / 1024) ** 0.5 + 1e-2, (mode, bn, s, err)
 
 
+@pytest.mark.parametrize("M,N,K,bn", [(4096, 6144, 1024, 256), (3000, 1000, 576, 256), (129, 4096, 2048, 128),
+                                        (1, 512, 64, 256), (8192, 1024, 3072, 128)])
+@pytest.mark.parametrize("bias,f32", [(False, False), (True, True)])
+def test_gemm_persistent(M, N, K, bn, bias, f32):
+    """Persistent tiles (plan mode 3) with ragged edges in M and N."""
+    torch.manual_seed(M + N + K)
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, device=DEV) * 0.1).to(torch.bfloat16) if bias else None
+    out = torch.empty(M, N, device=DEV, dtype=torch.float32 if f32 else torch.bfloat16)
+    ops.native().gemm(out, x, w, b, None, 1, 3, ops.error_word(x.device), bn)
+    torch.cuda.synchronize()
+    ops.check_device_errors(x.device)
+    _close(out, ref.gemm(x, w, b, torch.float32), atol=2e-2 * math.sqrt(K / 1024) + 1e-2, rtol=1e-2)
+
+
 def test_gemm_strided_input_fp32_out():
     torch.manual_seed(1)
     big = torch.randn(50, 3072, device=DEV, dtype=torch.bfloat16)
