@@ -343,6 +343,90 @@ void moe_experts(at::Tensor out, const at::Tensor& x, const at::Tensor& w1, cons
                               static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
 }
 
+// -------------------------------------------------------------- MXFP4 ----
+void mxfp4_quantize(at::Tensor packed, at::Tensor scales, const at::Tensor& w) {
+  check_cuda(w, "w");
+  MSG_CHECK(w.dim() == 3 && w.is_contiguous() && w.scalar_type() == at::kBFloat16, "mxfp4_quantize: w [E, N, K] bf16");
+  const int64_t E = w.size(0), N = w.size(1), K = w.size(2);
+  MSG_CHECK(K % 64 == 0, "mxfp4_quantize: K % 64 == 0");
+  MSG_CHECK(packed.scalar_type() == at::kByte && packed.is_contiguous() && packed.numel() == E * N * K / 2,
+            "mxfp4_quantize: packed uint8 [E, N, K / 2]");
+  MSG_CHECK(scales.scalar_type() == at::kByte && scales.is_contiguous() && scales.numel() == E * N * K / 32,
+            "mxfp4_quantize: scales uint8 [E, K / 64, N, 2]");
+  const c10::cuda::CUDAGuard guard(w.device());
+  minisgl::launch_mxfp4_quantize(packed.data_ptr(), scales.data_ptr(), w.data_ptr(), static_cast<int>(E),
+                                 static_cast<int>(N), static_cast<int>(K), stream_of(w));
+}
+
+// MXFP4 routed experts: align -> gather -> gate_up (E2M1 weights expanded
+// to bf16 in shared memory, SiLU x up epilogue) -> down -> weighted combine.
+void moe_experts_mxfp4(at::Tensor out, const at::Tensor& x, const at::Tensor& w1q, const at::Tensor& w1s,
+                       const at::Tensor& w2q, const at::Tensor& w2s, const at::Tensor& topk_w,
+                       const at::Tensor& topk_ids, int64_t tile, at::Tensor xs, at::Tensor h, at::Tensor ys,
+                       at::Tensor sorted_pair, at::Tensor pair_pos, at::Tensor tile_expert, at::Tensor tile_row,
+                       at::Tensor num_tiles, const c10::optional<at::Tensor>& err) {
+  check_cuda(x, "x");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "moe_experts_mxfp4: bf16 x");
+  MSG_CHECK(w1q.scalar_type() == at::kByte && w2q.scalar_type() == at::kByte && w1s.scalar_type() == at::kByte &&
+                w2s.scalar_type() == at::kByte && w1q.is_contiguous() && w2q.is_contiguous() && w1s.is_contiguous() &&
+                w2s.is_contiguous(),
+            "moe_experts_mxfp4: uint8 packed weights and scales");
+  const int64_t T = x.size(0), H = x.size(1), E = w1q.size(0), I2 = w1q.size(1), I = I2 / 2, k = topk_ids.size(1);
+  MSG_CHECK(w1q.dim() == 3 && w1q.size(2) * 2 == H && w2q.dim() == 3 && w2q.size(0) == E && w2q.size(1) == H &&
+                w2q.size(2) * 2 == I && w1s.numel() == E * I2 * H / 32 && w2s.numel() == E * H * I / 32,
+            "moe_experts_mxfp4: w1 packed [E, 2I, H / 2], w2 packed [E, H, I / 2] with their scales");
+  MSG_CHECK(I % 64 == 0 && H % 128 == 0 && I2 % 128 == 0, "moe_experts_mxfp4: I % 64 == 0 and H % 128 == 0");
+  MSG_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous() && topk_ids.size(0) == T,
+            "moe_experts_mxfp4: int32 topk_ids [T, k]");
+  MSG_CHECK(topk_w.scalar_type() == at::kFloat && topk_w.is_contiguous() && topk_w.numel() == T * k,
+            "moe_experts_mxfp4: float32 topk_w [T, k]");
+  MSG_CHECK(tile == 16 || tile == 32 || tile == 64 || tile == 128, "moe_experts_mxfp4: tile of 16, 32, 64 or 128");
+  const int64_t P = T * k + E * (tile - 1);
+  const int64_t Pp = (P + tile - 1) / tile * tile;
+  MSG_CHECK(xs.numel() >= Pp * H && h.numel() >= Pp * I && ys.numel() >= Pp * H && sorted_pair.numel() >= P &&
+                pair_pos.numel() >= T * k && tile_expert.numel() >= P / tile && tile_row.numel() >= P / tile &&
+                num_tiles.numel() >= 1,
+            "moe_experts_mxfp4: scratch too small");
+  MSG_CHECK(out.numel() == T * H && out.scalar_type() == at::kBFloat16, "moe_experts_mxfp4: out [T, H] bf16");
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = stream_of(x);
+  minisgl::MoeAlignArgs al{};
+  al.topk_ids = topk_ids.data_ptr<int32_t>();
+  al.T = static_cast<int>(T);
+  al.k = static_cast<int>(k);
+  al.E = static_cast<int>(E);
+  al.tile = static_cast<int>(tile);
+  al.sorted_pair = sorted_pair.data_ptr<int32_t>();
+  al.pair_pos = pair_pos.data_ptr<int32_t>();
+  al.tile_expert = tile_expert.data_ptr<int32_t>();
+  al.tile_row = tile_row.data_ptr<int32_t>();
+  al.num_tiles = num_tiles.data_ptr<int32_t>();
+  minisgl::launch_moe_align(al, st);
+  minisgl::launch_moe_gather(xs.data_ptr(), x.data_ptr(), al.sorted_pair, static_cast<int>(P), static_cast<int>(k),
+                             static_cast<int>(H), st);
+  for (int pass = 0; pass < 2; ++pass) {
+    minisgl::MoeMxfp4GemmArgs a{};
+    a.x = pass == 0 ? xs.data_ptr() : h.data_ptr();
+    a.packed = pass == 0 ? w1q.data_ptr() : w2q.data_ptr();
+    a.scales = pass == 0 ? w1s.data_ptr() : w2s.data_ptr();
+    a.out = pass == 0 ? h.data_ptr() : ys.data_ptr();
+    a.P = static_cast<int>(Pp);
+    a.E = static_cast<int>(E);
+    a.N = static_cast<int>(pass == 0 ? I2 : H);
+    a.K = static_cast<int>(pass == 0 ? H : I);
+    a.ldo = static_cast<int>(pass == 0 ? I : H);
+    a.tile = static_cast<int>(tile);
+    a.silu = pass == 0;
+    a.tile_expert = al.tile_expert;
+    a.tile_row = al.tile_row;
+    a.num_tiles = al.num_tiles;
+    a.err = err_ptr(err);
+    minisgl::launch_moe_mxfp4_gemm(a, st);
+  }
+  minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), al.pair_pos,
+                              static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
+}
+
 // ---------------------------------------------------------------- MLA ----
 // Grouped GEMM over G uniform groups: out[g] = x[g] @ w[g]^T with x rows of
 // group g at [g * rows_pad, + rows_pad) and w [G, N, K]; the tile tables map
@@ -894,6 +978,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_sample", &gemm_sample);
   m.def("moe_experts", &moe_experts);
   m.def("grouped_gemm", &grouped_gemm);
+  m.def("mxfp4_quantize", &mxfp4_quantize);
+  m.def("moe_experts_mxfp4", &moe_experts_mxfp4);
   m.def("mla_prepare", &mla_prepare);
   m.def("mla_attention", &mla_attention, py::arg("out"), py::arg("q_lat"), py::arg("q_pe"), py::arg("latent"),
         py::arg("page_table"), py::arg("req_rows"), py::arg("seq_lens"), py::arg("cu_q"), py::arg("page_size"),

@@ -167,7 +167,12 @@ __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a
   const int P = n + a.E * (a.tile - 1);
   for (int e = threadIdx.x; e < a.E; e += blockDim.x) cnt[e] = 0;
   __syncthreads();
-  for (int i = threadIdx.x; i < n; i += blockDim.x) atomicAdd(&cnt[a.topk_ids[i]], 1);
+  // ids outside [0, E) (experts held by another rank under expert
+  // parallelism) are dropped: no row, pair_pos -1, no share in the combine
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = a.topk_ids[i];
+    if (e >= 0 && e < a.E) atomicAdd(&cnt[e], 1);
+  }
   __syncthreads();
   if (threadIdx.x == 0) {
     int rows = 0, tiles = 0;
@@ -197,6 +202,10 @@ __global__ void __launch_bounds__(kAlignThreads) moe_align_kernel(MoeAlignArgs a
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int e = a.topk_ids[i];
+    if (e < 0 || e >= a.E) {
+      a.pair_pos[i] = -1;
+      continue;
+    }
     const int r = off[e] + atomicAdd(&cnt[e], 1);
     a.sorted_pair[r] = i;
     a.pair_pos[i] = r;
@@ -231,6 +240,7 @@ __global__ void moe_combine_kernel(__nv_bfloat16* out, const __nv_bfloat16* ys, 
     for (int j = 0; j < k; ++j) {
       const float w = topk_w[t * k + j];
       const int r = pair_pos[t * k + j];
+      if (r < 0) continue;  // expert on another rank
       const uint4 raw = *reinterpret_cast<const uint4*>(ys + static_cast<int64_t>(r) * H + c);
       const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
 #pragma unroll

@@ -249,6 +249,23 @@ void launch_moe_gather(void* xs, const void* x, const int32_t* sorted_pair, int 
 void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* pair_pos, int T, int k, int H,
                         cudaStream_t s);
 
+// --------------------------------------------------------------- MXFP4 ----
+// w [E, N, K] bf16 -> packed [E, N, K / 2] E2M1 + scales [E, K / 64, N, 2] E8M0
+void launch_mxfp4_quantize(void* packed, void* scales, const void* w, int E, int N, int K, cudaStream_t s);
+struct MoeMxfp4GemmArgs {
+  const void* x;              // [P, K] bf16 expert-sorted token rows
+  const void* packed;         // [E, N, K / 2]
+  const void* scales;         // [E, K / 64, N, 2]
+  void* out;                  // [P, ldo] bf16 (N / 2 features with silu, else N)
+  int P, E, N, K, ldo, tile;
+  bool silu;                  // interleaved gate|up rows -> silu(gate) * up
+  const int32_t* tile_expert;
+  const int32_t* tile_row;
+  const int32_t* num_tiles;
+  int* err;
+};
+void launch_moe_mxfp4_gemm(const MoeMxfp4GemmArgs& a, cudaStream_t s);
+
 // ------------------------------------------------------- NVLink collectives ----
 // kind 0: all-reduce of every rank's partial (bf16, n_elems, at the data
 // offset of each heap) into out (+ residual); kind 1: all-gather of

@@ -60,9 +60,14 @@ class EngineConfig:
 
     @cached_property
     def model_config(self) -> "ModelConfig":
+        import dataclasses
+
         from minisgl.models import ModelConfig
 
-        return ModelConfig.from_hf(self.hf_config)
+        cfg = ModelConfig.from_hf(self.hf_config)
+        ep = self.ep_size if self.ep_size > 1 else 1
+        return dataclasses.replace(cfg, moe_quant=self.moe_quant, ep_size=ep,
+                                   ep_rank=self.tp_info.rank % ep if ep > 1 else 0)
 
     @property
     def max_seq_len(self) -> int:

@@ -1,5 +1,10 @@
 """Routed-expert MLP layer (experts sharded over TP on the intermediate dim,
-or distributed over ranks with expert parallelism)."""
+or distributed over ranks with expert parallelism), bf16 or MXFP4.
+
+Expert parallelism runs over the tensor-parallel ranks: attention is
+replicated, every rank routes all tokens over all experts, runs only the
+experts it holds (the others are dropped by the align kernel) and the
+partial sums meet in the same all-reduce tensor parallelism needs."""
 
 from __future__ import annotations
 
@@ -20,8 +25,13 @@ class MoELayer(BaseOP):
     def __init__(self, num_experts: int, top_k: int, hidden_size: int, intermediate_size: int,
                  renormalize: bool = True, activation: str = "silu", scoring: str = "softmax",
                  n_group: int = 1, topk_group: int = 1, routed_scale: float = 1.0,
-                 has_correction_bias: bool = False, reduce_results: bool = True) -> None:
+                 has_correction_bias: bool = False, reduce_results: bool = True, quant: str = "none",
+                 ep_size: int = 1, ep_rank: int = 0) -> None:
         tp = get_tp_info().size
+        if ep_size > 1 and ep_size != tp:
+            raise ValueError("expert parallelism runs over the tensor-parallel ranks: ep_size must equal tp_size")
+        if quant not in ("none", "mxfp4"):
+            raise ValueError(f"unknown expert quantisation {quant!r}")
         self.num_experts = num_experts
         self.top_k = top_k
         self.hidden_size = hidden_size
@@ -35,11 +45,17 @@ class MoELayer(BaseOP):
         self._tp = tp
         self._reduce = reduce_results
         self._comm = DistributedCommunicator()
-        local_i = div_even(intermediate_size, tp)
-        self.gate_up_proj = torch.empty(num_experts, 2 * local_i, hidden_size)
-        self.down_proj = torch.empty(num_experts, hidden_size, local_i)
+        # expert parallelism: this rank holds experts [first, first + E / ep)
+        # whole; tensor parallelism: every rank holds a slice of every expert
+        local_e = div_even(num_experts, ep_size) if ep_size > 1 else num_experts
+        local_i = intermediate_size if ep_size > 1 else div_even(intermediate_size, tp)
+        self._first_expert = ep_rank * local_e if ep_size > 1 else 0
+        self.gate_up_proj = torch.empty(local_e, 2 * local_i, hidden_size)
+        self.down_proj = torch.empty(local_e, hidden_size, local_i)
         self.e_score_correction_bias = torch.empty(num_experts, dtype=torch.float32) if has_correction_bias else None
         self._interleaved = False
+        self._quant = quant
+        self._mxfp4 = None  # (w1 packed, w1 scales, w2 packed, w2 scales) after post_load
 
     def post_load(self) -> None:
         """Interleave each expert's gate|up rows in 64-row blocks (64 gate rows,
@@ -53,15 +69,34 @@ class MoELayer(BaseOP):
         w = self.gate_up_proj.view(E, 2, n // 64, 64, H).transpose(1, 2)
         self.gate_up_proj = w.reshape(E, 2 * n, H).contiguous()
         self._interleaved = True
+        if self._quant == "mxfp4":
+            self.quantize()
+
+    def quantize(self) -> None:
+        """Replace the bf16 expert weights by MXFP4 (E2M1 + E8M0 per 32; see
+        minisgl.quant.mxfp4). On the GPU the bf16 copies are released; on
+        the CPU they are kept for inspection."""
+        from minisgl.quant import quantize_mxfp4
+
+        w1q, w1s = quantize_mxfp4(self.gate_up_proj.to(torch.bfloat16).contiguous())
+        w2q, w2s = quantize_mxfp4(self.down_proj.to(torch.bfloat16).contiguous())
+        self._mxfp4 = (w1q, w1s, w2q, w2s)
+        if self.gate_up_proj.is_cuda:
+            self.gate_up_proj = self.gate_up_proj.new_empty(0)
+            self.down_proj = self.down_proj.new_empty(0)
+
+    def backend_kwargs(self) -> dict:
+        """Arguments of the MoE backend that describe this layer's experts."""
+        return dict(topk=self.top_k, renormalize=self.renormalize, activation=self.activation,
+                    scoring=self.scoring, n_group=self.n_group, topk_group=self.topk_group,
+                    routed_scale=self.routed_scale, interleaved=self._interleaved,
+                    expert_offset=self._first_expert, mxfp4=self._mxfp4)
 
     def forward(self, hidden_states: torch.Tensor, router_logits: torch.Tensor) -> torch.Tensor:
         ctx = get_global_ctx()
         out = ctx.moe_backend.forward(
             hidden_states=hidden_states, w1=self.gate_up_proj, w2=self.down_proj, gating_output=router_logits,
-            topk=self.top_k, renormalize=self.renormalize, activation=self.activation, scoring=self.scoring,
-            correction_bias=self.e_score_correction_bias, n_group=self.n_group, topk_group=self.topk_group,
-            routed_scale=self.routed_scale, interleaved=self._interleaved,
-        )
+            correction_bias=self.e_score_correction_bias, **self.backend_kwargs())
         if self._tp > 1 and self._reduce:
             out = self._comm.all_reduce(out)
         return out

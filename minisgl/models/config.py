@@ -55,6 +55,10 @@ class ModelConfig:
     routed_scaling_factor: float = 1.0
     scoring_func: str = "softmax"
     attention_bias: bool = False
+    # runtime choices that shape the layers (not part of the HF config)
+    moe_quant: str = "none"      # "none" | "mxfp4": routed expert weights in MXFP4
+    ep_size: int = 1             # routed experts split over this many ranks
+    ep_rank: int = 0
     extra: Dict[str, Any] = field(default_factory=dict)
 
     @property

@@ -117,7 +117,8 @@ class DeepseekMoE(BaseOP):
         self.experts = MoELayer(config.num_experts, config.num_experts_per_tok, config.hidden_size,
                                 config.moe_intermediate_size, renormalize=config.norm_topk_prob,
                                 scoring=config.scoring_func, n_group=config.n_group, topk_group=config.topk_group,
-                                routed_scale=config.routed_scaling_factor, reduce_results=False)
+                                routed_scale=config.routed_scaling_factor, reduce_results=False,
+                                quant=config.moe_quant, ep_size=config.ep_size, ep_rank=config.ep_rank)
         self.shared_experts = (GatedMLP(config, config.moe_intermediate_size * config.n_shared_experts)
                                if config.n_shared_experts > 0 else None)
         self._tp = get_tp_info().size
@@ -127,10 +128,8 @@ class DeepseekMoE(BaseOP):
         logits = ops.gemm(x, self.gate.weight, out_dtype=torch.float32)
         e = self.experts
         out = get_global_ctx().moe_backend.forward(
-            hidden_states=x, w1=e.gate_up_proj, w2=e.down_proj, gating_output=logits, topk=e.top_k,
-            renormalize=e.renormalize, activation=e.activation, scoring=e.scoring,
-            correction_bias=self.gate.e_score_correction_bias, n_group=e.n_group, topk_group=e.topk_group,
-            routed_scale=e.routed_scale, interleaved=e._interleaved)
+            hidden_states=x, w1=e.gate_up_proj, w2=e.down_proj, gating_output=logits,
+            correction_bias=self.gate.e_score_correction_bias, **e.backend_kwargs())
         if self.shared_experts is not None:
             s = self.shared_experts
             h = ops.silu_and_mul(s.gate_up_proj.forward(x))

@@ -73,7 +73,8 @@ class MoEMLP(BaseOP):
 
     def __init__(self, config: "ModelConfig") -> None:
         self.experts = MoELayer(config.num_experts, config.num_experts_per_tok, config.hidden_size,
-                                config.moe_intermediate_size, renormalize=config.norm_topk_prob)
+                                config.moe_intermediate_size, renormalize=config.norm_topk_prob,
+                                quant=config.moe_quant, ep_size=config.ep_size, ep_rank=config.ep_rank)
         self.gate = LinearReplicated(config.hidden_size, config.num_experts, has_bias=False)
 
     @nvtx_annotate("MoE")

@@ -576,6 +576,36 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_w: tor
     return out
 
 
+def moe_experts_mxfp4(x: torch.Tensor, w1q: torch.Tensor, w1s: torch.Tensor, w2q: torch.Tensor, w2s: torch.Tensor,
+                      topk_w: torch.Tensor, topk_ids: torch.Tensor, tile: int = 0) -> torch.Tensor:
+    """``moe_experts`` with MXFP4 expert weights (packed [E, N, K / 2] +
+    scales [E, K / 64, N, 2], see minisgl.quant.mxfp4): the grouped GEMMs
+    expand E2M1 to bf16 in shared memory, activations stay bf16."""
+    T, H = x.shape
+    E, I2 = w1q.shape[0], w1q.shape[1]
+    I, k = I2 // 2, topk_ids.shape[1]
+    out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    tile = tile or moe_tile(T, k, E)
+    P = T * k + E * (tile - 1)
+    Pp = (P + tile - 1) // tile * tile
+    dev, i32 = x.device, torch.int32
+    xs = torch.empty(Pp, H, dtype=x.dtype, device=dev)
+    h = torch.empty(Pp, I, dtype=x.dtype, device=dev)
+    ys = torch.empty(Pp, H, dtype=x.dtype, device=dev)
+    sorted_pair = torch.empty(P, dtype=i32, device=dev)
+    pair_pos = torch.empty(T * k, dtype=i32, device=dev)
+    tile_expert = torch.empty(P // tile, dtype=i32, device=dev)
+    tile_row = torch.empty(P // tile, dtype=i32, device=dev)
+    num_tiles = torch.empty(1, dtype=i32, device=dev)
+    _count(6)
+    native().moe_experts_mxfp4(out, x.contiguous(), w1q, w1s, w2q, w2s, topk_w.float().contiguous(),
+                               topk_ids.to(i32).contiguous(), tile, xs, h, ys, sorted_pair, pair_pos, tile_expert,
+                               tile_row, num_tiles, error_word(dev))
+    return out
+
+
 def moe_route(
     logits: torch.Tensor,
     k: int,

@@ -33,6 +33,7 @@ SOURCES = [
     "minisgl/csrc/moe.cu",
     "minisgl/csrc/symm.cu",
     "minisgl/csrc/mla.cu",
+    "minisgl/csrc/mxfp4.cu",
 ]
 
 
