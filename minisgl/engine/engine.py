@@ -24,6 +24,7 @@ from minisgl.attention import create_attention_backend
 from minisgl.core import FusedSample, Batch, Context, Req, reset_global_ctx, set_global_ctx
 from minisgl.kvcache import create_kvcache_pool
 from minisgl.layers import set_rope_device
+from minisgl.utils import fault
 from minisgl.models import create_model, load_weight, random_weights
 from minisgl.moe import create_moe_backend
 from minisgl.parallel import destroy_distributed, get_tp_info, reset_tp_info, set_tp_info
@@ -95,6 +96,9 @@ class Engine:
         # ------------------------------------------------------------- model
         mcfg = config.model_config
         self.model_config = mcfg
+        self.tp_rank = config.tp_info.rank
+        self._step = 0  # forwards run so far (the fault-injection clock)
+        self._faults = bool(fault.rules())
         set_rope_device(self.device)
         with torch.device("meta"), torch_dtype(config.dtype):
             self.model = create_model(mcfg)
@@ -271,6 +275,9 @@ class Engine:
 
     # -------------------------------------------------------------- forward
     def forward_batch(self, batch: Batch, args: BatchSamplingArgs) -> ForwardOutput:
+        if self._faults:
+            fault.at_step(self.tp_rank, self._step)
+        self._step += 1
         # greedy / temperature batches sample inside the LM-head GEMM (no
         # logits in memory); top-k / top-p batches sample from the logits
         fused = self.sampler.fusable(args, batch.size) and getattr(self.model, "samples_in_lm_head", False)

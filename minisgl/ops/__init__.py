@@ -78,13 +78,33 @@ def error_word(device: torch.device) -> torch.Tensor:
     return w
 
 
+class DeviceWaitTimeout(RuntimeError):
+    """A kernel gave up on an mbarrier wait (its pipeline stalled) and returned."""
+
+
+class CommTimeoutError(RuntimeError):
+    """A collective kernel gave up waiting for a peer rank's flag and returned:
+    the peer is late, stalled or gone. The device context stays usable."""
+
+
+ERR_MBAR_TIMEOUT = 1
+ERR_PEER_TIMEOUT = 2
+
+
 def check_device_errors(device: torch.device) -> None:
+    """Raise if a kernel on ``device`` recorded an error (and clear it):
+    CommTimeoutError for a peer wait that ran out, DeviceWaitTimeout for a
+    pipeline wait, RuntimeError otherwise."""
     w = _ERR_WORDS.get((device.type, device.index))
     if w is None:
         return
     code, site = w.tolist()
     if code != 0:
         w.zero_()
+        if code == ERR_PEER_TIMEOUT:
+            raise CommTimeoutError(f"minisgl collective kernel timed out waiting for a peer (site {site})")
+        if code == ERR_MBAR_TIMEOUT:
+            raise DeviceWaitTimeout(f"minisgl kernel pipeline wait timed out (site {site})")
         raise RuntimeError(f"minisgl kernel reported error code {code} at site {site}")
 
 

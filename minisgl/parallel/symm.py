@@ -29,6 +29,7 @@ import torch
 import torch.distributed as dist
 
 from minisgl import ops
+from minisgl.utils import fault
 
 from .comm import DistributedImpl, register_plugin
 
@@ -80,6 +81,8 @@ class SymmMemImpl(DistributedImpl):
         self.bases = torch.tensor(bases, dtype=torch.int64, device=device)
         # call counters: [0] the fused GEMM + all-reduce, [1] the collective kernels
         self.epoch = torch.zeros(2, dtype=torch.int32, device=device)
+        self.calls = 0  # collective launches so far (the fault-injection clock)
+        self._faults = bool(fault.rules())
         self.data = torch.as_tensor(_DeviceBuffer(own + DATA_OFFSET, self.capacity), device=device)
         dist.barrier(group=self._cpu_group)  # every heap is mapped before the first collective
 
@@ -94,6 +97,9 @@ class SymmMemImpl(DistributedImpl):
 
     def _collective(self, kind: int, out: torch.Tensor, n_elems: int, residual: Optional[torch.Tensor] = None,
                     rows: int = 0, row_elems: int = 0) -> None:
+        self.calls += 1
+        if self._faults and fault.skip_collective(self.rank, self.calls - 1):
+            return  # injected: this rank never arrives, the peers' bounded waits expire
         ops._count(2)
         ops.native().symm_collective(kind, out, residual, self.bases, self.epoch[1:], self.rank, self.world, n_elems,
                                      rows, row_elems, ops.error_word(out.device))

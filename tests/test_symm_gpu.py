@@ -175,3 +175,57 @@ def test_tp2_engine_fused_comm_matches_nccl():
     same = sum(p == q for x, y in zip(a, b) for p, q in zip(x, y))
     firsts = sum(x[0] == y[0] for x, y in zip(a, b))
     assert firsts >= 3 and same >= 0.6 * sum(len(x) for x in a), (a, b)
+
+
+def _skipped_peer(rank, world, port, q):
+    """Rank 1 skips its second collective (host-side fault injection): rank
+    0's entry wait runs out after its 2 s budget, the kernel returns with an
+    error code, and the host raises CommTimeoutError; the device stays usable."""
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from minisgl.utils import fault
+
+    os.environ[fault.ENV] = "skip_collective:rank=1:step=1"
+    import torch.distributed as dist
+
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world,
+                            timeout=timedelta(seconds=60), device_id=dev)
+    impl = None
+    status = []
+    try:
+        from minisgl import ops
+        from minisgl.parallel.symm import SymmMemImpl
+
+        impl = SymmMemImpl(dev, 1 << 20)
+        x = torch.ones(4096, device=dev, dtype=torch.bfloat16)
+        impl.all_reduce(x)  # call 0: both ranks
+        torch.cuda.synchronize(dev)
+        ops.check_device_errors(dev)
+        status.append(float(x[0].item()))
+        impl.all_reduce(x)  # call 1: rank 1 does not launch it
+        torch.cuda.synchronize(dev)
+        try:
+            ops.check_device_errors(dev)
+            status.append("no error")
+        except ops.CommTimeoutError:
+            status.append("timeout")
+        # the context still works after the timeout
+        y = torch.arange(8, device=dev, dtype=torch.float32) * 2
+        torch.cuda.synchronize(dev)
+        status.append(float(y.sum().item()))
+        dist.barrier(group=impl._cpu_group)  # both ranks are past their kernels
+    except Exception as e:  # reported to the parent
+        status.append(repr(e))
+    finally:
+        if impl is not None:
+            impl.shutdown()
+        dist.destroy_process_group()
+    q.put((rank, status))
+
+
+def test_skipped_peer_times_out_without_fault():
+    _need_two_gpus()
+    results = _spawn(_skipped_peer, 2)
+    assert results[0] == [2.0, "timeout", 56.0], results
+    assert results[1] == [2.0, "no error", 56.0], results
