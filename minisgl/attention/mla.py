@@ -6,7 +6,10 @@ space by W_UK, head-major [heads, T_pad, kv_lora], and the rotated q_pe
 head reads the same latent rows) and returns the latent output, head-major
 [heads, T_pad, kv_lora], which the model maps back to heads with W_UV. Metadata per batch is the GQA backend's:
 each request's page-table row, key count and query offset, in one pinned
-upload. The reference has no MLA (no DeepSeek-V3 architecture).
+upload. The reference has no MLA (no DeepSeek-V3 architecture). Under context
+parallelism each rank holds the latent rows of the 64-key tiles t with
+t % cp == rank and attends over those only; the partial outputs and
+log-sum-exps of all ranks are all-gathered and merged (``ops.mla_attention``).
 """
 
 from __future__ import annotations
@@ -18,7 +21,7 @@ import torch
 
 from minisgl import ops
 from minisgl.core import Batch, get_global_ctx
-from minisgl.parallel import get_tp_info
+from minisgl.parallel import get_cp_info, get_tp_info
 from minisgl.utils import div_even
 
 from .base import BaseAttnBackend, BaseAttnMetadata
@@ -65,6 +68,8 @@ class MLAAttnBackend(BaseAttnBackend):
         self.kv = ctx.kv_cache
         self.device = self.kv.device
         self.capture: Optional[Dict[str, torch.Tensor]] = None
+        cp = get_cp_info()
+        self.cp_size, self.cp_rank = (cp.size, cp.rank) if cp is not None else (1, 0)
 
     def forward(self, q: torch.Tensor, layer_id: int, batch: Batch) -> torch.Tensor:
         raise TypeError("the MLA backend takes (q_lat, q_pe): call forward_mla")
@@ -74,8 +79,14 @@ class MLAAttnBackend(BaseAttnBackend):
         latent output [H, T_pad, kv_lora]."""
         md = batch.attn_metadata
         assert isinstance(md, MLAAttnMetadata)
+        group = None
+        if self.cp_size > 1:
+            import torch.distributed as dist
+
+            group = dist.group.WORLD
         return ops.mla_attention(q_lat, q_pe, self.kv.latent(layer_id), get_global_ctx().page_table, md.req_rows,
-                                 md.seq_lens, md.cu_q, self.page_size, self.scale)
+                                 md.seq_lens, md.cu_q, self.page_size, self.scale, cp_size=self.cp_size,
+                                 cp_rank=self.cp_rank, cp_group=group)
 
     def prepare_metadata(self, batch: Batch) -> None:
         reqs = batch.padded_reqs

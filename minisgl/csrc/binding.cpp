@@ -468,7 +468,8 @@ void grouped_gemm(at::Tensor out, const at::Tensor& x, const at::Tensor& w, int6
 
 void mla_prepare(at::Tensor q_pe, at::Tensor xs, const at::Tensor& q, const at::Tensor& kv_a, const at::Tensor& norm_w,
                  double eps, const at::Tensor& positions, const at::Tensor& cos_sin, at::Tensor latent,
-                 const at::Tensor& out_loc, int64_t T_pad, const c10::optional<at::Tensor>& err) {
+                 const at::Tensor& out_loc, int64_t T_pad, const c10::optional<at::Tensor>& err, int64_t cp_size,
+                 int64_t cp_rank) {
   check_cuda(q, "q");
   MSG_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2) && q.scalar_type() == at::kBFloat16,
             "mla_prepare: q [T, H, nope + rope] bf16 with packed heads");
@@ -507,6 +508,8 @@ void mla_prepare(at::Tensor q_pe, at::Tensor xs, const at::Tensor& q, const at::
   a.nope = static_cast<int>(nope);
   a.kv_lora = static_cast<int>(kv_lora);
   a.rope = static_cast<int>(rope);
+  a.cp_size = static_cast<int>(cp_size);
+  a.cp_rank = static_cast<int>(cp_rank);
   a.err = err_ptr(err);
   minisgl::launch_mla_prepare(a, stream_of(q));
 }
@@ -515,7 +518,8 @@ void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_
                    const at::Tensor& page_table, const at::Tensor& req_rows, const at::Tensor& seq_lens,
                    const at::Tensor& cu_q, int64_t page_size, double scale, int64_t splits,
                    const c10::optional<at::Tensor>& part_o, const c10::optional<at::Tensor>& part_lse,
-                   const c10::optional<at::Tensor>& err, const c10::optional<at::Tensor>& trace) {
+                   const c10::optional<at::Tensor>& err, const c10::optional<at::Tensor>& trace, int64_t cp_size,
+                   int64_t cp_rank, bool combine_only) {
   check_cuda(q_lat, "q_lat");
   MSG_CHECK(q_lat.dim() == 3 && q_lat.is_contiguous() && q_lat.scalar_type() == at::kBFloat16,
             "mla_attention: q_lat [H, T_pad, kv_lora] bf16 contiguous");
@@ -552,10 +556,14 @@ void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_
   a.page_size = static_cast<int>(page_size);
   a.splits = static_cast<int>(splits);
   a.scale = static_cast<float>(scale);
-  if (splits > 1) {
+  a.cp_size = static_cast<int>(cp_size);
+  a.cp_rank = static_cast<int>(cp_rank);
+  MSG_CHECK(cp_size >= 1 && cp_rank >= 0 && cp_rank < cp_size, "mla_attention: cp_rank outside [0, cp_size)");
+  if (splits > 1 || cp_size > 1) {
+    const int64_t parts = splits * cp_size;
     MSG_CHECK(part_o.has_value() && part_lse.has_value() && part_o->scalar_type() == at::kFloat &&
-                  part_lse->scalar_type() == at::kFloat && part_o->numel() >= splits * T * H * q_lat.size(2) &&
-                  part_lse->numel() >= splits * T * H,
+                  part_lse->scalar_type() == at::kFloat && part_o->numel() >= parts * T * H * q_lat.size(2) &&
+                  part_lse->numel() >= parts * T * H,
               "mla_attention: fp32 split-KV scratch too small");
     a.part_o = part_o->data_ptr<float>();
     a.part_lse = part_lse->data_ptr<float>();
@@ -566,7 +574,8 @@ void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_
               "mla_attention: trace must be a CUDA int64 tensor of 512 slots");
     a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
   }
-  minisgl::launch_mla_attention(a, stream_of(q_lat));
+  if (combine_only) minisgl::launch_mla_combine(a, stream_of(q_lat));
+  else minisgl::launch_mla_attention(a, stream_of(q_lat));
 }
 
 void mla_heads_to_rows(at::Tensor out, const at::Tensor& in, int64_t T) {
@@ -980,11 +989,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("grouped_gemm", &grouped_gemm);
   m.def("mxfp4_quantize", &mxfp4_quantize);
   m.def("moe_experts_mxfp4", &moe_experts_mxfp4);
-  m.def("mla_prepare", &mla_prepare);
+  m.def("mla_prepare", &mla_prepare, py::arg("q_pe"), py::arg("xs"), py::arg("q"), py::arg("kv_a"),
+        py::arg("norm_w"), py::arg("eps"), py::arg("positions"), py::arg("cos_sin"), py::arg("latent"),
+        py::arg("out_loc"), py::arg("T_pad"), py::arg("err"), py::arg("cp_size") = 1, py::arg("cp_rank") = 0);
   m.def("mla_attention", &mla_attention, py::arg("out"), py::arg("q_lat"), py::arg("q_pe"), py::arg("latent"),
         py::arg("page_table"), py::arg("req_rows"), py::arg("seq_lens"), py::arg("cu_q"), py::arg("page_size"),
         py::arg("scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("err"),
-        py::arg("trace") = py::none());
+        py::arg("trace") = py::none(), py::arg("cp_size") = 1, py::arg("cp_rank") = 0,
+        py::arg("combine_only") = false);
   m.def("mla_heads_to_rows", &mla_heads_to_rows);
   m.def("mla_num_splits", [](int64_t T, int64_t H) { return minisgl::mla_num_splits(static_cast<int>(T), static_cast<int>(H)); });
   m.def("symm_create", &symm_create);

@@ -85,16 +85,18 @@ __global__ void __launch_bounds__(256) mla_prepare_kernel(MlaPrepareArgs a) {
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float rstd = rsqrtf(tot / kLora + a.eps);
   const int64_t slot = a.out_loc[t];
+  // context parallelism: the row lives on the rank owning its 64-key tile
+  const bool store = a.cp_size <= 1 || (a.positions[t] / kKeys) % a.cp_size == a.cp_rank;
   __nv_bfloat16* lat = reinterpret_cast<__nv_bfloat16*>(a.latent) + slot * kLat;
   const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
   {
     __nv_bfloat162 o;  // x * rstd * w in fp32, one rounding
     o.x = __float2bfloat16_rn(v0 * rstd * __bfloat162float(nw[2 * tid]));
     o.y = __float2bfloat16_rn(v1 * rstd * __bfloat162float(nw[2 * tid + 1]));
-    *reinterpret_cast<__nv_bfloat162*>(lat + 2 * tid) = o;
+    if (store) *reinterpret_cast<__nv_bfloat162*>(lat + 2 * tid) = o;
   }
   const float* cs = a.cos_sin + static_cast<int64_t>(a.positions[t]) * kRope;
-  if (tid < kRope / 2) {
+  if (store && tid < kRope / 2) {
     const float c = cs[tid], s = cs[kRope / 2 + tid];
     const float x0 = __bfloat162float(kva[kLora + 2 * tid]), x1 = __bfloat162float(kva[kLora + 2 * tid + 1]);
     __nv_bfloat162 o;
@@ -221,10 +223,15 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
 
   int row = 0, len = 0;
   mla_token(a, t, row, len);
-  const int ntiles_all = (max(len, 0) + kKeys - 1) / kKeys;
+  // context parallelism: this rank owns the 64-key tiles t with
+  // t % cp_size == cp_rank; local tile j is global tile cp_rank + cp_size j
+  const int cp = a.cp_size > 1 ? a.cp_size : 1, cpr = a.cp_size > 1 ? a.cp_rank : 0;
+  const int ntiles_glob = (max(len, 0) + kKeys - 1) / kKeys;
+  const int ntiles_all = ntiles_glob > cpr ? (ntiles_glob - cpr + cp - 1) / cp : 0;
   const int per = (ntiles_all + a.splits - 1) / a.splits;
   const int tile0 = split * per;
   const int n = max(0, min(ntiles_all, tile0 + per) - tile0);
+  auto tile_pos = [&](int j) { return (cpr + cp * (tile0 + j)) * kKeys; };  // first key of local tile j
   const ErrorSink err{a.err};
   const bool traced = a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0;
   int issued = 0;  // latent tiles whose copies the producer started
@@ -245,9 +252,8 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       const int P = a.page_size;
       const int seg = P < kKeys ? P : kKeys;
       const int segs = kKeys / seg;  // segments per tile
-      const int pos0 = tile0 * kKeys;
       auto page_of = [&](int k) {  // page id of segment k (positions past the end: page 0, masked later)
-        const int pos = pos0 + k * seg;
+        const int pos = tile_pos(k / segs) + (k % segs) * seg;
         return pos < len ? pt[pos] / P : 0;
       };
       int base = 0;
@@ -269,7 +275,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
           if (traced && j < 64) a.trace[j * 8 + 0] = globaltimer_ns();
         }
         uint8_t* st = sKV + s * kKvBytes;
-        const int p0 = (tile0 + j) * kKeys;
+        const int p0 = tile_pos(j);
         for (int q = 0; q < segs; ++q) {
           const int k = j * segs + q;
           if (k >= base + 32) {  // slide the window (warp-uniform)
@@ -389,7 +395,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[b]);
-      const int p0 = (tile0 + i) * kKeys;
+      const int p0 = tile_pos(i);
       const int valid = min(kKeys, len - p0);
       if (valid < kKeys) {
 #pragma unroll
@@ -489,7 +495,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       }
       if (h >= a.H) continue;
       const int d0 = half * 256 + c * 32;
-      if (a.splits == 1) {
+      if (a.splits == 1 && cp == 1) {
         __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (static_cast<int64_t>(h) * a.T_pad + t) * kLora + d0;
 #pragma unroll
         for (int q4 = 0; q4 < 4; ++q4) {
@@ -501,15 +507,16 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
           *reinterpret_cast<uint4*>(dst + q4 * 8) = v;
         }
       } else {
-        float* dst = a.part_o + ((static_cast<int64_t>(split) * a.T + t) * a.H + h) * kLora + d0;
+        float* dst = a.part_o + ((static_cast<int64_t>(cpr * a.splits + split) * a.T + t) * a.H + h) * kLora + d0;
 #pragma unroll
         for (int q4 = 0; q4 < 8; ++q4)
           *reinterpret_cast<float4*>(dst + q4 * 4) = make_float4(u2f(ov[q4 * 4]) * inv, u2f(ov[q4 * 4 + 1]) * inv,
                                                                  u2f(ov[q4 * 4 + 2]) * inv, u2f(ov[q4 * 4 + 3]) * inv);
       }
     }
-    if (a.splits > 1 && lower && h < a.H)
-      a.part_lse[(static_cast<int64_t>(split) * a.T + t) * a.H + h] = live && l_row > 0.f ? m_row + log2f(l_row) : -INFINITY;
+    if ((a.splits > 1 || cp > 1) && lower && h < a.H)
+      a.part_lse[(static_cast<int64_t>(cpr * a.splits + split) * a.T + t) * a.H + h] =
+          live && l_row > 0.f ? m_row + log2f(l_row) : -INFINITY;
   }
   tc_fence_before();
   __syncthreads();
@@ -532,10 +539,11 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(MlaAttnArgs a) {
   pdl_wait();
   const int t = blockIdx.x, h = blockIdx.y;
   float mx = -INFINITY;
-  for (int s = 0; s < a.splits; ++s) mx = fmaxf(mx, a.part_lse[(static_cast<int64_t>(s) * a.T + t) * a.H + h]);
+  const int parts = a.splits * (a.cp_size > 1 ? a.cp_size : 1);  // every rank's splits
+  for (int s = 0; s < parts; ++s) mx = fmaxf(mx, a.part_lse[(static_cast<int64_t>(s) * a.T + t) * a.H + h]);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   float wsum = 0.f;
-  for (int s = 0; s < a.splits; ++s) {
+  for (int s = 0; s < parts; ++s) {
     const float lse = a.part_lse[(static_cast<int64_t>(s) * a.T + t) * a.H + h];
     if (lse == -INFINITY) continue;
     const float w = exp2f(lse - mx);
@@ -582,8 +590,11 @@ void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s) {
   const int P = a.page_size;
   if (!(P == 8 || P == 16 || (P > 0 && P % 32 == 0)))
     throw std::runtime_error("minisgl.mla_attention: page_size must be 8, 16 or a multiple of 32");
-  if (a.splits < 1 || a.splits > 16 || (a.splits > 1 && (a.part_o == nullptr || a.part_lse == nullptr)))
+  const bool partials = a.splits > 1 || a.cp_size > 1;
+  if (a.splits < 1 || a.splits > 16 || (partials && (a.part_o == nullptr || a.part_lse == nullptr)))
     throw std::runtime_error("minisgl.mla_attention: splits in [1, 16] with partial buffers");
+  if (a.cp_size > 1 && (a.cp_rank < 0 || a.cp_rank >= a.cp_size))
+    throw std::runtime_error("minisgl.mla_attention: cp_rank outside [0, cp_size)");
   if (a.T_pad < a.T || a.B <= 0 || a.H <= 0) throw std::runtime_error("minisgl.mla_attention: bad shapes");
   static bool smem_set = false;
   if (!smem_set) {
@@ -604,7 +615,14 @@ void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s) {
                                 : make_tmap_bf16_2d_sw128(a.latent, static_cast<uint64_t>(a.num_slots), kLat, kLat, seg);
   dim3 grid(a.splits, a.T, (a.H + kHeadsCta - 1) / kHeadsCta);
   launch_pdl(mla_attn_kernel, grid, dim3(kMlaThreads), kMlaSmem, s, tq, tp, tl, a);
-  if (a.splits > 1) launch_pdl(mla_combine_kernel, dim3(a.T, a.H), dim3(128), 0, s, a);
+  // context parallelism: the partials of every rank are merged after the
+  // caller has gathered them (launch_mla_combine)
+  if (a.splits > 1 && a.cp_size <= 1) launch_pdl(mla_combine_kernel, dim3(a.T, a.H), dim3(128), 0, s, a);
+}
+
+void launch_mla_combine(const MlaAttnArgs& a, cudaStream_t s) {
+  if (a.T <= 0) return;
+  launch_pdl(mla_combine_kernel, dim3(a.T, a.H), dim3(128), 0, s, a);
 }
 
 }  // namespace minisgl

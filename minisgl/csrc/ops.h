@@ -171,6 +171,7 @@ struct MlaPrepareArgs {
   void* q_pe;             // out: [T, H, rope]
   void* xs;               // out: [H, T_pad, nope] (grouped GEMM input)
   int T, T_pad, H, nope, kv_lora, rope;
+  int cp_size, cp_rank;   // context parallelism: store only rows of owned 64-key tiles
   int* err;
 };
 struct MlaAttnArgs {
@@ -189,6 +190,10 @@ struct MlaAttnArgs {
   int B, T, T_pad, H, page_size, splits;
   float scale;
   int* err;
+  // context parallelism: this rank attends over the 64-key tiles t with
+  // t % cp_size == cp_rank and writes partials [cp_size * splits, T, H, ...]
+  // at slots cp_rank * splits + split (merged by launch_mla_combine)
+  int cp_size, cp_rank;
   // optional per-tile timestamps (%globaltimer ns) of CTA (0, 0, 0), 8 slots
   // per tile: 0 copy issued, 1 QK issued, 2 scores seen, 3 P written,
   // 4 PV issued, 5 PV seen complete
@@ -196,6 +201,7 @@ struct MlaAttnArgs {
 };
 void launch_mla_prepare(const MlaPrepareArgs& a, cudaStream_t s);
 void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s);
+void launch_mla_combine(const MlaAttnArgs& a, cudaStream_t s);
 void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, cudaStream_t s);
 int mla_num_splits(int T, int H);
 

@@ -27,7 +27,7 @@ from minisgl.layers import set_rope_device
 from minisgl.utils import fault
 from minisgl.models import create_model, load_weight, random_weights
 from minisgl.moe import create_moe_backend
-from minisgl.parallel import destroy_distributed, get_tp_info, reset_tp_info, set_tp_info
+from minisgl.parallel import destroy_distributed, get_tp_info, reset_cp_info, reset_tp_info, set_cp_info, set_tp_info
 from minisgl.utils import align_ceil, init_logger, torch_dtype
 
 from .config import EngineConfig
@@ -68,7 +68,17 @@ def _valid_page(p: int) -> bool:
 
 class Engine:
     def __init__(self, config: EngineConfig) -> None:
-        set_tp_info(config.tp_info.rank, config.tp_info.size)
+        if config.cp_size > 1:
+            # context parallelism: every rank holds the whole model and the
+            # attention over the KV tiles it owns; layers see one TP rank
+            if config.tp_info.size != config.cp_size:
+                raise ValueError("context parallelism runs over all ranks: tp_size must equal cp_size")
+            if not config.model_config.is_mla:
+                raise ValueError("context parallelism is implemented for MLA models (DeepSeek-V3 / Kimi-K2)")
+            set_tp_info(0, 1)
+            set_cp_info(config.tp_info.rank, config.cp_size)
+        else:
+            set_tp_info(config.tp_info.rank, config.tp_info.size)
         self.config = config
         self.device = _resolve_device(config)
         self.is_cuda = self.device.type == "cuda"
@@ -213,7 +223,7 @@ class Engine:
                                 init_method=config.distributed_addr,
                                 device_id=self.device if self.is_cuda else None)
         self._owns_pg = True
-        if self.is_cuda and config.comm == "fused":
+        if self.is_cuda and config.comm == "fused" and config.cp_size <= 1:
             from minisgl.parallel.symm import enable_symm_comm
 
             enable_symm_comm(self.device, config.max_forward_len * config.model_config.hidden_size
@@ -316,3 +326,4 @@ class Engine:
             dist.destroy_process_group()
         reset_global_ctx()
         reset_tp_info()
+        reset_cp_info()

@@ -95,11 +95,13 @@ class MLAAttention(BaseOP):
         else:
             q = self.q_proj.forward(x)
         kv_a = self.kv_a_proj_with_mqa.forward(x)
+        backend = ctx.attn_backend
         q_lat, q_pe = ops.mla_prepare(q.view(T, self.heads, self.nope + self.rope_dim), kv_a, self._w_uk_t,
                                       self.kv_a_layernorm.weight, self.eps, batch.positions,
                                       self._rotary.cos_sin_cache, ctx.kv_cache.latent(self._layer_id),
-                                      batch.out_loc, ctx.page_size)
-        o_lat = ctx.attn_backend.forward_mla(q_lat, q_pe, self._layer_id, batch)
+                                      batch.out_loc, ctx.page_size, getattr(backend, "cp_size", 1),
+                                      getattr(backend, "cp_rank", 0))
+        o_lat = backend.forward_mla(q_lat, q_pe, self._layer_id, batch)
         return self.o_proj.forward(ops.mla_output(o_lat, self._w_uv, T))
 
 

@@ -359,14 +359,15 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor, tile: int, out: Optional[torc
 
 def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_w: torch.Tensor, eps: float,
                 positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
-                page_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
+                page_size: int, cp_size: int = 1, cp_rank: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
     """MLA before attention: the normalised, rotated latent rows go into the
     cache; returns (q_lat [H, T_pad, kv_lora] head-major, q_pe [T, H, rope]).
     On the GPU one kernel writes the cache row, the rotated q_pe and q_nope
     head-major, then a grouped GEMM (heads as groups) absorbs q_nope through
     W_UK; rows past T of q_lat are padding."""
     if not q.is_cuda:
-        return ref.mla_prepare(q, kv_a, w_uk_t, norm_w, eps, positions, cos_sin, latent, out_loc, page_size)
+        return ref.mla_prepare(q, kv_a, w_uk_t, norm_w, eps, positions, cos_sin, latent, out_loc, page_size,
+                               cp_size, cp_rank)
     T, H, qk = q.shape
     kv_lora, nope = w_uk_t.shape[1], w_uk_t.shape[2]
     rope = qk - nope
@@ -376,7 +377,7 @@ def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_
     q_pe = torch.empty(T, H, rope, dtype=q.dtype, device=q.device)
     _count()
     native().mla_prepare(q_pe, xs, q, kv_a, norm_w, eps, positions, cos_sin, latent, out_loc, T_pad,
-                         error_word(q.device))
+                         error_word(q.device), cp_size, cp_rank)
     return grouped_gemm(xs, w_uk_t, tile), q_pe
 
 
@@ -409,6 +410,9 @@ def mla_attention(
     scale: float,
     splits: int = 0,
     trace: Optional[torch.Tensor] = None,
+    cp_size: int = 1,
+    cp_rank: int = 0,
+    cp_group=None,
 ) -> torch.Tensor:
     """Causal absorbed MLA over the paged latent cache of one layer:
     q_lat [H, T_pad, kv_lora] + q_pe [T, H, rope] -> [H, T_pad, kv_lora]
@@ -416,6 +420,9 @@ def mla_attention(
     tokens). ``trace``: optional int64 [512] device tensor that receives
     per-tile phase timestamps of the first CTA (copy issued, QK issued,
     scores seen, P written, PV issued, PV seen complete; 8 slots a tile)."""
+    if cp_size > 1:
+        return _mla_attention_cp(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale,
+                                 splits, cp_size, cp_rank, cp_group)
     if not q_lat.is_cuda:
         return ref.mla_attention(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale)
     H, T_pad, kv_lora = q_lat.shape
@@ -425,16 +432,56 @@ def mla_attention(
     out = torch.empty_like(q_lat)
     part_o = part_lse = None
     if splits > 1:
-        need = splits * T * H * (kv_lora + 1)
-        buf = _MLA_SCRATCH.get(q_lat.device)
-        if buf is None or buf.numel() < need:
-            buf = torch.empty(max(need, 148 * 64 * (kv_lora + 1)), dtype=torch.float32, device=q_lat.device)
-            _MLA_SCRATCH[q_lat.device] = buf
-        part_o = buf[: splits * T * H * kv_lora]
-        part_lse = buf[splits * T * H * kv_lora: need]
+        part_o, part_lse = _mla_partials(splits, T, H, kv_lora, q_lat.device)
     _count(2 if splits > 1 else 1)
     nat.mla_attention(out, q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits,
                       part_o, part_lse, error_word(q_lat.device), trace)
+    return out
+
+
+def _mla_partials(parts: int, T: int, H: int, kv_lora: int, device: torch.device):
+    """fp32 partial outputs [parts, T, H, kv_lora] and log-sum-exps
+    [parts, T, H] (one cached buffer per device)."""
+    need = parts * T * H * (kv_lora + 1)
+    buf = _MLA_SCRATCH.get(device)
+    if buf is None or buf.numel() < need:
+        buf = torch.empty(max(need, 148 * 64 * (kv_lora + 1)), dtype=torch.float32, device=device)
+        _MLA_SCRATCH[device] = buf
+    return buf[: parts * T * H * kv_lora], buf[parts * T * H * kv_lora: need]
+
+
+def _mla_attention_cp(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits, cp_size,
+                      cp_rank, cp_group):
+    """Context-parallel MLA: each rank attends over the 64-key tiles it holds
+    (tile t on rank t % cp), the partial outputs and log-sum-exps of all
+    ranks are all-gathered (in place) and merged."""
+    import torch.distributed as dist
+
+    H, T_pad, kv_lora = q_lat.shape
+    T = q_pe.shape[0]
+    if not q_lat.is_cuda:
+        o, lse = ref.mla_attention_partial(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size,
+                                           scale, cp_size, cp_rank)
+        os_ = [torch.empty_like(o) for _ in range(cp_size)]
+        ls_ = [torch.empty_like(lse) for _ in range(cp_size)]
+        dist.all_gather(os_, o.contiguous(), group=cp_group)
+        dist.all_gather(ls_, lse.contiguous(), group=cp_group)
+        merged = ref.merge_partials(torch.stack(os_), torch.stack(ls_)).to(q_lat.dtype)
+        out = torch.zeros_like(q_lat)
+        out[:, :T] = merged.transpose(0, 1)
+        return out
+    nat = native()
+    splits = splits or max(1, nat.mla_num_splits(T, H) // cp_size)
+    part_o, part_lse = _mla_partials(splits * cp_size, T, H, kv_lora, q_lat.device)
+    out = torch.empty_like(q_lat)
+    _count(2)
+    nat.mla_attention(out, q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits,
+                      part_o, part_lse, error_word(q_lat.device), None, cp_size, cp_rank, False)
+    per_o, per_l = splits * T * H * kv_lora, splits * T * H
+    dist.all_gather_into_tensor(part_o, part_o[cp_rank * per_o:(cp_rank + 1) * per_o], group=cp_group)
+    dist.all_gather_into_tensor(part_lse, part_lse[cp_rank * per_l:(cp_rank + 1) * per_l], group=cp_group)
+    nat.mla_attention(out, q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits,
+                      part_o, part_lse, error_word(q_lat.device), None, cp_size, cp_rank, True)
     return out
 
 

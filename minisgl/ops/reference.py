@@ -197,9 +197,17 @@ def rope_interleaved(x: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Te
     return out.to(x.dtype)
 
 
+CP_TILE = 64  # keys per context-parallel ownership unit: tile t belongs to rank t % cp
+
+
+def cp_owned(positions: torch.Tensor, cp_size: int, cp_rank: int) -> torch.Tensor:
+    """Which key positions this context-parallel rank holds."""
+    return (positions.long() // CP_TILE) % cp_size == cp_rank
+
+
 def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_w: torch.Tensor, eps: float,
                 positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
-                page_size: int) -> Tuple[torch.Tensor, torch.Tensor]:
+                page_size: int, cp_size: int = 1, cp_rank: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
     """Latent row [rmsnorm(c_kv) | rope(k_pe)] of every token into the paged
     cache; returns the absorbed queries as (q_lat [H, T, kv_lora] = q_nope
     W_UK per head, head-major; q_pe [T, H, rope] rotated). w_uk_t is
@@ -211,7 +219,11 @@ def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_
     c = rmsnorm(kv_a[:, :kv_lora], norm_w, eps)
     k_pe = rope_interleaved(kv_a[:, kv_lora:], positions, cos_sin)
     loc = out_loc.long()
-    latent[loc // page_size, loc % page_size] = torch.cat([c, k_pe], dim=-1).to(latent.dtype)
+    rows = torch.cat([c, k_pe], dim=-1).to(latent.dtype)
+    if cp_size > 1:  # the row lives on the rank that owns its 64-key tile
+        keep = cp_owned(positions, cp_size, cp_rank)
+        loc, rows = loc[keep], rows[keep]
+    latent[loc // page_size, loc % page_size] = rows
     q_pe = rope_interleaved(q[..., nope:], positions, cos_sin).contiguous()
     q_lat = torch.einsum("thn,hcn->htc", q[..., :nope].float(), w_uk_t.float()).to(q.dtype)
     return q_lat, q_pe
@@ -222,6 +234,51 @@ def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int) -> torch.Tensor:
     W_UV [H, v, kv_lora] -> [T, H * v]."""
     o = torch.einsum("htc,hvc->thv", o_lat[:, :T].float(), w_uv.float())
     return o.reshape(T, -1).to(o_lat.dtype)
+
+
+def mla_attention_partial(q_lat: torch.Tensor, q_pe: torch.Tensor, latent: torch.Tensor, page_table: torch.Tensor,
+                          req_rows: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor, page_size: int,
+                          scale: float, cp_size: int, cp_rank: int) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Causal absorbed MLA over the keys this context-parallel rank holds:
+    (o [T, H, kv_lora] normalised over those keys, lse [T, H] natural log;
+    -inf and zeros where the rank holds none of a token's keys)."""
+    T, H, _ = q_pe.shape
+    kv_lora = q_lat.shape[2]
+    q = torch.cat([q_lat[:, :T].transpose(0, 1), q_pe], dim=-1).float()
+    D = q.shape[-1]
+    o = torch.zeros(T, H, kv_lora, dtype=torch.float32, device=q.device)
+    lse = torch.full((T, H), float("-inf"), dtype=torch.float32, device=q.device)
+    rows, lens, cu = req_rows.tolist(), seq_lens.tolist(), cu_q.tolist()
+    for b, (row, L) in enumerate(zip(rows, lens)):
+        s, e = cu[b], cu[b + 1]
+        n = e - s
+        if n == 0 or L <= 0:
+            continue
+        pos = torch.arange(L, device=q.device)
+        mine = cp_owned(pos, cp_size, cp_rank)
+        if not bool(mine.any()):
+            continue
+        kv = latent.reshape(-1, D)[page_table[row, :L].long()].float()
+        scores = torch.einsum("nhd,ld->nhl", q[s:e], kv) * scale
+        qpos = torch.arange(L - n, L, device=q.device)
+        mask = (pos[None, :] > qpos[:, None]) | ~mine[None, :]
+        scores = scores.masked_fill(mask[:, None, :], float("-inf"))
+        m = scores.amax(dim=-1, keepdim=True)
+        has = torch.isfinite(m)
+        p = torch.where(has, torch.exp(scores - torch.where(has, m, torch.zeros_like(m))), torch.zeros_like(scores))
+        l = p.sum(-1, keepdim=True)
+        o[s:e] = torch.where(has, torch.einsum("nhl,lc->nhc", p, kv[:, :kv_lora]) / l.clamp_min(1e-30), 0.0)
+        lse[s:e] = torch.where(has, m + torch.log(l.clamp_min(1e-30)), torch.full_like(m, float("-inf")))[..., 0]
+    return o, lse
+
+
+def merge_partials(o: torch.Tensor, lse: torch.Tensor) -> torch.Tensor:
+    """o [R, T, H, C], lse [R, T, H] (natural log) -> the softmax-weighted
+    merge [T, H, C] over the R parts."""
+    m = lse.amax(dim=0, keepdim=True)
+    w = torch.where(torch.isfinite(lse), torch.exp(lse - torch.where(torch.isfinite(m), m, torch.zeros_like(m))),
+                    torch.zeros_like(lse))
+    return (o * w[..., None]).sum(0) / w.sum(0)[..., None].clamp_min(1e-30)
 
 
 def mla_attention(

@@ -43,3 +43,23 @@ def reset_tp_info() -> None:
     """Forget the rank (tests and in-process engine restarts)."""
     global _TP
     _TP = None
+
+
+# Context parallelism: the ranks of the process group split each sequence's
+# KV (attention over the latent cache) while every other layer is replicated;
+# layers then see a tensor-parallel size of 1.
+_CP: Optional[DistributedInfo] = None
+
+
+def set_cp_info(rank: int, size: int) -> None:
+    global _CP
+    _CP = DistributedInfo(rank, size) if size > 1 else None
+
+
+def get_cp_info() -> Optional[DistributedInfo]:
+    return _CP
+
+
+def reset_cp_info() -> None:
+    global _CP
+    _CP = None

@@ -135,7 +135,13 @@ def parse_args(args: List[str], run_shell: bool = False) -> Tuple[ServerArgs, bo
     kw["dtype"] = _DTYPES[dtype] if isinstance(dtype, str) else dtype
     if kw["dtype"] == torch.float32 and kw["device"] != "cpu":
         kw["dtype"] = torch.bfloat16  # the GPU kernels run bf16
-    kw["tp_info"] = DistributedInfo(0, kw.pop("tensor_parallel_size"))
+    ranks = kw.pop("tensor_parallel_size")
+    if kw.get("cp_size", 1) > 1:
+        # context parallelism spans every rank (layers replicated, KV split)
+        if ranks not in (1, kw["cp_size"]):
+            raise SystemExit("--cp-size runs over all ranks: leave --tp at 1 or set it equal to --cp-size")
+        ranks = kw["cp_size"]
+    kw["tp_info"] = DistributedInfo(0, ranks)
     result = ServerArgs(**kw)
     init_logger(__name__).info(f"Parsed arguments:\n{result}")
     return result, run_shell

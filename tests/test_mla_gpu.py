@@ -145,3 +145,55 @@ def test_small_kimi_engine_matches_oracle(cuda_graph):
     # bf16 engine vs fp32 oracle: a near-tie of the random-init logits may
     # flip a token and the sequence then diverges; a broken kernel scrambles all
     assert firsts >= 3 and same >= 0.6 * 24, (firsts, same)
+
+
+@pytest.mark.parametrize("cp,splits", [(2, 1), (3, 2)])
+def test_mla_context_parallel_partials_merge(cp, splits):
+    """Every context-parallel rank's partials (emulated on one GPU: ranks
+    write their slots of one partial buffer, no collective), merged by the
+    combine kernel, equal the single-rank attention; prepare stores only the
+    rows of owned 64-key tiles."""
+    lens = [1, 64, 65, 200, 777]
+    H, page_size = 64, 64
+    latent, pt, rows, sl, cu, q_lat, q_pe = _case(lens, [1] * len(lens), H, page_size, seed=cp)
+    scale = 192 ** -0.5
+    d = lambda t: t.to(DEV)  # noqa: E731
+    T = len(lens)
+    tile = 16
+    T_pad = (T + tile - 1) // tile * tile
+    ql = torch.zeros(H, T_pad, 512, dtype=torch.bfloat16)
+    ql[:, :T] = q_lat
+    args = (d(ql), d(q_pe), d(latent), d(pt), d(rows), d(sl), d(cu), page_size, scale)
+    want = ops.mla_attention(*args, splits=1)
+    part_o, part_lse = ops._mla_partials(cp * splits, T, H, 512, torch.device(DEV))
+    out = torch.empty_like(want)
+    nat = ops.native()
+    err = ops.error_word(torch.device(DEV))
+    for r in range(cp):
+        nat.mla_attention(out, *args, splits, part_o, part_lse, err, None, cp, r, False)
+    nat.mla_attention(out, *args, splits, part_o, part_lse, err, None, cp, 0, True)
+    torch.cuda.synchronize()
+    ops.check_device_errors(torch.device(DEV))
+    _close(out[:, :T].cpu(), want[:, :T].cpu(), 2e-2)
+
+
+def test_mla_prepare_context_parallel_stores_owned_rows():
+    g = torch.Generator().manual_seed(9)
+    T, H = 200, 16
+    bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
+    q = bf(torch.randn(T, H, 192, generator=g))
+    kv_a = bf(torch.randn(T, 576, generator=g))
+    w_uk_t = bf(torch.randn(H, 512, 128, generator=g) * 0.05)
+    norm_w = bf(torch.ones(512))
+    positions = torch.arange(T, dtype=torch.int32)
+    cos_sin = torch.randn(4096, 64)
+    out_loc = torch.arange(T, dtype=torch.int32)
+    d = lambda t: t.to(DEV)  # noqa: E731
+    lat = d(torch.zeros(4, 64, 576, dtype=torch.bfloat16))
+    ops.mla_prepare(d(q), d(kv_a), d(w_uk_t), d(norm_w), 1e-6, d(positions), d(cos_sin), lat, d(out_loc), 64,
+                    cp_size=2, cp_rank=1)
+    torch.cuda.synchronize()
+    flat = lat.view(-1, 576).cpu()
+    owned = (torch.arange(T) // 64) % 2 == 1
+    assert torch.all(flat[:T][~owned] == 0)
+    assert torch.all(flat[:T][owned].abs().sum(-1) > 0)
