@@ -65,7 +65,8 @@ class EngineConfig:
         from minisgl.models import ModelConfig
 
         cfg = ModelConfig.from_hf(self.hf_config)
-        ep = self.ep_size if self.ep_size > 1 else 1
+        # DP attention splits the routed experts over every rank
+        ep = self.tp_info.size if self.enable_dp_attention else (self.ep_size if self.ep_size > 1 else 1)
         return dataclasses.replace(cfg, moe_quant=self.moe_quant, ep_size=ep,
                                    ep_rank=self.tp_info.rank % ep if ep > 1 else 0)
 

@@ -27,7 +27,8 @@ from minisgl.layers import set_rope_device
 from minisgl.utils import fault
 from minisgl.models import create_model, load_weight, random_weights
 from minisgl.moe import create_moe_backend
-from minisgl.parallel import destroy_distributed, get_tp_info, reset_cp_info, reset_tp_info, set_cp_info, set_tp_info
+from minisgl.parallel import (destroy_distributed, get_tp_info, reset_cp_info, reset_dp_info, reset_tp_info, set_cp_info,
+                              set_dp_info, set_tp_info)
 from minisgl.utils import align_ceil, init_logger, torch_dtype
 
 from .config import EngineConfig
@@ -77,8 +78,19 @@ class Engine:
                 raise ValueError("context parallelism is implemented for MLA models (DeepSeek-V3 / Kimi-K2)")
             set_tp_info(0, 1)
             set_cp_info(config.tp_info.rank, config.cp_size)
+        elif config.enable_dp_attention and config.tp_info.size > 1:
+            # DP attention: replicated layers, experts split and tokens
+            # dispatched to them (minisgl/moe/ep_a2a.py)
+            if config.cp_size > 1:
+                raise ValueError("DP attention and context parallelism are exclusive")
+            set_tp_info(0, 1)
+            set_dp_info(config.tp_info.rank, config.tp_info.size)
         else:
+            if config.ep_size > 1 and config.ep_size != config.tp_info.size:
+                raise ValueError("expert parallelism runs over the tensor-parallel ranks: ep_size must equal "
+                                 "tp_size (or use --enable-dp-attention)")
             set_tp_info(config.tp_info.rank, config.tp_info.size)
+        self.dp = config.enable_dp_attention and config.tp_info.size > 1
         self.config = config
         self.device = _resolve_device(config)
         self.is_cuda = self.device.type == "cuda"
@@ -128,7 +140,9 @@ class Engine:
         self.ctx.attn_backend = self.attn_backend = create_attention_backend(
             config.attention_backend, mcfg, config.max_running_req + 1)
         if mcfg.is_moe:
-            self.ctx.moe_backend = self.moe_backend = create_moe_backend(config.moe_backend)
+            self.ctx.moe_backend = self.moe_backend = create_moe_backend(
+                config.moe_backend, ep_dispatch=self.dp, ep_size=mcfg.ep_size, ep_rank=mcfg.ep_rank,
+                group=self.tp_cpu_group if not self.is_cuda else None)
         self.sampler = Sampler(self.device, mcfg.vocab_size, config.weight_seed)
         if self.is_cuda:
             from minisgl import ops
@@ -152,8 +166,8 @@ class Engine:
 
     # ---------------------------------------------------------------- setup
     def _graph_max_bs(self, config: EngineConfig) -> Optional[int]:
-        if not self.is_cuda:
-            return 0
+        if not self.is_cuda or self.dp:
+            return 0  # DP attention: the token dispatch has host-side row counts
         mx = config.cuda_graph_max_bs
         if mx is None:
             return min(config.max_running_req, 256)
@@ -235,8 +249,8 @@ class Engine:
             return random_weights(self.model.state_dict(), self.device, seed=config.weight_seed,
                                   gen_device=config.dummy_weight_device)
         out: Dict[str, torch.Tensor] = {}
-        for name, t in load_weight(config.model_path, self.device, ep_size=config.ep_size,
-                                   ep_rank=config.tp_info.rank if config.ep_size > 1 else 0):
+        mcfg = config.model_config
+        for name, t in load_weight(config.model_path, self.device, ep_size=mcfg.ep_size, ep_rank=mcfg.ep_rank):
             keep_fp32 = t.dtype == torch.float32 and "correction_bias" in name
             out[name] = t if keep_fp32 else t.to(self.dtype)
         return out
@@ -327,3 +341,4 @@ class Engine:
         reset_global_ctx()
         reset_tp_info()
         reset_cp_info()
+        reset_dp_info()

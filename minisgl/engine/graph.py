@@ -122,12 +122,12 @@ class GraphRunner:
         logger.info_rank0(f"CUDA graphs ready; free memory {mem_GB(get_free_memory(self.device))}")
 
     def can_use_cuda_graph(self, batch: Batch) -> bool:
-        return batch.is_decode and batch.size <= self.max_graph_bs
+        return batch.is_decode and max(batch.size, 1) <= self.max_graph_bs
 
     def pad_batch(self, batch: Batch) -> None:
-        size = batch.size
+        size = max(batch.size, 1)  # an empty batch (a DP rank's filler step) runs the dummy request
         if self.can_use_cuda_graph(batch):
-            size = next(b for b in self.graph_bs_list if b >= batch.size)
+            size = next(b for b in self.graph_bs_list if b >= size)
         batch.padded_reqs = batch.reqs + [self.dummy_req] * (size - batch.size)
 
     def _load_inputs(self, batch: Batch) -> int:

@@ -1,10 +1,12 @@
 """Routed-expert MLP layer (experts sharded over TP on the intermediate dim,
 or distributed over ranks with expert parallelism), bf16 or MXFP4.
 
-Expert parallelism runs over the tensor-parallel ranks: attention is
-replicated, every rank routes all tokens over all experts, runs only the
-experts it holds (the others are dropped by the align kernel) and the
-partial sums meet in the same all-reduce tensor parallelism needs."""
+Expert parallelism over the tensor-parallel ranks: every rank routes all
+tokens over all experts, runs only the experts it holds (the others are
+dropped by the align kernel) and the partial sums meet in the same
+all-reduce tensor parallelism needs. With DP attention the tokens differ per
+rank and are dispatched to the experts' owners instead
+(minisgl/moe/ep_a2a.py)."""
 
 from __future__ import annotations
 
@@ -28,8 +30,6 @@ class MoELayer(BaseOP):
                  has_correction_bias: bool = False, reduce_results: bool = True, quant: str = "none",
                  ep_size: int = 1, ep_rank: int = 0) -> None:
         tp = get_tp_info().size
-        if ep_size > 1 and ep_size != tp:
-            raise ValueError("expert parallelism runs over the tensor-parallel ranks: ep_size must equal tp_size")
         if quant not in ("none", "mxfp4"):
             raise ValueError(f"unknown expert quantisation {quant!r}")
         self.num_experts = num_experts

@@ -72,19 +72,37 @@ class LLM(Scheduler):
     def run_when_idle(self) -> None:
         self.cache_manager.check_integrity()
 
+    def dp_has_pending(self) -> bool:
+        return bool(self.pending_requests)
+
+    def dp_all_idle(self) -> None:
+        raise RequestAllFinished()
+
     def generate(self, prompts: Sequence[Prompt],
                  sampling_params: Union[SamplingParams, Sequence[SamplingParams]]) -> List[Dict[str, object]]:
         self.pending_requests, self.status_map, self.counter = [], {}, 0
         if isinstance(sampling_params, SamplingParams):
             sampling_params = [sampling_params] * len(prompts)
-        self.pending_requests = [(p, SamplingParams(**vars(sp))) for p, sp in zip(prompts, sampling_params)]
+        jobs = list(enumerate(zip(prompts, sampling_params)))
+        dp = self.engine.dp
+        if dp:  # DP attention: rank r serves prompts r, r + R, ...; results are gathered at the end
+            rank, world = self.config.tp_info.rank, self.config.tp_info.size
+            jobs = jobs[rank::world]
+        self.pending_requests = [(p, SamplingParams(**vars(sp))) for _, (p, sp) in jobs]
         try:
             self.run_forever()
         except RequestAllFinished:
             pass
-        results = []
-        for i in range(len(prompts)):
-            ids = self.status_map[i].output_ids
+        mine = {}
+        for local, (i, _) in enumerate(jobs):
+            ids = self.status_map[local].output_ids
             text = self.tokenizer.decode(ids) if hasattr(self.tokenizer, "decode") else ""
-            results.append({"text": text, "token_ids": ids})
-        return results
+            mine[i] = {"text": text, "token_ids": ids}
+        if dp:
+            import torch.distributed as dist
+
+            parts = [None] * self.config.tp_info.size
+            dist.all_gather_object(parts, mine, group=self.tp_cpu_group)
+            for part in parts:
+                mine.update(part)
+        return [mine[i] for i in range(len(prompts))]

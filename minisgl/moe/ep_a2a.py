@@ -1,0 +1,90 @@
+"""Expert parallelism with token dispatch (DP attention).
+
+Under ``--enable-dp-attention`` every rank serves its own requests with a
+replicated copy of everything but the routed experts, which are split over
+the ranks (rank r holds experts [r E / R, (r + 1) E / R)). Each MoE layer:
+
+1. routes its own tokens over all experts (router kernel);
+2. dispatch: sorts the (token, slot) pairs by owning rank and sends each
+   pair's hidden row and local expert id to its owner (all-to-all; the
+   counts go first so every receiver knows its row count);
+3. runs its local experts over the rows it received (the grouped tcgen05
+   expert pipeline, bf16 or MXFP4, one slot per row);
+4. combine: returns every row to the rank it came from (the reverse
+   all-to-all) and sums each token's k rows weighted by the router, in slot
+   order (deterministic).
+
+The rows move with ``torch.distributed.all_to_all_single`` (NCCL on GPUs,
+gloo on CPU ranks). The reference has neither DP attention nor expert
+parallelism (its MoE is TP-sharded Triton / Marlin: python/minisgl/moe/).
+"""
+
+from __future__ import annotations
+
+from typing import List, Optional
+
+import torch
+import torch.distributed as dist
+
+from minisgl import ops
+
+from .base import BaseMoeBackend
+from .fused import FusedMoe
+
+
+class AllToAllMoe(BaseMoeBackend):
+    def __init__(self, ep_size: int, ep_rank: int, group: Optional[dist.ProcessGroup] = None) -> None:
+        self.ep_size = ep_size
+        self.ep_rank = ep_rank
+        self.group = group
+        self.local = FusedMoe()  # runs this rank's experts on the rows it received
+
+    def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: List[int], in_splits: List[int]) -> None:
+        dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
+
+    def forward(self, hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, gating_output: torch.Tensor,
+                topk: int, renormalize: bool, activation: str = "silu", scoring: str = "softmax",
+                correction_bias: Optional[torch.Tensor] = None, n_group: int = 1, topk_group: int = 1,
+                routed_scale: float = 1.0, interleaved: bool = False, expert_offset: int = 0,
+                mxfp4: Optional[tuple] = None) -> torch.Tensor:
+        x = hidden_states
+        T, H = x.shape
+        dev = x.device
+        topk_w, topk_ids = ops.moe_route(gating_output, topk, scoring, renormalize, correction_bias, n_group,
+                                         topk_group, routed_scale)
+        e_local = (mxfp4[0] if mxfp4 is not None else w1).shape[0]
+        ids = topk_ids.reshape(-1).long()
+        dest = ids // e_local
+        order = torch.argsort(dest, stable=True)  # pairs grouped by owning rank, slot order inside
+        send_counts = torch.bincount(dest, minlength=self.ep_size).to(torch.int64)
+        recv_counts = torch.empty_like(send_counts)
+        self._a2a(recv_counts, send_counts, [1] * self.ep_size, [1] * self.ep_size)
+        sc, rc = send_counts.tolist(), recv_counts.tolist()
+        # dispatch: hidden rows and local expert ids to the owners
+        send_x = x[order // topk].contiguous()
+        send_e = (ids[order] - dest[order] * e_local).to(torch.int32)
+        recv_x = x.new_empty(sum(rc), H)
+        recv_e = torch.empty(sum(rc), dtype=torch.int32, device=dev)
+        self._a2a(recv_x, send_x, rc, sc)
+        self._a2a(recv_e, send_e, rc, sc)
+        # local experts, one slot per received row (weight 1)
+        R = recv_x.shape[0]
+        ones = torch.ones(R, 1, dtype=torch.float32, device=dev)
+        if R == 0:
+            y = recv_x
+        elif not x.is_cuda:
+            from .fused import moe_reference
+
+            lw1, lw2 = self.local._cpu_weights(mxfp4) if mxfp4 is not None else (w1, w2)
+            y = moe_reference(recv_x, lw1, lw2, ones, recv_e[:, None], activation, interleaved)
+        elif mxfp4 is not None:
+            y = ops.moe_experts_mxfp4(recv_x, *mxfp4, ones, recv_e[:, None])
+        else:
+            y = ops.moe_experts(recv_x, w1, w2, ones, recv_e[:, None])
+        # combine: rows back to their source, weighted sum over each token's slots
+        back = x.new_empty(send_x.shape[0], H)
+        self._a2a(back, y.contiguous(), sc, rc)
+        pairs = x.new_empty(T * topk, H)
+        pairs[order] = back
+        out = (pairs.view(T, topk, H).float() * topk_w.view(T, topk, 1).float()).sum(dim=1)
+        return out.to(x.dtype)

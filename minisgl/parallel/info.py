@@ -63,3 +63,23 @@ def get_cp_info() -> Optional[DistributedInfo]:
 def reset_cp_info() -> None:
     global _CP
     _CP = None
+
+
+# DP attention: every rank serves its own requests with a replicated model
+# except the routed experts (split over the ranks); layers then see a
+# tensor-parallel size of 1 and this records the rank among the replicas.
+_DP: Optional[DistributedInfo] = None
+
+
+def set_dp_info(rank: int, size: int) -> None:
+    global _DP
+    _DP = DistributedInfo(rank, size) if size > 1 else None
+
+
+def get_dp_info() -> Optional[DistributedInfo]:
+    return _DP
+
+
+def reset_dp_info() -> None:
+    global _DP
+    _DP = None

@@ -88,6 +88,9 @@ class Scheduler(SchedulerIOMixin):
 
             self.profiler = StepProfiler()
         super().__init__(config, self.engine.tp_cpu_group)
+        if self.engine.dp and not config.offline_mode:
+            raise NotImplementedError("--enable-dp-attention is available in the offline LLM API; the server "
+                                      "replies through rank 0 only")
 
     # --------------------------------------------------------------- loops
     def run_when_idle(self) -> None:
@@ -117,8 +120,45 @@ class Scheduler(SchedulerIOMixin):
             data = (forward_input, self._forward(forward_input))
         self._process_last_data(data)
 
+    # DP attention: every rank schedules its own requests, but the MoE
+    # layers dispatch tokens between ranks, so all ranks run one forward per
+    # step together; a rank with nothing to run does a one-token filler step
+    def dp_loop(self) -> None:
+        import torch.distributed as dist
+
+        for msg in self.receive_msg(blocking=False):
+            self._process_one_msg(msg)
+        fin = self._schedule_next_batch()
+        busy = fin is not None or self.dp_has_pending() or self.prefill_manager.runnable or \
+            self.decode_manager.runnable
+        flags = torch.tensor([int(busy), int(fin is not None)], dtype=torch.int64)
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX, group=self.tp_cpu_group)
+        if int(flags[0]) == 0:
+            self.dp_all_idle()
+            return
+        if fin is None and int(flags[1]) != 0:
+            fin = self._prepare_batch(Batch(reqs=[], phase="decode"))
+        data = (fin, self._forward(fin)) if fin is not None else None
+        self._process_last_data(data)
+
+    def dp_has_pending(self) -> bool:
+        """Requests this rank has accepted but not scheduled yet (offline mode)."""
+        return False
+
+    def dp_all_idle(self) -> None:
+        """Every DP rank is idle this step."""
+        time.sleep(0.001)
+
     @torch.inference_mode()
     def run_forever(self):
+        if self.engine.dp:
+            if self.is_cuda:
+                with self.engine_stream_ctx:
+                    self.engine.stream.wait_stream(self.stream)
+                    while True:
+                        self.dp_loop()
+            while True:
+                self.dp_loop()
         if not self.is_cuda:
             while True:
                 self.normal_loop()

@@ -25,10 +25,10 @@ class _Formatter(logging.Formatter):
         self.use_rank = use_rank
 
     def format(self, record: logging.LogRecord) -> str:
-        from minisgl.parallel.info import get_cp_info, try_get_tp_info
+        from minisgl.parallel.info import get_cp_info, get_dp_info, try_get_tp_info
 
         tag = self.tag
-        info = get_cp_info() or try_get_tp_info()
+        info = get_cp_info() or get_dp_info() or try_get_tp_info()
         if info is not None and self.use_rank is not False:
             tag = f"{tag}|core|rank={info.rank}"
         stamp = self.formatTime(record, "%Y-%m-%d|%H:%M:%S")
@@ -40,9 +40,9 @@ class MiniLogger(logging.Logger):
     """Logger with *_rank0 variants that only emit on the primary TP rank."""
 
     def _rank0(self) -> bool:
-        from minisgl.parallel.info import get_cp_info, try_get_tp_info
+        from minisgl.parallel.info import get_cp_info, get_dp_info, try_get_tp_info
 
-        info = get_cp_info() or try_get_tp_info()
+        info = get_cp_info() or get_dp_info() or try_get_tp_info()
         return info is None or info.is_primary()
 
     def info_rank0(self, msg, *args, **kwargs):
