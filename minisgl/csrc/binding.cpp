@@ -279,7 +279,7 @@ void gemm_sample(at::Tensor out_tokens, const at::Tensor& x, const at::Tensor& w
 void moe_experts(at::Tensor out, const at::Tensor& x, const at::Tensor& w1, const at::Tensor& w2,
                  const at::Tensor& topk_w, const at::Tensor& topk_ids, int64_t tile, at::Tensor xs, at::Tensor h,
                  at::Tensor ys, at::Tensor sorted_pair, at::Tensor pair_pos, at::Tensor tile_expert,
-                 at::Tensor tile_row, at::Tensor num_tiles, const c10::optional<at::Tensor>& err) {
+                 at::Tensor tile_row, at::Tensor num_tiles, const c10::optional<at::Tensor>& err, bool combine) {
   check_cuda(x, "x");
   MSG_CHECK(x.scalar_type() == at::kBFloat16 && w1.scalar_type() == at::kBFloat16 && w2.scalar_type() == at::kBFloat16,
             "moe_experts: bf16 activations and expert weights");
@@ -300,7 +300,7 @@ void moe_experts(at::Tensor out, const at::Tensor& x, const at::Tensor& w1, cons
                 pair_pos.numel() >= T * k && tile_expert.numel() >= P / tile && tile_row.numel() >= P / tile &&
                 num_tiles.numel() >= 1,
             "moe_experts: scratch too small");
-  MSG_CHECK(out.numel() == T * H && out.scalar_type() == at::kBFloat16, "moe_experts: out [T, H] bf16");
+  MSG_CHECK(!combine || (out.numel() == T * H && out.scalar_type() == at::kBFloat16), "moe_experts: out [T, H] bf16");
   const c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t st = stream_of(x);
   minisgl::MoeAlignArgs al{};
@@ -339,8 +339,9 @@ void moe_experts(at::Tensor out, const at::Tensor& x, const at::Tensor& w1, cons
     a.g_experts = static_cast<int>(E);
     minisgl::launch_gemm(a, st);
   }
-  minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), al.pair_pos,
-                              static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
+  if (combine)  // otherwise the caller reads the expert rows ys through pair_pos
+    minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), al.pair_pos,
+                                static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
 }
 
 // -------------------------------------------------------------- MXFP4 ----
@@ -364,7 +365,7 @@ void moe_experts_mxfp4(at::Tensor out, const at::Tensor& x, const at::Tensor& w1
                        const at::Tensor& w2q, const at::Tensor& w2s, const at::Tensor& topk_w,
                        const at::Tensor& topk_ids, int64_t tile, at::Tensor xs, at::Tensor h, at::Tensor ys,
                        at::Tensor sorted_pair, at::Tensor pair_pos, at::Tensor tile_expert, at::Tensor tile_row,
-                       at::Tensor num_tiles, const c10::optional<at::Tensor>& err) {
+                       at::Tensor num_tiles, const c10::optional<at::Tensor>& err, bool combine) {
   check_cuda(x, "x");
   MSG_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "moe_experts_mxfp4: bf16 x");
   MSG_CHECK(w1q.scalar_type() == at::kByte && w2q.scalar_type() == at::kByte && w1s.scalar_type() == at::kByte &&
@@ -387,7 +388,8 @@ void moe_experts_mxfp4(at::Tensor out, const at::Tensor& x, const at::Tensor& w1
                 pair_pos.numel() >= T * k && tile_expert.numel() >= P / tile && tile_row.numel() >= P / tile &&
                 num_tiles.numel() >= 1,
             "moe_experts_mxfp4: scratch too small");
-  MSG_CHECK(out.numel() == T * H && out.scalar_type() == at::kBFloat16, "moe_experts_mxfp4: out [T, H] bf16");
+  MSG_CHECK(!combine || (out.numel() == T * H && out.scalar_type() == at::kBFloat16),
+            "moe_experts_mxfp4: out [T, H] bf16");
   const c10::cuda::CUDAGuard guard(x.device());
   cudaStream_t st = stream_of(x);
   minisgl::MoeAlignArgs al{};
@@ -423,8 +425,81 @@ void moe_experts_mxfp4(at::Tensor out, const at::Tensor& x, const at::Tensor& w1
     a.err = err_ptr(err);
     minisgl::launch_moe_mxfp4_gemm(a, st);
   }
-  minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), al.pair_pos,
-                              static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
+  if (combine)
+    minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), al.pair_pos,
+                                static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
+}
+
+void moe_combine(at::Tensor out, const at::Tensor& ys, const at::Tensor& topk_w, const at::Tensor& pair_pos, int64_t T,
+                 int64_t k) {
+  check_cuda(ys, "ys");
+  MSG_CHECK(ys.dim() == 2 && ys.is_contiguous() && ys.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
+                out.scalar_type() == at::kBFloat16 && out.numel() == T * ys.size(1),
+            "moe_combine: ys [P, H] and out [T, H] bf16");
+  MSG_CHECK(topk_w.scalar_type() == at::kFloat && topk_w.is_contiguous() && topk_w.numel() == T * k,
+            "moe_combine: float32 topk_w [T, k]");
+  check_i32(pair_pos, "pair_pos");
+  MSG_CHECK(pair_pos.numel() >= T * k, "moe_combine: pair_pos [T * k]");
+  const c10::cuda::CUDAGuard guard(ys.device());
+  minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), pair_pos.data_ptr<int32_t>(),
+                              static_cast<int>(T), static_cast<int>(k), static_cast<int>(ys.size(1)), stream_of(ys));
+}
+
+// ------------------------------------------------ EP dispatch / return ----
+minisgl::EpArgs ep_args(const at::Tensor& bases, at::Tensor epoch, int64_t rank, int64_t world, int64_t cap,
+                        int64_t ids_off, int64_t rows_off, int64_t back_off, int64_t H,
+                        const c10::optional<at::Tensor>& err) {
+  check_cuda(bases, "bases");
+  MSG_CHECK(bases.scalar_type() == at::kLong && bases.numel() == world && epoch.scalar_type() == at::kInt &&
+                epoch.is_cuda(),
+            "ep: int64 bases [world] and an int32 epoch on the device");
+  MSG_CHECK(world >= 1 && world <= 8 && rank >= 0 && rank < world && H % 8 == 0 && cap > 0,
+            "ep: 1..8 ranks, H % 8 == 0");
+  MSG_CHECK(ids_off % 16 == 0 && rows_off % 16 == 0 && back_off % 16 == 0, "ep: 16-byte aligned heap regions");
+  minisgl::EpArgs a{};
+  a.bases = bases.data_ptr<int64_t>();
+  a.epoch = reinterpret_cast<uint32_t*>(epoch.data_ptr<int32_t>());
+  a.rank = static_cast<int>(rank);
+  a.world = static_cast<int>(world);
+  a.cap = static_cast<int>(cap);
+  a.ids_off = ids_off;
+  a.rows_off = rows_off;
+  a.back_off = back_off;
+  a.H = static_cast<int>(H);
+  a.err = err_ptr(err);
+  return a;
+}
+
+void ep_dispatch(const at::Tensor& bases, at::Tensor epoch, int64_t rank, int64_t world, int64_t cap, int64_t ids_off,
+                 int64_t rows_off, int64_t back_off, const at::Tensor& x, const at::Tensor& topk_ids, int64_t e_local,
+                 const c10::optional<at::Tensor>& err) {
+  MSG_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous() && x.scalar_type() == at::kBFloat16,
+            "ep_dispatch: x [T, H] bf16 contiguous");
+  check_i32(topk_ids, "topk_ids");
+  MSG_CHECK(topk_ids.dim() == 2 && topk_ids.size(0) == x.size(0), "ep_dispatch: topk_ids [T, k]");
+  MSG_CHECK(topk_ids.numel() <= cap, "ep_dispatch: more pairs than the heap capacity");
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::EpArgs a = ep_args(bases, epoch, rank, world, cap, ids_off, rows_off, back_off, x.size(1), err);
+  a.x = x.data_ptr();
+  a.topk_ids = topk_ids.data_ptr<int32_t>();
+  a.T = static_cast<int>(x.size(0));
+  a.k = static_cast<int>(topk_ids.size(1));
+  a.e_local = static_cast<int>(e_local);
+  minisgl::launch_ep_dispatch(a, stream_of(x));
+}
+
+void ep_return(const at::Tensor& bases, at::Tensor epoch, int64_t rank, int64_t world, int64_t cap, int64_t ids_off,
+               int64_t rows_off, int64_t back_off, const at::Tensor& ys, const at::Tensor& pair_pos,
+               const c10::optional<at::Tensor>& err) {
+  MSG_CHECK(ys.is_cuda() && ys.dim() == 2 && ys.is_contiguous() && ys.scalar_type() == at::kBFloat16,
+            "ep_return: ys [P, H] bf16 contiguous");
+  check_i32(pair_pos, "pair_pos");
+  MSG_CHECK(pair_pos.numel() >= world * cap, "ep_return: pair_pos of world * cap slots");
+  const c10::cuda::CUDAGuard guard(ys.device());
+  minisgl::EpArgs a = ep_args(bases, epoch, rank, world, cap, ids_off, rows_off, back_off, ys.size(1), err);
+  a.ys = ys.data_ptr();
+  a.pair_pos = pair_pos.data_ptr<int32_t>();
+  minisgl::launch_ep_return(a, stream_of(ys));
 }
 
 // ---------------------------------------------------------------- MLA ----
@@ -985,10 +1060,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &decode_attention);
   m.def("gemm_fused", &gemm_fused);
   m.def("gemm_sample", &gemm_sample);
-  m.def("moe_experts", &moe_experts);
+  m.def("moe_experts", &moe_experts, py::arg("out"), py::arg("x"), py::arg("w1"), py::arg("w2"), py::arg("topk_w"),
+        py::arg("topk_ids"), py::arg("tile"), py::arg("xs"), py::arg("h"), py::arg("ys"), py::arg("sorted_pair"),
+        py::arg("pair_pos"), py::arg("tile_expert"), py::arg("tile_row"), py::arg("num_tiles"), py::arg("err"),
+        py::arg("combine") = true);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("moe_combine", &moe_combine);
+  m.def("ep_return", &ep_return);
   m.def("grouped_gemm", &grouped_gemm);
   m.def("mxfp4_quantize", &mxfp4_quantize);
-  m.def("moe_experts_mxfp4", &moe_experts_mxfp4);
+  m.def("moe_experts_mxfp4", &moe_experts_mxfp4, py::arg("out"), py::arg("x"), py::arg("w1q"), py::arg("w1s"),
+        py::arg("w2q"), py::arg("w2s"), py::arg("topk_w"), py::arg("topk_ids"), py::arg("tile"), py::arg("xs"),
+        py::arg("h"), py::arg("ys"), py::arg("sorted_pair"), py::arg("pair_pos"), py::arg("tile_expert"),
+        py::arg("tile_row"), py::arg("num_tiles"), py::arg("err"), py::arg("combine") = true);
   m.def("mla_prepare", &mla_prepare, py::arg("q_pe"), py::arg("xs"), py::arg("q"), py::arg("kv_a"),
         py::arg("norm_w"), py::arg("eps"), py::arg("positions"), py::arg("cos_sin"), py::arg("latent"),
         py::arg("out_loc"), py::arg("T_pad"), py::arg("err"), py::arg("cp_size") = 1, py::arg("cp_rank") = 0);

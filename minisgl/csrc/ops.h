@@ -255,6 +255,26 @@ void launch_moe_gather(void* xs, const void* x, const int32_t* sorted_pair, int 
 void launch_moe_combine(void* out, const void* ys, const float* topk_w, const int32_t* pair_pos, int T, int k, int H,
                         cudaStream_t s);
 
+// --------------------------------------------------- EP token dispatch ----
+struct EpArgs {
+  const int64_t* bases;   // [world] heap base of every rank
+  uint32_t* epoch;        // this rank's call counter (identical on every rank)
+  int rank, world;
+  int cap;                // pair slots per rank and step
+  int64_t ids_off, rows_off, back_off;  // byte offsets of the heap regions
+  int H;
+  // dispatch
+  const void* x;          // [T, H] bf16 this rank's tokens
+  const int32_t* topk_ids;  // [T * k] global expert ids
+  int T, k, e_local;
+  // return
+  const void* ys;         // [P, H] bf16 expert outputs of the received rows
+  const int32_t* pair_pos;  // [world * cap] row of ys per received slot (-1: none)
+  int* err;
+};
+void launch_ep_dispatch(const EpArgs& a, cudaStream_t s);
+void launch_ep_return(const EpArgs& a, cudaStream_t s);
+
 // --------------------------------------------------------------- MXFP4 ----
 // w [E, N, K] bf16 -> packed [E, N, K / 2] E2M1 + scales [E, K / 64, N, 2] E8M0
 void launch_mxfp4_quantize(void* packed, void* scales, const void* w, int E, int N, int K, cudaStream_t s);

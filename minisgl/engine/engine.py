@@ -139,10 +139,17 @@ class Engine:
         # ---------------------------------------------------------- backends
         self.ctx.attn_backend = self.attn_backend = create_attention_backend(
             config.attention_backend, mcfg, config.max_running_req + 1)
+        self._ep_heap = None
         if mcfg.is_moe:
+            if self.dp and self.is_cuda and config.comm == "fused":
+                from minisgl.parallel.ep_comm import EpHeap
+
+                # pair capacity of one step: the longest forward times k
+                cap = max(config.max_forward_len, config.max_running_req) * mcfg.num_experts_per_tok
+                self._ep_heap = EpHeap(self.device, cap, mcfg.hidden_size)
             self.ctx.moe_backend = self.moe_backend = create_moe_backend(
                 config.moe_backend, ep_dispatch=self.dp, ep_size=mcfg.ep_size, ep_rank=mcfg.ep_rank,
-                group=self.tp_cpu_group if not self.is_cuda else None)
+                group=self.tp_cpu_group if not self.is_cuda else None, heap=self._ep_heap)
         self.sampler = Sampler(self.device, mcfg.vocab_size, config.weight_seed)
         if self.is_cuda:
             from minisgl import ops
@@ -335,6 +342,9 @@ class Engine:
         self.graph_runner.destroy_cuda_graphs()
         import torch.distributed as dist
 
+        if getattr(self, "_ep_heap", None) is not None:
+            self._ep_heap.shutdown()
+            self._ep_heap = None
         destroy_distributed()
         if getattr(self, "_owns_pg", False) and dist.is_initialized():
             dist.destroy_process_group()

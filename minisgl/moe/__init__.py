@@ -17,13 +17,13 @@ def _fused() -> BaseMoeBackend:
 
 
 def create_moe_backend(backend: str, ep_dispatch: bool = False, ep_size: int = 1, ep_rank: int = 0,
-                       group=None) -> BaseMoeBackend:
+                       group=None, heap=None) -> BaseMoeBackend:
     """``ep_dispatch``: experts split over the ranks and tokens dispatched to
     their owners (DP attention); otherwise the named local backend."""
     if ep_dispatch:
         from .ep_a2a import AllToAllMoe
 
-        return AllToAllMoe(ep_size, ep_rank, group)
+        return AllToAllMoe(ep_size, ep_rank, group, heap)
     return SUPPORTED_MOE_BACKENDS["fused" if backend == "auto" else backend]()
 
 

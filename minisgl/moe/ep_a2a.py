@@ -14,8 +14,10 @@ the ranks (rank r holds experts [r E / R, (r + 1) E / R)). Each MoE layer:
    all-to-all) and sums each token's k rows weighted by the router, in slot
    order (deterministic).
 
-The rows move with ``torch.distributed.all_to_all_single`` (NCCL on GPUs,
-gloo on CPU ranks). The reference has neither DP attention nor expert
+With ``--comm fused`` on GPUs the rows move by peer stores over NVLink from
+our own kernels (``minisgl/parallel/ep_comm.py``, ``csrc/ep.cu``: no host
+synchronisation); otherwise with ``torch.distributed.all_to_all_single``
+(NCCL, or gloo on CPU ranks). The reference has neither DP attention nor expert
 parallelism (its MoE is TP-sharded Triton / Marlin: python/minisgl/moe/).
 """
 
@@ -33,11 +35,34 @@ from .fused import FusedMoe
 
 
 class AllToAllMoe(BaseMoeBackend):
-    def __init__(self, ep_size: int, ep_rank: int, group: Optional[dist.ProcessGroup] = None) -> None:
+    def __init__(self, ep_size: int, ep_rank: int, group: Optional[dist.ProcessGroup] = None,
+                 heap=None) -> None:
         self.ep_size = ep_size
         self.ep_rank = ep_rank
         self.group = group
+        self.heap = heap  # EpHeap: the NVLink dispatch (``--comm fused``), else torch.distributed
         self.local = FusedMoe()  # runs this rank's experts on the rows it received
+        self._ident: dict = {}
+
+    def _forward_nvlink(self, x, w1, w2, topk_w, topk_ids, e_local, mxfp4):
+        """Peer-store dispatch, local experts over the receive buffer, peer-store
+        return, weighted combine (no host synchronisation)."""
+        heap = self.heap
+        T, H = x.shape
+        k = topk_ids.shape[1]
+        heap.dispatch(x, topk_ids, e_local)
+        rows, ids = heap.recv_rows, heap.recv_ids.view(-1, 1)
+        ones = torch.ones(rows.shape[0], 1, dtype=torch.float32, device=x.device)
+        if mxfp4 is not None:
+            ys, pair_pos = ops.moe_experts_rows(rows, ones, ids, mxfp4=mxfp4)
+        else:
+            ys, pair_pos = ops.moe_experts_rows(rows, ones, ids, w1=w1, w2=w2)
+        heap.give_back(ys, pair_pos)
+        n = T * k
+        ident = self._ident.get(n)
+        if ident is None:
+            ident = self._ident[n] = torch.arange(n, dtype=torch.int32, device=x.device)
+        return ops.moe_combine(heap.back[:n], topk_w, ident, T, k)
 
     def _a2a(self, out: torch.Tensor, inp: torch.Tensor, out_splits: List[int], in_splits: List[int]) -> None:
         dist.all_to_all_single(out, inp, out_splits, in_splits, group=self.group)
@@ -53,6 +78,8 @@ class AllToAllMoe(BaseMoeBackend):
         topk_w, topk_ids = ops.moe_route(gating_output, topk, scoring, renormalize, correction_bias, n_group,
                                          topk_group, routed_scale)
         e_local = (mxfp4[0] if mxfp4 is not None else w1).shape[0]
+        if self.heap is not None and x.is_cuda:
+            return self._forward_nvlink(x, w1, w2, topk_w, topk_ids, e_local, mxfp4)
         ids = topk_ids.reshape(-1).long()
         dest = ids // e_local
         order = torch.argsort(dest, stable=True)  # pairs grouped by owning rank, slot order inside

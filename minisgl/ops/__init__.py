@@ -673,6 +673,48 @@ def moe_experts_mxfp4(x: torch.Tensor, w1q: torch.Tensor, w1s: torch.Tensor, w2q
     return out
 
 
+def moe_experts_rows(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, w1=None, w2=None,
+                     mxfp4: Optional[tuple] = None, tile: int = 0):
+    """The expert pipeline without the combine: returns (ys [P, H] expert
+    output rows, pair_pos [T * k] row of each (token, slot) pair, -1 for
+    pairs whose expert is not here)."""
+    T, H = x.shape
+    k = topk_ids.shape[1]
+    E = (mxfp4[0] if mxfp4 is not None else w1).shape[0]
+    I = (mxfp4[2].shape[2] * 2) if mxfp4 is not None else w2.shape[2]
+    tile = tile or moe_tile(T, k, E)
+    P = T * k + E * (tile - 1)
+    Pp = (P + tile - 1) // tile * tile
+    dev, i32 = x.device, torch.int32
+    xs = torch.empty(Pp, H, dtype=x.dtype, device=dev)
+    h = torch.empty(Pp, I, dtype=x.dtype, device=dev)
+    ys = torch.empty(Pp, H, dtype=x.dtype, device=dev)
+    sorted_pair = torch.empty(P, dtype=i32, device=dev)
+    pair_pos = torch.empty(T * k, dtype=i32, device=dev)
+    tile_expert = torch.empty(P // tile, dtype=i32, device=dev)
+    tile_row = torch.empty(P // tile, dtype=i32, device=dev)
+    num_tiles = torch.empty(1, dtype=i32, device=dev)
+    out = torch.empty(0, H, dtype=x.dtype, device=dev)
+    _count(5)
+    if mxfp4 is not None:
+        native().moe_experts_mxfp4(out, x, *mxfp4, topk_w.float().contiguous(), topk_ids.to(i32).contiguous(), tile,
+                                   xs, h, ys, sorted_pair, pair_pos, tile_expert, tile_row, num_tiles,
+                                   error_word(dev), False)
+    else:
+        native().moe_experts(out, x, w1, w2, topk_w.float().contiguous(), topk_ids.to(i32).contiguous(), tile, xs, h,
+                             ys, sorted_pair, pair_pos, tile_expert, tile_row, num_tiles, error_word(dev), False)
+    return ys, pair_pos
+
+
+def moe_combine(ys: torch.Tensor, topk_w: torch.Tensor, pair_pos: torch.Tensor, T: int, k: int) -> torch.Tensor:
+    """out[t] = sum_j topk_w[t, j] * ys[pair_pos[t * k + j]] (slot order; -1 rows skipped)."""
+    H = ys.shape[1]
+    out = torch.empty(T, H, dtype=ys.dtype, device=ys.device)
+    _count()
+    native().moe_combine(out, ys, topk_w.float().contiguous(), pair_pos, T, k)
+    return out
+
+
 def moe_route(
     logits: torch.Tensor,
     k: int,

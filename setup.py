@@ -34,6 +34,7 @@ SOURCES = [
     "minisgl/csrc/symm.cu",
     "minisgl/csrc/mla.cu",
     "minisgl/csrc/mxfp4.cu",
+    "minisgl/csrc/ep.cu",
 ]
 
 

@@ -1,6 +1,8 @@
-"""DP attention with expert-parallel token dispatch on 2 GPUs (NCCL
-all-to-all; NVLS off): a Qwen3-MoE-shape model served by two DP ranks, each
-holding half of the experts, generates what one GPU generates."""
+"""DP attention with expert-parallel token dispatch on GPUs (NVLS off): a
+Qwen3-MoE-shape model served by two DP ranks, each holding half of the
+experts, generates what one GPU generates, with the rows moved by NCCL or by
+our peer-store kernels (``--comm fused``); and the peer-store dispatch on a
+one-rank heap equals the local expert pipeline."""
 
 import os
 import socket
@@ -18,7 +20,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(rank, world, port, dp, q):
+def _run(rank, world, port, dp, q, comm="nccl"):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
@@ -30,18 +32,18 @@ def _run(rank, world, port, dp, q):
                                                                num_key_value_heads=1)),
               dtype=torch.bfloat16, device=f"cuda:{rank}", use_dummy_weight=True, dummy_weight_device="cpu",
               tp_info=DistributedInfo(rank, world), page_size=64, num_page_override=64, max_running_req=8,
-              max_seq_len_override=1024, distributed_port=port, enable_dp_attention=dp)
+              max_seq_len_override=1024, distributed_port=port, enable_dp_attention=dp, comm=comm)
     prompts = [[(7 * i + 3 * j) % 1000 for j in range(20 + 9 * i)] for i in range(5)]
     outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True))
     q.put((rank, [o["token_ids"] for o in outs]))
     llm.shutdown()
 
 
-def _spawn(world, dp):
+def _spawn(world, dp, comm="nccl"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, dp, q)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, dp, q, comm)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=400) for _ in range(world))
@@ -51,11 +53,49 @@ def _spawn(world, dp):
     return results
 
 
-def test_dp2_ep2_matches_one_gpu():
+@pytest.mark.parametrize("comm", ["nccl", "fused"])
+def test_dp2_ep2_matches_one_gpu(comm):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     one = _spawn(1, False)[0]
-    two = _spawn(2, True)
+    two = _spawn(2, True, comm)
     assert two[0] == two[1]
     same = sum(a == b for x, y in zip(one, two[0]) for a, b in zip(x, y))
     assert same >= 0.8 * sum(len(x) for x in one), (one, two[0])
+
+
+def test_nvlink_dispatch_one_rank_matches_local_experts():
+    """The peer-store dispatch / return kernels on a one-rank heap (rows
+    stored into this GPU's own heap) give what the local expert pipeline
+    gives."""
+    import torch.distributed as dist
+
+    from minisgl import ops
+    from minisgl.moe.ep_a2a import AllToAllMoe
+    from minisgl.moe.fused import FusedMoe
+    from minisgl.parallel.ep_comm import EpHeap
+
+    port = _free_port()
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=0, world_size=1)
+    heap = None
+    try:
+        dev = torch.device("cuda", 0)
+        g = torch.Generator(device="cpu").manual_seed(4)
+        T, H, I, E, k = 37, 256, 128, 8, 2
+        x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(dev)
+        w1 = (torch.randn(E, 2 * I, H, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+        w2 = (torch.randn(E, H, I, generator=g) * 0.05).to(torch.bfloat16).to(dev)
+        logits = torch.randn(T, E, generator=g).to(dev)
+        heap = EpHeap(dev, 64 * k, H)
+        a2a = AllToAllMoe(1, 0, None, heap)
+        got = a2a.forward(x, w1, w2, logits, k, True, interleaved=True)
+        got2 = a2a.forward(x, w1, w2, logits, k, True, interleaved=True)  # the barriers reset for a second step
+        want = FusedMoe().forward(x, w1, w2, logits, k, True, interleaved=True)
+        torch.cuda.synchronize()
+        ops.check_device_errors(dev)
+        assert torch.allclose(got.float(), want.float(), atol=2e-2, rtol=1e-2)
+        assert torch.equal(got, got2)
+    finally:
+        if heap is not None:
+            heap.shutdown()
+        dist.destroy_process_group()
