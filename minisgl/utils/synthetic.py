@@ -171,6 +171,8 @@ def write_random_checkpoint(folder: str, seed: int = 0, std: float = 0.02, norm_
     if not c.get("tie_word_embeddings", False):
         W["lm_head.weight"] = rnd(V, H)
     moe = c.get("num_experts", 0) > 0
+    if c.get("kv_lora_rank"):
+        return _write_deepseek(folder, c, W, rnd, norm_w, dt)
     for i in range(c["num_hidden_layers"]):
         p = f"model.layers.{i}."
         W[p + "input_layernorm.weight"] = norm_w(H)
@@ -198,5 +200,56 @@ def write_random_checkpoint(folder: str, seed: int = 0, std: float = 0.02, norm_
             W[p + "mlp.gate_proj.weight"] = rnd(I, H)
             W[p + "mlp.up_proj.weight"] = rnd(I, H)
             W[p + "mlp.down_proj.weight"] = rnd(H, I)
+    save_file({k: v.contiguous() for k, v in W.items()}, os.path.join(folder, "model.safetensors"))
+    return folder
+
+
+def _write_deepseek(folder: str, c: dict, W: dict, rnd, norm_w, dt) -> str:
+    """DeepSeek-V3 / Kimi-K2 HF layout: MLA projections (q LoRA, compressed
+    KV with the shared positional key, kv_b up-projection), dense MLP for
+    the first ``first_k_dense_replace`` layers, then the router (weight and
+    fp32 score-correction bias), per-expert routed MLPs and the shared
+    expert."""
+    import torch
+    from safetensors.torch import save_file
+
+    H, hq = c["hidden_size"], c["num_attention_heads"]
+    nope, rope, vd = c["qk_nope_head_dim"], c["qk_rope_head_dim"], c["v_head_dim"]
+    qlr, kvl = c.get("q_lora_rank") or 0, c["kv_lora_rank"]
+    E, I, Id = c["n_routed_experts"], c["moe_intermediate_size"], c["intermediate_size"]
+    shared = c.get("n_shared_experts", 0) or 0
+    for i in range(c["num_hidden_layers"]):
+        p = f"model.layers.{i}."
+        a = p + "self_attn."
+        W[p + "input_layernorm.weight"] = norm_w(H)
+        W[p + "post_attention_layernorm.weight"] = norm_w(H)
+        if qlr:
+            W[a + "q_a_proj.weight"] = rnd(qlr, H)
+            W[a + "q_a_layernorm.weight"] = norm_w(qlr)
+            W[a + "q_b_proj.weight"] = rnd(hq * (nope + rope), qlr)
+        else:
+            W[a + "q_proj.weight"] = rnd(hq * (nope + rope), H)
+        W[a + "kv_a_proj_with_mqa.weight"] = rnd(kvl + rope, H)
+        W[a + "kv_a_layernorm.weight"] = norm_w(kvl)
+        W[a + "kv_b_proj.weight"] = rnd(hq * (nope + vd), kvl)
+        W[a + "o_proj.weight"] = rnd(H, hq * vd)
+        m = p + "mlp."
+        if i < c.get("first_k_dense_replace", 0) or E == 0:
+            W[m + "gate_proj.weight"] = rnd(Id, H)
+            W[m + "up_proj.weight"] = rnd(Id, H)
+            W[m + "down_proj.weight"] = rnd(H, Id)
+            continue
+        W[m + "gate.weight"] = rnd(E, H)
+        if c.get("scoring_func") == "sigmoid":
+            W[m + "gate.e_score_correction_bias"] = (torch.randn(E) * 0.01).float()
+        for e in range(E):
+            q = m + f"experts.{e}."
+            W[q + "gate_proj.weight"] = rnd(I, H)
+            W[q + "up_proj.weight"] = rnd(I, H)
+            W[q + "down_proj.weight"] = rnd(H, I)
+        if shared:
+            W[m + "shared_experts.gate_proj.weight"] = rnd(I * shared, H)
+            W[m + "shared_experts.up_proj.weight"] = rnd(I * shared, H)
+            W[m + "shared_experts.down_proj.weight"] = rnd(H, I * shared)
     save_file({k: v.contiguous() for k, v in W.items()}, os.path.join(folder, "model.safetensors"))
     return folder

@@ -77,3 +77,33 @@ def test_dp2_odd_prompt_count(checkpoint):
     single = _generate(1, checkpoint, False, prompts, lens)[0]
     dp = _generate(2, checkpoint, True, prompts, lens)
     assert dp[0] == dp[1] == single
+
+
+@pytest.fixture(scope="module")
+def kimi_checkpoint():
+    from minisgl.utils.synthetic import make_model_dir, write_random_checkpoint
+
+    folder = tempfile.mkdtemp(prefix="minisgl_dp_kimi_")
+    shutil.rmtree(folder)
+    make_model_dir("tiny-kimi", folder=folder)
+    write_random_checkpoint(folder, seed=13, std=0.05)
+    yield folder
+    shutil.rmtree(folder, ignore_errors=True)
+
+
+def test_dp2_kimi_mla_moe_matches_single_rank(kimi_checkpoint):
+    """DeepSeek-V3 shape: MLA attention replicated per DP rank, routed experts
+    dispatched, the shared expert computed locally."""
+    lens = [5, 7, 3, 6]
+    single = _generate(1, kimi_checkpoint, False, PROMPTS, lens)[0]
+    dp = _generate(2, kimi_checkpoint, True, PROMPTS, lens)
+    assert dp[0] == dp[1] == single
+
+
+def test_tp2_kimi_checkpoint_matches_single_rank(kimi_checkpoint):
+    """The HF DeepSeek-V3 layout loaded with TP=2: q_b / kv_b split by heads,
+    experts and the shared expert split on the intermediate dimension."""
+    lens = [4, 4, 4, 4]
+    single = _generate(1, kimi_checkpoint, False, PROMPTS, lens)[0]
+    tp = _generate(2, kimi_checkpoint, False, PROMPTS, lens)
+    assert tp[0] == tp[1] == single
