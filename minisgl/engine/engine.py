@@ -173,8 +173,10 @@ class Engine:
 
     # ---------------------------------------------------------------- setup
     def _graph_max_bs(self, config: EngineConfig) -> Optional[int]:
-        if not self.is_cuda or self.dp:
-            return 0  # DP attention: the token dispatch has host-side row counts
+        if not self.is_cuda or (self.dp and config.comm != "fused"):
+            return 0  # DP attention over NCCL: the all-to-all needs host-side row counts
+        # (the peer-store dispatch of --comm fused has fixed-capacity slots:
+        # graphs of different batch sizes on different ranks still match)
         mx = config.cuda_graph_max_bs
         if mx is None:
             return min(config.max_running_req, 256)

@@ -17,7 +17,9 @@ the ranks (rank r holds experts [r E / R, (r + 1) E / R)). Each MoE layer:
 With ``--comm fused`` on GPUs the rows move by peer stores over NVLink from
 our own kernels (``minisgl/parallel/ep_comm.py``, ``csrc/ep.cu``: no host
 synchronisation); otherwise with ``torch.distributed.all_to_all_single``
-(NCCL, or gloo on CPU ranks). The reference has neither DP attention nor expert
+(NCCL, or gloo on CPU ranks). The peer-store path launches only kernels
+with fixed-capacity buffers, so decode steps run as CUDA graphs even when
+the ranks replay graphs of different batch sizes. The reference has neither DP attention nor expert
 parallelism (its MoE is TP-sharded Triton / Marlin: python/minisgl/moe/).
 """
 
