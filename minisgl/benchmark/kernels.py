@@ -136,6 +136,32 @@ def bench_mla_decode(B: int, L: int, H: int, page: int, peaks) -> Dict:
             "frac_tensor": round(tf / peaks["tflops"], 3)}
 
 
+def bench_moe_mxfp4(T: int, E: int, k: int, H: int, I: int, peaks) -> Dict:
+    """Routed experts with MXFP4 weights (Kimi-K2 expert dims by default):
+    router outputs uniform over E local experts, the full pipeline (align,
+    gather, gate_up with SiLU, down, combine) against the same experts in
+    bf16. Bytes: the MXFP4 weights of the experts hit (4.25 bits a weight)
+    plus activations; the bf16 row reads its bf16 weights."""
+    from minisgl.quant import quantize_mxfp4
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w1 = (torch.randn(E, 2 * I, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    q1, q2 = quantize_mxfp4(w1), quantize_mxfp4(w2)
+    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, device="cuda", generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    tw = torch.full((T, k), 1.0 / k, device="cuda")
+    hit = int(torch.unique(ids).numel())
+    ms = time_kernel(lambda: ops.moe_experts_mxfp4(x, *q1, *q2, tw, ids))
+    ms_bf16 = time_kernel(lambda: ops.moe_experts(x, w1, w2, tw, ids))
+    wbytes = hit * (3 * I * H) * 0.5 * (1 + 1 / 16)  # E2M1 + one E8M0 byte per 32
+    nbytes = wbytes + 2 * 2 * T * k * H
+    gbs = nbytes / ms / 1e6
+    return {"kernel": "moe_experts_mxfp4", "T": T, "E": E, "k": k, "H": H, "I": I, "experts_hit": hit,
+            "ms": round(ms, 4), "bf16_ms": round(ms_bf16, 4), "GB/s": round(gbs, 1),
+            "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
+
+
 def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
     x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
@@ -308,6 +334,8 @@ def main() -> None:
         cases.append((f"gemm[{lab} prefill]", lambda N=N, K=K, lab=lab: bench_gemm(16384, N, K, peaks,
                                                                                  f"{lab} prefill")))
     cases.append(("elementwise", lambda: bench_elementwise(peaks)))
+    for T in (16, 256):
+        cases.append((f"moe_mxfp4 T={T}", lambda T=T: bench_moe_mxfp4(T, 16, 8, 7168, 2048, peaks)))
     for M in (1, 8, 32, 64, 128, 192, 256):
         cases.append((f"layer_chain M={M};", lambda M=M: bench_layer_chain(M, peaks)))
     cases.append(("rowkernels M=256", lambda: bench_row_kernels(256, peaks)))
