@@ -18,8 +18,8 @@
 // the producer moves the packed weights (TMA, 128 rows x 32 bytes), their
 // scales (one 256-byte bulk copy) and the bf16 token tile (TMA, 128-byte
 // swizzle); four converter warps expand the weights to bf16 in the swizzled
-// K-major operand layout through a 256-entry byte -> bf16x2 table and one
-// exact power-of-two multiply, and the MMA thread runs kind::f16 tcgen05 MMAs
+// K-major operand layout with register byte permutes (no shared-memory table)
+// and one exact power-of-two multiply, and the MMA thread runs kind::f16 tcgen05 MMAs
 // on the expanded tile. Weight bytes per token tile are 4.25 bits per weight,
 // the quantity a decode step streams from HBM.
 #include <stdexcept>
@@ -102,7 +102,7 @@ struct QSmem {
   static constexpr int kStage = (kWideBytes + kAct + kPackedBytes + kScaleBytes + 1023) / 1024 * 1024;
   static constexpr int kStages = 4;
   static constexpr int kXchg = 64 * BN * 4;   // SiLU epilogue: the up rows, fp32
-  static constexpr int kBytes = 1024 + kStages * kStage + kXchg + 1024 /*lut*/ + 256;
+  static constexpr int kBytes = 1024 + kStages * kStage + kXchg + 256;
 };
 
 struct QParams {
@@ -117,15 +117,23 @@ struct QParams {
   ErrorSink err;
 };
 
-// bf16x2 pattern of the two E2M1 codes of a byte (unscaled), low nibble first
-__device__ __forceinline__ uint32_t e2m1_pair_bits(uint32_t byte) {
-  auto one = [](uint32_t c) -> uint32_t {
-    const uint32_t s = (c & 8u) << 12;
-    const uint32_t e = (c >> 1) & 3u, m = c & 1u;
-    const uint32_t mag = e != 0 ? (((e + 126u) << 7) | (m << 6)) : (m != 0 ? (126u << 7) : 0u);
-    return mag == 0 ? 0u : (s | mag);
-  };
-  return one(byte & 15u) | (one(byte >> 4) << 16);
+// Eight E2M1 codes (one 32-bit word, code j in bits 4j..4j+3) -> four
+// bf16x2 words (unscaled), in registers. The bf16 patterns of the eight
+// magnitudes {0, 0.5, 1, 1.5, 2, 3, 4, 6} are 0x0000, 0x3F00, 0x3F80,
+// 0x3FC0, 0x4000, 0x4040, 0x4080, 0x40C0: their high and low bytes form two
+// 8-byte tables that a byte permute indexes with four 3-bit magnitudes at a
+// time; two more permutes interleave low / high bytes into bf16 pairs and
+// the sign bits are ORed in (a negative zero stays -0, harmless in an MMA).
+__device__ __forceinline__ void e2m1x8_to_bf16x8(uint32_t w, uint32_t (&o)[4]) {
+  constexpr uint32_t kHiA = 0x3F3F3F00u, kHiB = 0x40404040u;  // high bytes of magnitudes 0..3, 4..7
+  constexpr uint32_t kLoA = 0xC0800000u, kLoB = 0xC0804000u;  // low bytes
+  const uint32_t m = w & 0x77777777u;
+  const uint32_t hi03 = __byte_perm(kHiA, kHiB, m), lo03 = __byte_perm(kLoA, kLoB, m);
+  const uint32_t hi47 = __byte_perm(kHiA, kHiB, m >> 16), lo47 = __byte_perm(kLoA, kLoB, m >> 16);
+  o[0] = __byte_perm(lo03, hi03, 0x5140) | ((w << 12) & 0x8000u) | ((w << 24) & 0x80000000u);
+  o[1] = __byte_perm(lo03, hi03, 0x7362) | ((w << 4) & 0x8000u) | ((w << 16) & 0x80000000u);
+  o[2] = __byte_perm(lo47, hi47, 0x5140) | ((w >> 4) & 0x8000u) | ((w << 8) & 0x80000000u);
+  o[3] = __byte_perm(lo47, hi47, 0x7362) | ((w >> 12) & 0x8000u) | (w & 0x80000000u);
 }
 
 template <int BN>
@@ -139,8 +147,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   // stage s: [wide bf16 16 KB][act BN x 128 B][packed 4 KB][scales 256 B]
   uint8_t* xchg = smem + kStages * S::kStage;
-  uint32_t* lut = reinterpret_cast<uint32_t*>(xchg + S::kXchg);
-  uint64_t* full = reinterpret_cast<uint64_t*>(reinterpret_cast<uint8_t*>(lut) + 1024);
+  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + S::kXchg);
   uint64_t* wide = full + kStages;
   uint64_t* empty = wide + kStages;
   uint64_t* done = empty + kStages;
@@ -155,7 +162,6 @@ __global__ void __launch_bounds__(kQThreads, 1)
   const int row0 = p.tile_row[tile];
   const int n0 = blockIdx.y * QBM;        // weight row block inside the expert
   const int nkb = p.K / QBK;
-  for (int i = threadIdx.x; i < 256; i += blockDim.x) lut[i] = e2m1_pair_bits(static_cast<uint32_t>(i));
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
@@ -237,12 +243,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
       const uint32_t words[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
 #pragma unroll
       for (int c = 0; c < 8; ++c) {  // 16-byte chunk c = elements 8c..8c+7 = bytes 4c..4c+3
-        const uint32_t w = words[c];
         uint32_t o[4];
+        e2m1x8_to_bf16x8(words[c], o);
 #pragma unroll
         for (int b = 0; b < 4; ++b) {
-          const uint32_t bits = lut[(w >> (8 * b)) & 0xFFu];
-          const __nv_bfloat162 v = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&bits),
+          const __nv_bfloat162 v = __hmul2(*reinterpret_cast<const __nv_bfloat162*>(&o[b]),
                                            *reinterpret_cast<const __nv_bfloat162*>(&mul[c >> 2]));
           o[b] = *reinterpret_cast<const uint32_t*>(&v);
         }
