@@ -22,6 +22,7 @@
 // and one exact power-of-two multiply, and the MMA thread runs kind::f16 tcgen05 MMAs
 // on the expanded tile. Weight bytes per token tile are 4.25 bits per weight,
 // the quantity a decode step streams from HBM.
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -95,12 +96,12 @@ constexpr int kPackedBytes = QBM * QBK / 2;   // 4 KB of E2M1 per k-block
 constexpr int kScaleBytes = QBM * 2;          // 256 B of E8M0 per k-block
 constexpr int kWideBytes = QBM * QBK * 2;     // 16 KB of expanded bf16
 
-template <int BN>
+template <int BN, int STAGES>
 struct QSmem {
   static constexpr int kAct = BN * QBK * 2;
   // rounded up to 1 KB: the swizzled operand tiles need 1024-byte alignment
   static constexpr int kStage = (kWideBytes + kAct + kPackedBytes + kScaleBytes + 1023) / 1024 * 1024;
-  static constexpr int kStages = 4;
+  static constexpr int kStages = STAGES;
   static constexpr int kXchg = 64 * BN * 4;   // SiLU epilogue: the up rows, fp32
   static constexpr int kBytes = 1024 + kStages * kStage + kXchg + 256;
 };
@@ -136,11 +137,11 @@ __device__ __forceinline__ void e2m1x8_to_bf16x8(uint32_t w, uint32_t (&o)[4]) {
   o[3] = __byte_perm(lo47, hi47, 0x7362) | ((w >> 12) & 0x8000u) | (w & 0x80000000u);
 }
 
-template <int BN>
+template <int BN, int STAGES>
 __global__ void __launch_bounds__(kQThreads, 1)
     moe_mxfp4_gemm_kernel(const __grid_constant__ CUtensorMap tm_w, const __grid_constant__ CUtensorMap tm_x,
                           const QParams p) {
-  using S = QSmem<BN>;
+  using S = QSmem<BN, STAGES>;
   constexpr int kStages = S::kStages;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
@@ -307,12 +308,12 @@ __global__ void __launch_bounds__(kQThreads, 1)
   }
 }
 
-template <int BN>
+template <int BN, int STAGES>
 void launch_q(const MoeMxfp4GemmArgs& a, cudaStream_t s) {
-  using S = QSmem<BN>;
+  using S = QSmem<BN, STAGES>;
   static bool attr = false;
   if (!attr) {
-    cudaFuncSetAttribute(moe_mxfp4_gemm_kernel<BN>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
+    cudaFuncSetAttribute(moe_mxfp4_gemm_kernel<BN, STAGES>, cudaFuncAttributeMaxDynamicSharedMemorySize, S::kBytes);
     attr = true;
   }
   uint64_t wd[2] = {static_cast<uint64_t>(a.K / 2), static_cast<uint64_t>(a.E) * a.N};
@@ -332,7 +333,7 @@ void launch_q(const MoeMxfp4GemmArgs& a, cudaStream_t s) {
   p.num_tiles = a.num_tiles;
   p.err = ErrorSink{a.err};
   dim3 grid(a.P / BN, a.N / QBM);
-  launch_pdl(moe_mxfp4_gemm_kernel<BN>, grid, dim3(kQThreads), S::kBytes, s, tw, tx, p);
+  launch_pdl(moe_mxfp4_gemm_kernel<BN, STAGES>, grid, dim3(kQThreads), S::kBytes, s, tw, tx, p);
 }
 
 }  // namespace
@@ -353,11 +354,18 @@ namespace minisgl {
 void launch_moe_mxfp4_gemm(const MoeMxfp4GemmArgs& a, cudaStream_t s) {
   if (a.N % 128 != 0 || a.K % 64 != 0) throw std::runtime_error("minisgl.moe_mxfp4: N % 128 == 0 and K % 64 == 0");
   if (a.P % a.tile != 0) throw std::runtime_error("minisgl.moe_mxfp4: rows must be a multiple of the tile");
+  static const bool deep = [] {
+    const char* v = std::getenv("MINISGL_MXFP4_STAGES");
+    return v != nullptr && std::string(v) == "4";
+  }();
   switch (a.tile) {
-    case 16: launch_q<16>(a, s); break;
-    case 32: launch_q<32>(a, s); break;
-    case 64: launch_q<64>(a, s); break;
-    case 128: launch_q<128>(a, s); break;
+    // token tiles up to 64: three stages (about 107 KB), so two CTAs share an
+    // SM and one's converter work overlaps the other's copies;
+    // MINISGL_MXFP4_STAGES=4 keeps one CTA per SM with a deeper ring
+    case 16: deep ? launch_q<16, 4>(a, s) : launch_q<16, 3>(a, s); break;
+    case 32: deep ? launch_q<32, 4>(a, s) : launch_q<32, 3>(a, s); break;
+    case 64: deep ? launch_q<64, 4>(a, s) : launch_q<64, 3>(a, s); break;
+    case 128: launch_q<128, 4>(a, s); break;
     default: throw std::runtime_error("minisgl.moe_mxfp4: tile of 16, 32, 64 or 128");
   }
 }
