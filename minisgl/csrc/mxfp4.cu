@@ -17,7 +17,8 @@
 // also weight-only: python/minisgl/moe/ + sgl-kernel marlin_moe). Per k-block
 // the producer moves the packed weights (TMA, 128 rows x 32 bytes), their
 // scales (one 256-byte bulk copy) and the bf16 token tile (TMA, 128-byte
-// swizzle); four converter warps expand the weights to bf16 in the swizzled
+// swizzle) into a deep ring of small stages; four converter warps expand
+// each stage's weights into one of two bf16 tiles in the swizzled
 // K-major operand layout with register byte permutes (no shared-memory table)
 // and one exact power-of-two multiply, and the MMA thread runs kind::f16 tcgen05 MMAs
 // on the expanded tile. Weight bytes per token tile are 4.25 bits per weight,
@@ -98,12 +99,15 @@ constexpr int kWideBytes = QBM * QBK * 2;     // 16 KB of expanded bf16
 
 template <int BN, int STAGES>
 struct QSmem {
+  // [expanded bf16 weights: 2 x 16 KB][STAGES x (token tile | packed | scales)][SiLU exchange][barriers]
+  // The copy ring is deep and cheap (6-13 KB a stage); only the two
+  // expanded tiles the converter and the MMA hand back and forth are wide.
   static constexpr int kAct = BN * QBK * 2;
-  // rounded up to 1 KB: the swizzled operand tiles need 1024-byte alignment
-  static constexpr int kStage = (kWideBytes + kAct + kPackedBytes + kScaleBytes + 1023) / 1024 * 1024;
+  static constexpr int kStage = (kAct + kPackedBytes + kScaleBytes + 1023) / 1024 * 1024;  // swizzle alignment
   static constexpr int kStages = STAGES;
+  static constexpr int kWide = 2 * kWideBytes;
   static constexpr int kXchg = 64 * BN * 4;   // SiLU epilogue: the up rows, fp32
-  static constexpr int kBytes = 1024 + kStages * kStage + kXchg + 256;
+  static constexpr int kBytes = 1024 + kWide + kStages * kStage + kXchg + 256;
 };
 
 struct QParams {
@@ -118,23 +122,37 @@ struct QParams {
   ErrorSink err;
 };
 
+// PTX byte permute in its default mode: selector nibble i picks byte
+// (nibble & 7) of {a, b} for result byte i; with bit 3 of the nibble set the
+// result byte is that byte's top bit replicated (0x00 or 0xFF).
+__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
+  uint32_t d;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(d) : "r"(a), "r"(b), "r"(sel));
+  return d;
+}
+
 // Eight E2M1 codes (one 32-bit word, code j in bits 4j..4j+3) -> four
 // bf16x2 words (unscaled), in registers. The bf16 patterns of the eight
 // magnitudes {0, 0.5, 1, 1.5, 2, 3, 4, 6} are 0x0000, 0x3F00, 0x3F80,
 // 0x3FC0, 0x4000, 0x4040, 0x4080, 0x40C0: their high and low bytes form two
-// 8-byte tables that a byte permute indexes with four 3-bit magnitudes at a
-// time; two more permutes interleave low / high bytes into bf16 pairs and
-// the sign bits are ORed in (a negative zero stays -0, harmless in an MMA).
+// 8-byte tables that a permute indexes with four 3-bit magnitudes at a
+// time. Signs: byte k of w << 4 has code 2k's sign bit on top and byte k of
+// w has code 2k + 1's, so a sign-replicating permute of the two gives a
+// 0xFF / 0x00 mask per code for the high bytes (a negative zero stays -0,
+// harmless in an MMA). Two more permutes interleave low and high bytes into
+// bf16 pairs: 14 integer operations for eight weights.
 __device__ __forceinline__ void e2m1x8_to_bf16x8(uint32_t w, uint32_t (&o)[4]) {
   constexpr uint32_t kHiA = 0x3F3F3F00u, kHiB = 0x40404040u;  // high bytes of magnitudes 0..3, 4..7
   constexpr uint32_t kLoA = 0xC0800000u, kLoB = 0xC0804000u;  // low bytes
   const uint32_t m = w & 0x77777777u;
-  const uint32_t hi03 = __byte_perm(kHiA, kHiB, m), lo03 = __byte_perm(kLoA, kLoB, m);
-  const uint32_t hi47 = __byte_perm(kHiA, kHiB, m >> 16), lo47 = __byte_perm(kLoA, kLoB, m >> 16);
-  o[0] = __byte_perm(lo03, hi03, 0x5140) | ((w << 12) & 0x8000u) | ((w << 24) & 0x80000000u);
-  o[1] = __byte_perm(lo03, hi03, 0x7362) | ((w << 4) & 0x8000u) | ((w << 16) & 0x80000000u);
-  o[2] = __byte_perm(lo47, hi47, 0x5140) | ((w >> 4) & 0x8000u) | ((w << 8) & 0x80000000u);
-  o[3] = __byte_perm(lo47, hi47, 0x7362) | ((w >> 12) & 0x8000u) | (w & 0x80000000u);
+  const uint32_t w4 = w << 4;
+  const uint32_t hi03 = prmt(kHiA, kHiB, m) | (prmt(w4, w, 0xD9C8u) & 0x80808080u);
+  const uint32_t hi47 = prmt(kHiA, kHiB, m >> 16) | (prmt(w4, w, 0xFBEAu) & 0x80808080u);
+  const uint32_t lo03 = prmt(kLoA, kLoB, m), lo47 = prmt(kLoA, kLoB, m >> 16);
+  o[0] = prmt(lo03, hi03, 0x5140u);
+  o[1] = prmt(lo03, hi03, 0x7362u);
+  o[2] = prmt(lo47, hi47, 0x5140u);
+  o[3] = prmt(lo47, hi47, 0x7362u);
 }
 
 template <int BN, int STAGES>
@@ -146,12 +164,14 @@ __global__ void __launch_bounds__(kQThreads, 1)
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  // stage s: [wide bf16 16 KB][act BN x 128 B][packed 4 KB][scales 256 B]
-  uint8_t* xchg = smem + kStages * S::kStage;
-  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + S::kXchg);
-  uint64_t* wide = full + kStages;
-  uint64_t* empty = wide + kStages;
-  uint64_t* done = empty + kStages;
+  uint8_t* wide_buf = smem;                         // two expanded 128 x 64 bf16 weight tiles
+  uint8_t* ring = smem + S::kWide;                   // stage s at ring + s * kStage: [act][packed][scales]
+  uint8_t* xchg = ring + kStages * S::kStage;
+  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + S::kXchg);  // [kStages] copies landed
+  uint64_t* empty = full + kStages;                                 // [kStages] MMA done with the stage
+  uint64_t* wfull = empty + kStages;                                // [2] expanded tile written
+  uint64_t* wempty = wfull + 2;                                     // [2] MMA done with the expanded tile
+  uint64_t* done = wempty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(done + 1);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -166,8 +186,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&wide[s], 4);
       mbar_init(&empty[s], 1);
+    }
+    for (int w = 0; w < 2; ++w) {
+      mbar_init(&wfull[w], 4);
+      mbar_init(&wempty[w], 1);
     }
     mbar_init(done, 1);
     fence_barrier_init();
@@ -192,12 +215,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
       for (int kb = 0; kb < nkb; ++kb) {
         const int s = kb % kStages;
         if (kb >= kStages && !mbar_wait(&empty[s], ((kb / kStages) - 1) & 1, p.err, 401)) break;
-        uint8_t* st = smem + s * S::kStage;
+        uint8_t* st = ring + s * S::kStage;
         mbar_arrive_expect_tx(&full[s], S::kAct + kPackedBytes + kScaleBytes);
-        tma_load_2d(st + kWideBytes, &tm_x, &full[s], kb * QBK, row0);
-        tma_load_2d(st + kWideBytes + S::kAct, &tm_w, &full[s], kb * (QBK / 2), expert * p.N + n0);
-        bulk_load(st + kWideBytes + S::kAct + kPackedBytes, sc + static_cast<int64_t>(kb) * p.N * 2, kScaleBytes,
-                  &full[s]);
+        tma_load_2d(st, &tm_x, &full[s], kb * QBK, row0);
+        tma_load_2d(st + S::kAct, &tm_w, &full[s], kb * (QBK / 2), expert * p.N + n0);
+        bulk_load(st + S::kAct + kPackedBytes, sc + static_cast<int64_t>(kb) * p.N * 2, kScaleBytes, &full[s]);
       }
     }
     __syncwarp();
@@ -205,18 +227,20 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // ------------------------------------------------------------ MMA ----
     constexpr uint32_t idesc = make_idesc_bf16(QBM, BN);
     for (int kb = 0; kb < nkb && ok; ++kb) {
-      const int s = kb % kStages;
-      ok = __all_sync(0xffffffffu, mbar_wait(&wide[s], (kb / kStages) & 1, p.err, 402));
+      const int s = kb % kStages, w = kb & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&wfull[w], (kb >> 1) & 1, p.err, 402) &&
+                                       mbar_wait(&full[s], (kb / kStages) & 1, p.err, 405));
       if (!ok) break;
       tc_fence_after();
       if (lane == 0) {
-        const uint32_t a = smem_u32(smem + s * S::kStage);
-        const uint32_t b = a + kWideBytes;
+        const uint32_t a = smem_u32(wide_buf + w * kWideBytes);
+        const uint32_t b = smem_u32(ring + s * S::kStage);
 #pragma unroll
         for (int k = 0; k < QBK / 16; ++k)
           tc_mma_f16(tmem, make_sdesc_k_sw128(a + k * 32), make_sdesc_k_sw128(b + k * 32), idesc,
                      (kb > 0 || k > 0) ? 1u : 0u);
         tc_commit(&empty[s]);
+        tc_commit(&wempty[w]);
       }
       __syncwarp();
     }
@@ -226,12 +250,14 @@ __global__ void __launch_bounds__(kQThreads, 1)
     // --------------------------------------------------- expand + store ----
     const int r = threadIdx.x - 64;  // weight row of this thread (0..127)
     for (int kb = 0; kb < nkb && ok; ++kb) {
-      const int s = kb % kStages;
-      ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (kb / kStages) & 1, p.err, 403));
+      const int s = kb % kStages, w = kb & 1;
+      ok = __all_sync(0xffffffffu, mbar_wait(&full[s], (kb / kStages) & 1, p.err, 403) &&
+                                       (kb < 2 || mbar_wait(&wempty[w], ((kb >> 1) - 1) & 1, p.err, 406)));
       if (!ok) break;
-      uint8_t* st = smem + s * S::kStage;
-      const uint4* src = reinterpret_cast<const uint4*>(st + kWideBytes + S::kAct + r * 32);
-      const uint8_t* scl = st + kWideBytes + S::kAct + kPackedBytes + r * 2;
+      uint8_t* st = ring + s * S::kStage;
+      uint8_t* dst = wide_buf + w * kWideBytes;
+      const uint4* src = reinterpret_cast<const uint4*>(st + S::kAct + r * 32);
+      const uint8_t* scl = st + S::kAct + kPackedBytes + r * 2;
       // 2^(byte - 127) as a bf16x2 multiplier (exact: a power of two)
       uint32_t mul[2];
 #pragma unroll
@@ -252,11 +278,11 @@ __global__ void __launch_bounds__(kQThreads, 1)
                                            *reinterpret_cast<const __nv_bfloat162*>(&mul[c >> 2]));
           o[b] = *reinterpret_cast<const uint32_t*>(&v);
         }
-        *reinterpret_cast<uint4*>(st + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(dst + r * 128 + ((c ^ (r & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
       }
       fence_proxy_async_smem();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&wide[s]);
+      if (lane == 0) mbar_arrive(&wfull[w]);
     }
     // epilogue: TMEM lane r holds weight row n0 + r for the BN tokens
     ok = __all_sync(0xffffffffu, ok && mbar_wait(done, 0, p.err, 404));
@@ -354,18 +380,13 @@ namespace minisgl {
 void launch_moe_mxfp4_gemm(const MoeMxfp4GemmArgs& a, cudaStream_t s) {
   if (a.N % 128 != 0 || a.K % 64 != 0) throw std::runtime_error("minisgl.moe_mxfp4: N % 128 == 0 and K % 64 == 0");
   if (a.P % a.tile != 0) throw std::runtime_error("minisgl.moe_mxfp4: rows must be a multiple of the tile");
-  static const bool deep = [] {
-    const char* v = std::getenv("MINISGL_MXFP4_STAGES");
-    return v != nullptr && std::string(v) == "4";
-  }();
   switch (a.tile) {
-    // token tiles up to 64: three stages (about 107 KB), so two CTAs share an
-    // SM and one's converter work overlaps the other's copies;
-    // MINISGL_MXFP4_STAGES=4 keeps one CTA per SM with a deeper ring
-    case 16: deep ? launch_q<16, 4>(a, s) : launch_q<16, 3>(a, s); break;
-    case 32: deep ? launch_q<32, 4>(a, s) : launch_q<32, 3>(a, s); break;
-    case 64: deep ? launch_q<64, 4>(a, s) : launch_q<64, 3>(a, s); break;
-    case 128: launch_q<128, 4>(a, s); break;
+    // copy-ring depths: two CTAs share an SM up to 64-token tiles (about
+    // 92-101 KB each), one CTA holds a 6-deep ring at 128
+    case 16: launch_q<16, 8>(a, s); break;
+    case 32: launch_q<32, 6>(a, s); break;
+    case 64: launch_q<64, 4>(a, s); break;
+    case 128: launch_q<128, 6>(a, s); break;
     default: throw std::runtime_error("minisgl.moe_mxfp4: tile of 16, 32, 64 or 128");
   }
 }
