@@ -153,13 +153,15 @@ def bench_moe_mxfp4(T: int, E: int, k: int, H: int, I: int, peaks) -> Dict:
     tw = torch.full((T, k), 1.0 / k, device="cuda")
     hit = int(torch.unique(ids).numel())
     ms = time_kernel(lambda: ops.moe_experts_mxfp4(x, *q1, *q2, tw, ids))
+    tiles = {t: round(time_kernel(lambda t=t: ops.moe_experts_mxfp4(x, *q1, *q2, tw, ids, tile=t)), 4)
+             for t in (16, 32, 64, 128) if t <= max(16, 2 * T * k // E)}
     ms_bf16 = time_kernel(lambda: ops.moe_experts(x, w1, w2, tw, ids))
     wbytes = hit * (3 * I * H) * 0.5 * (1 + 1 / 16)  # E2M1 + one E8M0 byte per 32
     nbytes = wbytes + 2 * 2 * T * k * H
     gbs = nbytes / ms / 1e6
     return {"kernel": "moe_experts_mxfp4", "T": T, "E": E, "k": k, "H": H, "I": I, "experts_hit": hit,
             "ms": round(ms, 4), "bf16_ms": round(ms_bf16, 4), "GB/s": round(gbs, 1),
-            "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
+            "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "ms_by_token_tile": tiles}
 
 
 def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:

@@ -99,15 +99,17 @@ constexpr int kWideBytes = QBM * QBK * 2;     // 16 KB of expanded bf16
 
 template <int BN, int STAGES>
 struct QSmem {
-  // [expanded bf16 weights: 2 x 16 KB][STAGES x (token tile | packed | scales)][SiLU exchange][barriers]
+  // [expanded bf16 weights: 2 x 16 KB][STAGES x (token tile | packed | scales)][barriers]; the SiLU
+  // exchange of the epilogue reuses the ring (every copy has been consumed by then)
   // The copy ring is deep and cheap (6-13 KB a stage); only the two
   // expanded tiles the converter and the MMA hand back and forth are wide.
   static constexpr int kAct = BN * QBK * 2;
   static constexpr int kStage = (kAct + kPackedBytes + kScaleBytes + 1023) / 1024 * 1024;  // swizzle alignment
   static constexpr int kStages = STAGES;
   static constexpr int kWide = 2 * kWideBytes;
-  static constexpr int kXchg = 64 * BN * 4;   // SiLU epilogue: the up rows, fp32
-  static constexpr int kBytes = 1024 + kWide + kStages * kStage + kXchg + 256;
+  static constexpr int kXchg = 64 * BN * 4;   // SiLU epilogue: the up rows, fp32 (aliases the ring)
+  static constexpr int kRing = kStages * kStage > kXchg ? kStages * kStage : kXchg;
+  static constexpr int kBytes = 1024 + kWide + kRing + 256;
 };
 
 struct QParams {
@@ -166,8 +168,8 @@ __global__ void __launch_bounds__(kQThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* wide_buf = smem;                         // two expanded 128 x 64 bf16 weight tiles
   uint8_t* ring = smem + S::kWide;                   // stage s at ring + s * kStage: [act][packed][scales]
-  uint8_t* xchg = ring + kStages * S::kStage;
-  uint64_t* full = reinterpret_cast<uint64_t*>(xchg + S::kXchg);  // [kStages] copies landed
+  uint8_t* xchg = ring;                              // epilogue only: after the last MMA completed
+  uint64_t* full = reinterpret_cast<uint64_t*>(ring + S::kRing);  // [kStages] copies landed
   uint64_t* empty = full + kStages;                                 // [kStages] MMA done with the stage
   uint64_t* wfull = empty + kStages;                                // [2] expanded tile written
   uint64_t* wempty = wfull + 2;                                     // [2] MMA done with the expanded tile
@@ -381,12 +383,11 @@ void launch_moe_mxfp4_gemm(const MoeMxfp4GemmArgs& a, cudaStream_t s) {
   if (a.N % 128 != 0 || a.K % 64 != 0) throw std::runtime_error("minisgl.moe_mxfp4: N % 128 == 0 and K % 64 == 0");
   if (a.P % a.tile != 0) throw std::runtime_error("minisgl.moe_mxfp4: rows must be a multiple of the tile");
   switch (a.tile) {
-    // copy-ring depths: two CTAs share an SM up to 64-token tiles (about
-    // 92-101 KB each), one CTA holds a 6-deep ring at 128
+    // copy-ring depths chosen so two CTAs share an SM (91-100 KB each)
     case 16: launch_q<16, 8>(a, s); break;
     case 32: launch_q<32, 6>(a, s); break;
-    case 64: launch_q<64, 4>(a, s); break;
-    case 128: launch_q<128, 6>(a, s); break;
+    case 64: launch_q<64, 5>(a, s); break;
+    case 128: launch_q<128, 3>(a, s); break;
     default: throw std::runtime_error("minisgl.moe_mxfp4: tile of 16, 32, 64 or 128");
   }
 }

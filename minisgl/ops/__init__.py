@@ -643,6 +643,15 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_w: tor
     return out
 
 
+def moe_tile_mxfp4(tokens: int, k: int, experts: int) -> int:
+    """Token tile of the MXFP4 expert GEMMs: every tile expands its expert's
+    weights to bf16 again, so tiles grow to 128 rows once an expert gets more
+    than 64 (measured at Kimi-K2 expert dims: 0.51 vs 0.61 ms at 128 rows per
+    expert)."""
+    avg = tokens * k / max(1, experts)
+    return 16 if avg <= 16 else 32 if avg <= 48 else 64 if avg <= 64 else 128
+
+
 def moe_experts_mxfp4(x: torch.Tensor, w1q: torch.Tensor, w1s: torch.Tensor, w2q: torch.Tensor, w2s: torch.Tensor,
                       topk_w: torch.Tensor, topk_ids: torch.Tensor, tile: int = 0) -> torch.Tensor:
     """``moe_experts`` with MXFP4 expert weights (packed [E, N, K / 2] +
@@ -654,7 +663,7 @@ def moe_experts_mxfp4(x: torch.Tensor, w1q: torch.Tensor, w1s: torch.Tensor, w2q
     out = torch.empty(T, H, dtype=x.dtype, device=x.device)
     if T == 0:
         return out
-    tile = tile or moe_tile(T, k, E)
+    tile = tile or moe_tile_mxfp4(T, k, E)
     P = T * k + E * (tile - 1)
     Pp = (P + tile - 1) // tile * tile
     dev, i32 = x.device, torch.int32
@@ -682,7 +691,7 @@ def moe_experts_rows(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tens
     k = topk_ids.shape[1]
     E = (mxfp4[0] if mxfp4 is not None else w1).shape[0]
     I = (mxfp4[2].shape[2] * 2) if mxfp4 is not None else w2.shape[2]
-    tile = tile or moe_tile(T, k, E)
+    tile = tile or (moe_tile_mxfp4(T, k, E) if mxfp4 is not None else moe_tile(T, k, E))
     P = T * k + E * (tile - 1)
     Pp = (P + tile - 1) // tile * tile
     dev, i32 = x.device, torch.int32
