@@ -35,7 +35,11 @@ class DecodeManager:
     def schedule_next_batch(self) -> Optional[Batch]:
         if not self.running_reqs:
             return None
-        return Batch(reqs=sorted(self.running_reqs, key=lambda r: r.uid), phase="decode")
+        # longest first: the decode attention grid walks requests in batch
+        # order, so long requests start in the first waves and the last wave
+        # holds only short ones (longest-processing-time scheduling of the
+        # split-KV CTAs); uid breaks ties, so the order is deterministic
+        return Batch(reqs=sorted(self.running_reqs, key=lambda r: (-r.device_len, r.uid)), phase="decode")
 
     @property
     def runnable(self) -> bool:
