@@ -164,6 +164,21 @@ def bench_moe_mxfp4(T: int, E: int, k: int, H: int, I: int, peaks) -> Dict:
             "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "ms_by_token_tile": tiles}
 
 
+def bench_sample(B: int, V: int, peaks) -> List[Dict]:
+    """Sampling from fp32 logits [B, V]: argmax (greedy) and Gumbel-max with
+    temperature (counter-based noise); bytes = the logits read once."""
+    logits = torch.randn(B, V, device="cuda") * 0.7
+    temps = torch.full((B,), 0.6, device="cuda")
+    out = []
+    for name, fn in (("argmax", lambda: ops.argmax(logits)),
+                     ("sample_temperature", lambda: ops.sample(logits, temps, None, None, 1234, None))):
+        ms = time_kernel(fn)
+        gbs = B * V * 4 / ms / 1e6
+        out.append({"kernel": name, "B": B, "V": V, "us": round(ms * 1000, 2), "GB/s": round(gbs, 1),
+                    "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)})
+    return out
+
+
 def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
     x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
     w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02
@@ -341,6 +356,8 @@ def main() -> None:
     for M in (1, 8, 32, 64, 128, 192, 256):
         cases.append((f"layer_chain M={M};", lambda M=M: bench_layer_chain(M, peaks)))
     cases.append(("rowkernels M=256", lambda: bench_row_kernels(256, peaks)))
+    for B in (64, 256):
+        cases.append((f"sample B={B}", lambda B=B: bench_sample(B, 151936, peaks)))
     rows: List[Dict] = []
     for label, fn in cases:
         if args.only and args.only not in label:

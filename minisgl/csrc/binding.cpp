@@ -953,9 +953,19 @@ void argmax(at::Tensor out, const at::Tensor& logits) {
             "logits must be float32 [B, V]");
   MSG_CHECK(out.numel() == logits.size(0), "argmax output size");
   const c10::cuda::CUDAGuard guard(logits.device());
-  minisgl::launch_argmax(out.data_ptr<int32_t>(), logits.data_ptr<float>(),
-                         static_cast<int>(logits.size(0)), static_cast<int>(logits.size(1)),
-                         static_cast<int>(logits.stride(0)), stream_of(logits));
+  const int64_t B = logits.size(0);
+  if (B == 0) return;
+  // rows split over vocabulary chunks (partials from torch's allocator)
+  const int64_t parts = B * minisgl::sample_split_chunks(static_cast<int>(logits.size(1)));
+  at::Tensor pv = at::empty({parts}, logits.options());
+  at::Tensor pi = at::empty({parts}, logits.options().dtype(at::kInt));
+  minisgl::SampleArgs a{};
+  a.out = out.data_ptr<int32_t>();
+  a.logits = logits.data_ptr<float>();
+  a.ld = static_cast<int>(logits.stride(0));
+  a.B = static_cast<int>(B);
+  a.V = static_cast<int>(logits.size(1));
+  minisgl::launch_sample_split(a, pv.data_ptr<float>(), pi.data_ptr<int32_t>(), stream_of(logits));
 }
 
 void sample(at::Tensor out, const at::Tensor& logits, const at::Tensor& temperature,
@@ -995,6 +1005,15 @@ void sample(at::Tensor out, const at::Tensor& logits, const at::Tensor& temperat
     a.step = step->data_ptr<int64_t>();
   }
   const c10::cuda::CUDAGuard guard(logits.device());
+  if (a.top_k == nullptr && a.top_p == nullptr && B > 0) {
+    // plain temperature sampling: rows split over vocabulary chunks (the
+    // step counter advances in the reduce, as in the LM-head sampling path)
+    const int64_t parts = B * minisgl::sample_split_chunks(a.V);
+    at::Tensor pv = at::empty({parts}, logits.options());
+    at::Tensor pi = at::empty({parts}, logits.options().dtype(at::kInt));
+    minisgl::launch_sample_split(a, pv.data_ptr<float>(), pi.data_ptr<int32_t>(), stream_of(logits));
+    return;
+  }
   minisgl::launch_sample(a, stream_of(logits));
 }
 

@@ -219,6 +219,11 @@ struct SampleArgs {
   const int64_t* step;       // device counter mixed into the random stream (may be nullptr)
 };
 void launch_sample(const SampleArgs& a, cudaStream_t s);
+// Greedy (temperature == nullptr) or temperature sampling with each row
+// split over vocabulary chunks: partials [B, sample_split_chunks(V)] then
+// the per-row reduce; same tokens as launch_argmax / launch_sample.
+int sample_split_chunks(int V);
+void launch_sample_split(const SampleArgs& a, float* part_val, int32_t* part_idx, cudaStream_t s);
 void launch_lm_sample_reduce(int32_t* out, const float* part_val, const int32_t* part_idx, int ntiles, int B,
                              const float* temps, int64_t* step, cudaStream_t s);
 

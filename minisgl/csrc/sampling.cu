@@ -212,6 +212,52 @@ __global__ void lm_sample_reduce_kernel(int32_t* out, const float* part_val, con
   }
 }
 
+// Split rows: CTA (c, b) scans vocabulary chunk c of row b and writes its
+// best (score, index): the plain logit without temperatures (greedy), else
+// logit / T + Gumbel noise of the same counter-based stream the whole-row
+// kernel draws. lm_sample_reduce_kernel then picks each row's winner with
+// the same tie rule, so tokens equal the whole-row kernels' tokens; a row no
+// longer occupies one SM for its whole vocabulary (64 rows kept 64 SMs busy).
+constexpr int kPartThreads = 256;
+constexpr int kPartChunk = 8192;  // 8 float4 per thread
+
+__global__ void __launch_bounds__(kPartThreads) sample_part_kernel(SampleArgs a, float* part_val,
+                                                                   int32_t* part_idx, int nchunks) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int b = blockIdx.y, c = blockIdx.x;
+  const float* row = a.logits + static_cast<int64_t>(b) * a.ld;
+  const bool greedy = a.temperature == nullptr;
+  const float inv_t = greedy ? 1.f : 1.f / fmaxf(a.temperature[b], 1e-6f);
+  const uint64_t step = a.step != nullptr ? static_cast<uint64_t>(*a.step) : 0ull;
+  const uint32_t key = row_key(a.seed, step, b);
+  const int i0 = c * kPartChunk, i1 = min(a.V, i0 + kPartChunk);
+  ArgMax best{-INFINITY, 0x7fffffff};
+  if ((a.V & 3) == 0 && (a.ld & 3) == 0) {
+    const float4* row4 = reinterpret_cast<const float4*>(row);
+#pragma unroll 4
+    for (int i4 = i0 / 4 + static_cast<int>(threadIdx.x); i4 < i1 / 4; i4 += kPartThreads) {
+      const float4 l4 = row4[i4];
+      const float ls[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int i = i4 * 4 + q;
+        best = better(best, ArgMax{greedy ? ls[q] : ls[q] * inv_t + gumbel(key, i), i});
+      }
+    }
+  } else {
+    for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += kPartThreads) {
+      const float l = row[i];
+      best = better(best, ArgMax{greedy ? l : l * inv_t + gumbel(key, i), i});
+    }
+  }
+  best = block_argmax(best);
+  if (threadIdx.x == 0) {
+    part_val[static_cast<int64_t>(b) * nchunks + c] = best.v;
+    part_idx[static_cast<int64_t>(b) * nchunks + c] = best.i;
+  }
+}
+
 __global__ void bump_step_kernel(int64_t* step) {
   pdl_launch_dependents();
   pdl_wait();  // the sampling kernel reads the counter first
@@ -229,6 +275,17 @@ void launch_lm_sample_reduce(int32_t* out, const float* part_val, const int32_t*
                              const float* temps, int64_t* step, cudaStream_t s) {
   if (B <= 0) return;
   launch_pdl(lm_sample_reduce_kernel, dim3(B), dim3(256), 0, s, out, part_val, part_idx, ntiles, B, temps, step);
+}
+
+int sample_split_chunks(int V) { return (V + kPartChunk - 1) / kPartChunk; }
+
+void launch_sample_split(const SampleArgs& a, float* part_val, int32_t* part_idx, cudaStream_t s) {
+  if (a.B <= 0) return;
+  if (a.top_k != nullptr || a.top_p != nullptr)
+    throw std::runtime_error("minisgl.sample: split rows take greedy / temperature sampling only");
+  const int nchunks = sample_split_chunks(a.V);
+  launch_pdl(sample_part_kernel, dim3(nchunks, a.B), dim3(kPartThreads), 0, s, a, part_val, part_idx, nchunks);
+  launch_lm_sample_reduce(a.out, part_val, part_idx, nchunks, a.B, a.temperature, const_cast<int64_t*>(a.step), s);
 }
 
 void launch_sample(const SampleArgs& a, cudaStream_t s) {
