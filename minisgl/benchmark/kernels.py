@@ -194,7 +194,7 @@ def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
     row = {"kernel": f"gemm[{label}]", "M": M, "N": N, "K": K, "ms": round(ms, 4), "cublas_ms": round(ms_cublas, 4),
            "graph_ms": round(ms_graph, 4), "cublas_graph_ms": round(ms_cublas_graph, 4),
            "TFLOP/s": round(tf, 1), "GB/s": round(gbs, 1), "frac_roofline": round(bound / ms, 3)}
-    if M >= 512 and K % 64 == 0:
+    if M >= 128 and K % 64 == 0:
         # persistent tiles (plan mode 3), both N tiles
         nat = ops.native()
         for bn in (256, 128):

@@ -55,6 +55,10 @@ def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
             for s in (1, 2, 4, 8):
                 if s <= num_kb:
                     out.append((1, bn, s))
+    if M >= 64 and K % 64 == 0:
+        # persistent 128 x N-tile CTAs: win on wide outputs such as the LM
+        # head (151936 features at 256 rows: 0.106 vs 0.138 ms)
+        out += [(3, 256, 1), (3, 128, 1)]
     return out
 
 
