@@ -255,8 +255,10 @@ class Engine:
 
     def _load_weights(self, config: EngineConfig) -> Dict[str, torch.Tensor]:
         if config.use_dummy_weight:
+            mcfg = config.model_config
+            first = mcfg.ep_rank * (mcfg.num_experts // mcfg.ep_size) if mcfg.ep_size > 1 else 0
             return random_weights(self.model.state_dict(), self.device, seed=config.weight_seed,
-                                  gen_device=config.dummy_weight_device)
+                                  gen_device=config.dummy_weight_device, first_expert=first)
         out: Dict[str, torch.Tensor] = {}
         mcfg = config.model_config
         for name, t in load_weight(config.model_path, self.device, ep_size=mcfg.ep_size, ep_rank=mcfg.ep_rank):

@@ -129,7 +129,8 @@ def load_weight(model_path: str, device: torch.device, *, ep_size: int = 1,
 
 
 def random_weights(shapes: Dict[str, torch.Tensor], device: torch.device, seed: int = 0,
-                   std: float = 0.02, gen_device: Optional[torch.device] = None) -> Dict[str, torch.Tensor]:
+                   std: float = 0.02, gen_device: Optional[torch.device] = None,
+                   first_expert: int = 0) -> Dict[str, torch.Tensor]:
     """N(0, std) for matrices, ones for norm weights, zeros for biases.
     ``shapes`` maps names to (meta) tensors giving shape and dtype. With
     ``gen_device`` the numbers are drawn there (e.g. on the CPU, so a GPU
@@ -146,6 +147,16 @@ def random_weights(shapes: Dict[str, torch.Tensor], device: torch.device, seed: 
             t = torch.ones(ref.shape, dtype=dt, device=device)
         elif "bias" in name:
             t = torch.zeros(ref.shape, dtype=dt, device=device)
+        elif name.endswith(("experts.gate_up_proj", "experts.down_proj")) and ref.dim() == 3:
+            # stacked routed experts: one seed per global expert, so under
+            # expert parallelism every rank holds its own experts' values
+            t = torch.empty(ref.shape, dtype=dt, device=device)
+            for e in range(ref.shape[0]):
+                gen.manual_seed(seed * 1000003 + zlib.crc32(f"{name}.{first_expert + e}".encode()))
+                part = torch.empty(ref.shape[1:], dtype=torch.float32 if gen_dev.type == "cpu" else dt,
+                                   device=gen_dev)
+                part.normal_(0.0, std, generator=gen)
+                t[e].copy_(part)
         else:
             # per-name seed: identical on every rank, so replicated weights agree
             gen.manual_seed(seed * 1000003 + zlib.crc32(name.encode()))

@@ -107,3 +107,16 @@ def test_tp2_kimi_checkpoint_matches_single_rank(kimi_checkpoint):
     single = _generate(1, kimi_checkpoint, False, PROMPTS, lens)[0]
     tp = _generate(2, kimi_checkpoint, False, PROMPTS, lens)
     assert tp[0] == tp[1] == single
+
+
+def test_random_init_experts_are_per_global_expert():
+    """--random-init under expert parallelism: rank r's local expert j has
+    the values the single-rank model gives global expert r * E / R + j."""
+    from minisgl.models.weight import random_weights
+
+    full = {"model.layers.1.mlp.experts.gate_up_proj": torch.empty(8, 16, 32, device="meta")}
+    half = {"model.layers.1.mlp.experts.gate_up_proj": torch.empty(4, 16, 32, device="meta")}
+    w = random_weights(full, torch.device("cpu"))["model.layers.1.mlp.experts.gate_up_proj"]
+    r1 = random_weights(half, torch.device("cpu"), first_expert=4)["model.layers.1.mlp.experts.gate_up_proj"]
+    r0 = random_weights(half, torch.device("cpu"), first_expert=0)["model.layers.1.mlp.experts.gate_up_proj"]
+    assert torch.equal(r0, w[:4]) and torch.equal(r1, w[4:])
