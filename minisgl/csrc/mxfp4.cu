@@ -107,7 +107,7 @@ struct QSmem {
   static constexpr int kStage = (kAct + kPackedBytes + kScaleBytes + 1023) / 1024 * 1024;  // swizzle alignment
   static constexpr int kStages = STAGES;
   static constexpr int kWide = 2 * kWideBytes;
-  static constexpr int kXchg = 64 * BN * 4;   // SiLU epilogue: the up rows, fp32 (aliases the ring)
+  static constexpr int kXchg = 64 * BN * 4;   // SiLU epilogue: the up rows, fp32, column-major (aliases the ring)
   static constexpr int kRing = kStages * kStage > kXchg ? kStages * kStage : kXchg;
   static constexpr int kBytes = 1024 + kWide + kRing + 256;
 };
@@ -311,7 +311,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
           out[static_cast<int64_t>(row0 + c + j) * p.ldo + n0 + lrow] = __float2bfloat16_rn(__uint_as_float(v[j]));
       } else if (ok && lrow >= 64) {
 #pragma unroll
-        for (int j = 0; j < CH; ++j) up[(lrow - 64) * BN + c + j] = __uint_as_float(v[j]);
+        for (int j = 0; j < CH; ++j) up[(c + j) * 64 + (lrow - 64)] = __uint_as_float(v[j]);  // lanes contiguous
       }
       if (p.silu) {
         asm volatile("bar.sync 1, 128;" ::: "memory");  // up rows of this column block are parked
@@ -320,7 +320,7 @@ __global__ void __launch_bounds__(kQThreads, 1)
 #pragma unroll
           for (int j = 0; j < CH; ++j) {
             const float g = __uint_as_float(v[j]);
-            const float u = up[lrow * BN + c + j];
+            const float u = up[(c + j) * 64 + lrow];
             out[static_cast<int64_t>(row0 + c + j) * p.ldo + f] = __float2bfloat16_rn(g / (1.f + __expf(-g)) * u);
           }
         }

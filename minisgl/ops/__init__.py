@@ -530,7 +530,7 @@ def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
         return y
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
-    _count()
+    _count(2)  # vocabulary-chunk partials + per-row reduce
     native().argmax(out, logits.float() if logits.dtype != torch.float32 else logits)
     return out
 
