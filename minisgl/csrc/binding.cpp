@@ -585,6 +585,7 @@ void mla_prepare(at::Tensor q_pe, at::Tensor xs, const at::Tensor& q, const at::
   a.rope = static_cast<int>(rope);
   a.cp_size = static_cast<int>(cp_size);
   a.cp_rank = static_cast<int>(cp_rank);
+  a.page_size = static_cast<int>(latent.size(1));
   a.err = err_ptr(err);
   minisgl::launch_mla_prepare(a, stream_of(q));
 }

@@ -84,9 +84,11 @@ __global__ void __launch_bounds__(256) mla_prepare_kernel(MlaPrepareArgs a) {
 #pragma unroll
   for (int i = 0; i < 8; ++i) tot += red[i];
   const float rstd = rsqrtf(tot / kLora + a.eps);
-  const int64_t slot = a.out_loc[t];
-  // context parallelism: the row lives on the rank owning its 64-key tile
+  int64_t slot = a.out_loc[t];
+  // context parallelism: the row lives on the rank owning its 64-key tile,
+  // in that rank's pool at local page (global page) / cp
   const bool store = a.cp_size <= 1 || (a.positions[t] / kKeys) % a.cp_size == a.cp_rank;
+  if (a.cp_size > 1) slot = (slot / a.page_size / a.cp_size) * a.page_size + slot % a.page_size;
   __nv_bfloat16* lat = reinterpret_cast<__nv_bfloat16*>(a.latent) + slot * kLat;
   const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
   {
@@ -254,7 +256,7 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
       const int segs = kKeys / seg;  // segments per tile
       auto page_of = [&](int k) {  // page id of segment k (positions past the end: page 0, masked later)
         const int pos = tile_pos(k / segs) + (k % segs) * seg;
-        return pos < len ? pt[pos] / P : 0;
+        return pos < len ? pt[pos] / P / cp : 0;  // context parallelism: local page (global page) / cp
       };
       int base = 0;
       int cur = page_of(lane), nxt = page_of(32 + lane);

@@ -172,6 +172,7 @@ struct MlaPrepareArgs {
   void* xs;               // out: [H, T_pad, nope] (grouped GEMM input)
   int T, T_pad, H, nope, kv_lora, rope;
   int cp_size, cp_rank;   // context parallelism: store only rows of owned 64-key tiles
+  int page_size;          // (at local page = global page / cp_size)
   int* err;
 };
 struct MlaAttnArgs {

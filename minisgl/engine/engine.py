@@ -128,9 +128,17 @@ class Engine:
 
         # ---------------------------------------------------------- KV cache
         self.num_pages = self._determine_num_pages(init_free, config)
+        self.cp_size = config.cp_size if config.cp_size > 1 else 1
+        if self.cp_size > 1:
+            # context parallelism: page g lives on rank g % cp at local index
+            # g // cp, so each rank allocates 1 / cp of the pages
+            if page_size != 64:
+                raise ValueError("context parallelism needs page size 64 (one page per 64-key tile)")
+            self.num_pages -= self.num_pages % self.cp_size
         num_tokens = self.num_pages * page_size
         self.ctx.kv_cache = self.kv_cache = create_kvcache_pool(
-            mcfg, self.num_pages + 1, page_size, self.dtype, self.device)  # +1: the dummy page
+            mcfg, self.num_pages + 1, page_size, self.dtype, self.device,
+            cp_size=self.cp_size)  # +1: the dummy page
         self.max_seq_len = min(config.max_seq_len, num_tokens)
         width = align_ceil(self.max_seq_len + page_size, max(64, page_size))
         self.ctx.page_table = self.page_table = torch.zeros(
@@ -285,8 +293,9 @@ class Engine:
     def _bytes_per_page(self) -> int:
         m = self.model_config
         itemsize = self.dtype.itemsize
-        if m.is_mla:
-            return m.num_layers * self.page_size * (m.kv_lora_rank + m.qk_rope_head_dim) * itemsize
+        if m.is_mla:  # under context parallelism a rank stores one page in cp
+            cp = self.config.cp_size if self.config.cp_size > 1 else 1
+            return max(1, m.num_layers * self.page_size * (m.kv_lora_rank + m.qk_rope_head_dim) * itemsize // cp)
         from minisgl.utils import div_even
 
         kv = div_even(m.num_kv_heads, get_tp_info().size, allow_replicate=True)

@@ -35,12 +35,12 @@ def create_prefix_cache(device: torch.device, type: str, page_size: int = 1) -> 
 
 
 def create_kvcache_pool(model_config: "ModelConfig", num_pages: int, page_size: int, dtype: torch.dtype,
-                        device: torch.device) -> BaseKVCachePool:
+                        device: torch.device, cp_size: int = 1) -> BaseKVCachePool:
     if model_config.is_mla:
         from .mla_pool import MLAKVCache
 
         return MLAKVCache(model_config.num_layers, model_config.kv_lora_rank, model_config.qk_rope_head_dim,
-                          num_pages, page_size, dtype, device)
+                          num_pages, page_size, dtype, device, cp_size=cp_size)
     from .mha_pool import MHAKVCache
 
     return MHAKVCache(model_config.num_kv_heads, model_config.num_layers, model_config.head_dim, num_pages,

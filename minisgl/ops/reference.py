@@ -220,10 +220,11 @@ def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_
     k_pe = rope_interleaved(kv_a[:, kv_lora:], positions, cos_sin)
     loc = out_loc.long()
     rows = torch.cat([c, k_pe], dim=-1).to(latent.dtype)
-    if cp_size > 1:  # the row lives on the rank that owns its 64-key tile
+    page = loc // page_size
+    if cp_size > 1:  # the row lives on the rank that owns its 64-key tile, at local page g // cp
         keep = cp_owned(positions, cp_size, cp_rank)
-        loc, rows = loc[keep], rows[keep]
-    latent[loc // page_size, loc % page_size] = rows
+        loc, rows, page = loc[keep], rows[keep], page[keep] // cp_size
+    latent[page, loc % page_size] = rows
     q_pe = rope_interleaved(q[..., nope:], positions, cos_sin).contiguous()
     q_lat = torch.einsum("thn,hcn->htc", q[..., :nope].float(), w_uk_t.float()).to(q.dtype)
     return q_lat, q_pe
@@ -258,7 +259,9 @@ def mla_attention_partial(q_lat: torch.Tensor, q_pe: torch.Tensor, latent: torch
         mine = cp_owned(pos, cp_size, cp_rank)
         if not bool(mine.any()):
             continue
-        kv = latent.reshape(-1, D)[page_table[row, :L].long()].float()
+        slots = page_table[row, :L].long()
+        local = (slots // page_size // cp_size) * page_size + slots % page_size  # this rank's local page
+        kv = latent.reshape(-1, D)[torch.where(mine, local, torch.zeros_like(local))].float()
         scores = torch.einsum("nhd,ld->nhl", q[s:e], kv) * scale
         qpos = torch.arange(L - n, L, device=q.device)
         mask = (pos[None, :] > qpos[:, None]) | ~mine[None, :]

@@ -24,10 +24,14 @@ if TYPE_CHECKING:
 
 
 class CacheManager:
-    def __init__(self, num_pages: int, page_size: int, page_table: torch.Tensor, type: str) -> None:
+    def __init__(self, num_pages: int, page_size: int, page_table: torch.Tensor, type: str,
+                 page_classes: int = 1) -> None:
         self.device = page_table.device
         self.num_pages = num_pages
         self.page_size = page_size
+        # context parallelism: page id g is stored on rank g % page_classes, and
+        # page p of a sequence (its 64-key tile p) must live on rank p % classes
+        self.page_classes = page_classes
         self.page_table = page_table
         self.free_slots = torch.arange(num_pages, dtype=torch.int32, device=self.device) * page_size
         self.prefix_cache = create_prefix_cache(self.device, type, page_size)
@@ -64,7 +68,11 @@ class CacheManager:
                 need += last - first
         if need == 0:
             return
-        pages = self._allocate(need)
+        if self.page_classes > 1:
+            classes = torch.cat([torch.arange(first, last) % self.page_classes for _, first, last in plan])
+            pages = self._allocate_classes(classes)
+        else:
+            pages = self._allocate(need)
         _write_page_table(self.page_table, self._expand(pages), plan, self.page_size)
 
     def cache_req(self, req: Req, *, finished: bool) -> None:
@@ -113,6 +121,38 @@ class CacheManager:
             if len(self.free_slots) < pages:
                 raise RuntimeError("eviction did not free enough pages")
         out, self.free_slots = self.free_slots[:pages], self.free_slots[pages:]
+        return out
+
+    def _allocate_classes(self, classes: torch.Tensor) -> torch.Tensor:
+        """Page-start slots whose page id class (id % page_classes) is
+        classes[i], in that order; evicts cached pages until every class has
+        enough."""
+        K, P = self.page_classes, self.page_size
+        need = torch.bincount(classes, minlength=K)
+        for _ in range(8):
+            have = torch.bincount(((self.free_slots // P) % K).long().cpu(), minlength=K)
+            short = (need - have).clamp(min=0)
+            if int(short.sum()) == 0:
+                break
+            # evicted pages may fall into any class: ask for K times the worst shortfall
+            want = min(int(short.max()) * K * P, self.prefix_cache.size_info.evictable_size // P * P)
+            if want <= 0:
+                raise RuntimeError(f"no free or evictable pages of the classes needed ({short.tolist()} short)")
+            evicted = self.prefix_cache.evict(want)
+            self.free_slots = torch.cat([self.free_slots, evicted[::P]])
+        else:
+            raise RuntimeError("eviction did not free enough pages of the classes needed")
+        cls_of_free = ((self.free_slots // P) % K).long()
+        out = torch.empty(len(classes), dtype=self.free_slots.dtype, device=self.free_slots.device)
+        keep = torch.ones(len(self.free_slots), dtype=torch.bool, device=self.free_slots.device)
+        for c in range(K):
+            n = int(need[c])
+            if n == 0:
+                continue
+            idx = (cls_of_free == c).nonzero().flatten()[:n]
+            out[(classes == c).nonzero().flatten().to(out.device)] = self.free_slots[idx]
+            keep[idx] = False
+        self.free_slots = self.free_slots[keep]
         return out
 
     def _free(self, slots: torch.Tensor) -> None:

@@ -66,7 +66,8 @@ class Scheduler(SchedulerIOMixin):
             torch.cuda.set_stream(self.stream)
         page_size = self.engine.page_size
         self.table_manager = TableManager(config.max_running_req, self.engine.page_table)
-        self.cache_manager = CacheManager(self.engine.num_pages, page_size, self.engine.page_table, config.cache_type)
+        self.cache_manager = CacheManager(self.engine.num_pages, page_size, self.engine.page_table, config.cache_type,
+                                          page_classes=self.engine.cp_size)
         self.decode_manager = DecodeManager(page_size)
         self.prefill_manager = PrefillManager(self.cache_manager, self.table_manager, self.decode_manager)
         self.finished_reqs: Set[Req] = set()

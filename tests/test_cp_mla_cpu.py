@@ -1,5 +1,6 @@
 """Context parallelism for MLA on CPU ranks (gloo, world size 2): each rank
-keeps the latent rows of the 64-key tiles it owns (tile t on rank t % 2),
+keeps the latent rows of the 64-key tiles it owns (tile t on rank t % 2) in
+a pool of half the pages (the allocator gives tile t a page of id = t mod 2),
 attends over them only, and the partial outputs / log-sum-exps of the ranks
 are gathered and merged; the generated tokens equal the single-rank
 engine's. Prompts are longer than one tile so both ranks hold keys."""
@@ -25,8 +26,10 @@ def _run(rank, world, port, cp, q):
     from minisgl.utils.synthetic import make_model_dir
 
     llm = LLM(make_model_dir("tiny-kimi"), dtype=torch.float32, device="cpu", use_dummy_weight=True,
-              tp_info=DistributedInfo(rank, world), page_size=16, num_page_override=128, max_running_req=4,
+              tp_info=DistributedInfo(rank, world), page_size=64, num_page_override=64, max_running_req=4,
               max_seq_len_override=512, max_extend_tokens=64, distributed_port=port, cp_size=cp)
+    if cp > 1:  # each rank holds one page in cp (plus spares)
+        assert llm.engine.kv_cache.pool.shape[1] == llm.engine.num_pages // cp + 2
     outs = llm.generate(PROMPTS, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
     q.put((rank, [o["token_ids"] for o in outs]))
     llm.shutdown()

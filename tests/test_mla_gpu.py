@@ -147,15 +147,43 @@ def test_small_kimi_engine_matches_oracle(cuda_graph):
     assert firsts >= 3 and same >= 0.6 * 24, (firsts, same)
 
 
+def _cp_case(lens, H, cp, seed):
+    """Pages allocated as under context parallelism: tile t of a sequence
+    gets a page with id = t mod cp; rank r's pool holds pages r, r + cp, ...
+    at local index id // cp (so it is full[r::cp])."""
+    g = torch.Generator().manual_seed(seed)
+    page = 64
+    tiles = [(L + page - 1) // page for L in lens]
+    per_class = max(sum(1 for b in range(len(lens)) for t in range(tiles[b]) if t % cp == c) for c in range(cp))
+    num_pages = per_class * cp
+    free = [list(range(c, num_pages, cp)) for c in range(cp)]
+    for c in range(cp):
+        order = torch.randperm(len(free[c]), generator=g).tolist()
+        free[c] = [free[c][i] for i in order]
+    pt = torch.zeros(len(lens) + 2, max(tiles) * page, dtype=torch.int32)
+    rows = []
+    for b, L in enumerate(lens):
+        rows.append(b + 1)
+        for t in range(tiles[b]):
+            pg = free[t % cp].pop()
+            pt[b + 1, t * page:(t + 1) * page] = pg * page + torch.arange(page, dtype=torch.int32)
+    full = (torch.randn(num_pages, page, 576, generator=g) * 0.5).to(torch.bfloat16)
+    T = len(lens)
+    q_lat = (torch.randn(H, T, 512, generator=g) * 0.5).to(torch.bfloat16)
+    q_pe = (torch.randn(T, H, 64, generator=g) * 0.5).to(torch.bfloat16)
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32)  # noqa: E731
+    return full, pt, i32(rows), i32(lens), i32(list(range(T + 1))), q_lat, q_pe
+
+
 @pytest.mark.parametrize("cp,splits", [(2, 1), (3, 2)])
 def test_mla_context_parallel_partials_merge(cp, splits):
     """Every context-parallel rank's partials (emulated on one GPU: ranks
-    write their slots of one partial buffer, no collective), merged by the
-    combine kernel, equal the single-rank attention; prepare stores only the
-    rows of owned 64-key tiles."""
+    attend over their own local pools and write their slots of one partial
+    buffer, no collective), merged by the combine kernel, equal the
+    single-pool attention."""
     lens = [1, 64, 65, 200, 777]
-    H, page_size = 64, 64
-    latent, pt, rows, sl, cu, q_lat, q_pe = _case(lens, [1] * len(lens), H, page_size, seed=cp)
+    H = 64
+    full, pt, rows, sl, cu, q_lat, q_pe = _cp_case(lens, H, cp, seed=cp)
     scale = 192 ** -0.5
     d = lambda t: t.to(DEV)  # noqa: E731
     T = len(lens)
@@ -163,21 +191,24 @@ def test_mla_context_parallel_partials_merge(cp, splits):
     T_pad = (T + tile - 1) // tile * tile
     ql = torch.zeros(H, T_pad, 512, dtype=torch.bfloat16)
     ql[:, :T] = q_lat
-    args = (d(ql), d(q_pe), d(latent), d(pt), d(rows), d(sl), d(cu), page_size, scale)
-    want = ops.mla_attention(*args, splits=1)
+    common = (d(pt), d(rows), d(sl), d(cu), 64, scale)
+    want = ops.mla_attention(d(ql), d(q_pe), d(full), *common, splits=1)
     part_o, part_lse = ops._mla_partials(cp * splits, T, H, 512, torch.device(DEV))
     out = torch.empty_like(want)
     nat = ops.native()
     err = ops.error_word(torch.device(DEV))
     for r in range(cp):
-        nat.mla_attention(out, *args, splits, part_o, part_lse, err, None, cp, r, False)
-    nat.mla_attention(out, *args, splits, part_o, part_lse, err, None, cp, 0, True)
+        local = d(full[r::cp].contiguous())
+        nat.mla_attention(out, d(ql), d(q_pe), local, *common, splits, part_o, part_lse, err, None, cp, r, False)
+    nat.mla_attention(out, d(ql), d(q_pe), d(full), *common, splits, part_o, part_lse, err, None, cp, 0, True)
     torch.cuda.synchronize()
     ops.check_device_errors(torch.device(DEV))
     _close(out[:, :T].cpu(), want[:, :T].cpu(), 2e-2)
 
 
 def test_mla_prepare_context_parallel_stores_owned_rows():
+    """Rank 1 of 2 stores the rows of tiles 1 and 3 (global pages 1 and 3)
+    at local pages 0 and 1 of its half-size pool, nothing else."""
     g = torch.Generator().manual_seed(9)
     T, H = 200, 16
     bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
@@ -187,13 +218,15 @@ def test_mla_prepare_context_parallel_stores_owned_rows():
     norm_w = bf(torch.ones(512))
     positions = torch.arange(T, dtype=torch.int32)
     cos_sin = torch.randn(4096, 64)
-    out_loc = torch.arange(T, dtype=torch.int32)
+    out_loc = torch.arange(T, dtype=torch.int32)  # position p in global page p // 64
     d = lambda t: t.to(DEV)  # noqa: E731
-    lat = d(torch.zeros(4, 64, 576, dtype=torch.bfloat16))
+    lat = d(torch.zeros(3, 64, 576, dtype=torch.bfloat16))
     ops.mla_prepare(d(q), d(kv_a), d(w_uk_t), d(norm_w), 1e-6, d(positions), d(cos_sin), lat, d(out_loc), 64,
                     cp_size=2, cp_rank=1)
     torch.cuda.synchronize()
     flat = lat.view(-1, 576).cpu()
-    owned = (torch.arange(T) // 64) % 2 == 1
-    assert torch.all(flat[:T][~owned] == 0)
-    assert torch.all(flat[:T][owned].abs().sum(-1) > 0)
+    filled = flat.abs().sum(-1) > 0
+    want = torch.zeros(3 * 64, dtype=torch.bool)
+    want[0:64] = True      # global page 1: positions 64..127
+    want[64:72] = True     # global page 3: positions 192..199
+    assert torch.equal(filled, want)
