@@ -93,18 +93,26 @@ def bench_decode_attention_varlen(B: int, lo: int, hi: int, hq: int, hk: int, pa
 
 
 def bench_prefill_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) -> Dict:
+    """Causal prefill of B requests of L tokens. `ms` is the tcgen05 kernel
+    (q read by TMA); `ms_plain_q` the warp-MMA kernel that the launcher takes
+    when the q row stride is not a multiple of 8 elements (same inputs, q
+    padded by 2 columns)."""
     d = 128
     lens = [L] * B
     pool, pt, rows = _pool(lens, hk, d, page)
     seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
     cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device="cuda")
-    q = torch.randn(B * L, hq * d, device="cuda", dtype=torch.bfloat16)
+    qp = torch.randn(B * L, hq * d + 2, device="cuda", dtype=torch.bfloat16)
+    q = qp[:, : hq * d].contiguous()
     ms = time_kernel(lambda: ops.prefill_attention(q, pool, 0, pt, rows, seq, cu, L, hq, hk, d, page, d ** -0.5),
                      iters=5)
+    ms_old = time_kernel(lambda: ops.prefill_attention(qp, pool, 0, pt, rows, seq, cu, L, hq, hk, d, page,
+                                                       d ** -0.5), iters=5)
     flops = 4 * B * hq * d * L * (L + 1) / 2
     tf = flops / ms / 1e9
     return {"kernel": "prefill_attention", "B": B, "L": L, "hq": hq, "hk": hk, "ms": round(ms, 4),
-            "TFLOP/s": round(tf, 1), "frac_tensor": round(tf / peaks["tflops"], 3)}
+            "TFLOP/s": round(tf, 1), "frac_tensor": round(tf / peaks["tflops"], 3),
+            "ms_plain_q": round(ms_old, 4), "speedup": round(ms_old / ms, 2)}
 
 
 def bench_mla_decode(B: int, L: int, H: int, page: int, peaks) -> Dict:
@@ -334,7 +342,9 @@ def main() -> None:
                       lambda B=B, lo=lo, hi=hi: bench_decode_attention_varlen(B, lo, hi, 16, 8, 64, peaks)))
     cases.append(("decode_attention qwen3-32b", lambda: bench_decode_attention(64, 2000, 64, 8, 64, peaks)))
     cases.append(("decode_attention qwen3-32b tp8", lambda: bench_decode_attention(64, 2000, 8, 1, 64, peaks)))
-    cases.append(("prefill_attention", lambda: bench_prefill_attention(16, 1024, 16, 8, 64, peaks)))
+    for B, L, hq, hk in [(16, 1024, 16, 8), (4, 4096, 16, 8), (1, 16384, 16, 8), (2, 4096, 64, 8)]:
+        cases.append((f"prefill_attention B={B} L={L} hq={hq}",
+                      lambda B=B, L=L, hq=hq, hk=hk: bench_prefill_attention(B, L, hq, hk, 64, peaks)))
     for B, L, Hh in [(256, 1024, 64), (128, 2048, 64), (64, 4096, 64), (8, 4096, 64), (1, 8192, 64), (32, 4096, 16),
                      (64, 2048, 128)]:
         cases.append((f"mla_decode B={B} L={L} H={Hh}",

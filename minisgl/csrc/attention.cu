@@ -516,6 +516,314 @@ __global__ void __launch_bounds__(128, 2)
   }
 }
 
+// ================================================== prefill (tcgen05) ====
+// grid (ceil(max_q / 128), hq, B); 192 threads. One CTA computes 128 query
+// rows of one head (the MMA M) against the 64-key tiles of the same paged
+// ring as above, with the products on the 5th-generation tensor cores:
+//
+//   S = Q . K^T   A = Q (K-major, two 64-dim chunks loaded once by TMA),
+//                 B = K tile (K-major), M = 128, N = 64, K = 128
+//   O += P . V    A = P (K-major, written by the softmax warps into one of
+//                 two buffers), B = the V tile read MN-major, N = 128
+//
+// TMEM (256 columns, lane = query row): O in columns 0-127, the scores of
+// tiles with j % 2 == 0 / 1 in columns 128-191 / 192-255. Warps 0-3 run the
+// softmax (thread = one query row), warp 4 issues TMA, warp 5 issues
+// tcgen05.mma in whichever order their inputs arrive (QK(j) as soon as tile
+// j and a free score buffer are there, PV(i) as soon as P_i is written).
+// Softmax is in the exp2 domain with a lazy rescale: O and l are rescaled
+// only when a row's running max grows by more than 8 (a factor of 256), so
+// P stays below 256 in bf16 and most tiles never touch O.
+constexpr int kTcRows = 128;                        // query rows per CTA
+constexpr int kTcStages = 3;
+constexpr int kTcQChunk = kTcRows * 128;            // one 64-dim chunk of Q (16 KB)
+constexpr int kTcPBytes = kTcRows * 128;            // P: 128 rows x 64 keys (16 KB)
+constexpr int kTcSCol = 128;                        // first TMEM column of the score buffers
+constexpr int kTcThreads = 192;
+constexpr int kTcSmem = 1024 + 2 * kTcQChunk + kTcStages * kStageBytes + 2 * kTcPBytes + 256;
+constexpr float kTcRescaleLog2 = 8.f;
+
+// 2^x on the special-function unit (PTX ex2.approx.ftz: relative error of a
+// few ulp, ex2(-inf) = +0).
+__device__ __forceinline__ float ex2_fast(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+__global__ void __launch_bounds__(kTcThreads, 1)
+    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                           AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = sQ + 2 * kTcQChunk;
+  uint8_t* sP = sKV + kTcStages * kStageBytes;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTcPBytes);
+  uint64_t* q_full = bars;
+  uint64_t* kv_full = bars + 1;               // [kTcStages]
+  uint64_t* kv_empty = kv_full + kTcStages;   // [kTcStages]
+  uint64_t* s_full = kv_empty + kTcStages;    // [2] score buffers
+  uint64_t* s_free = s_full + 2;              // [2]
+  uint64_t* p_full = s_free + 2;              // [2] P buffers
+  uint64_t* o_done = p_full + 2;              // [2] PV of tiles with j % 2 == h complete
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
+  int* s_abort = reinterpret_cast<int*>(o_done + 3);
+  const ErrorSink err{a.err};
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  pdl_launch_dependents();
+  pdl_wait();
+  const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // longest key ranges first
+  const int qh = blockIdx.y, b = blockIdx.z;
+  const int q_begin = a.cu_q[b];
+  const int q_len = a.cu_q[b + 1] - q_begin;
+  const int row0 = qt * kTcRows;
+  if (row0 >= q_len) return;  // uniform over the CTA, before any barrier or TMEM
+  const int L = a.seq_lens[b];
+  const int cached = L - q_len;
+  const int h = qh / (a.hq / a.hk);
+  const int n = (cached + min(q_len, row0 + kTcRows) - 1) / kTile + 1;  // key tiles up to the last row
+  const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+
+  if (threadIdx.x == 0) {
+    mbar_init(q_full, 1);
+    for (int i = 0; i < kTcStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&s_free[i], 4);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    *s_abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tm_kv);
+    prefetch_tmap(&tm_q);
+  }
+  if (warp == 5) {
+    tmem_alloc(tmem_slot, 256);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  int issued = 0;  // key tiles whose copies the producer started
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA ----
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * kTcQChunk);
+      // rows past the last query token read the next request's rows (or the
+      // zero fill past the end); their results are never stored
+      tma_load_2d(sQ, &tm_q, q_full, qh * kD, q_begin + row0);
+      tma_load_2d(sQ + kTcQChunk, &tm_q, q_full, qh * kD + 64, q_begin + row0);
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kTcStages;
+        if (j >= kTcStages && !mbar_wait(&kv_empty[s], ((j / kTcStages) - 1) & 1, err, 231)) {
+          atomicExch(s_abort, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(s_abort)) break;
+        ++issued;
+        issue_kv_tile(sKV + s * kStageBytes, &kv_full[s], &tm_kv, a, pt_row, L, j * kTile, h);
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA ----
+    constexpr uint32_t idesc_qk = make_idesc_bf16(kTcRows, kTile);
+    constexpr uint32_t idesc_pv = make_idesc_bf16(kTcRows, kD, false, true);
+    const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV), p_addr = smem_u32(sP);
+    bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, 232));
+    auto qk = [&](int j) {  // S[j % 2] = Q . K_j^T
+      const uint32_t st = kv_addr + (j % kTcStages) * kStageBytes;
+      const uint32_t d = tmem + kTcSCol + (j % 2) * kTile;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f16(d, make_sdesc_k_sw128(q_addr + c * kTcQChunk + k * 32),
+                     make_sdesc_k_sw128(st + c * kHalfBytes + k * 32), idesc_qk, (c | k) != 0 ? 1u : 0u);
+      tc_commit(&s_full[j % 2]);
+    };
+    auto pv = [&](int i) {  // O += P_i . V_i
+      const uint32_t v = kv_addr + (i % kTcStages) * kStageBytes + kTileBytes;
+      const uint32_t pbuf = p_addr + (i % 2) * kTcPBytes;
+#pragma unroll
+      for (int kk = 0; kk < kTile / 16; ++kk)
+        tc_mma_f16(tmem, make_sdesc_k_sw128(pbuf + kk * 32), make_sdesc_mn_sw128(v + kk * 2048, kHalfBytes),
+                   idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+      tc_commit(&kv_empty[i % kTcStages]);
+      tc_commit(&o_done[i % 2]);
+    };
+    int qn = 0, pn = 0;  // next QK, next PV
+    uint64_t t0 = globaltimer_ns();
+    uint32_t spins = 0;
+    while (ok && pn < n) {
+      // lane 0 polls and decides; the warp follows its choice
+      int choice = 0;
+      if (lane == 0) {
+        if (pn < qn && mbar_try_wait(&p_full[pn % 2], (pn / 2) & 1)) choice = 1;
+        else if (qn < n && qn <= pn + 1 && mbar_try_wait(&kv_full[qn % kTcStages], (qn / kTcStages) & 1) &&
+                 (qn < 2 || mbar_try_wait(&s_free[qn % 2], ((qn / 2) - 1) & 1)))
+          choice = 2;
+        else if (*reinterpret_cast<volatile int*>(s_abort) ||
+                 (((++spins) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs))
+          choice = 3;
+      }
+      choice = __shfl_sync(0xffffffffu, choice, 0);
+      if (choice == 3) {
+        if (lane == 0 && !*reinterpret_cast<volatile int*>(s_abort)) err.report(kErrMbarTimeout, 236);
+        ok = false;
+      } else if (choice != 0) {
+        tc_fence_after();
+        if (lane == 0) {
+          if (choice == 1) pv(pn);
+          else qk(qn);
+        }
+        if (choice == 1) ++pn;
+        else ++qn;
+        __syncwarp();
+        if (lane == 0) {
+          t0 = globaltimer_ns();
+          spins = 0;
+        }
+      }
+    }
+    if (!ok && lane == 0) atomicExch(s_abort, 1);
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------- softmax ----
+    const int r = 32 * warp + lane;  // this thread's query row (TMEM lane)
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    const float sl2 = a.scale * kLog2e;
+    const int pos = cached + row0 + r;  // position of this row's query token
+    float m_run = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      const int bf = i % 2;
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[bf], (i / 2) & 1, err, 233));
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[kTile];
+      tmem_ld_32x32b_x32(lane_base + kTcSCol + bf * kTile, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
+      tmem_ld_32x32b_x32(lane_base + kTcSCol + bf * kTile + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      tc_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&s_free[bf]);
+      // causal and length mask: keys [0, lim) of this tile are visible
+      const int kp0 = i * kTile;
+      const int lim = min(pos + 1, L) - kp0;
+      if (lim < kTile) {
+#pragma unroll
+        for (int j = 0; j < kTile; ++j)
+          if (j >= lim) sv[j] = __float_as_uint(-INFINITY);
+      }
+      float mr = __uint_as_float(sv[0]);
+#pragma unroll
+      for (int j = 1; j < kTile; ++j) mr = fmaxf(mr, __uint_as_float(sv[j]));
+      const float mt = mr * sl2;  // the scale is positive: max commutes with it
+      const bool grow = mt > m_run + kTcRescaleLog2;
+      float alpha = 1.f;
+      if (grow) {
+        alpha = ex2_fast(m_run - mt);  // 0 on the first tile (m_run = -inf)
+        l_sum *= alpha;
+        m_run = mt;
+      }
+      const bool any_grow = __any_sync(0xffffffffu, grow) && i > 0;
+      // P = 2^(s * scale * log2 e - m) as bf16 pairs
+      uint32_t pk[kTile / 2];
+      float ps = 0.f;
+#pragma unroll
+      for (int e = 0; e < kTile / 2; ++e) {
+        const float lo = ex2_fast(fmaf(__uint_as_float(sv[2 * e]), sl2, -m_run));
+        const float hi = ex2_fast(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -m_run));
+        ps += lo + hi;
+        pk[e] = pack_bf16x2(lo, hi);
+      }
+      l_sum += ps;
+      // P buffer i % 2 was last read by PV(i - 2)
+      if (i >= 2) {
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[bf], ((i - 2) / 2) & 1, err, 234));
+        if (!ok) break;
+      }
+      if (any_grow) {  // rescale O once PV(i - 1) is complete
+        ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(i - 1) % 2], ((i - 1) / 2) & 1, err, 235));
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll 1
+        for (int c = 0; c < kD / 32; ++c) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(lane_base + c * 32, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
+          tmem_st_32x32b_x32(lane_base + c * 32, ov);
+        }
+        tc_wait_st();
+      }
+      // row r of P, 128-byte-swizzled K-major layout
+      uint8_t* prow = sP + bf * kTcPBytes + r * 128;
+#pragma unroll
+      for (int c = 0; c < kTile / 8; ++c)
+        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
+            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
+      fence_proxy_async_smem();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[bf]);
+    }
+    // ------------------------------------------------------- epilogue ----
+    if (!ok && lane == 0) atomicExch(s_abort, 1);
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(n - 1) % 2], ((n - 1) / 2) & 1, err, 237));
+    tc_fence_after();
+    const float inv = ok && l_sum > 0.f ? 1.f / l_sum : 0.f;
+    const bool store = row0 + r < q_len;
+    __nv_bfloat16* dst =
+        reinterpret_cast<__nv_bfloat16*>(a.out) + (static_cast<int64_t>(q_begin + row0 + r) * a.hq + qh) * kD;
+#pragma unroll 1
+    for (int c = 0; c < kD / 32; ++c) {
+      uint32_t ov[32];
+      if (ok) {
+        tmem_ld_32x32b_x32(lane_base + c * 32, ov);
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ov[j] = 0u;
+      }
+      if (!store) continue;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 v;
+        v.x = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 0]) * inv, __uint_as_float(ov[q4 * 8 + 1]) * inv);
+        v.y = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 2]) * inv, __uint_as_float(ov[q4 * 8 + 3]) * inv);
+        v.z = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 4]) * inv, __uint_as_float(ov[q4 * 8 + 5]) * inv);
+        v.w = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 6]) * inv, __uint_as_float(ov[q4 * 8 + 7]) * inv);
+        *reinterpret_cast<uint4*>(dst + c * 32 + q4 * 8) = v;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4 && lane == 0 && *reinterpret_cast<volatile int*>(s_abort)) {
+    // after an abort, let the copies still in flight land before the CTA
+    // leaves (bounded waits; the normal path never gets here)
+    mbar_wait(q_full, 0, err, 238);
+    for (int j = max(0, issued - kTcStages); j < issued; ++j)
+      mbar_wait(&kv_full[j % kTcStages], (j / kTcStages) & 1, err, 239);
+  }
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 256);
+  }
+}
+
 constexpr int kAttnSmem = kStages * kStageBytes + 1024 + 128;
 static_assert(kConsumers * 16 * kMergeLd * 4 + 2 * kConsumers * 16 * 4 <= kStages * kStageBytes,
               "merge buffer must fit in the ring");
@@ -566,6 +874,20 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.max_q <= 0) return;
   check_args(a);
   CUtensorMap tm = pool_map(a);
+  // the tcgen05 kernel reads Q by TMA: a 16-byte aligned base and row stride
+  if (a.q_rows > 0 && reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && a.ld_q % 8 == 0) {
+    static bool attr_set[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!attr_set[dev & 63]) {
+      cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+      attr_set[dev & 63] = true;
+    }
+    const CUtensorMap tq = make_tmap_bf16_2d_sw128(a.q, a.q_rows, static_cast<uint64_t>(a.hq) * kD, a.ld_q, kTcRows);
+    dim3 grid((a.max_q + kTcRows - 1) / kTcRows, a.hq, a.B);
+    launch_pdl(prefill_attn_tc_kernel, grid, dim3(kTcThreads), kTcSmem, s, tm, tq, a);
+    return;
+  }
   set_smem_once<1>(prefill_attn_kernel);
   dim3 grid((a.max_q + 63) / 64, a.hq, a.B);
   launch_pdl(prefill_attn_kernel, grid, dim3(128), kAttnSmem, s, tm, a);

@@ -941,6 +941,7 @@ void prefill_attention(const at::Tensor& q, at::Tensor out, const at::Tensor& kv
   MSG_CHECK(cu_q.numel() == a.B + 1, "cu_q must have B + 1 entries");
   a.cu_q = cu_q.data_ptr<int32_t>();
   a.max_q = static_cast<int>(max_q);
+  a.q_rows = static_cast<int>(q.size(0));
   a.err = err_ptr(err);
   const c10::cuda::CUDAGuard guard(q.device());
   minisgl::launch_prefill_attention(a, stream_of(q));

@@ -152,6 +152,7 @@ struct AttnArgs {
   float* part_lse;           // [B, hq, max_splits]
   int max_splits;
   int* err;
+  int q_rows;                // prefill: rows of q (the TMA map extent); 0 selects the kernel without Q TMA
 };
 void launch_decode_attention(const AttnArgs& a, cudaStream_t s);
 void launch_prefill_attention(const AttnArgs& a, cudaStream_t s);

@@ -58,18 +58,16 @@ def test_decode_attention(hq, hk, page, splits):
     _close(out.view(B, hq, d), expect, atol=2e-2, rtol=2e-2)
 
 
-@pytest.mark.parametrize("hq,hk", [(16, 8), (8, 1)])
-@pytest.mark.parametrize("page", [16, 64])
-def test_prefill_attention(hq, hk, page):
+def _prefill_case(hq, hk, page, lens, qlens, qmul=1.0, pad=0):
+    """Prefill attention against the fp32 reference; `pad` extra columns make
+    the q row stride other than a multiple of 8 elements."""
     d = 128
-    lens = [5, 64, 130, 700, 257]
-    qlens = [5, 64, 30, 700, 100]  # some requests extend a cached prefix
     B = len(lens)
     pool, pt, rows = _make_pool(lens, hk, d, page, seed=1)
     seq = torch.tensor(lens, dtype=torch.int32, device=DEV)
     cu = torch.tensor([0] + torch.tensor(qlens).cumsum(0).tolist(), dtype=torch.int32, device=DEV)
     T = sum(qlens)
-    wide = torch.randn(T, (hq + 2 * hk) * d, device=DEV, dtype=torch.bfloat16)
+    wide = torch.randn(T, (hq + 2 * hk) * d + pad, device=DEV, dtype=torch.bfloat16) * qmul
     scale = d ** -0.5
     out = ops.prefill_attention(wide, pool, 0, pt, rows, seq, cu, max(qlens), hq, hk, d, page, scale)
     torch.cuda.synchronize()
@@ -77,6 +75,21 @@ def test_prefill_attention(hq, hk, page):
     q = wide[:, : hq * d].reshape(T, hq, d).cpu()
     expect = ref.attention(q, pool.cpu(), 0, pt.cpu(), rows.cpu(), seq.cpu(), cu.cpu(), hq, hk, d, page, scale)
     _close(out.view(T, hq, d), expect, atol=2e-2, rtol=2e-2)
+
+
+# 128-row query tiles on the tensor cores: partial tiles, cached prefixes,
+# several tiles per request, and scores large enough (qmul 6) that running
+# maxima grow across tiles and the output rescale runs
+@pytest.mark.parametrize("hq,hk", [(16, 8), (8, 1)])
+@pytest.mark.parametrize("page", [16, 64, 256])
+@pytest.mark.parametrize("qmul", [1.0, 6.0])
+def test_prefill_attention(hq, hk, page, qmul):
+    _prefill_case(hq, hk, page, [5, 64, 130, 700, 257, 1500], [5, 64, 30, 700, 100, 1300], qmul)
+
+
+def test_prefill_attention_unaligned_q_stride():
+    # a q row stride that TMA cannot take selects the kernel that reads q with plain loads
+    _prefill_case(16, 8, 64, [5, 130, 700], [5, 30, 700], pad=2)
 
 
 @pytest.mark.parametrize("B,V", [(1, 1000), (64, 151936), (3, 32000)])
