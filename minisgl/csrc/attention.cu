@@ -523,11 +523,14 @@ __global__ void __launch_bounds__(128, 2)
 //
 //   S = Q . K^T   A = Q (K-major, two 64-dim chunks loaded once by TMA),
 //                 B = K tile (K-major), M = 128, N = 64, K = 128
-//   O += P . V    A = P (K-major, written by the softmax warps into one of
-//                 two buffers), B = the V tile read MN-major, N = 128
+//   O += P . V    A = P in TMEM (bf16 pairs written by the softmax warps
+//                 with tcgen05.st, two buffers), B = the V tile read
+//                 MN-major, N = 128
 //
-// TMEM (256 columns, lane = query row): O in columns 0-127, the scores of
-// tiles with j % 2 == 0 / 1 in columns 128-191 / 192-255. Warps 0-3 run the
+// TMEM (512 columns, lane = query row): O in columns 0-127, the scores of
+// tiles with j % 2 == 0 / 1 in columns 128-191 / 192-255, P of those tiles
+// in columns 256-287 / 288-319. P never touches shared memory, which leaves
+// its bandwidth to the TMA writes and the Q / K / V operand reads. Warps 0-3 run the
 // softmax (thread = one query row), warp 4 issues TMA, warp 5 issues
 // tcgen05.mma in whichever order their inputs arrive (QK(j) as soon as tile
 // j and a free score buffer are there, PV(i) as soon as P_i is written).
@@ -535,12 +538,16 @@ __global__ void __launch_bounds__(128, 2)
 // only when a row's running max grows by more than 8 (a factor of 256), so
 // P stays below 256 in bf16 and most tiles never touch O.
 constexpr int kTcRows = 128;                        // query rows per CTA
-constexpr int kTcStages = 3;
+constexpr int kTcStages = 5;                        // K/V ring depth: copies start 4 tiles ahead
 constexpr int kTcQChunk = kTcRows * 128;            // one 64-dim chunk of Q (16 KB)
-constexpr int kTcPBytes = kTcRows * 128;            // P: 128 rows x 64 keys (16 KB)
 constexpr int kTcSCol = 128;                        // first TMEM column of the score buffers
-constexpr int kTcThreads = 192;
-constexpr int kTcSmem = 1024 + 2 * kTcQChunk + kTcStages * kStageBytes + 2 * kTcPBytes + 256;
+constexpr int kTcPCol = 256;                        // first TMEM column of the P buffers (32 each)
+constexpr int kTcSoftmaxWarps = 8;                 // two per TMEM lane quadrant
+constexpr int kTcProducer = kTcSoftmaxWarps, kTcIssuer = kTcSoftmaxWarps + 1;
+constexpr int kTcThreads = 32 * (kTcSoftmaxWarps + 2);
+constexpr int kTcRedBytes = 2 * 2 * kTcRows * 4;    // row-max exchange: [tile parity][half][row] fp32
+constexpr int kTcSmem = 1024 + 2 * kTcQChunk + kTcStages * kStageBytes + 256 + kTcRedBytes;
+static_assert(kTcSmem <= 227 * 1024, "prefill smem over the per-CTA limit");
 constexpr float kTcRescaleLog2 = 8.f;
 
 // 2^x on the special-function unit (PTX ex2.approx.ftz: relative error of a
@@ -559,17 +566,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = sQ + 2 * kTcQChunk;
-  uint8_t* sP = sKV + kTcStages * kStageBytes;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sP + 2 * kTcPBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kTcStages * kStageBytes);
   uint64_t* q_full = bars;
   uint64_t* kv_full = bars + 1;               // [kTcStages]
   uint64_t* kv_empty = kv_full + kTcStages;   // [kTcStages]
   uint64_t* s_full = kv_empty + kTcStages;    // [2] score buffers
   uint64_t* s_free = s_full + 2;              // [2]
-  uint64_t* p_full = s_free + 2;              // [2] P buffers
-  uint64_t* o_done = p_full + 2;              // [2] PV of tiles with j % 2 == h complete
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(o_done + 2);
-  int* s_abort = reinterpret_cast<int*>(o_done + 3);
+  uint64_t* p_full = s_free + 2;              // [2] P of tiles with j % 2 == h written
+  uint64_t* o_done = p_full + 2;              // [2] PV of tiles with j % 2 == h complete (P_h free)
+  uint64_t* x_full = o_done + 2;              // [4 quadrants][2] partial row maxima written
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(x_full + 8);
+  int* s_abort = reinterpret_cast<int*>(x_full + 9);
+  float* red = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(bars) + 256);
   const ErrorSink err{a.err};
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
@@ -586,6 +594,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int h = qh / (a.hq / a.hk);
   const int n = (cached + min(q_len, row0 + kTcRows) - 1) / kTile + 1;  // key tiles up to the last row
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+  unsigned long long* trace = (a.trace != nullptr && blockIdx.x == 0 && qh == 0 && b == 0) ? a.trace : nullptr;
+  auto stamp = [&](int i, int slot) {
+    if (trace != nullptr && i < 64) trace[i * 8 + slot] = globaltimer_ns();
+  };
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
@@ -595,17 +607,18 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     }
     for (int i = 0; i < 2; ++i) {
       mbar_init(&s_full[i], 1);
-      mbar_init(&s_free[i], 4);
-      mbar_init(&p_full[i], 4);
+      mbar_init(&s_free[i], kTcSoftmaxWarps);
+      mbar_init(&p_full[i], kTcSoftmaxWarps);
       mbar_init(&o_done[i], 1);
     }
+    for (int i = 0; i < 8; ++i) mbar_init(&x_full[i], 2);
     *s_abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tm_kv);
     prefetch_tmap(&tm_q);
   }
-  if (warp == 5) {
-    tmem_alloc(tmem_slot, 256);
+  if (warp == kTcIssuer) {
+    tmem_alloc(tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -614,7 +627,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const uint32_t tmem = *tmem_slot;
   int issued = 0;  // key tiles whose copies the producer started
 
-  if (warp == 4) {
+  if (warp == kTcProducer) {
     // ------------------------------------------------------------ TMA ----
     if (lane == 0) {
       mbar_arrive_expect_tx(q_full, 2 * kTcQChunk);
@@ -622,23 +635,54 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // zero fill past the end); their results are never stored
       tma_load_2d(sQ, &tm_q, q_full, qh * kD, q_begin + row0);
       tma_load_2d(sQ + kTcQChunk, &tm_q, q_full, qh * kD + 64, q_begin + row0);
+      // page ids of tile j + 1 are read while tile j waits for its stage, so
+      // no copy waits on a page-table load
+      const int P = a.page_size;
+      const int seg = P < kTile ? P : kTile;
+      int cur[kTile / 16], nxt[kTile / 16];
+      auto read_pages = [&](int (&pg)[kTile / 16], int j) {
+#pragma unroll
+        for (int q = 0; q < kTile / 16; ++q) {
+          const int pos = j * kTile + q * seg;
+          pg[q] = (q * seg < kTile && pos < L) ? pt_row[pos] / P : 0;  // past the end: page 0, masked later
+        }
+      };
+      read_pages(cur, 0);
       for (int j = 0; j < n; ++j) {
         const int s = j % kTcStages;
+        read_pages(nxt, j + 1);
         if (j >= kTcStages && !mbar_wait(&kv_empty[s], ((j / kTcStages) - 1) & 1, err, 231)) {
           atomicExch(s_abort, 1);
           break;
         }
         if (*reinterpret_cast<volatile int*>(s_abort)) break;
         ++issued;
-        issue_kv_tile(sKV + s * kStageBytes, &kv_full[s], &tm_kv, a, pt_row, L, j * kTile, h);
+        stamp(j, 0);
+        uint8_t* st = sKV + s * kStageBytes;
+        mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
+        const int64_t in_page = P < kTile ? 0 : (j * kTile) % P;
+#pragma unroll
+        for (int q = 0; q < kTile / 16; ++q) {
+          if (q * seg >= kTile) break;
+          const int64_t row = (static_cast<int64_t>(cur[q]) * a.hk + h) * P + in_page;
+          const int32_t rk = static_cast<int32_t>(a.k_row0 + row);
+          const int32_t rv = static_cast<int32_t>(a.v_row0 + row);
+          const int o = q * seg * 128;
+          tma_load_2d(st + o, &tm_kv, &kv_full[s], 0, rk);
+          tma_load_2d(st + kHalfBytes + o, &tm_kv, &kv_full[s], 64, rk);
+          tma_load_2d(st + kTileBytes + o, &tm_kv, &kv_full[s], 0, rv);
+          tma_load_2d(st + kTileBytes + kHalfBytes + o, &tm_kv, &kv_full[s], 64, rv);
+        }
+#pragma unroll
+        for (int q = 0; q < kTile / 16; ++q) cur[q] = nxt[q];
       }
     }
     __syncwarp();
-  } else if (warp == 5) {
+  } else if (warp == kTcIssuer) {
     // ------------------------------------------------------------ MMA ----
     constexpr uint32_t idesc_qk = make_idesc_bf16(kTcRows, kTile);
     constexpr uint32_t idesc_pv = make_idesc_bf16(kTcRows, kD, false, true);
-    const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV), p_addr = smem_u32(sP);
+    const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV);
     bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, 232));
     auto qk = [&](int j) {  // S[j % 2] = Q . K_j^T
       const uint32_t st = kv_addr + (j % kTcStages) * kStageBytes;
@@ -653,11 +697,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     };
     auto pv = [&](int i) {  // O += P_i . V_i
       const uint32_t v = kv_addr + (i % kTcStages) * kStageBytes + kTileBytes;
-      const uint32_t pbuf = p_addr + (i % 2) * kTcPBytes;
 #pragma unroll
-      for (int kk = 0; kk < kTile / 16; ++kk)
-        tc_mma_f16(tmem, make_sdesc_k_sw128(pbuf + kk * 32), make_sdesc_mn_sw128(v + kk * 2048, kHalfBytes),
-                   idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+      for (int kk = 0; kk < kTile / 16; ++kk)  // 16 keys = 8 TMEM columns of P per MMA
+        tc_mma_f16_ta(tmem, tmem + kTcPCol + (i % 2) * (kTile / 2) + kk * 8,
+                      make_sdesc_mn_sw128(v + kk * 2048, kHalfBytes), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
       tc_commit(&kv_empty[i % kTcStages]);
       tc_commit(&o_done[i % 2]);
     };
@@ -666,12 +709,15 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     uint32_t spins = 0;
     while (ok && pn < n) {
       // lane 0 polls and decides; the warp follows its choice
+      // QK first, tested without suspending: a try_wait on P_pn would sleep
+      // until the softmax of tile pn ends, and QK(pn + 1) would then start
+      // only after PV(pn), leaving the softmax of tile pn + 1 without scores
       int choice = 0;
       if (lane == 0) {
-        if (pn < qn && mbar_try_wait(&p_full[pn % 2], (pn / 2) & 1)) choice = 1;
-        else if (qn < n && qn <= pn + 1 && mbar_try_wait(&kv_full[qn % kTcStages], (qn / kTcStages) & 1) &&
-                 (qn < 2 || mbar_try_wait(&s_free[qn % 2], ((qn / 2) - 1) & 1)))
+        if (qn < n && qn <= pn + 1 && mbar_test_wait(&kv_full[qn % kTcStages], (qn / kTcStages) & 1) &&
+            (qn < 2 || mbar_test_wait(&s_free[qn % 2], ((qn / 2) - 1) & 1)))
           choice = 2;
+        else if (pn < qn && mbar_try_wait(&p_full[pn % 2], (pn / 2) & 1)) choice = 1;
         else if (*reinterpret_cast<volatile int*>(s_abort) ||
                  (((++spins) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs))
           choice = 3;
@@ -683,8 +729,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       } else if (choice != 0) {
         tc_fence_after();
         if (lane == 0) {
-          if (choice == 1) pv(pn);
-          else qk(qn);
+          if (choice == 1) {
+            pv(pn);
+            stamp(pn, 6);
+          } else {
+            qk(qn);
+            stamp(qn, 1);
+          }
         }
         if (choice == 1) ++pn;
         else ++qn;
@@ -699,37 +750,58 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     __syncwarp();
   } else {
     // -------------------------------------------------------- softmax ----
-    const int r = 32 * warp + lane;  // this thread's query row (TMEM lane)
-    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * warp) << 16);
+    // warps q and q + 4 share TMEM lane quadrant q: thread (half, r) owns key
+    // columns 32 half.. of row r, and output dims 64 half.. of that row. The
+    // two halves swap partial row maxima through shared memory each tile
+    // (x_full: one arrival per warp, bounded wait), so both apply the same
+    // running max; their partial sums are added once at the end.
+    const int quad = warp & 3, half = warp >> 2;
+    const int r = 32 * quad + lane;  // this thread's query row (TMEM lane)
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * quad) << 16);
     const float sl2 = a.scale * kLog2e;
     const int pos = cached + row0 + r;  // position of this row's query token
+    constexpr int kCols = kTile / 2;    // key columns per thread
     float m_run = -INFINITY, l_sum = 0.f;
     bool ok = true;
+    auto exchange = [&](float v, int i, int where, float& other) {  // swap v with the other half of row r
+      red[((i & 1) * 2 + half) * kTcRows + r] = v;
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&x_full[quad * 2 + (i & 1)]);
+      const bool got = __all_sync(0xffffffffu, mbar_wait(&x_full[quad * 2 + (i & 1)], (i >> 1) & 1, err, where));
+      other = red[((i & 1) * 2 + (half ^ 1)) * kTcRows + r];
+      return got;
+    };
     for (int i = 0; i < n; ++i) {
       const int bf = i % 2;
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[bf], (i / 2) & 1, err, 233));
       if (!ok) break;
+      const bool tr = warp == 0 && lane == 0;
+      if (tr) stamp(i, 2);
       tc_fence_after();
-      uint32_t sv[kTile];
-      tmem_ld_32x32b_x32(lane_base + kTcSCol + bf * kTile, *reinterpret_cast<uint32_t(*)[32]>(&sv[0]));
-      tmem_ld_32x32b_x32(lane_base + kTcSCol + bf * kTile + 32, *reinterpret_cast<uint32_t(*)[32]>(&sv[32]));
+      uint32_t sv[kCols];
+      tmem_ld_32x32b_x32(lane_base + kTcSCol + bf * kTile + half * kCols, sv);
       tc_wait_ld();
+      if (tr) stamp(i, 7);
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&s_free[bf]);
-      // causal and length mask: keys [0, lim) of this tile are visible
-      const int kp0 = i * kTile;
-      const int lim = min(pos + 1, L) - kp0;
-      if (lim < kTile) {
+      // causal and length mask: keys [0, lim) of this thread's columns are visible
+      const int lim = min(pos + 1, L) - i * kTile - half * kCols;
+      if (lim < kCols) {
 #pragma unroll
-        for (int j = 0; j < kTile; ++j)
+        for (int j = 0; j < kCols; ++j)
           if (j >= lim) sv[j] = __float_as_uint(-INFINITY);
       }
-      float mr = __uint_as_float(sv[0]);
+      float m4[4];  // four independent chains
 #pragma unroll
-      for (int j = 1; j < kTile; ++j) mr = fmaxf(mr, __uint_as_float(sv[j]));
-      const float mt = mr * sl2;  // the scale is positive: max commutes with it
-      const bool grow = mt > m_run + kTcRescaleLog2;
+      for (int c = 0; c < 4; ++c) m4[c] = __uint_as_float(sv[c]);
+#pragma unroll
+      for (int j = 4; j < kCols; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(sv[j]));
+      float other;
+      ok = exchange(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])), i, 240, other);
+      if (!ok) break;
+      const float mt = fmaxf(fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])), other) * sl2;
+      const bool grow = mt > m_run + kTcRescaleLog2;  // the same decision in both halves
       float alpha = 1.f;
       if (grow) {
         alpha = ex2_fast(m_run - mt);  // 0 on the first tile (m_run = -inf)
@@ -738,60 +810,62 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       }
       const bool any_grow = __any_sync(0xffffffffu, grow) && i > 0;
       // P = 2^(s * scale * log2 e - m) as bf16 pairs
-      uint32_t pk[kTile / 2];
-      float ps = 0.f;
+      uint32_t pk[kCols / 2];
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-      for (int e = 0; e < kTile / 2; ++e) {
+      for (int e = 0; e < kCols / 2; ++e) {
         const float lo = ex2_fast(fmaf(__uint_as_float(sv[2 * e]), sl2, -m_run));
         const float hi = ex2_fast(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -m_run));
-        ps += lo + hi;
+        ps[e & 3] += lo + hi;
         pk[e] = pack_bf16x2(lo, hi);
       }
-      l_sum += ps;
+      l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      if (tr) stamp(i, 3);
       // P buffer i % 2 was last read by PV(i - 2)
       if (i >= 2) {
         ok = __all_sync(0xffffffffu, mbar_wait(&o_done[bf], ((i - 2) / 2) & 1, err, 234));
         if (!ok) break;
       }
+      if (tr) stamp(i, 4);
       if (any_grow) {  // rescale O once PV(i - 1) is complete
         ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(i - 1) % 2], ((i - 1) / 2) & 1, err, 235));
         if (!ok) break;
         tc_fence_after();
 #pragma unroll 1
-        for (int c = 0; c < kD / 32; ++c) {
+        for (int c = 0; c < 2; ++c) {
           uint32_t ov[32];
-          tmem_ld_32x32b_x32(lane_base + c * 32, ov);
+          const uint32_t col = lane_base + half * 64 + c * 32;
+          tmem_ld_32x32b_x32(col, ov);
           tc_wait_ld();
 #pragma unroll
           for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
-          tmem_st_32x32b_x32(lane_base + c * 32, ov);
+          tmem_st_32x32b_x32(col, ov);
         }
-        tc_wait_st();
       }
-      // row r of P, 128-byte-swizzled K-major layout
-      uint8_t* prow = sP + bf * kTcPBytes + r * 128;
-#pragma unroll
-      for (int c = 0; c < kTile / 8; ++c)
-        *reinterpret_cast<uint4*>(prow + ((c ^ (r & 7)) << 4)) =
-            make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
-      fence_proxy_async_smem();
+      // keys 32 half.. of row r of P: 16 TMEM columns of bf16 pairs
+      tmem_st_32x32b_x16(lane_base + kTcPCol + bf * (kTile / 2) + half * (kCols / 2), pk);
+      tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[bf]);
+      if (tr) stamp(i, 5);
     }
     // ------------------------------------------------------- epilogue ----
     if (!ok && lane == 0) atomicExch(s_abort, 1);
+    float l_other = 0.f;
+    if (ok) ok = exchange(l_sum, n, 241, l_other);
     if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[(n - 1) % 2], ((n - 1) / 2) & 1, err, 237));
     tc_fence_after();
-    const float inv = ok && l_sum > 0.f ? 1.f / l_sum : 0.f;
+    const float l_row = l_sum + l_other;
+    const float inv = ok && l_row > 0.f ? 1.f / l_row : 0.f;
     const bool store = row0 + r < q_len;
-    __nv_bfloat16* dst =
-        reinterpret_cast<__nv_bfloat16*>(a.out) + (static_cast<int64_t>(q_begin + row0 + r) * a.hq + qh) * kD;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) +
+                         (static_cast<int64_t>(q_begin + row0 + r) * a.hq + qh) * kD + half * 64;
 #pragma unroll 1
-    for (int c = 0; c < kD / 32; ++c) {
+    for (int c = 0; c < 2; ++c) {
       uint32_t ov[32];
       if (ok) {
-        tmem_ld_32x32b_x32(lane_base + c * 32, ov);
+        tmem_ld_32x32b_x32(lane_base + half * 64 + c * 32, ov);
         tc_wait_ld();
       } else {
 #pragma unroll
@@ -811,16 +885,16 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4 && lane == 0 && *reinterpret_cast<volatile int*>(s_abort)) {
+  if (warp == kTcProducer && lane == 0 && *reinterpret_cast<volatile int*>(s_abort)) {
     // after an abort, let the copies still in flight land before the CTA
     // leaves (bounded waits; the normal path never gets here)
     mbar_wait(q_full, 0, err, 238);
     for (int j = max(0, issued - kTcStages); j < issued; ++j)
       mbar_wait(&kv_full[j % kTcStages], (j / kTcStages) & 1, err, 239);
   }
-  if (warp == 5) {
+  if (warp == kTcIssuer) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 

@@ -935,8 +935,13 @@ void prefill_attention(const at::Tensor& q, at::Tensor out, const at::Tensor& kv
                        const at::Tensor& page_table, const at::Tensor& req_rows,
                        const at::Tensor& seq_lens, const at::Tensor& cu_q, int64_t max_q,
                        int64_t hq, int64_t hk, int64_t d, int64_t page_size, double scale,
-                       const c10::optional<at::Tensor>& err) {
+                       const c10::optional<at::Tensor>& err, const c10::optional<at::Tensor>& trace) {
   auto a = attn_common(q, out, kv_pool, layer, page_table, req_rows, seq_lens, hq, hk, d, page_size, scale);
+  if (trace.has_value()) {
+    MSG_CHECK(trace->scalar_type() == at::kLong && trace->is_cuda() && trace->numel() >= 64 * 8,
+              "prefill_attention: trace must be a CUDA int64 tensor of 512 slots");
+    a.trace = reinterpret_cast<unsigned long long*>(trace->data_ptr<int64_t>());
+  }
   check_i32(cu_q, "cu_q");
   MSG_CHECK(cu_q.numel() == a.B + 1, "cu_q must have B + 1 entries");
   a.cu_q = cu_q.data_ptr<int32_t>();

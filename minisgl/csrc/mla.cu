@@ -337,12 +337,14 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
     uint32_t spins = 0;
     while (ok && pn < n) {
       // lane 0 polls and decides; the warp follows its choice
+      // QK first, tested without suspending (a try_wait on P_pn sleeps until
+      // that softmax ends, which would start QK(pn + 1) only after PV(pn))
       int choice = 0;
       if (lane == 0) {
-        if (pn < qn && mbar_try_wait(&p_full[pn % 2], (pn / 2) & 1)) choice = 1;
-        else if (qn < n && qn <= pn + 1 && mbar_try_wait(&kv_full[qn % kStages], (qn / kStages) & 1) &&
-                 (qn < 2 || mbar_try_wait(&s_free[qn % 2], ((qn / 2) - 1) & 1)))
+        if (qn < n && qn <= pn + 1 && mbar_test_wait(&kv_full[qn % kStages], (qn / kStages) & 1) &&
+            (qn < 2 || mbar_test_wait(&s_free[qn % 2], ((qn / 2) - 1) & 1)))
           choice = 2;
+        else if (pn < qn && mbar_try_wait(&p_full[pn % 2], (pn / 2) & 1)) choice = 1;
         else if (((++spins) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs)
           choice = 3;
       }

@@ -153,6 +153,7 @@ struct AttnArgs {
   int max_splits;
   int* err;
   int q_rows;                // prefill: rows of q (the TMA map extent); 0 selects the kernel without Q TMA
+  unsigned long long* trace; // optional [64 tiles x 8] %globaltimer stamps of one prefill CTA (profiling)
 };
 void launch_decode_attention(const AttnArgs& a, cudaStream_t s);
 void launch_prefill_attention(const AttnArgs& a, cudaStream_t s);

@@ -500,7 +500,13 @@ def prefill_attention(
     page_size: int,
     scale: float,
     out: Optional[torch.Tensor] = None,
+    trace: Optional[torch.Tensor] = None,
 ) -> torch.Tensor:
+    """Causal prefill / extend attention over the paged pool. ``trace``:
+    optional int64 [512] device tensor that receives %globaltimer stamps of
+    the first 64 key tiles of one CTA (the one with the longest key range of
+    request 0, head 0) — producer copy, QK issue, scores ready, exps done,
+    previous PV done, P written, PV issue, scores read — for profiling."""
     T = q.shape[0]
     if not q.is_cuda:
         qv = q[:, : hq * d].reshape(T, hq, d)
@@ -515,7 +521,7 @@ def prefill_attention(
     _count()
     native().prefill_attention(
         q, out, kv_pool, layer, page_table, req_rows, seq_lens, cu_q, max_q, hq, hk, d, page_size, scale,
-        error_word(q.device),
+        error_word(q.device), trace,
     )
     return out
 
