@@ -115,6 +115,39 @@ def bench_prefill_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) 
             "ms_plain_q": round(ms_old, 4), "speedup": round(ms_old / ms, 2)}
 
 
+def trace_prefill_attention(B: int = 1, L: int = 16384, hq: int = 16, hk: int = 8, page: int = 64) -> Dict:
+    """Median per-tile phase times (ns) of one prefill CTA from the kernel's
+    %globaltimer trace: the CTA with the longest key range of request 0,
+    head 0; tiles 4-59 of its first 64."""
+    import statistics
+
+    d = 128
+    pool, pt, rows = _pool([L] * B, hk, d, page)
+    seq = torch.tensor([L] * B, dtype=torch.int32, device="cuda")
+    cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device="cuda")
+    q = torch.randn(B * L, hq * d, device="cuda", dtype=torch.bfloat16)
+    tr = torch.zeros(512, dtype=torch.int64, device="cuda")
+    for _ in range(3):
+        ops.prefill_attention(q, pool, 0, pt, rows, seq, cu, L, hq, hk, d, page, d ** -0.5, trace=tr)
+    torch.cuda.synchronize()
+    t = tr.view(64, 8).cpu().tolist()
+    # slots: 0 copy issued, 1 QK issued, 2 scores ready, 7 scores loaded, 3 exps done,
+    # 4 PV(i - 2) done, 5 P written, 6 PV issued
+    phases = {
+        "period": lambda i: t[i][5] - t[i - 1][5],
+        "copy_to_qk_issue": lambda i: t[i][1] - t[i][0],
+        "qk_issue_to_scores": lambda i: t[i][2] - t[i][1],
+        "softmax_idle": lambda i: t[i][2] - t[i - 1][5],
+        "exps": lambda i: t[i][3] - t[i][7],
+        "p_written_to_pv_issue": lambda i: t[i][6] - t[i][5],
+        "qk_issue_to_pv_issue": lambda i: t[i][6] - t[i][1],
+    }
+    out = {"trace": "prefill_attention", "B": B, "L": L, "hq": hq, "hk": hk}
+    for k, f in phases.items():
+        out[k + "_ns"] = statistics.median(f(i) for i in range(4, 60))
+    return out
+
+
 def bench_mla_decode(B: int, L: int, H: int, page: int, peaks) -> Dict:
     """Absorbed MLA decode over a paged latent cache (576 bf16 per token).
     Bytes: every latent row once (head groups of 64 re-read it from L2);
@@ -330,7 +363,11 @@ def main() -> None:
     p.add_argument("--json", default="")
     p.add_argument("--quick", action="store_true")
     p.add_argument("--only", default="", help="run only cases whose label contains this text")
+    p.add_argument("--trace-prefill", action="store_true", help="print the prefill attention phase trace and exit")
     args = p.parse_args()
+    if args.trace_prefill:
+        print(json.dumps(trace_prefill_attention()), flush=True)
+        return
     peaks = _peaks()
     random.seed(0)
     torch.manual_seed(0)

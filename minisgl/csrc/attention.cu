@@ -6,9 +6,12 @@
 //
 // KV tiles of 64 keys x head_dim (128) bf16 are moved by TMA (2-D tensor map
 // over the whole pool, 128-byte swizzle, one box per page segment and
-// 64-column half) into a multi-stage mbarrier ring. Scores and P.V use the
-// warp-level bf16 tensor-core MMA (m16n8k16) with ldmatrix fragments read
-// from the swizzled tiles. Decode attention moves ~2 bytes per multiply-add
+// 64-column half) into a multi-stage mbarrier ring. Prefill runs on tcgen05
+// (prefill_attn_tc_kernel: 128 query rows per CTA, S / O / P in TMEM). Decode
+// and the prefill kernel for q strides TMA cannot take use the warp-level
+// bf16 MMA (m16n8k16) with ldmatrix fragments read from the swizzled tiles:
+// decode has 1-16 query rows per KV head, too few for a 128-row tcgen05
+// tile. Decode attention moves ~2 bytes per multiply-add
 // pair (GQA group <= 16 query rows per key), so it is bound by HBM bandwidth,
 // not by the tensor pipe; the design goal is to keep enough bytes in flight
 // (3 stages x 32 KB per CTA, 2 CTAs per SM) to saturate HBM3e.
