@@ -89,9 +89,16 @@ class Scheduler(SchedulerIOMixin):
 
             self.profiler = StepProfiler()
         super().__init__(config, self.engine.tp_cpu_group)
-        if self.engine.dp and not config.offline_mode:
-            raise NotImplementedError("--enable-dp-attention is available in the offline LLM API; the server "
-                                      "replies through rank 0 only")
+        # DP attention behind the server: rank 0 still pulls every message and
+        # re-publishes it to the other ranks; each rank keeps the requests with
+        # uid % ranks == rank, and the replies of each lockstep step (filler
+        # steps included, so every rank takes part) are gathered to rank 0,
+        # the only rank linked to the detokenizer
+        self.dp_online = self.engine.dp and not config.offline_mode
+        if self.dp_online:
+            self.dp_rank, self.dp_size = config.tp_info.rank, config.tp_info.size
+            self._dp_reply_rank0 = self.send_result
+            self.send_result = self._dp_gather_reply
 
     # --------------------------------------------------------------- loops
     def run_when_idle(self) -> None:
@@ -141,6 +148,14 @@ class Scheduler(SchedulerIOMixin):
             fin = self._prepare_batch(Batch(reqs=[], phase="decode"))
         data = (fin, self._forward(fin)) if fin is not None else None
         self._process_last_data(data)
+
+    def _dp_gather_reply(self, reply: List[DetokenizeMsg]) -> None:
+        import torch.distributed as dist
+
+        parts = [None] * self.dp_size if self.dp_rank == 0 else None
+        dist.gather_object(reply, parts, dst=0, group=self.tp_cpu_group)
+        if self.dp_rank == 0:
+            self._dp_reply_rank0([m for part in parts for m in part])
 
     def dp_has_pending(self) -> bool:
         """Requests this rank has accepted but not scheduled yet (offline mode)."""
@@ -216,6 +231,8 @@ class Scheduler(SchedulerIOMixin):
         elif isinstance(msg, ExitMsg):
             raise KeyboardInterrupt
         elif isinstance(msg, UserMsg):
+            if self.dp_online and msg.uid % self.dp_size != self.dp_rank:
+                return  # another DP rank serves this request
             n, cap = len(msg.input_ids), self.engine.max_seq_len
             room = cap - n
             if room <= 0:
