@@ -235,12 +235,13 @@ class Scheduler(SchedulerIOMixin):
                 return  # another DP rank serves this request
             n, cap = len(msg.input_ids), self.engine.max_seq_len
             room = cap - n
+            warn = logger.warning if self.dp_online else logger.warning_rank0  # under DP the owner reports
             if room <= 0:
-                logger.warning_rank0(f"request {msg.uid} dropped: {n} prompt tokens exceed {cap}")
+                warn(f"request {msg.uid} dropped: {n} prompt tokens exceed {cap}")
                 return
             if msg.sampling_params.max_tokens > room:
                 msg.sampling_params.max_tokens = room
-                logger.warning_rank0(f"request {msg.uid}: max_tokens clamped to {room}")
+                warn(f"request {msg.uid}: max_tokens clamped to {room}")
             self.prefill_manager.add_one_req(msg)
         elif isinstance(msg, AbortBackendMsg):
             req = self.prefill_manager.abort_req(msg.uid) or self.decode_manager.abort_req(msg.uid)
