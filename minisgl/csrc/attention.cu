@@ -520,7 +520,7 @@ __global__ void __launch_bounds__(128, 2)
 }
 
 // ================================================== prefill (tcgen05) ====
-// grid (ceil(max_q / 128), hq, B); 192 threads. One CTA computes 128 query
+// grid (ceil(max_q / 128), hq, B); 320 threads. One CTA computes 128 query
 // rows of one head (the MMA M) against the 64-key tiles of the same paged
 // ring as above, with the products on the 5th-generation tensor cores:
 //
@@ -533,10 +533,12 @@ __global__ void __launch_bounds__(128, 2)
 // TMEM (512 columns, lane = query row): O in columns 0-127, the scores of
 // tiles with j % 2 == 0 / 1 in columns 128-191 / 192-255, P of those tiles
 // in columns 256-287 / 288-319. P never touches shared memory, which leaves
-// its bandwidth to the TMA writes and the Q / K / V operand reads. Warps 0-3 run the
-// softmax (thread = one query row), warp 4 issues TMA, warp 5 issues
-// tcgen05.mma in whichever order their inputs arrive (QK(j) as soon as tile
-// j and a free score buffer are there, PV(i) as soon as P_i is written).
+// its bandwidth to the TMA writes and the Q / K / V operand reads. Warps 0-7
+// run the softmax (warps q and q + 4 share lane quadrant q, one half of each
+// row's 64 keys per thread), warp 8 issues TMA (page ids read one tile
+// ahead), warp 9 issues tcgen05.mma in whichever order their inputs arrive
+// (QK(j) as soon as tile j and a free score buffer are there, PV(i) as soon
+// as P_i is written).
 // Softmax is in the exp2 domain with a lazy rescale: O and l are rescaled
 // only when a row's running max grows by more than 8 (a factor of 256), so
 // P stays below 256 in bf16 and most tiles never touch O.
