@@ -84,6 +84,7 @@ class _Env:
     STATS_INTERVAL = _int(0)            # log a stats line every N steps (0 = off)
     SAMPLING_SEED = _int(0)
     NO_FUSED_SAMPLING = _bool(False)    # sample from materialised logits even when the LM head could
+    CUDA_PROFILER_STEPS = EnvVar("", str)  # "a:b": cudaProfilerStart before step a, Stop before step b
 
     def __init__(self) -> None:
         self.reload()

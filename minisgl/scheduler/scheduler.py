@@ -88,6 +88,13 @@ class Scheduler(SchedulerIOMixin):
             from .profile import StepProfiler
 
             self.profiler = StepProfiler()
+        self.cuda_profiler_window = None
+        if self.is_cuda:
+            from .profile import CudaProfilerWindow, parse_step_window
+
+            window = parse_step_window(ENV.CUDA_PROFILER_STEPS.value)
+            if window is not None:
+                self.cuda_profiler_window = CudaProfilerWindow(window)
         super().__init__(config, self.engine.tp_cpu_group)
         # DP attention behind the server: rank 0 still pulls every message and
         # re-publishes it to the other ranks; each rank keeps the requests with
@@ -293,6 +300,8 @@ class Scheduler(SchedulerIOMixin):
 
     def _forward(self, fin: ForwardInput) -> "ForwardOutput":
         batch = fin.batch
+        if self.cuda_profiler_window is not None:
+            self.cuda_profiler_window.on_step(self.step_count)
         prof = self.profiler.begin() if self.profiler is not None else None
         batch.input_ids = self.token_pool[fin.input_tuple]
         out = self.engine.forward_batch(batch, fin.sample_args)
