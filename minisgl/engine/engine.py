@@ -322,6 +322,10 @@ class Engine:
         if self._faults:
             fault.at_step(self.tp_rank, self._step)
         self._step += 1
+        if ENV.DEBUG_BOUNDS:
+            from .bounds import check_kv_bounds
+
+            check_kv_bounds(self.page_table, batch, self.num_pages * self.page_size, self.page_size)
         # greedy / temperature batches sample inside the LM-head GEMM (no
         # logits in memory); top-k / top-p batches sample from the logits
         fused = self.sampler.fusable(args, batch.size) and getattr(self.model, "samples_in_lm_head", False)
