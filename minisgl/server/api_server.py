@@ -23,6 +23,7 @@ from contextlib import asynccontextmanager
 from dataclasses import dataclass, field
 from typing import AsyncIterator, Callable, Dict, List, Literal, Optional
 
+from fastapi import Request  # module level: the route signatures' string annotations resolve here
 from pydantic import BaseModel, Field
 
 from minisgl.core import SamplingParams
@@ -185,7 +186,7 @@ def get_global_state() -> FrontendManager:
 
 
 def create_app():
-    from fastapi import FastAPI, Request
+    from fastapi import FastAPI
     from fastapi.responses import StreamingResponse
 
     @asynccontextmanager

@@ -1,0 +1,110 @@
+"""The whole server on the CPU, end to end over HTTP.
+
+`python -m minisgl --model synthetic:tiny-qwen3 --device cpu` starts the API
+process, the tokenizer / detokenizer and a scheduler. The test calls:
+
+- /v1/models;
+- /v1/chat/completions, plain and streamed (SSE);
+- /generate (streamed).
+
+It checks the response formats and the token counts. Greedy requests must be
+repeatable. The server's process group is killed at the end (it was started
+in its own session, so only its processes are signalled).
+"""
+
+import json
+import os
+import signal
+import socket
+import subprocess
+import sys
+import time
+import urllib.error
+import urllib.request
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _free_port():
+    while True:
+        with socket.socket() as s:
+            s.bind(("127.0.0.1", 0))
+            port = s.getsockname()[1]
+        with socket.socket() as s2:  # the server also binds port + 1 for its process group
+            try:
+                s2.bind(("127.0.0.1", port + 1))
+                return port
+            except OSError:
+                continue
+
+
+def _post(url, body, timeout=120):
+    req = urllib.request.Request(url, data=json.dumps(body).encode(), headers={"Content-Type": "application/json"})
+    return urllib.request.urlopen(req, timeout=timeout)
+
+
+def _sse_payloads(resp):
+    out = []
+    for raw in resp:
+        line = raw.decode().rstrip("\n")
+        if line.startswith("data: "):
+            out.append(line[len("data: "):])
+    return out
+
+
+def test_http_server_end_to_end(tmp_path):
+    port = _free_port()
+    base = f"http://127.0.0.1:{port}"
+    log_path = tmp_path / "server.log"
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
+    with open(log_path, "w") as log:
+        proc = subprocess.Popen([sys.executable, "-m", "minisgl", "--model", "synthetic:tiny-qwen3", "--device", "cpu",
+                                 "--port", str(port), "--max-running-requests", "4", "--max-seq-len-override", "256",
+                                 "--num-pages", "64", "--page-size", "16"],
+                                cwd=ROOT, env=env, stdout=log, stderr=subprocess.STDOUT, start_new_session=True)
+    try:
+        deadline = time.monotonic() + 300
+        while True:
+            assert proc.poll() is None, "server exited:\n" + log_path.read_text()[-3000:]
+            assert time.monotonic() < deadline, "server not ready:\n" + log_path.read_text()[-3000:]
+            try:
+                with urllib.request.urlopen(base + "/v1/models", timeout=5) as r:
+                    models = json.load(r)
+                break
+            except (urllib.error.URLError, ConnectionError, OSError):
+                time.sleep(1)
+        assert models["data"] and models["data"][0]["id"]
+
+        chat = {"model": "tiny", "messages": [{"role": "user", "content": "hello there"}], "max_tokens": 5,
+                "temperature": 0.0, "ignore_eos": True}
+        with _post(base + "/v1/chat/completions", chat) as r:
+            first = json.load(r)
+        assert first["object"] == "chat.completion"
+        assert first["choices"][0]["message"]["role"] == "assistant"
+        assert first["usage"]["completion_tokens"] == 5
+        with _post(base + "/v1/chat/completions", chat) as r:
+            again = json.load(r)
+        assert again["choices"][0]["message"]["content"] == first["choices"][0]["message"]["content"]
+
+        with _post(base + "/v1/chat/completions", dict(chat, stream=True)) as r:
+            payloads = _sse_payloads(r)
+        assert payloads[-1] == "[DONE]"
+        chunks = [json.loads(p) for p in payloads[:-1]]
+        assert chunks[0]["choices"][0]["delta"].get("role") == "assistant"
+        assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+        streamed = "".join(c["choices"][0]["delta"].get("content", "") for c in chunks)
+        assert streamed == first["choices"][0]["message"]["content"]
+
+        with _post(base + "/generate", {"prompt": "hello there", "max_tokens": 4, "ignore_eos": True}) as r:
+            payloads = _sse_payloads(r)
+        assert payloads[-1] == "[DONE]" and len(payloads) == 4 + 1
+    finally:
+        try:
+            os.killpg(proc.pid, signal.SIGTERM)
+            proc.wait(timeout=30)
+        except (ProcessLookupError, subprocess.TimeoutExpired):
+            try:
+                os.killpg(proc.pid, signal.SIGKILL)
+            except ProcessLookupError:
+                pass
+            proc.wait(timeout=30)
