@@ -108,3 +108,24 @@ def test_http_server_end_to_end(tmp_path):
             except ProcessLookupError:
                 pass
             proc.wait(timeout=30)
+
+
+def test_shell_mode_answers_and_exits(tmp_path):
+    """`--shell` reads lines from standard input, prints each answer, and
+    leaves on /exit with its worker processes stopped."""
+    env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""),
+               MINISGL_SHELL_MAX_TOKENS="4", MINISGL_SHELL_TEMPERATURE="0")
+    proc = subprocess.Popen([sys.executable, "-m", "minisgl", "--model", "synthetic:tiny-qwen3", "--device", "cpu",
+                             "--port", str(_free_port()), "--max-seq-len-override", "256", "--num-pages", "64",
+                             "--page-size", "16", "--shell"],
+                            cwd=ROOT, env=env, stdin=subprocess.PIPE, stdout=subprocess.PIPE,
+                            stderr=subprocess.STDOUT, start_new_session=True)
+    try:
+        out, _ = proc.communicate(b"hello there\n/reset\n/bogus\n/exit\n", timeout=300)
+    finally:
+        if proc.poll() is None:
+            os.killpg(proc.pid, signal.SIGKILL)
+            proc.wait(timeout=30)
+    text = out.decode(errors="replace")
+    assert "unknown command /bogus" in text, text[-3000:]
+    assert "Exiting shell..." in text, text[-3000:]
