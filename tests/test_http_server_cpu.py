@@ -22,6 +22,8 @@ import time
 import urllib.error
 import urllib.request
 
+import pytest
+
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
@@ -52,7 +54,8 @@ def _sse_payloads(resp):
     return out
 
 
-def test_http_server_end_to_end(tmp_path):
+@pytest.mark.parametrize("num_tokenizer", [0, 1])  # 0: the detokenizer also tokenizes; 1: a separate tokenizer
+def test_http_server_end_to_end(tmp_path, num_tokenizer):
     port = _free_port()
     base = f"http://127.0.0.1:{port}"
     log_path = tmp_path / "server.log"
@@ -60,7 +63,7 @@ def test_http_server_end_to_end(tmp_path):
     with open(log_path, "w") as log:
         proc = subprocess.Popen([sys.executable, "-m", "minisgl", "--model", "synthetic:tiny-qwen3", "--device", "cpu",
                                  "--port", str(port), "--max-running-requests", "4", "--max-seq-len-override", "256",
-                                 "--num-pages", "64", "--page-size", "16"],
+                                 "--num-pages", "64", "--page-size", "16", "--num-tokenizer", str(num_tokenizer)],
                                 cwd=ROOT, env=env, stdout=log, stderr=subprocess.STDOUT, start_new_session=True)
     try:
         deadline = time.monotonic() + 300
