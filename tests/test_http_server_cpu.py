@@ -1,7 +1,7 @@
 """The whole server on the CPU, end to end over HTTP.
 
-`python -m minisgl --model synthetic:tiny-qwen3 --device cpu` starts the API
-process, the tokenizer / detokenizer and a scheduler. The test calls:
+`python -m minisgl --model synthetic:<shape> --device cpu` starts the API
+process, the tokenizer / detokenizer and the scheduler ranks. The test calls:
 
 - /v1/models;
 - /v1/chat/completions, plain and streamed (SSE);
@@ -54,16 +54,21 @@ def _sse_payloads(resp):
     return out
 
 
-@pytest.mark.parametrize("num_tokenizer", [0, 1])  # 0: the detokenizer also tokenizes; 1: a separate tokenizer
-def test_http_server_end_to_end(tmp_path, num_tokenizer):
+# 0 extra tokenizers: the detokenizer also tokenizes; 1: a separate tokenizer process; the MoE case runs two
+# ranks with DP attention (each rank serves its own requests, experts split over the ranks)
+@pytest.mark.parametrize("model,extra", [("tiny-qwen3", ["--num-tokenizer", "0"]),
+                                         ("tiny-qwen3", ["--num-tokenizer", "1"]),
+                                         ("tiny-qwen3-moe", ["--tp", "2", "--enable-dp-attention"])],
+                         ids=["shared-tokenizer", "separate-tokenizer", "tp2-dp-attention"])
+def test_http_server_end_to_end(tmp_path, model, extra):
     port = _free_port()
     base = f"http://127.0.0.1:{port}"
     log_path = tmp_path / "server.log"
     env = dict(os.environ, PYTHONPATH=ROOT + os.pathsep + os.environ.get("PYTHONPATH", ""))
     with open(log_path, "w") as log:
-        proc = subprocess.Popen([sys.executable, "-m", "minisgl", "--model", "synthetic:tiny-qwen3", "--device", "cpu",
+        proc = subprocess.Popen([sys.executable, "-m", "minisgl", "--model", f"synthetic:{model}", "--device", "cpu",
                                  "--port", str(port), "--max-running-requests", "4", "--max-seq-len-override", "256",
-                                 "--num-pages", "64", "--page-size", "16", "--num-tokenizer", str(num_tokenizer)],
+                                 "--num-pages", "64", "--page-size", "16"] + extra,
                                 cwd=ROOT, env=env, stdout=log, stderr=subprocess.STDOUT, start_new_session=True)
     try:
         deadline = time.monotonic() + 300
