@@ -1,0 +1,172 @@
+"""Online serving benchmark: streamed chat completions against a running server.
+
+    python -m minisgl.benchmark.online --url http://127.0.0.1:1919 \\
+        --num-requests 64 --concurrency 16 --input-len 256 --output-len 128 [--tokenizer PATH]
+
+Each request streams `/v1/chat/completions` (greedy, `ignore_eos`) and records:
+
+- TTFT: request sent -> first token chunk;
+- TPOT: (last token - first token) / (tokens - 1);
+- end-to-end latency.
+
+At most `--concurrency` requests are in flight; with `--request-rate R` new ones
+also start as a Poisson process of R per second.
+
+One JSON line reports avg / p50 / p90 / p99 / max of each metric, plus output and
+input tokens per second over the whole run. These are the client-side metrics of the
+reference's client (python/minisgl/benchmark/client.py:320-384), measured with
+aiohttp instead of the openai package.
+
+Prompts are random token ids decoded by `--tokenizer` (a model folder), so a prompt
+holds about `--input-len` tokens. Without a tokenizer they are random words.
+"""
+
+from __future__ import annotations
+
+import argparse
+import asyncio
+import json
+import random
+import time
+from dataclasses import dataclass, field
+from typing import Dict, List, Optional
+
+_WORDS = ("the of and to in is was for on as with by at from that this which be are an or it not have "
+          "time year people way day man thing woman life child world school state family student group "
+          "country problem hand part place case week company system program question work government").split()
+
+
+@dataclass
+class RequestResult:
+    ok: bool
+    prompt_chars: int
+    tokens: int = 0
+    ttft: float = 0.0
+    e2e: float = 0.0
+    token_times: List[float] = field(default_factory=list)
+    error: str = ""
+
+    @property
+    def tpot(self) -> Optional[float]:
+        if self.tokens < 2:
+            return None
+        return (self.token_times[-1] - self.token_times[0]) / (self.tokens - 1)
+
+
+def make_prompts(n: int, input_len: int, tokenizer_path: Optional[str], seed: int) -> List[str]:
+    rng = random.Random(seed)
+    if tokenizer_path:
+        from minisgl.utils import load_tokenizer
+
+        tok = load_tokenizer(tokenizer_path)
+        vocab = getattr(tok, "vocab_size", 32000)
+        return [tok.decode([rng.randrange(100, max(101, vocab - 100)) for _ in range(input_len)]) for _ in range(n)]
+    return [" ".join(rng.choice(_WORDS) for _ in range(input_len)) for _ in range(n)]
+
+
+async def _one(session, url: str, model: str, prompt: str, output_len: int, timeout: float) -> RequestResult:
+    import aiohttp
+
+    body = {"model": model, "messages": [{"role": "user", "content": prompt}], "max_tokens": output_len,
+            "temperature": 0.0, "ignore_eos": True, "stream": True}
+    res = RequestResult(ok=False, prompt_chars=len(prompt))
+    t0 = time.perf_counter()
+    try:
+        async with session.post(url + "/v1/chat/completions", json=body,
+                                timeout=aiohttp.ClientTimeout(total=timeout)) as resp:
+            if resp.status != 200:
+                res.error = f"HTTP {resp.status}: {(await resp.text())[:200]}"
+                return res
+            async for raw in resp.content:
+                line = raw.decode().strip()
+                if not line.startswith("data: "):
+                    continue
+                data = line[len("data: "):]
+                if data == "[DONE]":
+                    break
+                choice = json.loads(data)["choices"][0]
+                if choice.get("finish_reason") is not None:
+                    continue  # the closing chunk carries no token
+                now = time.perf_counter() - t0
+                if not res.token_times:
+                    res.ttft = now
+                res.token_times.append(now)
+        res.tokens = len(res.token_times)
+        res.e2e = time.perf_counter() - t0
+        res.ok = res.tokens > 0
+        if not res.ok:
+            res.error = "no tokens"
+    except Exception as e:  # one failed request is reported, not fatal
+        res.error = f"{type(e).__name__}: {e}"
+    return res
+
+
+def _stats(xs: List[float]) -> Dict[str, float]:
+    if not xs:
+        return {}
+    s = sorted(xs)
+
+    def pct(p: float) -> float:
+        return s[min(len(s) - 1, int(round(p / 100.0 * (len(s) - 1))))]
+
+    return {"avg": round(sum(s) / len(s) * 1e3, 3), "p50": round(pct(50) * 1e3, 3), "p90": round(pct(90) * 1e3, 3),
+            "p99": round(pct(99) * 1e3, 3), "max": round(s[-1] * 1e3, 3)}
+
+
+def summarize(results: List[RequestResult], wall: float, input_len: int) -> Dict[str, object]:
+    ok = [r for r in results if r.ok]
+    out_tokens = sum(r.tokens for r in ok)
+    tpots = [t for t in (r.tpot for r in ok) if t is not None]
+    return {"bench": "online", "requests": len(results), "completed": len(ok),
+            "errors": sorted({r.error for r in results if not r.ok})[:5],
+            "wall_s": round(wall, 3), "output_tokens": out_tokens,
+            "output_tok_per_s": round(out_tokens / wall, 1) if wall > 0 else 0.0,
+            "input_tok_per_s": round(len(ok) * input_len / wall, 1) if wall > 0 else 0.0,
+            "ttft_ms": _stats([r.ttft for r in ok]), "tpot_ms": _stats(tpots), "e2e_ms": _stats([r.e2e for r in ok])}
+
+
+async def run(url: str, num_requests: int, concurrency: int, input_len: int, output_len: int,
+              request_rate: float = float("inf"), tokenizer: Optional[str] = None, seed: int = 0,
+              timeout: float = 600.0) -> Dict[str, object]:
+    import aiohttp
+
+    prompts = make_prompts(num_requests, input_len, tokenizer, seed)
+    rng = random.Random(seed + 1)
+    sem = asyncio.Semaphore(max(1, concurrency))
+    async with aiohttp.ClientSession() as session:
+        async with session.get(url + "/v1/models") as resp:
+            model = (await resp.json())["data"][0]["id"]
+
+        async def guarded(p: str) -> RequestResult:
+            async with sem:
+                return await _one(session, url, model, p, output_len, timeout)
+
+        t0 = time.perf_counter()
+        tasks = []
+        for p in prompts:
+            tasks.append(asyncio.create_task(guarded(p)))
+            if request_rate != float("inf"):
+                await asyncio.sleep(rng.expovariate(request_rate))
+        results = await asyncio.gather(*tasks)
+        wall = time.perf_counter() - t0
+    return summarize(list(results), wall, input_len)
+
+
+def main() -> None:
+    p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
+    p.add_argument("--url", default="http://127.0.0.1:1919")
+    p.add_argument("--num-requests", type=int, default=64)
+    p.add_argument("--concurrency", type=int, default=16)
+    p.add_argument("--input-len", type=int, default=256)
+    p.add_argument("--output-len", type=int, default=128)
+    p.add_argument("--request-rate", type=float, default=float("inf"), help="requests per second (Poisson)")
+    p.add_argument("--tokenizer", default=None, help="model folder whose tokenizer builds the prompts")
+    p.add_argument("--seed", type=int, default=0)
+    args = p.parse_args()
+    out = asyncio.run(run(args.url.rstrip("/"), args.num_requests, args.concurrency, args.input_len, args.output_len,
+                          args.request_rate, args.tokenizer, args.seed))
+    print(json.dumps(out), flush=True)
+
+
+if __name__ == "__main__":
+    main()

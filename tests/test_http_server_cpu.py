@@ -5,7 +5,8 @@ process, the tokenizer / detokenizer and the scheduler ranks. The test calls:
 
 - /v1/models;
 - /v1/chat/completions, plain and streamed (SSE);
-- /generate (streamed).
+- /generate (streamed);
+- the online benchmark client (minisgl/benchmark/online.py), a short run.
 
 It checks the response formats and the token counts. Greedy requests must be
 repeatable. The server's process group is killed at the end (it was started
@@ -106,6 +107,18 @@ def test_http_server_end_to_end(tmp_path, model, extra):
         with _post(base + "/generate", {"prompt": "hello there", "max_tokens": 4, "ignore_eos": True}) as r:
             payloads = _sse_payloads(r)
         assert payloads[-1] == "[DONE]" and len(payloads) == 4 + 1
+
+        if extra == ["--num-tokenizer", "0"]:  # the online benchmark client against this server
+            import asyncio
+
+            from minisgl.benchmark import online
+
+            res = asyncio.run(online.run(base, num_requests=6, concurrency=3, input_len=12, output_len=5))
+            assert res["completed"] == 6 and res["output_tokens"] == 30, res
+            for key in ("ttft_ms", "tpot_ms", "e2e_ms"):
+                st = res[key]
+                assert 0 < st["p50"] <= st["max"] and st["avg"] > 0, (key, st)
+            assert res["ttft_ms"]["max"] <= res["e2e_ms"]["max"]
     finally:
         try:
             os.killpg(proc.pid, signal.SIGTERM)
