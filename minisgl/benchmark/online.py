@@ -19,6 +19,13 @@ aiohttp instead of the openai package.
 
 Prompts are random token ids decoded by `--tokenizer` (a model folder), so a prompt
 holds about `--input-len` tokens. Without a tokenizer they are random words.
+
+`--trace FILE --trace-format {qwen,mooncake}` replays a request trace instead. Both
+formats are JSON lines with `timestamp`, `input_length` and `output_length`; other
+fields are ignored. Timestamps are seconds in Qwen traces and milliseconds in Mooncake
+traces, as in the reference's readers (python/minisgl/benchmark/client.py:407-495).
+Each request starts at its offset from the first one, times `--trace-scale`, with no
+concurrency cap.
 """
 
 from __future__ import annotations
@@ -101,6 +108,33 @@ async def _one(session, url: str, model: str, prompt: str, output_len: int, time
     return res
 
 
+@dataclass
+class TraceEntry:
+    start_s: float  # offset from the first request (after scaling)
+    input_len: int
+    output_len: int
+
+
+def read_trace(path: str, fmt: str, n: Optional[int] = None, scale: float = 1.0) -> List[TraceEntry]:
+    """Requests of a Qwen (seconds) or Mooncake (milliseconds) JSON-lines trace, sorted by start."""
+    if fmt not in ("qwen", "mooncake"):
+        raise ValueError(f"unknown trace format {fmt!r} (qwen or mooncake)")
+    unit = 1.0 if fmt == "qwen" else 1e-3
+    rows = []
+    with open(path) as f:
+        for line in f:
+            if not line.strip():
+                continue
+            obj = json.loads(line)
+            rows.append((float(obj["timestamp"]) * unit, int(obj["input_length"]), int(obj["output_length"])))
+            if n is not None and len(rows) >= n:
+                break
+    if not rows:
+        return []
+    t0 = min(r[0] for r in rows)
+    return sorted((TraceEntry((t - t0) * scale, i, o) for t, i, o in rows), key=lambda e: e.start_s)
+
+
 def _stats(xs: List[float]) -> Dict[str, float]:
     if not xs:
         return {}
@@ -113,15 +147,18 @@ def _stats(xs: List[float]) -> Dict[str, float]:
             "p99": round(pct(99) * 1e3, 3), "max": round(s[-1] * 1e3, 3)}
 
 
-def summarize(results: List[RequestResult], wall: float, input_len: int) -> Dict[str, object]:
+def summarize(results: List[RequestResult], wall: float, input_len: int,
+              input_lens: Optional[List[int]] = None) -> Dict[str, object]:
     ok = [r for r in results if r.ok]
+    in_tokens = (sum(n for r, n in zip(results, input_lens) if r.ok) if input_lens is not None
+                 else len(ok) * input_len)
     out_tokens = sum(r.tokens for r in ok)
     tpots = [t for t in (r.tpot for r in ok) if t is not None]
     return {"bench": "online", "requests": len(results), "completed": len(ok),
             "errors": sorted({r.error for r in results if not r.ok})[:5],
             "wall_s": round(wall, 3), "output_tokens": out_tokens,
             "output_tok_per_s": round(out_tokens / wall, 1) if wall > 0 else 0.0,
-            "input_tok_per_s": round(len(ok) * input_len / wall, 1) if wall > 0 else 0.0,
+            "input_tok_per_s": round(in_tokens / wall, 1) if wall > 0 else 0.0,
             "ttft_ms": _stats([r.ttft for r in ok]), "tpot_ms": _stats(tpots), "e2e_ms": _stats([r.e2e for r in ok])}
 
 
@@ -152,6 +189,27 @@ async def run(url: str, num_requests: int, concurrency: int, input_len: int, out
     return summarize(list(results), wall, input_len)
 
 
+async def run_trace(url: str, entries: List[TraceEntry], tokenizer: Optional[str] = None, seed: int = 0,
+                    timeout: float = 600.0) -> Dict[str, object]:
+    import aiohttp
+
+    prompts = [make_prompts(1, e.input_len, tokenizer, seed + i)[0] for i, e in enumerate(entries)]
+    async with aiohttp.ClientSession() as session:
+        async with session.get(url + "/v1/models") as resp:
+            model = (await resp.json())["data"][0]["id"]
+        t0 = time.perf_counter()
+
+        async def timed(e: TraceEntry, prompt: str) -> RequestResult:
+            await asyncio.sleep(max(0.0, t0 + e.start_s - time.perf_counter()))
+            return await _one(session, url, model, prompt, e.output_len, timeout)
+
+        results = await asyncio.gather(*(timed(e, p) for e, p in zip(entries, prompts)))
+        wall = time.perf_counter() - t0
+    out = summarize(list(results), wall, 0, [e.input_len for e in entries])
+    out["bench"] = "online_trace"
+    return out
+
+
 def main() -> None:
     p = argparse.ArgumentParser(description=__doc__.split("\n")[0])
     p.add_argument("--url", default="http://127.0.0.1:1919")
@@ -162,9 +220,17 @@ def main() -> None:
     p.add_argument("--request-rate", type=float, default=float("inf"), help="requests per second (Poisson)")
     p.add_argument("--tokenizer", default=None, help="model folder whose tokenizer builds the prompts")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--trace", default=None, help="JSON-lines request trace to replay")
+    p.add_argument("--trace-format", default="qwen", choices=["qwen", "mooncake"])
+    p.add_argument("--trace-scale", type=float, default=1.0, help="multiplies the trace's time offsets")
     args = p.parse_args()
-    out = asyncio.run(run(args.url.rstrip("/"), args.num_requests, args.concurrency, args.input_len, args.output_len,
-                          args.request_rate, args.tokenizer, args.seed))
+    url = args.url.rstrip("/")
+    if args.trace:
+        entries = read_trace(args.trace, args.trace_format, args.num_requests, args.trace_scale)
+        out = asyncio.run(run_trace(url, entries, args.tokenizer, args.seed))
+    else:
+        out = asyncio.run(run(url, args.num_requests, args.concurrency, args.input_len, args.output_len,
+                              args.request_rate, args.tokenizer, args.seed))
     print(json.dumps(out), flush=True)
 
 

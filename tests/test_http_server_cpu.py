@@ -119,6 +119,11 @@ def test_http_server_end_to_end(tmp_path, model, extra):
                 st = res[key]
                 assert 0 < st["p50"] <= st["max"] and st["avg"] > 0, (key, st)
             assert res["ttft_ms"]["max"] <= res["e2e_ms"]["max"]
+            trace = tmp_path / "trace.jsonl"
+            trace.write_text("".join(json.dumps({"timestamp": t, "input_length": 10, "output_length": 3}) + "\n"
+                                     for t in (0, 200, 400)))  # Mooncake format: milliseconds
+            res = asyncio.run(online.run_trace(base, online.read_trace(str(trace), "mooncake")))
+            assert res["completed"] == 3 and res["output_tokens"] == 9 and res["wall_s"] >= 0.4, res
     finally:
         try:
             os.killpg(proc.pid, signal.SIGTERM)
