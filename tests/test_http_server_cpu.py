@@ -6,7 +6,8 @@ process, the tokenizer / detokenizer and the scheduler ranks. The test calls:
 - /v1/models;
 - /v1/chat/completions, plain and streamed (SSE);
 - /generate (streamed);
-- the online benchmark client (minisgl/benchmark/online.py), a short run.
+- the online benchmark client (minisgl/benchmark/online.py), a short run and a trace replay;
+- a client that disconnects mid-stream (its request is aborted, serving goes on).
 
 It checks the response formats and the token counts. Greedy requests must be
 repeatable. The server's process group is killed at the end (it was started
@@ -124,6 +125,25 @@ def test_http_server_end_to_end(tmp_path, model, extra):
                                      for t in (0, 200, 400)))  # Mooncake format: milliseconds
             res = asyncio.run(online.run_trace(base, online.read_trace(str(trace), "mooncake")))
             assert res["completed"] == 3 and res["output_tokens"] == 9 and res["wall_s"] >= 0.4, res
+
+            # a client that leaves mid-stream: the server aborts its request and keeps serving
+            import http.client
+
+            conn = http.client.HTTPConnection("127.0.0.1", port, timeout=60)
+            conn.request("POST", "/v1/chat/completions", body=json.dumps(dict(chat, max_tokens=240, stream=True)),
+                         headers={"Content-Type": "application/json"})
+            resp = conn.getresponse()
+            got = 0
+            while got < 2:
+                if resp.readline().startswith(b"data: "):
+                    got += 1
+            conn.close()
+            deadline = time.monotonic() + 60
+            while "aborting request" not in log_path.read_text():
+                assert time.monotonic() < deadline, "no abort after the disconnect:\n" + log_path.read_text()[-3000:]
+                time.sleep(0.2)
+            with _post(base + "/v1/chat/completions", chat) as r:
+                assert json.load(r)["usage"]["completion_tokens"] == 5
     finally:
         try:
             os.killpg(proc.pid, signal.SIGTERM)
