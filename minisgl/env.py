@@ -82,6 +82,7 @@ class _Env:
     # B200 engine switches
     DEBUG_CHECK_ERRORS = _bool(False)   # read the kernel error word after every step
     DEBUG_BOUNDS = _bool(False)         # check every KV slot a batch touches against the pool (host, syncs)
+    BROADCAST_TIMEOUT_S = _float(60.0)  # a rank's wait for a request message rank 0 counted for it
     STATS_INTERVAL = _int(0)            # log a stats line every N steps (0 = off)
     SAMPLING_SEED = _int(0)
     NO_FUSED_SAMPLING = _bool(False)    # sample from materialised logits even when the LM head could

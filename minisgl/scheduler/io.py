@@ -16,12 +16,17 @@ from typing import TYPE_CHECKING, List
 import torch
 
 from minisgl.message import BaseBackendMsg, BaseTokenizerMsg, BatchTokenizerMsg, DetokenizeMsg
-from minisgl.utils import ZmqPubQueue, ZmqPullQueue, ZmqPushQueue, ZmqSubQueue, init_logger
+from minisgl.env import ENV
+from minisgl.utils import ZmqPubQueue, ZmqPullQueue, ZmqPushQueue, ZmqSubQueue, fault, init_logger
 
 if TYPE_CHECKING:
     from .config import SchedulerConfig
 
 logger = init_logger(__name__)
+
+
+class MessageLostError(RuntimeError):
+    """A rank did not receive a request message that rank 0 counted for it."""
 
 
 class SchedulerIOMixin:
@@ -39,6 +44,8 @@ class SchedulerIOMixin:
                                                      create=config.backend_create_detokenizer_link,
                                                      encoder=BaseTokenizerMsg.encoder)
         recv, send = self._recv_single, self._reply_rank0
+        self._published = 0  # request messages rank 0 re-published so far
+        self._drop_faults = bool(fault.rules())
         if info.size > 1:
             if info.is_primary():
                 self._send_into_ranks = ZmqPubQueue(config.zmq_scheduler_broadcast_addr, create=True,
@@ -92,7 +99,9 @@ class SchedulerIOMixin:
         count = torch.tensor(len(raws))
         dist.broadcast(count, src=0, group=self.tp_cpu_group)
         for raw in raws:
-            self._send_into_ranks.put_raw(raw)
+            if not (self._drop_faults and fault.drops_broadcast(0, self._published)):
+                self._send_into_ranks.put_raw(raw)
+            self._published += 1
             msgs.append(self._recv_from_tokenizer.decode(raw))
         return msgs
 
@@ -105,7 +114,14 @@ class SchedulerIOMixin:
             msgs.append(self._recv_from_rank0.get())
         count = torch.tensor(-1)
         dist.broadcast(count, src=0, group=self.tp_cpu_group)
-        for _ in range(int(count)):
+        # rank 0 published these before the count: a bounded wait turns a lost
+        # message into an error instead of a rank that waits forever
+        budget_ms = int(ENV.BROADCAST_TIMEOUT_S.value * 1000)
+        for i in range(int(count)):
+            if not self._recv_from_rank0.poll(budget_ms):
+                raise MessageLostError(f"rank {dist.get_rank(self.tp_cpu_group)}: request message {i + 1} of "
+                                       f"{int(count)} from rank 0 did not arrive within "
+                                       f"{ENV.BROADCAST_TIMEOUT_S.value} s")
             msgs.append(self._recv_from_rank0.get())
         return msgs
 

@@ -11,7 +11,12 @@ tensor-parallel rank) at engine step s (default 0):
 * ``skip_collective`` — the NVLink collective kernels of that rank are not
   launched from step s on, so the peers' bounded device waits expire and the
   host reports ``CommTimeoutError`` (no kernel faults or hangs: every device
-  wait in this code base has a time budget).
+  wait in this code base has a time budget);
+* ``drop_broadcast`` — rank 0 of a multi-rank server does not re-publish the
+  s-th message (counting from 0) of those it announces in a count broadcast
+  (messages taken while idle go out before any count and are never dropped):
+  the other ranks' bounded wait for it expires and they raise
+  ``MessageLostError`` instead of hanging.
 
 Nothing here touches a GPU: faults are made on the host, as the failure
 paths must be exercised without faulting shared devices. The reference has
@@ -42,7 +47,7 @@ class FaultRule:
     seconds: float = 30.0
 
 
-_ACTIONS = ("raise", "stall", "exit", "skip_collective")
+_ACTIONS = ("raise", "stall", "exit", "skip_collective", "drop_broadcast")
 
 
 def parse(spec: Optional[str]) -> List[FaultRule]:
@@ -84,3 +89,8 @@ def at_step(rank: int, step: int) -> None:
 def skip_collective(rank: int, step: int) -> bool:
     """True when this rank's NVLink collective launches are to be skipped."""
     return any(r.action == "skip_collective" and r.rank == rank and step >= r.step for r in rules())
+
+
+def drops_broadcast(rank: int, index: int) -> bool:
+    """Whether rank `rank` must not re-publish its `index`-th message."""
+    return any(r.action == "drop_broadcast" and r.rank == rank and r.step == index for r in rules())

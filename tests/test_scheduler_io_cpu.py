@@ -73,6 +73,9 @@ def _scheduler_rank(cfg, rank, world, q):
             sched.run_forever()
         except KeyboardInterrupt:
             sched.shutdown()
+        except Exception as e:  # reported to the test, then the rank dies with it
+            q.put(("error", rank, type(e).__name__, str(e)))
+            raise
     q.put(("done", rank))
 
 
@@ -190,3 +193,26 @@ def test_abort_stops_a_request(checkpoint):
         assert len(client.tokens[1]) == 4
     finally:
         _stop(procs, q, client)
+
+
+def test_lost_broadcast_message_is_detected(checkpoint, monkeypatch):
+    """Rank 0 drops the first message it announces to rank 1 (host fault
+    injection): rank 1's bounded wait runs out and it raises MessageLostError
+    instead of waiting forever."""
+    monkeypatch.setenv("MINISGL_FAULT_INJECT", "drop_broadcast:rank=0:step=0")
+    monkeypatch.setenv("MINISGL_BROADCAST_TIMEOUT_S", "3")
+    procs, q, client = _start(checkpoint, 2)
+    try:
+        client.send(0, PROMPTS[0], 100)  # taken while idle: published before any count, never dropped
+        client.drain(lambda: len(client.tokens[0]) >= 2)  # both ranks are stepping now
+        client.send(1, PROMPTS[1], 4)  # announced in a count broadcast: the dropped one
+        event = q.get(timeout=120)
+        assert event[:3] == ("error", 1, "MessageLostError"), event
+        assert "did not arrive within 3.0 s" in event[3]
+        procs[1].join(timeout=60)
+        assert procs[1].exitcode not in (0, None)
+    finally:
+        for p in procs:  # rank 0 loses its peer; stop it directly
+            if p.is_alive():
+                p.kill()
+            p.join(timeout=60)
