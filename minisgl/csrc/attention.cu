@@ -1095,6 +1095,9 @@ extern "C" __attribute__((visibility("default"))) int minisgl_decode_attention_n
   if (max_splits < 1 || max_splits > kNoAllocMaxSplits)
     return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: max_splits must be in [1, %d] (got %d)", kName,
                         kNoAllocMaxSplits, max_splits);
+  if (ld_pt < 1)
+    return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: ld_pt (page-table row stride) must be >= 1 (got %d)",
+                        kName, ld_pt);
   if (ld_q < hq * d || (ld_q & 7) != 0)
     return noalloc_fail(msg, msg_len, MINISGL_NOALLOC_EINVAL, "%s: ld_q must be >= hq*d and a multiple of 8 (got %d)",
                         kName, ld_q);

@@ -58,7 +58,7 @@ extern "C" {
  *              may sit at the start of a fused qkv row)
  *   kv_pool    bf16 [2, num_layers, num_pages, hk, page_size, d], contiguous
  *   layer      layer index into the pool
- *   page_table int32 [rows, ld_pt]: token slot (page * page_size + offset)
+ *   page_table int32 [rows, ld_pt] (ld_pt >= 1): token slot (page * page_size + offset)
  *              of every position of a request's row
  *   req_rows   int32 [B]: page-table row of each request
  *   seq_lens   int32 [B]: key count of each request (>= 1)

@@ -114,8 +114,9 @@ class SchedulerIOMixin:
             msgs.append(self._recv_from_rank0.get())
         count = torch.tensor(-1)
         dist.broadcast(count, src=0, group=self.tp_cpu_group)
-        # rank 0 published these before the count: a bounded wait turns a lost
-        # message into an error instead of a rank that waits forever
+        # rank 0 publishes these right after the count broadcast; the poll budget
+        # covers that delay, and a bounded wait turns a lost message into an
+        # error instead of a rank that waits forever
         budget_ms = int(ENV.BROADCAST_TIMEOUT_S.value * 1000)
         for i in range(int(count)):
             if not self._recv_from_rank0.poll(budget_ms):

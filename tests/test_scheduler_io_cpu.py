@@ -120,14 +120,14 @@ class _Client:
             self._take()
 
 
-def _start(checkpoint, world):
+def _start(checkpoint, world, **overrides):
     from minisgl.parallel import DistributedInfo
     from minisgl.scheduler import SchedulerConfig
 
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     cfg = SchedulerConfig(model_path=checkpoint, tp_info=DistributedInfo(0, world), offline_mode=False,
-                          distributed_port=_free_port(), **ENGINE)
+                          distributed_port=_free_port(), **dict(ENGINE, **overrides))
     procs = [ctx.Process(target=_scheduler_rank, args=(cfg, r, world, q)) for r in range(world)]
     for p in procs:
         p.start()
@@ -198,21 +198,31 @@ def test_abort_stops_a_request(checkpoint):
 def test_lost_broadcast_message_is_detected(checkpoint, monkeypatch):
     """Rank 0 drops the first message it announces to rank 1 (host fault
     injection): rank 1's bounded wait runs out and it raises MessageLostError
-    instead of waiting forever."""
+    instead of waiting forever. Rank 0 learns of it through the CPU process
+    group: its next count broadcast fails (the peer is gone, or the group's
+    short timeout runs out) and it exits with an error too."""
     monkeypatch.setenv("MINISGL_FAULT_INJECT", "drop_broadcast:rank=0:step=0")
     monkeypatch.setenv("MINISGL_BROADCAST_TIMEOUT_S", "3")
-    procs, q, client = _start(checkpoint, 2)
+    procs, q, client = _start(checkpoint, 2, distributed_timeout=10.0)
     try:
         client.send(0, PROMPTS[0], 100)  # taken while idle: published before any count, never dropped
         client.drain(lambda: len(client.tokens[0]) >= 2)  # both ranks are stepping now
         client.send(1, PROMPTS[1], 4)  # announced in a count broadcast: the dropped one
-        event = q.get(timeout=120)
-        assert event[:3] == ("error", 1, "MessageLostError"), event
-        assert "did not arrive within 3.0 s" in event[3]
-        procs[1].join(timeout=60)
-        assert procs[1].exitcode not in (0, None)
+        t0 = time.monotonic()
+        events = {}
+        while len(events) < 2:
+            event = q.get(timeout=120)
+            assert event[0] == "error", event
+            events[event[1]] = event
+        assert events[1][2] == "MessageLostError", events[1]
+        assert "did not arrive within 3.0 s" in events[1][3]
+        # rank 0 fails in its collective within the group's 10 s timeout (plus slack), not later
+        assert time.monotonic() - t0 < 60.0
+        for p in procs:
+            p.join(timeout=60)
+            assert p.exitcode not in (0, None)
     finally:
-        for p in procs:  # rank 0 loses its peer; stop it directly
+        for p in procs:
             if p.is_alive():
                 p.kill()
             p.join(timeout=60)

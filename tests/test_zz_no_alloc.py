@@ -1,5 +1,7 @@
 """The allocation-free decode attention entry point, called through its
-exported C symbol and checked against minisgl.ops.decode_attention.
+exported C symbol and checked against minisgl.ops.decode_attention and
+against the fp32 PyTorch statement of paged attention
+(minisgl.ops.reference.attention).
 
 Collected last on purpose: it must also pass after every other GPU test has
 run in the same process (with the library's other state already warm).
@@ -11,6 +13,7 @@ import pytest
 import torch
 
 from minisgl import ops
+from minisgl.ops import reference
 
 pytestmark = pytest.mark.gpu
 DEV = "cuda"
@@ -72,6 +75,16 @@ def _expected(c):
                                 c["d"], c["page"], c["scale"], part_o, part_lse, c["splits"])
 
 
+def _oracle(c):
+    """fp32 paged attention over the same pool, page table and queries."""
+    B, hq, d = c["rows"].numel(), c["hq"], c["d"]
+    q = c["q"][:, : hq * d].float().reshape(B, hq, d)
+    cu = torch.arange(B + 1, dtype=torch.int32, device=DEV)
+    out = reference.attention(q, c["pool"].float(), c["layer"], c["pt"], c["rows"], c["seq"], cu, hq, c["hk"], d,
+                              c["page"], c["scale"])
+    return out.reshape(B, hq * d)
+
+
 def _run(fn, c, err):
     out = torch.empty(c["rows"].numel(), c["hq"] * c["d"], device=DEV, dtype=torch.bfloat16)
     rc, msg = _call(fn, out, c["q"], c["pool"], c["layer"], c["pt"], c["rows"], c["seq"], c["hq"], c["hk"],
@@ -101,13 +114,17 @@ def test_noalloc_matches_regular_entry_twice_in_a_row():
     ops.check_device_errors(torch.device(DEV))
     _close(out_a, _expected(a))
     _close(out_b, _expected(b))
+    _close(out_a, _oracle(a))
+    _close(out_b, _oracle(b))
     torch.cuda.synchronize()
 
 
 def test_noalloc_single_split_and_limits():
     fn = _entry()
     c = _case([3, 300, 77], hq=16, hk=8, page=256, splits=1, seed=3)
-    _close(_run(fn, c, None), _expected(c))
+    out1 = _run(fn, c, None)
+    _close(out1, _expected(c))
+    _close(out1, _oracle(c))
     # a request whose scratch would not fit is rejected with a clear error
     B = 64
     big = _case([10] * B, hq=16, hk=8, page=16, splits=16, seed=4)
@@ -120,4 +137,10 @@ def test_noalloc_single_split_and_limits():
     rc, msg = _call(fn, out, big["q"], big["pool"], big["layer"], big["pt"], big["rows"], big["seq"], 16, 8, 64,
                     16, big["scale"], 1, None)
     assert rc == 1 and "head_dim" in msg, (rc, msg)
+    # a page-table row stride below one element (here 0) is rejected before any launch
+    pt0 = big["pt"].as_strided(tuple(big["pt"].shape), (0, 1))
+    assert pt0.stride(0) == 0
+    rc, msg = _call(fn, out, big["q"], big["pool"], big["layer"], pt0, big["rows"], big["seq"], 16, 8, 128, 16,
+                    big["scale"], 1, None)
+    assert rc == 1 and "ld_pt" in msg, (rc, msg)
     torch.cuda.synchronize()
