@@ -1,12 +1,21 @@
 """Run the unmodified reference engine (installed in baseline/_ref) on the
-bench.py workload and print one JSON result line.
+bench.py request pool and print one JSON result line (one process per rank).
 
-Only the reference's public offline API is used (``minisgl.llm.LLM`` and
-``SamplingParams`` of the reference package) with the settings of the
-reference's own offline benchmark (benchmark/offline/bench.py: page 256,
-max_extend_tokens 16384, CUDA graphs up to batch 256, seq len 4096). The one
-setting changed from outside is the TCP port of its single-rank gloo
-rendezvous, so that several replicas can start on one machine.
+Only the reference's own offline code path is used: its ``LLM`` class (the
+offline scheduler loop, its ``generate`` and result hooks), ``SamplingParams``
+and, under it, its engine (pynccl collectives, flashinfer / TRT-LLM attention,
+cuBLAS GEMMs, CUDA-graph decode). Settings are those of the reference's own
+offline benchmark (benchmark/offline/bench.py: max_extend_tokens 16384, CUDA
+graphs up to batch 256, ``--dummy-weight``) with the bench's page size (64,
+the size the reference itself picks on sm100) and sequence-length cap.
+
+Two things are set from outside, because the reference's ``LLM`` is built for
+one rank (python/minisgl/llm/llm.py:28-39 fixes ``DistributedInfo(0, 1)``):
+
+* the TCP port of its gloo rendezvous (a property on its ``EngineConfig``);
+* for tensor parallelism over N ranks, the ``LLM`` subclass below builds the
+  same ``SchedulerConfig`` with ``tp_info = DistributedInfo(rank, N)``; the
+  offline hooks, scheduler and engine are the reference's code unchanged.
 """
 
 import argparse
@@ -14,7 +23,6 @@ import importlib.util
 import json
 import os
 import sys
-import time
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(HERE)
@@ -32,15 +40,14 @@ def _load_bench():
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("--rank", type=int, default=0)
+    p.add_argument("--world", type=int, default=1)
     p.add_argument("--port", type=int, default=29700)
     p.add_argument("--model-dir", required=True)
-    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--steps", type=int, default=8)
     p.add_argument("--warmup", type=int, default=3)
-    p.add_argument("--shape", default="qwen3-0.6b")
-    p.add_argument("--num-reqs", type=int, default=256)
-    p.add_argument("--min-len", type=int, default=100)
-    p.add_argument("--max-input", type=int, default=1024)
-    p.add_argument("--max-output", type=int, default=1024)
+    p.add_argument("--shape", default="qwen3-32b")
+    p.add_argument("--num-reqs", type=int, default=1000)
+    p.add_argument("--step-tokens", type=int, default=8192)
     p.add_argument("--temperature", type=float, default=0.6)
     p.add_argument("--seed", type=int, default=0)
     args = p.parse_args()
@@ -53,33 +60,35 @@ def main() -> None:
     import minisgl.engine.config as ref_cfg
     import torch
     from minisgl.core import SamplingParams
+    from minisgl.distributed import DistributedInfo
     from minisgl.llm import LLM
+    from minisgl.scheduler import Scheduler, SchedulerConfig
 
     ref_cfg.EngineConfig.distributed_addr = property(lambda self: f"tcp://127.0.0.1:{args.port}")
-    llm = LLM(args.model_dir, use_dummy_weight=True, max_seq_len_override=4096, max_extend_tokens=16384,
-              cuda_graph_max_bs=256, page_size=256)
-    llm.generate(["Benchmark: "], SamplingParams(temperature=0.1))
 
-    def step(i):
-        prompts, outs = bench.make_workload(args, i, args.rank)
-        params = [SamplingParams(temperature=args.temperature, ignore_eos=True, max_tokens=o) for o in outs]
-        torch.cuda.synchronize()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        start.record()
-        t0 = time.perf_counter()
-        llm.generate(prompts, params)
-        wall = time.perf_counter() - t0
-        torch.cuda.synchronize()
-        end.record()
-        end.synchronize()
-        return start.elapsed_time(end), wall, sum(outs)
+    class TensorParallelLLM(LLM):
+        """The reference's offline LLM on rank ``rank`` of ``world``."""
 
-    for i in range(args.warmup):
-        step(i)
-    res = [step(args.warmup + k) for k in range(args.steps)]
-    print(json.dumps({"ref_result": True, "dev_ms": sum(r[0] for r in res), "wall_s": sum(r[1] for r in res),
-                      "tokens": sum(r[2] for r in res), "attn": llm.engine.attn_backend.__class__.__name__}),
-          flush=True)
+        def __init__(self, model_path, dtype=torch.bfloat16, *, rank, world, **kwargs):
+            config = SchedulerConfig(model_path=model_path, tp_info=DistributedInfo(rank, world), dtype=dtype,
+                                     offline_mode=True, **kwargs)
+            Scheduler.__init__(self, config)
+            self.pending_requests, self.status_map, self.counter = [], {}, 0
+
+    base = TensorParallelLLM if args.world > 1 else LLM
+    extra = dict(rank=args.rank, world=args.world) if args.world > 1 else {}
+    torch.cuda.set_device(args.rank if args.world > 1 else 0)
+    llm = bench.metered_llm_class(base)(args.model_dir, use_dummy_weight=True, max_seq_len_override=20480,
+                                        max_extend_tokens=16384, cuda_graph_max_bs=256, max_running_req=256,
+                                        page_size=bench.PAGE_SIZE, **extra)
+    llm.generate([[1, 2, 3, 4]], SamplingParams(temperature=0.1, max_tokens=4))
+    prompts, outs = bench.make_pool(args.shape, args.num_reqs, args.seed)
+    res = bench.run_metered(llm, prompts, outs, args.temperature, llm.engine.stream, args, SamplingParams,
+                            counters=lambda: (llm.h2d_counted, llm.d2h_counted))
+    ctx = getattr(llm.engine, "ctx", None)
+    page = getattr(ctx, "page_size", None) or getattr(llm.engine.config, "page_size", None)
+    print(json.dumps(dict(res, ref_result=True, page_size=page,
+                          attn=llm.engine.attn_backend.__class__.__name__)), flush=True)
     os._exit(0)  # the reference's scheduler holds process groups / graphs; skip teardown
 
 

@@ -1,72 +1,213 @@
-"""Offline serving throughput benchmark (the reference's headline workload).
+"""Serving throughput benchmark: output tok/s of the whole box.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl minisgl|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl minisgl|reference] [--shape qwen3-32b]
 
-Workload (the reference's benchmark/offline/bench.py):
-Qwen3-0.6B-shape decoder with random bf16 weights, 256 requests per GPU,
-prompt lengths U[100, 1024] of random token ids, output lengths U[100, 1024],
-temperature 0.6, ignore_eos. One *step* is one ``LLM.generate`` call over a
-fresh set of 256 requests (new prompts every step, so the prefix cache never
-serves a previous step). For N > 1 (launched by torchrun) every GPU runs its
-own engine on its own requests: data-parallel replicas, weak scaling.
+Default workload: the Qwen3-32B-shape dense decoder (64 layers, hidden 5120,
+64 q / 8 kv heads, head_dim 128, SwiGLU 25600, vocabulary 151936), bf16,
+random-init weights, tensor parallel over the N GPUs (TP = N, one rank per
+GPU, launched by torchrun for N > 1). A pool of 1000 synthetic requests is
+served continuously (all submitted at the start: the box runs saturated,
+up to 256 requests at a time): prompt lengths lognormal with median 1024
+(clipped to [32, 16384]), output lengths lognormal with median 256 (clipped
+to [16, 2048]), random token ids, ignore_eos, temperature 0.6; 30% of the
+requests start with one of 50 seeded shared prefixes of 512-2048 tokens
+(the radix prefix cache serves them).
 
-Reported ``value``: output tokens of all ranks / max-over-ranks device time
-(CUDA events around each generate call, synchronised on both sides).
-``e2e``: the same through the public API with host wall-clock time (includes
-tokenised inputs going host->device and every sampled token coming back).
+A *step* is ``--step-tokens`` output tokens (default 8192) of that run: the
+run is cut at the scheduler iterations where the running output count
+crosses each multiple; W untimed warm-up steps (the initial prefill burst
+among them), then K timed steps, after which the run stops. Strong scaling:
+the same request pool at every N.
+
+Reported ``value``: output tokens of the K timed steps / device time between
+the CUDA events recorded on the engine stream at the step boundaries, the
+max over ranks (every rank runs the same schedule). ``e2e``: the same tokens
+over the host wall clock between the boundaries, through the offline ``LLM``
+API (tokenised prompts go host->device from pinned buffers and every sampled
+token comes back each iteration; the byte counts are the engine's). The
+latencies are per request in the timed window, from submission: p50 TTFT is
+queueing + prefill under saturation; p50 TPOT is the inter-token time.
+
+``--impl reference`` runs the unmodified reference (installed under
+baseline/_ref) on the same pool through its own ``LLM`` class; see
+baseline/run_reference.py. ``--shape qwen3-0.6b`` selects the reference's
+offline-benchmark shape (prompts and outputs uniform in [100, 1024]).
 """
 
 from __future__ import annotations
 
 import argparse
 import json
+import math
 import os
 import random
 import statistics
 import subprocess
 import sys
 import time
-from typing import Dict, List, Optional
+from typing import Dict, List, Optional, Tuple
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "output tok/s (whole box, device-timed, max over ranks)"
-MODEL_NAME = "Qwen3-0.6B-shape"
+MODEL_NAMES = {"qwen3-32b": "Qwen3-32B-shape", "qwen3-0.6b": "Qwen3-0.6B-shape", "qwen3-8b": "Qwen3-8B-shape"}
+PAGE_SIZE = 64
 
 
 def parse_args(argv=None):
     p = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     p.add_argument("--gpus", type=int, default=1)
-    p.add_argument("--steps", type=int, default=2)
+    p.add_argument("--steps", type=int, default=8)
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["minisgl", "reference"], default="minisgl")
-    p.add_argument("--shape", default="qwen3-0.6b")
-    p.add_argument("--num-reqs", type=int, default=256)
-    p.add_argument("--min-len", type=int, default=100)
-    p.add_argument("--max-input", type=int, default=1024)
-    p.add_argument("--max-output", type=int, default=1024)
+    p.add_argument("--shape", default="qwen3-32b")
+    p.add_argument("--num-reqs", type=int, default=1000)
+    p.add_argument("--step-tokens", type=int, default=8192)
     p.add_argument("--temperature", type=float, default=0.6)
-    p.add_argument("--page-size", type=int, default=64)
+    p.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--json-out", default="")
     return p.parse_args(argv)
 
 
-def dist_env():
+def dist_env() -> Tuple[int, int, int]:
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     return rank, world, local
 
 
-def make_workload(args, step: int, rank: int, vocab_limit: int = 10000):
-    """Fresh prompts every step (token ids in [0, 10000) like the reference)."""
-    rng = random.Random(args.seed * 1_000_003 + rank * 10_007 + step)
-    prompts = [[rng.randint(0, vocab_limit - 1) for _ in range(rng.randint(args.min_len, args.max_input))]
-               for _ in range(args.num_reqs)]
-    outs = [rng.randint(args.min_len, args.max_output) for _ in range(args.num_reqs)]
+# ------------------------------------------------------------------ workload
+def _lognormal_len(rng: random.Random, median: float, sigma: float, lo: int, hi: int) -> int:
+    return int(min(hi, max(lo, round(median * math.exp(rng.gauss(0.0, sigma))))))
+
+
+def make_pool(shape: str, num_reqs: int, seed: int, vocab_limit: int = 10000) -> Tuple[List[List[int]], List[int]]:
+    """The request pool (same on every rank and in both arms): prompt token
+    ids and output lengths."""
+    rng = random.Random(seed * 1_000_003 + 17)
+    prompts: List[List[int]] = []
+    outs: List[int] = []
+    if shape == "qwen3-0.6b":  # the reference's offline benchmark distributions
+        for _ in range(num_reqs):
+            prompts.append([rng.randrange(vocab_limit) for _ in range(rng.randint(100, 1024))])
+            outs.append(rng.randint(100, 1024))
+        return prompts, outs
+    prefixes = [[rng.randrange(vocab_limit) for _ in range(rng.randint(512, 2048))] for _ in range(50)]
+    for _ in range(num_reqs):
+        n = _lognormal_len(rng, 1024, 0.8, 32, 16384)
+        if rng.random() < 0.3:
+            pre = prefixes[rng.randrange(len(prefixes))]
+            tail = max(16, n - len(pre))
+            prompts.append(pre + [rng.randrange(vocab_limit) for _ in range(tail)])
+        else:
+            prompts.append([rng.randrange(vocab_limit) for _ in range(n)])
+        outs.append(_lognormal_len(rng, 256, 0.8, 16, 2048))
     return prompts, outs
 
 
+class StopRun(Exception):
+    """Raised from the result hook once the last timed step has ended."""
+
+
+class StepMeter:
+    """Cuts a continuous serving run into steps of ``step_tokens`` output
+    tokens. ``on_reply`` is called with each iteration's replies (from the
+    engine's offline result hook); at every boundary it records a CUDA event
+    on the engine stream and the host clock."""
+
+    def __init__(self, stream, step_tokens: int, warmup: int, steps: int, counters=None) -> None:
+        import torch
+
+        self.torch = torch
+        self.stream = stream
+        self.step_tokens = step_tokens
+        self.warmup, self.steps = warmup, steps
+        self.counters = counters  # callable -> (h2d bytes, d2h bytes) so far, or None
+        self.tokens = 0
+        self.marks: List[Tuple[object, int, float, Tuple[int, int]]] = []
+        self.t_submit = time.perf_counter()
+        self.first: Dict[int, float] = {}
+        self.last: Dict[int, float] = {}
+        self.count: Dict[int, int] = {}
+        self._mark()
+
+    def _mark(self) -> None:
+        ev = self.torch.cuda.Event(enable_timing=True)
+        ev.record(self.stream)
+        self.marks.append((ev, self.tokens, time.perf_counter(), self.counters() if self.counters else (0, 0)))
+
+    def on_reply(self, replies) -> None:
+        now = time.perf_counter()
+        for m in replies:
+            self.tokens += 1
+            uid = m.uid
+            if uid not in self.first:
+                self.first[uid] = now
+                self.count[uid] = 0
+            self.last[uid] = now
+            self.count[uid] += 1
+        while self.tokens >= len(self.marks) * self.step_tokens and len(self.marks) <= self.warmup + self.steps:
+            self._mark()
+        if len(self.marks) > self.warmup + self.steps:
+            raise StopRun()
+
+    def result(self) -> Dict[str, float]:
+        self.torch.cuda.synchronize()
+        a, b = self.marks[self.warmup], self.marks[self.warmup + self.steps]
+        t0, t1 = a[2], b[2]
+        ttft = [self.first[u] - self.t_submit for u in self.first if t0 <= self.first[u] <= t1]
+        tpot = [(self.last[u] - self.first[u]) / (self.count[u] - 1) for u in self.first
+                if self.count[u] > 1 and t0 <= self.last[u] <= t1]
+        return {"dev_ms": a[0].elapsed_time(b[0]), "wall_s": t1 - t0, "tokens": b[1] - a[1],
+                "h2d": b[3][0] - a[3][0], "d2h": b[3][1] - a[3][1],
+                "ttft_p50_ms": 1000 * statistics.median(ttft) if ttft else None,
+                "tpot_p50_ms": 1000 * statistics.median(tpot) if tpot else None}
+
+
+def metered_llm_class(base):
+    """A subclass of an offline ``LLM`` class (ours or the reference's) whose
+    per-iteration result hook feeds a StepMeter; everything else is the
+    class's own code path."""
+
+    class Metered(base):
+        meter: Optional[StepMeter] = None
+        h2d_counted = 0  # int32 prompt ids handed to the engine
+        d2h_counted = 0  # int32 sampled tokens handed back
+
+        def offline_receive_msg(self, blocking: bool = False):
+            msgs = super().offline_receive_msg(blocking)
+            for m in msgs:
+                ids = getattr(m, "input_ids", None)
+                if ids is not None:
+                    self.h2d_counted += 4 * len(ids)
+            return msgs
+
+        def offline_send_result(self, reply):
+            super().offline_send_result(reply)
+            self.d2h_counted += 4 * len(reply)
+            if self.meter is not None:
+                self.meter.on_reply(reply)
+
+    return Metered
+
+
+def run_metered(llm, prompts, outs, temperature, stream, args, sampling_params_cls,
+                counters=None) -> Dict[str, float]:
+    """Serve the pool until W + K steps have passed; returns the meter's result."""
+    params = [sampling_params_cls(temperature=temperature, ignore_eos=True, max_tokens=o) for o in outs]
+    llm.meter = StepMeter(stream, args.step_tokens, args.warmup, args.steps, counters)
+    try:
+        llm.generate(prompts, params)
+    except StopRun:
+        pass
+    meter, llm.meter = llm.meter, None
+    if len(meter.marks) <= args.warmup + args.steps:
+        raise RuntimeError(f"request pool exhausted after {len(meter.marks) - 1} steps; "
+                           f"raise --num-reqs or lower --step-tokens")
+    return meter.result()
+
+
+# ------------------------------------------------------------------- clocks
 class ClockSampler:
     """nvidia-smi sampling of SM clocks and throttle reasons while running."""
 
@@ -116,110 +257,103 @@ class ClockSampler:
                 "samples_under_load": len(clocks)}
 
 
-def allreduce(vals: List[float], op: str) -> List[float]:
+def reduce_over_ranks(vals: List[float], op: str) -> List[float]:
     import torch
     import torch.distributed as dist
 
     if not dist.is_initialized():
         return vals
-    t = torch.tensor(vals, dtype=torch.float64)
+    t = torch.tensor([float(v) for v in vals], dtype=torch.float64)
     dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
     return t.tolist()
 
 
+def config_of(args, world: int) -> Dict[str, object]:
+    cfg = {"model": MODEL_NAMES.get(args.shape, args.shape), "global_batch": 256, "parallelism": f"tp{world}",
+           "requests": args.num_reqs, "step_tokens": args.step_tokens, "page_size": PAGE_SIZE,
+           "temperature": args.temperature,
+           "l2": "inputs larger than L2 (tens of GB of weights and KV cache streamed per step)"}
+    if args.shape == "qwen3-0.6b":
+        cfg["seq_len"] = "prompt U[100,1024] + output U[100,1024]"
+    else:
+        cfg["seq_len"] = ("prompt lognormal(median 1024) in [32,16384] + output lognormal(median 256) in [16,2048]; "
+                          "30% share one of 50 prefixes of 512-2048 tokens")
+    return cfg
+
+
+def emit(line: Dict[str, object], args) -> None:
+    print(json.dumps(line), flush=True)
+    if args.json_out:
+        with open(args.json_out, "w") as f:
+            json.dump(line, f)
+
+
+# ------------------------------------------------------------------ our arm
 def run_minisgl(args) -> None:
+    from datetime import timedelta
+
     import torch
     import torch.distributed as dist
 
     rank, world, local = dist_env()
-    if world > 1:
-        dist.init_process_group("gloo", timeout=__import__("datetime").timedelta(seconds=600))
     torch.cuda.set_device(local)
     sys.path.insert(0, ROOT)
     from minisgl import ops
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
+    from minisgl.parallel import DistributedInfo
     from minisgl.utils.synthetic import make_model_dir
 
+    if world > 1:  # the engine joins this group (NCCL for tensors, gloo for the host side)
+        dist.init_process_group("cpu:gloo,cuda:nccl", timeout=timedelta(seconds=300),
+                                device_id=torch.device(f"cuda:{local}"))
     model_dir = make_model_dir(args.shape)
-    llm = LLM(model_dir, dtype=torch.bfloat16, use_dummy_weight=True, device=f"cuda:{local}",
-              max_seq_len_override=4096, max_extend_tokens=16384, cuda_graph_max_bs=256,
-              max_running_req=256, page_size=args.page_size)
-    engine_stream = llm.engine.stream
-
-    def one_step(step: int):
-        prompts, outs = make_workload(args, step, rank)
-        params = [SamplingParams(temperature=args.temperature, ignore_eos=True, max_tokens=o) for o in outs]
-        torch.cuda.synchronize()
-        if world > 1:
-            dist.barrier()
-        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        h2d0, d2h0 = llm.h2d_bytes, llm.d2h_bytes
-        launches0 = ops.LAUNCHES[0]
-        start.record(engine_stream)
-        t0 = time.perf_counter()
-        res = llm.generate(prompts, params)
-        t_api = time.perf_counter() - t0
-        torch.cuda.synchronize()
-        end.record(engine_stream)
-        end.synchronize()
-        dev_ms = start.elapsed_time(end)
-        got = sum(len(r["token_ids"]) for r in res)
-        assert got == sum(outs), f"generated {got} tokens, expected {sum(outs)}"
-        prompt_bytes = 4 * sum(len(p) for p in prompts)
-        return dict(dev_ms=dev_ms, wall_s=t_api, tokens=sum(outs), h2d=llm.h2d_bytes - h2d0 + prompt_bytes,
-                    d2h=llm.d2h_bytes - d2h0, launches=ops.LAUNCHES[0] - launches0)
-
-    for w in range(args.warmup):
-        one_step(w)
-    sampler = ClockSampler([local]) if local == 0 else None
-    gpu_ids = list(range(world))
+    prompts, outs = make_pool(args.shape, args.num_reqs, args.seed)
+    llm = metered_llm_class(LLM)(
+        model_dir, dtype=torch.bfloat16, use_dummy_weight=True, device=f"cuda:{local}",
+        tp_info=DistributedInfo(rank, world), comm=args.comm, max_seq_len_override=20480,
+        max_extend_tokens=16384, cuda_graph_max_bs=256, max_running_req=256, page_size=PAGE_SIZE)
+    launches0 = ops.LAUNCHES[0]
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
     if sampler is not None:
-        sampler.gpus = set(gpu_ids)
         sampler.start()
-    stats = [one_step(args.warmup + k) for k in range(args.steps)]
+    res = run_metered(llm, prompts, outs, args.temperature, llm.engine.stream, args, SamplingParams,
+                      counters=lambda: (llm.h2d_bytes, llm.d2h_bytes))
     clocks = sampler.stop() if sampler is not None else {}
-    dev_ms = sum(s["dev_ms"] for s in stats)
-    wall_s = sum(s["wall_s"] for s in stats)
-    tokens = sum(s["tokens"] for s in stats)
-    h2d = sum(s["h2d"] for s in stats) / args.steps
-    d2h = sum(s["d2h"] for s in stats) / args.steps
-    launches = sum(s["launches"] for s in stats)
-    max_dev_ms, max_wall = allreduce([dev_ms, wall_s], "max")
-    tot_tokens, tot_h2d, tot_d2h, tot_launches = allreduce([tokens, h2d, d2h, launches], "sum")
+    launches = ops.LAUNCHES[0] - launches0
+    max_dev_ms, max_wall = reduce_over_ranks([res["dev_ms"], res["wall_s"]], "max")
+    tot_launches, = reduce_over_ranks([launches], "sum")
     if rank == 0:
-        value = tot_tokens / (max_dev_ms / 1000.0)
-        line = {
+        tokens = res["tokens"]  # every rank serves the same requests (tensor parallel)
+        value = tokens / (max_dev_ms / 1000.0)
+        emit({
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(max_dev_ms / args.steps, 2), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (random token ids, random-init N(0,0.02) weights)",
-            "config": {"model": MODEL_NAME, "global_batch": args.num_reqs * world,
-                       "seq_len": f"prompt U[{args.min_len},{args.max_input}] + output U[{args.min_len},{args.max_output}]",
-                       "parallelism": f"dp{world}" if world > 1 else "tp1", "page_size": args.page_size,
-                       "temperature": args.temperature, "requests_per_gpu": args.num_reqs,
-                       "l2": "inputs larger than L2 (multi-GB KV cache and 1.2 GB of weights per step)"},
+            "config": dict(config_of(args, world), comm=args.comm),
             "clocks": clocks,
-            "e2e": {"value": round(tot_tokens / max_wall, 1), "unit": "tok/s (LLM.generate wall clock)",
-                    "h2d_bytes_per_step": int(tot_h2d), "d2h_bytes_per_step": int(tot_d2h)},
-            "gpu_launches": int(tot_launches),
-            "impl": "minisgl",
-        }
-        print(json.dumps(line), flush=True)
-        if args.json_out:
-            with open(args.json_out, "w") as f:
-                json.dump(line, f)
+            "e2e": {"value": round(tokens / max_wall, 1), "unit": "tok/s (LLM.generate wall clock)",
+                    "h2d_bytes_per_step": int(res["h2d"] / args.steps),
+                    "d2h_bytes_per_step": int(res["d2h"] / args.steps)},
+            "latency": {"ttft_p50_ms": res["ttft_p50_ms"], "tpot_p50_ms": res["tpot_p50_ms"],
+                        "note": "saturated run, all requests submitted at t=0"},
+            "gpu_launches": int(tot_launches), "impl": "minisgl",
+        }, args)
     llm.shutdown()
-    if world > 1:
+    if world > 1 and dist.is_initialized():
         dist.destroy_process_group()
 
 
+# ------------------------------------------------------------ reference arm
 def run_reference(args) -> None:
-    """Run the unmodified reference (baseline/_ref) on the same workload."""
+    """Run the unmodified reference (baseline/_ref) on the same pool: one
+    subprocess per rank whose import path holds only the reference package."""
     rank, world, local = dist_env()
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_dir, "minisgl")):
-        print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "baseline/_ref is not installed"}))
         return
     import torch.distributed as dist
 
@@ -229,41 +363,47 @@ def run_reference(args) -> None:
     from minisgl.utils.synthetic import make_model_dir
 
     model_dir = make_model_dir(args.shape)
-    env = dict(os.environ, CUDA_VISIBLE_DEVICES=str(local) if "CUDA_VISIBLE_DEVICES" not in os.environ
-               else os.environ["CUDA_VISIBLE_DEVICES"].split(",")[local])
+    env = dict(os.environ)
     for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT", "LOCAL_WORLD_SIZE",
               "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID"):
         env.pop(k, None)
+    port = 29700 + (int(os.environ.get("MASTER_PORT", "29500")) % 97) * 3
     cmd = [sys.executable, os.path.join(ROOT, "baseline", "run_reference.py"), "--rank", str(rank),
-           "--port", str(29700 + local), "--model-dir", model_dir] + [f"--{k.replace('_', '-')}={v}" for k, v in vars(args).items()
-                                             if k in ("steps", "warmup", "shape", "num_reqs", "min_len", "max_input",
-                                                      "max_output", "temperature", "seed")]
+           "--world", str(world), "--port", str(port), "--model-dir", model_dir] + \
+          [f"--{k.replace('_', '-')}={v}" for k, v in vars(args).items()
+           if k in ("steps", "warmup", "shape", "num_reqs", "step_tokens", "temperature", "seed")]
     proc = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=3000)
     result = None
     for line in proc.stdout.splitlines():
         if line.startswith("{") and "ref_result" in line:
             result = json.loads(line)
-    ok = 1.0 if result is not None else 0.0
-    (all_ok,) = allreduce([ok], "sum")
+    (all_ok,) = reduce_over_ranks([1.0 if result is not None else 0.0], "sum")
     if all_ok < world:
         if rank == 0:
             tail = (proc.stderr or proc.stdout).strip().splitlines()[-3:]
             print(json.dumps({"impl": "reference", "unavailable": "reference run failed: " + " | ".join(tail)[:400]}))
+        if world > 1:
+            dist.destroy_process_group()
         return
-    max_dev_ms, max_wall = allreduce([result["dev_ms"], result["wall_s"]], "max")
-    (tot_tokens,) = allreduce([result["tokens"]], "sum")
+    max_dev_ms, max_wall = reduce_over_ranks([result["dev_ms"], result["wall_s"]], "max")
     if rank == 0:
-        print(json.dumps({
-            "metric": METRIC, "value": round(tot_tokens / (max_dev_ms / 1000.0), 1), "unit": "tok/s",
+        tokens = result["tokens"]
+        cfg = dict(config_of(args, world), page_size=result.get("page_size"),
+                   attention_backend=result.get("attn"))
+        emit({
+            "metric": METRIC, "value": round(tokens / (max_dev_ms / 1000.0), 1), "unit": "tok/s",
             "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": round(max_dev_ms / args.steps, 2), "higher_is_better": True, "scaling": "weak",
+            "ms_per_step": round(max_dev_ms / args.steps, 2), "higher_is_better": True, "scaling": "strong",
             "vs_baseline": None, "dtype": "bf16", "data": "synthetic (random token ids, reference --dummy-weight)",
-            "config": {"model": MODEL_NAME, "global_batch": args.num_reqs * world,
-                       "parallelism": f"dp{world}" if world > 1 else "tp1", "page_size": 256,
-                       "attention_backend": result.get("attn"), "l2": "inputs larger than L2"},
-            "e2e": {"value": round(tot_tokens / max_wall, 1), "unit": "tok/s (LLM.generate wall clock)"},
+            "config": cfg,
+            "e2e": {"value": round(tokens / max_wall, 1), "unit": "tok/s (LLM.generate wall clock)",
+                    "h2d_bytes_per_step": int(result["h2d"] / args.steps),
+                    "d2h_bytes_per_step": int(result["d2h"] / args.steps),
+                    "bytes": "int32 prompt ids admitted + int32 sampled tokens, counted from the requests"},
+            "latency": {"ttft_p50_ms": result["ttft_p50_ms"], "tpot_p50_ms": result["tpot_p50_ms"],
+                        "note": "saturated run, all requests submitted at t=0"},
             "impl": "reference",
-        }), flush=True)
+        }, args)
     if world > 1:
         dist.destroy_process_group()
 

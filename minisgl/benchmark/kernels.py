@@ -1,6 +1,13 @@
 """Per-kernel timings at serving shapes, with roofline fractions.
 
-    python -m minisgl.benchmark.kernels [--shape qwen3-0.6b] [--json out.json]
+    python -m minisgl.benchmark.kernels [--only <label text>] [--json out.json]
+    python -m minisgl.benchmark.kernels --probe M,N,K,mode,bn,splits[,kps] [--trace]
+
+``--probe`` times one forced GEMM tile plan (mode 1 token-major, 2
+weight-major, 3 persistent; N tile; split-K factor; k-blocks per stage) over
+back-to-back launches cycling 8 weight copies; ``--trace`` adds per-CTA
+%globaltimer phase stamps (entry, set-up done, producer past
+griddepcontrol.wait, first stage consumed, accumulator ready, exit).
 
 Denominators are the measured B200 peaks in MEASURED_PEAKS.json when present
 (STREAM-style copy bandwidth and cuBLAS bf16 GEMM throughput), else the
@@ -245,6 +252,50 @@ def bench_gemm(M: int, N: int, K: int, peaks, label: str) -> Dict:
     return row
 
 
+def _cycle_ms(run, ws: List[torch.Tensor], reps: int = 24) -> float:
+    """Mean ms of ``run(w)`` over back-to-back launches in a CUDA graph that
+    cycles through weight copies larger than L2 in total (weights stream
+    from HBM, as in a decode step); best of three replays."""
+    run(ws[0])
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for i in range(reps):
+            run(ws[i % len(ws)])
+    best = float("inf")
+    for _ in range(3):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        e.synchronize()
+        best = min(best, s.elapsed_time(e) / reps)
+    del g
+    return best
+
+
+def bench_gemm_cold(M: int, N: int, K: int, peaks, label: str) -> Dict:
+    """Our GEMM with its autotuned plan vs cuBLAS, weights cold (copies
+    cycled beyond L2), back to back in a CUDA graph."""
+    from minisgl.ops import gemm_tune
+
+    dev = torch.device("cuda")
+    gemm_tune.tune([(N, K)], [M], dev)
+    w = torch.randn(N, K, device=dev, dtype=torch.bfloat16) * 0.02
+    copies = max(1, min(16, -(-(256 << 20) // w.nbytes)))
+    ws = [w] + [w.clone() for _ in range(copies - 1)]
+    x = torch.randn(M, K, device=dev, dtype=torch.bfloat16)
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    ms = _cycle_ms(lambda w_: ops.gemm(x, w_, out=out), ws)
+    ms_cublas = _cycle_ms(lambda w_: torch.matmul(x, w_.t(), out=out), ws)
+    flops, nbytes = 2 * M * N * K, 2 * (M * K + N * K + M * N)
+    bound = max(flops / (peaks["tflops"] * 1e9), nbytes / (peaks["hbm_gbs"] * 1e6))
+    return {"kernel": f"gemm_cold[{label}]", "M": M, "N": N, "K": K, "plan": gemm_tune.lookup(M, N, K),
+            "ms": round(ms, 4), "cublas_ms": round(ms_cublas, 4), "vs_cublas": round(ms_cublas / ms, 3),
+            "GB/s": round(nbytes / ms / 1e6, 1), "TFLOP/s": round(flops / ms / 1e9, 1),
+            "frac_roofline": round(bound / ms, 3), "cublas_frac_roofline": round(bound / ms_cublas, 3)}
+
+
 def bench_layer_chain(M: int, peaks, layers: int = 28) -> List[Dict]:
     """The non-attention kernels of one Qwen3-0.6B decode layer (tp1) at M
     tokens, per layer, over ``layers`` weight copies (~0.9 GB, so weights
@@ -358,13 +409,62 @@ def bench_elementwise(peaks) -> List[Dict]:
     return out
 
 
+def _quantiles(v: torch.Tensor) -> str:
+    v = v.sort().values
+    return f"min {v[0]:.2f} med {v[len(v) // 2]:.2f} max {v[-1]:.2f}"
+
+
+def probe_plan(M: int, N: int, K: int, mode: int, bn: int, splits: int, kps: int = 0, trace: bool = False,
+               iters: int = 40) -> Dict:
+    """Mean microseconds per launch of one forced tile plan (and, with
+    ``trace``, the phase stamps of one more launch, as quantiles over CTAs)."""
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    ws = [torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02 for _ in range(8)]
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    nat = ops.native()
+
+    def run(w, tr=None):
+        nat.gemm(out, x, w, None, None, splits, mode, None, bn, tr, kps)
+
+    for i in range(8):
+        run(ws[i % 8])
+    torch.cuda.synchronize()
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for i in range(iters):
+        run(ws[i % 8])
+    e.record()
+    torch.cuda.synchronize()
+    row: Dict = {"M": M, "N": N, "K": K, "plan": [mode, bn, splits], "kps": kps,
+                 "us_per_launch": round(s.elapsed_time(e) / iters * 1000, 2)}
+    if trace:
+        tr = torch.zeros(1 << 16, dtype=torch.int64, device="cuda")
+        run(ws[3], tr)
+        torch.cuda.synchronize()
+        t = tr.view(-1, 8).cpu()
+        t = t[t[:, 0] > 0].double()
+        rel = (t - t[:, 0].min()) / 1000.0
+        row.update({"ctas": len(t), "entry": _quantiles(rel[:, 0]), "set-up": _quantiles(rel[:, 1] - rel[:, 0]),
+                    "producer past wait": _quantiles(rel[:, 2]),
+                    "first stage after wait": _quantiles(rel[:, 3] - rel[:, 2]),
+                    "mainloop": _quantiles(rel[:, 4] - rel[:, 3]), "epilogue": _quantiles(rel[:, 5] - rel[:, 4]),
+                    "exit": _quantiles(rel[:, 5])})
+    return row
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
+    p.add_argument("--probe", default="", help="M,N,K,mode,bn,splits[,kps]: time one forced GEMM tile plan")
+    p.add_argument("--trace", action="store_true", help="with --probe: per-CTA phase stamps")
     p.add_argument("--json", default="")
     p.add_argument("--quick", action="store_true")
     p.add_argument("--only", default="", help="run only cases whose label contains this text")
     p.add_argument("--trace-prefill", action="store_true", help="print the prefill attention phase trace and exit")
     args = p.parse_args()
+    if args.probe:
+        vals = [int(v) for v in args.probe.split(",")]
+        print(json.dumps(probe_plan(*vals[:7], trace=args.trace)), flush=True)
+        return
     if args.trace_prefill:
         print(json.dumps(trace_prefill_attention()), flush=True)
         return
@@ -398,6 +498,15 @@ def main() -> None:
         cases.append((f"gemm[{lab} prefill]", lambda N=N, K=K, lab=lab: bench_gemm(16384, N, K, peaks,
                                                                                  f"{lab} prefill")))
     cases.append(("elementwise", lambda: bench_elementwise(peaks)))
+    # Qwen3-32B projections at TP1 and TP8, decode batch sizes and a prefill chunk
+    H32, I32, d = 5120, 25600, 128
+    for tp in (1, 8):
+        for lab, N, K in (("qkv", (64 + 16) * d // tp, H32), ("o", H32, 64 * d // tp),
+                          ("gate_up", 2 * I32 // tp, H32), ("down", H32, I32 // tp)):
+            for M in (1, 32, 128, 256, 8192):
+                name = f"32b tp{tp} {lab} M={M}"
+                cases.append((f"gemm32b[{name}]", lambda M=M, N=N, K=K, name=name: bench_gemm_cold(M, N, K, peaks,
+                                                                                                  name)))
     for T in (16, 256):
         cases.append((f"moe_mxfp4 T={T}", lambda T=T: bench_moe_mxfp4(T, 16, 8, 7168, 2048, peaks)))
     for M in (1, 8, 32, 64, 128, 192, 256):

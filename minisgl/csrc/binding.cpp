@@ -723,6 +723,30 @@ void symm_collective(int64_t kind, at::Tensor out, const c10::optional<at::Tenso
                                   stream_of(out));
 }
 
+// Reduce-scatter + residual + RMSNorm + all-gather over the symmetric heaps
+// (see symm.cu). resid: this rank's residual slice [rows, hidden] bf16.
+void symm_rsn(at::Tensor resid, bool add_resid, const c10::optional<at::Tensor>& norm_w, double eps,
+              const at::Tensor& bases, at::Tensor epoch, int64_t rank, int64_t world, int64_t data_off,
+              int64_t gather_off, const c10::optional<at::Tensor>& err) {
+  check_cuda(resid, "resid");
+  MSG_CHECK(resid.scalar_type() == at::kBFloat16 && resid.is_contiguous() && resid.dim() == 2,
+            "symm_rsn: resid must be a contiguous bf16 [rows, hidden] tensor");
+  MSG_CHECK(bases.is_cuda() && bases.scalar_type() == at::kLong && bases.numel() == world, "symm_rsn: bases");
+  MSG_CHECK(epoch.is_cuda() && epoch.scalar_type() == at::kInt && epoch.numel() == 1, "symm_rsn: epoch");
+  MSG_CHECK(data_off % 16 == 0 && gather_off % 16 == 0, "symm_rsn: heap offsets must be 16-byte aligned");
+  const void* w = nullptr;
+  if (norm_w.has_value()) {
+    MSG_CHECK(norm_w->scalar_type() == at::kBFloat16 && norm_w->is_contiguous() && norm_w->numel() == resid.size(1),
+              "symm_rsn: norm weight must be bf16 [hidden]");
+    w = norm_w->data_ptr();
+  }
+  const c10::cuda::CUDAGuard guard(resid.device());
+  minisgl::launch_symm_rsn(bases.data_ptr<int64_t>(), reinterpret_cast<uint32_t*>(epoch.data_ptr<int32_t>()),
+                           static_cast<int>(rank), static_cast<int>(world), static_cast<int>(resid.size(0)),
+                           static_cast<int>(resid.size(1)), data_off, gather_off, resid.data_ptr(), add_resid, w,
+                           static_cast<float>(eps), err_ptr(err), stream_of(resid));
+}
+
 // residual += all-reduce over ranks of x @ w^T (+ bias on the caller's rank
 // 0): one fused kernel when the grid is resident (see gemm.cu). epoch: int32
 // [2] device counters (fused GEMM, collective kernel).
@@ -1114,6 +1138,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_free", &symm_free);
   m.def("symm_collective", &symm_collective);
+  m.def("symm_rsn", &symm_rsn);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);

@@ -309,6 +309,13 @@ void launch_moe_mxfp4_gemm(const MoeMxfp4GemmArgs& a, cudaStream_t s);
 void launch_symm_collective(int kind, const int64_t* bases, uint32_t* epoch, int rank, int world, int64_t n_elems,
                             void* out, const void* residual, int rows_per_rank, int row_elems, int* err,
                             cudaStream_t s);
+// Reduce-scatter of every rank's partial [rows * world, hidden] (heap data
+// region at data_off) into this rank's residual slice resid [rows, hidden]
+// (+= when add_resid), RMSNorm of the new rows (times norm_w when given) and
+// all-gather of the normalised rows into every heap's region at gather_off.
+void launch_symm_rsn(const int64_t* bases, uint32_t* epoch, int rank, int world, int rows, int hidden,
+                     int64_t data_off, int64_t gather_off, void* resid, bool add_resid, const void* norm_w, float eps,
+                     int* err, cudaStream_t s);
 constexpr int64_t kSymmSignalBytes = 4096;
 // GEMM with the all-reduce fused (kEpiAllReduce) when the grid is resident,
 // otherwise GEMM into the heap data region + launch_symm_collective. Heap

@@ -97,12 +97,15 @@ __device__ uint32_t symm_enter(const SymmArgs& a) {
   return e;
 }
 
-// Exit barrier, run by the last CTA of this rank to finish reading.
-__device__ void symm_exit(const SymmArgs& a, uint32_t e) {
+// Exit barrier, run by the last CTA of this rank to finish reading. Kernels
+// that stored into peer heaps pass sys_fence so those stores are visible to
+// the peers before this rank's exit signal.
+__device__ void symm_exit(const SymmArgs& a, uint32_t e, bool sys_fence = false) {
   __shared__ bool last;
   __syncthreads();
   if (threadIdx.x == 0) {
-    __threadfence();
+    if (sys_fence) __threadfence_system();
+    else __threadfence();
     uint32_t* done = reinterpret_cast<uint32_t*>(a.bases[a.rank]) + kDone;
     last = atomicAdd(done, 1u) == gridDim.x - 1;
     if (last) *done = 0;  // ready for the next call (which starts after this kernel)
@@ -174,6 +177,134 @@ __global__ void symm_all_gather_kernel(SymmArgs a) {
   symm_exit(a, e);
 }
 
+// ------------------------------------------- reduce-scatter + norm + gather
+// The row-parallel projection's collective on a token-sharded residual
+// stream. Each rank's heap data region holds its partial product [T, H]
+// (T = rows * world); rank r owns rows [r * rows, (r + 1) * rows):
+//   1. (entry barrier) sum the owned rows of every rank's partial, in rank
+//      order, in fp32; round the sum to bf16 (what a bf16 all-reduce returns)
+//      and add it to this rank's residual slice (or start the slice with it),
+//      rounding the new residual to bf16 (the residual stream's dtype);
+//   2. RMS-normalise each new residual row (times the norm weight, when one is
+//      given; otherwise the weight is folded into the next GEMM) and store the
+//      bf16 row into the gather region of EVERY rank's heap (peer stores);
+//   3. (exit barrier, system-scope fences) every rank's gather region then
+//      holds all T normalised rows, the input of the next column-parallel
+//      GEMM, read from local memory.
+// NVLink traffic per rank: (world - 1) / world of the partial in and the
+// same of the normalised rows out, the bytes of a two-shot all-reduce,
+// with the add and the norm of the next layer folded in.
+struct RsnArgs {
+  SymmArgs s;                   // bases, epoch, rank, world, err
+  int rows;                     // rows of each rank's slice
+  int vecs;                     // H / 8 (16-byte vectors per row)
+  int64_t data_off;             // byte offset of the partial region in every heap
+  int64_t gather_off;           // byte offset of the gather region in every heap
+  __nv_bfloat16* resid;         // [rows, H] this rank's residual slice (in / out)
+  int add_resid;                // 1: resid += sum, 0: resid = sum
+  const __nv_bfloat16* norm_w;  // [H] or nullptr
+  float eps;
+};
+
+template <int VPT>
+__global__ void __launch_bounds__(1024) symm_rsn_kernel(RsnArgs a) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const uint32_t e = symm_enter(a.s);
+  const int world = a.s.world;
+  __shared__ float red[32];
+  for (int row = blockIdx.x; row < a.rows; row += gridDim.x) {
+    const int64_t grow = static_cast<int64_t>(a.s.rank) * a.rows + row;
+    float v[VPT][8];
+    float ss = 0.f;
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = threadIdx.x + j * blockDim.x;
+      if (c >= a.vecs) continue;
+      const int64_t idx = grow * a.vecs + c;
+      uint4 raw[kMaxRanks];
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r)  // every load in flight before the adds
+        if (r < world)
+          raw[r] = reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(a.s.bases[r]) + a.data_off)[idx];
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r) {
+        if (r >= world) break;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[r]);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          acc[2 * q] += f.x;
+          acc[2 * q + 1] += f.y;
+        }
+      }
+      uint4* rp = reinterpret_cast<uint4*>(a.resid) + static_cast<int64_t>(row) * a.vecs + c;
+      float old[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      if (a.add_resid) {
+        const uint4 rr = *rp;
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&rr);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          old[2 * q] = f.x;
+          old[2 * q + 1] = f.y;
+        }
+      }
+      uint4 pk;
+      uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        pw[q] = pack_bf16x2(__bfloat162float(__float2bfloat16_rn(acc[2 * q])) + old[2 * q],
+                            __bfloat162float(__float2bfloat16_rn(acc[2 * q + 1])) + old[2 * q + 1]);
+      *rp = pk;
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&pk);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const float2 f = __bfloat1622float2(h[q]);
+        v[j][2 * q] = f.x;
+        v[j][2 * q + 1] = f.y;
+        ss += f.x * f.x + f.y * f.y;
+      }
+    }
+    // block-wide sum of squares of the row
+    ss = warp_sum(ss);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+    __syncthreads();
+    float tot = (threadIdx.x & 31) < (blockDim.x >> 5) ? red[threadIdx.x & 31] : 0.f;
+    tot = warp_sum(tot);
+    __syncthreads();
+    const float inv = rsqrtf(tot / static_cast<float>(a.vecs * 8) + a.eps);
+#pragma unroll
+    for (int j = 0; j < VPT; ++j) {
+      const int c = threadIdx.x + j * blockDim.x;
+      if (c >= a.vecs) continue;
+      float wv[8] = {1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f, 1.f};
+      if (a.norm_w != nullptr) {
+        const uint4 ww = reinterpret_cast<const uint4*>(a.norm_w)[c];
+        const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&ww);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h[q]);
+          wv[2 * q] = f.x;
+          wv[2 * q + 1] = f.y;
+        }
+      }
+      uint4 pk;
+      uint32_t* pw = reinterpret_cast<uint32_t*>(&pk);
+#pragma unroll
+      for (int q = 0; q < 4; ++q)
+        pw[q] = pack_bf16x2(v[j][2 * q] * inv * wv[2 * q], v[j][2 * q + 1] * inv * wv[2 * q + 1]);
+      const int64_t idx = grow * a.vecs + c;
+#pragma unroll
+      for (int r = 0; r < kMaxRanks; ++r)
+        if (r < world)
+          reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(a.s.bases[r]) + a.gather_off)[idx] = pk;
+    }
+  }
+  symm_exit(a.s, e, /*sys_fence=*/true);
+}
+
 __global__ void symm_bump_kernel(uint32_t* epoch) {
   pdl_launch_dependents();
   pdl_wait();  // every CTA of the collective has read the old value
@@ -181,6 +312,35 @@ __global__ void symm_bump_kernel(uint32_t* epoch) {
 }
 
 }  // namespace
+
+void launch_symm_rsn(const int64_t* bases, uint32_t* epoch, int rank, int world, int rows, int hidden,
+                     int64_t data_off, int64_t gather_off, void* resid, bool add_resid, const void* norm_w, float eps,
+                     int* err, cudaStream_t s) {
+  if (world < 1 || world > kMaxRanks) throw std::runtime_error("minisgl.symm_rsn: 1..8 ranks");
+  if (hidden % 8 != 0 || hidden > 8 * 1024 * 4) throw std::runtime_error("minisgl.symm_rsn: hidden % 8, <= 32768");
+  if (rows <= 0) return;
+  RsnArgs a{};
+  a.s.bases = bases;
+  a.s.epoch = epoch;
+  a.s.rank = rank;
+  a.s.world = world;
+  a.s.err = ErrorSink{err};
+  a.rows = rows;
+  a.vecs = hidden / 8;
+  a.data_off = data_off;
+  a.gather_off = gather_off;
+  a.resid = static_cast<__nv_bfloat16*>(resid);
+  a.add_resid = add_resid ? 1 : 0;
+  a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+  a.eps = eps;
+  const int vpt = (a.vecs + 1023) / 1024;
+  const int threads = ((a.vecs + vpt - 1) / vpt + 31) / 32 * 32;
+  const int blocks = std::min(rows, 148 * 2);
+  if (vpt == 1) launch_pdl(symm_rsn_kernel<1>, dim3(blocks), dim3(threads), 0, s, a);
+  else if (vpt == 2) launch_pdl(symm_rsn_kernel<2>, dim3(blocks), dim3(threads), 0, s, a);
+  else launch_pdl(symm_rsn_kernel<4>, dim3(blocks), dim3(threads), 0, s, a);
+  launch_pdl(symm_bump_kernel, dim3(1), dim3(1), 0, s, epoch);
+}
 
 void launch_epoch_bump(uint32_t* epoch, cudaStream_t s) {
   launch_pdl(symm_bump_kernel, dim3(1), dim3(1), 0, s, epoch);

@@ -246,19 +246,19 @@ class Engine:
         size = config.tp_info.size
         if size == 1:
             return None
-        if dist.is_initialized():
-            return dist.group.WORLD
-        backend = "cpu:gloo,cuda:nccl" if self.is_cuda else "gloo"
-        dist.init_process_group(backend=backend, rank=config.tp_info.rank, world_size=size,
-                                timeout=timedelta(seconds=config.distributed_timeout),
-                                init_method=config.distributed_addr,
-                                device_id=self.device if self.is_cuda else None)
-        self._owns_pg = True
+        if not dist.is_initialized():  # otherwise the launcher's group (e.g. torchrun's) is joined
+            backend = "cpu:gloo,cuda:nccl" if self.is_cuda else "gloo"
+            dist.init_process_group(backend=backend, rank=config.tp_info.rank, world_size=size,
+                                    timeout=timedelta(seconds=config.distributed_timeout),
+                                    init_method=config.distributed_addr,
+                                    device_id=self.device if self.is_cuda else None)
+            self._owns_pg = True
         if self.is_cuda and config.comm == "fused" and config.cp_size <= 1:
             from minisgl.parallel.symm import enable_symm_comm
 
-            enable_symm_comm(self.device, config.max_forward_len * config.model_config.hidden_size
-                             * self.dtype.itemsize)
+            # one more row per rank: the sequence-parallel form pads token counts to a multiple of the ranks
+            rows = config.max_forward_len + size
+            enable_symm_comm(self.device, rows * config.model_config.hidden_size * self.dtype.itemsize)
         return dist.group.WORLD
 
     def _load_weights(self, config: EngineConfig) -> Dict[str, torch.Tensor]:

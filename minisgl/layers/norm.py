@@ -43,6 +43,11 @@ class RMSNormFused(BaseOP):
     def folded(self) -> bool:
         return self._folded
 
+    @property
+    def active_weight(self) -> Optional[torch.Tensor]:
+        """The weight the norm itself applies (None once folded)."""
+        return None if self._folded else self.weight
+
     def forward(self, x: torch.Tensor, residual: Optional[torch.Tensor] = None) -> Tuple[torch.Tensor, torch.Tensor]:
         w = None if self._folded else self.weight
         if residual is None:

@@ -11,6 +11,7 @@ import torch
 from minisgl import ops
 from minisgl.core import get_global_ctx
 from minisgl.layers import BaseOP, OPList, ParallelLMHead, RMSNormFused, VocabParallelEmbedding
+from minisgl.parallel import DistributedImpl, get_tp_info, sequence_parallel_comm
 from minisgl.utils import nvtx_annotate
 
 from .base import BaseLLMModel
@@ -35,6 +36,10 @@ class DecoderLayer(BaseOP):
     * ``forward_fused`` (decode and short chunks): four GEMMs per layer whose
       epilogues carry the RMSNorms, q/k-norm + RoPE + KV store, SiLU x up and
       both residual adds; the residual stream is updated in place.
+
+    Under tensor parallelism with a sequence-parallel communicator
+    (``forward_sp``) the residual stream is token-sharded and the collectives
+    after o_proj / down_proj carry the residual adds and the RMSNorms.
 
     After loading, the input / post-attention RMSNorm weights are folded into
     the columns of the qkv / gate_up weights (norm(x) @ W^T = rstd(x) *
@@ -88,6 +93,43 @@ class DecoderLayer(BaseOP):
         h = ops.rmsnorm(r, self.post_attention_layernorm.weight, self.post_attention_layernorm.eps)
         return r.add_(self.mlp.forward(h))
 
+    @nvtx_annotate("Layer_{}", layer_id_field="_layer_id")
+    def forward_sp(self, x: torch.Tensor, r: torch.Tensor, comm: DistributedImpl, T: int,
+                   next_norm: RMSNormFused) -> torch.Tensor:
+        """Sequence-parallel block over tensor-parallel ranks. ``x`` [T_pad, H]
+        holds every rank's normalised input rows (gathered by the previous
+        collective), ``r`` this rank's slice of the residual stream (updated in
+        place). Each row-parallel projection writes its partial product where
+        ``comm.rs_norm_ag`` reduce-scatters it into ``r``, normalises the new
+        rows and gathers them for the next column-parallel GEMM; the last
+        collective applies ``next_norm`` (the next layer's input norm or the
+        final norm). Returns the gathered rows after this block."""
+        Tp, H = x.shape
+        first = get_tp_info().rank == 0
+        attn = self.self_attn
+        fused = T <= FUSED_MAX_TOKENS and self._fused_attn
+        xt = x[:T]
+        if fused:  # q/k norm, RoPE and the KV store in the qkv GEMM's epilogue
+            q = torch.empty(T, attn.attn.qo_attn_dim, dtype=x.dtype, device=x.device)
+            ops.gemm_fused(xt, attn.qkv_proj.weight, bias=attn.qkv_proj.bias, rope=attn.attn.rope_args(), out=q)
+            o = attn.attn.attend(q)
+        else:
+            o = attn.attn.forward(attn.qkv_proj.forward(xt))
+        part = comm.sp_partial(Tp, H, x.dtype, x.device)
+        ops.gemm(o, attn.o_proj.weight, attn.o_proj.bias if first else None, out=part[:T])
+        norm = self.post_attention_layernorm
+        x = comm.rs_norm_ag(part, r, True, norm.active_weight, norm.eps)
+        xt = x[:T]
+        mlp = self.mlp
+        if fused and self._fused_mlp:
+            h = ops.gemm_fused(xt, mlp.gate_up_proj.weight, silu=True)
+        else:
+            g = mlp.gate_up_proj.forward(xt)
+            h = ops.silu_and_mul(g, interleaved=True) if mlp._interleaved else mlp._act(g)
+        part = comm.sp_partial(Tp, H, x.dtype, x.device)
+        ops.gemm(h, mlp.down_proj.weight, mlp.down_proj.bias if first else None, out=part[:T])
+        return comm.rs_norm_ag(part, r, True, next_norm.active_weight, next_norm.eps)
+
 
 class DecoderModel(BaseOP):
     def __init__(self, config: "ModelConfig", **flags: bool) -> None:
@@ -99,7 +141,45 @@ class DecoderModel(BaseOP):
     def fusable(self) -> bool:
         return all(layer.fusable for layer in self.layers.op_list)
 
+    @property
+    def sp_capable(self) -> bool:
+        """Dense blocks only: the sequence-parallel form needs every MLP to be a
+        row-parallel GatedMLP (MoE layers keep the all-reduce form)."""
+        return all(isinstance(layer.mlp, GatedMLP) for layer in self.layers.op_list)
+
+    def sp_comm(self) -> Optional[DistributedImpl]:
+        comm = sequence_parallel_comm()
+        return comm if comm is not None and self.sp_capable else None
+
+    def forward_sp(self, input_ids: torch.Tensor, comm: DistributedImpl) -> torch.Tensor:
+        """Tensor parallelism with a token-sharded residual stream: T tokens
+        are padded to a multiple of the rank count R and rank r keeps residual
+        rows [r * T_pad / R, (r + 1) * T_pad / R). The vocabulary-sharded
+        embedding's partial rows are reduce-scattered like a projection's;
+        every collective also applies the following RMSNorm and gathers the
+        normalised rows. Returns the final-normed hidden rows [T, H]."""
+        T = input_ids.shape[0]
+        R = get_tp_info().size
+        rows = -(-T // R)
+        Tp = rows * R
+        emb = self.embed_tokens
+        H = emb.weight.shape[1]
+        part = comm.sp_partial(Tp, H, emb.weight.dtype, emb.weight.device)
+        ops.embedding(input_ids, emb.weight, emb.vocab_range, out=part[:T])
+        if Tp > T:
+            part[T:].zero_()
+        r = torch.empty(rows, H, dtype=emb.weight.dtype, device=emb.weight.device)
+        layers = self.layers.op_list
+        norm0 = layers[0].input_layernorm if layers else self.norm
+        x = comm.rs_norm_ag(part, r, False, norm0.active_weight, norm0.eps)
+        for i, layer in enumerate(layers):
+            x = layer.forward_sp(x, r, comm, T, layers[i + 1].input_layernorm if i + 1 < len(layers) else self.norm)
+        return x[:T]
+
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        comm = self.sp_comm()
+        if comm is not None:
+            return self.forward_sp(input_ids, comm)
         x = self.embed_tokens.forward(input_ids)
         if self.fusable and x.shape[0] <= FUSED_MAX_TOKENS:
             r = x  # a fresh buffer: the residual stream is updated in place
@@ -140,14 +220,20 @@ class DecoderForCausalLM(BaseLLMModel):
         out: Dict[Tuple[int, int], Tuple[int, int, int]] = {}
         if not self.model.fusable:
             return out
+        # sequence parallel: the collectives apply the norms and the residual
+        # adds, so the GEMMs carry only RoPE / SiLU epilogues
+        sp = self.model.sp_comm() is not None
+        norm = 0 if sp else ops.EPI_NORM
         for layer in self.model.layers.op_list:
             attn = layer.self_attn
             hq, hk = attn.attn.num_qo_heads, attn.attn.num_kv_heads
-            out[tuple(attn.qkv_proj.weight.shape)] = (ops.EPI_NORM | ops.EPI_ROPE, hq, hk)
-            out[tuple(attn.o_proj.weight.shape)] = (ops.EPI_RESIDUAL, hq, hk)
+            out[tuple(attn.qkv_proj.weight.shape)] = (norm | ops.EPI_ROPE, hq, hk)
+            if not sp:
+                out[tuple(attn.o_proj.weight.shape)] = (ops.EPI_RESIDUAL, hq, hk)
             if layer._fused_mlp:
-                out[tuple(layer.mlp.gate_up_proj.weight.shape)] = (ops.EPI_NORM | ops.EPI_SILU, hq, hk)
-                out[tuple(layer.mlp.down_proj.weight.shape)] = (ops.EPI_RESIDUAL, hq, hk)
+                out[tuple(layer.mlp.gate_up_proj.weight.shape)] = (norm | ops.EPI_SILU, hq, hk)
+                if not sp:
+                    out[tuple(layer.mlp.down_proj.weight.shape)] = (ops.EPI_RESIDUAL, hq, hk)
         if self.samples_in_lm_head:
             head = self.lm_head._tied.weight if self.lm_head._tied is not None else self.lm_head.weight
             out[tuple(head.shape)] = (ops.EPI_SAMPLE, 0, 0)

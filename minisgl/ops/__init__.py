@@ -242,11 +242,17 @@ def _act_and_mul(x: torch.Tensor, act: str, out: Optional[torch.Tensor], interle
     return out
 
 
-def embedding(ids: torch.Tensor, weight: torch.Tensor, vocab_range: Optional[Tuple[int, int]] = None) -> torch.Tensor:
+def embedding(ids: torch.Tensor, weight: torch.Tensor, vocab_range: Optional[Tuple[int, int]] = None,
+              out: Optional[torch.Tensor] = None) -> torch.Tensor:
     lo, n = vocab_range if vocab_range is not None else (0, weight.shape[0])
     if not weight.is_cuda:
-        return ref.embedding(ids, weight, lo, n)
-    out = torch.empty(ids.numel(), weight.shape[1], dtype=weight.dtype, device=weight.device)
+        y = ref.embedding(ids, weight, lo, n)
+        if out is not None:
+            out.copy_(y)
+            return out
+        return y
+    if out is None:
+        out = torch.empty(ids.numel(), weight.shape[1], dtype=weight.dtype, device=weight.device)
     _count()
     native().embedding(out, weight, ids.to(torch.int32), lo, n)
     return out

@@ -64,7 +64,8 @@ class SymmMemImpl(DistributedImpl):
         self._cpu_group = dist.new_group(ranks=ranks, backend="gloo")
         with torch.cuda.device(device):
             # [signals][GEMM flags][collective data][two GEMM partial halves]
-            own, handle = native.symm_create(DATA_OFFSET + 3 * self.capacity)
+            # [gathered rows of the sequence-parallel collective]
+            own, handle = native.symm_create(DATA_OFFSET + 4 * self.capacity)
         handles: List[Optional[bytes]] = [None] * self.world
         dist.all_gather_object(handles, handle, group=self._cpu_group)
         bases: List[int] = []
@@ -84,6 +85,8 @@ class SymmMemImpl(DistributedImpl):
         self.calls = 0  # collective launches so far (the fault-injection clock)
         self._faults = bool(fault.rules())
         self.data = torch.as_tensor(_DeviceBuffer(own + DATA_OFFSET, self.capacity), device=device)
+        self.gather_offset = DATA_OFFSET + 3 * self.capacity
+        self.gathered = torch.as_tensor(_DeviceBuffer(own + self.gather_offset, self.capacity), device=device)
         dist.barrier(group=self._cpu_group)  # every heap is mapped before the first collective
 
     # -------------------------------------------------------------- buffers
@@ -103,6 +106,37 @@ class SymmMemImpl(DistributedImpl):
         ops._count(2)
         ops.native().symm_collective(kind, out, residual, self.bases, self.epoch[1:], self.rank, self.world, n_elems,
                                      rows, row_elems, ops.error_word(out.device))
+
+    # ----------------------------------------------- sequence parallelism
+    # The decoder keeps the residual stream token-sharded between layers
+    # (rank r holds rows [r * T / R, (r + 1) * T / R)); each row-parallel
+    # projection writes its partial product into ``sp_partial`` and
+    # ``rs_norm_ag`` reduce-scatters it into the residual slice, normalises the
+    # new rows and gathers them on every rank for the next column-parallel GEMM.
+    sequence_parallel = True
+
+    def sp_partial(self, rows: int, cols: int, dtype: torch.dtype, device: torch.device) -> torch.Tensor:
+        """Where a row-parallel GEMM writes its partial product [rows, cols]."""
+        return self.partial_buffer(rows, cols, dtype)
+
+    def rs_norm_ag(self, partial: torch.Tensor, resid: torch.Tensor, add_resid: bool,
+                   norm_w: Optional[torch.Tensor], eps: float) -> torch.Tensor:
+        """Reduce-scatter ``partial`` (an ``sp_partial`` view, [R * rows, H])
+        into ``resid`` [rows, H] (added to it when ``add_resid``), RMS-normalise
+        the new rows (times ``norm_w`` when given) and return all ranks'
+        normalised rows [R * rows, H] (a view of the heap's gather region, valid
+        until the next call). One kernel (``minisgl/csrc/symm.cu``)."""
+        rows, H = resid.shape
+        assert partial.data_ptr() == self.data.data_ptr() and partial.shape == (rows * self.world, H)
+        if 2 * rows * self.world * H > self.capacity:
+            raise RuntimeError("symmetric heap too small for the sequence-parallel collective")
+        self.calls += 1
+        if self._faults and fault.skip_collective(self.rank, self.calls - 1):
+            return self.gathered[: 2 * rows * self.world * H].view(torch.bfloat16).view(rows * self.world, H)
+        ops._count(2)
+        ops.native().symm_rsn(resid, add_resid, norm_w, eps, self.bases, self.epoch[1:], self.rank, self.world,
+                              DATA_OFFSET, self.gather_offset, ops.error_word(resid.device))
+        return self.gathered[: 2 * rows * self.world * H].view(torch.bfloat16).view(rows * self.world, H)
 
     # ---------------------------------------------------------- collectives
     def gemm_reduce_into(self, x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor],

@@ -20,7 +20,7 @@ from minisgl.kvcache import BaseCacheHandle, MatchResult, create_prefix_cache
 from minisgl.utils import div_ceil
 
 if TYPE_CHECKING:
-    from .utils import PendingReq
+    from .prefill import PendingReq
 
 
 class CacheManager:

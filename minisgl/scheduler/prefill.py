@@ -18,9 +18,8 @@ import torch
 
 from minisgl.core import Batch, Req
 
-from .utils import PendingReq
-
 if TYPE_CHECKING:
+    from minisgl.core import SamplingParams
     from minisgl.kvcache import BaseCacheHandle
     from minisgl.message import UserMsg
 
@@ -38,6 +37,25 @@ class ChunkedReq(Req):
     @property
     def can_decode(self) -> bool:
         return False
+
+
+@dataclass(slots=True)
+class PendingReq:
+    """A request waiting for (more of) its prefill. Its prompt and output
+    lengths are fixed when it arrives, so admission reads them as fields;
+    ``chunked_req`` holds the part already admitted while the prompt is
+    split over several steps."""
+
+    uid: int
+    input_ids: torch.Tensor
+    sampling_params: "SamplingParams"
+    input_len: int = field(init=False)
+    output_len: int = field(init=False)
+    chunked_req: Optional[ChunkedReq] = None
+
+    def __post_init__(self) -> None:
+        self.input_len = int(self.input_ids.shape[0])
+        self.output_len = int(self.sampling_params.max_tokens)
 
 
 def _copy_to_device(dst: torch.Tensor, src: torch.Tensor) -> None:

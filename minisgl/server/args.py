@@ -35,13 +35,13 @@ class ServerArgs(SchedulerConfig):
 
     @property
     def zmq_frontend_addr(self) -> str:
-        return "ipc:///tmp/minisgl_3" + self._unique_suffix
+        return self.ipc_endpoint("frontend")
 
     @property
     def zmq_tokenizer_addr(self) -> str:
         if self.share_tokenizer:
             return self.zmq_detokenizer_addr
-        return "ipc:///tmp/minisgl_4" + self._unique_suffix
+        return self.ipc_endpoint("tokenizer")
 
     @property
     def tokenizer_create_addr(self) -> bool:

@@ -31,11 +31,11 @@ _QWEN3_BASE: Dict[str, Any] = {
 }
 
 SHAPES: Dict[str, Dict[str, Any]] = {
-    # tiny Qwen3-style decoder (CPU, fp32)
+    # tiny Qwen3-style decoder for CPU tests (fp32)
     "tiny-qwen3": dict(_QWEN3_BASE, num_hidden_layers=2, hidden_size=256, num_attention_heads=4,
                        num_key_value_heads=2, head_dim=64, intermediate_size=512, vocab_size=1024,
                        tie_word_embeddings=True, max_position_embeddings=4096, torch_dtype="float32"),
-    # BASELINE config 2
+    # Qwen3-0.6B: the reference's offline-benchmark model
     "qwen3-0.6b": dict(_QWEN3_BASE, num_hidden_layers=28, hidden_size=1024, num_attention_heads=16,
                        num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=151936,
                        tie_word_embeddings=True),
@@ -43,7 +43,7 @@ SHAPES: Dict[str, Dict[str, Any]] = {
     "small-qwen3": dict(_QWEN3_BASE, num_hidden_layers=2, hidden_size=1024, num_attention_heads=16,
                         num_key_value_heads=8, head_dim=128, intermediate_size=3072, vocab_size=4096,
                         tie_word_embeddings=False, max_position_embeddings=8192),
-    # BASELINE config 3
+    # Qwen3-32B: the tensor-parallel serving benchmark model
     "qwen3-32b": dict(_QWEN3_BASE, num_hidden_layers=64, hidden_size=5120, num_attention_heads=64,
                       num_key_value_heads=8, head_dim=128, intermediate_size=25600, vocab_size=151936,
                       tie_word_embeddings=False),
@@ -68,7 +68,7 @@ SHAPES: Dict[str, Dict[str, Any]] = {
         "rope_scaling": {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
                          "original_max_position_embeddings": 1024},
     },
-    # BASELINE config 4 / 5: Kimi-K2 shape (DeepSeek-V3 architecture)
+    # Kimi-K2 shape (DeepSeek-V3 architecture): expert / context parallel benchmarks
     "kimi-k2": {
         "model_type": "kimi_k2", "architectures": ["DeepseekV3ForCausalLM"], "hidden_act": "silu",
         "rms_norm_eps": 1e-6, "rope_theta": 50000.0, "max_position_embeddings": 262144,

@@ -1,4 +1,4 @@
-"""End-to-end engine on the CPU: the paged, chunked,
+"""End-to-end engine on the CPU (tiny Qwen3, fp32): the paged, chunked,
 radix-cached scheduler must reproduce the dense fp32 oracle token for token."""
 
 import random

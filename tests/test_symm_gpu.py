@@ -1,7 +1,8 @@
 """NVLink collectives from our own kernels (``--comm fused``) on 2 GPUs: the
-one-shot all-reduce (plain and with the residual add fused), the all-gather
-and a CUDA-graph replay against NCCL, and a TP=2 engine with the fused
-communicator against one with NCCL. Ranks are child processes; NCCL's NVLS
+one-shot all-reduce (plain and with the residual add fused), the all-gather,
+the sequence-parallel reduce-scatter + residual + RMSNorm + all-gather and a
+CUDA-graph replay against NCCL, and a TP=2 engine with the fused
+communicator (sequence-parallel decoder) against one with NCCL. Ranks are child processes; NCCL's NVLS
 is off and no multicast object is created."""
 
 import os
@@ -93,6 +94,25 @@ def _collectives(rank, world, port, q):
             dist.all_gather(outs, got)
             if not all(torch.equal(o, outs[0]) for o in outs):
                 msgs.append(f"gemm_reduce_into ranks differ M={M}")
+        # sequence-parallel collective: reduce-scatter into the residual slice,
+        # RMSNorm (with and without a weight), all-gather of the normalised rows
+        from minisgl.parallel.comm import TorchDistributedImpl
+
+        lib = TorchDistributedImpl()
+        for rows, H, add, weighted in ((1, 1024, False, False), (5, 5120, True, True), (64, 12288, True, False)):
+            part = impl.sp_partial(rows * world, H, torch.bfloat16, dev)
+            part.copy_(torch.randn(rows * world, H, device=dev, generator=g).to(torch.bfloat16))
+            resid = torch.randn(rows, H, device=dev, generator=g).to(torch.bfloat16)
+            w = (1.0 + 0.1 * torch.randn(H, device=dev, generator=g)).to(torch.bfloat16) if weighted else None
+            resid_ref = resid.clone()
+            want = lib.rs_norm_ag(part.clone(), resid_ref, add, w, 1e-6)
+            got = impl.rs_norm_ag(part, resid, add, w, 1e-6)
+            if not _close(resid, resid_ref, 1e-2) or not _close(got, want, 3e-2):
+                msgs.append(f"rs_norm_ag rows={rows} H={H}")
+            outs = [torch.empty_like(got) for _ in range(world)]
+            dist.all_gather(outs, got.contiguous())
+            if not all(torch.equal(o, outs[0]) for o in outs):
+                msgs.append(f"rs_norm_ag ranks differ rows={rows} H={H}")
         # CUDA graph: the device epoch advances on every replay
         buf = torch.zeros(4096, device=dev, dtype=torch.bfloat16)
         stream = torch.cuda.Stream(dev)

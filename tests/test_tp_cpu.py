@@ -2,7 +2,11 @@
 loading the same HF checkpoint must generate what the single-rank engine
 generates. Exercises the weight loader's shard/merge rules, vocab-parallel
 embedding and LM head, row-parallel all-reduce and the rank-0 message
-fan-out path of the engine."""
+fan-out path of the engine. The sequence-parallel form of the decoder
+(token-sharded residual stream; reduce-scatter + residual + RMSNorm +
+all-gather after each row-parallel projection, token counts padded to a
+multiple of the rank count) runs here through the library collectives and
+must generate the same tokens."""
 
 import os
 import shutil
@@ -22,15 +26,21 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(rank, world, folder, port, out_q):
+def _run(rank, world, folder, port, out_q, sp=False):
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
-    from minisgl.parallel import DistributedInfo
+    from minisgl.parallel import DistributedCommunicator, DistributedInfo
 
     llm = LLM(folder, dtype=torch.float32, device="cpu", tp_info=DistributedInfo(rank, world), page_size=16,
               num_page_override=64, max_running_req=4, max_seq_len_override=256, max_extend_tokens=64,
               distributed_port=port)
-    outs = llm.generate(PROMPTS, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
+    if sp:
+        DistributedCommunicator.plugins[-1].sequence_parallel = True
+        assert llm.engine.model.model.sp_comm() is not None
+    # 21 prompt tokens (odd: the sequence-parallel form pads), then decode
+    # batches of 2 and, after the second request ends, of 1
+    sps = [SamplingParams(temperature=0.0, max_tokens=m, ignore_eos=True) for m in (8, 5)]
+    outs = llm.generate(PROMPTS, sps)
     out_q.put((rank, [o["token_ids"] for o in outs]))
     llm.shutdown()
 
@@ -47,11 +57,11 @@ def checkpoint():
     shutil.rmtree(folder, ignore_errors=True)
 
 
-def _generate(world, folder):
+def _generate(world, folder, sp=False):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, folder, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, folder, port, q, sp)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(world))
@@ -61,7 +71,16 @@ def _generate(world, folder):
     return results
 
 
-def test_tp2_matches_tp1(checkpoint):
-    single = _generate(1, checkpoint)[0]
+@pytest.fixture(scope="module")
+def single(checkpoint):
+    return _generate(1, checkpoint)[0]
+
+
+def test_tp2_matches_tp1(checkpoint, single):
     tp = _generate(2, checkpoint)
+    assert tp[0] == tp[1] == single
+
+
+def test_tp2_sequence_parallel_matches_tp1(checkpoint, single):
+    tp = _generate(2, checkpoint, sp=True)
     assert tp[0] == tp[1] == single
