@@ -77,7 +77,6 @@ def main() -> None:
 
     base = TensorParallelLLM if args.world > 1 else LLM
     extra = dict(rank=args.rank, world=args.world) if args.world > 1 else {}
-    torch.cuda.set_device(args.rank if args.world > 1 else 0)
     llm = bench.metered_llm_class(base)(args.model_dir, use_dummy_weight=True, max_seq_len_override=20480,
                                         max_extend_tokens=16384, cuda_graph_max_bs=256, max_running_req=256,
                                         page_size=bench.PAGE_SIZE, **extra)

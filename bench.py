@@ -363,10 +363,11 @@ def run_reference(args) -> None:
     from minisgl.utils.synthetic import make_model_dir
 
     model_dir = make_model_dir(args.shape)
-    env = dict(os.environ)
-    for k in ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT", "LOCAL_WORLD_SIZE",
-              "GROUP_RANK", "ROLE_RANK", "TORCHELASTIC_RUN_ID"):
-        env.pop(k, None)
+    # the reference sets up its own process group: drop torchrun's rendezvous
+    # variables (TORCHELASTIC_USE_AGENT_STORE would make its rank 0 a client)
+    launcher = ("RANK", "WORLD_SIZE", "LOCAL_RANK", "MASTER_ADDR", "MASTER_PORT", "LOCAL_WORLD_SIZE", "GROUP_RANK",
+                "ROLE_RANK", "ROLE_NAME", "GROUP_WORLD_SIZE", "ROLE_WORLD_SIZE", "OMP_NUM_THREADS")
+    env = {k: v for k, v in os.environ.items() if k not in launcher and not k.startswith("TORCHELASTIC_")}
     port = 29700 + (int(os.environ.get("MASTER_PORT", "29500")) % 97) * 3
     cmd = [sys.executable, os.path.join(ROOT, "baseline", "run_reference.py"), "--rank", str(rank),
            "--world", str(world), "--port", str(port), "--model-dir", model_dir] + \

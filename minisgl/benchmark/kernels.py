@@ -423,8 +423,10 @@ def probe_plan(M: int, N: int, K: int, mode: int, bn: int, splits: int, kps: int
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     nat = ops.native()
 
+    ws = ops.streamk_workspace(x.device) if mode == ops.GEMM_STREAMK else None
+
     def run(w, tr=None):
-        nat.gemm(out, x, w, None, None, splits, mode, None, bn, tr, kps)
+        nat.gemm(out, x, w, None, ws, splits, mode, None, bn, tr, kps)
 
     for i in range(8):
         run(ws[i % 8])
@@ -444,6 +446,15 @@ def probe_plan(M: int, N: int, K: int, mode: int, bn: int, splits: int, kps: int
         t = tr.view(-1, 8).cpu()
         t = t[t[:, 0] > 0].double()
         rel = (t - t[:, 0].min()) / 1000.0
+        if mode == ops.GEMM_STREAMK:
+            last = torch.where(t[:, 4] > 0, rel[:, 4], rel[:, 3])
+            own = t[:, 5] > 0
+            row.update({"ctas": len(t), "entry": _quantiles(rel[:, 0]), "set-up": _quantiles(rel[:, 1] - rel[:, 0]),
+                        "producer past wait": _quantiles(rel[:, 2]), "first acc ready": _quantiles(rel[:, 3]),
+                        "last acc ready": _quantiles(last),
+                        "owner waits": _quantiles(rel[own, 5] - last[own]) if bool(own.any()) else "none",
+                        "epilogue after last acc": _quantiles(rel[:, 6] - last), "exit": _quantiles(rel[:, 6])})
+            return row
         row.update({"ctas": len(t), "entry": _quantiles(rel[:, 0]), "set-up": _quantiles(rel[:, 1] - rel[:, 0]),
                     "producer past wait": _quantiles(rel[:, 2]),
                     "first stage after wait": _quantiles(rel[:, 3] - rel[:, 2]),

@@ -1048,6 +1048,68 @@ void sample(at::Tensor out, const at::Tensor& logits, const at::Tensor& temperat
   minisgl::launch_sample(a, stream_of(logits));
 }
 
+// Vocabulary-sharded sampling: packed partials of this rank's logits shard
+// (global indices from `offset`), then (after an all-gather of the packed
+// rows) the tokens. temperature None: greedy.
+int64_t sample_shard_chunks(int64_t v_shard) { return minisgl::sample_split_chunks(static_cast<int>(v_shard)); }
+
+void sample_shard_partials(at::Tensor packed, const at::Tensor& logits, const c10::optional<at::Tensor>& temperature,
+                           int64_t seed, const c10::optional<at::Tensor>& step, int64_t offset) {
+  check_cuda(logits, "logits");
+  check_i32(packed, "packed");
+  MSG_CHECK(logits.scalar_type() == at::kFloat && logits.dim() == 2 && logits.stride(1) == 1,
+            "logits must be float32 [B, V_shard]");
+  const int64_t B = logits.size(0);
+  MSG_CHECK(packed.dim() == 2 && packed.size(0) == B && packed.is_contiguous() &&
+                packed.size(1) >= 2 * minisgl::sample_split_chunks(static_cast<int>(logits.size(1))),
+            "packed partials must be int32 [B, >= 2 chunks]");
+  minisgl::SampleArgs a{};
+  a.logits = logits.data_ptr<float>();
+  a.ld = static_cast<int>(logits.stride(0));
+  a.B = static_cast<int>(B);
+  a.V = static_cast<int>(logits.size(1));
+  a.temperature = nullptr;
+  if (temperature.has_value()) {
+    MSG_CHECK(temperature->scalar_type() == at::kFloat && temperature->numel() >= B && temperature->is_contiguous(),
+              "temperature must be float32 [B]");
+    a.temperature = temperature->data_ptr<float>();
+  }
+  a.seed = static_cast<uint64_t>(seed);
+  a.step = nullptr;
+  if (step.has_value()) {
+    MSG_CHECK(step->scalar_type() == at::kLong && step->is_cuda(), "step must be a CUDA int64 scalar");
+    a.step = step->data_ptr<int64_t>();
+  }
+  a.index_offset = static_cast<int>(offset);
+  const c10::cuda::CUDAGuard guard(logits.device());
+  minisgl::launch_sample_shard_partials(a, packed.data_ptr<int32_t>(), static_cast<int>(packed.size(1)),
+                                        stream_of(logits));
+}
+
+void sample_shard_reduce(at::Tensor out, const at::Tensor& gathered, int64_t chunks, int64_t ranks,
+                         const c10::optional<at::Tensor>& temperature, const c10::optional<at::Tensor>& step) {
+  check_i32(out, "out");
+  check_i32(gathered, "gathered");
+  const int64_t B = out.numel();
+  MSG_CHECK(gathered.dim() == 2 && gathered.is_contiguous() && gathered.size(0) == ranks * B &&
+                gathered.size(1) >= 2 * chunks,
+            "gathered partials must be int32 [ranks * B, >= 2 chunks]");
+  const float* t = nullptr;
+  if (temperature.has_value()) {
+    MSG_CHECK(temperature->scalar_type() == at::kFloat && temperature->numel() >= B, "temperature float32 [B]");
+    t = temperature->data_ptr<float>();
+  }
+  int64_t* st = nullptr;
+  if (step.has_value()) {
+    MSG_CHECK(step->scalar_type() == at::kLong && step->is_cuda(), "step must be a CUDA int64 scalar");
+    st = step->data_ptr<int64_t>();
+  }
+  const c10::cuda::CUDAGuard guard(gathered.device());
+  minisgl::launch_sample_shard_reduce(out.data_ptr<int32_t>(), gathered.data_ptr<int32_t>(), static_cast<int>(chunks),
+                                      static_cast<int>(gathered.size(1)), static_cast<int>(ranks),
+                                      static_cast<int>(B), t, st, stream_of(gathered));
+}
+
 // -------------------------------------------------------------------- MoE
 void moe_route(const at::Tensor& logits, const c10::optional<at::Tensor>& bias, at::Tensor topk_w,
                at::Tensor topk_ids, int64_t scoring, bool renormalize, int64_t n_group,
@@ -1139,6 +1201,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_free", &symm_free);
   m.def("symm_collective", &symm_collective);
   m.def("symm_rsn", &symm_rsn);
+  m.def("sample_shard_chunks", &sample_shard_chunks);
+  m.def("sample_shard_partials", &sample_shard_partials);
+  m.def("sample_shard_reduce", &sample_shard_reduce);
   m.def("gemm_allreduce", &gemm_allreduce);
   m.def("prefill_attention", &prefill_attention);
   m.def("argmax", &argmax);

@@ -992,6 +992,39 @@ std::vector<int64_t> gemm_plan_desc(int64_t M, int64_t N, int64_t K) {
 
 void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   if (a.M <= 0 || a.N <= 0) return;
+  if (a.force_mode == 4) {
+    // stream-K weight streaming (gemm_streamk.cu): force_bn = weight sub-tiles
+    // per work tile (R), force_kps = k-blocks per stage (0: automatic); the
+    // workspace holds one partial tile per SM followed by the ready flags
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    if (a.workspace == nullptr || a.workspace_elems < static_cast<int64_t>(sms) * (kStreamKSlotFloats + 1))
+      throw std::runtime_error("minisgl.gemm: the stream-K plan needs its workspace");
+    GemmStreamKArgs k{};
+    k.x = a.x;
+    k.w = a.w;
+    k.bias = a.bias;
+    k.out = a.out;
+    k.M = a.M;
+    k.N = a.N;
+    k.K = a.K;
+    k.ldx = a.ldx;
+    k.ldw = a.ldw;
+    k.ldo = a.ldo;
+    k.out_f32 = a.out_f32 ? 1 : 0;
+    k.R = a.force_bn == 2 ? 2 : 1;
+    k.kps = a.force_kps;
+    k.grid = gemm_streamk_grid(a.M, a.N, a.K, k.R, sms);
+    k.ws = a.workspace;
+    k.flags = reinterpret_cast<int*>(a.workspace + static_cast<int64_t>(sms) * kStreamKSlotFloats);
+    k.ws_slots = sms;
+    k.ws_slot_floats = kStreamKSlotFloats;
+    k.err = a.err;
+    k.trace = a.trace;
+    launch_gemm_streamk(k, stream);
+    return;
+  }
   if (a.K % 8 != 0 || a.ldx % 8 != 0 || a.ldw % 8 != 0)
     throw std::runtime_error("minisgl.gemm: K and row strides must be multiples of 8 elements");
   if (a.N % 4 != 0) throw std::runtime_error("minisgl.gemm: N must be a multiple of 4");

@@ -90,6 +90,31 @@ struct GemmArgs {
   int g_experts;
 };
 void launch_gemm(const GemmArgs& a, cudaStream_t stream);
+// Stream-K weight-streaming GEMM for up to 256 tokens (gemm_streamk.cu):
+// R = 1 or 2 weight sub-tiles of 128 rows per work tile; ws holds ws_slots
+// fp32 partial tiles of ws_slot_floats each, flags ws_slots int32 (all 0
+// between launches). grid <= ws_slots CTAs (one per SM).
+struct GemmStreamKArgs {
+  const void* x;
+  const void* w;
+  const void* bias;
+  void* out;
+  int M, N, K;
+  int ldx, ldw, ldo;
+  int out_f32;
+  int R;
+  int kps;  // 0 = from the shared-memory budget
+  int grid;
+  float* ws;
+  int* flags;
+  int ws_slots;
+  int64_t ws_slot_floats;
+  int* err;
+  void* trace;  // optional uint64 [grid * 8] phase stamps
+};
+constexpr int64_t kStreamKSlotFloats = 2 * 256 * 128;  // R = 2, 256 tokens
+int gemm_streamk_grid(int M, int N, int K, int R, int sms);
+void launch_gemm_streamk(const GemmStreamKArgs& a, cudaStream_t stream);
 // Persistent 128 x {128, 256} tiles with double-buffered TMEM accumulators
 // (force_mode 3): plain GEMMs (no fused epilogue) with K % 64 == 0.
 bool gemm_persistent_supported(const GemmArgs& a);
@@ -220,6 +245,7 @@ struct SampleArgs {
   const float* top_p;        // [B] or nullptr
   uint64_t seed;
   const int64_t* step;       // device counter mixed into the random stream (may be nullptr)
+  int index_offset;          // vocabulary index of column 0 (a tensor-parallel shard's first row)
 };
 void launch_sample(const SampleArgs& a, cudaStream_t s);
 // Greedy (temperature == nullptr) or temperature sampling with each row
@@ -229,6 +255,15 @@ int sample_split_chunks(int V);
 void launch_sample_split(const SampleArgs& a, float* part_val, int32_t* part_idx, cudaStream_t s);
 void launch_lm_sample_reduce(int32_t* out, const float* part_val, const int32_t* part_idx, int ntiles, int B,
                              const float* temps, int64_t* step, cudaStream_t s);
+// Vocabulary-sharded sampling (tensor parallelism): partials of this rank's
+// logits shard [B, V_shard] (global indices from a.index_offset), written as
+// rows of `ld` int32 words: values (fp32 bits) in columns [0, chunks), indices
+// in [chunks, 2 chunks); sample_split_chunks(V_shard) chunks per row.
+void launch_sample_shard_partials(const SampleArgs& a, int32_t* packed, int ld, cudaStream_t s);
+// Tokens from every rank's packed partials [ranks][B][ld] (same tie rule as
+// the whole-vocabulary kernels); advances the step counter like them.
+void launch_sample_shard_reduce(int32_t* out, const int32_t* packed, int chunks, int ld, int ranks, int B,
+                                const float* temps, int64_t* step, cudaStream_t s);
 
 // ------------------------------------------------------------------- MoE ----
 struct MoeRouteArgs {

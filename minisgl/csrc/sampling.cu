@@ -222,7 +222,7 @@ constexpr int kPartThreads = 256;
 constexpr int kPartChunk = 8192;  // 8 float4 per thread
 
 __global__ void __launch_bounds__(kPartThreads) sample_part_kernel(SampleArgs a, float* part_val,
-                                                                   int32_t* part_idx, int nchunks) {
+                                                                   int32_t* part_idx, int nchunks, int ld) {
   pdl_launch_dependents();
   pdl_wait();
   const int b = blockIdx.y, c = blockIdx.x;
@@ -232,6 +232,7 @@ __global__ void __launch_bounds__(kPartThreads) sample_part_kernel(SampleArgs a,
   const uint64_t step = a.step != nullptr ? static_cast<uint64_t>(*a.step) : 0ull;
   const uint32_t key = row_key(a.seed, step, b);
   const int i0 = c * kPartChunk, i1 = min(a.V, i0 + kPartChunk);
+  const int off = a.index_offset;  // global index = off + local column
   ArgMax best{-INFINITY, 0x7fffffff};
   if ((a.V & 3) == 0 && (a.ld & 3) == 0) {
     const float4* row4 = reinterpret_cast<const float4*>(row);
@@ -241,20 +242,43 @@ __global__ void __launch_bounds__(kPartThreads) sample_part_kernel(SampleArgs a,
       const float ls[4] = {l4.x, l4.y, l4.z, l4.w};
 #pragma unroll
       for (int q = 0; q < 4; ++q) {
-        const int i = i4 * 4 + q;
+        const int i = off + i4 * 4 + q;
         best = better(best, ArgMax{greedy ? ls[q] : ls[q] * inv_t + gumbel(key, i), i});
       }
     }
   } else {
-    for (int i = i0 + static_cast<int>(threadIdx.x); i < i1; i += kPartThreads) {
-      const float l = row[i];
+    for (int j = i0 + static_cast<int>(threadIdx.x); j < i1; j += kPartThreads) {
+      const float l = row[j];
+      const int i = off + j;
       best = better(best, ArgMax{greedy ? l : l * inv_t + gumbel(key, i), i});
     }
   }
   best = block_argmax(best);
   if (threadIdx.x == 0) {
-    part_val[static_cast<int64_t>(b) * nchunks + c] = best.v;
-    part_idx[static_cast<int64_t>(b) * nchunks + c] = best.i;
+    part_val[static_cast<int64_t>(b) * ld + c] = best.v;
+    part_idx[static_cast<int64_t>(b) * ld + c] = best.i;
+  }
+}
+
+// Token of each row from the packed partials of every rank's vocabulary
+// shard ([ranks][B][ld] int32: fp32 value bits, then indices); the same
+// argmax and step advance as lm_sample_reduce_kernel.
+__global__ void shard_sample_reduce_kernel(int32_t* out, const int32_t* packed, int chunks, int ld, int ranks, int B,
+                                           const float* temps, int64_t* step) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x;
+  ArgMax best{-INFINITY, 0x7fffffff};
+  for (int t = threadIdx.x; t < ranks * chunks; t += blockDim.x) {
+    const int32_t* row = packed + (static_cast<int64_t>(t / chunks) * B + r) * ld;
+    best = better(best, ArgMax{__int_as_float(row[t % chunks]), row[chunks + t % chunks]});
+  }
+  best = block_argmax(best);
+  if (threadIdx.x == 0) out[r] = best.i == 0x7fffffff ? 0 : best.i;
+  if (r == 0 && step != nullptr && temps != nullptr) {
+    int any = 0;
+    for (int i = threadIdx.x; i < B; i += blockDim.x) any |= temps[i] > 0.f;
+    if (__syncthreads_or(any) && threadIdx.x == 0) *step += 1;
   }
 }
 
@@ -284,8 +308,23 @@ void launch_sample_split(const SampleArgs& a, float* part_val, int32_t* part_idx
   if (a.top_k != nullptr || a.top_p != nullptr)
     throw std::runtime_error("minisgl.sample: split rows take greedy / temperature sampling only");
   const int nchunks = sample_split_chunks(a.V);
-  launch_pdl(sample_part_kernel, dim3(nchunks, a.B), dim3(kPartThreads), 0, s, a, part_val, part_idx, nchunks);
+  launch_pdl(sample_part_kernel, dim3(nchunks, a.B), dim3(kPartThreads), 0, s, a, part_val, part_idx, nchunks,
+             nchunks);
   launch_lm_sample_reduce(a.out, part_val, part_idx, nchunks, a.B, a.temperature, const_cast<int64_t*>(a.step), s);
+}
+
+void launch_sample_shard_partials(const SampleArgs& a, int32_t* packed, int ld, cudaStream_t s) {
+  if (a.B <= 0) return;
+  const int nchunks = sample_split_chunks(a.V);
+  if (ld < 2 * nchunks) throw std::runtime_error("minisgl.sample_shard: packed row too short");
+  launch_pdl(sample_part_kernel, dim3(nchunks, a.B), dim3(kPartThreads), 0, s, a,
+             reinterpret_cast<float*>(packed), packed + nchunks, nchunks, ld);
+}
+
+void launch_sample_shard_reduce(int32_t* out, const int32_t* packed, int chunks, int ld, int ranks, int B,
+                                const float* temps, int64_t* step, cudaStream_t s) {
+  if (B <= 0) return;
+  launch_pdl(shard_sample_reduce_kernel, dim3(B), dim3(256), 0, s, out, packed, chunks, ld, ranks, B, temps, step);
 }
 
 void launch_sample(const SampleArgs& a, cudaStream_t s) {

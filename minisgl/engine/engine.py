@@ -20,6 +20,7 @@ import torch
 
 from minisgl.env import ENV
 
+from minisgl import ops
 from minisgl.attention import create_attention_backend
 from minisgl.core import FusedSample, Batch, Context, Req, reset_global_ctx, set_global_ctx
 from minisgl.kvcache import create_kvcache_pool
@@ -27,8 +28,8 @@ from minisgl.layers import set_rope_device
 from minisgl.utils import fault
 from minisgl.models import create_model, load_weight, random_weights
 from minisgl.moe import create_moe_backend
-from minisgl.parallel import (destroy_distributed, get_tp_info, reset_cp_info, reset_dp_info, reset_tp_info, set_cp_info,
-                              set_dp_info, set_tp_info)
+from minisgl.parallel import (DistributedCommunicator, destroy_distributed, get_tp_info, reset_cp_info, reset_dp_info,
+                              reset_tp_info, set_cp_info, set_dp_info, set_tp_info)
 from minisgl.utils import align_ceil, init_logger, torch_dtype
 
 from .config import EngineConfig
@@ -159,6 +160,14 @@ class Engine:
                 config.moe_backend, ep_dispatch=self.dp, ep_size=mcfg.ep_size, ep_rank=mcfg.ep_rank,
                 group=self.tp_cpu_group if not self.is_cuda else None, heap=self._ep_heap)
         self.sampler = Sampler(self.device, mcfg.vocab_size, config.weight_seed)
+        # tensor parallelism on GPUs: sample from each rank's vocabulary shard
+        # of the logits instead of gathering [B, V] fp32 logits every step
+        self._lm_head_local = None
+        head = getattr(self.model, "lm_head", None)
+        if (self.is_cuda and config.tp_info.size > 1 and not self.dp and config.cp_size <= 1
+                and head is not None and hasattr(head, "local_logits")):
+            head.local_logits = True
+            self._lm_head_local = head
         if self.is_cuda:
             from minisgl import ops
 
@@ -346,7 +355,12 @@ class Engine:
                 logits = self.model.forward()
         for r in batch.reqs:
             r.complete_one()
-        next_gpu = tokens[: batch.size] if tokens is not None else self.sampler.sample(logits[: batch.size], args)
+        if tokens is not None:
+            next_gpu = tokens[: batch.size]
+        elif self._lm_head_local is not None:
+            next_gpu = self._sample_shards(logits[: batch.size], args)
+        else:
+            next_gpu = self.sampler.sample(logits[: batch.size], args)
         if not self.is_cuda:
             return ForwardOutput(next_gpu, next_gpu, _Done())
         next_cpu = torch.empty(next_gpu.shape, dtype=next_gpu.dtype, pin_memory=True)
@@ -354,6 +368,17 @@ class Engine:
         event = torch.cuda.Event()
         event.record(self.stream)
         return ForwardOutput(next_gpu, next_cpu, event)
+
+    def _sample_shards(self, logits: torch.Tensor, args: BatchSamplingArgs) -> torch.Tensor:
+        """Tokens from this rank's vocabulary shard of the logits: greedy and
+        temperature batches sample from the shards (only per-chunk winners
+        cross the ranks); top-k / top-p batches gather the whole rows first."""
+        head = self._lm_head_local
+        if args.top_k is None and args.top_p is None:
+            lo, n = head.vocab_range
+            return ops.sample_sharded(logits[:, :n], args.temperatures, self.sampler.seed, self.sampler.step, lo,
+                                      DistributedCommunicator.plugins[-1])
+        return self.sampler.sample(head.gather_logits(logits), args)
 
     def shutdown(self) -> None:
         self.graph_runner.destroy_cuda_graphs()

@@ -40,12 +40,18 @@ class VocabParallelEmbedding(BaseOP):
 
 
 class ParallelLMHead(VocabParallelEmbedding):
+    """``local_logits`` (set by the engine under tensor parallelism on GPUs):
+    ``forward`` returns this rank's vocabulary shard of the logits; the
+    engine samples from the shards (``ops.sample_sharded``) or, for top-k /
+    top-p batches, gathers them with ``gather_logits``."""
+
     def __init__(self, num_embeddings: int, embedding_dim: int, bias: bool = False, tie_word_embeddings: bool = False,
                  tied_embedding: Optional[VocabParallelEmbedding] = None) -> None:
         super().__init__(num_embeddings, embedding_dim)
         assert (tied_embedding is not None) == tie_word_embeddings
         self.bias = torch.empty(self.num_embeddings_tp) if bias else None
         self._tied = tied_embedding
+        self.local_logits = False
         if tied_embedding is not None:
             del self.weight  # the embedding table is the projection
 
@@ -74,9 +80,13 @@ class ParallelLMHead(VocabParallelEmbedding):
             return ops.lm_head_sample(x, w, self.bias.to(w.dtype) if self.bias is not None else None,
                                       fs.temperatures, fs.seed, fs.step, out=fs.out)
         logits = ops.gemm(x, w, self.bias.to(w.dtype) if self.bias is not None else None, out_dtype=torch.float32)
-        if self.tp_size == 1:
+        if self.tp_size == 1 or self.local_logits:
             return logits
-        gathered = self._comm.all_gather(logits)  # [tp * rows, V_tp]
+        return self.gather_logits(logits)
+
+    def gather_logits(self, logits: torch.Tensor) -> torch.Tensor:
+        """[rows, V] from every rank's [rows, V_tp] shard."""
+        gathered = self._comm.all_gather(logits.contiguous())  # [tp * rows, V_tp]
         rows = logits.shape[0]
         full = gathered.view(self.tp_size, rows, -1).permute(1, 0, 2).reshape(rows, -1)
         return full[:, : self.num_embeddings]

@@ -132,10 +132,35 @@ def gemm(
     _count()
     if plan is None:
         native().gemm(out, x, w, bias, None, 0, 0, error_word(x.device))
+    elif plan[0] == GEMM_STREAMK:
+        _, r, kps = plan
+        native().gemm(out, x, w, bias, streamk_workspace(x.device), 0, GEMM_STREAMK, error_word(x.device), r,
+                      None, kps)
     else:
         mode, bn, splits = plan
         native().gemm(out, x, w, bias, None, splits, mode, error_word(x.device), bn)
     return out
+
+
+# tile-plan mode of the stream-K weight-streaming GEMM (up to 256 tokens,
+# K % 64 == 0); its plan is (GEMM_STREAMK, weight sub-tiles R, k-blocks per stage)
+GEMM_STREAMK = 4
+_SK_WORKSPACE: dict = {}
+_SK_SLOT_FLOATS = 2 * 256 * 128
+
+
+def streamk_workspace(device: torch.device) -> torch.Tensor:
+    """Per (device, stream) scratch of the stream-K GEMM: one fp32 partial
+    tile per SM, then one int32 ready flag per SM (zero between launches).
+    Kernels on one stream never overlap on it; each stream gets its own."""
+    stream = torch.cuda.current_stream(device)
+    key = (device.index, stream.cuda_stream)
+    ws = _SK_WORKSPACE.get(key)
+    if ws is None:
+        sms = torch.cuda.get_device_properties(device).multi_processor_count
+        ws = torch.zeros(sms * (_SK_SLOT_FLOATS + 1), dtype=torch.float32, device=device)
+        _SK_WORKSPACE[key] = ws
+    return ws
 
 
 # ------------------------------------------------------------ elementwise
@@ -572,6 +597,28 @@ def sample(
 
 
 _SAMPLE_PARTS: dict = {}
+
+
+def sample_sharded(logits: torch.Tensor, temperature: Optional[torch.Tensor], seed: int, step: torch.Tensor,
+                   offset: int, comm) -> torch.Tensor:
+    """Tokens from vocabulary-sharded logits under tensor parallelism: each
+    rank reduces its shard [B, V_shard] (global indices from ``offset``) to
+    per-chunk (best score, index) pairs, the pairs of every rank are gathered
+    (``comm.all_gather``, a few KB instead of the [B, V] logits) and one small
+    kernel picks each row's token. Scores are those of ``sample`` / ``argmax``
+    over the whole vocabulary (same counter-based Gumbel stream, same tie
+    rule), so every rank draws the same tokens as an unsharded sampler would.
+    ``temperature`` None: greedy."""
+    B = logits.shape[0]
+    chunks = native().sample_shard_chunks(logits.shape[1])
+    ld = (2 * chunks + 3) // 4 * 4  # rows of whole 16-byte vectors for the gather
+    packed = torch.empty(B, ld, dtype=torch.int32, device=logits.device)
+    out = torch.empty(B, dtype=torch.int32, device=logits.device)
+    _count(2)
+    native().sample_shard_partials(packed, logits, temperature, seed, step, offset)
+    gathered = comm.all_gather(packed)
+    native().sample_shard_reduce(out, gathered, chunks, gathered.shape[0] // max(B, 1), temperature, step)
+    return out
 
 
 def lm_head_sample(

@@ -59,7 +59,23 @@ def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
         # persistent 128 x N-tile CTAs: win on wide outputs such as the LM
         # head (151936 features at 256 rows: 0.106 vs 0.138 ms)
         out += [(3, 256, 1), (3, 128, 1)]
+    if M <= 256 and K % 64 == 0:
+        # stream-K weight streaming over every SM, 128 or 256 weight rows per
+        # work tile (mode 4: (4, R, k-blocks per stage; 0 = automatic))
+        out += [(4, 1, 0), (4, 2, 0)]
     return out
+
+
+def run_plan(out: torch.Tensor, x: torch.Tensor, w: torch.Tensor, plan: Plan) -> None:
+    """One plain GEMM launch with a forced plan (the stream-K mode takes its
+    per-stream workspace)."""
+    from minisgl import ops
+
+    mode, bn, s = plan
+    if mode == ops.GEMM_STREAMK:
+        ops.native().gemm(out, x, w, None, ops.streamk_workspace(x.device), 0, mode, None, bn, None, s)
+    else:
+        ops.native().gemm(out, x, w, None, None, s, mode, None, bn)
 
 
 # bytes of weight copies cycled through while timing: above the 126 MB L2, so
@@ -150,7 +166,7 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
 
     native = ops.native()
     fused = dict(fused or {})
-    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only|sample"
+    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only|sample|streamk"
     cached = _load(cache_file, key_dev)
     shapes = sorted(set(shapes) | set(fused))
     wanted = sorted(set(int(m) for m in batch_sizes if m > 0))
@@ -172,10 +188,8 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
                 else:
                     timed = []
                     for plan in candidates(M, K, full=False):
-                        mode, bn, s = plan
                         try:
-                            timed.append((_time_runs(lambda w_, m=mode, b=bn, sp=s: native.gemm(
-                                out, x, w_, None, None, sp, m, None, b), ws), plan))
+                            timed.append((_time_runs(lambda w_, p_=plan: run_plan(out, x, w_, p_), ws), plan))
                         except RuntimeError:
                             continue
                     if timed:

@@ -26,6 +26,7 @@ SOURCES = [
     "minisgl/csrc/radix.cpp",
     "minisgl/csrc/gemm.cu",
     "minisgl/csrc/gemm_persistent.cu",
+    "minisgl/csrc/gemm_streamk.cu",
     "minisgl/csrc/attention.cu",
     "minisgl/csrc/elementwise.cu",
     "minisgl/csrc/rope_store.cu",

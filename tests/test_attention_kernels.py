@@ -162,3 +162,43 @@ def test_moe_route_grouped():
     w, ids = ops.moe_route(x, k, "sigmoid", True, bias, 8, 4, 2.5)
     w2, ids2 = ref.moe_route(x.cpu(), k, "sigmoid", True, bias.cpu(), 8, 4, 2.5)
     assert torch.equal(ids.cpu().sort(-1).values, ids2.sort(-1).values)
+
+
+class _ConcatGather:
+    """Stands in for a tensor-parallel communicator: the 'ranks' are the
+    shards of one process, gathered by concatenation in rank order."""
+
+    def __init__(self, parts):
+        self.parts = parts
+
+    def all_gather(self, x):
+        return torch.cat(self.parts, 0)
+
+
+@pytest.mark.parametrize("ranks,V", [(2, 151936), (8, 151936), (3, 1000)])
+@pytest.mark.parametrize("greedy", [True, False])
+def test_sample_sharded_matches_whole_vocabulary(ranks, V, greedy):
+    """Sampling from vocabulary shards (tensor parallelism) draws the tokens
+    the whole-vocabulary sampler draws for the same seed and step, and
+    advances the step counter the same way."""
+    B = 37
+    x = torch.randn(B, V, device=DEV) * 2
+    t = None if greedy else torch.full((B,), 0.7, device=DEV)
+    step_full = torch.full((), 5, dtype=torch.int64, device=DEV)
+    step_shard = step_full.clone()
+    want = ops.argmax(x) if greedy else ops.sample(x, t, seed=99, step=step_full)
+    per = -(-V // ranks)
+    nat = ops.native()
+    chunks = nat.sample_shard_chunks(per)
+    ld = (2 * chunks + 3) // 4 * 4
+    parts = []
+    for r in range(ranks):
+        lo, hi = r * per, min(V, (r + 1) * per)
+        packed = torch.zeros(B, ld, dtype=torch.int32, device=DEV)
+        nat.sample_shard_partials(packed, x[:, lo:hi], t, 99, step_shard, lo)
+        parts.append(packed)
+    got = torch.empty(B, dtype=torch.int32, device=DEV)
+    nat.sample_shard_reduce(got, _ConcatGather(parts).all_gather(None), chunks, ranks, t, step_shard)
+    torch.cuda.synchronize()
+    assert torch.equal(got.cpu(), want.cpu())
+    assert int(step_shard) == int(step_full)

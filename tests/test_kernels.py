@@ -77,14 +77,45 @@ def test_gemm_every_plan(M, N, K):
     x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
     w = (torch.randn(N, K, device=DEV) * 0.05).to(torch.bfloat16)
     expect = ref.gemm(x, w, None, torch.float32).cpu()
-    from minisgl.ops.gemm_tune import candidates
+    from minisgl.ops.gemm_tune import candidates, run_plan
 
     for mode, bn, s in candidates(M, K):
         out = torch.zeros(M, N, device=DEV, dtype=torch.float32)
-        ops.native().gemm(out, x, w, None, None, s, mode, None, bn)
+        run_plan(out, x, w, (mode, bn, s))
         torch.cuda.synchronize()
         err = (out.cpu() - expect).abs().max().item()
         assert err < 3e-2 * (K / 1024) ** 0.5 + 1e-2, (mode, bn, s, err)
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 1280, 5120), (5, 1000, 1024), (16, 5120, 3200), (33, 640, 64),
+                                   (100, 6400, 5120), (256, 5120, 3200), (256, 1536, 25600)])
+@pytest.mark.parametrize("R", [1, 2])
+def test_gemm_streamk(M, N, K, R):
+    """Stream-K weight streaming (plan mode 4): split tiles are summed from
+    the per-CTA partials in a fixed order, so two launches give identical
+    bits, and the ready flags are reset for the next launch."""
+    torch.manual_seed(M * 7 + N + R)
+    big = torch.randn(M, K + 64, device=DEV, dtype=torch.bfloat16)
+    x = big[:, 64:]  # row stride K + 64
+    w = (torch.randn(N, K, device=DEV) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, device=DEV) * 0.1).to(torch.bfloat16)
+    ws = ops.streamk_workspace(x.device)
+    err = ops.error_word(x.device)
+    outs = []
+    for f32 in (False, True, True):
+        out = torch.full((M, N), float("nan"), device=DEV, dtype=torch.float32 if f32 else torch.bfloat16)
+        ops.native().gemm(out, x, w, b, ws, 0, ops.GEMM_STREAMK, err, R, None, 0)
+        outs.append(out)
+    torch.cuda.synchronize()
+    ops.check_device_errors(x.device)
+    expect = ref.gemm(x, w, b, torch.float32)
+    tol = 2e-2 * math.sqrt(K / 1024) + 1e-2
+    _close(outs[0], expect, atol=tol, rtol=1e-2)
+    _close(outs[1], expect, atol=tol, rtol=1e-2)
+    assert torch.equal(outs[1], outs[2])
+    sms = torch.cuda.get_device_properties(x.device).multi_processor_count
+    flags = ws[-sms:].view(torch.int32)
+    assert int(flags.abs().sum()) == 0
 
 
 @pytest.mark.parametrize("M,N,K,bn", [(4096, 6144, 1024, 256), (3000, 1000, 576, 256), (129, 4096, 2048, 128),
