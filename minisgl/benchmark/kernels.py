@@ -423,10 +423,10 @@ def probe_plan(M: int, N: int, K: int, mode: int, bn: int, splits: int, kps: int
     out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
     nat = ops.native()
 
-    ws = ops.streamk_workspace(x.device) if mode == ops.GEMM_STREAMK else None
+    scratch = ops.streamk_workspace(x.device) if mode == ops.GEMM_STREAMK else None
 
     def run(w, tr=None):
-        nat.gemm(out, x, w, None, ws, splits, mode, None, bn, tr, kps)
+        nat.gemm(out, x, w, None, scratch, splits, mode, None, bn, tr, kps)
 
     for i in range(8):
         run(ws[i % 8])
@@ -440,8 +440,11 @@ def probe_plan(M: int, N: int, K: int, mode: int, bn: int, splits: int, kps: int
     row: Dict = {"M": M, "N": N, "K": K, "plan": [mode, bn, splits], "kps": kps,
                  "us_per_launch": round(s.elapsed_time(e) / iters * 1000, 2)}
     if trace:
+        # stamps of the last of 16 back-to-back launches (each launch
+        # overwrites the buffer), so the overlap with its predecessor shows
         tr = torch.zeros(1 << 16, dtype=torch.int64, device="cuda")
-        run(ws[3], tr)
+        for i in range(16):
+            run(ws[i % 8], tr)
         torch.cuda.synchronize()
         t = tr.view(-1, 8).cpu()
         t = t[t[:, 0] > 0].double()

@@ -14,6 +14,14 @@ every rank, as the engine does), cycling over ``--layers`` weight copies
   grid does not fit on the GPU);
 * ``gemm_then_nvlink``: the tuned plain GEMM writing into the symmetric heap,
   then the NVLink all-reduce kernel with the residual add;
+* ``sp_nccl``: the sequence-parallel step as library collectives: GEMM,
+  NCCL all-reduce, fused residual add + RMSNorm (the reference's o_proj /
+  down_proj followed by its next fused_add_rmsnorm);
+* ``sp``: the same step on the token-sharded residual stream: the tuned
+  GEMM into the symmetric heap, then one NVLink kernel that reduce-scatters
+  into this rank's residual rows, RMS-normalises them and all-gathers the
+  normalised rows (``SymmMemImpl.rs_norm_ag``); ``sp_frac_roofline`` is its
+  fraction of the roofline below;
 * ``roofline``: the slowest of the GEMM at the measured bf16 peak, the
   weight bytes at the measured HBM copy bandwidth, and the bytes an
   all-reduce must move per GPU over NVLink (2 (N - 1) / N of the output) at
@@ -84,7 +92,7 @@ def main() -> None:
     dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     from minisgl.parallel.symm import SymmMemImpl
 
-    impl = SymmMemImpl(dev, 256 * 5120 * 2)
+    impl = SymmMemImpl(dev, (256 + world) * 5120 * 2)
     tflops, hbm = _peaks()
     H = 5120
     from minisgl.ops import gemm_tune
@@ -120,9 +128,26 @@ def main() -> None:
                 ops.gemm(x, ws[i % len(ws)], out=part)
                 impl.reduce_into(part, res)
 
+            rows = -(-M // world)
+            sp_part = impl.sp_partial(rows * world, H, torch.bfloat16, dev)
+            r_slice = torch.randn(rows, H, device=dev, dtype=torch.bfloat16)
+            norm_w = torch.ones(H, device=dev, dtype=torch.bfloat16)
+            h = torch.empty(M, H, device=dev, dtype=torch.bfloat16)
+
+            def sp(i=0):
+                ops.gemm(x, ws[i % len(ws)], out=sp_part[:M])
+                impl.rs_norm_ag(sp_part, r_slice, True, norm_w, 1e-6)
+
+            def sp_nccl(i=0):
+                ops.gemm(x, ws[i % len(ws)], out=h)
+                dist.all_reduce(h)
+                ops.fused_add_rmsnorm(h, res, norm_w, 1e-6)
+
             t_nccl = _time(nccl, args.layers)
             t_fused = _time(fused, args.layers)
             t_two = _time(two_kernel, args.layers)
+            t_sp = _time(sp, args.layers)
+            t_sp_nccl = _time(sp_nccl, args.layers)
             flops = 2.0 * M * K * H
             link_bytes = (world - 1) / max(world, 1) * M * H * 2 * (2 if world > 1 else 0)
             bound = max(flops / (tflops * 1e9), link_bytes / (LINK_GBS * 1e6), H * K * 2 / (hbm * 1e6))
@@ -131,8 +156,10 @@ def main() -> None:
                                   "plan": gemm_tune.FUSED_PLANS.get((M, H, K)),
                                   "nccl_us": round(t_nccl * 1000, 2), "fused_us": round(t_fused * 1000, 2),
                                   "gemm_then_nvlink_us": round(t_two * 1000, 2),
+                                  "sp_nccl_us": round(t_sp_nccl * 1000, 2), "sp_us": round(t_sp * 1000, 2),
                                   "roofline_us": round(bound * 1000, 2),
-                                  "fused_frac_roofline": round(bound / t_fused, 3)}), flush=True)
+                                  "fused_frac_roofline": round(bound / t_fused, 3),
+                                  "sp_frac_roofline": round(bound / t_sp, 3)}), flush=True)
     impl.shutdown()
     dist.destroy_process_group()
 

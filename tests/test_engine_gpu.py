@@ -1,7 +1,9 @@
 """The engine on a B200: native kernels end to end, checked against the
 dense fp32 oracle with teacher forcing (bf16 vs fp32 may flip near-ties, so
 each generated token must be the oracle's argmax or within a small logit
-margin of it), and CUDA-graph decode identical to eager decode."""
+margin of it) - both on the engine's own folded weights and on the original
+checkpoint before the norm weights are folded into the projections - and
+CUDA-graph decode identical to eager decode."""
 
 import random
 
@@ -45,7 +47,43 @@ def test_gpu_engine_tracks_oracle():
             logits = dense_logits(state, cfg, p + toks[:-1],
                                   fused_layout=llm.engine.model.fused_layout)[len(p) - 1 :]
             for t, row in zip(toks, logits):
-                assert row[t] >= row.max() - 0.05 * row.abs().max(), (t, int(row.argmax()))
+                assert row[t] >= row.max() - 0.03 * row.abs().max(), (t, int(row.argmax()))
+    finally:
+        llm.shutdown()
+
+
+def test_gpu_engine_tracks_unfolded_checkpoint(tmp_path):
+    """A bf16 checkpoint with non-unit norm weights, loaded from disk: the
+    engine folds the norm weights into the qkv / gate_up projections (in
+    bf16); its tokens are checked against the fp32 oracle run on the
+    checkpoint as written, so the error of the folding is inside the check."""
+    import os
+
+    from minisgl.models.weight import load_weight
+    from minisgl.utils.synthetic import write_random_checkpoint
+
+    folder = os.path.join(str(tmp_path), "m")
+    make_model_dir("small-qwen3", folder=folder)
+    write_random_checkpoint(folder, seed=11, std=0.05, norm_std=0.3)
+    llm = LLM(folder, dtype=torch.bfloat16, device="cuda:0", use_dummy_weight=False, page_size=64,
+              max_running_req=16, max_seq_len_override=2048, num_page_override=256, cuda_graph_max_bs=16,
+              max_extend_tokens=256)
+    try:
+        assert llm.engine.model.fused_layout
+        prompts = _prompts(6, seed=2)
+        outs = llm.generate(prompts, SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True))
+        ops.check_device_errors(torch.device("cuda:0"))
+        state = {k: v.float() for k, v in load_weight(folder, torch.device("cpu"))}
+        cfg = llm.engine.model_config
+        exact = total = 0
+        for p, o in zip(prompts, outs):
+            toks = o["token_ids"]
+            logits = dense_logits(state, cfg, p + toks[:-1], fused_layout=False)[len(p) - 1 :]
+            for t, row in zip(toks, logits):
+                assert row[t] >= row.max() - 0.03 * row.abs().max(), (t, int(row.argmax()))
+                exact += int(t == int(row.argmax()))
+                total += 1
+        assert exact >= 0.8 * total, (exact, total)
     finally:
         llm.shutdown()
 
@@ -107,4 +145,4 @@ def test_fused_sampling_matches_logits_path():
     a, b = outs[True][1], outs[False][1]
     assert [x[0] for x in a] == [y[0] for y in b]
     same = sum(p == q for x, y in zip(a, b) for p, q in zip(x, y))
-    assert same >= 0.75 * sum(len(x) for x in a)
+    assert same >= 0.9 * sum(len(x) for x in a)
