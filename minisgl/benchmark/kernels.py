@@ -466,8 +466,59 @@ def probe_plan(M: int, N: int, K: int, mode: int, bn: int, splits: int, kps: int
     return row
 
 
+def probe_launch_modes(M: int, N: int, K: int, mode: int, bn: int, splits: int, kps: int = 0) -> Dict:
+    """Microseconds per launch of one forced plan, launched eagerly and
+    from a CUDA graph (one weight, and 8 weight copies cycled beyond L2), and
+    the device error word afterwards: separates host launch cost, kernel time
+    and inter-launch effects."""
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    ws = [torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02 for _ in range(8)]
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    nat = ops.native()
+    scratch = ops.streamk_workspace(x.device) if mode == ops.GEMM_STREAMK else None
+    err = ops.error_word(x.device)
+
+    def run(w):
+        nat.gemm(out, x, w, None, scratch, splits, mode, err, bn, None, kps)
+
+    def eager(n=40):
+        for i in range(8):
+            run(ws[i % 8])
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        for i in range(n):
+            run(ws[i % 8])
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n * 1000
+
+    def graph(copies, n=40):
+        g = torch.cuda.CUDAGraph()
+        run(ws[0])
+        torch.cuda.synchronize()
+        with torch.cuda.graph(g):
+            for i in range(n):
+                run(ws[i % copies])
+        g.replay()
+        torch.cuda.synchronize()
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        g.replay()
+        e.record()
+        torch.cuda.synchronize()
+        del g
+        return s.elapsed_time(e) / n * 1000
+
+    row = {"M": M, "N": N, "K": K, "plan": [mode, bn, splits], "eager_us": round(eager(), 2),
+           "graph_1copy_us": round(graph(1), 2), "graph_8copies_us": round(graph(8), 2)}
+    row["error_word"] = err.tolist()
+    return row
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
+    p.add_argument("--launch-modes", default="", help="M,N,K,mode,bn,splits[,kps]: eager vs graph launch timing")
     p.add_argument("--probe", default="", help="M,N,K,mode,bn,splits[,kps]: time one forced GEMM tile plan")
     p.add_argument("--trace", action="store_true", help="with --probe: per-CTA phase stamps")
     p.add_argument("--json", default="")
@@ -475,6 +526,10 @@ def main() -> None:
     p.add_argument("--only", default="", help="run only cases whose label contains this text")
     p.add_argument("--trace-prefill", action="store_true", help="print the prefill attention phase trace and exit")
     args = p.parse_args()
+    if args.launch_modes:
+        vals = [int(v) for v in args.launch_modes.split(",")]
+        print(json.dumps(probe_launch_modes(*vals[:7])), flush=True)
+        return
     if args.probe:
         vals = [int(v) for v in args.probe.split(",")]
         print(json.dumps(probe_plan(*vals[:7], trace=args.trace)), flush=True)

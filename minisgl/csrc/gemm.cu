@@ -999,7 +999,7 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    if (a.workspace == nullptr || a.workspace_elems < static_cast<int64_t>(sms) * (kStreamKSlotFloats + 1))
+    if (a.workspace == nullptr || a.workspace_elems < static_cast<int64_t>(sms) * (kStreamKSlotFloats + kStreamKFlagWords))
       throw std::runtime_error("minisgl.gemm: the stream-K plan needs its workspace");
     GemmStreamKArgs k{};
     k.x = a.x;

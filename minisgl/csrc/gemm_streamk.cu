@@ -36,6 +36,7 @@
 // launch). Workspace and flags are only touched after griddepcontrol.wait, so
 // back-to-back launches on one stream never overlap on them.
 #include <algorithm>
+#include <cstdlib>
 #include <stdexcept>
 #include <string>
 
@@ -48,6 +49,7 @@ namespace minisgl {
 namespace {
 
 constexpr int kSkThreads = 192;
+constexpr int kFlagStride = 32;  // int32 words between ready flags (one 128-byte line each)
 constexpr int kSkSmemBudget = 200 * 1024;  // stage ring bytes
 
 struct SkParams {
@@ -62,12 +64,15 @@ struct SkParams {
   int stages;
   int grid;       // CTAs (= workspace slots)
   float* ws;      // [grid][R * BN * 128] fp32 partial tiles
-  int* flags;     // [grid] ready flags (0 between launches)
+  int* flags;     // [grid * kFlagStride] ready flags (0 between launches)
   ErrorSink err;
   // optional per-CTA %globaltimer stamps, 8 slots per CTA: 0 entry, 1 set-up
   // done, 2 producer past griddepcontrol.wait, 3 first accumulator ready,
   // 4 last accumulator ready, 5 owner's contributors ready, 6 epilogue done
   unsigned long long* trace;
+  // measurement switches (MINISGL_STREAMK_DEBUG): 1 skip global stores,
+  // 2 skip the MMAs, 4 skip the x loads, 8 skip the weight loads
+  int dbg;
 };
 
 __device__ __forceinline__ void sk_stamp(const SkParams& p, int slot) {
@@ -185,26 +190,30 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     for (StageCursor c2 = cur; c2.valid(); c2.next()) ++total;
     const int pre = min(total, stages);
     StageCursor c1 = cur;
+    const bool do_x = (p.dbg & 4) == 0, do_w = (p.dbg & 8) == 0;
+    const uint32_t tx_bytes = (do_w ? stA : 0u) + (do_x ? stB : 0u);
     for (int it = 0; it < pre; ++it, c1.next()) {
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[it], stage_bytes);
-        tma_load_3d(sA + it * stA, &tmW, &full[it], 0, c1.tile * 128 * R, c1.kb);
+        if (tx_bytes > 0) mbar_arrive_expect_tx(&full[it], tx_bytes);
+        else mbar_arrive(&full[it]);
+        if (do_w) tma_load_3d(sA + it * stA, &tmW, &full[it], 0, c1.tile * 128 * R, c1.kb);
       }
     }
     pdl_wait();
     if (lane == 0) sk_stamp(p, 2);
     c1 = cur;
     for (int it = 0; it < pre; ++it, c1.next())
-      if (lane == 0) tma_load_3d(sB + it * stB, &tmX, &full[it], 0, 0, c1.kb);
+      if (lane == 0 && do_x) tma_load_3d(sB + it * stB, &tmX, &full[it], 0, 0, c1.kb);
     __syncwarp();
     for (int it = pre; it < total; ++it, c1.next()) {
       const int s = it % stages;
       const uint32_t ph = (it / stages) & 1u;
       if (!__all_sync(0xffffffffu, mbar_wait(&empty[s], ph ^ 1u, p.err, 401))) break;
       if (lane == 0) {
-        mbar_arrive_expect_tx(&full[s], stage_bytes);
-        tma_load_3d(sA + s * stA, &tmW, &full[s], 0, c1.tile * 128 * R, c1.kb);
-        tma_load_3d(sB + s * stB, &tmX, &full[s], 0, 0, c1.kb);
+        if (tx_bytes > 0) mbar_arrive_expect_tx(&full[s], tx_bytes);
+        else mbar_arrive(&full[s]);
+        if (do_w) tma_load_3d(sA + s * stA, &tmW, &full[s], 0, c1.tile * 128 * R, c1.kb);
+        if (do_x) tma_load_3d(sB + s * stB, &tmX, &full[s], 0, 0, c1.kb);
       }
       __syncwarp();
     }
@@ -232,7 +241,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         }
         tc_fence_after();
         if (lane == 0) {
-          const int nj = min(kps, nkb - i * kps);
+          const int nj = (p.dbg & 2) ? 0 : min(kps, nkb - i * kps);
           for (int j = 0; j < nj; ++j) {
 #pragma unroll
             for (int r = 0; r < R; ++r) {
@@ -290,30 +299,42 @@ __global__ void __launch_bounds__(kSkThreads, 1)
               tmem_ld_32x32b_x32(taddr + r * BN + c, v);
             }
             tc_wait_ld();
+            if ((p.dbg & 1) == 0) {
 #pragma unroll
-            for (int j = 0; j < (BN < 32 ? BN : 32); ++j)
-              slot[(static_cast<size_t>(r) * BN + c + j) * 128 + row] = ok ? __uint_as_float(v[j]) : 0.f;
+              for (int j = 0; j < (BN < 32 ? BN : 32); ++j)
+                slot[(static_cast<size_t>(r) * BN + c + j) * 128 + row] = ok ? __uint_as_float(v[j]) : 0.f;
+            }
           }
         }
-        __threadfence();
+        // every epilogue thread's partial is written; one thread publishes
+        // them (the barrier orders the other threads' stores before its
+        // release store, which is cumulative at GPU scope)
         asm volatile("bar.sync 1, 128;" ::: "memory");
-        if (et == 0) st_release_gpu(p.flags + blockIdx.x, 1);
+        if (et == 0) {
+          __threadfence();
+          st_release_gpu(p.flags + static_cast<size_t>(blockIdx.x) * kFlagStride, 1);
+        }
       } else {
         // owner (or a whole tile): contributors are the CTAs that start inside this tile
         int c_last = blockIdx.x;
         if (!whole) {
           while (c_last + 1 < p.grid && unit_start(c_last + 1, units, p.grid) < t_end) ++c_last;
-          // every thread waits on the flags it will read (bounded)
-          for (int c2 = blockIdx.x + 1; c2 <= c_last; ++c2) {
-            const uint64_t t0 = globaltimer_ns();
-            uint32_t spins = 0;
-            while (ld_acquire_gpu(p.flags + c2) == 0) {
-              if (((++spins) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
-                p.err.report(kErrMbarTimeout, 405);
-                break;
+          // one thread polls the contributors' flags (bounded, backing off so
+          // the flag lines are not hammered), then releases the others
+          if (et == 0) {
+            for (int c2 = blockIdx.x + 1; c2 <= c_last; ++c2) {
+              const uint64_t t0 = globaltimer_ns();
+              uint32_t spins = 0;
+              while (ld_acquire_gpu(p.flags + static_cast<size_t>(c2) * kFlagStride) == 0) {
+                __nanosleep(64);
+                if (((++spins) & 0xFFu) == 0 && globaltimer_ns() - t0 > kWaitBudgetNs) {
+                  p.err.report(kErrMbarTimeout, 405);
+                  break;
+                }
               }
             }
           }
+          asm volatile("bar.sync 1, 128;" ::: "memory");
         }
         if (et == 0) sk_stamp(p, 5);
         const int tok_step = BN < 32 ? BN : 32;
@@ -342,7 +363,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
               for (int j = 0; j < 32; ++j)
                 if (j < tok_step) acc[j] += slot[(static_cast<size_t>(r) * BN + c + j) * 128 + row];
             }
-            if (f < p.N) {
+            if (f < p.N && (p.dbg & 1) == 0) {
 #pragma unroll
               for (int j = 0; j < 32; ++j) {
                 const int m = c + j;
@@ -357,8 +378,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         }
         if (!whole) {
           asm volatile("bar.sync 1, 128;" ::: "memory");
-          if (et == 0)
-            for (int c2 = blockIdx.x + 1; c2 <= c_last; ++c2) p.flags[c2] = 0;  // ready for the next launch
+          if (et == 0)  // ready for the next launch
+            for (int c2 = blockIdx.x + 1; c2 <= c_last; ++c2) p.flags[static_cast<size_t>(c2) * kFlagStride] = 0;
         }
       }
       tc_fence_before();
@@ -419,8 +440,14 @@ void dispatch_bn(int bn, const GemmStreamKArgs& a, const SkParams& p, cudaStream
 int gemm_streamk_grid(int M, int N, int K, int R, int sms) {
   const int tiles = (N + 128 * R - 1) / (128 * R);
   const int64_t units = static_cast<int64_t>(tiles) * (K / 64);
+  // MINISGL_STREAMK_CTAS caps the grid (measurement switch)
+  static const int cap = [] {
+    const char* v = std::getenv("MINISGL_STREAMK_CTAS");
+    return v != nullptr && v[0] != '\0' ? std::atoi(v) : 0;
+  }();
+  const int limit = cap > 0 ? std::min(cap, sms) : sms;
   // at least two k-blocks per CTA
-  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(sms, units / 2)));
+  return static_cast<int>(std::max<int64_t>(1, std::min<int64_t>(limit, units / 2)));
 }
 
 void launch_gemm_streamk(const GemmStreamKArgs& a, cudaStream_t stream) {
@@ -445,6 +472,11 @@ void launch_gemm_streamk(const GemmStreamKArgs& a, cudaStream_t stream) {
   p.flags = a.flags;
   p.err = ErrorSink{a.err};
   p.trace = static_cast<unsigned long long*>(a.trace);
+  static const int dbg = [] {
+    const char* v = std::getenv("MINISGL_STREAMK_DEBUG");
+    return v != nullptr && v[0] != '\0' ? std::atoi(v) : 0;
+  }();
+  p.dbg = dbg;
   if (p.grid < 1 || p.grid > a.ws_slots) throw std::runtime_error("minisgl.gemm_streamk: grid exceeds the workspace");
   if (static_cast<int64_t>(a.R) * bn * 128 > a.ws_slot_floats)
     throw std::runtime_error("minisgl.gemm_streamk: workspace slot too small");

@@ -92,8 +92,9 @@ struct GemmArgs {
 void launch_gemm(const GemmArgs& a, cudaStream_t stream);
 // Stream-K weight-streaming GEMM for up to 256 tokens (gemm_streamk.cu):
 // R = 1 or 2 weight sub-tiles of 128 rows per work tile; ws holds ws_slots
-// fp32 partial tiles of ws_slot_floats each, flags ws_slots int32 (all 0
-// between launches). grid <= ws_slots CTAs (one per SM).
+// fp32 partial tiles of ws_slot_floats each, flags ws_slots * 32 int32 (one
+// flag per 128-byte line, all 0 between launches). grid <= ws_slots CTAs
+// (one per SM).
 struct GemmStreamKArgs {
   const void* x;
   const void* w;
@@ -113,6 +114,7 @@ struct GemmStreamKArgs {
   void* trace;  // optional uint64 [grid * 8] phase stamps
 };
 constexpr int64_t kStreamKSlotFloats = 2 * 256 * 128;  // R = 2, 256 tokens
+constexpr int64_t kStreamKFlagWords = 32;               // per slot
 int gemm_streamk_grid(int M, int N, int K, int R, int sms);
 void launch_gemm_streamk(const GemmStreamKArgs& a, cudaStream_t stream);
 // Persistent 128 x {128, 256} tiles with double-buffered TMEM accumulators

@@ -147,18 +147,20 @@ def gemm(
 GEMM_STREAMK = 4
 _SK_WORKSPACE: dict = {}
 _SK_SLOT_FLOATS = 2 * 256 * 128
+_SK_FLAG_WORDS = 32
 
 
 def streamk_workspace(device: torch.device) -> torch.Tensor:
     """Per (device, stream) scratch of the stream-K GEMM: one fp32 partial
-    tile per SM, then one int32 ready flag per SM (zero between launches).
-    Kernels on one stream never overlap on it; each stream gets its own."""
+    tile per SM, then one int32 ready flag per SM, each on its own 128-byte
+    line (zero between launches). Kernels on one stream never overlap on it;
+    each stream gets its own."""
     stream = torch.cuda.current_stream(device)
     key = (device.index, stream.cuda_stream)
     ws = _SK_WORKSPACE.get(key)
     if ws is None:
         sms = torch.cuda.get_device_properties(device).multi_processor_count
-        ws = torch.zeros(sms * (_SK_SLOT_FLOATS + 1), dtype=torch.float32, device=device)
+        ws = torch.zeros(sms * (_SK_SLOT_FLOATS + _SK_FLAG_WORDS), dtype=torch.float32, device=device)
         _SK_WORKSPACE[key] = ws
     return ws
 

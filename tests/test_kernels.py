@@ -114,7 +114,7 @@ def test_gemm_streamk(M, N, K, R):
     _close(outs[1], expect, atol=tol, rtol=1e-2)
     assert torch.equal(outs[1], outs[2])
     sms = torch.cuda.get_device_properties(x.device).multi_processor_count
-    flags = ws[-sms:].view(torch.int32)
+    flags = ws[-32 * sms:].view(torch.int32)
     assert int(flags.abs().sum()) == 0
 
 
