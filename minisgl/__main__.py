@@ -1,4 +1,11 @@
 from minisgl.server import launch_server
 
-if __name__ == "__main__":
+
+def main() -> None:
+    """Console entry point (``minisgl`` after ``pip install``): same as
+    ``python -m minisgl``."""
     launch_server()
+
+
+if __name__ == "__main__":
+    main()

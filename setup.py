@@ -1,9 +1,10 @@
 """Build script for the minisgl native library (sm_100a only).
 
-    python setup.py build_ext --inplace
+    python setup.py build_ext --inplace      # development: _C*.so next to the sources
+    pip install --no-build-isolation .      # installable package (metadata in pyproject.toml)
 
-produces ``minisgl/_C*.so`` next to the Python sources, so the built library
-travels with a copy of the source tree.
+The in-place build produces ``minisgl/_C*.so`` next to the Python sources,
+so the built library travels with a copy of the source tree.
 """
 
 import os
@@ -60,10 +61,10 @@ def cmdclass():
 if __name__ == "__main__":
     # torch's own arch list must not add other targets: the gencode above is the only one
     os.environ["TORCH_CUDA_ARCH_LIST"] = "10.0a"
+    from setuptools import find_packages
+
     setup(
-        name="minisgl",
-        version="0.1.0",
-        packages=[],
+        packages=find_packages(include=["minisgl", "minisgl.*"]),
         ext_modules=ext_modules(),
         cmdclass=cmdclass(),
     )
