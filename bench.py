@@ -321,6 +321,8 @@ def run_minisgl(args) -> None:
                       counters=lambda: (llm.h2d_bytes, llm.d2h_bytes))
     clocks = sampler.stop() if sampler is not None else {}
     launches = ops.LAUNCHES[0] - launches0
+    if getattr(llm, "profiler", None) is not None and rank == 0:  # MINISGL_PROFILE_STEPS=1: time per phase
+        print(json.dumps({"step_profile": llm.profiler.summary()}), file=sys.stderr, flush=True)
     max_dev_ms, max_wall = reduce_over_ranks([res["dev_ms"], res["wall_s"]], "max")
     tot_launches, = reduce_over_ranks([launches], "sum")
     if rank == 0:

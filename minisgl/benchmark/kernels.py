@@ -23,7 +23,7 @@ import argparse
 import json
 import os
 import random
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import torch
 
@@ -71,8 +71,11 @@ def bench_decode_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) -
                                                   part_o, part_lse, splits))
     nbytes = 2 * B * L * hk * d * 2
     gbs = nbytes / ms / 1e6
+    ms_trt = _trtllm_attention_ms(pool, pt, rows, seq, q, 1, hq, hk, d, page)
     return {"kernel": "decode_attention", "B": B, "L": L, "hq": hq, "hk": hk, "page": page, "splits": splits,
-            "ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
+            "ms": round(ms, 4), "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3),
+            "trtllm_ms": None if ms_trt is None else round(ms_trt, 4),
+            "vs_trtllm": None if ms_trt is None else round(ms_trt / ms, 3)}
 
 
 def bench_decode_attention_varlen(B: int, lo: int, hi: int, hq: int, hk: int, page: int, peaks) -> List[Dict]:
@@ -99,6 +102,38 @@ def bench_decode_attention_varlen(B: int, lo: int, hi: int, hq: int, hk: int, pa
     return out
 
 
+def _trtllm_attention_ms(pool, pt, rows, seq, q, L_q: int, hq: int, hk: int, d: int, page: int) -> Optional[float]:
+    """Milliseconds of the TRT-LLM FMHA kernels that flashinfer ships (the
+    reference's default attention backend on sm100) on the same paged pool
+    (HND pages of this layer) and queries, or None when flashinfer is not
+    importable. Prefill when L_q > 1 (every request has L_q new tokens),
+    decode otherwise. Timed for comparison only; the engine never calls it."""
+    try:
+        from flashinfer.decode import trtllm_batch_decode_with_kv_cache
+        from flashinfer.prefill import trtllm_batch_context_with_kv_cache
+    except Exception:  # noqa: BLE001 - an optional library
+        return None
+    B = rows.numel()
+    kv = (pool[0, 0], pool[1, 0])  # [pages, hk, page, d]
+    blocks = (pt[rows.long(), ::page] // page).to(torch.int32).contiguous()
+    ws = torch.empty(128 << 20, dtype=torch.uint8, device="cuda")
+    qv = q.view(-1, hq, d)
+    max_kv = int(seq.max())
+    try:
+        if L_q > 1:
+            cu_q = torch.arange(0, (B + 1) * L_q, L_q, dtype=torch.int32, device="cuda")
+            cu_kv = torch.cat([torch.zeros(1, dtype=torch.int32, device="cuda"), seq.cumsum(0).to(torch.int32)])
+            fn = lambda: trtllm_batch_context_with_kv_cache(  # noqa: E731
+                qv, kv, ws, blocks, seq, L_q, max_kv, d ** -0.5, 1.0, B, cu_q, cu_kv, kv_layout="HND",
+                out_dtype=torch.bfloat16)
+        else:
+            fn = lambda: trtllm_batch_decode_with_kv_cache(  # noqa: E731
+                qv, kv, ws, blocks, seq, max_kv, d ** -0.5, 1.0, kv_layout="HND", out_dtype=torch.bfloat16)
+        return time_kernel(fn, iters=5)
+    except Exception:  # noqa: BLE001 - shapes the library does not take
+        return None
+
+
 def bench_prefill_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) -> Dict:
     """Causal prefill of B requests of L tokens. `ms` is the tcgen05 kernel
     (q read by TMA); `ms_plain_q` the warp-MMA kernel that the launcher takes
@@ -117,9 +152,12 @@ def bench_prefill_attention(B: int, L: int, hq: int, hk: int, page: int, peaks) 
                                                        d ** -0.5), iters=5)
     flops = 4 * B * hq * d * L * (L + 1) / 2
     tf = flops / ms / 1e9
+    ms_trt = _trtllm_attention_ms(pool, pt, rows, seq, q, L, hq, hk, d, page)
     return {"kernel": "prefill_attention", "B": B, "L": L, "hq": hq, "hk": hk, "ms": round(ms, 4),
             "TFLOP/s": round(tf, 1), "frac_tensor": round(tf / peaks["tflops"], 3),
-            "ms_plain_q": round(ms_old, 4), "speedup": round(ms_old / ms, 2)}
+            "ms_plain_q": round(ms_old, 4), "speedup": round(ms_old / ms, 2),
+            "trtllm_ms": None if ms_trt is None else round(ms_trt, 4),
+            "vs_trtllm": None if ms_trt is None else round(ms_trt / ms, 3)}
 
 
 def trace_prefill_attention(B: int = 1, L: int = 16384, hq: int = 16, hk: int = 8, page: int = 64) -> Dict:
@@ -547,6 +585,9 @@ def main() -> None:
         cases.append((f"decode_attention varlen B={B}",
                       lambda B=B, lo=lo, hi=hi: bench_decode_attention_varlen(B, lo, hi, 16, 8, 64, peaks)))
     cases.append(("decode_attention qwen3-32b", lambda: bench_decode_attention(64, 2000, 64, 8, 64, peaks)))
+    for B, L in [(8, 2048), (2, 8192), (1, 16384)]:
+        cases.append((f"prefill_attention qwen3-32b B={B} L={L}",
+                      lambda B=B, L=L: bench_prefill_attention(B, L, 64, 8, 64, peaks)))
     cases.append(("decode_attention qwen3-32b tp8", lambda: bench_decode_attention(64, 2000, 8, 1, 64, peaks)))
     for B, L, hq, hk in [(16, 1024, 16, 8), (4, 4096, 16, 8), (1, 16384, 16, 8), (2, 4096, 64, 8)]:
         cases.append((f"prefill_attention B={B} L={L} hq={hq}",

@@ -50,7 +50,9 @@ namespace {
 
 constexpr int kSkThreads = 192;
 constexpr int kFlagStride = 32;  // int32 words between ready flags (one 128-byte line each)
-constexpr int kSkSmemBudget = 200 * 1024;  // stage ring bytes
+constexpr int kStageLd = 132;    // floats per token row of the output staging tile (128 + pad)
+constexpr uint32_t kStageBytes = 32 * kStageLd * 4;
+constexpr int kSkSmemBudget = 196 * 1024;  // stage ring bytes (the output staging tile comes on top)
 
 struct SkParams {
   void* out;
@@ -58,6 +60,7 @@ struct SkParams {
   int M, N, K;
   int ldo;
   int out_f32;
+  int vec_ok;     // out and ldo allow 16-byte (bf16) / 32-byte (fp32) row stores
   int num_tiles;  // ceil(N / (128 R))
   int num_kb;     // K / 64
   int kps;        // k-blocks per stage
@@ -128,7 +131,8 @@ struct SkSmem {
                                         : kBufs * kBufCols <= 64 ? 64
                                         : kBufs * kBufCols <= 128 ? 128
                                         : kBufs * kBufCols <= 256 ? 256 : 512;
-  static uint32_t bytes(int stages, int kps) { return stages * kps * (kA + kB) + 1024 + 512; }
+  // ring, barriers (512 B), output staging tile, alignment slack
+  static uint32_t bytes(int stages, int kps) { return stages * kps * (kA + kB) + 512 + kStageBytes + 1024; }
 };
 
 template <int BN, int R>
@@ -266,6 +270,7 @@ __global__ void __launch_bounds__(kSkThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int sub = warp & 3;
     const int row = sub * 32 + lane;  // TMEM lane == weight row within a 128-row sub-tile
+    float* stage = reinterpret_cast<float*>(smem + stages * (stA + stB) + 512);  // [32][kStageLd] output staging
     const int et = threadIdx.x - 64;  // 0..127
     int seg = 0;
     for (int64_t u = u0; u < u1; ++seg) {
@@ -300,9 +305,15 @@ __global__ void __launch_bounds__(kSkThreads, 1)
             }
             tc_wait_ld();
             if ((p.dbg & 1) == 0) {
+              // layout [R][BN / 4][128 rows][4 tokens]: a warp's float4
+              // stores cover 512 contiguous bytes
+              float4* s4 = reinterpret_cast<float4*>(slot) + (static_cast<size_t>(r) * (BN / 4) + c / 4) * 128 + row;
 #pragma unroll
-              for (int j = 0; j < (BN < 32 ? BN : 32); ++j)
-                slot[(static_cast<size_t>(r) * BN + c + j) * 128 + row] = ok ? __uint_as_float(v[j]) : 0.f;
+              for (int q = 0; q < (BN < 32 ? BN : 32) / 4; ++q)
+                s4[static_cast<size_t>(q) * 128] =
+                    ok ? make_float4(__uint_as_float(v[4 * q]), __uint_as_float(v[4 * q + 1]),
+                                     __uint_as_float(v[4 * q + 2]), __uint_as_float(v[4 * q + 3]))
+                       : make_float4(0.f, 0.f, 0.f, 0.f);
             }
           }
         }
@@ -340,8 +351,8 @@ __global__ void __launch_bounds__(kSkThreads, 1)
         const int tok_step = BN < 32 ? BN : 32;
 #pragma unroll 1
         for (int r = 0; r < R; ++r) {
-          const int f = tile * 128 * R + r * 128 + row;  // output feature
-          const float b = (p.bias != nullptr && f < p.N) ? __bfloat162float(p.bias[f]) : 0.f;
+          const int f_row = tile * 128 * R + r * 128 + row;  // this thread's output feature
+          const float b = (p.bias != nullptr && f_row < p.N) ? __bfloat162float(p.bias[f_row]) : 0.f;
 #pragma unroll 1
           for (int c = 0; c < BN; c += tok_step) {
             uint32_t v[32];
@@ -358,22 +369,68 @@ __global__ void __launch_bounds__(kSkThreads, 1)
 #pragma unroll
             for (int j = 0; j < 32; ++j) acc[j] = j < tok_step ? __uint_as_float(v[j]) : 0.f;
             for (int c2 = blockIdx.x + 1; c2 <= c_last; ++c2) {
-              const float* slot = p.ws + static_cast<size_t>(c2) * (R * BN * 128);
+              const float4* s4 = reinterpret_cast<const float4*>(p.ws + static_cast<size_t>(c2) * (R * BN * 128)) +
+                                 (static_cast<size_t>(r) * (BN / 4) + c / 4) * 128 + row;
+              float4 pv[8];
 #pragma unroll
-              for (int j = 0; j < 32; ++j)
-                if (j < tok_step) acc[j] += slot[(static_cast<size_t>(r) * BN + c + j) * 128 + row];
+              for (int q = 0; q < 8; ++q)  // every load in flight before the adds
+                if (q < tok_step / 4) pv[q] = s4[static_cast<size_t>(q) * 128];
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                if (q < tok_step / 4) {
+                  acc[4 * q] += pv[q].x;
+                  acc[4 * q + 1] += pv[q].y;
+                  acc[4 * q + 2] += pv[q].z;
+                  acc[4 * q + 3] += pv[q].w;
+                }
             }
-            if (f < p.N && (p.dbg & 1) == 0) {
+            // stage the chunk token-major in shared memory, then store each
+            // token's 128 features with 16-byte vectors (256 contiguous bytes
+            // per half-warp) instead of one 2-byte store per element
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                const int m = c + j;
-                if (j < tok_step && m < p.M) {
-                  const float y = acc[j] + b;
-                  if (p.out_f32) reinterpret_cast<float*>(p.out)[static_cast<size_t>(m) * p.ldo + f] = y;
-                  else reinterpret_cast<__nv_bfloat16*>(p.out)[static_cast<size_t>(m) * p.ldo + f] = __float2bfloat16_rn(y);
+            for (int j = 0; j < 32; ++j)
+              if (j < tok_step) stage[j * kStageLd + row] = acc[j] + b;
+            asm volatile("bar.sync 1, 128;" ::: "memory");
+            if ((p.dbg & 1) == 0) {
+              const int f0 = tile * 128 * R + r * 128;
+              const int col = (lane & 15) * 8;  // 8 features per lane
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const int t = sub * 8 + i * 2 + (lane >> 4);  // token within the chunk
+                const int m = c + t;
+                if (t >= tok_step || m >= p.M) continue;
+                const float* src = stage + t * kStageLd + col;
+                const float4 lo = *reinterpret_cast<const float4*>(src);
+                const float4 hi = *reinterpret_cast<const float4*>(src + 4);
+                const int f = f0 + col;
+                if (p.out_f32) {
+                  float* dst = reinterpret_cast<float*>(p.out) + static_cast<size_t>(m) * p.ldo + f;
+                  if (p.vec_ok && f + 8 <= p.N) {
+                    *reinterpret_cast<float4*>(dst) = lo;
+                    *reinterpret_cast<float4*>(dst + 4) = hi;
+                  } else {
+                    const float e8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                    for (int q = 0; q < 8; ++q)
+                      if (f + q < p.N) dst[q] = e8[q];
+                  }
+                } else {
+                  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.out) + static_cast<size_t>(m) * p.ldo + f;
+                  if (p.vec_ok && f + 8 <= p.N) {
+                    uint4 pk;
+                    pk.x = pack_bf16x2(lo.x, lo.y);
+                    pk.y = pack_bf16x2(lo.z, lo.w);
+                    pk.z = pack_bf16x2(hi.x, hi.y);
+                    pk.w = pack_bf16x2(hi.z, hi.w);
+                    *reinterpret_cast<uint4*>(dst) = pk;
+                  } else {
+                    const float e8[8] = {lo.x, lo.y, lo.z, lo.w, hi.x, hi.y, hi.z, hi.w};
+                    for (int q = 0; q < 8; ++q)
+                      if (f + q < p.N) dst[q] = __float2bfloat16_rn(e8[q]);
+                  }
                 }
               }
             }
+            asm volatile("bar.sync 1, 128;" ::: "memory");  // the stage is rewritten by the next chunk
           }
         }
         if (!whole) {
@@ -465,6 +522,7 @@ void launch_gemm_streamk(const GemmStreamKArgs& a, cudaStream_t stream) {
   p.K = a.K;
   p.ldo = a.ldo;
   p.out_f32 = a.out_f32;
+  p.vec_ok = (reinterpret_cast<uintptr_t>(a.out) % 16 == 0) && (a.ldo % (a.out_f32 ? 4 : 8) == 0);
   p.num_tiles = (a.N + 128 * a.R - 1) / (128 * a.R);
   p.num_kb = a.K / 64;
   p.grid = a.grid;

@@ -186,7 +186,7 @@ class Engine:
         self.graph_runner = GraphRunner(
             self.stream, self.device, self.model, self.attn_backend, config.cuda_graph_bs,
             self._graph_max_bs(config), init_free, width, mcfg.vocab_size, self.dummy_req,
-            sampler=None if ENV.NO_FUSED_SAMPLING.value else self.sampler)
+            sampler=None if ENV.NO_FUSED_SAMPLING.value else self.sampler, cpu_group=self.tp_cpu_group)
 
     # ---------------------------------------------------------------- setup
     def _graph_max_bs(self, config: EngineConfig) -> Optional[int]:

@@ -52,9 +52,10 @@ class GraphRunner:
     def __init__(self, stream: Optional[torch.cuda.Stream], device: torch.device, model: "BaseLLMModel",
                  attn_backend: "BaseAttnBackend", cuda_graph_bs: Optional[List[int]],
                  cuda_graph_max_bs: Optional[int], free_memory: int, max_seq_len: int, vocab_size: int,
-                 dummy_req: Req, sampler: Optional["Sampler"] = None) -> None:
+                 dummy_req: Req, sampler: Optional["Sampler"] = None, cpu_group=None) -> None:
         self.stream = stream
         self.sampler = sampler
+        self.cpu_group = cpu_group  # tensor-parallel ranks agree on the measured layer forms
         # graphs that sample inside the LM head (greedy / temperature batches)
         self.sample_graph_map: Dict[int, torch.cuda.CUDAGraph] = {}
         self.logits_out: Dict[int, torch.Tensor] = {}
@@ -84,6 +85,8 @@ class GraphRunner:
                           f"free memory {mem_GB(get_free_memory(self.device))}")
         ctx = get_global_ctx()
         pool = None
+        variants = model.forward_variants() if hasattr(model, "forward_variants") else (None,)
+        chosen: Dict[int, object] = {}
         for bs in sorted(self.graph_bs_list, reverse=True):
             batch = Batch(reqs=[self.dummy_req] * bs, phase="decode")
             batch.padded_reqs = batch.reqs
@@ -91,17 +94,35 @@ class GraphRunner:
             batch.positions = self.positions[:bs]
             batch.out_loc = self.out_loc[:bs]
             self.attn_backend.prepare_for_capture(batch)
-            graph = torch.cuda.CUDAGraph()
-            with ctx.forward_batch(batch):
-                model.forward()  # warm-up outside the capture
-                before = ops.LAUNCHES[0]
-                with torch.cuda.graph(graph, pool=pool, stream=self.stream):
-                    # the graph's own output tensor is the static logits buffer
-                    self.logits_out[bs] = model.forward()
-                self.graph_launches[bs] = ops.LAUNCHES[0] - before
-                ops.LAUNCHES[0] = before
-            if pool is None:
-                pool = graph.pool()
+            # capture every layer form the model offers and keep the fastest
+            # (every rank captures and replays the same forms the same number
+            # of times, so the collectives inside them stay paired)
+            captured = []
+            for variant in variants:
+                if variant is not None:
+                    model.set_forward_variant(bs, variant)
+                graph = torch.cuda.CUDAGraph()
+                with ctx.forward_batch(batch):
+                    model.forward()  # warm-up outside the capture
+                    before = ops.LAUNCHES[0]
+                    with torch.cuda.graph(graph, pool=pool, stream=self.stream):
+                        # the graph's own output tensor is the static logits buffer
+                        logits = model.forward()
+                    launches = ops.LAUNCHES[0] - before
+                    ops.LAUNCHES[0] = before
+                if pool is None:
+                    pool = graph.pool()
+                ms = self._time_graph(graph) if len(variants) > 1 else 0.0
+                captured.append((ms, variant, graph, logits, launches))
+            times = self._slowest_rank([c[0] for c in captured])
+            pick = min(range(len(captured)), key=lambda i: times[i])
+            _, variant, graph, logits, launches = captured[pick]
+            del captured
+            if variant is not None:
+                model.set_forward_variant(bs, variant)
+                chosen[bs] = variant
+            self.logits_out[bs] = logits
+            self.graph_launches[bs] = launches
             self.graph_map[bs] = graph
             if (self.sampler is not None and getattr(model, "samples_in_lm_head", False)
                     and bs <= self.sampler.FUSED_MAX_ROWS):
@@ -119,7 +140,35 @@ class GraphRunner:
                     ctx.fused_sample = None
                 self.sample_graph_map[bs] = sgraph
         torch.cuda.synchronize(self.device)
+        if chosen:
+            fused = sorted(b for b, v in chosen.items() if v)
+            logger.info_rank0(f"Fused-epilogue layers at batch sizes {fused}; plain GEMMs + row kernels at the rest")
         logger.info_rank0(f"CUDA graphs ready; free memory {mem_GB(get_free_memory(self.device))}")
+
+    def _time_graph(self, graph: torch.cuda.CUDAGraph, reps: int = 3) -> float:
+        """Device milliseconds of one replay (best of ``reps`` after one warm-up)."""
+        graph.replay()
+        best = float("inf")
+        for _ in range(reps):
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record(self.stream)
+            graph.replay()
+            e.record(self.stream)
+            e.synchronize()
+            best = min(best, s.elapsed_time(e))
+        return best
+
+    def _slowest_rank(self, times: List[float]) -> List[float]:
+        """Per layer form, the slowest tensor-parallel rank's time: every rank
+        then picks the same form (graphs of different ranks must run the same
+        collectives in the same order)."""
+        if self.cpu_group is None or len(times) < 2:
+            return times
+        import torch.distributed as dist
+
+        t = torch.tensor(times, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.cpu_group)
+        return t.tolist()
 
     def can_use_cuda_graph(self, batch: Batch) -> bool:
         return batch.is_decode and max(batch.size, 1) <= self.max_graph_bs

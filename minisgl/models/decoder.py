@@ -95,7 +95,7 @@ class DecoderLayer(BaseOP):
 
     @nvtx_annotate("Layer_{}", layer_id_field="_layer_id")
     def forward_sp(self, x: torch.Tensor, r: torch.Tensor, comm: DistributedImpl, T: int,
-                   next_norm: RMSNormFused) -> torch.Tensor:
+                   next_norm: RMSNormFused, fused: bool) -> torch.Tensor:
         """Sequence-parallel block over tensor-parallel ranks. ``x`` [T_pad, H]
         holds every rank's normalised input rows (gathered by the previous
         collective), ``r`` this rank's slice of the residual stream (updated in
@@ -107,7 +107,7 @@ class DecoderLayer(BaseOP):
         Tp, H = x.shape
         first = get_tp_info().rank == 0
         attn = self.self_attn
-        fused = T <= FUSED_MAX_TOKENS and self._fused_attn
+        fused = fused and self._fused_attn
         xt = x[:T]
         if fused:  # q/k norm, RoPE and the KV store in the qkv GEMM's epilogue
             q = torch.empty(T, attn.attn.qo_attn_dim, dtype=x.dtype, device=x.device)
@@ -136,6 +136,20 @@ class DecoderModel(BaseOP):
         self.embed_tokens = VocabParallelEmbedding(config.vocab_size, config.hidden_size)
         self.layers = OPList([DecoderLayer(config, i, **flags) for i in range(config.num_layers)])
         self.norm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
+        # batch size -> whether the fused-epilogue layer form runs at that size;
+        # measured per CUDA-graph batch size when the graphs are captured (the
+        # fused form wins on narrow models, the plain-GEMM form with separate
+        # row kernels can win on wide ones at large batches)
+        self._fused_choice: Dict[int, bool] = {}
+
+    def fused_for(self, T: int) -> bool:
+        """Whether a batch of T tokens takes the fused-epilogue form: the
+        measured choice of the smallest captured size >= T (fused when none
+        was measured), never beyond FUSED_MAX_TOKENS."""
+        if T > FUSED_MAX_TOKENS or not self.fusable:
+            return False
+        size = min((b for b in self._fused_choice if b >= T), default=None)
+        return self._fused_choice[size] if size is not None else True
 
     @property
     def fusable(self) -> bool:
@@ -172,8 +186,10 @@ class DecoderModel(BaseOP):
         layers = self.layers.op_list
         norm0 = layers[0].input_layernorm if layers else self.norm
         x = comm.rs_norm_ag(part, r, False, norm0.active_weight, norm0.eps)
+        fused = self.fused_for(T)
         for i, layer in enumerate(layers):
-            x = layer.forward_sp(x, r, comm, T, layers[i + 1].input_layernorm if i + 1 < len(layers) else self.norm)
+            x = layer.forward_sp(x, r, comm, T, layers[i + 1].input_layernorm if i + 1 < len(layers) else self.norm,
+                                 fused)
         return x[:T]
 
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
@@ -181,7 +197,7 @@ class DecoderModel(BaseOP):
         if comm is not None:
             return self.forward_sp(input_ids, comm)
         x = self.embed_tokens.forward(input_ids)
-        if self.fusable and x.shape[0] <= FUSED_MAX_TOKENS:
+        if self.fused_for(x.shape[0]):
             r = x  # a fresh buffer: the residual stream is updated in place
             for layer in self.layers.op_list:
                 r = layer.forward_fused(r)
@@ -202,6 +218,15 @@ class DecoderForCausalLM(BaseLLMModel):
         tied = config.tie_word_embeddings
         self.lm_head = ParallelLMHead(config.vocab_size, config.hidden_size, tie_word_embeddings=tied,
                                       tied_embedding=self.model.embed_tokens if tied else None)
+
+    def forward_variants(self) -> Tuple[Optional[bool], ...]:
+        """Layer forms the graph runner measures per batch size (fused
+        epilogues, plain GEMMs + row kernels); (None,) when only one exists."""
+        return (True, False) if self.model.fusable else (None,)
+
+    def set_forward_variant(self, batch_size: int, fused: Optional[bool]) -> None:
+        if fused is not None:
+            self.model._fused_choice[batch_size] = fused
 
     @property
     def samples_in_lm_head(self) -> bool:

@@ -84,3 +84,11 @@ def test_tp2_matches_tp1(checkpoint, single):
 def test_tp2_sequence_parallel_matches_tp1(checkpoint, single):
     tp = _generate(2, checkpoint, sp=True)
     assert tp[0] == tp[1] == single
+
+
+def test_tp4_sequence_parallel_matches_tp1(checkpoint, single):
+    """Four ranks: more ranks than kv heads (the kv heads are replicated), and
+    token counts padded up to a multiple of 4 (21 prompt tokens, then decode
+    batches of 2 and 1)."""
+    tp = _generate(4, checkpoint, sp=True)
+    assert tp[0] == tp[1] == tp[2] == tp[3] == single
