@@ -18,6 +18,7 @@
 //
 // Softmax runs in the exp2 domain: q is pre-scaled by scale * log2(e).
 #include <algorithm>
+#include <cstdlib>
 #include <cstdarg>
 #include <cstdio>
 #include <mutex>
@@ -903,6 +904,325 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
+// ------------------------------------------------------ head-pair prefill ----
+// Two query heads of one KV group per CTA (128 query rows each), sharing every
+// K/V tile. Tensor memory (512 columns): O of head h at columns [128 h, +128),
+// scores S_h at [256 + 64 h, +64) with P_h (bf16 pairs) written over the first
+// 32 of them, and Q_h (bf16 pairs, loaded once) at [384 + 64 h, +64) as the A
+// operand of Q.K^T, so the MMAs read only K and V from shared memory. The MMA
+// thread ping-pongs the heads,
+//   QK0(0) QK1(0) | PV0(i) QK0(i+1) PV1(i) QK1(i+1) | ...,
+// so the softmax of one head runs while the tensor core works on the other.
+// tcgen05 operations of one thread complete in order, which is what makes
+// the single S/P buffer per head safe: QK_h(i+1) is issued after PV_h(i), and
+// S_h(i+1) being ready implies PV_h(i) finished (the softmax may rescale O_h
+// then without another wait). Warps 0-3 own the rows of head 0 and warps 4-7
+// those of head 1 (one row per thread, the whole 64-key tile), so no row
+// statistics cross warps.
+constexpr int kPrStages = 5;
+constexpr int kPrSCol = 256;
+constexpr int kPrQCol = 384;
+constexpr int kPrProducer = 8, kPrIssuer = 9;
+constexpr int kPrThreads = 32 * 10;
+constexpr int kPrSmem = 1024 + kPrStages * kStageBytes + 256;
+static_assert(kPrSmem <= 227 * 1024, "head-pair prefill smem over the per-CTA limit");
+
+__global__ void __launch_bounds__(kPrThreads, 1)
+    prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tm_kv, AttnArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
+                                             ~static_cast<uintptr_t>(1023));
+  uint8_t* sKV = smem;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kPrStages * kStageBytes);
+  uint64_t* kv_full = bars;                  // [kPrStages]
+  uint64_t* kv_empty = kv_full + kPrStages;  // [kPrStages]
+  uint64_t* s_full = kv_empty + kPrStages;   // [2 heads]
+  uint64_t* p_full = s_full + 2;             // [2 heads]
+  uint64_t* o_done = p_full + 2;             // [2 heads]
+  uint64_t* q_ready = o_done + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(q_ready + 1);
+  int* s_abort = reinterpret_cast<int*>(tmem_slot + 1);
+  const ErrorSink err{a.err};
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  pdl_launch_dependents();
+  pdl_wait();
+  const int qt = static_cast<int>(gridDim.x) - 1 - static_cast<int>(blockIdx.x);  // longest key ranges first
+  const int qh0 = 2 * static_cast<int>(blockIdx.y), b = blockIdx.z;
+  const int q_begin = a.cu_q[b];
+  const int q_len = a.cu_q[b + 1] - q_begin;
+  const int row0 = qt * kTcRows;
+  if (row0 >= q_len) return;  // uniform over the CTA, before any barrier or TMEM
+  const int L = a.seq_lens[b];
+  const int cached = L - q_len;
+  const int h = qh0 / (a.hq / a.hk);  // both heads of the pair share this KV head
+  const int n = (cached + min(q_len, row0 + kTcRows) - 1) / kTile + 1;
+  const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kPrStages; ++i) {
+      mbar_init(&kv_full[i], 1);
+      mbar_init(&kv_empty[i], 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(&s_full[i], 1);
+      mbar_init(&p_full[i], 4);
+      mbar_init(&o_done[i], 1);
+    }
+    mbar_init(q_ready, 8);
+    *s_abort = 0;
+    fence_barrier_init();
+    prefetch_tmap(&tm_kv);
+  }
+  if (warp == kPrIssuer) {
+    tmem_alloc(tmem_slot, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  int issued = 0;  // key tiles whose copies the producer started
+
+  if (warp == kPrProducer) {
+    // ------------------------------------------------------------ TMA ----
+    if (lane == 0) {
+      const int P = a.page_size;
+      const int seg = P < kTile ? P : kTile;
+      int cur[kTile / 16], nxt[kTile / 16];
+      auto read_pages = [&](int (&pg)[kTile / 16], int j) {
+#pragma unroll
+        for (int q = 0; q < kTile / 16; ++q) {
+          const int pos = j * kTile + q * seg;
+          pg[q] = (q * seg < kTile && pos < L) ? pt_row[pos] / P : 0;  // past the end: page 0, masked later
+        }
+      };
+      read_pages(cur, 0);
+      for (int j = 0; j < n; ++j) {
+        const int s = j % kPrStages;
+        read_pages(nxt, j + 1);
+        if (j >= kPrStages && !mbar_wait(&kv_empty[s], ((j / kPrStages) - 1) & 1, err, 251)) {
+          atomicExch(s_abort, 1);
+          break;
+        }
+        if (*reinterpret_cast<volatile int*>(s_abort)) break;
+        ++issued;
+        uint8_t* st = sKV + s * kStageBytes;
+        mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
+        const int64_t in_page = P < kTile ? 0 : (j * kTile) % P;
+#pragma unroll
+        for (int q = 0; q < kTile / 16; ++q) {
+          if (q * seg >= kTile) break;
+          const int64_t row = (static_cast<int64_t>(cur[q]) * a.hk + h) * P + in_page;
+          const int32_t rk = static_cast<int32_t>(a.k_row0 + row);
+          const int32_t rv = static_cast<int32_t>(a.v_row0 + row);
+          const int o = q * seg * 128;
+          tma_load_2d(st + o, &tm_kv, &kv_full[s], 0, rk);
+          tma_load_2d(st + kHalfBytes + o, &tm_kv, &kv_full[s], 64, rk);
+          tma_load_2d(st + kTileBytes + o, &tm_kv, &kv_full[s], 0, rv);
+          tma_load_2d(st + kTileBytes + kHalfBytes + o, &tm_kv, &kv_full[s], 64, rv);
+        }
+#pragma unroll
+        for (int q = 0; q < kTile / 16; ++q) cur[q] = nxt[q];
+      }
+    }
+    __syncwarp();
+  } else if (warp == kPrIssuer) {
+    // ------------------------------------------------------------ MMA ----
+    constexpr uint32_t idesc_qk = make_idesc_bf16(kTcRows, kTile);
+    constexpr uint32_t idesc_pv = make_idesc_bf16(kTcRows, kD, false, true);
+    const uint32_t kv_addr = smem_u32(sKV);
+    auto qk = [&](int hh, int j) {  // S_hh = Q_hh . K_j^T (Q from tensor memory)
+      const uint32_t st = kv_addr + (j % kPrStages) * kStageBytes;
+#pragma unroll
+      for (int c = 0; c < 2; ++c)
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f16_ta(tmem + kPrSCol + 64 * hh, tmem + kPrQCol + 64 * hh + (c * 4 + k) * 8,
+                        make_sdesc_k_sw128(st + c * kHalfBytes + k * 32), idesc_qk, (c | k) != 0 ? 1u : 0u);
+      tc_commit(&s_full[hh]);
+    };
+    auto pv = [&](int hh, int i) {  // O_hh += P_hh . V_i
+      const uint32_t v = kv_addr + (i % kPrStages) * kStageBytes + kTileBytes;
+#pragma unroll
+      for (int kk = 0; kk < kTile / 16; ++kk)  // 16 keys = 8 TMEM columns of P per MMA
+        tc_mma_f16_ta(tmem + 128 * hh, tmem + kPrSCol + 64 * hh + kk * 8,
+                      make_sdesc_mn_sw128(v + kk * 2048, kHalfBytes), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+      tc_commit(&o_done[hh]);
+    };
+    // every wait of this warp is bounded; the warp follows lane 0's result
+    auto wait = [&](uint64_t* bar, uint32_t parity, int where) {  // uniform over the warp
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, where) &&
+                                         !*reinterpret_cast<volatile int*>(s_abort));
+    };
+    bool ok = wait(q_ready, 0, 252) && wait(&kv_full[0], 0, 253);
+    tc_fence_after();
+    if (ok && lane == 0) {
+      qk(0, 0);
+      qk(1, 0);
+    }
+    __syncwarp();
+    for (int i = 0; ok && i < n; ++i) {
+      const bool more = i + 1 < n;
+      ok = wait(&p_full[0], i & 1, 254);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) pv(0, i);
+      __syncwarp();
+      if (more) {
+        ok = wait(&kv_full[(i + 1) % kPrStages], ((i + 1) / kPrStages) & 1, 255);
+        if (!ok) break;
+        tc_fence_after();
+        if (lane == 0) qk(0, i + 1);
+        __syncwarp();
+      }
+      ok = wait(&p_full[1], i & 1, 256);
+      if (!ok) break;
+      tc_fence_after();
+      if (lane == 0) {
+        pv(1, i);
+        tc_commit(&kv_empty[i % kPrStages]);  // both heads have read tile i
+        if (more) qk(1, i + 1);
+      }
+      __syncwarp();
+    }
+    if (!ok && lane == 0) atomicExch(s_abort, 1);
+    __syncwarp();
+  } else {
+    // -------------------------------------------------------- softmax ----
+    const int hh = warp >> 2, quad = warp & 3;
+    const int r = 32 * quad + lane;  // this thread's query row (TMEM lane)
+    const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * quad) << 16);
+    const bool row_valid = row0 + r < q_len;
+    const int64_t tok = q_begin + row0 + (row_valid ? r : 0);
+    // Q row of head qh0 + hh into tensor memory: 128 bf16 = 64 columns of pairs
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.q) + tok * a.ld_q +
+                                                        static_cast<int64_t>(qh0 + hh) * kD);
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t w[32];
+#pragma unroll
+        for (int v = 0; v < 8; ++v) {
+          const uint4 x = row_valid ? src[c * 8 + v] : make_uint4(0u, 0u, 0u, 0u);
+          w[4 * v] = x.x, w[4 * v + 1] = x.y, w[4 * v + 2] = x.z, w[4 * v + 3] = x.w;
+        }
+        tmem_st_32x32b_x32(lane_base + kPrQCol + 64 * hh + 32 * c, w);
+      }
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(q_ready);
+    }
+    const float sl2 = a.scale * kLog2e;
+    const int pos = cached + row0 + r;  // position of this row's query token
+    const uint32_t s_col = lane_base + kPrSCol + 64 * hh;
+    const uint32_t o_col = lane_base + 128 * hh;
+    float m_run = -INFINITY, l_sum = 0.f;
+    bool ok = true;
+    for (int i = 0; i < n; ++i) {
+      ok = __all_sync(0xffffffffu, mbar_wait(&s_full[hh], i & 1, err, 257) &&
+                                       !*reinterpret_cast<volatile int*>(s_abort));  // uniform over the warp
+      if (!ok) break;
+      tc_fence_after();
+      uint32_t sv[kTile];
+      tmem_ld_32x32b_x32(s_col, *reinterpret_cast<uint32_t(*)[32]>(sv));
+      tmem_ld_32x32b_x32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
+      tc_wait_ld();
+      // causal and length mask: keys [0, lim) of the tile are visible to this row
+      const int lim = min(pos + 1, L) - i * kTile;
+      if (lim < kTile) {
+#pragma unroll
+        for (int j = 0; j < kTile; ++j)
+          if (j >= lim) sv[j] = __float_as_uint(-INFINITY);
+      }
+      float m4[4];
+#pragma unroll
+      for (int c = 0; c < 4; ++c) m4[c] = __uint_as_float(sv[c]);
+#pragma unroll
+      for (int j = 4; j < kTile; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(sv[j]));
+      const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+      // lazy rescale: the running max moves only when it grows by more than
+      // 2^kTcRescaleLog2, so P stays below that bound in bf16
+      const bool grow = mt > m_run + kTcRescaleLog2;
+      float alpha = 1.f;
+      if (grow) {
+        alpha = ex2_fast(m_run - mt);  // 0 on the first tile (m_run = -inf)
+        l_sum *= alpha;
+        m_run = mt;
+      }
+      // tcgen05.ld / st are warp-collective: the whole warp rescales when any
+      // of its rows grew (the others multiply by 1). O_hh holds PV_hh(0 .. i-1)
+      // complete: S_hh(i) was committed after them.
+      if (__any_sync(0xffffffffu, grow) && i > 0) {
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t ov[32];
+          tmem_ld_32x32b_x32(o_col + 32 * c, ov);
+          tc_wait_ld();
+#pragma unroll
+          for (int j = 0; j < 32; ++j) ov[j] = __float_as_uint(__uint_as_float(ov[j]) * alpha);
+          tmem_st_32x32b_x32(o_col + 32 * c, ov);
+        }
+      }
+      // P = 2^(s * scale * log2 e - m) as bf16 pairs over the first 32 score columns
+      uint32_t pk[kTile / 2];
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+      for (int e = 0; e < kTile / 2; ++e) {
+        const float lo = ex2_fast(fmaf(__uint_as_float(sv[2 * e]), sl2, -m_run));
+        const float hi = ex2_fast(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -m_run));
+        ps[e & 3] += lo + hi;
+        pk[e] = pack_bf16x2(lo, hi);
+      }
+      l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      tmem_st_32x32b_x32(s_col, pk);
+      tc_wait_st();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&p_full[hh]);
+    }
+    // ------------------------------------------------------- epilogue ----
+    if (!ok && lane == 0) atomicExch(s_abort, 1);
+    if (ok) ok = __all_sync(0xffffffffu, mbar_wait(&o_done[hh], (n - 1) & 1, err, 258));
+    tc_fence_after();
+    const float inv = ok && l_sum > 0.f ? 1.f / l_sum : 0.f;
+    __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(a.out) + (tok * a.hq + qh0 + hh) * kD;
+#pragma unroll 1
+    for (int c = 0; c < 4; ++c) {
+      uint32_t ov[32];
+      if (ok) {
+        tmem_ld_32x32b_x32(o_col + 32 * c, ov);
+        tc_wait_ld();
+      } else {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) ov[j] = 0u;
+      }
+      if (!row_valid) continue;
+#pragma unroll
+      for (int q4 = 0; q4 < 4; ++q4) {
+        uint4 v;
+        v.x = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 0]) * inv, __uint_as_float(ov[q4 * 8 + 1]) * inv);
+        v.y = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 2]) * inv, __uint_as_float(ov[q4 * 8 + 3]) * inv);
+        v.z = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 4]) * inv, __uint_as_float(ov[q4 * 8 + 5]) * inv);
+        v.w = pack_bf16x2(__uint_as_float(ov[q4 * 8 + 6]) * inv, __uint_as_float(ov[q4 * 8 + 7]) * inv);
+        *reinterpret_cast<uint4*>(dst + c * 32 + q4 * 8) = v;
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kPrProducer && lane == 0 && *reinterpret_cast<volatile int*>(s_abort)) {
+    // after an abort, let the copies still in flight land before the CTA leaves
+    for (int j = max(0, issued - kPrStages); j < issued; ++j)
+      mbar_wait(&kv_full[j % kPrStages], (j / kPrStages) & 1, err, 259);
+  }
+  if (warp == kPrIssuer) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 512);
+  }
+}
+
 constexpr int kAttnSmem = kStages * kStageBytes + 1024 + 128;
 static_assert(kConsumers * 16 * kMergeLd * 4 + 2 * kConsumers * 16 * 4 <= kStages * kStageBytes,
               "merge buffer must fit in the ring");
@@ -953,8 +1273,27 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
   if (a.B <= 0 || a.max_q <= 0) return;
   check_args(a);
   CUtensorMap tm = pool_map(a);
+  const bool q_aligned = reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && a.ld_q % 8 == 0;
+  // head pairs of one KV group share the K/V stream (MINISGL_PREFILL_PAIR=1
+  // selects them; a measurement switch while the kernel is validated)
+  static const bool pair_on = [] {
+    const char* v = std::getenv("MINISGL_PREFILL_PAIR");
+    return v != nullptr && v[0] == '1';
+  }();
+  if (pair_on && q_aligned && (a.hq / a.hk) % 2 == 0) {
+    static bool pair_attr[64] = {};
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (!pair_attr[dev & 63]) {
+      cudaFuncSetAttribute(prefill_attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrSmem);
+      pair_attr[dev & 63] = true;
+    }
+    dim3 grid((a.max_q + kTcRows - 1) / kTcRows, a.hq / 2, a.B);
+    launch_pdl(prefill_attn_pair_kernel, grid, dim3(kPrThreads), kPrSmem, s, tm, a);
+    return;
+  }
   // the tcgen05 kernel reads Q by TMA: a 16-byte aligned base and row stride
-  if (a.q_rows > 0 && reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && a.ld_q % 8 == 0) {
+  if (a.q_rows > 0 && q_aligned) {
     static bool attr_set[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);

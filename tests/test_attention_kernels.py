@@ -79,8 +79,9 @@ def _prefill_case(hq, hk, page, lens, qlens, qmul=1.0, pad=0):
 
 # 128-row query tiles on the tensor cores: partial tiles, cached prefixes,
 # several tiles per request, and scores large enough (qmul 6) that running
-# maxima grow across tiles and the output rescale runs
-@pytest.mark.parametrize("hq,hk", [(16, 8), (8, 1)])
+# maxima grow across tiles and the output rescale runs. Even GQA groups run
+# the head-pair kernel, the odd group (12 / 4) the one-head kernel.
+@pytest.mark.parametrize("hq,hk", [(16, 8), (8, 1), (12, 4)])
 @pytest.mark.parametrize("page", [16, 64, 256])
 @pytest.mark.parametrize("qmul", [1.0, 6.0])
 def test_prefill_attention(hq, hk, page, qmul):
