@@ -1274,11 +1274,11 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
   check_args(a);
   CUtensorMap tm = pool_map(a);
   const bool q_aligned = reinterpret_cast<uintptr_t>(a.q) % 16 == 0 && a.ld_q % 8 == 0;
-  // head pairs of one KV group share the K/V stream (MINISGL_PREFILL_PAIR=1
-  // selects them; a measurement switch while the kernel is validated)
+  // head pairs of one KV group share the K/V stream (MINISGL_PREFILL_PAIR=0
+  // selects the one-head kernel instead, a measurement switch)
   static const bool pair_on = [] {
     const char* v = std::getenv("MINISGL_PREFILL_PAIR");
-    return v != nullptr && v[0] == '1';
+    return v == nullptr || v[0] != '0';
   }();
   if (pair_on && q_aligned && (a.hq / a.hk) % 2 == 0) {
     static bool pair_attr[64] = {};
