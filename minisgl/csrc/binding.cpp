@@ -590,12 +590,84 @@ void mla_prepare(at::Tensor q_pe, at::Tensor xs, const at::Tensor& q, const at::
   minisgl::launch_mla_prepare(a, stream_of(q));
 }
 
+// Key rows only: the normalised, rotated latent rows of T tokens into the
+// cache (token-sharded context parallelism stores a rank's own tokens).
+void mla_store_latent(const at::Tensor& kv_a, const at::Tensor& norm_w, double eps, const at::Tensor& positions,
+                      const at::Tensor& cos_sin, at::Tensor latent, const at::Tensor& out_loc,
+                      const c10::optional<at::Tensor>& err, int64_t cp_size, int64_t cp_rank) {
+  check_cuda(kv_a, "kv_a");
+  MSG_CHECK(kv_a.dim() == 2 && kv_a.stride(1) == 1 && kv_a.scalar_type() == at::kBFloat16,
+            "mla_store_latent: kv_a [T, kv_lora + rope] bf16");
+  MSG_CHECK(latent.dim() == 3 && latent.is_contiguous() && latent.size(2) == kv_a.size(1) &&
+                latent.scalar_type() == at::kBFloat16,
+            "mla_store_latent: latent [pages, page, kv_lora + rope] bf16 contiguous");
+  const int64_t T = kv_a.size(0), rope = cos_sin.size(1), kv_lora = kv_a.size(1) - rope;
+  MSG_CHECK(norm_w.numel() == kv_lora && norm_w.scalar_type() == at::kBFloat16, "mla_store_latent: bf16 norm weight");
+  MSG_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous(), "mla_store_latent: fp32 cos_sin");
+  check_i32(positions, "positions");
+  check_i32(out_loc, "out_loc");
+  MSG_CHECK(positions.numel() >= T && out_loc.numel() >= T, "mla_store_latent: positions / out_loc of T tokens");
+  MSG_CHECK(cp_size >= 1 && cp_rank >= 0 && cp_rank < cp_size, "mla_store_latent: cp_rank outside [0, cp_size)");
+  const c10::cuda::CUDAGuard guard(kv_a.device());
+  minisgl::MlaPrepareArgs a{};
+  a.kv_a = kv_a.data_ptr();
+  a.ld_kv_a = static_cast<int>(kv_a.stride(0));
+  a.norm_w = norm_w.data_ptr();
+  a.eps = static_cast<float>(eps);
+  a.positions = positions.data_ptr<int32_t>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.latent = latent.data_ptr();
+  a.out_loc = out_loc.data_ptr<int32_t>();
+  a.T = static_cast<int>(T);
+  a.T_pad = static_cast<int>(T);
+  a.H = 1;
+  a.kv_lora = static_cast<int>(kv_lora);
+  a.rope = static_cast<int>(rope);
+  a.cp_size = static_cast<int>(cp_size);
+  a.cp_rank = static_cast<int>(cp_rank);
+  a.page_size = static_cast<int>(latent.size(1));
+  a.err = err_ptr(err);
+  minisgl::launch_mla_prepare(a, stream_of(kv_a));
+}
+
+// Queries only: rotated q_pe [T, H, rope] and q_nope head-major into xs.
+void mla_prepare_q(at::Tensor q_pe, at::Tensor xs, const at::Tensor& q, const at::Tensor& positions,
+                   const at::Tensor& cos_sin, int64_t T_pad, const c10::optional<at::Tensor>& err) {
+  check_cuda(q, "q");
+  MSG_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2) && q.scalar_type() == at::kBFloat16,
+            "mla_prepare_q: q [T, H, nope + rope] bf16 with packed heads");
+  const int64_t T = q.size(0), H = q.size(1), rope = q_pe.size(2), nope = q.size(2) - rope;
+  MSG_CHECK(q_pe.is_contiguous() && q_pe.size(0) == T && q_pe.size(1) == H, "mla_prepare_q: q_pe [T, H, rope]");
+  MSG_CHECK(xs.is_contiguous() && xs.numel() >= H * T_pad * nope && T_pad >= T, "mla_prepare_q: xs [H, T_pad, nope]");
+  MSG_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == rope,
+            "mla_prepare_q: fp32 cos_sin [max_pos, rope]");
+  check_i32(positions, "positions");
+  MSG_CHECK(positions.numel() >= T, "mla_prepare_q: positions of T tokens");
+  const c10::cuda::CUDAGuard guard(q.device());
+  minisgl::MlaPrepareArgs a{};
+  a.q = q.data_ptr();
+  a.ld_q = static_cast<int>(q.stride(0));
+  a.positions = positions.data_ptr<int32_t>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.q_pe = q_pe.data_ptr();
+  a.xs = xs.data_ptr();
+  a.T = static_cast<int>(T);
+  a.T_pad = static_cast<int>(T_pad);
+  a.H = static_cast<int>(H);
+  a.nope = static_cast<int>(nope);
+  a.kv_lora = 512;
+  a.rope = static_cast<int>(rope);
+  a.cp_size = 1;
+  a.err = err_ptr(err);
+  minisgl::launch_mla_prepare(a, stream_of(q));
+}
+
 void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_pe, const at::Tensor& latent,
                    const at::Tensor& page_table, const at::Tensor& req_rows, const at::Tensor& seq_lens,
                    const at::Tensor& cu_q, int64_t page_size, double scale, int64_t splits,
                    const c10::optional<at::Tensor>& part_o, const c10::optional<at::Tensor>& part_lse,
                    const c10::optional<at::Tensor>& err, const c10::optional<at::Tensor>& trace, int64_t cp_size,
-                   int64_t cp_rank, bool combine_only) {
+                   int64_t cp_rank, bool combine_only, bool own_only) {
   check_cuda(q_lat, "q_lat");
   MSG_CHECK(q_lat.dim() == 3 && q_lat.is_contiguous() && q_lat.scalar_type() == at::kBFloat16,
             "mla_attention: q_lat [H, T_pad, kv_lora] bf16 contiguous");
@@ -634,7 +706,9 @@ void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_
   a.scale = static_cast<float>(scale);
   a.cp_size = static_cast<int>(cp_size);
   a.cp_rank = static_cast<int>(cp_rank);
+  a.own_only = own_only ? 1 : 0;
   MSG_CHECK(cp_size >= 1 && cp_rank >= 0 && cp_rank < cp_size, "mla_attention: cp_rank outside [0, cp_size)");
+  MSG_CHECK(!own_only || (combine_only && cp_size > 1), "mla_attention: own_only is a context-parallel combine");
   if (splits > 1 || cp_size > 1) {
     const int64_t parts = splits * cp_size;
     MSG_CHECK(part_o.has_value() && part_lse.has_value() && part_o->scalar_type() == at::kFloat &&
@@ -654,14 +728,26 @@ void mla_attention(at::Tensor out, const at::Tensor& q_lat, const at::Tensor& q_
   else minisgl::launch_mla_attention(a, stream_of(q_lat));
 }
 
-void mla_heads_to_rows(at::Tensor out, const at::Tensor& in, int64_t T) {
+void mla_heads_to_rows(at::Tensor out, const at::Tensor& in, int64_t T, const c10::optional<at::Tensor>& row_map,
+                       const c10::optional<at::Tensor>& err) {
   check_cuda(in, "in");
+  const int64_t hv = in.size(0) * in.size(2);
   MSG_CHECK(in.dim() == 3 && in.is_contiguous() && in.scalar_type() == at::kBFloat16 && out.is_contiguous() &&
-                out.scalar_type() == at::kBFloat16 && out.numel() == T * in.size(0) * in.size(2) && in.size(1) >= T,
-            "mla_heads_to_rows: in [H, T_pad, v] -> out [T, H * v] bf16");
+                out.scalar_type() == at::kBFloat16 && in.size(1) >= T && out.numel() % hv == 0,
+            "mla_heads_to_rows: in [H, T_pad, v] -> out [rows, H * v] bf16");
+  const int64_t out_rows = out.numel() / hv;
+  const int32_t* map = nullptr;
+  if (row_map.has_value()) {
+    check_i32(*row_map, "row_map");
+    MSG_CHECK(row_map->numel() >= T, "mla_heads_to_rows: a row for each of T tokens");
+    map = row_map->data_ptr<int32_t>();
+  } else {
+    MSG_CHECK(out_rows == T, "mla_heads_to_rows: out [T, H * v] without a row map");
+  }
   const c10::cuda::CUDAGuard guard(in.device());
   minisgl::launch_mla_heads_to_rows(out.data_ptr(), in.data_ptr(), static_cast<int>(T), static_cast<int>(in.size(1)),
-                                    static_cast<int>(in.size(0)), static_cast<int>(in.size(2)), stream_of(in));
+                                    static_cast<int>(in.size(0)), static_cast<int>(in.size(2)), map,
+                                    static_cast<int>(out_rows), err_ptr(err), stream_of(in));
 }
 
 // ------------------------------------------------- symmetric heap (IPC) ----
@@ -1192,8 +1278,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("page_table"), py::arg("req_rows"), py::arg("seq_lens"), py::arg("cu_q"), py::arg("page_size"),
         py::arg("scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("err"),
         py::arg("trace") = py::none(), py::arg("cp_size") = 1, py::arg("cp_rank") = 0,
-        py::arg("combine_only") = false);
-  m.def("mla_heads_to_rows", &mla_heads_to_rows);
+        py::arg("combine_only") = false, py::arg("own_only") = false);
+  m.def("mla_store_latent", &mla_store_latent, py::arg("kv_a"), py::arg("norm_w"), py::arg("eps"),
+        py::arg("positions"), py::arg("cos_sin"), py::arg("latent"), py::arg("out_loc"), py::arg("err"),
+        py::arg("cp_size") = 1, py::arg("cp_rank") = 0);
+  m.def("mla_prepare_q", &mla_prepare_q, py::arg("q_pe"), py::arg("xs"), py::arg("q"), py::arg("positions"),
+        py::arg("cos_sin"), py::arg("T_pad"), py::arg("err"));
+  m.def("mla_heads_to_rows", &mla_heads_to_rows, py::arg("out"), py::arg("in"), py::arg("T"),
+        py::arg("row_map") = py::none(), py::arg("err") = py::none());
   m.def("mla_num_splits", [](int64_t T, int64_t H) { return minisgl::mla_num_splits(static_cast<int>(T), static_cast<int>(H)); });
   m.def("symm_create", &symm_create);
   m.def("symm_open", &symm_open);

@@ -73,39 +73,45 @@ __global__ void __launch_bounds__(256) mla_prepare_kernel(MlaPrepareArgs a) {
   pdl_wait();
   const int t = blockIdx.x;
   const int tid = threadIdx.x;
-  __shared__ float red[8];
-  const __nv_bfloat16* kva = reinterpret_cast<const __nv_bfloat16*>(a.kv_a) + static_cast<int64_t>(t) * a.ld_kv_a;
-  // rmsnorm over kv_lora (512): two values per thread
-  float v0 = __bfloat162float(kva[2 * tid]), v1 = __bfloat162float(kva[2 * tid + 1]);
-  float ss = warp_sum(v0 * v0 + v1 * v1);
-  if ((tid & 31) == 0) red[tid >> 5] = ss;
-  __syncthreads();
-  float tot = 0.f;
-#pragma unroll
-  for (int i = 0; i < 8; ++i) tot += red[i];
-  const float rstd = rsqrtf(tot / kLora + a.eps);
-  int64_t slot = a.out_loc[t];
-  // context parallelism: the row lives on the rank owning its 64-key tile,
-  // in that rank's pool at local page (global page) / cp
-  const bool store = a.cp_size <= 1 || (a.positions[t] / kKeys) % a.cp_size == a.cp_rank;
-  if (a.cp_size > 1) slot = (slot / a.page_size / a.cp_size) * a.page_size + slot % a.page_size;
-  __nv_bfloat16* lat = reinterpret_cast<__nv_bfloat16*>(a.latent) + slot * kLat;
-  const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
-  {
-    __nv_bfloat162 o;  // x * rstd * w in fp32, one rounding
-    o.x = __float2bfloat16_rn(v0 * rstd * __bfloat162float(nw[2 * tid]));
-    o.y = __float2bfloat16_rn(v1 * rstd * __bfloat162float(nw[2 * tid + 1]));
-    if (store) *reinterpret_cast<__nv_bfloat162*>(lat + 2 * tid) = o;
-  }
   const float* cs = a.cos_sin + static_cast<int64_t>(a.positions[t]) * kRope;
-  if (store && tid < kRope / 2) {
-    const float c = cs[tid], s = cs[kRope / 2 + tid];
-    const float x0 = __bfloat162float(kva[kLora + 2 * tid]), x1 = __bfloat162float(kva[kLora + 2 * tid + 1]);
-    __nv_bfloat162 o;
-    o.x = __float2bfloat16_rn(x0 * c - x1 * s);
-    o.y = __float2bfloat16_rn(x1 * c + x0 * s);
-    *reinterpret_cast<__nv_bfloat162*>(lat + kLora + 2 * tid) = o;
+  // the two halves run alone when the key rows and the queries are of
+  // different token sets (token-sharded context parallelism); both
+  // conditions are uniform over the CTA
+  if (a.latent != nullptr) {
+    __shared__ float red[8];
+    const __nv_bfloat16* kva = reinterpret_cast<const __nv_bfloat16*>(a.kv_a) + static_cast<int64_t>(t) * a.ld_kv_a;
+    // rmsnorm over kv_lora (512): two values per thread
+    float v0 = __bfloat162float(kva[2 * tid]), v1 = __bfloat162float(kva[2 * tid + 1]);
+    float ss = warp_sum(v0 * v0 + v1 * v1);
+    if ((tid & 31) == 0) red[tid >> 5] = ss;
+    __syncthreads();
+    float tot = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) tot += red[i];
+    const float rstd = rsqrtf(tot / kLora + a.eps);
+    int64_t slot = a.out_loc[t];
+    // context parallelism: the row lives on the rank owning its 64-key tile,
+    // in that rank's pool at local page (global page) / cp
+    const bool store = a.cp_size <= 1 || (a.positions[t] / kKeys) % a.cp_size == a.cp_rank;
+    if (a.cp_size > 1) slot = (slot / a.page_size / a.cp_size) * a.page_size + slot % a.page_size;
+    __nv_bfloat16* lat = reinterpret_cast<__nv_bfloat16*>(a.latent) + slot * kLat;
+    const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
+    {
+      __nv_bfloat162 o;  // x * rstd * w in fp32, one rounding
+      o.x = __float2bfloat16_rn(v0 * rstd * __bfloat162float(nw[2 * tid]));
+      o.y = __float2bfloat16_rn(v1 * rstd * __bfloat162float(nw[2 * tid + 1]));
+      if (store) *reinterpret_cast<__nv_bfloat162*>(lat + 2 * tid) = o;
+    }
+    if (store && tid < kRope / 2) {
+      const float c = cs[tid], s = cs[kRope / 2 + tid];
+      const float x0 = __bfloat162float(kva[kLora + 2 * tid]), x1 = __bfloat162float(kva[kLora + 2 * tid + 1]);
+      __nv_bfloat162 o;
+      o.x = __float2bfloat16_rn(x0 * c - x1 * s);
+      o.y = __float2bfloat16_rn(x1 * c + x0 * s);
+      *reinterpret_cast<__nv_bfloat162*>(lat + kLora + 2 * tid) = o;
+    }
   }
+  if (a.q == nullptr) return;
   // queries: H heads of (nope + 64) values
   const int qk = a.nope + kRope;
   const __nv_bfloat16* q = reinterpret_cast<const __nv_bfloat16*>(a.q) + static_cast<int64_t>(t) * a.ld_q;
@@ -130,16 +136,24 @@ __global__ void __launch_bounds__(256) mla_prepare_kernel(MlaPrepareArgs a) {
   }
 }
 
-// [H, T_pad, v] (the W_UV grouped GEMM output) -> [T, H * v] rows for o_proj.
+// [H, T_pad, v] (the W_UV grouped GEMM output) -> [T, H * v] rows for o_proj;
+// with a row map, token t lands in row row_map[t] of out_rows rows (the
+// rank-major layout a reduce-scatter over context-parallel ranks takes).
 __global__ void __launch_bounds__(128) mla_heads_to_rows_kernel(__nv_bfloat16* out, const __nv_bfloat16* in, int T,
-                                                               int T_pad, int H, int v) {
+                                                               int T_pad, int H, int v, const int32_t* row_map,
+                                                               int out_rows, ErrorSink err) {
   pdl_launch_dependents();
   pdl_wait();
   const int t = blockIdx.x;
+  const int row = row_map != nullptr ? row_map[t] : t;
+  if (row < 0 || row >= out_rows) {
+    if (threadIdx.x == 0) err.report(kErrBadIndex, 901);
+    return;
+  }
   const int n8 = H * v / 8;
   for (int i = threadIdx.x; i < n8; i += blockDim.x) {
     const int h = (i * 8) / v, c = i * 8 - h * v;
-    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(t) * H * v + h * v + c) =
+    *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * H * v + h * v + c) =
         *reinterpret_cast<const uint4*>(in + (static_cast<int64_t>(h) * T_pad + t) * v + c);
   }
 }
@@ -537,13 +551,19 @@ __global__ void __launch_bounds__(kMlaThreads, 1)
   }
 }
 
-// Merge the split-KV partials: grid (T, H), 128 threads x 4 dims.
+// Merge the split-KV partials: grid (T, H), 128 threads x 4 dims. With
+// own_only (token-sharded context parallelism) the normaliser runs over the
+// log-sum-exps of every rank's splits but only this rank's partial outputs
+// are summed: the result is this rank's share of the merged output, and the
+// shares of all ranks add up to it (after any linear map, such as W_UV).
 __global__ void __launch_bounds__(128) mla_combine_kernel(MlaAttnArgs a) {
   pdl_launch_dependents();
   pdl_wait();
   const int t = blockIdx.x, h = blockIdx.y;
   float mx = -INFINITY;
   const int parts = a.splits * (a.cp_size > 1 ? a.cp_size : 1);  // every rank's splits
+  const int own_lo = a.own_only ? a.cp_rank * a.splits : 0;
+  const int own_hi = a.own_only ? own_lo + a.splits : parts;
   for (int s = 0; s < parts; ++s) mx = fmaxf(mx, a.part_lse[(static_cast<int64_t>(s) * a.T + t) * a.H + h]);
   float acc[4] = {0.f, 0.f, 0.f, 0.f};
   float wsum = 0.f;
@@ -552,6 +572,7 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(MlaAttnArgs a) {
     if (lse == -INFINITY) continue;
     const float w = exp2f(lse - mx);
     wsum += w;
+    if (s < own_lo || s >= own_hi) continue;
     const float4 v = *reinterpret_cast<const float4*>(a.part_o + ((static_cast<int64_t>(s) * a.T + t) * a.H + h) * kLora +
                                                       threadIdx.x * 4);
     acc[0] += w * v.x, acc[1] += w * v.y, acc[2] += w * v.z, acc[3] += w * v.w;
@@ -569,7 +590,7 @@ __global__ void __launch_bounds__(128) mla_combine_kernel(MlaAttnArgs a) {
 
 // ---------------------------------------------------------------- host ----
 void launch_mla_prepare(const MlaPrepareArgs& a, cudaStream_t s) {
-  if (a.T <= 0) return;
+  if (a.T <= 0 || (a.latent == nullptr && a.q == nullptr)) return;
   if (a.kv_lora != kLora || a.rope != kRope)
     throw std::runtime_error("minisgl.mla_prepare: the sm_100a kernels take kv_lora_rank 512 and qk_rope_head_dim 64");
   if (a.nope % 2 != 0 || a.T_pad < a.T || a.H <= 0)
@@ -577,11 +598,12 @@ void launch_mla_prepare(const MlaPrepareArgs& a, cudaStream_t s) {
   launch_pdl(mla_prepare_kernel, dim3(a.T), dim3(256), 0, s, a);
 }
 
-void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, cudaStream_t s) {
+void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, const int32_t* row_map,
+                              int out_rows, int* err, cudaStream_t s) {
   if (T <= 0) return;
   if ((H * v) % 8 != 0 || v % 8 != 0) throw std::runtime_error("minisgl.mla_output: v must be a multiple of 8");
   launch_pdl(mla_heads_to_rows_kernel, dim3(T), dim3(128), 0, s, static_cast<__nv_bfloat16*>(out),
-             static_cast<const __nv_bfloat16*>(in), T, T_pad, H, v);
+             static_cast<const __nv_bfloat16*>(in), T, T_pad, H, v, row_map, out_rows, ErrorSink{err});
 }
 
 int mla_num_splits(int T, int H) {

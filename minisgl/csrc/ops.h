@@ -187,6 +187,8 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s);
 
 // ------------------------------------------------------------------ MLA ----
 struct MlaPrepareArgs {
+  // either half may be absent: q == nullptr stores key rows only, latent ==
+  // nullptr prepares queries only
   const void* q;          // [T, H, nope + rope] (token stride ld_q)
   int ld_q;
   const void* kv_a;       // [T, kv_lora + rope] (token stride ld_kv_a)
@@ -224,6 +226,9 @@ struct MlaAttnArgs {
   // t % cp_size == cp_rank and writes partials [cp_size * splits, T, H, ...]
   // at slots cp_rank * splits + split (merged by launch_mla_combine)
   int cp_size, cp_rank;
+  // combine only: sum this rank's partial outputs under the normaliser of
+  // every rank's log-sum-exps (token-sharded context parallelism)
+  int own_only;
   // optional per-tile timestamps (%globaltimer ns) of CTA (0, 0, 0), 8 slots
   // per tile: 0 copy issued, 1 QK issued, 2 scores seen, 3 P written,
   // 4 PV issued, 5 PV seen complete
@@ -232,7 +237,8 @@ struct MlaAttnArgs {
 void launch_mla_prepare(const MlaPrepareArgs& a, cudaStream_t s);
 void launch_mla_attention(const MlaAttnArgs& a, cudaStream_t s);
 void launch_mla_combine(const MlaAttnArgs& a, cudaStream_t s);
-void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, cudaStream_t s);
+void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, const int32_t* row_map,
+                              int out_rows, int* err, cudaStream_t s);
 int mla_num_splits(int T, int H);
 
 // -------------------------------------------------------------- sampling ----

@@ -50,6 +50,17 @@ if TYPE_CHECKING:
     from .config import ModelConfig
 
 
+class _CPComm:
+    """All-reduce over the context-parallel ranks (the whole world: layers
+    see a single tensor-parallel rank under context parallelism)."""
+
+    def all_reduce(self, x: torch.Tensor) -> torch.Tensor:
+        import torch.distributed as dist
+
+        dist.all_reduce(x)
+        return x
+
+
 class MLAAttention(BaseOP):
     def __init__(self, config: "ModelConfig", layer_id: int) -> None:
         tp = get_tp_info().size
@@ -77,6 +88,7 @@ class MLAAttention(BaseOP):
         self._rotary = get_rope(self.rope_dim, self.rope_dim, rc.max_position, rc.base, scaling)
         self._layer_id = layer_id
         self._q_lora = config.q_lora_rank > 0
+        self._comm = _CPComm()
 
     def post_load(self) -> None:
         super().post_load()
@@ -86,23 +98,60 @@ class MLAAttention(BaseOP):
         self._w_uk_t = kv_b[:, : self.nope, :].transpose(1, 2).contiguous()
         self._w_uv = kv_b[:, self.nope :, :].contiguous()
 
+    def _q(self, x: torch.Tensor) -> torch.Tensor:
+        if self._q_lora:
+            return self.q_b_proj.forward(self.q_a_layernorm.forward(self.q_a_proj.forward(x)))
+        return self.q_proj.forward(x)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         ctx = get_global_ctx()
+        backend = ctx.attn_backend
+        if getattr(backend, "cp_size", 1) > 1:
+            return self._forward_cp(x, ctx, backend)
         batch = ctx.batch
         T = x.shape[0]
-        if self._q_lora:
-            q = self.q_b_proj.forward(self.q_a_layernorm.forward(self.q_a_proj.forward(x)))
-        else:
-            q = self.q_proj.forward(x)
+        q = self._q(x)
         kv_a = self.kv_a_proj_with_mqa.forward(x)
-        backend = ctx.attn_backend
         q_lat, q_pe = ops.mla_prepare(q.view(T, self.heads, self.nope + self.rope_dim), kv_a, self._w_uk_t,
                                       self.kv_a_layernorm.weight, self.eps, batch.positions,
                                       self._rotary.cos_sin_cache, ctx.kv_cache.latent(self._layer_id),
-                                      batch.out_loc, ctx.page_size, getattr(backend, "cp_size", 1),
-                                      getattr(backend, "cp_rank", 0))
+                                      batch.out_loc, ctx.page_size)
         o_lat = backend.forward_mla(q_lat, q_pe, self._layer_id, batch)
         return self.o_proj.forward(ops.mla_output(o_lat, self._w_uv, T))
+
+    def _forward_cp(self, x: torch.Tensor, ctx, backend) -> torch.Tensor:
+        """Context parallelism. x holds this rank's rows: the tokens of its
+        own 64-key tiles (plus padding) for a sharded prefill, every token
+        for a decode batch. The rank stores the latent rows of its tiles,
+        builds the queries of every token (for a sharded prefill from the
+        all-gathered query input: q_lora_rank values a token, the narrowest
+        tensor before the heads fan out), attends them over its tiles and
+        maps its share of the output through W_UV; the shares meet in one
+        reduce-scatter back to the owners' rows (one all-reduce when decode
+        rows are replicated), and o_proj runs on the rank's own rows."""
+        batch = ctx.batch
+        plan = batch.attn_metadata.cp_plan
+        kv_a = self.kv_a_proj_with_mqa.forward(x)
+        ops.mla_store_latent(kv_a, self.kv_a_layernorm.weight, self.eps,
+                             plan.positions if plan is not None else batch.positions, self._rotary.cos_sin_cache,
+                             ctx.kv_cache.latent(self._layer_id), plan.out_loc if plan is not None else batch.out_loc,
+                             ctx.page_size, backend.cp_size, backend.cp_rank)
+        if self._q_lora:
+            q_in = self.q_a_layernorm.forward(self.q_a_proj.forward(x))
+            q_up = self.q_b_proj
+        else:
+            q_in, q_up = x, self.q_proj
+        if plan is not None:
+            q_in = plan.gather(q_in)
+        T = q_in.shape[0]
+        q = q_up.forward(q_in).view(T, self.heads, self.nope + self.rope_dim)
+        q_lat, q_pe = ops.mla_prepare_q(q, self._w_uk_t, batch.positions, self._rotary.cos_sin_cache)
+        share = backend.forward_mla(q_lat, q_pe, self._layer_id, batch)
+        if plan is not None:
+            y = plan.reduce_scatter(ops.mla_output(share, self._w_uv, T, plan.row_map, plan.cp * plan.T_max))
+        else:
+            y = self._comm.all_reduce(ops.mla_output(share, self._w_uv, T))
+        return self.o_proj.forward(y)
 
 
 class DeepseekGate(BaseOP):
@@ -163,11 +212,18 @@ class DeepseekModel(BaseOP):
         self.norm = RMSNormFused(config.hidden_size, config.rms_norm_eps)
 
     def forward(self, input_ids: torch.Tensor) -> torch.Tensor:
+        batch = get_global_ctx().batch
+        plan = getattr(batch.attn_metadata, "cp_plan", None)
+        if plan is not None:  # token-sharded prefill: this rank's rows only
+            input_ids = input_ids.index_select(0, plan.local)
         x = self.embed_tokens.forward(input_ids)
         residual: Optional[torch.Tensor] = None
         for layer in self.layers.op_list:
             x, residual = layer.forward(x, residual)
-        return self.norm.forward(x, residual)[0]
+        h = self.norm.forward(x, residual)[0]
+        if plan is not None:  # one row per request for the LM head
+            h = plan.last_rows(h, batch.size)
+        return h
 
 
 class DeepseekV3ForCausalLM(BaseLLMModel):

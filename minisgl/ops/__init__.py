@@ -414,17 +414,51 @@ def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_
     return grouped_gemm(xs, w_uk_t, tile), q_pe
 
 
-def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int) -> torch.Tensor:
+def mla_store_latent(kv_a: torch.Tensor, norm_w: torch.Tensor, eps: float, positions: torch.Tensor,
+                     cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor, page_size: int,
+                     cp_size: int = 1, cp_rank: int = 0) -> None:
+    """The cache half of ``mla_prepare`` alone: latent rows of the tokens of
+    kv_a (under context parallelism only those of this rank's tiles)."""
+    if not kv_a.is_cuda:
+        return ref.mla_store_latent(kv_a, norm_w, eps, positions, cos_sin, latent, out_loc, page_size, cp_size,
+                                    cp_rank)
+    _count()
+    native().mla_store_latent(kv_a, norm_w, eps, positions, cos_sin, latent, out_loc, error_word(kv_a.device),
+                              cp_size, cp_rank)
+
+
+def mla_prepare_q(q: torch.Tensor, w_uk_t: torch.Tensor, positions: torch.Tensor,
+                  cos_sin: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """The query half of ``mla_prepare`` alone: (q_lat [H, T_pad, kv_lora],
+    q_pe [T, H, rope])."""
+    if not q.is_cuda:
+        return ref.mla_prepare_q(q, w_uk_t, positions, cos_sin)
+    T, H, qk = q.shape
+    nope = w_uk_t.shape[2]
+    tile = _group_tile(T)
+    T_pad = (T + tile - 1) // tile * tile
+    xs = torch.empty(H, T_pad, nope, dtype=q.dtype, device=q.device)
+    q_pe = torch.empty(T, H, qk - nope, dtype=q.dtype, device=q.device)
+    _count()
+    native().mla_prepare_q(q_pe, xs, q, positions, cos_sin, T_pad, error_word(q.device))
+    return grouped_gemm(xs, w_uk_t, tile), q_pe
+
+
+def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int, row_map: Optional[torch.Tensor] = None,
+               out_rows: Optional[int] = None) -> torch.Tensor:
     """[H, T_pad, kv_lora] latent attention output -> [T, H * v] through W_UV
     (a grouped GEMM with heads as groups, then a head-major -> row-major
-    copy for o_proj)."""
+    copy for o_proj). With ``row_map`` (int32 [T]) token t lands in row
+    row_map[t] of an [out_rows, H * v] result; rows no token maps to are
+    left unwritten on the GPU (zero on the CPU)."""
     if not o_lat.is_cuda:
-        return ref.mla_output(o_lat, w_uv, T)
+        return ref.mla_output(o_lat, w_uv, T, row_map, out_rows)
     H, T_pad, _ = o_lat.shape
     ys = grouped_gemm(o_lat, w_uv, _group_tile(T))
-    out = torch.empty(T, H * w_uv.shape[1], dtype=o_lat.dtype, device=o_lat.device)
+    rows = T if row_map is None else out_rows
+    out = torch.empty(rows, H * w_uv.shape[1], dtype=o_lat.dtype, device=o_lat.device)
     _count()
-    native().mla_heads_to_rows(out, ys, T)
+    native().mla_heads_to_rows(out, ys, T, row_map, error_word(o_lat.device))
     return out
 
 
@@ -443,9 +477,6 @@ def mla_attention(
     scale: float,
     splits: int = 0,
     trace: Optional[torch.Tensor] = None,
-    cp_size: int = 1,
-    cp_rank: int = 0,
-    cp_group=None,
 ) -> torch.Tensor:
     """Causal absorbed MLA over the paged latent cache of one layer:
     q_lat [H, T_pad, kv_lora] + q_pe [T, H, rope] -> [H, T_pad, kv_lora]
@@ -453,9 +484,6 @@ def mla_attention(
     tokens). ``trace``: optional int64 [512] device tensor that receives
     per-tile phase timestamps of the first CTA (copy issued, QK issued,
     scores seen, P written, PV issued, PV seen complete; 8 slots a tile)."""
-    if cp_size > 1:
-        return _mla_attention_cp(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale,
-                                 splits, cp_size, cp_rank, cp_group)
     if not q_lat.is_cuda:
         return ref.mla_attention(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale)
     H, T_pad, kv_lora = q_lat.shape
@@ -483,11 +511,16 @@ def _mla_partials(parts: int, T: int, H: int, kv_lora: int, device: torch.device
     return buf[: parts * T * H * kv_lora], buf[parts * T * H * kv_lora: need]
 
 
-def _mla_attention_cp(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits, cp_size,
-                      cp_rank, cp_group):
-    """Context-parallel MLA: each rank attends over the 64-key tiles it holds
-    (tile t on rank t % cp), the partial outputs and log-sum-exps of all
-    ranks are all-gathered (in place) and merged."""
+def mla_attention_share(q_lat: torch.Tensor, q_pe: torch.Tensor, latent: torch.Tensor, page_table: torch.Tensor,
+                        req_rows: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor, page_size: int,
+                        scale: float, cp_size: int, cp_rank: int, cp_group, splits: int = 0) -> torch.Tensor:
+    """Context-parallel MLA: this rank attends every query over the 64-key
+    tiles it holds (tile t on rank t % cp) and returns its SHARE of the
+    merged output, [H, T_pad, kv_lora]: its partial output weighted by
+    exp(lse_rank - lse_all). Only the log-sum-exps cross the ranks (one
+    in-place all-gather of [cp * splits, T, H] fp32); the shares add up to
+    the attention output, so the caller reduces them after W_UV, where a
+    token's row is 4x narrower than the latent output (128 vs 512 per head)."""
     import torch.distributed as dist
 
     H, T_pad, kv_lora = q_lat.shape
@@ -495,26 +528,24 @@ def _mla_attention_cp(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q,
     if not q_lat.is_cuda:
         o, lse = ref.mla_attention_partial(q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size,
                                            scale, cp_size, cp_rank)
-        os_ = [torch.empty_like(o) for _ in range(cp_size)]
-        ls_ = [torch.empty_like(lse) for _ in range(cp_size)]
-        dist.all_gather(os_, o.contiguous(), group=cp_group)
-        dist.all_gather(ls_, lse.contiguous(), group=cp_group)
-        merged = ref.merge_partials(torch.stack(os_), torch.stack(ls_)).to(q_lat.dtype)
+        lses = [torch.empty_like(lse) for _ in range(cp_size)]
+        dist.all_gather(lses, lse.contiguous(), group=cp_group)
+        share = ref.mla_share(o, torch.stack(lses), cp_rank).to(q_lat.dtype)
         out = torch.zeros_like(q_lat)
-        out[:, :T] = merged.transpose(0, 1)
+        out[:, :T] = share
         return out
     nat = native()
     splits = splits or max(1, nat.mla_num_splits(T, H) // cp_size)
     part_o, part_lse = _mla_partials(splits * cp_size, T, H, kv_lora, q_lat.device)
     out = torch.empty_like(q_lat)
     _count(2)
+    err = error_word(q_lat.device)
     nat.mla_attention(out, q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits,
-                      part_o, part_lse, error_word(q_lat.device), None, cp_size, cp_rank, False)
-    per_o, per_l = splits * T * H * kv_lora, splits * T * H
-    dist.all_gather_into_tensor(part_o, part_o[cp_rank * per_o:(cp_rank + 1) * per_o], group=cp_group)
+                      part_o, part_lse, err, None, cp_size, cp_rank, False)
+    per_l = splits * T * H
     dist.all_gather_into_tensor(part_lse, part_lse[cp_rank * per_l:(cp_rank + 1) * per_l], group=cp_group)
     nat.mla_attention(out, q_lat, q_pe, latent, page_table, req_rows, seq_lens, cu_q, page_size, scale, splits,
-                      part_o, part_lse, error_word(q_lat.device), None, cp_size, cp_rank, True)
+                      part_o, part_lse, err, None, cp_size, cp_rank, True, True)
     return out
 
 

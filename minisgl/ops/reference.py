@@ -205,36 +205,68 @@ def cp_owned(positions: torch.Tensor, cp_size: int, cp_rank: int) -> torch.Tenso
     return (positions.long() // CP_TILE) % cp_size == cp_rank
 
 
-def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_w: torch.Tensor, eps: float,
-                positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
-                page_size: int, cp_size: int = 1, cp_rank: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+def mla_store_latent(kv_a: torch.Tensor, norm_w: torch.Tensor, eps: float, positions: torch.Tensor,
+                     cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor, page_size: int,
+                     cp_size: int = 1, cp_rank: int = 0) -> None:
     """Latent row [rmsnorm(c_kv) | rope(k_pe)] of every token into the paged
-    cache; returns the absorbed queries as (q_lat [H, T, kv_lora] = q_nope
-    W_UK per head, head-major; q_pe [T, H, rope] rotated). w_uk_t is
-    [H, kv_lora, nope] (W_UK of each head, transposed)."""
-    T, H, qk = q.shape
-    kv_lora = w_uk_t.shape[1]
-    rope = kv_a.shape[1] - kv_lora
-    nope = qk - rope
+    cache; under context parallelism only the rows of this rank's 64-key
+    tiles, at local page (global page) // cp."""
+    kv_lora = norm_w.shape[0]
     c = rmsnorm(kv_a[:, :kv_lora], norm_w, eps)
     k_pe = rope_interleaved(kv_a[:, kv_lora:], positions, cos_sin)
     loc = out_loc.long()
     rows = torch.cat([c, k_pe], dim=-1).to(latent.dtype)
     page = loc // page_size
-    if cp_size > 1:  # the row lives on the rank that owns its 64-key tile, at local page g // cp
+    if cp_size > 1:
         keep = cp_owned(positions, cp_size, cp_rank)
         loc, rows, page = loc[keep], rows[keep], page[keep] // cp_size
     latent[page, loc % page_size] = rows
+
+
+def mla_prepare_q(q: torch.Tensor, w_uk_t: torch.Tensor, positions: torch.Tensor,
+                  cos_sin: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Absorbed queries (q_lat [H, T, kv_lora] = q_nope W_UK per head,
+    head-major; q_pe [T, H, rope] rotated). w_uk_t is [H, kv_lora, nope]
+    (W_UK of each head, transposed)."""
+    nope = w_uk_t.shape[2]
     q_pe = rope_interleaved(q[..., nope:], positions, cos_sin).contiguous()
     q_lat = torch.einsum("thn,hcn->htc", q[..., :nope].float(), w_uk_t.float()).to(q.dtype)
     return q_lat, q_pe
 
 
-def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int) -> torch.Tensor:
+def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_w: torch.Tensor, eps: float,
+                positions: torch.Tensor, cos_sin: torch.Tensor, latent: torch.Tensor, out_loc: torch.Tensor,
+                page_size: int, cp_size: int = 1, cp_rank: int = 0) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Both halves for one token set: the cache rows, then the queries."""
+    mla_store_latent(kv_a, norm_w, eps, positions, cos_sin, latent, out_loc, page_size, cp_size, cp_rank)
+    return mla_prepare_q(q, w_uk_t, positions, cos_sin)
+
+
+def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int, row_map: Optional[torch.Tensor] = None,
+               out_rows: Optional[int] = None) -> torch.Tensor:
     """Latent attention output back to heads: o_lat [H, >= T, kv_lora] x
-    W_UV [H, v, kv_lora] -> [T, H * v]."""
+    W_UV [H, v, kv_lora] -> [T, H * v]; with a row map, token t goes to row
+    row_map[t] of [out_rows, H * v] (other rows zero)."""
     o = torch.einsum("htc,hvc->thv", o_lat[:, :T].float(), w_uv.float())
-    return o.reshape(T, -1).to(o_lat.dtype)
+    o = o.reshape(T, -1).to(o_lat.dtype)
+    if row_map is None:
+        return o
+    out = torch.zeros(out_rows, o.shape[1], dtype=o.dtype, device=o.device)
+    out[row_map.long()] = o
+    return out
+
+
+def mla_share(o_own: torch.Tensor, lse_all: torch.Tensor, rank: int) -> torch.Tensor:
+    """This context-parallel rank's share of the merged attention output:
+    its own partial o_own [T, H, C] weighted by exp(lse_rank - lse_total),
+    where lse_all [R, T, H] holds every rank's log-sum-exp. The shares of
+    all ranks sum to the merged output."""
+    m = lse_all.amax(dim=0)
+    fin = torch.isfinite(m)
+    m0 = torch.where(fin, m, torch.zeros_like(m))
+    w = torch.where(torch.isfinite(lse_all), torch.exp(lse_all - m0), torch.zeros_like(lse_all))
+    share = o_own * (w[rank] / w.sum(0).clamp_min(1e-30))[..., None]
+    return share.transpose(0, 1)
 
 
 def mla_attention_partial(q_lat: torch.Tensor, q_pe: torch.Tensor, latent: torch.Tensor, page_table: torch.Tensor,

@@ -1,12 +1,16 @@
-"""Context parallelism for MLA on CPU ranks (gloo, world size 2): each rank
-keeps the latent rows of the 64-key tiles it owns (tile t on rank t % 2) in
-a pool of half the pages (the allocator gives tile t a page of id = t mod 2),
-attends over them only, and the partial outputs / log-sum-exps of the ranks
-are gathered and merged; the generated tokens equal the single-rank
-engine's. Prompts are longer than one tile so both ranks hold keys."""
+"""Context parallelism for MLA on CPU ranks (gloo, world sizes 2 and 4):
+each rank keeps the latent rows of the 64-key tiles it owns (tile t on rank
+t % cp) in a pool of 1/cp of the pages (the allocator gives tile t a page of
+id = t mod cp) and attends every query over them only. Prefill batches are
+token-sharded (each rank runs the layers on the tokens of its own tiles);
+the ranks' shares of the attention output meet after W_UV. The generated
+tokens equal the single-rank engine's. Prompts are longer than one tile so
+several ranks hold keys, and chunks of 256 tokens put several requests and
+tiles of every rank into one prefill batch."""
 
 import socket
 
+import pytest
 import torch
 import torch.multiprocessing as mp
 
@@ -25,13 +29,23 @@ def _run(rank, world, port, cp, q):
     from minisgl.parallel import DistributedInfo
     from minisgl.utils.synthetic import make_model_dir
 
+    from minisgl.attention import mla as mla_backend
+
+    plans = []  # (batch tokens, rows per rank) of every sharded prefill
+    init = mla_backend.CPShardPlan.__init__
+
+    def record(self, *args, **kwargs):
+        init(self, *args, **kwargs)
+        plans.append((self.T, self.T_max))
+
+    mla_backend.CPShardPlan.__init__ = record
     llm = LLM(make_model_dir("tiny-kimi"), dtype=torch.float32, device="cpu", use_dummy_weight=True,
               tp_info=DistributedInfo(rank, world), page_size=64, num_page_override=64, max_running_req=4,
-              max_seq_len_override=512, max_extend_tokens=64, distributed_port=port, cp_size=cp)
+              max_seq_len_override=512, max_extend_tokens=256, distributed_port=port, cp_size=cp)
     if cp > 1:  # each rank holds one page in cp (plus spares)
         assert llm.engine.kv_cache.pool.shape[1] == llm.engine.num_pages // cp + 2
     outs = llm.generate(PROMPTS, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
-    q.put((rank, [o["token_ids"] for o in outs]))
+    q.put((rank, ([o["token_ids"] for o in outs], plans)))
     llm.shutdown()
 
 
@@ -49,7 +63,14 @@ def _generate(world, cp):
     return results
 
 
-def test_cp2_matches_single_rank():
-    single = _generate(1, 1)[0]
-    cp = _generate(2, 2)
-    assert cp[0] == cp[1] == single
+@pytest.mark.parametrize("cp", [2, 4])
+def test_cp_matches_single_rank(cp):
+    single, plans = _generate(1, 1)[0]
+    assert plans == []
+    got = _generate(cp, cp)
+    for r in range(cp):
+        tokens, plans = got[r]
+        assert tokens == single, (r, tokens, single)
+        # the prefill really was split: some batch ran fewer rows per rank
+        # than it has tokens
+        assert plans and any(t_max < T for T, t_max in plans), plans

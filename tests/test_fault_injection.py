@@ -42,6 +42,9 @@ def _run(rank, world, port, spec, q):
 
 
 def _spawn(spec, expect_reports):
+    """Runs two ranks; waits for the reports of ranks 0 .. expect_reports - 1
+    (a rank outside that set may report too, e.g. when a loaded machine
+    makes it fail before its injected fault; such a report is kept)."""
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
@@ -49,9 +52,10 @@ def _spawn(spec, expect_reports):
     for p in procs:
         p.start()
     reports = {}
+    deadline = time.time() + 240
     try:
-        for _ in range(expect_reports):
-            rank, status, payload, secs = q.get(timeout=180)
+        while any(r not in reports for r in range(expect_reports)):
+            rank, status, payload, secs = q.get(timeout=max(1.0, deadline - time.time()))
             reports[rank] = (status, payload, secs)
     finally:
         for p in procs:

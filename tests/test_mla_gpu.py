@@ -206,6 +206,84 @@ def test_mla_context_parallel_partials_merge(cp, splits):
     _close(out[:, :T].cpu(), want[:, :T].cpu(), 2e-2)
 
 
+def test_mla_store_and_query_halves_match_prepare():
+    """The store-only and query-only halves (token-sharded context
+    parallelism runs them on different token sets) write the same cache rows
+    and queries as the fused prepare, and the row-mapped W_UV output puts
+    token t in row row_map[t]."""
+    g = torch.Generator().manual_seed(5)
+    T, H, page_size = 45, 16, 64
+    bf = lambda t: t.to(torch.bfloat16)  # noqa: E731
+    d = lambda t: t.to(DEV)  # noqa: E731
+    q = bf(torch.randn(T, H, 192, generator=g))
+    kv_a = bf(torch.randn(T, 576, generator=g))
+    w_uk_t = bf(torch.randn(H, 512, 128, generator=g) * 0.05)
+    w_uv = bf(torch.randn(H, 128, 512, generator=g) * 0.05)
+    norm_w = bf(1 + 0.1 * torch.randn(512, generator=g))
+    positions = torch.randint(0, 4000, (T,), generator=g, dtype=torch.int32)
+    cos_sin = torch.randn(4096, 64)
+    out_loc = torch.randperm(4 * page_size, generator=g)[:T].to(torch.int32)
+    lat_a = d(torch.zeros(4, page_size, 576, dtype=torch.bfloat16))
+    lat_b = d(torch.zeros(4, page_size, 576, dtype=torch.bfloat16))
+    ql_a, qpe_a = ops.mla_prepare(d(q), d(kv_a), d(w_uk_t), d(norm_w), 1e-6, d(positions), d(cos_sin), lat_a,
+                                  d(out_loc), page_size)
+    ops.mla_store_latent(d(kv_a), d(norm_w), 1e-6, d(positions), d(cos_sin), lat_b, d(out_loc), page_size)
+    ql_b, qpe_b = ops.mla_prepare_q(d(q), d(w_uk_t), d(positions), d(cos_sin))
+    torch.cuda.synchronize()
+    assert torch.equal(lat_a.cpu(), lat_b.cpu())
+    assert torch.equal(qpe_a.cpu(), qpe_b.cpu())
+    assert torch.equal(ql_a[:, :T].cpu(), ql_b[:, :T].cpu())
+    o_lat = bf(torch.randn(H, ql_a.shape[1], 512, generator=g))
+    row_map = torch.randperm(2 * T, generator=g)[:T].to(torch.int32)
+    got = ops.mla_output(d(o_lat), d(w_uv), T, d(row_map), 2 * T)
+    plain = ops.mla_output(d(o_lat), d(w_uv), T)
+    torch.cuda.synchronize()
+    ops.check_device_errors(torch.device(DEV))
+    assert torch.equal(got[row_map.long().to(DEV)].cpu(), plain.cpu())
+    _close(plain.cpu(), ref.mla_output(o_lat, w_uv, T), 2e-2)
+
+
+@pytest.mark.parametrize("cp,splits", [(2, 1), (4, 2)])
+def test_mla_context_parallel_shares_sum_to_attention(cp, splits):
+    """Each rank's share (its partials under the normaliser of every rank's
+    log-sum-exps, emulated on one GPU: every rank writes its slots of one
+    partial buffer) sums over the ranks to the single-pool attention, and
+    equals the fp32 statement of the share."""
+    lens = [1, 64, 65, 200, 777, 300]
+    H = 64
+    full, pt, rows, sl, cu, q_lat, q_pe = _cp_case(lens, H, cp, seed=10 + cp)
+    scale = 192 ** -0.5
+    d = lambda t: t.to(DEV)  # noqa: E731
+    T = len(lens)
+    T_pad = (T + 15) // 16 * 16
+    ql = torch.zeros(H, T_pad, 512, dtype=torch.bfloat16)
+    ql[:, :T] = q_lat
+    common = (d(pt), d(rows), d(sl), d(cu), 64, scale)
+    want = ops.mla_attention(d(ql), d(q_pe), d(full), *common, splits=1)
+    part_o, part_lse = ops._mla_partials(cp * splits, T, H, 512, torch.device(DEV))
+    nat = ops.native()
+    err = ops.error_word(torch.device(DEV))
+    scratch = torch.empty_like(want)
+    for r in range(cp):
+        local = d(full[r::cp].contiguous())
+        nat.mla_attention(scratch, d(ql), d(q_pe), local, *common, splits, part_o, part_lse, err, None, cp, r, False)
+    total = torch.zeros(H, T_pad, 512, dtype=torch.float32, device=DEV)
+    lse_all = []
+    for r in range(cp):
+        o_r, lse_r = ref.mla_attention_partial(ql, q_pe, full[r::cp].contiguous(), pt, rows, sl, cu, 64, scale, cp, r)
+        lse_all.append(lse_r)
+    for r in range(cp):
+        share = torch.empty_like(want)
+        nat.mla_attention(share, d(ql), d(q_pe), d(full), *common, splits, part_o, part_lse, err, None, cp, r, True,
+                          True)
+        total += share.float()
+        o_r, _ = ref.mla_attention_partial(ql, q_pe, full[r::cp].contiguous(), pt, rows, sl, cu, 64, scale, cp, r)
+        _close(share[:, :T].cpu(), ref.mla_share(o_r, torch.stack(lse_all), r), 2e-2)
+    torch.cuda.synchronize()
+    ops.check_device_errors(torch.device(DEV))
+    _close(total[:, :T].cpu(), want[:, :T].float().cpu(), 3e-2)
+
+
 def test_mla_prepare_context_parallel_stores_owned_rows():
     """Rank 1 of 2 stores the rows of tiles 1 and 3 (global pages 1 and 3)
     at local pages 0 and 1 of its half-size pool, nothing else."""
