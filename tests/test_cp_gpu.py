@@ -1,0 +1,70 @@
+"""Context parallelism on two GPUs (NVLS off): a small Kimi-K2-shape model
+(the latent dims the sm_100a MLA kernels take) served by two CP ranks, with
+token-sharded prefill (NCCL all-gather / reduce-scatter between the layers'
+halves) and replicated decode in CUDA graphs, generates what one GPU
+generates."""
+
+import os
+import random
+import socket
+
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _prompts():
+    rng = random.Random(23)
+    # several 64-key tiles per prompt, so both ranks own keys and tokens
+    return [[rng.randrange(4096) for _ in range(rng.randint(70, 400))] for _ in range(5)]
+
+
+def _run(rank, world, port, q):
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    from minisgl.core import SamplingParams
+    from minisgl.llm import LLM
+    from minisgl.parallel import DistributedInfo
+    from minisgl.utils.synthetic import make_model_dir
+
+    torch.cuda.set_device(rank)
+    llm = LLM(make_model_dir("small-kimi"), dtype=torch.bfloat16, device=f"cuda:{rank}", use_dummy_weight=True,
+              tp_info=DistributedInfo(rank, world), page_size=64, num_page_override=64, max_running_req=8,
+              max_seq_len_override=1024, max_extend_tokens=512, cuda_graph_max_bs=8, distributed_port=port,
+              cp_size=world if world > 1 else 1, distributed_timeout=60)
+    outs = llm.generate(_prompts(), SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True))
+    q.put((rank, [o["token_ids"] for o in outs]))
+    llm.shutdown()
+
+
+def _spawn(world):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_run, args=(r, world, port, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    results = dict(q.get(timeout=400) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    return results
+
+
+def test_cp2_matches_one_gpu():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    one = _spawn(1)[0]
+    two = _spawn(2)
+    assert two[0] == two[1]
+    # bf16 sums in another order (shares reduced over the ranks): a near-tie
+    # may flip a token; a broken split scrambles all of them
+    same = sum(a == b for x, y in zip(one, two[0]) for a, b in zip(x, y))
+    assert same >= 0.8 * sum(len(x) for x in one), (one, two[0])
