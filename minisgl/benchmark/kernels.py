@@ -326,10 +326,15 @@ def bench_gemm_cold(M: int, N: int, K: int, peaks, label: str) -> Dict:
     out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
     ms = _cycle_ms(lambda w_: ops.gemm(x, w_, out=out), ws)
     ms_cublas = _cycle_ms(lambda w_: torch.matmul(x, w_.t(), out=out), ws)
+    # the CTA-pair persistent plan, timed on its own for comparison
+    ms_pair = None
+    if M >= 256 and K % 64 == 0:
+        ms_pair = _cycle_ms(lambda w_: gemm_tune.run_plan(out, x, w_, (ops.GEMM_PAIR, 256, 1)), ws)
     flops, nbytes = 2 * M * N * K, 2 * (M * K + N * K + M * N)
     bound = max(flops / (peaks["tflops"] * 1e9), nbytes / (peaks["hbm_gbs"] * 1e6))
     return {"kernel": f"gemm_cold[{label}]", "M": M, "N": N, "K": K, "plan": gemm_tune.lookup(M, N, K),
             "ms": round(ms, 4), "cublas_ms": round(ms_cublas, 4), "vs_cublas": round(ms_cublas / ms, 3),
+            "pair_ms": None if ms_pair is None else round(ms_pair, 4),
             "GB/s": round(nbytes / ms / 1e6, 1), "TFLOP/s": round(flops / ms / 1e9, 1),
             "frac_roofline": round(bound / ms, 3), "cublas_frac_roofline": round(bound / ms_cublas, 3)}
 
@@ -608,9 +613,9 @@ def main() -> None:
         cases.append((f"gemm[{lab} prefill]", lambda N=N, K=K, lab=lab: bench_gemm(16384, N, K, peaks,
                                                                                  f"{lab} prefill")))
     cases.append(("elementwise", lambda: bench_elementwise(peaks)))
-    # Qwen3-32B projections at TP1 and TP8, decode batch sizes and a prefill chunk
+    # Qwen3-32B projections at TP1 / 2 / 4 / 8, decode batch sizes and a prefill chunk
     H32, I32, d = 5120, 25600, 128
-    for tp in (1, 8):
+    for tp in (1, 2, 4, 8):
         for lab, N, K in (("qkv", (64 + 16) * d // tp, H32), ("o", H32, 64 * d // tp),
                           ("gate_up", 2 * I32 // tp, H32), ("down", H32, I32 // tp)):
             for M in (1, 32, 128, 256, 8192):

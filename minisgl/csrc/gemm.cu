@@ -1034,6 +1034,10 @@ void launch_gemm(const GemmArgs& a, cudaStream_t stream) {
   // persistent tiles: asked for (plan mode 3), or the default for long
   // token batches of a plain GEMM (measured 1.7-2x faster than one tile per
   // CTA at 16k tokens on B200)
+  if (a.force_mode == 5) {  // persistent CTA pairs (256 x 256 tiles, cta_group::2)
+    launch_gemm_pair(a, stream);
+    return;
+  }
   if (a.force_mode == 3 ||
       (a.force_mode == 0 && a.force_splits <= 1 && a.M >= 1024 && gemm_persistent_supported(a))) {
     launch_gemm_persistent(a, stream);

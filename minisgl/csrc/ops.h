@@ -121,6 +121,8 @@ void launch_gemm_streamk(const GemmStreamKArgs& a, cudaStream_t stream);
 // (force_mode 3): plain GEMMs (no fused epilogue) with K % 64 == 0.
 bool gemm_persistent_supported(const GemmArgs& a);
 void launch_gemm_persistent(const GemmArgs& a, cudaStream_t stream);
+bool gemm_pair_supported(const GemmArgs& a);
+void launch_gemm_pair(const GemmArgs& a, cudaStream_t stream);
 // Number of fp32 workspace elements launch_gemm may need for this shape.
 int64_t gemm_workspace_elems(int M, int N, int K);
 

@@ -145,6 +145,8 @@ def gemm(
 # tile-plan mode of the stream-K weight-streaming GEMM (up to 256 tokens,
 # K % 64 == 0); its plan is (GEMM_STREAMK, weight sub-tiles R, k-blocks per stage)
 GEMM_STREAMK = 4
+# persistent 256 x 256 tiles on CTA pairs (cta_group::2 MMAs, K % 64 == 0)
+GEMM_PAIR = 5
 _SK_WORKSPACE: dict = {}
 _SK_SLOT_FLOATS = 2 * 256 * 128
 _SK_FLAG_WORDS = 32

@@ -59,6 +59,11 @@ def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
         # persistent 128 x N-tile CTAs: win on wide outputs such as the LM
         # head (151936 features at 256 rows: 0.106 vs 0.138 ms)
         out += [(3, 256, 1), (3, 128, 1)]
+    if M >= 128 and K % 64 == 0:
+        # persistent 256 x 256 tiles on CTA pairs (cta_group::2): half the
+        # operand traffic per SM; wins some Qwen3-32B shapes (TP1 gate_up at
+        # 256 rows 0.122 vs 0.136 ms, TP2 o_proj at 8192 rows 0.256 vs 0.265)
+        out.append((5, 256, 1))
     if M <= 256 and K % 64 == 0:
         # stream-K weight streaming over every SM, 128 or 256 weight rows per
         # work tile (mode 4: (4, R, k-blocks per stage; 0 = automatic))
@@ -166,7 +171,7 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
 
     native = ops.native()
     fused = dict(fused or {})
-    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only|sample|streamk"
+    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only|sample|streamk|pairs"
     cached = _load(cache_file, key_dev)
     shapes = sorted(set(shapes) | set(fused))
     wanted = sorted(set(int(m) for m in batch_sizes if m > 0))

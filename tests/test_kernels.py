@@ -134,6 +134,24 @@ def test_gemm_persistent(M, N, K, bn, bias, f32):
     _close(out, ref.gemm(x, w, b, torch.float32), atol=2e-2 * math.sqrt(K / 1024) + 1e-2, rtol=1e-2)
 
 
+@pytest.mark.parametrize("M,N,K", [(4096, 6144, 1024), (3000, 1000, 576), (300, 4096, 2048), (1, 512, 64),
+                                   (8192, 1024, 3072)])
+@pytest.mark.parametrize("bias,f32", [(False, False), (True, True)])
+def test_gemm_cta_pairs(M, N, K, bias, f32):
+    """Persistent 256 x 256 tiles on CTA pairs (plan mode 5, cta_group::2
+    MMAs) with ragged edges in M and N, including a pair whose odd CTA's rows
+    all lie past M."""
+    torch.manual_seed(M + N + K + 1)
+    x = torch.randn(M, K, device=DEV, dtype=torch.bfloat16)
+    w = (torch.randn(N, K, device=DEV) * 0.05).to(torch.bfloat16)
+    b = (torch.randn(N, device=DEV) * 0.1).to(torch.bfloat16) if bias else None
+    out = torch.empty(M, N, device=DEV, dtype=torch.float32 if f32 else torch.bfloat16)
+    ops.native().gemm(out, x, w, b, None, 1, ops.GEMM_PAIR, ops.error_word(x.device), 256)
+    torch.cuda.synchronize()
+    ops.check_device_errors(x.device)
+    _close(out, ref.gemm(x, w, b, torch.float32), atol=2e-2 * math.sqrt(K / 1024) + 1e-2, rtol=1e-2)
+
+
 def test_gemm_strided_input_fp32_out():
     torch.manual_seed(1)
     big = torch.randn(50, 3072, device=DEV, dtype=torch.bfloat16)
