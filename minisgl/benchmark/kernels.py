@@ -339,6 +339,36 @@ def bench_gemm_cold(M: int, N: int, K: int, peaks, label: str) -> Dict:
             "frac_roofline": round(bound / ms, 3), "cublas_frac_roofline": round(bound / ms_cublas, 3)}
 
 
+def long_gemm_variants(M: int, N: int, K: int) -> Dict:
+    """Prefill-sized GEMM: the persistent one-SM plan (3, 256, 1), the
+    CTA-pair plan (5, 256, 1) and cuBLAS, each timed back to back in a CUDA
+    graph over two weight copies (best of three replays), then each launched
+    once inside the NVTX range 'measure'."""
+    import os
+
+    from minisgl.ops import gemm_tune
+
+    x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+    ws = [torch.randn(N, K, device="cuda", dtype=torch.bfloat16) * 0.02 for _ in range(2)]
+    out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+    runs = {"persistent": lambda w: gemm_tune.run_plan(out, x, w, (3, 256, 1)),
+            "pair": lambda w: gemm_tune.run_plan(out, x, w, (ops.GEMM_PAIR, 256, 1)),
+            "cublas": lambda w: torch.matmul(x, w.t(), out=out)}
+    res: Dict = {"M": M, "N": N, "K": K, "debug": os.environ.get("MINISGL_GEMM_DEBUG", "0"),
+                 "prefetch": os.environ.get("MINISGL_GEMM_PREFETCH", "0")}
+    for name, run in runs.items():
+        ms = _cycle_ms(run, ws, reps=10)
+        res[f"{name}_ms"] = round(ms, 4)
+        res[f"{name}_tflops"] = round(2 * M * N * K / ms / 1e9, 1)
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_push("measure")
+    for run in runs.values():
+        run(ws[0])
+    torch.cuda.synchronize()
+    torch.cuda.nvtx.range_pop()
+    return res
+
+
 def bench_layer_chain(M: int, peaks, layers: int = 28) -> List[Dict]:
     """The non-attention kernels of one Qwen3-0.6B decode layer (tp1) at M
     tokens, per layer, over ``layers`` weight copies (~0.9 GB, so weights
@@ -564,6 +594,9 @@ def main() -> None:
     p.add_argument("--launch-modes", default="", help="M,N,K,mode,bn,splits[,kps]: eager vs graph launch timing")
     p.add_argument("--probe", default="", help="M,N,K,mode,bn,splits[,kps]: time one forced GEMM tile plan")
     p.add_argument("--trace", action="store_true", help="with --probe: per-CTA phase stamps")
+    p.add_argument("--long-gemms", default="", help="M,N,K: the persistent one-SM and CTA-pair plans and cuBLAS, "
+                   "timed; each launched once more inside an NVTX range 'measure' (for an ncu --nvtx-include "
+                   "capture). MINISGL_GEMM_DEBUG / MINISGL_GEMM_PREFETCH select the kernels' measurement switches")
     p.add_argument("--json", default="")
     p.add_argument("--quick", action="store_true")
     p.add_argument("--only", default="", help="run only cases whose label contains this text")
@@ -572,6 +605,10 @@ def main() -> None:
     if args.launch_modes:
         vals = [int(v) for v in args.launch_modes.split(",")]
         print(json.dumps(probe_launch_modes(*vals[:7])), flush=True)
+        return
+    if args.long_gemms:
+        M, N, K = (int(v) for v in args.long_gemms.split(","))
+        print(json.dumps(long_gemm_variants(M, N, K)), flush=True)
         return
     if args.probe:
         vals = [int(v) for v in args.probe.split(",")]
