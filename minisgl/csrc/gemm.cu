@@ -705,14 +705,17 @@ __global__ void __launch_bounds__(kThreads, 1)
     constexpr int kLd = SWAP ? S::kRedLdSwap : S::kRedLdTok;
     const int nsplit = static_cast<int>(gridDim.z);  // == cluster size along z
     const int rank = static_cast<int>(cluster_ctarank());
-    const int rows_per = kOutRows / nsplit;
+    // rows [row_lo, row_lo + rows_per) of the tile; a split count that does
+    // not divide the rows gives the ranks ragged shares
+    const int row_lo = rank * kOutRows / nsplit;
+    const int rows_per = (rank + 1) * kOutRows / nsplit - row_lo;
     const uint32_t red_base = smem_u32(smem);
     const int tok0 = SWAP ? b_row0 : a_row0;
     const int feat0 = SWAP ? a_row0 : b_row0;
     if (do_norm) {
       // rstd of this rank's rows from every CTA's partial sum of squares
       for (int r = threadIdx.x; r < rows_per; r += kThreads) {
-        const int orow = rank * rows_per + r;
+        const int orow = row_lo + r;
         const uint32_t off = smem_u32(s_ss + orow);
         float ss = 0.f;
         if (nsplit == 1) ss = s_ss[orow];
@@ -728,7 +731,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       constexpr int kBlocks = kOutCols / 128;
       const int vecs = rows_per * kBlocks * 16;
       for (int e = threadIdx.x; e < vecs; e += kThreads) {
-        const int orow = rank * rows_per + e / (kBlocks * 16);
+        const int orow = row_lo + e / (kBlocks * 16);
         const int blk = (e % (kBlocks * 16)) / 16;
         const int ocol = blk * 128 + (e % 16) * 4;
         const float4 g = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol) * 4), nsplit);
@@ -764,7 +767,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // kEpiRope relies on one warp covering one 128-feature head of one
         // token row: kOutCols / 4 is a multiple of 32 vectors per row and
         // kThreads a multiple of 32 (the host asks for N tiles of >= 128)
-        const int orow = rank * rows_per + e / (kOutCols / 4);
+        const int orow = row_lo + e / (kOutCols / 4);
         const int ocol = (e % (kOutCols / 4)) * 4;
         const float4 acc = reduce_parts(red_base + static_cast<uint32_t>((orow * kLd + ocol) * 4), nsplit);
         const int m = tok0 + orow;
@@ -822,7 +825,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (threadIdx.x < p.epi.ar_world) ar_wait(p, ar_flag(p, threadIdx.x, cta), ar_e);
         __syncthreads();
         for (int e = threadIdx.x; e < vecs; e += kThreads) {
-          const int orow = rank * rows_per + e / (kOutCols / 4);
+          const int orow = row_lo + e / (kOutCols / 4);
           const int ocol = (e % (kOutCols / 4)) * 4;
           const int m = tok0 + orow;
           const int n = feat0 + ocol;
@@ -974,7 +977,7 @@ Plan make_plan(int M, int N, int K, int force_mode, int force_splits, int force_
     while (splits < kMaxSplits && pl.tiles * splits * 2 <= kTargetCtas && num_kb / (splits * 2) >= 2) splits *= 2;
   }
   splits = std::max(1, std::min(splits, kMaxSplits));
-  while (splits > 1 && (splits > num_kb || (out_rows % splits) != 0)) splits /= 2;
+  while (splits > 1 && (splits > num_kb || splits > out_rows)) splits /= 2;
   pl.kb_per_split = (num_kb + splits - 1) / splits;
   pl.splits = splits;
   return pl;

@@ -44,15 +44,18 @@ def candidates(M: int, K: int, full: bool = True) -> List[Plan]:
     top = 16
     while top < M and top < 256:
         top *= 2
+    # split counts: powers of two, and 3 / 6 so that a few dozen tiles can
+    # fill the 148 SMs (40 tiles x 3 = 120 CTAs where x 4 would spill over a
+    # second wave); the cluster reduction gives ragged row shares
     for bn in (16, 32, 64, 128, 256):
         if bn > top or (not full and bn < top // 8):
             continue
-        for s in (1, 2, 4, 8, 16):
-            if s <= num_kb and bn % s == 0 and (full or s * 2 <= num_kb):
+        for s in (1, 2, 3, 4, 6, 8, 16):
+            if s <= num_kb and s <= bn and (full or s * 2 <= num_kb):
                 out.append((2, bn, s))
     if M >= (32 if full else 128):
         for bn in (32, 64, 128, 256) if full else (64, 128, 256):
-            for s in (1, 2, 4, 8):
+            for s in (1, 2, 3, 4, 6, 8):
                 if s <= num_kb:
                     out.append((1, bn, s))
     if M >= 64 and K % 64 == 0:
@@ -171,7 +174,7 @@ def tune(shapes: Iterable[Tuple[int, int]], batch_sizes: Iterable[int], device: 
 
     native = ops.native()
     fused = dict(fused or {})
-    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only|sample|streamk|pairs"
+    key_dev = torch.cuda.get_device_name(device) + "|cold-weights|fused-kinds|tcgen05-only|sample|streamk|pairs|splits3"
     cached = _load(cache_file, key_dev)
     shapes = sorted(set(shapes) | set(fused))
     wanted = sorted(set(int(m) for m in batch_sizes if m > 0))
