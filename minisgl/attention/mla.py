@@ -151,6 +151,11 @@ class MLAAttnMetadata(BaseAttnMetadata):
     max_q: int
     last_indices: Optional[torch.Tensor] = None
     cp_plan: Optional[CPShardPlan] = None   # token-sharded prefill under context parallelism
+    # non-absorbed prefill (kv_b expansion of every key, then 192 / 128-dim
+    # attention) when its FLOPs are below the absorbed form's; the key layout
+    # for the GPU kernels (None on the CPU, whose reference needs none)
+    expanded: bool = False
+    prefill_plan: Optional["ops.MlaPrefillPlan"] = None
 
     def get_last_indices(self, bs: int) -> torch.Tensor:
         if self.last_indices is None:
@@ -164,6 +169,8 @@ class MLAAttnBackend(BaseAttnBackend):
         self.heads = div_even(config.num_qo_heads, get_tp_info().size)
         self.kv_lora = config.kv_lora_rank
         self.rope = config.qk_rope_head_dim
+        self.nope = config.qk_nope_head_dim
+        self.v_dim = config.v_head_dim
         self.scale = mla_softmax_scale(config)
         self.page_size = ctx.page_size
         self.kv = ctx.kv_cache
@@ -217,7 +224,27 @@ class MLAAttnBackend(BaseAttnBackend):
                                batch.out_loc, self.device, self.cp_group)
         # a sharded prefill hands the LM head one row per request already
         last = None if batch.is_decode or plan is not None else (cu_q[1:] - 1).long()
-        batch.attn_metadata = MLAAttnMetadata(dev[:B], dev[B : 2 * B], cu_q, max(qlens), last, plan)
+        md = MLAAttnMetadata(dev[:B], dev[B : 2 * B], cu_q, max(qlens), last, plan)
+        if not batch.is_decode and self.cp_size <= 1 and self.expanded_prefill(lens, qlens):
+            md.expanded = True
+            if self.device.type == "cuda":
+                md.prefill_plan = ops.MlaPrefillPlan(lens, self.device)
+        batch.attn_metadata = md
+
+    def expanded_prefill(self, lens: List[int], qlens: List[int]) -> bool:
+        """Whether the non-absorbed form costs fewer FLOPs for this batch: per
+        head, expanding every key through kv_b_proj costs 2 * kv_lora *
+        (nope + v) FLOPs a key, and each query-key pair 2 * (nope + rope + v)
+        instead of 2 * (2 * kv_lora + rope). MINISGL_MLA_PREFILL=absorbed
+        or =expanded forces one form."""
+        import os
+
+        force = os.environ.get("MINISGL_MLA_PREFILL", "")
+        if force in ("absorbed", "expanded"):
+            return force == "expanded"
+        pairs = sum(n * L for n, L in zip(qlens, lens))
+        expand = 2 * self.kv_lora * (self.nope + self.v_dim) * sum(lens)
+        return expand + 2 * (self.nope + self.rope + self.v_dim) * pairs < 2 * (2 * self.kv_lora + self.rope) * pairs
 
     def init_capture_graph(self, max_seq_len: int, bs_list: List[int]) -> None:
         n = max(bs_list)

@@ -176,6 +176,23 @@ def trace_prefill_attention(B: int = 1, L: int = 16384, hq: int = 16, hk: int = 
         ops.prefill_attention(q, pool, 0, pt, rows, seq, cu, L, hq, hk, d, page, d ** -0.5, trace=tr)
     torch.cuda.synchronize()
     t = tr.view(64, 8).cpu().tolist()
+    if os.environ.get("MINISGL_PREFILL_PAIR", "1") != "0" and (hq // hk) % 2 == 0:
+        # head-pair kernel slots: 0 / 4 scores seen (head 0 / 1), 1 scores
+        # loaded, 2 exps done, 3 / 5 P handed over, 6 / 7 MMA thread saw P
+        pair = {
+            "period": lambda i: t[i][3] - t[i - 1][3],
+            "scores_seen_to_loaded": lambda i: t[i][1] - t[i][0],
+            "loaded_to_exps_done": lambda i: t[i][2] - t[i][1],
+            "exps_done_to_p_handed": lambda i: t[i][3] - t[i][2],
+            "p_handed_to_mma_sees_p": lambda i: t[i][6] - t[i][3],
+            "p_handed_to_next_scores": lambda i: t[i + 1][0] - t[i][3],
+            "head1_p_after_head0_p": lambda i: t[i][5] - t[i][3],
+            "head0_scores_after_head1_p": lambda i: t[i + 1][0] - t[i][5],
+        }
+        out = {"trace": "prefill_attention (head pairs)", "B": B, "L": L, "hq": hq, "hk": hk}
+        for k, f in pair.items():
+            out[k + "_ns"] = statistics.median(f(i) for i in range(4, 59))
+        return out
     # slots: 0 copy issued, 1 QK issued, 2 scores ready, 7 scores loaded, 3 exps done,
     # 4 PV(i - 2) done, 5 P written, 6 PV issued
     phases = {

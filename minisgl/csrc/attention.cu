@@ -554,6 +554,13 @@ constexpr int kTcThreads = 32 * (kTcSoftmaxWarps + 2);
 constexpr int kTcRedBytes = 2 * 2 * kTcRows * 4;    // row-max exchange: [tile parity][half][row] fp32
 constexpr int kTcSmem = 1024 + 2 * kTcQChunk + kTcStages * kStageBytes + 256 + kTcRedBytes;
 static_assert(kTcSmem <= 227 * 1024, "prefill smem over the per-CTA limit");
+// The rope variant (non-absorbed MLA prefill): a third 64-dim Q chunk (the
+// rotated query rope part) and, per key tile, the keys' shared 64-dim rope
+// rows next to K and V; one stage less to fit.
+constexpr int kRopeTileBytes = kTile * 128;
+constexpr int kTcRopeStages = kTcStages - 1;
+constexpr int kTcRopeSmem = 1024 + 3 * kTcQChunk + kTcRopeStages * (kStageBytes + kRopeTileBytes) + 256 + kTcRedBytes;
+static_assert(kTcRopeSmem <= 227 * 1024, "rope prefill smem over the per-CTA limit");
 constexpr float kTcRescaleLog2 = 8.f;
 
 // 2^x on the special-function unit (PTX ex2.approx.ftz: relative error of a
@@ -564,19 +571,85 @@ __device__ __forceinline__ float ex2_fast(float x) {
   return y;
 }
 
+// Packed fp32 pairs (sm_100 f32x2 arithmetic: one instruction for two lanes
+// of work) for the softmax inner loop.
+__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float& a, float& b) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
+}
+__device__ __forceinline__ float max3(float a, float b, float c) {
+  float d;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(d) : "f"(a), "f"(b), "f"(c));
+  return d;
+}
+
+// 2^x for a pair of arguments on the FMA pipe, to take part of a softmax's
+// exponentials off the special-function unit (which otherwise bounds it).
+// Method: x = n + f with n = round(x) (adding and subtracting 1.5 * 2^23
+// rounds to the nearest integer and leaves n in the low mantissa bits),
+// f in [-1/2, 1/2]; 2^f by a cubic fitted here for minimal relative error
+// on [-1/2, 1/2] (Lawson-weighted least squares; max relative error 7.5e-5,
+// far below the 2^-8 of the bf16 P it feeds); 2^n added to the exponent
+// field as n << 23. Arguments are clamped at -126 so that field stays in
+// range: 2^-126 and below all come out as about 1e-38 instead of 0, which
+// adds nothing measurable to a softmax whose largest term is at least 1.
+__device__ __forceinline__ void exp2_poly_pair(uint64_t x2, float& y0, float& y1) {
+  constexpr float kRound = 12582912.f;  // 1.5 * 2^23
+  float x0, x1;
+  f2_unpack(x2, x0, x1);
+  x2 = f2_pack(fmaxf(x0, -126.f), fmaxf(x1, -126.f));
+  const uint64_t t = f2_add(x2, f2_pack(kRound, kRound));
+  const uint64_t r = f2_add(t, f2_pack(-kRound, -kRound));
+  const uint64_t f = f2_fma(r, f2_pack(-1.f, -1.f), x2);
+  uint64_t q = f2_fma(f, f2_pack(0.05517132f, 0.05517132f), f2_pack(0.24261054f, 0.24261054f));
+  q = f2_fma(q, f, f2_pack(0.69326097f, 0.69326097f));
+  q = f2_fma(q, f, f2_pack(0.99992812f, 0.99992812f));
+  float q0, q1, t0, t1;
+  f2_unpack(q, q0, q1);
+  f2_unpack(t, t0, t1);
+  y0 = __uint_as_float(__float_as_uint(q0) + (__float_as_uint(t0) << 23));
+  y1 = __uint_as_float(__float_as_uint(q1) + (__float_as_uint(t1) << 23));
+}
+
+// kRope: the non-absorbed MLA prefill form. Scores are q_nope . k_nope (the
+// two 64-dim chunks of the usual path, with q heads a.q_head_stride
+// elements apart in a q row) plus q_rope . k_rope, the rotated 64-dim rope
+// parts: the query's from its own [T, hq, 64] tensor (map tm_qr), the key's
+// shared by every head and read per key tile from [slots, 64] rows at the
+// same page-table slots as K and V (map tm_kr). V and the output keep 128
+// dims.
+template <bool kRope>
 __global__ void __launch_bounds__(kTcThreads, 1)
     prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                           const __grid_constant__ CUtensorMap tm_qr, const __grid_constant__ CUtensorMap tm_kr,
                            AttnArgs a) {
+  constexpr int kQC = kRope ? 3 : 2;                    // 64-dim Q chunks in shared memory
+  constexpr int kSt = kRope ? kTcRopeStages : kTcStages;
+  constexpr int kStage = kStageBytes + (kRope ? kRopeTileBytes : 0);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
   uint8_t* sQ = smem;
-  uint8_t* sKV = sQ + 2 * kTcQChunk;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kTcStages * kStageBytes);
+  uint8_t* sKV = sQ + kQC * kTcQChunk;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kSt * kStage);
   uint64_t* q_full = bars;
-  uint64_t* kv_full = bars + 1;               // [kTcStages]
-  uint64_t* kv_empty = kv_full + kTcStages;   // [kTcStages]
-  uint64_t* s_full = kv_empty + kTcStages;    // [2] score buffers
+  uint64_t* kv_full = bars + 1;               // [kSt]
+  uint64_t* kv_empty = kv_full + kSt;         // [kSt]
+  uint64_t* s_full = kv_empty + kSt;          // [2] score buffers
   uint64_t* s_free = s_full + 2;              // [2]
   uint64_t* p_full = s_free + 2;              // [2] P of tiles with j % 2 == h written
   uint64_t* o_done = p_full + 2;              // [2] PV of tiles with j % 2 == h complete (P_h free)
@@ -607,7 +680,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
   if (threadIdx.x == 0) {
     mbar_init(q_full, 1);
-    for (int i = 0; i < kTcStages; ++i) {
+    for (int i = 0; i < kSt; ++i) {
       mbar_init(&kv_full[i], 1);
       mbar_init(&kv_empty[i], 1);
     }
@@ -622,6 +695,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     fence_barrier_init();
     prefetch_tmap(&tm_kv);
     prefetch_tmap(&tm_q);
+    if (kRope) {
+      prefetch_tmap(&tm_qr);
+      prefetch_tmap(&tm_kr);
+    }
   }
   if (warp == kTcIssuer) {
     tmem_alloc(tmem_slot, 512);
@@ -636,11 +713,13 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   if (warp == kTcProducer) {
     // ------------------------------------------------------------ TMA ----
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * kTcQChunk);
+      mbar_arrive_expect_tx(q_full, kQC * kTcQChunk);
       // rows past the last query token read the next request's rows (or the
       // zero fill past the end); their results are never stored
-      tma_load_2d(sQ, &tm_q, q_full, qh * kD, q_begin + row0);
-      tma_load_2d(sQ + kTcQChunk, &tm_q, q_full, qh * kD + 64, q_begin + row0);
+      const int qx = qh * (a.q_head_stride > 0 ? a.q_head_stride : kD);
+      tma_load_2d(sQ, &tm_q, q_full, qx, q_begin + row0);
+      tma_load_2d(sQ + kTcQChunk, &tm_q, q_full, qx + 64, q_begin + row0);
+      if (kRope) tma_load_2d(sQ + 2 * kTcQChunk, &tm_qr, q_full, qh * 64, q_begin + row0);
       // page ids of tile j + 1 are read while tile j waits for its stage, so
       // no copy waits on a page-table load
       const int P = a.page_size;
@@ -655,17 +734,17 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       };
       read_pages(cur, 0);
       for (int j = 0; j < n; ++j) {
-        const int s = j % kTcStages;
+        const int s = j % kSt;
         read_pages(nxt, j + 1);
-        if (j >= kTcStages && !mbar_wait(&kv_empty[s], ((j / kTcStages) - 1) & 1, err, 231)) {
+        if (j >= kSt && !mbar_wait(&kv_empty[s], ((j / kSt) - 1) & 1, err, 231)) {
           atomicExch(s_abort, 1);
           break;
         }
         if (*reinterpret_cast<volatile int*>(s_abort)) break;
         ++issued;
         stamp(j, 0);
-        uint8_t* st = sKV + s * kStageBytes;
-        mbar_arrive_expect_tx(&kv_full[s], kStageBytes);
+        uint8_t* st = sKV + s * kStage;
+        mbar_arrive_expect_tx(&kv_full[s], kStage);
         const int64_t in_page = P < kTile ? 0 : (j * kTile) % P;
 #pragma unroll
         for (int q = 0; q < kTile / 16; ++q) {
@@ -678,6 +757,9 @@ __global__ void __launch_bounds__(kTcThreads, 1)
           tma_load_2d(st + kHalfBytes + o, &tm_kv, &kv_full[s], 64, rk);
           tma_load_2d(st + kTileBytes + o, &tm_kv, &kv_full[s], 0, rv);
           tma_load_2d(st + kTileBytes + kHalfBytes + o, &tm_kv, &kv_full[s], 64, rv);
+          if (kRope)  // the keys' rope rows: one 64-dim row per slot
+            tma_load_2d(st + kStageBytes + o, &tm_kr, &kv_full[s], 0,
+                        static_cast<int32_t>(static_cast<int64_t>(cur[q]) * P + in_page));
         }
 #pragma unroll
         for (int q = 0; q < kTile / 16; ++q) cur[q] = nxt[q];
@@ -691,7 +773,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     const uint32_t q_addr = smem_u32(sQ), kv_addr = smem_u32(sKV);
     bool ok = __all_sync(0xffffffffu, mbar_wait(q_full, 0, err, 232));
     auto qk = [&](int j) {  // S[j % 2] = Q . K_j^T
-      const uint32_t st = kv_addr + (j % kTcStages) * kStageBytes;
+      const uint32_t st = kv_addr + (j % kSt) * kStage;
       const uint32_t d = tmem + kTcSCol + (j % 2) * kTile;
 #pragma unroll
       for (int c = 0; c < 2; ++c)
@@ -699,15 +781,21 @@ __global__ void __launch_bounds__(kTcThreads, 1)
         for (int k = 0; k < 4; ++k)
           tc_mma_f16(d, make_sdesc_k_sw128(q_addr + c * kTcQChunk + k * 32),
                      make_sdesc_k_sw128(st + c * kHalfBytes + k * 32), idesc_qk, (c | k) != 0 ? 1u : 0u);
+      if (kRope) {  // + q_rope . k_rope
+#pragma unroll
+        for (int k = 0; k < 4; ++k)
+          tc_mma_f16(d, make_sdesc_k_sw128(q_addr + 2 * kTcQChunk + k * 32),
+                     make_sdesc_k_sw128(st + kStageBytes + k * 32), idesc_qk, 1u);
+      }
       tc_commit(&s_full[j % 2]);
     };
     auto pv = [&](int i) {  // O += P_i . V_i
-      const uint32_t v = kv_addr + (i % kTcStages) * kStageBytes + kTileBytes;
+      const uint32_t v = kv_addr + (i % kSt) * kStage + kTileBytes;
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk)  // 16 keys = 8 TMEM columns of P per MMA
         tc_mma_f16_ta(tmem, tmem + kTcPCol + (i % 2) * (kTile / 2) + kk * 8,
                       make_sdesc_mn_sw128(v + kk * 2048, kHalfBytes), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-      tc_commit(&kv_empty[i % kTcStages]);
+      tc_commit(&kv_empty[i % kSt]);
       tc_commit(&o_done[i % 2]);
     };
     int qn = 0, pn = 0;  // next QK, next PV
@@ -720,7 +808,7 @@ __global__ void __launch_bounds__(kTcThreads, 1)
       // only after PV(pn), leaving the softmax of tile pn + 1 without scores
       int choice = 0;
       if (lane == 0) {
-        if (qn < n && qn <= pn + 1 && mbar_test_wait(&kv_full[qn % kTcStages], (qn / kTcStages) & 1) &&
+        if (qn < n && qn <= pn + 1 && mbar_test_wait(&kv_full[qn % kSt], (qn / kSt) & 1) &&
             (qn < 2 || mbar_test_wait(&s_free[qn % 2], ((qn / 2) - 1) & 1)))
           choice = 2;
         else if (pn < qn && mbar_try_wait(&p_full[pn % 2], (pn / 2) & 1)) choice = 1;
@@ -895,8 +983,8 @@ __global__ void __launch_bounds__(kTcThreads, 1)
     // after an abort, let the copies still in flight land before the CTA
     // leaves (bounded waits; the normal path never gets here)
     mbar_wait(q_full, 0, err, 238);
-    for (int j = max(0, issued - kTcStages); j < issued; ++j)
-      mbar_wait(&kv_full[j % kTcStages], (j / kTcStages) & 1, err, 239);
+    for (int j = max(0, issued - kSt); j < issued; ++j)
+      mbar_wait(&kv_full[j % kSt], (j / kSt) & 1, err, 239);
   }
   if (warp == kTcIssuer) {
     tc_fence_after();
@@ -924,6 +1012,7 @@ constexpr int kPrSCol = 256;
 constexpr int kPrQCol = 384;
 constexpr int kPrProducer = 8, kPrIssuer = 9;
 constexpr int kPrThreads = 32 * 10;
+constexpr int kPrPolyPairs = 3;  // of every 8 exponent pairs, computed on the FMA pipe
 constexpr int kPrSmem = 1024 + kPrStages * kStageBytes + 256;
 static_assert(kPrSmem <= 227 * 1024, "head-pair prefill smem over the per-CTA limit");
 
@@ -958,6 +1047,14 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   const int h = qh0 / (a.hq / a.hk);  // both heads of the pair share this KV head
   const int n = (cached + min(q_len, row0 + kTcRows) - 1) / kTile + 1;
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+  // optional per-tile phase stamps of CTA (0, 0, 0) (the longest key range
+  // of request 0's first head pair), 8 slots a tile: 0 / 4 scores seen by
+  // head 0 / 1, 1 scores loaded, 2 exps done, 3 / 5 P handed over by head
+  // 0 / 1, 6 / 7 the MMA thread saw P of head 0 / 1
+  unsigned long long* trace = (a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && b == 0) ? a.trace : nullptr;
+  auto stamp = [&](int i, int slot) {
+    if (trace != nullptr && i < 64) trace[i * 8 + slot] = globaltimer_ns();
+  };
 
   if (threadIdx.x == 0) {
     for (int i = 0; i < kPrStages; ++i) {
@@ -1066,6 +1163,7 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       const bool more = i + 1 < n;
       ok = wait(&p_full[0], i & 1, 254);
       if (!ok) break;
+      if (lane == 0) stamp(i, 6);
       tc_fence_after();
       if (lane == 0) pv(0, i);
       __syncwarp();
@@ -1078,6 +1176,7 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       }
       ok = wait(&p_full[1], i & 1, 256);
       if (!ok) break;
+      if (lane == 0) stamp(i, 7);
       tc_fence_after();
       if (lane == 0) {
         pv(1, i);
@@ -1124,11 +1223,14 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[hh], i & 1, err, 257) &&
                                        !*reinterpret_cast<volatile int*>(s_abort));  // uniform over the warp
       if (!ok) break;
+      const bool stamper = lane == 0 && quad == 0;
+      if (stamper) stamp(i, hh == 0 ? 0 : 4);
       tc_fence_after();
       uint32_t sv[kTile];
       tmem_ld_32x32b_x32(s_col, *reinterpret_cast<uint32_t(*)[32]>(sv));
       tmem_ld_32x32b_x32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
       tc_wait_ld();
+      if (stamper && hh == 0) stamp(i, 1);
       // causal and length mask: keys [0, lim) of the tile are visible to this row
       const int lim = min(pos + 1, L) - i * kTile;
       if (lim < kTile) {
@@ -1136,12 +1238,18 @@ __global__ void __launch_bounds__(kPrThreads, 1)
         for (int j = 0; j < kTile; ++j)
           if (j >= lim) sv[j] = __float_as_uint(-INFINITY);
       }
+      // row max: four independent chains of 3-input max
       float m4[4];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) m4[c] = __uint_as_float(sv[c]);
+      for (int c = 0; c < 4; ++c) m4[c] = fmaxf(__uint_as_float(sv[2 * c]), __uint_as_float(sv[2 * c + 1]));
 #pragma unroll
-      for (int j = 4; j < kTile; ++j) m4[j & 3] = fmaxf(m4[j & 3], __uint_as_float(sv[j]));
-      const float mt = fmaxf(fmaxf(m4[0], m4[1]), fmaxf(m4[2], m4[3])) * sl2;
+      for (int j = 8; j < kTile; j += 8) {
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          m4[c] = max3(m4[c], __uint_as_float(sv[j + 2 * c]), __uint_as_float(sv[j + 2 * c + 1]));
+      }
+      static_assert(kTile % 8 == 0, "row max reads the tile in groups of 8");
+      const float mt = max3(m4[0], m4[1], fmaxf(m4[2], m4[3])) * sl2;
       // lazy rescale: the running max moves only when it grows by more than
       // 2^kTcRescaleLog2, so P stays below that bound in bf16
       const bool grow = mt > m_run + kTcRescaleLog2;
@@ -1165,22 +1273,40 @@ __global__ void __launch_bounds__(kPrThreads, 1)
           tmem_st_32x32b_x32(o_col + 32 * c, ov);
         }
       }
-      // P = 2^(s * scale * log2 e - m) as bf16 pairs over the first 32 score columns
+      // P = 2^(s * scale * log2 e - m) as bf16 pairs over the first 32 score
+      // columns; arguments and sums in packed pairs, and 3 pairs in 8 take
+      // the FMA-pipe exponential so the special-function unit is not the
+      // bound of the loop
       uint32_t pk[kTile / 2];
-      float ps[4] = {0.f, 0.f, 0.f, 0.f};
+      const uint64_t sl2x2 = f2_pack(sl2, sl2), negm = f2_pack(-m_run, -m_run);
+      uint64_t ps2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll
       for (int e = 0; e < kTile / 2; ++e) {
-        const float lo = ex2_fast(fmaf(__uint_as_float(sv[2 * e]), sl2, -m_run));
-        const float hi = ex2_fast(fmaf(__uint_as_float(sv[2 * e + 1]), sl2, -m_run));
-        ps[e & 3] += lo + hi;
+        const uint64_t x2 = f2_fma(f2_pack(__uint_as_float(sv[2 * e]), __uint_as_float(sv[2 * e + 1])), sl2x2, negm);
+        float lo, hi;
+        if (kPrPolyPairs > 0 && (e % 8) < kPrPolyPairs) {
+          exp2_poly_pair(x2, lo, hi);
+        } else {
+          float x0, x1;
+          f2_unpack(x2, x0, x1);
+          lo = ex2_fast(x0);
+          hi = ex2_fast(x1);
+        }
+        ps2[e & 1] = f2_add(ps2[e & 1], f2_pack(lo, hi));
         pk[e] = pack_bf16x2(lo, hi);
       }
-      l_sum += (ps[0] + ps[1]) + (ps[2] + ps[3]);
+      {
+        float a0, a1;
+        f2_unpack(f2_add(ps2[0], ps2[1]), a0, a1);
+        l_sum += a0 + a1;
+      }
+      if (stamper && hh == 0) stamp(i, 2);
       tmem_st_32x32b_x32(s_col, pk);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[hh]);
+      if (stamper) stamp(i, hh == 0 ? 3 : 5);
     }
     // ------------------------------------------------------- epilogue ----
     if (!ok && lane == 0) atomicExch(s_abort, 1);
@@ -1298,17 +1424,46 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
     int dev = 0;
     cudaGetDevice(&dev);
     if (!attr_set[dev & 63]) {
-      cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
+      cudaFuncSetAttribute(prefill_attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcSmem);
       attr_set[dev & 63] = true;
     }
     const CUtensorMap tq = make_tmap_bf16_2d_sw128(a.q, a.q_rows, static_cast<uint64_t>(a.hq) * kD, a.ld_q, kTcRows);
     dim3 grid((a.max_q + kTcRows - 1) / kTcRows, a.hq, a.B);
-    launch_pdl(prefill_attn_tc_kernel, grid, dim3(kTcThreads), kTcSmem, s, tm, tq, a);
+    // the rope maps are unused in this variant: the Q map stands in for them
+    launch_pdl(prefill_attn_tc_kernel<false>, grid, dim3(kTcThreads), kTcSmem, s, tm, tq, tq, tq, a);
     return;
   }
   set_smem_once<1>(prefill_attn_kernel);
   dim3 grid((a.max_q + 63) / 64, a.hq, a.B);
   launch_pdl(prefill_attn_kernel, grid, dim3(128), kAttnSmem, s, tm, a);
+}
+
+void launch_mla_prefill_attention(const AttnArgs& a, cudaStream_t s) {
+  if (a.B <= 0 || a.max_q <= 0) return;
+  check_args(a);
+  if (a.q_rope == nullptr || a.k_rope == nullptr || a.q_rows <= 0 || a.q_head_stride < kD ||
+      a.q_head_stride % 8 != 0)
+    throw std::runtime_error("minisgl.mla_prefill_attention: q heads of >= 128 values (multiple of 8), "
+                             "q_rope and k_rope are required");
+  if (reinterpret_cast<uintptr_t>(a.q) % 16 != 0 || a.ld_q % 8 != 0 ||
+      reinterpret_cast<uintptr_t>(a.q_rope) % 16 != 0 || reinterpret_cast<uintptr_t>(a.k_rope) % 16 != 0)
+    throw std::runtime_error("minisgl.mla_prefill_attention: 16-byte aligned q / q_rope / k_rope rows");
+  static bool attr_set[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (!attr_set[dev & 63]) {
+    cudaFuncSetAttribute(prefill_attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, kTcRopeSmem);
+    attr_set[dev & 63] = true;
+  }
+  const CUtensorMap tm = pool_map(a);
+  const CUtensorMap tq =
+      make_tmap_bf16_2d_sw128(a.q, a.q_rows, static_cast<uint64_t>(a.hq) * a.q_head_stride, a.ld_q, kTcRows);
+  const CUtensorMap tqr = make_tmap_bf16_2d_sw128(a.q_rope, a.q_rows, static_cast<uint64_t>(a.hq) * 64,
+                                                  static_cast<uint64_t>(a.hq) * 64, kTcRows);
+  const uint32_t seg = a.page_size < kTile ? a.page_size : kTile;
+  const CUtensorMap tkr = make_tmap_bf16_2d_sw128(a.k_rope, a.rope_rows, 64, 64, seg);
+  dim3 grid((a.max_q + kTcRows - 1) / kTcRows, a.hq, a.B);
+  launch_pdl(prefill_attn_tc_kernel<true>, grid, dim3(kTcThreads), kTcRopeSmem, s, tm, tq, tqr, tkr, a);
 }
 
 }  // namespace minisgl

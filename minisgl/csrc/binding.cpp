@@ -1062,6 +1062,107 @@ void prefill_attention(const at::Tensor& q, at::Tensor out, const at::Tensor& kv
   minisgl::launch_prefill_attention(a, stream_of(q));
 }
 
+// Keys of a prefill batch gathered for the kv_b expansion (row_req / row_pos
+// give each compact row's request and position; -1 pads).
+void mla_gather_keys(at::Tensor x, at::Tensor k_rope, const at::Tensor& latent, const at::Tensor& page_table,
+                     const at::Tensor& req_rows, const at::Tensor& row_req, const at::Tensor& row_pos,
+                     const c10::optional<at::Tensor>& err) {
+  check_cuda(latent, "latent");
+  check_i32(page_table, "page_table");
+  check_i32(req_rows, "req_rows");
+  check_i32(row_req, "row_req");
+  check_i32(row_pos, "row_pos");
+  const int64_t R = row_req.numel();
+  MSG_CHECK(latent.scalar_type() == at::kBFloat16 && latent.is_contiguous() && latent.size(-1) == 576,
+            "mla_gather_keys: latent [pages, page, 576] bf16");
+  MSG_CHECK(x.is_contiguous() && x.scalar_type() == at::kBFloat16 && x.numel() == R * 512,
+            "mla_gather_keys: x [R, 512] bf16");
+  MSG_CHECK(k_rope.is_contiguous() && k_rope.scalar_type() == at::kBFloat16 && k_rope.numel() == R * 64,
+            "mla_gather_keys: k_rope [R, 64] bf16");
+  MSG_CHECK(row_pos.numel() == R && page_table.dim() == 2 && page_table.stride(1) == 1,
+            "mla_gather_keys: row_pos of R rows, int32 page table");
+  const c10::cuda::CUDAGuard guard(latent.device());
+  minisgl::launch_mla_gather_keys(x.data_ptr(), k_rope.data_ptr(), latent.data_ptr(), latent.numel() / 576,
+                                  page_table.data_ptr<int32_t>(), static_cast<int>(page_table.stride(0)),
+                                  req_rows.data_ptr<int32_t>(), row_req.data_ptr<int32_t>(),
+                                  row_pos.data_ptr<int32_t>(), static_cast<int>(R), err_ptr(err), stream_of(latent));
+}
+
+void mla_scatter_kv(at::Tensor pool, const at::Tensor& y, int64_t H) {
+  check_cuda(y, "y");
+  MSG_CHECK(y.scalar_type() == at::kBFloat16 && y.is_contiguous() && y.dim() == 2 && y.size(1) == H * 256,
+            "mla_scatter_kv: y [R, H * 256] bf16");
+  const int64_t R = y.size(0);
+  MSG_CHECK(pool.scalar_type() == at::kBFloat16 && pool.is_contiguous() && pool.numel() == 2 * R * H * 128,
+            "mla_scatter_kv: pool [2, R / 64, H, 64, 128] bf16");
+  const c10::cuda::CUDAGuard guard(y.device());
+  minisgl::launch_mla_scatter_kv(pool.data_ptr(), y.data_ptr(), static_cast<int>(R), static_cast<int>(H),
+                                 stream_of(y));
+}
+
+// Rotated query rope parts only: q_pe [T, H, rope] from q [T, H, nope + rope].
+void mla_rope_q(at::Tensor q_pe, const at::Tensor& q, const at::Tensor& positions, const at::Tensor& cos_sin,
+                const c10::optional<at::Tensor>& err) {
+  check_cuda(q, "q");
+  MSG_CHECK(q.dim() == 3 && q.stride(2) == 1 && q.stride(1) == q.size(2) && q.scalar_type() == at::kBFloat16,
+            "mla_rope_q: q [T, H, nope + rope] bf16 with packed heads");
+  const int64_t T = q.size(0), H = q.size(1), rope = q_pe.size(2), nope = q.size(2) - rope;
+  MSG_CHECK(q_pe.is_contiguous() && q_pe.size(0) == T && q_pe.size(1) == H, "mla_rope_q: q_pe [T, H, rope]");
+  MSG_CHECK(cos_sin.scalar_type() == at::kFloat && cos_sin.is_contiguous() && cos_sin.size(1) == rope,
+            "mla_rope_q: fp32 cos_sin [max_pos, rope]");
+  check_i32(positions, "positions");
+  MSG_CHECK(positions.numel() >= T, "mla_rope_q: positions of T tokens");
+  const c10::cuda::CUDAGuard guard(q.device());
+  minisgl::MlaPrepareArgs a{};
+  a.q = q.data_ptr();
+  a.ld_q = static_cast<int>(q.stride(0));
+  a.positions = positions.data_ptr<int32_t>();
+  a.cos_sin = cos_sin.data_ptr<float>();
+  a.q_pe = q_pe.data_ptr();
+  a.T = static_cast<int>(T);
+  a.T_pad = static_cast<int>(T);
+  a.H = static_cast<int>(H);
+  a.nope = static_cast<int>(nope);
+  a.kv_lora = 512;
+  a.rope = static_cast<int>(rope);
+  a.cp_size = 1;
+  a.err = err_ptr(err);
+  minisgl::launch_mla_prepare(a, stream_of(q));
+}
+
+// Non-absorbed MLA prefill: q [T, hq * qk] (q_nope first in each head),
+// q_rope [T, hq, 64] rotated, K_nope / V expanded into kv_pool
+// [2, 1, pages, hq, page, 128] and the keys' rope rows k_rope [slots, 64],
+// both at the slots of page_table; out [T, hq * 128].
+void mla_prefill_attention(const at::Tensor& q, at::Tensor out, const at::Tensor& kv_pool,
+                           const at::Tensor& page_table, const at::Tensor& req_rows, const at::Tensor& seq_lens,
+                           const at::Tensor& cu_q, int64_t max_q, int64_t hq, int64_t qk, int64_t page_size,
+                           double scale, const at::Tensor& q_rope, const at::Tensor& k_rope,
+                           const c10::optional<at::Tensor>& err) {
+  auto a = attn_common(q, out, kv_pool, 0, page_table, req_rows, seq_lens, hq, hq, 128, page_size, scale);
+  MSG_CHECK(q.size(1) == hq * qk && qk >= 128 + 64, "mla_prefill_attention: q [T, hq * (nope + rope)]");
+  check_cuda(q_rope, "q_rope");
+  check_cuda(k_rope, "k_rope");
+  MSG_CHECK(q_rope.scalar_type() == at::kBFloat16 && q_rope.is_contiguous() && q_rope.numel() == q.size(0) * hq * 64,
+            "mla_prefill_attention: q_rope [T, hq, 64] bf16 contiguous");
+  MSG_CHECK(k_rope.scalar_type() == at::kBFloat16 && k_rope.is_contiguous() && k_rope.dim() == 2 &&
+                k_rope.size(1) == 64,
+            "mla_prefill_attention: k_rope [slots, 64] bf16 contiguous");
+  MSG_CHECK(k_rope.size(0) >= kv_pool.size(2) * page_size, "mla_prefill_attention: k_rope covers every slot");
+  check_i32(cu_q, "cu_q");
+  MSG_CHECK(cu_q.numel() == a.B + 1, "cu_q must have B + 1 entries");
+  a.cu_q = cu_q.data_ptr<int32_t>();
+  a.max_q = static_cast<int>(max_q);
+  a.q_rows = static_cast<int>(q.size(0));
+  a.q_head_stride = static_cast<int>(qk);
+  a.q_rope = q_rope.data_ptr();
+  a.k_rope = k_rope.data_ptr();
+  a.rope_rows = k_rope.size(0);
+  a.err = err_ptr(err);
+  const c10::cuda::CUDAGuard guard(q.device());
+  minisgl::launch_mla_prefill_attention(a, stream_of(q));
+}
+
 // --------------------------------------------------------------- sampling
 void argmax(at::Tensor out, const at::Tensor& logits) {
   check_cuda(logits, "logits");
@@ -1279,6 +1380,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("scale"), py::arg("splits"), py::arg("part_o"), py::arg("part_lse"), py::arg("err"),
         py::arg("trace") = py::none(), py::arg("cp_size") = 1, py::arg("cp_rank") = 0,
         py::arg("combine_only") = false, py::arg("own_only") = false);
+  m.def("mla_prefill_attention", &mla_prefill_attention);
+  m.def("mla_gather_keys", &mla_gather_keys);
+  m.def("mla_scatter_kv", &mla_scatter_kv);
+  m.def("mla_rope_q", &mla_rope_q);
   m.def("mla_store_latent", &mla_store_latent, py::arg("kv_a"), py::arg("norm_w"), py::arg("eps"),
         py::arg("positions"), py::arg("cos_sin"), py::arg("latent"), py::arg("out_loc"), py::arg("err"),
         py::arg("cp_size") = 1, py::arg("cp_rank") = 0);

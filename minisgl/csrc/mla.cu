@@ -123,7 +123,8 @@ __global__ void __launch_bounds__(256) mla_prepare_kernel(MlaPrepareArgs a) {
     const int j = 2 * (i - h * (qk / 2));  // even column inside the head
     const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(q + h * qk + j);
     if (j < a.nope) {
-      *reinterpret_cast<__nv_bfloat162*>(xs + (static_cast<int64_t>(h) * a.T_pad + t) * a.nope + j) = v;
+      if (xs != nullptr)  // absent when only the rotated rope part is wanted
+        *reinterpret_cast<__nv_bfloat162*>(xs + (static_cast<int64_t>(h) * a.T_pad + t) * a.nope + j) = v;
     } else {
       const int r = (j - a.nope) / 2;
       const float c = cs[r], s = cs[kRope / 2 + r];
@@ -156,6 +157,53 @@ __global__ void __launch_bounds__(128) mla_heads_to_rows_kernel(__nv_bfloat16* o
     *reinterpret_cast<uint4*>(out + static_cast<int64_t>(row) * H * v + h * v + c) =
         *reinterpret_cast<const uint4*>(in + (static_cast<int64_t>(h) * T_pad + t) * v + c);
   }
+}
+
+// ------------------------------------------------ non-absorbed prefill ----
+// Latent rows of every key of a prefill batch in a compact page-aligned order:
+// row r holds (request row_req[r], position row_pos[r]) and reads that key's
+// cache slot (rows with row_req < 0 pad a request to whole pages and read
+// slot 0; the attention masks them). c_kv (512) goes to x [R, 512], the kv_b
+// GEMM input, and the rotated rope part (64) to k_rope [R, 64]. One warp per
+// row.
+__global__ void __launch_bounds__(256) mla_gather_keys_kernel(__nv_bfloat16* x, __nv_bfloat16* k_rope,
+                                                             const __nv_bfloat16* latent, const int32_t* page_table,
+                                                             int ld_pt, const int32_t* req_rows,
+                                                             const int32_t* row_req, const int32_t* row_pos, int R,
+                                                             int64_t num_slots, ErrorSink err) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int r = blockIdx.x * 8 + (threadIdx.x >> 5), lane = threadIdx.x & 31;
+  if (r >= R) return;
+  const int b = row_req[r];
+  int64_t slot = b < 0 ? 0 : page_table[static_cast<int64_t>(req_rows[b]) * ld_pt + row_pos[r]];
+  if (slot < 0 || slot >= num_slots) {
+    if (lane == 0) err.report(kErrBadIndex, 911);
+    slot = 0;
+  }
+  const uint4* src = reinterpret_cast<const uint4*>(latent + slot * kLat);
+  uint4* dx = reinterpret_cast<uint4*>(x + static_cast<int64_t>(r) * kLora);
+  dx[lane] = src[lane];
+  dx[lane + 32] = src[lane + 32];
+  if (lane < 8) reinterpret_cast<uint4*>(k_rope + static_cast<int64_t>(r) * kRope)[lane] = src[64 + lane];
+}
+
+// kv_b_proj output y [R, H * 256] (per head 128 k_nope values, then 128 v)
+// into the prefill attention's pool layout [2, R / 64, H, 64, 128]: row r at
+// page r / 64, position r % 64. One warp per (row, head).
+__global__ void __launch_bounds__(256) mla_scatter_kv_kernel(__nv_bfloat16* pool, const __nv_bfloat16* y, int R,
+                                                            int H) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t w = static_cast<int64_t>(blockIdx.x) * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (w >= static_cast<int64_t>(R) * H) return;
+  const int r = static_cast<int>(w / H), h = static_cast<int>(w % H);
+  const int64_t plane = static_cast<int64_t>(R) * H * 128;  // elements of the K plane
+  const int64_t dst = ((static_cast<int64_t>(r / 64) * H + h) * 64 + r % 64) * 128;
+  const uint4 v = reinterpret_cast<const uint4*>(y + (static_cast<int64_t>(r) * H + h) * 256)[lane];
+  // lanes 0-15: k_nope (128 values), 16-31: v
+  reinterpret_cast<uint4*>(pool + (lane < 16 ? 0 : plane) + dst)[lane & 15] = v;
 }
 
 // ---------------------------------------------------------- attention ----
@@ -604,6 +652,23 @@ void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H
   if ((H * v) % 8 != 0 || v % 8 != 0) throw std::runtime_error("minisgl.mla_output: v must be a multiple of 8");
   launch_pdl(mla_heads_to_rows_kernel, dim3(T), dim3(128), 0, s, static_cast<__nv_bfloat16*>(out),
              static_cast<const __nv_bfloat16*>(in), T, T_pad, H, v, row_map, out_rows, ErrorSink{err});
+}
+
+void launch_mla_gather_keys(void* x, void* k_rope, const void* latent, int64_t num_slots, const int32_t* page_table,
+                            int ld_pt, const int32_t* req_rows, const int32_t* row_req, const int32_t* row_pos, int R,
+                            int* err, cudaStream_t s) {
+  if (R <= 0) return;
+  launch_pdl(mla_gather_keys_kernel, dim3((R + 7) / 8), dim3(256), 0, s, static_cast<__nv_bfloat16*>(x),
+             static_cast<__nv_bfloat16*>(k_rope), static_cast<const __nv_bfloat16*>(latent), page_table, ld_pt,
+             req_rows, row_req, row_pos, R, num_slots, ErrorSink{err});
+}
+
+void launch_mla_scatter_kv(void* pool, const void* y, int R, int H, cudaStream_t s) {
+  if (R <= 0) return;
+  if (R % 64 != 0) throw std::runtime_error("minisgl.mla_scatter_kv: rows must fill whole pages of 64");
+  const int64_t warps = static_cast<int64_t>(R) * H;
+  launch_pdl(mla_scatter_kv_kernel, dim3(static_cast<unsigned>((warps + 7) / 8)), dim3(256), 0, s,
+             static_cast<__nv_bfloat16*>(pool), static_cast<const __nv_bfloat16*>(y), R, H);
 }
 
 int mla_num_splits(int T, int H) {

@@ -183,9 +183,18 @@ struct AttnArgs {
   int* err;
   int q_rows;                // prefill: rows of q (the TMA map extent); 0 selects the kernel without Q TMA
   unsigned long long* trace; // optional [64 tiles x 8] %globaltimer stamps of one prefill CTA (profiling)
+  // non-absorbed MLA prefill (launch_mla_prefill_attention): q heads are
+  // q_head_stride elements apart in a q row (their first 128 are q_nope),
+  // q_rope [q_rows, hq, 64] holds the rotated query rope parts and k_rope
+  // [rope_rows, 64] the keys' shared rope rows at the page-table slots
+  int q_head_stride;
+  const void* q_rope;
+  const void* k_rope;
+  int64_t rope_rows;
 };
 void launch_decode_attention(const AttnArgs& a, cudaStream_t s);
 void launch_prefill_attention(const AttnArgs& a, cudaStream_t s);
+void launch_mla_prefill_attention(const AttnArgs& a, cudaStream_t s);
 
 // ------------------------------------------------------------------ MLA ----
 struct MlaPrepareArgs {
@@ -242,6 +251,10 @@ void launch_mla_combine(const MlaAttnArgs& a, cudaStream_t s);
 void launch_mla_heads_to_rows(void* out, const void* in, int T, int T_pad, int H, int v, const int32_t* row_map,
                               int out_rows, int* err, cudaStream_t s);
 int mla_num_splits(int T, int H);
+void launch_mla_gather_keys(void* x, void* k_rope, const void* latent, int64_t num_slots, const int32_t* page_table,
+                            int ld_pt, const int32_t* req_rows, const int32_t* row_req, const int32_t* row_pos, int R,
+                            int* err, cudaStream_t s);
+void launch_mla_scatter_kv(void* pool, const void* y, int R, int H, cudaStream_t s);
 
 // -------------------------------------------------------------- sampling ----
 // logits fp32 [B, V] (row stride ld); writes int32 token ids.

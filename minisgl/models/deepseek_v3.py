@@ -8,7 +8,10 @@ Per layer (HF names kept, so DeepSeek-V3 / Kimi-K2 checkpoints load):
   q LoRA), [T, heads, qk_nope + qk_rope]; kv_a_proj_with_mqa(x) gives the
   compressed KV (kv_lora_rank, normalised by kv_a_layernorm) and one shared
   positional key (qk_rope). The latent row [c_kv | rope(k_pe)] is cached.
-  Attention runs in the absorbed form: q_nope goes into the latent space
+  Prefill batches whose keys are long enough run the non-absorbed form
+  (every key's c_kv expanded through kv_b_proj into per-head k_nope / v,
+  then 192 / 128-dim attention: ``ops.mla_prefill_attention``); decode and
+  short prefills run the absorbed form: q_nope goes into the latent space
   through W_UK (the first qk_nope rows of each head of kv_b_proj), scores are
   q_lat . c_kv + q_pe . k_pe, the latent output comes back through W_UV (the
   last v_head_dim rows) and o_proj. RoPE is DeepSeek's interleaved (GPT-J)
@@ -112,6 +115,19 @@ class MLAAttention(BaseOP):
         T = x.shape[0]
         q = self._q(x)
         kv_a = self.kv_a_proj_with_mqa.forward(x)
+        md = batch.attn_metadata
+        if getattr(md, "expanded", False):
+            # non-absorbed prefill: the new latent rows into the cache, then
+            # attention over every key expanded through kv_b_proj
+            ops.mla_store_latent(kv_a, self.kv_a_layernorm.weight, self.eps, batch.positions,
+                                 self._rotary.cos_sin_cache, ctx.kv_cache.latent(self._layer_id), batch.out_loc,
+                                 ctx.page_size)
+            qh = q.view(T, self.heads, self.nope + self.rope_dim)
+            q_rope = ops.mla_rope_q(qh, self.rope_dim, batch.positions, self._rotary.cos_sin_cache)
+            o = ops.mla_prefill_attention(qh, q_rope, ctx.kv_cache.latent(self._layer_id), ctx.page_table,
+                                          md.req_rows, md.seq_lens, md.cu_q, md.max_q, self.kv_b_proj.weight,
+                                          self.nope, self.v_dim, ctx.page_size, backend.scale, md.prefill_plan)
+            return self.o_proj.forward(o)
         q_lat, q_pe = ops.mla_prepare(q.view(T, self.heads, self.nope + self.rope_dim), kv_a, self._w_uk_t,
                                       self.kv_a_layernorm.weight, self.eps, batch.positions,
                                       self._rotary.cos_sin_cache, ctx.kv_cache.latent(self._layer_id),

@@ -9,7 +9,7 @@ falling back. CPU tensors run the fp32 PyTorch restatement in
 from __future__ import annotations
 
 import functools
-from typing import Optional, Tuple
+from typing import List, Optional, Tuple
 
 import torch
 
@@ -461,6 +461,95 @@ def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int, row_map: Optiona
     out = torch.empty(rows, H * w_uv.shape[1], dtype=o_lat.dtype, device=o_lat.device)
     _count()
     native().mla_heads_to_rows(out, ys, T, row_map, error_word(o_lat.device))
+    return out
+
+
+class MlaPrefillPlan:
+    """Host-built layout of a prefill batch's keys for the non-absorbed MLA
+    path: every request's keys (cached and new) in a compact order padded to
+    whole pages of 64, with the page table of that order and each compact
+    row's (request, position) for the gather. Built once per batch; used by
+    every layer."""
+
+    PAGE = 64
+
+    def __init__(self, lens: List[int], device: torch.device) -> None:
+        import numpy as np
+
+        P = self.PAGE
+        pages = [(L + P - 1) // P for L in lens]
+        base = np.concatenate([[0], np.cumsum(pages)]).astype(np.int64)
+        self.rows = int(base[-1]) * P                       # R: compact key rows
+        width = max(P, max(pages) * P)
+        table = np.zeros((len(lens), width), dtype=np.int32)
+        row_req = np.full(self.rows, -1, dtype=np.int32)
+        row_pos = np.zeros(self.rows, dtype=np.int32)
+        for b, L in enumerate(lens):
+            start = int(base[b]) * P
+            table[b, :pages[b] * P] = start + np.arange(pages[b] * P, dtype=np.int32)
+            row_req[start:start + L] = b
+            row_pos[start:start + L] = np.arange(L, dtype=np.int32)
+        host = torch.from_numpy(np.concatenate([table.reshape(-1), row_req, row_pos]))
+        if device.type == "cuda":
+            host = host.pin_memory()
+        dev = host.to(device, non_blocking=True)
+        n = table.size
+        self.page_table = dev[:n].view(len(lens), width)
+        self.rows_in_order = torch.arange(len(lens), dtype=torch.int32, device=device)
+        self.row_req = dev[n:n + self.rows]
+        self.row_pos = dev[n + self.rows:]
+
+
+def mla_rope_q(q: torch.Tensor, rope: int, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+    """Rotated rope parts [T, H, rope] of q [T, H, nope + rope] (no W_UK
+    absorption): the non-absorbed prefill's queries keep q_nope as it is."""
+    if not q.is_cuda:
+        return ref.mla_rope_q(q, rope, positions, cos_sin)
+    T, H, _ = q.shape
+    q_pe = torch.empty(T, H, rope, dtype=q.dtype, device=q.device)
+    _count()
+    native().mla_rope_q(q_pe, q, positions, cos_sin, error_word(q.device))
+    return q_pe
+
+
+def mla_prefill_attention(q: torch.Tensor, q_rope: torch.Tensor, latent: torch.Tensor, page_table: torch.Tensor,
+                          req_rows: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor, max_q: int,
+                          w_kv_b: torch.Tensor, nope: int, v_dim: int, page_size: int, scale: float,
+                          plan: Optional[MlaPrefillPlan] = None) -> torch.Tensor:
+    """Non-absorbed causal MLA for prefill: q [T, H, nope + rope] (q_nope as
+    projected), q_rope [T, H, rope] rotated -> [T, H * v_dim].
+
+    On the GPU: gather every key's latent row of the batch (``plan`` order),
+    expand c_kv through kv_b_proj with the tcgen05 GEMM into per-head
+    k_nope / v, lay them out as a paged pool, and run the prefill attention
+    kernel with the 64-dim rope part as a third Q chunk and a per-tile
+    k_rope tile. Per query-key pair and head that is 2 * (192 + 128) FLOPs
+    against 2 * (576 + 512) for the absorbed form, for an expansion of
+    2 * 512 * H * 256 FLOPs per key once per layer."""
+    T, H, qk = q.shape
+    kv_lora = latent.shape[-1] - (qk - nope)
+    if not q.is_cuda:
+        return ref.mla_prefill_attention(q, q_rope, latent, page_table, req_rows, seq_lens, cu_q, w_kv_b, kv_lora,
+                                         nope, v_dim, page_size, scale)
+    if nope != 128 or v_dim != 128 or qk - nope != 64 or kv_lora != 512:
+        raise ValueError("the sm_100a MLA prefill kernel takes nope 128, rope 64, v 128 and kv_lora 512")
+    if plan is None:
+        plan = MlaPrefillPlan(seq_lens.tolist(), q.device)
+    nat = native()
+    err = error_word(q.device)
+    R = plan.rows
+    x = torch.empty(R, kv_lora, dtype=q.dtype, device=q.device)
+    k_rope = torch.empty(R, 64, dtype=q.dtype, device=q.device)
+    _count()
+    nat.mla_gather_keys(x, k_rope, latent, page_table, req_rows, plan.row_req, plan.row_pos, err)
+    y = gemm(x, w_kv_b)                                           # [R, H * 256]
+    pool = torch.empty(2, 1, R // MlaPrefillPlan.PAGE, H, MlaPrefillPlan.PAGE, 128, dtype=q.dtype, device=q.device)
+    _count()
+    nat.mla_scatter_kv(pool, y, H)
+    out = torch.empty(T, H * v_dim, dtype=q.dtype, device=q.device)
+    _count()
+    nat.mla_prefill_attention(q.reshape(T, H * qk), out, pool, plan.page_table, plan.rows_in_order, seq_lens, cu_q,
+                              max_q, H, qk, MlaPrefillPlan.PAGE, scale, q_rope, k_rope, err)
     return out
 
 

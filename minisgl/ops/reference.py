@@ -242,6 +242,44 @@ def mla_prepare(q: torch.Tensor, kv_a: torch.Tensor, w_uk_t: torch.Tensor, norm_
     return mla_prepare_q(q, w_uk_t, positions, cos_sin)
 
 
+def mla_rope_q(q: torch.Tensor, rope: int, positions: torch.Tensor, cos_sin: torch.Tensor) -> torch.Tensor:
+    """The rotated rope part [T, H, rope] of q [T, H, nope + rope]."""
+    return rope_interleaved(q[..., q.shape[-1] - rope:], positions, cos_sin).contiguous()
+
+
+def mla_prefill_attention(q: torch.Tensor, q_rope: torch.Tensor, latent: torch.Tensor, page_table: torch.Tensor,
+                          req_rows: torch.Tensor, seq_lens: torch.Tensor, cu_q: torch.Tensor, w_kv_b: torch.Tensor,
+                          kv_lora: int, nope: int, v_dim: int, page_size: int, scale: float) -> torch.Tensor:
+    """Non-absorbed causal MLA for prefill: every key's c_kv goes through
+    kv_b_proj (w_kv_b [H * (nope + v), kv_lora], per head nope rows then v
+    rows) into per-head k_nope / v; scores are q_nope . k_nope + q_rope .
+    k_rope (the key's cached, rotated rope part, shared by the heads);
+    returns [T, H * v] in q's dtype (fp32 math)."""
+    T, H, qk = q.shape
+    rope = qk - nope
+    out = torch.zeros(T, H, v_dim, dtype=torch.float32, device=q.device)
+    w = w_kv_b.float().view(H, nope + v_dim, kv_lora)
+    flat = latent.reshape(-1, latent.shape[-1])
+    rows, lens, cu = req_rows.tolist(), seq_lens.tolist(), cu_q.tolist()
+    for b, (row, L) in enumerate(zip(rows, lens)):
+        s, e = cu[b], cu[b + 1]
+        n = e - s
+        if n == 0 or L <= 0:
+            continue
+        kv = flat[page_table[row, :L].long()].float()               # [L, kv_lora + rope]
+        k_nope = torch.einsum("lc,hnc->lhn", kv[:, :kv_lora], w[:, :nope])
+        v = torch.einsum("lc,hvc->lhv", kv[:, :kv_lora], w[:, nope:])
+        k_rope = kv[:, kv_lora:kv_lora + rope]
+        qb = q[s:e].float()
+        scores = (torch.einsum("nhd,lhd->hnl", qb[..., :nope], k_nope)
+                  + torch.einsum("nhd,ld->hnl", q_rope[s:e].float(), k_rope)) * scale
+        qpos = torch.arange(L - n, L, device=q.device)
+        mask = torch.arange(L, device=q.device)[None, :] > qpos[:, None]
+        p = torch.softmax(scores.masked_fill(mask[None], float("-inf")), dim=-1)
+        out[s:e] = torch.einsum("hnl,lhv->nhv", p, v)
+    return out.reshape(T, H * v_dim).to(q.dtype)
+
+
 def mla_output(o_lat: torch.Tensor, w_uv: torch.Tensor, T: int, row_map: Optional[torch.Tensor] = None,
                out_rows: Optional[int] = None) -> torch.Tensor:
     """Latent attention output back to heads: o_lat [H, >= T, kv_lora] x

@@ -37,3 +37,4 @@ def test_latent_cache_is_one_row_per_token(llm):
     cfg = llm.engine.model_config
     assert pool.latent(0).shape[-1] == cfg.kv_lora_rank + cfg.qk_rope_head_dim
     assert pool.v_cache(0).shape[-1] == cfg.kv_lora_rank
+

@@ -119,8 +119,10 @@ def test_mla_prepare_and_output_match_reference():
     _close(got.cpu(), want, 2e-2)
 
 
-@pytest.mark.parametrize("cuda_graph", [False, True])
-def test_small_kimi_engine_matches_oracle(cuda_graph):
+@pytest.mark.parametrize("cuda_graph,prefill", [(False, "auto"), (True, "auto"), (True, "expanded")])
+def test_small_kimi_engine_matches_oracle(cuda_graph, prefill, monkeypatch):
+    if prefill == "expanded":  # the non-absorbed prefill for every prefill batch
+        monkeypatch.setenv("MINISGL_MLA_PREFILL", "expanded")
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
     from minisgl.models.oracle import greedy_generate
@@ -145,6 +147,44 @@ def test_small_kimi_engine_matches_oracle(cuda_graph):
     # bf16 engine vs fp32 oracle: a near-tie of the random-init logits may
     # flip a token and the sequence then diverges; a broken kernel scrambles all
     assert firsts >= 3 and same >= 0.6 * 24, (firsts, same)
+
+
+@pytest.mark.parametrize("H", [16, 64])
+def test_mla_prefill_expanded_matches_reference(H):
+    """Non-absorbed MLA prefill on the GPU (gather, kv_b expansion GEMM,
+    scatter into the pool layout, 192 / 128-dim attention kernel) against the
+    fp32 statement; requests with cached prefixes, several 128-row query
+    tiles and partial pages."""
+    g = torch.Generator().manual_seed(H)
+    page, kv_lora, rope, nope, v = 64, 512, 64, 128, 128
+    lens, qlens = [1, 70, 300, 700, 129], [1, 70, 20, 700, 64]
+    pages = sum((L + page - 1) // page for L in lens) + 2
+    latent = (torch.randn(pages, page, kv_lora + rope, generator=g) * 0.5).to(torch.bfloat16)
+    perm = torch.randperm(pages, generator=g).tolist()
+    pt = torch.zeros(len(lens) + 1, 768, dtype=torch.int32)
+    rows = []
+    for b, L in enumerate(lens):
+        row = len(lens) - b  # rows deliberately not equal to b
+        rows.append(row)
+        for p in range(0, L, page):
+            pg = perm.pop()
+            n = min(page, L - p)
+            pt[row, p:p + n] = pg * page + torch.arange(n, dtype=torch.int32)
+    T = sum(qlens)
+    q = (torch.randn(T, H, nope + rope, generator=g)).to(torch.bfloat16)
+    q_rope = (torch.randn(T, H, rope, generator=g)).to(torch.bfloat16)
+    w = (torch.randn(H * (nope + v), kv_lora, generator=g) * 0.05).to(torch.bfloat16)
+    i32 = lambda x: torch.tensor(x, dtype=torch.int32)  # noqa: E731
+    rows_t, seq = i32(rows), i32(lens)
+    cu = i32([0] + torch.tensor(qlens).cumsum(0).tolist())
+    scale = 192 ** -0.5
+    want = ref.mla_prefill_attention(q, q_rope, latent, pt, rows_t, seq, cu, w, kv_lora, nope, v, page, scale)
+    d = lambda t: t.to(DEV)  # noqa: E731
+    got = ops.mla_prefill_attention(d(q), d(q_rope), d(latent), d(pt), d(rows_t), d(seq), d(cu), max(qlens), d(w),
+                                    nope, v, page, scale)
+    torch.cuda.synchronize()
+    ops.check_device_errors(torch.device(DEV))
+    _close(got.cpu(), want, 3e-2)
 
 
 def _cp_case(lens, H, cp, seed):
