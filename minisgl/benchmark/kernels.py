@@ -239,6 +239,56 @@ def bench_mla_decode(B: int, L: int, H: int, page: int, peaks) -> Dict:
             "frac_tensor": round(tf / peaks["tflops"], 3)}
 
 
+def bench_mla_prefill(B: int, L: int, H: int, peaks) -> Dict:
+    """Causal MLA prefill of B requests of L new tokens at Kimi-K2 latent
+    dims, both forms: absorbed (queries through W_UK, attention over the
+    576-dim latent rows, output through W_UV) and non-absorbed (every key
+    expanded through kv_b_proj, then 192 / 128-dim attention). FLOPs of the
+    non-absorbed form: expansion 2 * 512 * 256 * H per key plus 2 * (192 +
+    128) * H per causal query-key pair."""
+    page = 64
+    lens = [L] * B
+    pages_per = (L + page - 1) // page
+    num_pages = B * pages_per + 1
+    latent = torch.randn(num_pages, page, 576, device="cuda", dtype=torch.bfloat16) * 0.5
+    perm = torch.randperm(num_pages - 1)
+    pos = torch.arange(pages_per * page)
+    pt = (perm[: B * pages_per].view(B, pages_per)[:, pos // page] * page + pos % page).to(torch.int32).cuda()
+    rows = torch.arange(B, dtype=torch.int32, device="cuda")
+    seq = torch.tensor(lens, dtype=torch.int32, device="cuda")
+    cu = torch.arange(0, (B + 1) * L, L, dtype=torch.int32, device="cuda")
+    T = B * L
+    scale = 192 ** -0.5
+    q = torch.randn(T, H, 192, device="cuda", dtype=torch.bfloat16)
+    q_rope = torch.randn(T, H, 64, device="cuda", dtype=torch.bfloat16)
+    w_kv_b = torch.randn(H * 256, 512, device="cuda", dtype=torch.bfloat16) * 0.05
+    w_uk_t = torch.randn(H, 512, 128, device="cuda", dtype=torch.bfloat16) * 0.05
+    w_uv = torch.randn(H, 128, 512, device="cuda", dtype=torch.bfloat16) * 0.05
+    plan = ops.MlaPrefillPlan(lens, torch.device("cuda"))
+    tile = ops._group_tile(T)
+    T_pad = (T + tile - 1) // tile * tile
+
+    def absorbed():
+        xs = torch.empty(H, T_pad, 128, device="cuda", dtype=torch.bfloat16)
+        xs[:, :T] = q[..., :128].transpose(0, 1)
+        q_lat = ops.grouped_gemm(xs, w_uk_t, tile)
+        o_lat = ops.mla_attention(q_lat, q_rope, latent, pt, rows, seq, cu, page, scale)
+        return ops.mla_output(o_lat, w_uv, T)
+
+    def expanded():
+        return ops.mla_prefill_attention(q, q_rope, latent, pt, rows, seq, cu, L, w_kv_b, 128, 128, page, scale,
+                                         plan)
+
+    ms_abs = time_kernel(absorbed, iters=3)
+    ms_exp = time_kernel(expanded, iters=3)
+    pairs = B * L * (L + 1) / 2
+    flops_exp = 2.0 * 512 * 256 * H * B * L + 2.0 * (192 + 128) * H * pairs
+    return {"kernel": "mla_prefill", "B": B, "L": L, "heads": H, "absorbed_ms": round(ms_abs, 3),
+            "expanded_ms": round(ms_exp, 3), "speedup": round(ms_abs / ms_exp, 2),
+            "expanded_TFLOP/s": round(flops_exp / ms_exp / 1e9, 1),
+            "expanded_frac_tensor": round(flops_exp / ms_exp / 1e9 / peaks["tflops"], 3)}
+
+
 def bench_moe_mxfp4(T: int, E: int, k: int, H: int, I: int, peaks) -> Dict:
     """Routed experts with MXFP4 weights (Kimi-K2 expert dims by default):
     router outputs uniform over E local experts, the full pipeline (align,
@@ -655,6 +705,8 @@ def main() -> None:
                      (64, 2048, 128)]:
         cases.append((f"mla_decode B={B} L={L} H={Hh}",
                       lambda B=B, L=L, Hh=Hh: bench_mla_decode(B, L, Hh, 64, peaks)))
+    for B, L in ((1, 4096), (1, 16384), (4, 2048)):
+        cases.append((f"mla_prefill B={B} L={L}", lambda B=B, L=L: bench_mla_prefill(B, L, 64, peaks)))
     H, I, V = 1024, 3072, 151936
     for M in (1, 64, 256):
         for lab, N, K in (("qkv", 4096, H), ("o", H, 2048), ("gate_up", 2 * I, H), ("down", H, I)):
