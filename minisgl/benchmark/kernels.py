@@ -177,17 +177,17 @@ def trace_prefill_attention(B: int = 1, L: int = 16384, hq: int = 16, hk: int = 
     torch.cuda.synchronize()
     t = tr.view(64, 8).cpu().tolist()
     if os.environ.get("MINISGL_PREFILL_PAIR", "1") != "0" and (hq // hk) % 2 == 0:
-        # head-pair kernel slots: 0 / 4 scores seen (head 0 / 1), 1 scores
-        # loaded, 2 exps done, 3 / 5 P handed over, 6 / 7 MMA thread saw P
+        # head-pair kernel slots: 0 scores seen (head 0, warp 0), 1-4 P
+        # handed over by head 0's warps 0-3, 5 MMA thread saw P, 6 PV issued,
+        # 7 next QK issued
         pair = {
-            "period": lambda i: t[i][3] - t[i - 1][3],
-            "scores_seen_to_loaded": lambda i: t[i][1] - t[i][0],
-            "loaded_to_exps_done": lambda i: t[i][2] - t[i][1],
-            "exps_done_to_p_handed": lambda i: t[i][3] - t[i][2],
-            "p_handed_to_mma_sees_p": lambda i: t[i][6] - t[i][3],
-            "p_handed_to_next_scores": lambda i: t[i + 1][0] - t[i][3],
-            "head1_p_after_head0_p": lambda i: t[i][5] - t[i][3],
-            "head0_scores_after_head1_p": lambda i: t[i + 1][0] - t[i][5],
+            "period": lambda i: t[i][1] - t[i - 1][1],
+            "scores_seen_to_p_handed_w0": lambda i: t[i][1] - t[i][0],
+            "p_handed_skew_last_minus_first": lambda i: max(t[i][1:5]) - min(t[i][1:5]),
+            "last_p_to_mma_sees_p": lambda i: t[i][5] - max(t[i][1:5]),
+            "pv_issue": lambda i: t[i][6] - t[i][5],
+            "kv_wait_and_qk_issue": lambda i: t[i][7] - t[i][6],
+            "qk_issued_to_next_scores": lambda i: t[i + 1][0] - t[i][7],
         }
         out = {"trace": "prefill_attention (head pairs)", "B": B, "L": L, "hq": hq, "hk": hk}
         for k, f in pair.items():

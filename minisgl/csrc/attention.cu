@@ -994,11 +994,11 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 
 // ------------------------------------------------------ head-pair prefill ----
 // Two query heads of one KV group per CTA (128 query rows each), sharing every
-// K/V tile. Tensor memory (512 columns): O of head h at columns [128 h, +128),
-// scores S_h at [256 + 64 h, +64) with P_h (bf16 pairs) written over the first
-// 32 of them, and Q_h (bf16 pairs, loaded once) at [384 + 64 h, +64) as the A
-// operand of Q.K^T, so the MMAs read only K and V from shared memory. The MMA
-// thread ping-pongs the heads,
+// K/V tile. Tensor memory: O of head h at columns [128 h, +128), scores S_h at
+// [256 + 64 h, +64) with P_h (bf16 pairs) written over the first 32 of them.
+// Both heads' Q tiles (64 KB) sit in shared memory, loaded once by TMA, as
+// the A operand of Q.K^T (with A in tensor memory the MMA thread took twice
+// as long to issue each Q.K^T MMA). The MMA thread ping-pongs the heads,
 //   QK0(0) QK1(0) | PV0(i) QK0(i+1) PV1(i) QK1(i+1) | ...,
 // so the softmax of one head runs while the tensor core works on the other.
 // tcgen05 operations of one thread complete in order, which is what makes
@@ -1009,19 +1009,20 @@ __global__ void __launch_bounds__(kTcThreads, 1)
 // statistics cross warps.
 constexpr int kPrStages = 5;
 constexpr int kPrSCol = 256;
-constexpr int kPrQCol = 384;
 constexpr int kPrProducer = 8, kPrIssuer = 9;
 constexpr int kPrThreads = 32 * 10;
 constexpr int kPrPolyPairs = 3;  // of every 8 exponent pairs, computed on the FMA pipe
-constexpr int kPrSmem = 1024 + kPrStages * kStageBytes + 256;
+constexpr int kPrSmem = 1024 + 4 * kTcQChunk + kPrStages * kStageBytes + 256;
 static_assert(kPrSmem <= 227 * 1024, "head-pair prefill smem over the per-CTA limit");
 
 __global__ void __launch_bounds__(kPrThreads, 1)
-    prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tm_kv, AttnArgs a) {
+    prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
+                             AttnArgs a) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) &
                                              ~static_cast<uintptr_t>(1023));
-  uint8_t* sKV = smem;
+  uint8_t* sQ = smem;                        // [head][64-dim chunk] of 128 rows x 128 B
+  uint8_t* sKV = sQ + 4 * kTcQChunk;
   uint64_t* bars = reinterpret_cast<uint64_t*>(sKV + kPrStages * kStageBytes);
   uint64_t* kv_full = bars;                  // [kPrStages]
   uint64_t* kv_empty = kv_full + kPrStages;  // [kPrStages]
@@ -1048,9 +1049,9 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   const int n = (cached + min(q_len, row0 + kTcRows) - 1) / kTile + 1;
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
   // optional per-tile phase stamps of CTA (0, 0, 0) (the longest key range
-  // of request 0's first head pair), 8 slots a tile: 0 / 4 scores seen by
-  // head 0 / 1, 1 scores loaded, 2 exps done, 3 / 5 P handed over by head
-  // 0 / 1, 6 / 7 the MMA thread saw P of head 0 / 1
+  // of request 0's first head pair), 8 slots a tile: 0 scores seen by head
+  // 0 (warp 0), 1-4 P handed over by head 0's warps 0-3, 5 the MMA thread
+  // saw P of head 0, 6 PV of head 0 issued, 7 QK of head 0's next tile issued
   unsigned long long* trace = (a.trace != nullptr && blockIdx.x == 0 && blockIdx.y == 0 && b == 0) ? a.trace : nullptr;
   auto stamp = [&](int i, int slot) {
     if (trace != nullptr && i < 64) trace[i * 8 + slot] = globaltimer_ns();
@@ -1066,10 +1067,11 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       mbar_init(&p_full[i], 4);
       mbar_init(&o_done[i], 1);
     }
-    mbar_init(q_ready, 8);
+    mbar_init(q_ready, 1);
     *s_abort = 0;
     fence_barrier_init();
     prefetch_tmap(&tm_kv);
+    prefetch_tmap(&tm_q);
   }
   if (warp == kPrIssuer) {
     tmem_alloc(tmem_slot, 512);
@@ -1084,6 +1086,14 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   if (warp == kPrProducer) {
     // ------------------------------------------------------------ TMA ----
     if (lane == 0) {
+      // both heads' Q tiles; rows past the last query token read the next
+      // request's rows (or the zero fill past the end), never stored
+      mbar_arrive_expect_tx(q_ready, 4 * kTcQChunk);
+#pragma unroll
+      for (int hh = 0; hh < 2; ++hh)
+#pragma unroll
+        for (int c = 0; c < 2; ++c)
+          tma_load_2d(sQ + (2 * hh + c) * kTcQChunk, &tm_q, q_ready, (qh0 + hh) * kD + 64 * c, q_begin + row0);
       const int P = a.page_size;
       const int seg = P < kTile ? P : kTile;
       int cur[kTile / 16], nxt[kTile / 16];
@@ -1126,31 +1136,42 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     __syncwarp();
   } else if (warp == kPrIssuer) {
     // ------------------------------------------------------------ MMA ----
+    // (one MMA warp per head was measured slower: 2.2 vs 1.7 us per tile,
+    // the second warp's issue competing with the softmax warps)
     constexpr uint32_t idesc_qk = make_idesc_bf16(kTcRows, kTile);
     constexpr uint32_t idesc_pv = make_idesc_bf16(kTcRows, kD, false, true);
+    // descriptors of stage 0; a stage, head, half or k-step moves only the
+    // start address field (bytes >> 4, well inside its 14 bits), so each MMA
+    // adds a constant to a warp-uniform base instead of rebuilding one
     const uint32_t kv_addr = smem_u32(sKV);
-    auto qk = [&](int hh, int j) {  // S_hh = Q_hh . K_j^T (Q from tensor memory)
-      const uint32_t st = kv_addr + (j % kPrStages) * kStageBytes;
+    const uint64_t k_desc0 = make_sdesc_k_sw128(kv_addr);
+    const uint64_t v_desc0 = make_sdesc_mn_sw128(kv_addr + kTileBytes, kHalfBytes);
+    const uint64_t q_desc0 = make_sdesc_k_sw128(smem_u32(sQ));
+    const uint32_t tm = __shfl_sync(0xffffffffu, tmem, 0);  // warp-uniform for the MMA operands
+    auto qk = [&](int hh, int j) {  // S_hh = Q_hh . K_j^T
+      const uint64_t st = k_desc0 + static_cast<uint64_t>((j % kPrStages) * (kStageBytes >> 4));
 #pragma unroll
       for (int c = 0; c < 2; ++c)
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          tc_mma_f16_ta(tmem + kPrSCol + 64 * hh, tmem + kPrQCol + 64 * hh + (c * 4 + k) * 8,
-                        make_sdesc_k_sw128(st + c * kHalfBytes + k * 32), idesc_qk, (c | k) != 0 ? 1u : 0u);
+          tc_mma_f16(tm + kPrSCol + 64 * hh, q_desc0 + static_cast<uint64_t>(((2 * hh + c) * kTcQChunk + k * 32) >> 4),
+                     st + static_cast<uint64_t>((c * kHalfBytes + k * 32) >> 4), idesc_qk, (c | k) != 0 ? 1u : 0u);
       tc_commit(&s_full[hh]);
     };
     auto pv = [&](int hh, int i) {  // O_hh += P_hh . V_i
-      const uint32_t v = kv_addr + (i % kPrStages) * kStageBytes + kTileBytes;
+      const uint64_t v = v_desc0 + static_cast<uint64_t>((i % kPrStages) * (kStageBytes >> 4));
 #pragma unroll
       for (int kk = 0; kk < kTile / 16; ++kk)  // 16 keys = 8 TMEM columns of P per MMA
-        tc_mma_f16_ta(tmem + 128 * hh, tmem + kPrSCol + 64 * hh + kk * 8,
-                      make_sdesc_mn_sw128(v + kk * 2048, kHalfBytes), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        tc_mma_f16_ta(tm + 128 * hh, tm + kPrSCol + 64 * hh + kk * 8, v + static_cast<uint64_t>(kk * (2048 >> 4)),
+                      idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
       tc_commit(&o_done[hh]);
     };
-    // every wait of this warp is bounded; the warp follows lane 0's result
+    // every wait of this warp is bounded; lane 0 polls alone and the warp
+    // follows its result
     auto wait = [&](uint64_t* bar, uint32_t parity, int where) {  // uniform over the warp
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, err, where) &&
-                                         !*reinterpret_cast<volatile int*>(s_abort));
+      int ok = 1;
+      if (lane == 0) ok = mbar_wait(bar, parity, err, where) && !*reinterpret_cast<volatile int*>(s_abort);
+      return __shfl_sync(0xffffffffu, ok, 0) != 0;
     };
     bool ok = wait(q_ready, 0, 252) && wait(&kv_full[0], 0, 253);
     tc_fence_after();
@@ -1163,20 +1184,21 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       const bool more = i + 1 < n;
       ok = wait(&p_full[0], i & 1, 254);
       if (!ok) break;
-      if (lane == 0) stamp(i, 6);
+      if (lane == 0) stamp(i, 5);
       tc_fence_after();
       if (lane == 0) pv(0, i);
+      if (lane == 0) stamp(i, 6);
       __syncwarp();
       if (more) {
         ok = wait(&kv_full[(i + 1) % kPrStages], ((i + 1) / kPrStages) & 1, 255);
         if (!ok) break;
         tc_fence_after();
         if (lane == 0) qk(0, i + 1);
+        if (lane == 0) stamp(i, 7);
         __syncwarp();
       }
       ok = wait(&p_full[1], i & 1, 256);
       if (!ok) break;
-      if (lane == 0) stamp(i, 7);
       tc_fence_after();
       if (lane == 0) {
         pv(1, i);
@@ -1194,25 +1216,6 @@ __global__ void __launch_bounds__(kPrThreads, 1)
     const uint32_t lane_base = tmem + (static_cast<uint32_t>(32 * quad) << 16);
     const bool row_valid = row0 + r < q_len;
     const int64_t tok = q_begin + row0 + (row_valid ? r : 0);
-    // Q row of head qh0 + hh into tensor memory: 128 bf16 = 64 columns of pairs
-    {
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const __nv_bfloat16*>(a.q) + tok * a.ld_q +
-                                                        static_cast<int64_t>(qh0 + hh) * kD);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t w[32];
-#pragma unroll
-        for (int v = 0; v < 8; ++v) {
-          const uint4 x = row_valid ? src[c * 8 + v] : make_uint4(0u, 0u, 0u, 0u);
-          w[4 * v] = x.x, w[4 * v + 1] = x.y, w[4 * v + 2] = x.z, w[4 * v + 3] = x.w;
-        }
-        tmem_st_32x32b_x32(lane_base + kPrQCol + 64 * hh + 32 * c, w);
-      }
-      tc_wait_st();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(q_ready);
-    }
     const float sl2 = a.scale * kLog2e;
     const int pos = cached + row0 + r;  // position of this row's query token
     const uint32_t s_col = lane_base + kPrSCol + 64 * hh;
@@ -1223,14 +1226,12 @@ __global__ void __launch_bounds__(kPrThreads, 1)
       ok = __all_sync(0xffffffffu, mbar_wait(&s_full[hh], i & 1, err, 257) &&
                                        !*reinterpret_cast<volatile int*>(s_abort));  // uniform over the warp
       if (!ok) break;
-      const bool stamper = lane == 0 && quad == 0;
-      if (stamper) stamp(i, hh == 0 ? 0 : 4);
+      if (lane == 0 && quad == 0 && hh == 0) stamp(i, 0);
       tc_fence_after();
       uint32_t sv[kTile];
       tmem_ld_32x32b_x32(s_col, *reinterpret_cast<uint32_t(*)[32]>(sv));
       tmem_ld_32x32b_x32(s_col + 32, *reinterpret_cast<uint32_t(*)[32]>(sv + 32));
       tc_wait_ld();
-      if (stamper && hh == 0) stamp(i, 1);
       // causal and length mask: keys [0, lim) of the tile are visible to this row
       const int lim = min(pos + 1, L) - i * kTile;
       if (lim < kTile) {
@@ -1300,13 +1301,12 @@ __global__ void __launch_bounds__(kPrThreads, 1)
         f2_unpack(f2_add(ps2[0], ps2[1]), a0, a1);
         l_sum += a0 + a1;
       }
-      if (stamper && hh == 0) stamp(i, 2);
       tmem_st_32x32b_x32(s_col, pk);
       tc_wait_st();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&p_full[hh]);
-      if (stamper) stamp(i, hh == 0 ? 3 : 5);
+      if (lane == 0 && hh == 0) stamp(i, 1 + quad);
     }
     // ------------------------------------------------------- epilogue ----
     if (!ok && lane == 0) atomicExch(s_abort, 1);
@@ -1340,6 +1340,7 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   __syncthreads();
   if (warp == kPrProducer && lane == 0 && *reinterpret_cast<volatile int*>(s_abort)) {
     // after an abort, let the copies still in flight land before the CTA leaves
+    mbar_wait(q_ready, 0, err, 260);
     for (int j = max(0, issued - kPrStages); j < issued; ++j)
       mbar_wait(&kv_full[j % kPrStages], (j / kPrStages) & 1, err, 259);
   }
@@ -1406,7 +1407,7 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
     const char* v = std::getenv("MINISGL_PREFILL_PAIR");
     return v == nullptr || v[0] != '0';
   }();
-  if (pair_on && q_aligned && (a.hq / a.hk) % 2 == 0) {
+  if (pair_on && q_aligned && a.q_rows > 0 && (a.hq / a.hk) % 2 == 0) {
     static bool pair_attr[64] = {};
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1414,8 +1415,9 @@ void launch_prefill_attention(const AttnArgs& a, cudaStream_t s) {
       cudaFuncSetAttribute(prefill_attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kPrSmem);
       pair_attr[dev & 63] = true;
     }
+    const CUtensorMap tq = make_tmap_bf16_2d_sw128(a.q, a.q_rows, static_cast<uint64_t>(a.hq) * kD, a.ld_q, kTcRows);
     dim3 grid((a.max_q + kTcRows - 1) / kTcRows, a.hq / 2, a.B);
-    launch_pdl(prefill_attn_pair_kernel, grid, dim3(kPrThreads), kPrSmem, s, tm, a);
+    launch_pdl(prefill_attn_pair_kernel, grid, dim3(kPrThreads), kPrSmem, s, tm, tq, a);
     return;
   }
   // the tcgen05 kernel reads Q by TMA: a 16-byte aligned base and row stride
