@@ -71,12 +71,16 @@ def _valid_page(p: int) -> bool:
 class Engine:
     def __init__(self, config: EngineConfig) -> None:
         if config.cp_size > 1:
-            # context parallelism: every rank holds the whole model and the
-            # attention over the KV tiles it owns; layers see one TP rank
+            # context parallelism: every rank holds the model (the routed
+            # experts split over the ranks with --ep cp) and the attention over
+            # the KV tiles it owns; layers see one TP rank
             if config.tp_info.size != config.cp_size:
                 raise ValueError("context parallelism runs over all ranks: tp_size must equal cp_size")
             if not config.model_config.is_mla:
                 raise ValueError("context parallelism is implemented for MLA models (DeepSeek-V3 / Kimi-K2)")
+            if config.ep_size not in (1, config.cp_size):
+                raise ValueError("expert parallelism under context parallelism spans every rank: ep_size must be "
+                                 "1 or cp_size")
             set_tp_info(0, 1)
             set_cp_info(config.tp_info.rank, config.cp_size)
         elif config.enable_dp_attention and config.tp_info.size > 1:
@@ -158,7 +162,8 @@ class Engine:
                 self._ep_heap = EpHeap(self.device, cap, mcfg.hidden_size)
             self.ctx.moe_backend = self.moe_backend = create_moe_backend(
                 config.moe_backend, ep_dispatch=self.dp, ep_size=mcfg.ep_size, ep_rank=mcfg.ep_rank,
-                group=self.tp_cpu_group if not self.is_cuda else None, heap=self._ep_heap)
+                group=self.tp_cpu_group if not self.is_cuda else None, heap=self._ep_heap,
+                context_parallel=self.cp_size > 1 and mcfg.ep_size > 1)
         self.sampler = Sampler(self.device, mcfg.vocab_size, config.weight_seed)
         # tensor parallelism on GPUs: sample from each rank's vocabulary shard
         # of the logits instead of gathering [B, V] fp32 logits every step

@@ -117,3 +117,33 @@ class AllToAllMoe(BaseMoeBackend):
         pairs[order] = back
         out = (pairs.view(T, topk, H).float() * topk_w.view(T, topk, 1).float()).sum(dim=1)
         return out.to(x.dtype)
+
+
+class ContextParallelMoe(BaseMoeBackend):
+    """Routed experts split over the context-parallel ranks. A token-sharded
+    prefill batch holds different tokens on every rank, so its rows go to
+    their experts' owners and back (``AllToAllMoe``); a decode batch runs
+    replicated, so each rank applies its own experts to every row (the others
+    contribute nothing) and one all-reduce over the ranks sums the parts."""
+
+    def __init__(self, ep_size: int, ep_rank: int, group: Optional[dist.ProcessGroup] = None) -> None:
+        self.dispatch = AllToAllMoe(ep_size, ep_rank, group)
+        self.local = FusedMoe()
+        self.group = group
+
+    def forward(self, hidden_states: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, gating_output: torch.Tensor,
+                topk: int, renormalize: bool, activation: str = "silu", scoring: str = "softmax",
+                correction_bias: Optional[torch.Tensor] = None, n_group: int = 1, topk_group: int = 1,
+                routed_scale: float = 1.0, interleaved: bool = False, expert_offset: int = 0,
+                mxfp4: Optional[tuple] = None) -> torch.Tensor:
+        from minisgl.core import get_global_ctx
+
+        kw = dict(hidden_states=hidden_states, w1=w1, w2=w2, gating_output=gating_output, topk=topk,
+                  renormalize=renormalize, activation=activation, scoring=scoring, correction_bias=correction_bias,
+                  n_group=n_group, topk_group=topk_group, routed_scale=routed_scale, interleaved=interleaved,
+                  mxfp4=mxfp4)
+        if getattr(get_global_ctx().batch.attn_metadata, "cp_plan", None) is not None:
+            return self.dispatch.forward(**kw)
+        out = self.local.forward(expert_offset=expert_offset, **kw)
+        dist.all_reduce(out, group=self.group)
+        return out

@@ -137,7 +137,8 @@ def parse_args(args: List[str], run_shell: bool = False) -> Tuple[ServerArgs, bo
         kw["dtype"] = torch.bfloat16  # the GPU kernels run bf16
     ranks = kw.pop("tensor_parallel_size")
     if kw.get("cp_size", 1) > 1:
-        # context parallelism spans every rank (layers replicated, KV split)
+        # context parallelism spans every rank (KV split by 64-key tiles,
+        # prefill tokens sharded, experts split with --ep cp)
         if ranks not in (1, kw["cp_size"]):
             raise SystemExit("--cp-size runs over all ranks: leave --tp at 1 or set it equal to --cp-size")
         ranks = kw["cp_size"]

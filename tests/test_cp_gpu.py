@@ -27,7 +27,7 @@ def _prompts():
     return [[rng.randrange(4096) for _ in range(rng.randint(70, 400))] for _ in range(5)]
 
 
-def _run(rank, world, port, q):
+def _run(rank, world, port, q, ep=1):
     os.environ["NCCL_NVLS_ENABLE"] = "0"
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
@@ -38,17 +38,17 @@ def _run(rank, world, port, q):
     llm = LLM(make_model_dir("small-kimi"), dtype=torch.bfloat16, device=f"cuda:{rank}", use_dummy_weight=True,
               tp_info=DistributedInfo(rank, world), page_size=64, num_page_override=64, max_running_req=8,
               max_seq_len_override=1024, max_extend_tokens=512, cuda_graph_max_bs=8, distributed_port=port,
-              cp_size=world if world > 1 else 1, distributed_timeout=60)
+              cp_size=world if world > 1 else 1, ep_size=ep if world > 1 else 1, distributed_timeout=60)
     outs = llm.generate(_prompts(), SamplingParams(temperature=0.0, max_tokens=6, ignore_eos=True))
     q.put((rank, [o["token_ids"] for o in outs]))
     llm.shutdown()
 
 
-def _spawn(world):
+def _spawn(world, ep=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, q)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, q, ep)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=400) for _ in range(world))
@@ -58,11 +58,13 @@ def _spawn(world):
     return results
 
 
-def test_cp2_matches_one_gpu():
+@pytest.mark.parametrize("ep", [1, 2])
+def test_cp2_matches_one_gpu(ep):
+    """ep 2: the routed experts split over the two ranks as well."""
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
     one = _spawn(1)[0]
-    two = _spawn(2)
+    two = _spawn(2, ep)
     assert two[0] == two[1]
     # bf16 sums in another order (shares reduced over the ranks): a near-tie
     # may flip a token; a broken split scrambles all of them

@@ -4,9 +4,10 @@ t % cp) in a pool of 1/cp of the pages (the allocator gives tile t a page of
 id = t mod cp) and attends every query over them only. Prefill batches are
 token-sharded (each rank runs the layers on the tokens of its own tiles);
 the ranks' shares of the attention output meet after W_UV. The generated
-tokens equal the single-rank engine's. Prompts are longer than one tile so
-several ranks hold keys, and chunks of 256 tokens put several requests and
-tiles of every rank into one prefill batch."""
+tokens equal the single-rank engine's, also with the routed experts split
+over the ranks (--ep). Prompts are longer than one tile so several ranks
+hold keys, and chunks of 256 tokens put several requests and tiles of every
+rank into one prefill batch."""
 
 import socket
 
@@ -23,7 +24,7 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(rank, world, port, cp, q):
+def _run(rank, world, port, cp, q, ep=1):
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
     from minisgl.parallel import DistributedInfo
@@ -41,7 +42,7 @@ def _run(rank, world, port, cp, q):
     mla_backend.CPShardPlan.__init__ = record
     llm = LLM(make_model_dir("tiny-kimi"), dtype=torch.float32, device="cpu", use_dummy_weight=True,
               tp_info=DistributedInfo(rank, world), page_size=64, num_page_override=64, max_running_req=4,
-              max_seq_len_override=512, max_extend_tokens=256, distributed_port=port, cp_size=cp)
+              max_seq_len_override=512, max_extend_tokens=256, distributed_port=port, cp_size=cp, ep_size=ep)
     if cp > 1:  # each rank holds one page in cp (plus spares)
         assert llm.engine.kv_cache.pool.shape[1] == llm.engine.num_pages // cp + 2
     outs = llm.generate(PROMPTS, SamplingParams(temperature=0.0, max_tokens=8, ignore_eos=True))
@@ -49,11 +50,11 @@ def _run(rank, world, port, cp, q):
     llm.shutdown()
 
 
-def _generate(world, cp):
+def _generate(world, cp, ep=1):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, port, cp, q)) for r in range(world)]
+    procs = [ctx.Process(target=_run, args=(r, world, port, cp, q, ep)) for r in range(world)]
     for p in procs:
         p.start()
     results = dict(q.get(timeout=300) for _ in range(world))
@@ -73,4 +74,16 @@ def test_cp_matches_single_rank(cp):
         assert tokens == single, (r, tokens, single)
         # the prefill really was split: some batch ran fewer rows per rank
         # than it has tokens
+        assert plans and any(t_max < T for T, t_max in plans), plans
+
+
+def test_cp_with_expert_parallelism_matches_single_rank():
+    """cp 2 with the routed experts split over the two ranks: prefill rows
+    travel to their experts' owners (all-to-all), decode rows run each
+    rank's experts and are summed (all-reduce)."""
+    single, _ = _generate(1, 1)[0]
+    got = _generate(2, 2, ep=2)
+    for r in range(2):
+        tokens, plans = got[r]
+        assert tokens == single, (r, tokens, single)
         assert plans and any(t_max < T for T, t_max in plans), plans
