@@ -164,6 +164,10 @@ __global__ void __launch_bounds__(kDecodeThreads, 2)
   const int k_end = min(L, k_begin + chunk);
   const int ntiles = k_end > k_begin ? (k_end - k_begin + kTile - 1) / kTile : 0;
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+  if (a.pt_rows > 0 && (a.req_rows[b] < 0 || a.req_rows[b] >= a.pt_rows)) {  // uniform over the CTA
+    if (threadIdx.x == 0) err.report(kErrBadIndex, 921);
+    return;
+  }
   __syncthreads();
 
   const int g = lane >> 2, t = lane & 3;
@@ -389,6 +393,10 @@ __global__ void __launch_bounds__(128, 2)
   const int last_pos = cached + min(q_len, row0 + 64) - 1;  // largest position in the tile
   const int ntiles = last_pos / kTile + 1;
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+  if (a.pt_rows > 0 && (a.req_rows[b] < 0 || a.req_rows[b] >= a.pt_rows)) {  // uniform over the CTA
+    if (threadIdx.x == 0) err.report(kErrBadIndex, 922);
+    return;
+  }
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
@@ -673,6 +681,10 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   const int h = qh / (a.hq / a.hk);
   const int n = (cached + min(q_len, row0 + kTcRows) - 1) / kTile + 1;  // key tiles up to the last row
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+  if (a.pt_rows > 0 && (a.req_rows[b] < 0 || a.req_rows[b] >= a.pt_rows)) {  // uniform over the CTA
+    if (threadIdx.x == 0) err.report(kErrBadIndex, 923);
+    return;
+  }
   unsigned long long* trace = (a.trace != nullptr && blockIdx.x == 0 && qh == 0 && b == 0) ? a.trace : nullptr;
   auto stamp = [&](int i, int slot) {
     if (trace != nullptr && i < 64) trace[i * 8 + slot] = globaltimer_ns();
@@ -1048,6 +1060,10 @@ __global__ void __launch_bounds__(kPrThreads, 1)
   const int h = qh0 / (a.hq / a.hk);  // both heads of the pair share this KV head
   const int n = (cached + min(q_len, row0 + kTcRows) - 1) / kTile + 1;
   const int32_t* pt_row = a.page_table + static_cast<int64_t>(a.req_rows[b]) * a.ld_pt;
+  if (a.pt_rows > 0 && (a.req_rows[b] < 0 || a.req_rows[b] >= a.pt_rows)) {  // uniform over the CTA
+    if (threadIdx.x == 0) err.report(kErrBadIndex, 924);
+    return;
+  }
   // optional per-tile phase stamps of CTA (0, 0, 0) (the longest key range
   // of request 0's first head pair), 8 slots a tile: 0 scores seen by head
   // 0 (warp 0), 1-4 P handed over by head 0's warps 0-3, 5 the MMA thread

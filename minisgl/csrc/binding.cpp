@@ -203,6 +203,7 @@ void gemm_fused(at::Tensor out, const at::Tensor& x, const at::Tensor& w, const 
     e.hq = static_cast<int>(hq);
     e.hk = static_cast<int>(hk);
     e.page_size = static_cast<int>(page_size);
+    e.kv_slots = k_cache->size(0) * page_size;  // [pages, hk, page, 128]: a slot outside is reported
   }
   const c10::cuda::CUDAGuard guard(x.device());
   minisgl::launch_gemm(a, stream_of(x));
@@ -586,6 +587,7 @@ void mla_prepare(at::Tensor q_pe, at::Tensor xs, const at::Tensor& q, const at::
   a.cp_size = static_cast<int>(cp_size);
   a.cp_rank = static_cast<int>(cp_rank);
   a.page_size = static_cast<int>(latent.size(1));
+  a.num_slots = latent.size(0) * latent.size(1);
   a.err = err_ptr(err);
   minisgl::launch_mla_prepare(a, stream_of(q));
 }
@@ -626,6 +628,7 @@ void mla_store_latent(const at::Tensor& kv_a, const at::Tensor& norm_w, double e
   a.cp_size = static_cast<int>(cp_size);
   a.cp_rank = static_cast<int>(cp_rank);
   a.page_size = static_cast<int>(latent.size(1));
+  a.num_slots = latent.size(0) * latent.size(1);
   a.err = err_ptr(err);
   minisgl::launch_mla_prepare(a, stream_of(kv_a));
 }
@@ -939,7 +942,7 @@ void embedding(at::Tensor out, const at::Tensor& w, const at::Tensor& ids, int64
 void rope_store(at::Tensor qkv, const at::Tensor& positions, const at::Tensor& cos_sin,
                 const c10::optional<at::Tensor>& q_norm_w, const c10::optional<at::Tensor>& k_norm_w,
                 at::Tensor k_cache, at::Tensor v_cache, const at::Tensor& out_loc, int64_t hq,
-                int64_t hk, int64_t d, int64_t page_size, double eps) {
+                int64_t hk, int64_t d, int64_t page_size, double eps, const c10::optional<at::Tensor>& err) {
   check_cuda(qkv, "qkv");
   check_rowmajor(qkv, "qkv");
   check_i32(positions, "positions");
@@ -968,6 +971,9 @@ void rope_store(at::Tensor qkv, const at::Tensor& positions, const at::Tensor& c
   a.page_size = static_cast<int>(page_size);
   a.eps = static_cast<float>(eps);
   a.dt = dtype_of(qkv);
+  // the cache's own extent: a slot outside it is reported and not written
+  a.kv_slots = k_cache.dim() >= 1 ? k_cache.size(0) * page_size : 0;
+  a.err = err_ptr(err);
   const c10::cuda::CUDAGuard guard(qkv.device());
   minisgl::launch_rope_store(a, stream_of(qkv));
 }
@@ -1011,6 +1017,7 @@ minisgl::AttnArgs attn_common(const at::Tensor& q, at::Tensor& out, const at::Te
   a.d = static_cast<int>(d);
   a.page_size = static_cast<int>(page_size);
   a.scale = static_cast<float>(scale);
+  a.pt_rows = static_cast<int>(page_table.size(0));
   return a;
 }
 
@@ -1355,7 +1362,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("fused_add_rmsnorm", &fused_add_rmsnorm);
   m.def("act_and_mul", &act_and_mul, py::arg("out"), py::arg("x"), py::arg("act"), py::arg("interleaved") = false);
   m.def("embedding", &embedding);
-  m.def("rope_store", &rope_store);
+  m.def("rope_store", &rope_store, py::arg("qkv"), py::arg("positions"), py::arg("cos_sin"), py::arg("q_norm_w"),
+        py::arg("k_norm_w"), py::arg("k_cache"), py::arg("v_cache"), py::arg("out_loc"), py::arg("hq"),
+        py::arg("hk"), py::arg("d"), py::arg("page_size"), py::arg("eps"), py::arg("err") = py::none());
   m.def("decode_attention", &decode_attention);
   m.def("gemm_fused", &gemm_fused);
   m.def("gemm_sample", &gemm_sample);

@@ -185,6 +185,10 @@ __device__ __forceinline__ void rope_epilogue(const KParams& p, int head, int m,
   }
   const int kvh = is_k ? head - e.hq : head - e.hq - e.hk;
   const int slot = e.out_loc[m];
+  if (e.kv_slots > 0 && (slot < 0 || slot >= e.kv_slots)) {  // uniform over the warp
+    if (lane == 0) p.err.report(kErrBadIndex, 941);
+    return;
+  }
   const int page = slot / e.page_size, off = slot % e.page_size;
   __nv_bfloat16* cache = static_cast<__nv_bfloat16*>(is_k ? e.k_cache : e.v_cache);
   store4_bf16(cache + ((static_cast<int64_t>(page) * e.hk + kvh) * e.page_size + off) * 128 + ocol, v);

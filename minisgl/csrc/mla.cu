@@ -94,6 +94,10 @@ __global__ void __launch_bounds__(256) mla_prepare_kernel(MlaPrepareArgs a) {
     // in that rank's pool at local page (global page) / cp
     const bool store = a.cp_size <= 1 || (a.positions[t] / kKeys) % a.cp_size == a.cp_rank;
     if (a.cp_size > 1) slot = (slot / a.page_size / a.cp_size) * a.page_size + slot % a.page_size;
+    if (store && a.num_slots > 0 && (slot < 0 || slot >= a.num_slots)) {  // uniform over the CTA
+      if (tid == 0) ErrorSink{a.err}.report(kErrBadIndex, 951);
+      return;
+    }
     __nv_bfloat16* lat = reinterpret_cast<__nv_bfloat16*>(a.latent) + slot * kLat;
     const __nv_bfloat16* nw = reinterpret_cast<const __nv_bfloat16*>(a.norm_w);
     {

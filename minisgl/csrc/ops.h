@@ -53,6 +53,7 @@ struct GemmEpilogue {
   void* k_cache;              // bf16 [pages, hk, page_size, 128] of this layer
   void* v_cache;
   int hq, hk, page_size;
+  int64_t kv_slots;           // pages * page_size: slots outside [0, kv_slots) are reported, not written
   const float* temps;         // kEpiSample: [M] temperatures (nullptr: all greedy)
   uint64_t seed;
   const int64_t* step;        // device step counter (read only here)
@@ -153,6 +154,8 @@ struct RopeStoreArgs {
   int T, hq, hk, d, rot_dim, page_size;
   float eps;
   DType dt;
+  int64_t kv_slots;          // pages * page_size: slots outside [0, kv_slots) are reported, not written
+  int* err;
 };
 void launch_rope_store(const RopeStoreArgs& a, cudaStream_t s);
 
@@ -182,6 +185,7 @@ struct AttnArgs {
   int max_splits;
   int* err;
   int q_rows;                // prefill: rows of q (the TMA map extent); 0 selects the kernel without Q TMA
+  int pt_rows;               // rows of page_table: a request row outside [0, pt_rows) is reported and skipped
   unsigned long long* trace; // optional [64 tiles x 8] %globaltimer stamps of one prefill CTA (profiling)
   // non-absorbed MLA prefill (launch_mla_prefill_attention): q heads are
   // q_head_stride elements apart in a q row (their first 128 are q_nope),
@@ -215,6 +219,7 @@ struct MlaPrepareArgs {
   int T, T_pad, H, nope, kv_lora, rope;
   int cp_size, cp_rank;   // context parallelism: store only rows of owned 64-key tiles
   int page_size;          // (at local page = global page / cp_size)
+  int64_t num_slots;      // latent rows of this layer's pool (0: unchecked)
   int* err;
 };
 struct MlaAttnArgs {

@@ -79,6 +79,10 @@ __global__ void rope_store_kernel(RopeStoreArgs a) {
   }
   const int kvh = is_k ? head - a.hq : head - a.hq - a.hk;
   const int slot = a.out_loc[t];
+  if (a.kv_slots > 0 && (slot < 0 || slot >= a.kv_slots)) {  // uniform over the warp
+    if (lane == 0) ErrorSink{a.err}.report(kErrBadIndex, 931);
+    return;
+  }
   const int page = slot / a.page_size, off = slot % a.page_size;
   T* cache = static_cast<T*>(is_k ? a.k_cache : a.v_cache);
   T* dst = cache + ((static_cast<int64_t>(page) * a.hk + kvh) * a.page_size + off) * D + lane * E;

@@ -82,6 +82,12 @@ class DeviceWaitTimeout(RuntimeError):
     """A kernel gave up on an mbarrier wait (its pipeline stalled) and returned."""
 
 
+class DeviceIndexError(RuntimeError):
+    """A kernel met an index outside the buffer it addresses (a KV slot past
+    the cache, a request row past the page table), reported it and skipped
+    the access instead of touching memory it does not own."""
+
+
 class CommTimeoutError(RuntimeError):
     """A collective kernel gave up waiting for a peer rank's flag and returned:
     the peer is late, stalled or gone. The device context stays usable."""
@@ -89,6 +95,7 @@ class CommTimeoutError(RuntimeError):
 
 ERR_MBAR_TIMEOUT = 1
 ERR_PEER_TIMEOUT = 2
+ERR_BAD_INDEX = 3
 
 
 def check_device_errors(device: torch.device) -> None:
@@ -105,6 +112,9 @@ def check_device_errors(device: torch.device) -> None:
             raise CommTimeoutError(f"minisgl collective kernel timed out waiting for a peer (site {site})")
         if code == ERR_MBAR_TIMEOUT:
             raise DeviceWaitTimeout(f"minisgl kernel pipeline wait timed out (site {site})")
+        if code == ERR_BAD_INDEX:
+            raise DeviceIndexError(f"minisgl kernel skipped an index outside its buffer (site {site}): a KV slot "
+                                   "outside the cache or a request row outside the page table")
         raise RuntimeError(f"minisgl kernel reported error code {code} at site {site}")
 
 
@@ -307,7 +317,8 @@ def rope_store(
         ref.rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache, out_loc, hq, hk, d, page_size, eps)
         return
     _count()
-    native().rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache, out_loc, hq, hk, d, page_size, eps)
+    native().rope_store(qkv, positions, cos_sin, q_norm_w, k_norm_w, k_cache, v_cache, out_loc, hq, hk, d, page_size, eps,
+                        error_word(qkv.device))
 
 
 # -------------------------------------------------------------- attention
