@@ -142,7 +142,8 @@ class ContextParallelMoe(BaseMoeBackend):
                   renormalize=renormalize, activation=activation, scoring=scoring, correction_bias=correction_bias,
                   n_group=n_group, topk_group=topk_group, routed_scale=routed_scale, interleaved=interleaved,
                   mxfp4=mxfp4)
-        if getattr(get_global_ctx().batch.attn_metadata, "cp_plan", None) is not None:
+        md = getattr(get_global_ctx().batch, "attn_metadata", None)
+        if getattr(md, "cp_plan", None) is not None:
             return self.dispatch.forward(**kw)
         out = self.local.forward(expert_offset=expert_offset, **kw)
         dist.all_reduce(out, group=self.group)
