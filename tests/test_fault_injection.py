@@ -33,7 +33,7 @@ def _run(rank, world, port, spec, q):
     try:
         llm = LLM(make_model_dir("tiny-qwen3"), dtype=torch.float32, device="cpu", use_dummy_weight=True,
                   tp_info=DistributedInfo(rank, world), page_size=16, num_page_override=64, max_running_req=4,
-                  max_seq_len_override=256, max_extend_tokens=64, distributed_port=port, distributed_timeout=6)
+                  max_seq_len_override=256, max_extend_tokens=64, distributed_port=port, distributed_timeout=15)
         outs = llm.generate(PROMPTS, SamplingParams(temperature=0.0, max_tokens=12, ignore_eos=True))
         q.put((rank, "ok", [o["token_ids"] for o in outs], time.time() - t0))
         llm.shutdown()
@@ -90,7 +90,7 @@ def test_dead_rank_fails_its_peer():
 
 
 def test_stalled_rank_times_out_its_peer():
-    # rank 1 sleeps far beyond the 6 s process-group timeout at step 2
+    # rank 1 sleeps far beyond the 15 s process-group timeout at step 2
     reports, _ = _spawn("stall:rank=1:step=2:seconds=120", 1)
     status, payload, secs = reports[0]
     assert status == "error", payload
