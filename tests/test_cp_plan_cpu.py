@@ -1,6 +1,7 @@
-"""Host-side layouts of the MLA paths, checked on their own (no ranks, no
-kernels): the token-sharded context-parallel plan of a prefill batch and
-the compact key layout of the non-absorbed MLA prefill."""
+"""Host-side decisions and layouts of the MLA paths, checked on their own
+(no ranks, no kernels): the token-sharded context-parallel plan of a prefill
+batch, the compact key layout of the non-absorbed MLA prefill and the FLOP
+rule that picks the prefill form."""
 
 import numpy as np
 import torch
@@ -65,3 +66,24 @@ def test_mla_prefill_plan_is_compact_and_page_aligned():
         assert (req[start + L:start + pages[b] * 64] == -1).all()
         base += pages[b]
     assert torch.equal(plan.rows_in_order, torch.arange(len(lens), dtype=torch.int32))
+
+
+def test_mla_prefill_form_follows_flop_count(monkeypatch):
+    """Kimi-K2 latent dims: the non-absorbed form (every key expanded through
+    kv_b_proj) pays off once a request has a few hundred new tokens per key;
+    a short extend over a long cached prefix stays absorbed; the switch
+    forces either form."""
+    from types import SimpleNamespace
+
+    from minisgl.attention.mla import MLAAttnBackend
+
+    dims = SimpleNamespace(kv_lora=512, nope=128, rope=64, v_dim=128)
+    pick = lambda lens, qlens: MLAAttnBackend.expanded_prefill(dims, lens, qlens)  # noqa: E731
+    monkeypatch.delenv("MINISGL_MLA_PREFILL", raising=False)
+    assert pick([4096], [4096])             # a long prompt without cache
+    assert not pick([64], [64])             # a short one
+    assert not pick([8192], [16])           # a few new tokens after a long prefix
+    monkeypatch.setenv("MINISGL_MLA_PREFILL", "expanded")
+    assert pick([64], [64])
+    monkeypatch.setenv("MINISGL_MLA_PREFILL", "absorbed")
+    assert not pick([4096], [4096])
