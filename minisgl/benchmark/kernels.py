@@ -29,7 +29,7 @@ import torch
 
 from minisgl import ops
 
-from .perf import time_graph, time_kernel
+from .perf import SmClockLog, time_graph, time_kernel
 
 
 def _peaks() -> Dict[str, float]:
@@ -736,14 +736,18 @@ def main() -> None:
     for B in (64, 256):
         cases.append((f"sample B={B}", lambda B=B: bench_sample(B, 151936, peaks)))
     rows: List[Dict] = []
+    clocks = SmClockLog(torch.cuda.current_device()).start()
     for label, fn in cases:
         if args.only and args.only not in label:
             continue
         r = fn()
         rows.extend(r if isinstance(r, list) else [r])
+    clock_summary = clocks.stop()
     for r in rows:
         r["peaks"] = peaks["source"]
         print(json.dumps(r), flush=True)
+    # SM clocks over the whole run, to read the timings above against
+    print(json.dumps(clock_summary), flush=True)
     if args.json:
         with open(args.json, "w") as f:
             json.dump(rows, f, indent=1)

@@ -1,6 +1,7 @@
-"""Trace reading of the online benchmark client (no server needed): Qwen
-traces carry seconds, Mooncake traces milliseconds; offsets start at zero,
-scale with --trace-scale, and come back sorted; extra fields are ignored."""
+"""Benchmark helpers without a GPU or server: trace reading of the online
+client (Qwen traces carry seconds, Mooncake traces milliseconds; offsets
+start at zero, scale with --trace-scale, and come back sorted; extra fields
+are ignored) and the kernel benchmarks' SM clock summary."""
 
 import json
 
@@ -38,3 +39,19 @@ def test_prompts_and_stats():
     st = _stats([0.001 * i for i in range(1, 101)])
     assert st["p50"] == pytest.approx(51.0) and st["max"] == pytest.approx(100.0) and st["avg"] == pytest.approx(50.5)
     assert _stats([]) == {}
+
+
+def test_sm_clock_log_summary():
+    """The kernel benchmarks' clock summary keeps only the chosen GPU's
+    samples, takes the median clock of the samples under load and lists
+    the throttle reasons seen active."""
+    from minisgl.benchmark.perf import SmClockLog
+
+    text = ("0, 1455, 1965, 950.3, Not Active, Not Active, Not Active, Active\n"
+            "0, 1500, 1965, 980.0, Not Active, Not Active, Not Active, Not Active\n"
+            "0, 1965, 1965, 120.0, Not Active, Not Active, Not Active, Not Active\n"
+            "1, 900, 1965, 999.0, Active, Not Active, Not Active, Not Active\n"
+            "garbage line\n")
+    c = SmClockLog.summarize(text, 0)["clocks"]
+    assert c["sm_mhz_median_under_load"] == 1477.5 and c["samples_under_load"] == 2
+    assert c["sm_max_mhz"] == 1965.0 and c["reasons"] == ["sw_power_cap"]
