@@ -42,7 +42,7 @@ class EngineConfig:
     cp_size: int = 1                  # context parallelism (sequence split across ranks)
     enable_dp_attention: bool = False
     moe_quant: str = "none"           # "none" | "mxfp4"
-    comm: str = "nccl"                # "nccl" (baseline) | "fused" (in-kernel NVLink collectives)
+    comm: str = "fused"               # "fused" (in-kernel NVLink collectives) | "nccl" (baseline)
     weight_seed: int = 0
     dummy_weight_device: Optional[str] = None  # draw random weights here ("cpu" for bit-identical tests)
     hf_config_override: Optional[Dict[str, Any]] = field(default=None, hash=False, compare=False)

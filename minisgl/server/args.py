@@ -4,7 +4,8 @@ Every flag of the reference (python/minisgl/server/args.py:54-268) is kept
 with the same names, aliases and defaults. Added: ``--ep-size/--ep``,
 ``--cp-size/--cp``, ``--enable-dp-attention``, ``--moe-quant``,
 ``--random-init`` (alias of ``--dummy-weight``: seeded N(0, 0.02) weights),
-``--comm {nccl,fused}`` and ``--device``. ``--model synthetic:<shape>``
+``--comm {fused,nccl}`` (default fused; ``--disable-pynccl`` selects nccl)
+and ``--device``. ``--model synthetic:<shape>``
 serves a synthetic model folder (see ``minisgl.utils.synthetic``).
 """
 
@@ -77,8 +78,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--context-parallel-size", "--cp-size", dest="cp_size", type=int, default=1)
     p.add_argument("--enable-dp-attention", action="store_true")
     p.add_argument("--moe-quant", choices=["none", "mxfp4"], default="none")
-    p.add_argument("--comm", choices=["nccl", "fused"], default="nccl",
-                   help="TP collectives: NCCL (baseline) or in-kernel NVLink collectives")
+    p.add_argument("--comm", choices=["nccl", "fused"], default="fused",
+                   help="TP collectives: in-kernel NVLink collectives (default) or NCCL (baseline); "
+                        "ignored on --device cpu")
     p.add_argument("--device", default="cuda", help="cuda (one GPU per TP rank) or cpu (fp32 reference path)")
     p.add_argument("--max-running-requests", type=int, dest="max_running_req", default=ServerArgs.max_running_req)
     p.add_argument("--max-seq-len-override", type=int, default=ServerArgs.max_seq_len_override)
@@ -135,6 +137,10 @@ def parse_args(args: List[str], run_shell: bool = False) -> Tuple[ServerArgs, bo
     kw["dtype"] = _DTYPES[dtype] if isinstance(dtype, str) else dtype
     if kw["dtype"] == torch.float32 and kw["device"] != "cpu":
         kw["dtype"] = torch.bfloat16  # the GPU kernels run bf16
+    if not kw["use_pynccl"]:
+        # the reference's switch from its own NCCL kernels to torch.distributed:
+        # here, from the in-kernel NVLink collectives to the NCCL baseline
+        kw["comm"] = "nccl"
     ranks = kw.pop("tensor_parallel_size")
     if kw.get("cp_size", 1) > 1:
         # context parallelism spans every rank (KV split by 64-key tiles,
