@@ -13,8 +13,9 @@
 // 6. Blocks with amax below 2^-124 (or zero) get scale byte 0 and zero
 // elements.
 //
-// The GEMM keeps activations in bf16 (the reference's Marlin MXFP4 MoE is
-// also weight-only: python/minisgl/moe/ + sgl-kernel marlin_moe). Per k-block
+// The GEMM keeps activations in bf16 (weight-only quantisation; the reference
+// has no MXFP4 path, its experts run the bf16 Triton fused_moe kernel of
+// python/minisgl/kernel/triton/fused_moe.py:50-193). Per k-block
 // the producer moves the packed weights (TMA, 128 rows x 32 bytes), their
 // scales (one 256-byte bulk copy) and the bf16 token tile (TMA, 128-byte
 // swizzle) into a deep ring of small stages; four converter warps expand

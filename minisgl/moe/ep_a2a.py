@@ -20,7 +20,8 @@ synchronisation); otherwise with ``torch.distributed.all_to_all_single``
 (NCCL, or gloo on CPU ranks). The peer-store path launches only kernels
 with fixed-capacity buffers, so decode steps run as CUDA graphs even when
 the ranks replay graphs of different batch sizes. The reference has neither DP attention nor expert
-parallelism (its MoE is TP-sharded Triton / Marlin: python/minisgl/moe/).
+parallelism (its MoE is the TP-sharded Triton fused_moe kernel:
+python/minisgl/moe/fused.py, python/minisgl/kernel/triton/fused_moe.py).
 """
 
 from __future__ import annotations

@@ -12,9 +12,9 @@ Per block: e = floor(log2 amax) - 2 (2 is E2M1's largest exponent), scale
 byte e + 127, elements x / 2^e rounded to nearest even onto
 {0, 0.5, 1, 1.5, 2, 3, 4, 6} with saturation at 6. Blocks whose amax is
 below 2^-124 (or zero) get scale byte 0 and zero elements. The reference has
-no quantiser of its own (its MXFP4 path loads pre-quantised checkpoints into
-Marlin kernels: python/minisgl/moe/); this module and ``csrc/mxfp4.cu``
-produce the same bytes.
+no MXFP4 path (its experts run bf16 through the Triton fused_moe kernel,
+python/minisgl/kernel/triton/fused_moe.py); this module and
+``csrc/mxfp4.cu`` produce the same bytes.
 """
 
 from __future__ import annotations
