@@ -431,6 +431,117 @@ void moe_experts_mxfp4(at::Tensor out, const at::Tensor& x, const at::Tensor& w1
                                 static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
 }
 
+// MXFP8 rows for the block-scaled expert GEMM: q [rows, K] E4M3 (uint8) and
+// scale blocks sf [rows / tile, K / 128, 512] (E8M0), row p from x[idx[p] / k]
+// (zeros where idx[p] < 0) or, without idx, from x[p].
+void mx8_quantize(at::Tensor q, at::Tensor sf, const at::Tensor& x, const c10::optional<at::Tensor>& idx, int64_t k,
+                  int64_t rows, int64_t tile) {
+  check_cuda(x, "x");
+  MSG_CHECK(x.dim() == 2 && x.is_contiguous() && x.scalar_type() == at::kBFloat16, "mx8_quantize: x [*, K] bf16");
+  const int64_t K = x.size(1);
+  MSG_CHECK(K % 128 == 0, "mx8_quantize: K % 128 == 0");
+  MSG_CHECK(tile == 16 || tile == 32 || tile == 64 || tile == 128, "mx8_quantize: tile of 16, 32, 64 or 128");
+  MSG_CHECK(rows % tile == 0, "mx8_quantize: rows must be a multiple of the tile");
+  MSG_CHECK(q.scalar_type() == at::kByte && q.is_contiguous() && q.numel() >= rows * K,
+            "mx8_quantize: q uint8 [rows, K]");
+  MSG_CHECK(sf.scalar_type() == at::kByte && sf.is_contiguous() && sf.numel() >= rows / tile * (K / 128) * 512,
+            "mx8_quantize: sf uint8 [rows / tile, K / 128, 512]");
+  const int32_t* ip = nullptr;
+  if (idx.has_value()) {
+    check_i32(*idx, "idx");
+    MSG_CHECK(idx->numel() >= rows, "mx8_quantize: idx [rows]");
+    ip = idx->data_ptr<int32_t>();
+  } else {
+    MSG_CHECK(x.size(0) >= rows, "mx8_quantize: x has fewer than rows rows");
+  }
+  const c10::cuda::CUDAGuard guard(x.device());
+  minisgl::launch_mx8_quantize_rows(q.data_ptr(), sf.data_ptr(), x.data_ptr(), ip, static_cast<int>(k),
+                                    static_cast<int>(rows), static_cast<int>(K), static_cast<int>(tile), nullptr,
+                                    stream_of(x));
+}
+
+// Block-scaled MX routed experts: align -> gather + MXFP8 quantise -> gate_up
+// (tcgen05 kind::mxf8f6f4, E2M1 weights x E4M3 tokens, SiLU x up epilogue)
+// -> MXFP8 quantise -> down -> weighted combine.
+void moe_experts_mx(at::Tensor out, const at::Tensor& x, const at::Tensor& w1q, const at::Tensor& w1sb,
+                    const at::Tensor& w2q, const at::Tensor& w2sb, const at::Tensor& topk_w, const at::Tensor& topk_ids,
+                    int64_t tile, at::Tensor xq, at::Tensor xsf, at::Tensor h, at::Tensor hq, at::Tensor hsf,
+                    at::Tensor ys, at::Tensor sorted_pair, at::Tensor pair_pos, at::Tensor tile_expert,
+                    at::Tensor tile_row, at::Tensor num_tiles, const c10::optional<at::Tensor>& err, bool combine) {
+  check_cuda(x, "x");
+  MSG_CHECK(x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "moe_experts_mx: bf16 x");
+  for (const at::Tensor* t :
+       std::initializer_list<const at::Tensor*>{&w1q, &w2q, &w1sb, &w2sb, &xq, &xsf, &hq, &hsf})
+    MSG_CHECK(t->scalar_type() == at::kByte && t->is_contiguous(), "moe_experts_mx: uint8 weights, scales, rows");
+  const int64_t T = x.size(0), H = x.size(1), E = w1q.size(0), I2 = w1q.size(1), I = I2 / 2, k = topk_ids.size(1);
+  MSG_CHECK(w1q.dim() == 3 && w1q.size(2) * 2 == H && w2q.dim() == 3 && w2q.size(0) == E && w2q.size(1) == H &&
+                w2q.size(2) * 2 == I,
+            "moe_experts_mx: w1 packed [E, 2I, H / 2], w2 packed [E, H, I / 2]");
+  MSG_CHECK(I % 128 == 0 && H % 128 == 0, "moe_experts_mx: I % 128 == 0 and H % 128 == 0");
+  MSG_CHECK(w1sb.numel() == E * I2 * H / 32 && w2sb.numel() == E * H * I / 32,
+            "moe_experts_mx: scale blocks [E, N / 128, K / 128, 512]");
+  MSG_CHECK(topk_ids.scalar_type() == at::kInt && topk_ids.is_contiguous() && topk_ids.size(0) == T,
+            "moe_experts_mx: int32 topk_ids [T, k]");
+  MSG_CHECK(topk_w.scalar_type() == at::kFloat && topk_w.is_contiguous() && topk_w.numel() == T * k,
+            "moe_experts_mx: float32 topk_w [T, k]");
+  MSG_CHECK(tile == 16 || tile == 32 || tile == 64 || tile == 128, "moe_experts_mx: tile of 16, 32, 64 or 128");
+  const int64_t P = T * k + E * (tile - 1);
+  const int64_t Pp = (P + tile - 1) / tile * tile;
+  MSG_CHECK(xq.numel() >= Pp * H && xsf.numel() >= Pp / tile * (H / 128) * 512 && h.numel() >= Pp * I &&
+                hq.numel() >= Pp * I && hsf.numel() >= Pp / tile * (I / 128) * 512 && ys.numel() >= Pp * H &&
+                sorted_pair.numel() >= P && pair_pos.numel() >= T * k && tile_expert.numel() >= P / tile &&
+                tile_row.numel() >= P / tile && num_tiles.numel() >= 1,
+            "moe_experts_mx: scratch too small");
+  MSG_CHECK(h.scalar_type() == at::kBFloat16 && ys.scalar_type() == at::kBFloat16, "moe_experts_mx: bf16 h and ys");
+  MSG_CHECK(!combine || (out.numel() == T * H && out.scalar_type() == at::kBFloat16),
+            "moe_experts_mx: out [T, H] bf16");
+  const c10::cuda::CUDAGuard guard(x.device());
+  cudaStream_t st = stream_of(x);
+  minisgl::MoeAlignArgs al{};
+  al.topk_ids = topk_ids.data_ptr<int32_t>();
+  al.T = static_cast<int>(T);
+  al.k = static_cast<int>(k);
+  al.E = static_cast<int>(E);
+  al.tile = static_cast<int>(tile);
+  al.sorted_pair = sorted_pair.data_ptr<int32_t>();
+  al.pair_pos = pair_pos.data_ptr<int32_t>();
+  al.tile_expert = tile_expert.data_ptr<int32_t>();
+  al.tile_row = tile_row.data_ptr<int32_t>();
+  al.num_tiles = num_tiles.data_ptr<int32_t>();
+  minisgl::launch_moe_align(al, st);
+  // rows of tiles at or beyond num_tiles are never read: only the tiles'
+  // rows are gathered (P / tile tiles at most)
+  const int rows = static_cast<int>(P / tile * tile);
+  minisgl::launch_mx8_quantize_rows(xq.data_ptr(), xsf.data_ptr(), x.data_ptr(), al.sorted_pair, static_cast<int>(k),
+                                    rows, static_cast<int>(H), static_cast<int>(tile), al.num_tiles, st);
+  for (int pass = 0; pass < 2; ++pass) {
+    if (pass == 1)
+      minisgl::launch_mx8_quantize_rows(hq.data_ptr(), hsf.data_ptr(), h.data_ptr(), nullptr, 1, rows,
+                                        static_cast<int>(I), static_cast<int>(tile), al.num_tiles, st);
+    minisgl::MoeMxGemmArgs a{};
+    a.xq = pass == 0 ? xq.data_ptr() : hq.data_ptr();
+    a.sfx = pass == 0 ? xsf.data_ptr() : hsf.data_ptr();
+    a.packed = pass == 0 ? w1q.data_ptr() : w2q.data_ptr();
+    a.sfw = pass == 0 ? w1sb.data_ptr() : w2sb.data_ptr();
+    a.out = pass == 0 ? h.data_ptr() : ys.data_ptr();
+    a.P = static_cast<int>(Pp);
+    a.E = static_cast<int>(E);
+    a.N = static_cast<int>(pass == 0 ? I2 : H);
+    a.K = static_cast<int>(pass == 0 ? H : I);
+    a.ldo = static_cast<int>(pass == 0 ? I : H);
+    a.tile = static_cast<int>(tile);
+    a.silu = pass == 0;
+    a.tile_expert = al.tile_expert;
+    a.tile_row = al.tile_row;
+    a.num_tiles = al.num_tiles;
+    a.err = err_ptr(err);
+    minisgl::launch_moe_mx_gemm(a, st);
+  }
+  if (combine)
+    minisgl::launch_moe_combine(out.data_ptr(), ys.data_ptr(), topk_w.data_ptr<float>(), al.pair_pos,
+                                static_cast<int>(T), static_cast<int>(k), static_cast<int>(H), st);
+}
+
 void moe_combine(at::Tensor out, const at::Tensor& ys, const at::Tensor& topk_w, const at::Tensor& pair_pos, int64_t T,
                  int64_t k) {
   check_cuda(ys, "ys");
@@ -1381,6 +1492,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("w2q"), py::arg("w2s"), py::arg("topk_w"), py::arg("topk_ids"), py::arg("tile"), py::arg("xs"),
         py::arg("h"), py::arg("ys"), py::arg("sorted_pair"), py::arg("pair_pos"), py::arg("tile_expert"),
         py::arg("tile_row"), py::arg("num_tiles"), py::arg("err"), py::arg("combine") = true);
+  m.def("mx8_quantize", &mx8_quantize, py::arg("q"), py::arg("sf"), py::arg("x"), py::arg("idx"), py::arg("k"),
+        py::arg("rows"), py::arg("tile"));
+  m.def("moe_experts_mx", &moe_experts_mx, py::arg("out"), py::arg("x"), py::arg("w1q"), py::arg("w1sb"),
+        py::arg("w2q"), py::arg("w2sb"), py::arg("topk_w"), py::arg("topk_ids"), py::arg("tile"), py::arg("xq"),
+        py::arg("xsf"), py::arg("h"), py::arg("hq"), py::arg("hsf"), py::arg("ys"), py::arg("sorted_pair"),
+        py::arg("pair_pos"), py::arg("tile_expert"), py::arg("tile_row"), py::arg("num_tiles"), py::arg("err"),
+        py::arg("combine") = true);
   m.def("mla_prepare", &mla_prepare, py::arg("q_pe"), py::arg("xs"), py::arg("q"), py::arg("kv_a"),
         py::arg("norm_w"), py::arg("eps"), py::arg("positions"), py::arg("cos_sin"), py::arg("latent"),
         py::arg("out_loc"), py::arg("T_pad"), py::arg("err"), py::arg("cp_size") = 1, py::arg("cp_rank") = 0);

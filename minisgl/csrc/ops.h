@@ -363,6 +363,29 @@ struct MoeMxfp4GemmArgs {
 };
 void launch_moe_mxfp4_gemm(const MoeMxfp4GemmArgs& a, cudaStream_t s);
 
+// Block-scaled MX grouped GEMM (mx_gemm.cu): MXFP4 weights x MXFP8 token rows
+// on tcgen05 kind::mxf8f6f4 with E8M0 scales in the 512-byte scale-block layout.
+struct MoeMxGemmArgs {
+  const void* xq;             // [P, K] E4M3 expert-sorted token rows
+  const void* sfx;            // [P / tile, K / 128, 512] their scale blocks
+  const void* packed;         // [E, N, K / 2] E2M1 weights
+  const void* sfw;            // [E, N / 128, K / 128, 512] weight scale blocks
+  void* out;                  // [P, ldo] bf16 (N / 2 features with silu, else N)
+  int P, E, N, K, ldo, tile;
+  bool silu;                  // interleaved gate|up rows -> silu(gate) * up
+  const int32_t* tile_expert;
+  const int32_t* tile_row;
+  const int32_t* num_tiles;
+  int* err;
+};
+void launch_moe_mx_gemm(const MoeMxGemmArgs& a, cudaStream_t s);
+// MXFP8 (E4M3 + E8M0 per 32) of `rows` bf16 rows of K into q [rows, K] and
+// scale blocks [rows / tile, K / 128, 512]; row p comes from x[idx[p] / k]
+// (zeros where idx[p] < 0) or, without idx, from x[p]. Rows of tiles at or
+// beyond *num_tiles (when given) are skipped.
+void launch_mx8_quantize_rows(void* q, void* sf, const void* x, const int32_t* idx, int k, int rows, int K, int tile,
+                              const int32_t* num_tiles, cudaStream_t s);
+
 // ------------------------------------------------------- NVLink collectives ----
 // kind 0: all-reduce of every rank's partial (bf16, n_elems, at the data
 // offset of each heap) into out (+ residual); kind 1: all-gather of

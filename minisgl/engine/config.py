@@ -41,7 +41,7 @@ class EngineConfig:
     ep_size: int = 1                  # expert parallelism (routed experts split across ranks)
     cp_size: int = 1                  # context parallelism (sequence split across ranks)
     enable_dp_attention: bool = False
-    moe_quant: str = "none"           # "none" | "mxfp4"
+    moe_quant: str = "none"           # "none" | "mxfp4" | "mxfp4-a8"
     comm: str = "fused"               # "fused" (in-kernel NVLink collectives) | "nccl" (baseline)
     weight_seed: int = 0
     dummy_weight_device: Optional[str] = None  # draw random weights here ("cpu" for bit-identical tests)

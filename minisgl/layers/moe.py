@@ -30,7 +30,7 @@ class MoELayer(BaseOP):
                  has_correction_bias: bool = False, reduce_results: bool = True, quant: str = "none",
                  ep_size: int = 1, ep_rank: int = 0) -> None:
         tp = get_tp_info().size
-        if quant not in ("none", "mxfp4"):
+        if quant not in ("none", "mxfp4", "mxfp4-a8"):
             raise ValueError(f"unknown expert quantisation {quant!r}")
         self.num_experts = num_experts
         self.top_k = top_k
@@ -69,18 +69,21 @@ class MoELayer(BaseOP):
         w = self.gate_up_proj.view(E, 2, n // 64, 64, H).transpose(1, 2)
         self.gate_up_proj = w.reshape(E, 2 * n, H).contiguous()
         self._interleaved = True
-        if self._quant == "mxfp4":
+        if self._quant in ("mxfp4", "mxfp4-a8"):
             self.quantize()
 
     def quantize(self) -> None:
         """Replace the bf16 expert weights by MXFP4 (E2M1 + E8M0 per 32; see
         minisgl.quant.mxfp4). On the GPU the bf16 copies are released; on
         the CPU they are kept for inspection."""
-        from minisgl.quant import quantize_mxfp4
+        from minisgl.quant import MxfpExperts, block_scales, quantize_mxfp4
 
         w1q, w1s = quantize_mxfp4(self.gate_up_proj.to(torch.bfloat16).contiguous())
         w2q, w2s = quantize_mxfp4(self.down_proj.to(torch.bfloat16).contiguous())
-        self._mxfp4 = (w1q, w1s, w2q, w2s)
+        self._mxfp4 = MxfpExperts((w1q, w1s, w2q, w2s))
+        if self._quant == "mxfp4-a8":
+            # the block-scaled GEMM reads the scales in 512-byte scale blocks
+            self._mxfp4.blocked = (block_scales(w1s), block_scales(w2s))
         if self.gate_up_proj.is_cuda:
             self.gate_up_proj = self.gate_up_proj.new_empty(0)
             self.down_proj = self.down_proj.new_empty(0)

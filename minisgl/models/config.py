@@ -56,7 +56,7 @@ class ModelConfig:
     scoring_func: str = "softmax"
     attention_bias: bool = False
     # runtime choices that shape the layers (not part of the HF config)
-    moe_quant: str = "none"      # "none" | "mxfp4": routed expert weights in MXFP4
+    moe_quant: str = "none"      # "none" | "mxfp4" | "mxfp4-a8": routed expert weights in MXFP4 (a8: MXFP8 activations)
     ep_size: int = 1             # routed experts split over this many ranks
     ep_rank: int = 0
     extra: Dict[str, Any] = field(default_factory=dict)

@@ -60,6 +60,11 @@ class FusedMoe(BaseMoeBackend):
         if expert_offset:
             topk_ids = topk_ids - expert_offset  # global -> local ids; others fall outside [0, E_local)
         if not hidden_states.is_cuda:
+            if getattr(mxfp4, "blocked", None) is not None and interleaved:
+                from minisgl.quant import moe_experts_mx_reference
+
+                # the block-scaled path's statement: MXFP8 token and SiLU rows
+                return moe_experts_mx_reference(hidden_states, *mxfp4, topk_w, topk_ids).to(hidden_states.dtype)
             if mxfp4 is not None:
                 w1, w2 = self._cpu_weights(mxfp4)
             return moe_reference(hidden_states, w1, w2, topk_w, topk_ids, activation, interleaved)
@@ -67,5 +72,8 @@ class FusedMoe(BaseMoeBackend):
             raise RuntimeError("minisgl: the CUDA MoE path needs SiLU experts with gate|up rows interleaved "
                                "in 64-row blocks (MoELayer does this after loading)")
         if mxfp4 is not None:
+            blocked = getattr(mxfp4, "blocked", None)
+            if blocked is not None:  # MXFP8 activations on the block-scaled tensor cores
+                return ops.moe_experts_mx(hidden_states, mxfp4[0], blocked[0], mxfp4[2], blocked[1], topk_w, topk_ids)
             return ops.moe_experts_mxfp4(hidden_states, *mxfp4, topk_w, topk_ids)
         return ops.moe_experts(hidden_states, w1, w2, topk_w, topk_ids)

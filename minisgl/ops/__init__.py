@@ -831,7 +831,7 @@ def moe_experts(x: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor, topk_w: tor
     tile_expert = torch.empty(P // tile, dtype=i32, device=dev)
     tile_row = torch.empty(P // tile, dtype=i32, device=dev)
     num_tiles = torch.empty(1, dtype=i32, device=dev)
-    _count(6)
+    _count(5)  # align, gather, two grouped GEMMs, combine
     native().moe_experts(out, x.contiguous(), w1, w2, topk_w.float().contiguous(), topk_ids.to(i32).contiguous(),
                          tile, xs, h, ys, sorted_pair, pair_pos, tile_expert, tile_row, num_tiles, error_word(dev))
     return out
@@ -869,10 +869,61 @@ def moe_experts_mxfp4(x: torch.Tensor, w1q: torch.Tensor, w1s: torch.Tensor, w2q
     tile_expert = torch.empty(P // tile, dtype=i32, device=dev)
     tile_row = torch.empty(P // tile, dtype=i32, device=dev)
     num_tiles = torch.empty(1, dtype=i32, device=dev)
-    _count(6)
+    _count(5)  # align, gather, two grouped GEMMs, combine
     native().moe_experts_mxfp4(out, x.contiguous(), w1q, w1s, w2q, w2s, topk_w.float().contiguous(),
                                topk_ids.to(i32).contiguous(), tile, xs, h, ys, sorted_pair, pair_pos, tile_expert,
                                tile_row, num_tiles, error_word(dev))
+    return out
+
+
+def mx8_quantize(x: torch.Tensor, tile: int, idx: Optional[torch.Tensor] = None, k: int = 1,
+                 rows: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
+    """MXFP8 rows for the block-scaled expert GEMM (E4M3 + E8M0 per 32, as
+    minisgl.quant.quantize_mx8_reference states it): returns (q uint8
+    [rows, K], scale blocks uint8 [rows / tile, K / 128, 512]). Row p is
+    x[idx[p] // k] (zeros where idx[p] < 0) or, without idx, x[p]."""
+    K = x.shape[1]
+    rows = rows if rows is not None else (idx.shape[0] if idx is not None else x.shape[0])
+    q = torch.empty(rows, K, dtype=torch.uint8, device=x.device)
+    sf = torch.empty(rows // tile, K // 128, 512, dtype=torch.uint8, device=x.device)
+    _count()
+    native().mx8_quantize(q, sf, x.contiguous(), None if idx is None else idx.to(torch.int32).contiguous(), k, rows,
+                          tile)
+    return q, sf
+
+
+def moe_experts_mx(x: torch.Tensor, w1q: torch.Tensor, w1sb: torch.Tensor, w2q: torch.Tensor, w2sb: torch.Tensor,
+                   topk_w: torch.Tensor, topk_ids: torch.Tensor, tile: int = 0) -> torch.Tensor:
+    """``moe_experts`` on the block-scaled tensor cores: MXFP4 expert weights
+    (packed [E, N, K / 2] with scale blocks [E, N / 128, K / 128, 512] from
+    minisgl.quant.block_scales) times MXFP8 token rows (quantised on the
+    fly, per 32 along K), tcgen05 .kind::mxf8f6f4 with E8M0 scales. Oracle:
+    minisgl.quant.moe_experts_mx_reference."""
+    T, H = x.shape
+    E, I2 = w1q.shape[0], w1q.shape[1]
+    I, k = I2 // 2, topk_ids.shape[1]
+    out = torch.empty(T, H, dtype=x.dtype, device=x.device)
+    if T == 0:
+        return out
+    tile = tile or moe_tile(T, k, E)
+    P = T * k + E * (tile - 1)
+    Pp = (P + tile - 1) // tile * tile
+    dev, i32, u8 = x.device, torch.int32, torch.uint8
+    xq = torch.empty(Pp, H, dtype=u8, device=dev)
+    xsf = torch.empty(Pp // tile, H // 128, 512, dtype=u8, device=dev)
+    h = torch.empty(Pp, I, dtype=x.dtype, device=dev)
+    hq = torch.empty(Pp, I, dtype=u8, device=dev)
+    hsf = torch.empty(Pp // tile, I // 128, 512, dtype=u8, device=dev)
+    ys = torch.empty(Pp, H, dtype=x.dtype, device=dev)
+    sorted_pair = torch.empty(P, dtype=i32, device=dev)
+    pair_pos = torch.empty(T * k, dtype=i32, device=dev)
+    tile_expert = torch.empty(P // tile, dtype=i32, device=dev)
+    tile_row = torch.empty(P // tile, dtype=i32, device=dev)
+    num_tiles = torch.empty(1, dtype=i32, device=dev)
+    _count(6)  # align, gather + quantise, gate_up GEMM, quantise, down GEMM, combine
+    native().moe_experts_mx(out, x.contiguous(), w1q, w1sb, w2q, w2sb, topk_w.float().contiguous(),
+                            topk_ids.to(i32).contiguous(), tile, xq, xsf, h, hq, hsf, ys, sorted_pair, pair_pos,
+                            tile_expert, tile_row, num_tiles, error_word(dev))
     return out
 
 
@@ -898,7 +949,7 @@ def moe_experts_rows(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tens
     tile_row = torch.empty(P // tile, dtype=i32, device=dev)
     num_tiles = torch.empty(1, dtype=i32, device=dev)
     out = torch.empty(0, H, dtype=x.dtype, device=dev)
-    _count(5)
+    _count(4)  # align, gather, two grouped GEMMs
     if mxfp4 is not None:
         native().moe_experts_mxfp4(out, x, *mxfp4, topk_w.float().contiguous(), topk_ids.to(i32).contiguous(), tile,
                                    xs, h, ys, sorted_pair, pair_pos, tile_expert, tile_row, num_tiles,

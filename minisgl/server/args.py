@@ -77,7 +77,9 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--expert-parallel-size", "--ep-size", dest="ep_size", type=int, default=1)
     p.add_argument("--context-parallel-size", "--cp-size", dest="cp_size", type=int, default=1)
     p.add_argument("--enable-dp-attention", action="store_true")
-    p.add_argument("--moe-quant", choices=["none", "mxfp4"], default="none")
+    p.add_argument("--moe-quant", choices=["none", "mxfp4", "mxfp4-a8"], default="none",
+                   help="routed experts: bf16, MXFP4 weights with bf16 activations, or MXFP4 weights x MXFP8 "
+                        "activations on the block-scaled tensor cores")
     p.add_argument("--comm", choices=["nccl", "fused"], default="fused",
                    help="TP collectives: in-kernel NVLink collectives (default) or NCCL (baseline); "
                         "ignored on --device cpu")

@@ -36,6 +36,7 @@ SOURCES = [
     "minisgl/csrc/symm.cu",
     "minisgl/csrc/mla.cu",
     "minisgl/csrc/mxfp4.cu",
+    "minisgl/csrc/mx_gemm.cu",
     "minisgl/csrc/ep.cu",
 ]
 
