@@ -317,6 +317,37 @@ def bench_moe_mxfp4(T: int, E: int, k: int, H: int, I: int, peaks) -> Dict:
             "frac_hbm": round(gbs / peaks["hbm_gbs"], 3), "ms_by_token_tile": tiles}
 
 
+def bench_moe_mx(T: int, E: int, k: int, H: int, I: int, peaks) -> Dict:
+    """Routed experts on the block-scaled tensor cores (MXFP4 weights x
+    MXFP8 activations, ``--moe-quant mxfp4-a8``) at the same shapes as
+    bench_moe_mxfp4, with the error against the path's PyTorch statement
+    (max |got - want| over max |want|) and the W4A16 time beside it."""
+    from minisgl.quant import block_scales, moe_experts_mx_reference, quantize_mxfp4
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    w1 = (torch.randn(E, 2 * I, H, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, I, device="cuda", generator=g) * 0.02).to(torch.bfloat16)
+    q1, q2 = quantize_mxfp4(w1), quantize_mxfp4(w2)
+    b1, b2 = block_scales(q1[1]), block_scales(q2[1])
+    x = torch.randn(T, H, device="cuda", generator=g).to(torch.bfloat16)
+    ids = torch.stack([torch.randperm(E, device="cuda", generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    tw = torch.full((T, k), 1.0 / k, device="cuda")
+    got = ops.moe_experts_mx(x, q1[0], b1, q2[0], b2, tw, ids)
+    torch.cuda.synchronize()
+    ops.check_device_errors(torch.device("cuda", torch.cuda.current_device()))
+    want = moe_experts_mx_reference(x, *q1, *q2, tw, ids).float()  # PyTorch ops, on the GPU
+    err = ((got.float() - want).abs().max() / want.abs().max()).item()
+    ms = time_kernel(lambda: ops.moe_experts_mx(x, q1[0], b1, q2[0], b2, tw, ids))
+    ms_w4a16 = time_kernel(lambda: ops.moe_experts_mxfp4(x, *q1, *q2, tw, ids))
+    hit = int(torch.unique(ids).numel())
+    wbytes = hit * (3 * I * H) * 0.5 * (1 + 1 / 16)
+    nbytes = wbytes + 2 * T * k * H + 2 * T * H  # MXFP4 weights, MXFP8 rows in, bf16 rows out
+    gbs = nbytes / ms / 1e6
+    return {"kernel": "moe_experts_mx", "T": T, "E": E, "k": k, "H": H, "I": I, "experts_hit": hit,
+            "ms": round(ms, 4), "w4a16_ms": round(ms_w4a16, 4), "max_rel_err": round(err, 5),
+            "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
+
+
 def bench_sample(B: int, V: int, peaks) -> List[Dict]:
     """Sampling from fp32 logits [B, V]: argmax (greedy) and Gumbel-max with
     temperature (counter-based noise); bytes = the logits read once."""
@@ -730,6 +761,8 @@ def main() -> None:
                                                                                                   name)))
     for T in (16, 256):
         cases.append((f"moe_mxfp4 T={T}", lambda T=T: bench_moe_mxfp4(T, 16, 8, 7168, 2048, peaks)))
+    for T in (16, 256):
+        cases.append((f"moe_mx T={T}", lambda T=T: bench_moe_mx(T, 16, 8, 7168, 2048, peaks)))
     for M in (1, 8, 32, 64, 128, 192, 256):
         cases.append((f"layer_chain M={M};", lambda M=M: bench_layer_chain(M, peaks)))
     cases.append(("rowkernels M=256", lambda: bench_row_kernels(256, peaks)))

@@ -30,7 +30,7 @@ def main() -> None:
     p.add_argument("--layers", type=int, default=4)
     p.add_argument("--experts", type=int, default=48)
     p.add_argument("--reqs", type=int, default=64)
-    p.add_argument("--quant", default="mxfp4", choices=["mxfp4", "none"])
+    p.add_argument("--quant", default="mxfp4", choices=["mxfp4", "mxfp4-a8", "none"])
     args = p.parse_args()
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
