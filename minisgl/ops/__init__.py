@@ -67,10 +67,19 @@ def gemm_workspace(device: torch.device) -> torch.Tensor:
     return ws
 
 
+def _device_key(device) -> tuple:
+    """(type, index) of a device; a CUDA device without an index is the
+    current one, so torch.device("cuda") and the tensors' cuda:N agree."""
+    device = torch.device(device)
+    if device.type == "cuda" and device.index is None:
+        return ("cuda", torch.cuda.current_device())
+    return (device.type, device.index)
+
+
 def error_word(device: torch.device) -> torch.Tensor:
     """Per-device int32[2]: (error code, site) written by kernels whose bounded
     waits ran out. Zero means no error."""
-    key = (device.type, device.index)
+    key = _device_key(device)
     w = _ERR_WORDS.get(key)
     if w is None:
         w = torch.zeros(2, dtype=torch.int32, device=device)
@@ -102,7 +111,7 @@ def check_device_errors(device: torch.device) -> None:
     """Raise if a kernel on ``device`` recorded an error (and clear it):
     CommTimeoutError for a peer wait that ran out, DeviceWaitTimeout for a
     pipeline wait, RuntimeError otherwise."""
-    w = _ERR_WORDS.get((device.type, device.index))
+    w = _ERR_WORDS.get(_device_key(device))
     if w is None:
         return
     code, site = w.tolist()
