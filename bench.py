@@ -32,6 +32,18 @@ queueing + prefill under saturation; p50 TPOT is the inter-token time.
 baseline/_ref) on the same pool through its own ``LLM`` class; see
 baseline/run_reference.py. ``--shape qwen3-0.6b`` selects the reference's
 offline-benchmark shape (prompts and outputs uniform in [100, 1024]).
+
+``--shape kimi-k2`` serves the Kimi-K2-shape MLA + MoE decoder (61 layers,
+384 routed experts top-8 with MXFP4 weights, a bf16 shared expert) with
+attention data-parallel and the routed experts split over the N ranks
+(EP = N, tokens dispatched to their experts' ranks): 512 requests, prompts
+uniform in [512, 4096], outputs uniform in [128, 1024]. Each rank serves its
+own requests; a step is ``--step-tokens`` output tokens summed over the
+ranks (the count is all-reduced every lockstep iteration, so all ranks cut
+the run at the same iteration). The full shape needs 8 GPUs (about 67 GB of
+MXFP4 experts and 23 GB of replicated bf16 weights per rank); ``--layers``
+runs a slice on fewer. The reference has no MLA, expert parallelism, DP
+attention or MXFP4, so its arm reports itself unavailable for this shape.
 """
 
 from __future__ import annotations
@@ -49,7 +61,8 @@ from typing import Dict, List, Optional, Tuple
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "output tok/s (whole box, device-timed, max over ranks)"
-MODEL_NAMES = {"qwen3-32b": "Qwen3-32B-shape", "qwen3-0.6b": "Qwen3-0.6B-shape", "qwen3-8b": "Qwen3-8B-shape"}
+MODEL_NAMES = {"qwen3-32b": "Qwen3-32B-shape", "qwen3-0.6b": "Qwen3-0.6B-shape", "qwen3-8b": "Qwen3-8B-shape",
+               "kimi-k2": "Kimi-K2-shape"}
 PAGE_SIZE = 64
 
 
@@ -60,13 +73,19 @@ def parse_args(argv=None):
     p.add_argument("--warmup", type=int, default=3)
     p.add_argument("--impl", choices=["minisgl", "reference"], default="minisgl")
     p.add_argument("--shape", default="qwen3-32b")
-    p.add_argument("--num-reqs", type=int, default=1000)
+    p.add_argument("--layers", type=int, default=None, help="kimi-k2: decoder layers (default: all 61)")
+    p.add_argument("--moe-quant", default="mxfp4", choices=["mxfp4", "mxfp4-a8", "none"],
+                   help="kimi-k2: routed expert weights")
+    p.add_argument("--num-reqs", type=int, default=None, help="request pool (default 1000; kimi-k2: 512)")
     p.add_argument("--step-tokens", type=int, default=8192)
     p.add_argument("--temperature", type=float, default=0.6)
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"])
     p.add_argument("--seed", type=int, default=0)
     p.add_argument("--json-out", default="")
-    return p.parse_args(argv)
+    args = p.parse_args(argv)
+    if args.num_reqs is None:
+        args.num_reqs = 512 if args.shape == "kimi-k2" else 1000
+    return args
 
 
 def dist_env() -> Tuple[int, int, int]:
@@ -92,6 +111,11 @@ def make_pool(shape: str, num_reqs: int, seed: int, vocab_limit: int = 10000) ->
             prompts.append([rng.randrange(vocab_limit) for _ in range(rng.randint(100, 1024))])
             outs.append(rng.randint(100, 1024))
         return prompts, outs
+    if shape == "kimi-k2":  # the expert-parallel serving config
+        for _ in range(num_reqs):
+            prompts.append([rng.randrange(vocab_limit) for _ in range(rng.randint(512, 4096))])
+            outs.append(rng.randint(128, 1024))
+        return prompts, outs
     prefixes = [[rng.randrange(vocab_limit) for _ in range(rng.randint(512, 2048))] for _ in range(50)]
     for _ in range(num_reqs):
         n = _lognormal_len(rng, 1024, 0.8, 32, 16384)
@@ -115,10 +139,11 @@ class StepMeter:
     engine's offline result hook); at every boundary it records a CUDA event
     on the engine stream and the host clock."""
 
-    def __init__(self, stream, step_tokens: int, warmup: int, steps: int, counters=None) -> None:
+    def __init__(self, stream, step_tokens: int, warmup: int, steps: int, counters=None, group=None) -> None:
         import torch
 
         self.torch = torch
+        self.group = group  # DP attention: count output tokens over all ranks (lockstep iterations)
         self.stream = stream
         self.step_tokens = step_tokens
         self.warmup, self.steps = warmup, steps
@@ -138,6 +163,12 @@ class StepMeter:
 
     def on_reply(self, replies) -> None:
         now = time.perf_counter()
+        if self.group is not None:
+            import torch.distributed as dist
+
+            n = self.torch.tensor([len(replies)], dtype=self.torch.int64)
+            dist.all_reduce(n, group=self.group)
+            self.tokens += int(n) - len(replies)  # the other ranks' tokens; this rank's follow
         for m in replies:
             self.tokens += 1
             uid = m.uid
@@ -192,10 +223,10 @@ def metered_llm_class(base):
 
 
 def run_metered(llm, prompts, outs, temperature, stream, args, sampling_params_cls,
-                counters=None) -> Dict[str, float]:
+                counters=None, group=None) -> Dict[str, float]:
     """Serve the pool until W + K steps have passed; returns the meter's result."""
     params = [sampling_params_cls(temperature=temperature, ignore_eos=True, max_tokens=o) for o in outs]
-    llm.meter = StepMeter(stream, args.step_tokens, args.warmup, args.steps, counters)
+    llm.meter = StepMeter(stream, args.step_tokens, args.warmup, args.steps, counters, group)
     try:
         llm.generate(prompts, params)
     except StopRun:
@@ -275,6 +306,11 @@ def config_of(args, world: int) -> Dict[str, object]:
            "l2": "inputs larger than L2 (tens of GB of weights and KV cache streamed per step)"}
     if args.shape == "qwen3-0.6b":
         cfg["seq_len"] = "prompt U[100,1024] + output U[100,1024]"
+    elif args.shape == "kimi-k2":
+        cfg.update(seq_len="prompt U[512,4096] + output U[128,1024]", global_batch=args.num_reqs,
+                   parallelism=f"dp-attention{world}+ep{world}" if world > 1 else "single GPU",
+                   layers=args.layers or 61, routed_experts=f"384 top-8, {args.moe_quant}",
+                   latency_note="TTFT / TPOT of rank 0's requests")
     else:
         cfg["seq_len"] = ("prompt lognormal(median 1024) in [32,16384] + output lognormal(median 256) in [16,2048]; "
                           "30% share one of 50 prefixes of 512-2048 tokens")
@@ -307,31 +343,45 @@ def run_minisgl(args) -> None:
     if world > 1:  # the engine joins this group (NCCL for tensors, gloo for the host side)
         dist.init_process_group("cpu:gloo,cuda:nccl", timeout=timedelta(seconds=300),
                                 device_id=torch.device(f"cuda:{local}"))
-    model_dir = make_model_dir(args.shape)
     prompts, outs = make_pool(args.shape, args.num_reqs, args.seed)
+    moe = args.shape == "kimi-k2"
+    if moe:  # attention data-parallel, routed experts split over the ranks (EP = N), MXFP4 experts
+        overrides = {"num_hidden_layers": args.layers} if args.layers else None
+        model_dir = make_model_dir(args.shape, overrides=overrides)
+        extra = dict(enable_dp_attention=world > 1, moe_quant=args.moe_quant, max_seq_len_override=5120,
+                     max_extend_tokens=8192)
+    else:
+        model_dir = make_model_dir(args.shape)
+        extra = dict(max_seq_len_override=20480, max_extend_tokens=16384)
     llm = metered_llm_class(LLM)(
         model_dir, dtype=torch.bfloat16, use_dummy_weight=True, device=f"cuda:{local}",
-        tp_info=DistributedInfo(rank, world), comm=args.comm, max_seq_len_override=20480,
-        max_extend_tokens=16384, cuda_graph_max_bs=256, max_running_req=256, page_size=PAGE_SIZE)
+        tp_info=DistributedInfo(rank, world), comm=args.comm, cuda_graph_max_bs=256, max_running_req=256,
+        page_size=PAGE_SIZE, **extra)
+    dp_group = llm.tp_cpu_group if moe and world > 1 else None
     launches0 = ops.LAUNCHES[0]
     sampler = ClockSampler(list(range(world))) if rank == 0 else None
     if sampler is not None:
         sampler.start()
     res = run_metered(llm, prompts, outs, args.temperature, llm.engine.stream, args, SamplingParams,
-                      counters=lambda: (llm.h2d_bytes, llm.d2h_bytes))
+                      counters=lambda: (llm.h2d_bytes, llm.d2h_bytes), group=dp_group)
     clocks = sampler.stop() if sampler is not None else {}
     launches = ops.LAUNCHES[0] - launches0
     if getattr(llm, "profiler", None) is not None and rank == 0:  # MINISGL_PROFILE_STEPS=1: time per phase
         print(json.dumps({"step_profile": llm.profiler.summary()}), file=sys.stderr, flush=True)
     max_dev_ms, max_wall = reduce_over_ranks([res["dev_ms"], res["wall_s"]], "max")
     tot_launches, = reduce_over_ranks([launches], "sum")
+    if dp_group is not None:  # each rank moved its own requests' bytes
+        res["h2d"], res["d2h"] = reduce_over_ranks([res["h2d"], res["d2h"]], "sum")
     if rank == 0:
-        tokens = res["tokens"]  # every rank serves the same requests (tensor parallel)
+        # tensor parallel: every rank serves the same requests; DP attention:
+        # the meter already summed the ranks' tokens
+        tokens = res["tokens"]
         value = tokens / (max_dev_ms / 1000.0)
         emit({
             "metric": METRIC, "value": round(value, 1), "unit": "tok/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(max_dev_ms / args.steps, 2), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong", "vs_baseline": None,
+            "dtype": "bf16" if not moe else f"bf16 (routed experts {args.moe_quant})",
             "data": "synthetic (random token ids, random-init N(0,0.02) weights)",
             "config": dict(config_of(args, world), comm=args.comm),
             "clocks": clocks,
@@ -352,6 +402,11 @@ def run_reference(args) -> None:
     """Run the unmodified reference (baseline/_ref) on the same pool: one
     subprocess per rank whose import path holds only the reference package."""
     rank, world, local = dist_env()
+    if args.shape == "kimi-k2":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no MLA / DeepSeek-V3 "
+                              "architecture, expert parallelism, DP attention or MXFP4 experts"}))
+        return
     ref_dir = os.path.join(ROOT, "baseline", "_ref")
     if not os.path.isdir(os.path.join(ref_dir, "minisgl")):
         if rank == 0:

@@ -26,7 +26,7 @@ from minisgl.core import FusedSample, Batch, Context, Req, reset_global_ctx, set
 from minisgl.kvcache import create_kvcache_pool
 from minisgl.layers import set_rope_device
 from minisgl.utils import fault
-from minisgl.models import create_model, load_weight, random_weights
+from minisgl.models import LazyRandomWeights, create_model, load_weight, random_weights
 from minisgl.moe import create_moe_backend
 from minisgl.parallel import (DistributedCommunicator, destroy_distributed, get_tp_info, reset_cp_info, reset_dp_info,
                               reset_tp_info, set_cp_info, set_dp_info, set_tp_info)
@@ -279,8 +279,11 @@ class Engine:
         if config.use_dummy_weight:
             mcfg = config.model_config
             first = mcfg.ep_rank * (mcfg.num_experts // mcfg.ep_size) if mcfg.ep_size > 1 else 0
-            return random_weights(self.model.state_dict(), self.device, seed=config.weight_seed,
-                                  gen_device=config.dummy_weight_device, first_expert=first)
+            # quantised experts: draw each weight as the model takes it, so the
+            # MoE layers quantise one layer's bf16 experts at a time
+            draw = LazyRandomWeights if mcfg.moe_quant != "none" else random_weights
+            return draw(self.model.state_dict(), self.device, seed=config.weight_seed,
+                        gen_device=config.dummy_weight_device, first_expert=first)
         out: Dict[str, torch.Tensor] = {}
         mcfg = config.model_config
         for name, t in load_weight(config.model_path, self.device, ep_size=mcfg.ep_size, ep_rank=mcfg.ep_rank):

@@ -62,8 +62,10 @@ class MoELayer(BaseOP):
         then the matching 64 up rows): the layout whose grouped GEMM applies
         SiLU x up in its epilogue."""
         super().post_load()
+        if self._interleaved:  # already done when the weights were loaded
+            return
         n = self.gate_up_proj.shape[1] // 2
-        if self._interleaved or self.activation != "silu" or n % 64 != 0:
+        if self.activation != "silu" or n % 64 != 0:
             return
         E, _, H = self.gate_up_proj.shape
         w = self.gate_up_proj.view(E, 2, n // 64, 64, H).transpose(1, 2)
@@ -71,6 +73,14 @@ class MoELayer(BaseOP):
         self._interleaved = True
         if self._quant in ("mxfp4", "mxfp4-a8"):
             self.quantize()
+
+    def load_state_dict(self, state_dict, *, prefix: str = "", _internal: bool = False) -> None:
+        super().load_state_dict(state_dict, prefix=prefix, _internal=_internal)
+        if self._quant != "none":
+            # interleave and quantise now rather than after the whole model is
+            # in place: with weights drawn or read as they are taken, only this
+            # layer's bf16 experts are alive
+            self.post_load()
 
     def quantize(self) -> None:
         """Replace the bf16 expert weights by MXFP4 (E2M1 + E8M0 per 32; see

@@ -128,6 +128,34 @@ def load_weight(model_path: str, device: torch.device, *, ep_size: int = 1,
         raise RuntimeError(f"checkpoint is incomplete: {sorted(merges)[:4]} {sorted(experts)[:4]}")
 
 
+def _random_tensor(name: str, ref: torch.Tensor, device: torch.device, gen: torch.Generator,
+                   gen_dev: torch.device, seed: int, std: float, first_expert: int) -> torch.Tensor:
+    """The random-init value of one named weight (its seed depends only on
+    the name, so the order in which weights are drawn does not matter)."""
+    import zlib
+
+    dt = ref.dtype  # the model was built with the right dtype per tensor
+    if name.endswith("norm.weight") or "layernorm" in name or name.endswith("_norm.weight"):
+        return torch.ones(ref.shape, dtype=dt, device=device)
+    if "bias" in name:
+        return torch.zeros(ref.shape, dtype=dt, device=device)
+    if name.endswith(("experts.gate_up_proj", "experts.down_proj")) and ref.dim() == 3:
+        # stacked routed experts: one seed per global expert, so under
+        # expert parallelism every rank holds its own experts' values
+        t = torch.empty(ref.shape, dtype=dt, device=device)
+        for e in range(ref.shape[0]):
+            gen.manual_seed(seed * 1000003 + zlib.crc32(f"{name}.{first_expert + e}".encode()))
+            part = torch.empty(ref.shape[1:], dtype=torch.float32 if gen_dev.type == "cpu" else dt, device=gen_dev)
+            part.normal_(0.0, std, generator=gen)
+            t[e].copy_(part)
+        return t
+    # per-name seed: identical on every rank, so replicated weights agree
+    gen.manual_seed(seed * 1000003 + zlib.crc32(name.encode()))
+    t = torch.empty(ref.shape, dtype=torch.float32 if gen_dev.type == "cpu" else dt, device=gen_dev)
+    t.normal_(0.0, std, generator=gen)
+    return t.to(device=device, dtype=dt)
+
+
 def random_weights(shapes: Dict[str, torch.Tensor], device: torch.device, seed: int = 0,
                    std: float = 0.02, gen_device: Optional[torch.device] = None,
                    first_expert: int = 0) -> Dict[str, torch.Tensor]:
@@ -135,33 +163,49 @@ def random_weights(shapes: Dict[str, torch.Tensor], device: torch.device, seed: 
     ``shapes`` maps names to (meta) tensors giving shape and dtype. With
     ``gen_device`` the numbers are drawn there (e.g. on the CPU, so a GPU
     engine and the CPU oracle get identical weights) and then moved."""
-    import zlib
+    lazy = LazyRandomWeights(shapes, device, seed, std, gen_device, first_expert)
+    return {name: lazy[name] for name in sorted(shapes)}
 
-    gen_dev = torch.device(gen_device) if gen_device is not None else torch.device(device)
-    gen = torch.Generator(device=gen_dev)
-    out: Dict[str, torch.Tensor] = {}
-    for name in sorted(shapes):
-        ref = shapes[name]
-        dt = ref.dtype  # the model was built with the right dtype per tensor
-        if name.endswith("norm.weight") or "layernorm" in name or name.endswith("_norm.weight"):
-            t = torch.ones(ref.shape, dtype=dt, device=device)
-        elif "bias" in name:
-            t = torch.zeros(ref.shape, dtype=dt, device=device)
-        elif name.endswith(("experts.gate_up_proj", "experts.down_proj")) and ref.dim() == 3:
-            # stacked routed experts: one seed per global expert, so under
-            # expert parallelism every rank holds its own experts' values
-            t = torch.empty(ref.shape, dtype=dt, device=device)
-            for e in range(ref.shape[0]):
-                gen.manual_seed(seed * 1000003 + zlib.crc32(f"{name}.{first_expert + e}".encode()))
-                part = torch.empty(ref.shape[1:], dtype=torch.float32 if gen_dev.type == "cpu" else dt,
-                                   device=gen_dev)
-                part.normal_(0.0, std, generator=gen)
-                t[e].copy_(part)
-        else:
-            # per-name seed: identical on every rank, so replicated weights agree
-            gen.manual_seed(seed * 1000003 + zlib.crc32(name.encode()))
-            t = torch.empty(ref.shape, dtype=torch.float32 if gen_dev.type == "cpu" else dt, device=gen_dev)
-            t.normal_(0.0, std, generator=gen)
-            t = t.to(device=device, dtype=dt)
-        out[name] = t
-    return out
+
+class LazyRandomWeights:
+    """``random_weights`` drawn one tensor at a time, when the model's
+    ``load_state_dict`` takes it (``pop``): the same values, but the peak
+    memory of loading is the model plus one tensor instead of two copies of
+    the model. With quantised experts, whose layer quantises them as soon as
+    they are loaded, only one layer's bf16 experts exist at any time (a
+    Kimi-K2-shape model holds 254 GB of bf16 experts per rank at EP8, 67 GB
+    once quantised to MXFP4). Supports what ``load_state_dict`` uses: ``in``,
+    ``pop``, ``len`` and iteration over the names not yet taken."""
+
+    def __init__(self, shapes: Dict[str, torch.Tensor], device: torch.device, seed: int = 0, std: float = 0.02,
+                 gen_device: Optional[torch.device] = None, first_expert: int = 0) -> None:
+        self._shapes = dict(shapes)
+        self._device = torch.device(device)
+        self._gen_dev = torch.device(gen_device) if gen_device is not None else self._device
+        self._gen = torch.Generator(device=self._gen_dev)
+        self._seed, self._std, self._first = seed, std, first_expert
+
+    def __contains__(self, name: object) -> bool:
+        return name in self._shapes
+
+    def __len__(self) -> int:
+        return len(self._shapes)
+
+    def __iter__(self):
+        return iter(list(self._shapes))
+
+    def keys(self):
+        return list(self._shapes)
+
+    def __getitem__(self, name: str) -> torch.Tensor:
+        return _random_tensor(name, self._shapes[name], self._device, self._gen, self._gen_dev, self._seed,
+                              self._std, self._first)
+
+    def pop(self, name: str, *default):
+        if name not in self._shapes:
+            if default:
+                return default[0]
+            raise KeyError(name)
+        t = self[name]
+        del self._shapes[name]
+        return t
