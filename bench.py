@@ -44,6 +44,15 @@ the run at the same iteration). The full shape needs 8 GPUs (about 67 GB of
 MXFP4 experts and 23 GB of replicated bf16 weights per rank); ``--layers``
 runs a slice on fewer. The reference has no MLA, expert parallelism, DP
 attention or MXFP4, so its arm reports itself unavailable for this shape.
+
+``--shape kimi-k2-cp`` is the long-context config: an 8-layer slice of the
+Kimi-K2 shape (MXFP4 experts) with context parallelism over the N ranks
+(CP = EP = N: prefill tokens sharded, KV pages spread over the ranks) on a
+batch of 4 requests of 131072 prompt tokens, then 256 greedy output tokens
+each (``--prompt-len`` / ``--num-reqs`` scale it down). A step is one whole
+batch; the line reports output tok/s over the device time of the K timed
+batches, with the prefill part (until every request has its first token)
+and the decode part beside it.
 """
 
 from __future__ import annotations
@@ -62,7 +71,7 @@ from typing import Dict, List, Optional, Tuple
 ROOT = os.path.dirname(os.path.abspath(__file__))
 METRIC = "output tok/s (whole box, device-timed, max over ranks)"
 MODEL_NAMES = {"qwen3-32b": "Qwen3-32B-shape", "qwen3-0.6b": "Qwen3-0.6B-shape", "qwen3-8b": "Qwen3-8B-shape",
-               "kimi-k2": "Kimi-K2-shape"}
+               "kimi-k2": "Kimi-K2-shape", "kimi-k2-cp": "Kimi-K2-shape 8-layer slice"}
 PAGE_SIZE = 64
 
 
@@ -76,7 +85,10 @@ def parse_args(argv=None):
     p.add_argument("--layers", type=int, default=None, help="kimi-k2: decoder layers (default: all 61)")
     p.add_argument("--moe-quant", default="mxfp4", choices=["mxfp4", "mxfp4-a8", "none"],
                    help="kimi-k2: routed expert weights")
-    p.add_argument("--num-reqs", type=int, default=None, help="request pool (default 1000; kimi-k2: 512)")
+    p.add_argument("--num-reqs", type=int, default=None,
+                   help="request pool (default 1000; kimi-k2: 512; kimi-k2-cp: 4 per batch)")
+    p.add_argument("--prompt-len", type=int, default=131072, help="kimi-k2-cp: prompt tokens per request")
+    p.add_argument("--output-len", type=int, default=256, help="kimi-k2-cp: output tokens per request")
     p.add_argument("--step-tokens", type=int, default=8192)
     p.add_argument("--temperature", type=float, default=0.6)
     p.add_argument("--comm", default="fused", choices=["fused", "nccl"])
@@ -84,7 +96,7 @@ def parse_args(argv=None):
     p.add_argument("--json-out", default="")
     args = p.parse_args(argv)
     if args.num_reqs is None:
-        args.num_reqs = 512 if args.shape == "kimi-k2" else 1000
+        args.num_reqs = {"kimi-k2": 512, "kimi-k2-cp": 4}.get(args.shape, 1000)
     return args
 
 
@@ -306,6 +318,12 @@ def config_of(args, world: int) -> Dict[str, object]:
            "l2": "inputs larger than L2 (tens of GB of weights and KV cache streamed per step)"}
     if args.shape == "qwen3-0.6b":
         cfg["seq_len"] = "prompt U[100,1024] + output U[100,1024]"
+    elif args.shape == "kimi-k2-cp":
+        cfg.update(seq_len=f"{args.num_reqs} x {args.prompt_len} prompt tokens + {args.output_len} greedy outputs",
+                   model=f"Kimi-K2-shape {args.layers or 8}-layer slice", global_batch=args.num_reqs,
+                   parallelism=f"cp{world}+ep{world}", routed_experts=f"384 top-8, {args.moe_quant}",
+                   step="one whole batch of fresh prompts", temperature=0.0)
+        cfg.pop("step_tokens")
     elif args.shape == "kimi-k2":
         cfg.update(seq_len="prompt U[512,4096] + output U[128,1024]", global_batch=args.num_reqs,
                    parallelism=f"dp-attention{world}+ep{world}" if world > 1 else "single GPU",
@@ -397,12 +415,120 @@ def run_minisgl(args) -> None:
         dist.destroy_process_group()
 
 
+def run_minisgl_cp(args) -> None:
+    """The long-context context-parallel config: W untimed and K timed
+    batches of ``num_reqs`` fresh random prompts of ``prompt_len`` tokens
+    (fresh, so the prefix cache serves none of them), ``output_len`` greedy
+    tokens each, on an 8-layer Kimi-K2-shape slice with CP = EP = N. Every
+    rank serves the whole batch (token-sharded prefill, replicated decode),
+    so the device times are taken per rank and the max is reported."""
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    sys.path.insert(0, ROOT)
+    from minisgl import ops
+    from minisgl.core import SamplingParams
+    from minisgl.llm import LLM
+    from minisgl.parallel import DistributedInfo
+    from minisgl.utils.synthetic import make_model_dir
+
+    if world > 1:
+        dist.init_process_group("cpu:gloo,cuda:nccl", timeout=timedelta(seconds=900),
+                                device_id=torch.device(f"cuda:{local}"))
+    n, L, out_len = args.num_reqs, args.prompt_len, args.output_len
+    model_dir = make_model_dir("kimi-k2", overrides={"num_hidden_layers": args.layers or 8})
+    llm = metered_llm_class(LLM)(
+        model_dir, dtype=torch.bfloat16, use_dummy_weight=True, device=f"cuda:{local}",
+        tp_info=DistributedInfo(rank, world), cp_size=world, ep_size=world, moe_quant=args.moe_quant,
+        comm=args.comm, page_size=PAGE_SIZE, max_running_req=max(8, n), cuda_graph_max_bs=max(8, n),
+        max_seq_len_override=L + out_len + PAGE_SIZE, max_extend_tokens=16384)
+    stream = llm.engine.stream
+
+    def event():
+        ev = torch.cuda.Event(enable_timing=True)
+        ev.record(stream)
+        return ev
+
+    class BatchMeter:
+        """Events at the start, once every request has its first token, and
+        at the end of one batch."""
+
+        def __init__(self) -> None:
+            self.first: set = set()
+            self.tokens = 0
+            self.start, self.prefilled = event(), None
+
+        def on_reply(self, replies) -> None:
+            for m in replies:
+                self.tokens += 1
+                self.first.add(m.uid)
+            if self.prefilled is None and len(self.first) == n:
+                self.prefilled = event()
+
+    launches0 = ops.LAUNCHES[0]
+    sampler = ClockSampler(list(range(world))) if rank == 0 else None
+    timed = {"total": 0.0, "prefill": 0.0, "decode": 0.0, "wall": 0.0, "tokens": 0, "h2d": 0, "d2h": 0}
+    params = SamplingParams(temperature=0.0, ignore_eos=True, max_tokens=out_len)
+    for b in range(args.warmup + args.steps):
+        rng = random.Random(args.seed * 7919 + b)
+        prompts = [[rng.randrange(10000) for _ in range(L)] for _ in range(n)]
+        if b == args.warmup:
+            launches0 = ops.LAUNCHES[0]
+            if sampler is not None:
+                sampler.start()
+        h2d0, d2h0 = llm.h2d_bytes, llm.d2h_bytes
+        torch.cuda.synchronize()
+        t0 = time.perf_counter()
+        llm.meter = m = BatchMeter()
+        llm.generate(prompts, params)
+        end = event()
+        end.synchronize()
+        wall = time.perf_counter() - t0
+        llm.meter = None
+        if b >= args.warmup:
+            timed["total"] += m.start.elapsed_time(end)
+            timed["prefill"] += m.start.elapsed_time(m.prefilled)
+            timed["decode"] += m.prefilled.elapsed_time(end)
+            timed["wall"] += wall
+            timed["tokens"] += m.tokens
+            timed["h2d"] += llm.h2d_bytes - h2d0
+            timed["d2h"] += llm.d2h_bytes - d2h0
+    clocks = sampler.stop() if sampler is not None else {}
+    launches = ops.LAUNCHES[0] - launches0
+    tot, pre, dec, wall = reduce_over_ranks([timed["total"], timed["prefill"], timed["decode"], timed["wall"]], "max")
+    tot_launches, = reduce_over_ranks([launches], "sum")
+    if rank == 0:
+        K, tokens = args.steps, timed["tokens"]  # every rank serves the same batch
+        emit({
+            "metric": METRIC, "value": round(tokens / (tot / 1000.0), 1), "unit": "tok/s", "n_gpus": world,
+            "steps": K, "warmup": args.warmup, "ms_per_step": round(tot / K, 2), "higher_is_better": True,
+            "scaling": "strong", "vs_baseline": None, "dtype": f"bf16 (routed experts {args.moe_quant})",
+            "data": "synthetic (random token ids, random-init N(0,0.02) weights)",
+            "config": dict(config_of(args, world), comm=args.comm),
+            "clocks": clocks,
+            "phases": {"prefill_ms_per_batch": round(pre / K, 2), "decode_ms_per_batch": round(dec / K, 2),
+                       "prefill_tok_s": round(n * L * K / (pre / 1000.0), 1),
+                       "decode_tpot_ms": round(dec / K / max(1, out_len - 1), 3),
+                       "note": "prefill: until every request has its first token (max over ranks)"},
+            "e2e": {"value": round(tokens / wall, 1), "unit": "tok/s (LLM.generate wall clock)",
+                    "h2d_bytes_per_step": int(timed["h2d"] / K), "d2h_bytes_per_step": int(timed["d2h"] / K)},
+            "gpu_launches": int(tot_launches), "impl": "minisgl",
+        }, args)
+    llm.shutdown()
+    if world > 1 and dist.is_initialized():
+        dist.destroy_process_group()
+
+
 # ------------------------------------------------------------ reference arm
 def run_reference(args) -> None:
     """Run the unmodified reference (baseline/_ref) on the same pool: one
     subprocess per rank whose import path holds only the reference package."""
     rank, world, local = dist_env()
-    if args.shape == "kimi-k2":
+    if args.shape in ("kimi-k2", "kimi-k2-cp"):
         if rank == 0:
             print(json.dumps({"impl": "reference", "unavailable": "the reference has no MLA / DeepSeek-V3 "
                               "architecture, expert parallelism, DP attention or MXFP4 experts"}))
@@ -470,6 +596,8 @@ def main(argv=None) -> None:
     args = parse_args(argv)
     if args.impl == "reference":
         run_reference(args)
+    elif args.shape == "kimi-k2-cp":
+        run_minisgl_cp(args)
     else:
         run_minisgl(args)
 
