@@ -12,18 +12,17 @@ from minisgl.utils import torch_dtype
 from minisgl.utils.synthetic import make_model_dir
 
 
-def _meta_model(quant: str):
-    if info._TP is None:
-        info.set_tp_info(0, 1)
-    assert info.get_tp_info().size == 1
+def _meta_model(quant: str, monkeypatch):
+    # the engine sets this once per process; restored after the test
+    monkeypatch.setattr(info, "_TP", DistributedInfo(0, 1))
     cfg = EngineConfig(model_path=make_model_dir("tiny-qwen3-moe"), tp_info=DistributedInfo(0, 1),
                        dtype=torch.float32, device="cpu", moe_quant=quant)
     with torch.device("meta"), torch_dtype(torch.float32):
         return create_model(cfg.model_config)
 
 
-def test_lazy_draw_gives_the_eager_values():
-    shapes = _meta_model("none").state_dict()
+def test_lazy_draw_gives_the_eager_values(monkeypatch):
+    shapes = _meta_model("none", monkeypatch).state_dict()
     eager = random_weights(shapes, torch.device("cpu"), seed=3)
     lazy = LazyRandomWeights(shapes, torch.device("cpu"), seed=3)
     assert sorted(lazy) == sorted(eager) and len(lazy) == len(eager)
@@ -32,8 +31,8 @@ def test_lazy_draw_gives_the_eager_values():
     assert lazy.pop("no.such.weight", None) is None
 
 
-def test_experts_are_quantised_layer_by_layer():
-    model = _meta_model("mxfp4")
+def test_experts_are_quantised_layer_by_layer(monkeypatch):
+    model = _meta_model("mxfp4", monkeypatch)
     layers = model.model.layers.op_list
     shapes = model.state_dict()
     seen = []
