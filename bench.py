@@ -59,7 +59,6 @@ from __future__ import annotations
 
 import argparse
 import json
-import math
 import os
 import random
 import statistics
@@ -108,37 +107,25 @@ def dist_env() -> Tuple[int, int, int]:
 
 
 # ------------------------------------------------------------------ workload
-def _lognormal_len(rng: random.Random, median: float, sigma: float, lo: int, hi: int) -> int:
-    return int(min(hi, max(lo, round(median * math.exp(rng.gauss(0.0, sigma))))))
+def _workload():
+    """minisgl/benchmark/workload.py, loaded by path: the reference arm's
+    process imports this file while its ``minisgl`` is the reference's."""
+    import importlib.util
+
+    mod = sys.modules.get("_minisgl_bench_workload")
+    if mod is None:
+        spec = importlib.util.spec_from_file_location(
+            "_minisgl_bench_workload", os.path.join(ROOT, "minisgl", "benchmark", "workload.py"))
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        sys.modules["_minisgl_bench_workload"] = mod
+    return mod
 
 
 def make_pool(shape: str, num_reqs: int, seed: int, vocab_limit: int = 10000) -> Tuple[List[List[int]], List[int]]:
     """The request pool (same on every rank and in both arms): prompt token
-    ids and output lengths."""
-    rng = random.Random(seed * 1_000_003 + 17)
-    prompts: List[List[int]] = []
-    outs: List[int] = []
-    if shape == "qwen3-0.6b":  # the reference's offline benchmark distributions
-        for _ in range(num_reqs):
-            prompts.append([rng.randrange(vocab_limit) for _ in range(rng.randint(100, 1024))])
-            outs.append(rng.randint(100, 1024))
-        return prompts, outs
-    if shape == "kimi-k2":  # the expert-parallel serving config
-        for _ in range(num_reqs):
-            prompts.append([rng.randrange(vocab_limit) for _ in range(rng.randint(512, 4096))])
-            outs.append(rng.randint(128, 1024))
-        return prompts, outs
-    prefixes = [[rng.randrange(vocab_limit) for _ in range(rng.randint(512, 2048))] for _ in range(50)]
-    for _ in range(num_reqs):
-        n = _lognormal_len(rng, 1024, 0.8, 32, 16384)
-        if rng.random() < 0.3:
-            pre = prefixes[rng.randrange(len(prefixes))]
-            tail = max(16, n - len(pre))
-            prompts.append(pre + [rng.randrange(vocab_limit) for _ in range(tail)])
-        else:
-            prompts.append([rng.randrange(vocab_limit) for _ in range(n)])
-        outs.append(_lognormal_len(rng, 256, 0.8, 16, 2048))
-    return prompts, outs
+    ids and output lengths (minisgl.benchmark.workload)."""
+    return _workload().make_pool(shape, num_reqs, seed, vocab_limit)
 
 
 class StopRun(Exception):

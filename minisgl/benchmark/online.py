@@ -20,6 +20,13 @@ aiohttp instead of the openai package.
 Prompts are random token ids decoded by `--tokenizer` (a model folder), so a prompt
 holds about `--input-len` tokens. Without a tokenizer they are random words.
 
+`--workload qwen3-32b` (or another pool of minisgl.benchmark.workload) sends
+that pool instead: lognormal prompt and output lengths, 30 % of the prompts
+behind one of 50 shared prefixes (the same text, so the server's radix cache
+serves them). `--rate-sweep 0.5,1,2,4` runs the requests once per Poisson
+rate, without a concurrency cap, and prints one line per rate: the
+throughput / TTFT / TPOT curve of an online serving benchmark.
+
 `--trace FILE --trace-format {qwen,mooncake}` replays a request trace instead. Both
 formats are JSON lines with `timestamp`, `input_length` and `output_length`; other
 fields are ignored. Timestamps are seconds in Qwen traces and milliseconds in Mooncake
@@ -69,6 +76,26 @@ def make_prompts(n: int, input_len: int, tokenizer_path: Optional[str], seed: in
         vocab = getattr(tok, "vocab_size", 32000)
         return [tok.decode([rng.randrange(100, max(101, vocab - 100)) for _ in range(input_len)]) for _ in range(n)]
     return [" ".join(rng.choice(_WORDS) for _ in range(input_len)) for _ in range(n)]
+
+
+def pool_prompts(shape: str, n: int, tokenizer_path: Optional[str], seed: int):
+    """(prompt texts, output lengths, prompt lengths in pool tokens) of a
+    minisgl.benchmark.workload pool.
+    Token ids become text through the tokenizer (ids moved clear of the
+    special ids at the bottom of the vocabulary) or as words; equal id
+    prefixes give equal text prefixes."""
+    from minisgl.benchmark.workload import make_pool
+
+    ids, outs = make_pool(shape, n, seed)
+    if tokenizer_path:
+        from minisgl.utils import load_tokenizer
+
+        tok = load_tokenizer(tokenizer_path)
+        span = max(1, getattr(tok, "vocab_size", 32000) - 200)
+        texts = [tok.decode([100 + t % span for t in p]) for p in ids]
+    else:
+        texts = [" ".join(_WORDS[t % len(_WORDS)] for t in p) for p in ids]
+    return texts, outs, [len(p) for p in ids]
 
 
 async def _one(session, url: str, model: str, prompt: str, output_len: int, timeout: float) -> RequestResult:
@@ -165,28 +192,45 @@ def summarize(results: List[RequestResult], wall: float, input_len: int,
 async def run(url: str, num_requests: int, concurrency: int, input_len: int, output_len: int,
               request_rate: float = float("inf"), tokenizer: Optional[str] = None, seed: int = 0,
               timeout: float = 600.0) -> Dict[str, object]:
+    prompts = make_prompts(num_requests, input_len, tokenizer, seed)
+    return await run_requests(url, prompts, [output_len] * len(prompts), concurrency, request_rate, seed, timeout,
+                              input_len=input_len)
+
+
+async def run_requests(url: str, prompts: List[str], output_lens: List[int], concurrency: int,
+                       request_rate: float = float("inf"), seed: int = 0, timeout: float = 600.0,
+                       input_len: int = 0, input_lens: Optional[List[int]] = None) -> Dict[str, object]:
+    """Send the prompts (at most ``concurrency`` in flight; with a finite
+    ``request_rate`` starting as a Poisson process) and summarise."""
     import aiohttp
 
-    prompts = make_prompts(num_requests, input_len, tokenizer, seed)
     rng = random.Random(seed + 1)
     sem = asyncio.Semaphore(max(1, concurrency))
     async with aiohttp.ClientSession() as session:
         async with session.get(url + "/v1/models") as resp:
             model = (await resp.json())["data"][0]["id"]
 
-        async def guarded(p: str) -> RequestResult:
+        async def guarded(p: str, n_out: int) -> RequestResult:
             async with sem:
-                return await _one(session, url, model, p, output_len, timeout)
+                return await _one(session, url, model, p, n_out, timeout)
 
         t0 = time.perf_counter()
         tasks = []
-        for p in prompts:
-            tasks.append(asyncio.create_task(guarded(p)))
+        for p, n_out in zip(prompts, output_lens):
+            tasks.append(asyncio.create_task(guarded(p, n_out)))
             if request_rate != float("inf"):
                 await asyncio.sleep(rng.expovariate(request_rate))
         results = await asyncio.gather(*tasks)
         wall = time.perf_counter() - t0
-    return summarize(list(results), wall, input_len)
+    return summarize(list(results), wall, input_len, input_lens)
+
+
+def parse_rates(text: str) -> List[float]:
+    """"0.5,1,2" -> [0.5, 1.0, 2.0]; "inf" allowed."""
+    rates = [float(x) for x in text.split(",") if x.strip()]
+    if not rates or any(r <= 0 for r in rates):
+        raise ValueError(f"request rates must be positive: {text!r}")
+    return rates
 
 
 async def run_trace(url: str, entries: List[TraceEntry], tokenizer: Optional[str] = None, seed: int = 0,
@@ -223,8 +267,27 @@ def main() -> None:
     p.add_argument("--trace", default=None, help="JSON-lines request trace to replay")
     p.add_argument("--trace-format", default="qwen", choices=["qwen", "mooncake"])
     p.add_argument("--trace-scale", type=float, default=1.0, help="multiplies the trace's time offsets")
+    p.add_argument("--workload", default="fixed",
+                   help="fixed (--input-len / --output-len) or a pool of minisgl.benchmark.workload: qwen3-32b, "
+                        "qwen3-0.6b, kimi-k2")
+    p.add_argument("--rate-sweep", default=None, help="comma-separated Poisson rates (req/s), one run and line each")
     args = p.parse_args()
     url = args.url.rstrip("/")
+    if args.workload != "fixed" or args.rate_sweep:
+        if args.workload == "fixed":
+            prompts = make_prompts(args.num_requests, args.input_len, args.tokenizer, args.seed)
+            outs, in_lens = [args.output_len] * len(prompts), [args.input_len] * len(prompts)
+        else:
+            prompts, outs, in_lens = pool_prompts(args.workload, args.num_requests, args.tokenizer, args.seed)
+        rates = parse_rates(args.rate_sweep) if args.rate_sweep else [args.request_rate]
+        for rate in rates:
+            # a sweep point is an open-loop Poisson run: no concurrency cap
+            conc = len(prompts) if args.rate_sweep else args.concurrency
+            out = asyncio.run(run_requests(url, prompts, outs, conc, rate, args.seed, input_lens=in_lens,
+                                           input_len=args.input_len))
+            out.update(workload=args.workload, request_rate=rate)
+            print(json.dumps(out), flush=True)
+        return
     if args.trace:
         entries = read_trace(args.trace, args.trace_format, args.num_requests, args.trace_scale)
         out = asyncio.run(run_trace(url, entries, args.tokenizer, args.seed))

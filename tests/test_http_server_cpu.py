@@ -125,6 +125,10 @@ def test_http_server_end_to_end(tmp_path, model, extra):
                                      for t in (0, 200, 400)))  # Mooncake format: milliseconds
             res = asyncio.run(online.run_trace(base, online.read_trace(str(trace), "mooncake")))
             assert res["completed"] == 3 and res["output_tokens"] == 9 and res["wall_s"] >= 0.4, res
+            # per-request output lengths, Poisson arrivals (one point of a rate sweep)
+            res = asyncio.run(online.run_requests(base, ["alpha beta gamma"] * 4, [2, 3, 4, 5], 4,
+                                                  request_rate=20.0, input_lens=[3] * 4))
+            assert res["completed"] == 4 and res["output_tokens"] == 14, res
 
             # a client that leaves mid-stream: the server aborts its request and keeps serving
             import http.client

@@ -55,3 +55,23 @@ def test_sm_clock_log_summary():
     c = SmClockLog.summarize(text, 0)["clocks"]
     assert c["sm_mhz_median_under_load"] == 1477.5 and c["samples_under_load"] == 2
     assert c["sm_max_mhz"] == 1965.0 and c["reasons"] == ["sw_power_cap"]
+
+
+def test_pool_prompts_and_rates():
+    """A benchmark pool as text: lengths and output lengths follow the pool,
+    shared id prefixes stay shared text prefixes (the radix cache's hits),
+    and sweep rates must be positive."""
+    from minisgl.benchmark.online import parse_rates, pool_prompts
+    from minisgl.benchmark.workload import make_pool
+
+    texts, outs, lens = pool_prompts("qwen3-32b", 60, None, seed=2)
+    ids, want_outs = make_pool("qwen3-32b", 60, 2)
+    assert outs == want_outs and lens == [len(p) for p in ids]
+    assert [len(t.split()) for t in texts] == lens
+    shared = [(i, j) for i in range(60) for j in range(i) if ids[i][:512] == ids[j][:512]]
+    assert shared  # 30 % of the prompts start with one of 50 prefixes
+    for i, j in shared:
+        assert texts[i].split()[:512] == texts[j].split()[:512]
+    assert parse_rates("0.5, 2,inf") == [0.5, 2.0, float("inf")]
+    with pytest.raises(ValueError):
+        parse_rates("1,0")
