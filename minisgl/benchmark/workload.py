@@ -8,7 +8,8 @@ Shapes:
                        of the prompts start with one of 50 seeded shared
                        prefixes of 512-2048 tokens (the radix cache serves them)
   qwen3-0.6b           prompts and outputs uniform in [100, 1024] (the
-                       reference's offline benchmark)
+                       reference's offline benchmark,
+                       benchmark/offline/bench.py:12-30)
   kimi-k2              prompts uniform in [512, 4096], outputs in [128, 1024]
 
 The same (shape, size, seed) gives the same pool on every rank and in both

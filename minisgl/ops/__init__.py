@@ -907,7 +907,9 @@ def moe_experts_mx(x: torch.Tensor, w1q: torch.Tensor, w1sb: torch.Tensor, w2q: 
     (packed [E, N, K / 2] with scale blocks [E, N / 128, K / 128, 512] from
     minisgl.quant.block_scales) times MXFP8 token rows (quantised on the
     fly, per 32 along K), tcgen05 .kind::mxf8f6f4 with E8M0 scales. Oracle:
-    minisgl.quant.moe_experts_mx_reference."""
+    minisgl.quant.moe_experts_mx_reference. Takes the place of the
+    reference's bf16 Triton expert kernel
+    (python/minisgl/kernel/triton/fused_moe.py:50-193) for quantised experts."""
     T, H = x.shape
     E, I2 = w1q.shape[0], w1q.shape[1]
     I, k = I2 // 2, topk_ids.shape[1]
