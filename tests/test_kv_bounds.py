@@ -1,7 +1,8 @@
 """Host KV bounds check (MINISGL_DEBUG_BOUNDS=1): bad slots in a batch's
 writes or in a request's page-table row raise KVBoundsError naming the
 request; a normal run (chunked prefill, radix reuse, decode) passes with the
-check on and produces the same tokens as without it."""
+check on and produces the same tokens as without it. Also the keying of the
+device error word that the in-kernel index checks report through."""
 
 from types import SimpleNamespace
 
@@ -58,3 +59,18 @@ def test_engine_run_with_bounds_check(monkeypatch):
         assert len(calls) >= 6  # prefill chunks and every decode step were checked
     finally:
         llm.shutdown()
+
+
+def test_error_word_key_names_the_current_device(monkeypatch):
+    """The device error word is kept per (type, index); a CUDA device given
+    without an index means the current one, so a check through
+    torch.device("cuda") reads the word kernels on cuda:N write."""
+    import torch
+
+    from minisgl import ops
+
+    monkeypatch.setattr(torch.cuda, "current_device", lambda: 3)
+    assert ops._device_key(torch.device("cuda")) == ("cuda", 3)
+    assert ops._device_key("cuda") == ("cuda", 3)
+    assert ops._device_key(torch.device("cuda", 1)) == ("cuda", 1)
+    assert ops._device_key(torch.device("cpu")) == ("cpu", None)
