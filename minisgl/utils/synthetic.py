@@ -68,6 +68,20 @@ SHAPES: Dict[str, Dict[str, Any]] = {
         "rope_scaling": {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0, "high_freq_factor": 4.0,
                          "original_max_position_embeddings": 1024},
     },
+    # Qwen2 (q/k/v biases, no q/k norm) and Mistral (Llama-style, plain RoPE)
+    "tiny-qwen2": {
+        "model_type": "qwen2", "architectures": ["Qwen2ForCausalLM"], "hidden_act": "silu", "rms_norm_eps": 1e-6,
+        "rope_theta": 1000000.0, "max_position_embeddings": 4096, "num_hidden_layers": 2, "hidden_size": 256,
+        "num_attention_heads": 4, "num_key_value_heads": 2, "intermediate_size": 512, "vocab_size": 1024,
+        "tie_word_embeddings": False, "torch_dtype": "float32", "bos_token_id": 0, "eos_token_id": 1,
+    },
+    "tiny-mistral": {
+        "model_type": "mistral", "architectures": ["MistralForCausalLM"], "hidden_act": "silu",
+        "rms_norm_eps": 1e-5, "rope_theta": 10000.0, "max_position_embeddings": 4096, "num_hidden_layers": 2,
+        "hidden_size": 256, "num_attention_heads": 4, "num_key_value_heads": 2, "head_dim": 64,
+        "intermediate_size": 512, "vocab_size": 1024, "tie_word_embeddings": False, "torch_dtype": "float32",
+        "bos_token_id": 0, "eos_token_id": 1, "sliding_window": None,
+    },
     # Kimi-K2 shape (DeepSeek-V3 architecture): expert / context parallel benchmarks
     "kimi-k2": {
         "model_type": "kimi_k2", "architectures": ["DeepseekV3ForCausalLM"], "hidden_act": "silu",
