@@ -114,3 +114,33 @@ def test_nvlink_dispatch_one_rank_matches_local_experts():
         if heap is not None:
             heap.shutdown()
         dist.destroy_process_group()
+
+
+@pytest.fixture(scope="module")
+def tp_checkpoint():
+    import shutil
+    import tempfile
+
+    from minisgl.utils.synthetic import make_model_dir, write_random_checkpoint
+
+    folder = tempfile.mkdtemp(prefix="minisgl_tp_moe_gpu_ckpt_")
+    shutil.rmtree(folder)
+    make_model_dir("tiny-qwen3-moe", folder=folder, overrides=dict(head_dim=128, num_attention_heads=4,
+                                                                    num_key_value_heads=2))
+    write_random_checkpoint(folder, seed=19, std=0.05)
+    yield folder
+    shutil.rmtree(folder, ignore_errors=True)
+
+
+def test_tp2_moe_fused_comm_matches_nccl(tp_checkpoint):
+    """Plain tensor parallelism over a MoE model (experts sharded over the
+    ranks; MoE decoders keep the all-reduce form, not the sequence-parallel
+    one): the NVLink collectives, the default, generate what NCCL generates
+    (the two reduce in different orders, so a near-tie may flip a token)."""
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs 2 GPUs")
+    fused = _spawn(2, False, tp_checkpoint, "fused")
+    nccl = _spawn(2, False, tp_checkpoint, "nccl")
+    assert fused[0] == fused[1] and nccl[0] == nccl[1]
+    same = sum(a == b for x, y in zip(fused[0], nccl[0]) for a, b in zip(x, y))
+    assert same >= 0.8 * sum(len(x) for x in fused[0]), (fused[0], nccl[0])
