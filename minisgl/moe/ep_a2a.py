@@ -105,10 +105,15 @@ class AllToAllMoe(BaseMoeBackend):
         elif not x.is_cuda:
             from .fused import moe_reference
 
-            lw1, lw2 = self.local._cpu_weights(mxfp4) if mxfp4 is not None else (w1, w2)
-            y = moe_reference(recv_x, lw1, lw2, ones, recv_e[:, None], activation, interleaved)
+            if getattr(mxfp4, "blocked", None) is not None and interleaved:
+                from minisgl.quant import moe_experts_mx_reference
+
+                y = moe_experts_mx_reference(recv_x, *mxfp4, ones, recv_e[:, None]).to(recv_x.dtype)
+            else:
+                lw1, lw2 = self.local._cpu_weights(mxfp4) if mxfp4 is not None else (w1, w2)
+                y = moe_reference(recv_x, lw1, lw2, ones, recv_e[:, None], activation, interleaved)
         elif mxfp4 is not None:
-            y = ops.moe_experts_mxfp4(recv_x, *mxfp4, ones, recv_e[:, None])
+            y = ops.moe_experts_quantised(recv_x, mxfp4, ones, recv_e[:, None])
         else:
             y = ops.moe_experts(recv_x, w1, w2, ones, recv_e[:, None])
         # combine: rows back to their source, weighted sum over each token's slots

@@ -71,9 +71,6 @@ class FusedMoe(BaseMoeBackend):
         if not interleaved:
             raise RuntimeError("minisgl: the CUDA MoE path needs SiLU experts with gate|up rows interleaved "
                                "in 64-row blocks (MoELayer does this after loading)")
-        if mxfp4 is not None:
-            blocked = getattr(mxfp4, "blocked", None)
-            if blocked is not None:  # MXFP8 activations on the block-scaled tensor cores
-                return ops.moe_experts_mx(hidden_states, mxfp4[0], blocked[0], mxfp4[2], blocked[1], topk_w, topk_ids)
-            return ops.moe_experts_mxfp4(hidden_states, *mxfp4, topk_w, topk_ids)
+        if mxfp4 is not None:  # W4A16, or MXFP8 activations on the block-scaled tensor cores
+            return ops.moe_experts_quantised(hidden_states, mxfp4, topk_w, topk_ids)
         return ops.moe_experts(hidden_states, w1, w2, topk_w, topk_ids)

@@ -885,6 +885,29 @@ def moe_experts_mxfp4(x: torch.Tensor, w1q: torch.Tensor, w1s: torch.Tensor, w2q
     return out
 
 
+def _moe_experts_mx_rows(x, mxfp4, blocked, topk_w, topk_ids, tile: int):
+    """moe_experts_rows for block-scaled MX experts: (ys, pair_pos)."""
+    T, H = x.shape
+    k = topk_ids.shape[1]
+    E, I = mxfp4[0].shape[0], mxfp4[0].shape[1] // 2
+    P = T * k + E * (tile - 1)
+    Pp = (P + tile - 1) // tile * tile
+    dev, i32, u8 = x.device, torch.int32, torch.uint8
+    ys = torch.empty(Pp, H, dtype=x.dtype, device=dev)
+    pair_pos = torch.empty(T * k, dtype=i32, device=dev)
+    _count(5)  # align, gather + quantise, gate_up GEMM, quantise, down GEMM
+    native().moe_experts_mx(torch.empty(0, H, dtype=x.dtype, device=dev), x.contiguous(), mxfp4[0], blocked[0],
+                            mxfp4[2], blocked[1], topk_w.float().contiguous(), topk_ids.to(i32).contiguous(), tile,
+                            torch.empty(Pp, H, dtype=u8, device=dev),
+                            torch.empty(Pp // tile, H // 128, 512, dtype=u8, device=dev),
+                            torch.empty(Pp, I, dtype=x.dtype, device=dev), torch.empty(Pp, I, dtype=u8, device=dev),
+                            torch.empty(Pp // tile, I // 128, 512, dtype=u8, device=dev), ys,
+                            torch.empty(P, dtype=i32, device=dev), pair_pos,
+                            torch.empty(P // tile, dtype=i32, device=dev), torch.empty(P // tile, dtype=i32, device=dev),
+                            torch.empty(1, dtype=i32, device=dev), error_word(dev), False)
+    return ys, pair_pos
+
+
 def mx8_quantize(x: torch.Tensor, tile: int, idx: Optional[torch.Tensor] = None, k: int = 1,
                  rows: Optional[int] = None) -> Tuple[torch.Tensor, torch.Tensor]:
     """MXFP8 rows for the block-scaled expert GEMM (E4M3 + E8M0 per 32, as
@@ -938,6 +961,16 @@ def moe_experts_mx(x: torch.Tensor, w1q: torch.Tensor, w1sb: torch.Tensor, w2q: 
     return out
 
 
+def moe_experts_quantised(x: torch.Tensor, mxfp4: tuple, topk_w: torch.Tensor, topk_ids: torch.Tensor) -> torch.Tensor:
+    """MXFP4 routed experts: on the block-scaled tensor cores with MXFP8
+    activations when the weights carry scale blocks (``--moe-quant
+    mxfp4-a8``, minisgl.quant.MxfpExperts.blocked), else W4A16."""
+    blocked = getattr(mxfp4, "blocked", None)
+    if blocked is not None:
+        return moe_experts_mx(x, mxfp4[0], blocked[0], mxfp4[2], blocked[1], topk_w, topk_ids)
+    return moe_experts_mxfp4(x, *mxfp4, topk_w, topk_ids)
+
+
 def moe_experts_rows(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tensor, w1=None, w2=None,
                      mxfp4: Optional[tuple] = None, tile: int = 0):
     """The expert pipeline without the combine: returns (ys [P, H] expert
@@ -947,6 +980,9 @@ def moe_experts_rows(x: torch.Tensor, topk_w: torch.Tensor, topk_ids: torch.Tens
     k = topk_ids.shape[1]
     E = (mxfp4[0] if mxfp4 is not None else w1).shape[0]
     I = (mxfp4[2].shape[2] * 2) if mxfp4 is not None else w2.shape[2]
+    blocked = getattr(mxfp4, "blocked", None)
+    if blocked is not None:  # block-scaled MX experts (MXFP8 activations)
+        return _moe_experts_mx_rows(x, mxfp4, blocked, topk_w, topk_ids, tile or moe_tile(T, k, E))
     tile = tile or (moe_tile_mxfp4(T, k, E) if mxfp4 is not None else moe_tile(T, k, E))
     P = T * k + E * (tile - 1)
     Pp = (P + tile - 1) // tile * tile

@@ -119,7 +119,8 @@ class MxfpExperts(tuple):
     """MXFP4 routed-expert weights (w1 packed, w1 scales, w2 packed, w2
     scales). ``blocked`` holds (w1, w2) scale blocks when the experts run on
     the block-scaled tensor cores with MXFP8 activations
-    (``--moe-quant mxfp4-a8``); backends without that path use the tuple."""
+    (``--moe-quant mxfp4-a8``; every MoE backend routes them through
+    ``minisgl.ops.moe_experts_quantised`` / ``moe_experts_rows``)."""
 
     blocked: Optional[Tuple[torch.Tensor, torch.Tensor]] = None
 

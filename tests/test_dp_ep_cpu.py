@@ -24,14 +24,14 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _run(rank, world, folder, port, dp, prompts, max_tokens, q):
+def _run(rank, world, folder, port, dp, prompts, max_tokens, q, quant="none"):
     from minisgl.core import SamplingParams
     from minisgl.llm import LLM
     from minisgl.parallel import DistributedInfo
 
     llm = LLM(folder, dtype=torch.float32, device="cpu", tp_info=DistributedInfo(rank, world), page_size=16,
               num_page_override=64, max_running_req=4, max_seq_len_override=256, max_extend_tokens=64,
-              distributed_port=port, enable_dp_attention=dp)
+              distributed_port=port, enable_dp_attention=dp, moe_quant=quant)
     sps = [SamplingParams(temperature=0.0, max_tokens=m, ignore_eos=True) for m in max_tokens]
     outs = llm.generate(prompts, sps)
     q.put((rank, [o["token_ids"] for o in outs]))
@@ -50,11 +50,11 @@ def checkpoint():
     shutil.rmtree(folder, ignore_errors=True)
 
 
-def _generate(world, folder, dp, prompts, max_tokens):
+def _generate(world, folder, dp, prompts, max_tokens, quant="none"):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_run, args=(r, world, folder, port, dp, prompts, max_tokens, q))
+    procs = [ctx.Process(target=_run, args=(r, world, folder, port, dp, prompts, max_tokens, q, quant))
              for r in range(world)]
     for p in procs:
         p.start()
@@ -69,6 +69,15 @@ def test_dp2_ep2_matches_single_rank(checkpoint):
     lens = [8, 3, 12, 5]  # uneven: one rank finishes first and keeps stepping with filler batches
     single = _generate(1, checkpoint, False, PROMPTS, lens)[0]
     dp = _generate(2, checkpoint, True, PROMPTS, lens)
+    assert dp[0] == dp[1] == single
+
+
+def test_dp2_mx_a8_matches_single_rank(checkpoint):
+    """Block-scaled MX experts (``--moe-quant mxfp4-a8``) behind the token
+    dispatch: the received rows go through the same MXFP8 statement."""
+    lens = [6, 4, 7, 5]
+    single = _generate(1, checkpoint, False, PROMPTS, lens, quant="mxfp4-a8")[0]
+    dp = _generate(2, checkpoint, True, PROMPTS, lens, quant="mxfp4-a8")
     assert dp[0] == dp[1] == single
 
 

@@ -111,3 +111,11 @@ def test_mxfp4_error_and_layer():
     tw, ti = ref.moe_route(logits, k, "softmax", True)
     want = moe_reference(x, d1, dequantize_mxfp4(*q2), tw, ti, "silu")
     assert torch.allclose(got, want, atol=1e-5)
+
+
+def test_ep2_mx_a8_matches_single_rank(checkpoint):
+    """Block-scaled MX experts (MXFP8 activations, ``--moe-quant mxfp4-a8``)
+    through the expert-parallel dispatch generate what one rank generates."""
+    single = _generate(1, checkpoint, quant="mxfp4-a8")[0]
+    ep = _generate(2, checkpoint, ep=2, quant="mxfp4-a8")
+    assert ep[0] == ep[1] == single
