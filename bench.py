@@ -353,8 +353,11 @@ def run_minisgl(args) -> None:
     if moe:  # attention data-parallel, routed experts split over the ranks (EP = N), MXFP4 experts
         overrides = {"num_hidden_layers": args.layers} if args.layers else None
         model_dir = make_model_dir(args.shape, overrides=overrides)
+        # 2048-token prefill chunks: the DP token dispatch sizes its peer slots
+        # and expert buffers for chunk x top-k pairs from every rank (about
+        # 6 GB per rank at 2048; 25 GB at 8192), held beside the KV cache
         extra = dict(enable_dp_attention=world > 1, moe_quant=args.moe_quant, max_seq_len_override=5120,
-                     max_extend_tokens=8192)
+                     max_extend_tokens=2048, memory_ratio=0.85)
     else:
         model_dir = make_model_dir(args.shape)
         extra = dict(max_seq_len_override=20480, max_extend_tokens=16384)
