@@ -104,12 +104,28 @@ def build_parser() -> argparse.ArgumentParser:
     p.add_argument("--moe-backend", default=ServerArgs.moe_backend,
                    choices=["auto"] + SUPPORTED_MOE_BACKENDS.supported_names())
     p.add_argument("--shell-mode", action="store_true")
+    p.add_argument("--profile-steps", default=None, metavar="A:B",
+                   help="bracket scheduler steps A..B-1 with cudaProfilerStart / Stop (for nsys "
+                        "--capture-range=cudaProfilerApi or ncu --profile-from-start off); sets "
+                        "MINISGL_CUDA_PROFILER_STEPS for the scheduler processes")
     return p
 
 
 def parse_args(args: List[str], run_shell: bool = False) -> Tuple[ServerArgs, bool]:
     kw = vars(build_parser().parse_args(args)).copy()
     run_shell |= kw.pop("shell_mode")
+    window = kw.pop("profile_steps")
+    if window is not None:
+        from minisgl.env import ENV
+        from minisgl.scheduler.profile import parse_step_window
+
+        try:
+            parse_step_window(window)
+        except ValueError as e:
+            raise SystemExit(f"--profile-steps: {e}") from e
+        # the scheduler processes read it when they start (spawned with this environment)
+        os.environ["MINISGL_CUDA_PROFILER_STEPS"] = window
+        ENV.CUDA_PROFILER_STEPS.value = window
     if run_shell:
         kw.update(cuda_graph_max_bs=1, max_running_req=1, silent_output=True)
     path: str = kw["model_path"]

@@ -36,3 +36,17 @@ def test_cpu_device_runs_fp32_and_shell_mode_serves_one_request():
     args, shell = parse_args(["--model", "synthetic:tiny-qwen3", "--device", "cpu", "--shell-mode"])
     assert shell and args.dtype == torch.float32
     assert args.max_running_req == 1 and args.cuda_graph_max_bs == 1
+
+
+def test_profile_steps_flag_sets_the_profiler_window(monkeypatch):
+    from minisgl.env import ENV
+
+    # recorded by monkeypatch, so the value parse_args sets is undone afterwards
+    monkeypatch.setenv("MINISGL_CUDA_PROFILER_STEPS", "")
+    monkeypatch.setattr(ENV.CUDA_PROFILER_STEPS, "value", "")
+    parse_args(["--model", "synthetic:tiny-qwen3", "--profile-steps", "10:20"])
+    import os
+
+    assert os.environ["MINISGL_CUDA_PROFILER_STEPS"] == "10:20" and ENV.CUDA_PROFILER_STEPS.value == "10:20"
+    with pytest.raises(SystemExit):
+        parse_args(["--model", "synthetic:tiny-qwen3", "--profile-steps", "20:10"])
