@@ -1,13 +1,15 @@
 """NVLink collectives from our own kernels (``--comm fused``) on 2, 4 and 8
 GPUs (as many as the box has): the
 one-shot all-reduce (plain and with the residual add fused), the all-gather,
-the sequence-parallel reduce-scatter + residual + RMSNorm + all-gather and a
-CUDA-graph replay against NCCL, and a TP=2 engine with the fused
+the sequence-parallel reduce-scatter + residual + RMSNorm + all-gather, a
+rank that enters late (within the wait budget) and a CUDA-graph replay
+against NCCL, and a TP=2 engine with the fused
 communicator (sequence-parallel decoder) against one with NCCL. Ranks are child processes; NCCL's NVLS
 is off and no multicast object is created."""
 
 import os
 import socket
+import time
 from datetime import timedelta
 
 import pytest
@@ -60,6 +62,16 @@ def _collectives(rank, world, port, q):
             dist.all_gather(outs, out)
             if not all(torch.equal(o, outs[0]) for o in outs):
                 msgs.append(f"ranks differ n={n}")
+        # a lagging rank (rank 0 enters half a second late, well inside the
+        # peers' 2 s wait budget): the others wait for it and the sums hold
+        lag = torch.full((4096,), float(rank + 1), device=dev, dtype=torch.bfloat16)
+        torch.cuda.synchronize(dev)
+        if rank == 0:
+            time.sleep(0.5)
+        impl.all_reduce(lag)
+        torch.cuda.synchronize(dev)
+        if not torch.all(lag.float() == float(world * (world + 1) // 2)):
+            msgs.append("lagging rank")
         # GEMM partial written into the heap, reduced into the residual in place
         part = impl.partial_buffer(64, 1024)
         part.copy_(torch.randn(64, 1024, device=dev, generator=g).to(torch.bfloat16))
