@@ -139,3 +139,21 @@ def test_mx_experts_engine_on_cpu():
         assert firsts == len(a), (a, b)
     finally:
         shutil.rmtree(folder, ignore_errors=True)
+
+
+def test_mx8_tiny_blocks_stay_finite():
+    """Block maxima down in fp32's subnormal range: amax / 448 has a zero
+    exponent field, the scale byte is 1 (2^-126), and the elements stay
+    finite and within half an E4M3 step (or half its subnormal step)."""
+    x = torch.zeros(16, 128)
+    x[0, :32] = torch.linspace(-1e-39, 1e-39, 32)   # subnormal fp32 values
+    x[1, 32:64] = 3e-37
+    q, sf = quantize_mx8_reference(x, 16)
+    deq = dequantize_mx8(q, sf, 16)
+    assert torch.isfinite(deq).all()
+    off = scale_block_offsets(16)
+    assert sf[0, 0, off[0, 0]] == 1 and sf[0, 0, off[1, 1]] >= 1
+    scale = 2.0 ** -126
+    err = (deq[0, :32].double() - x[0, :32].double()).abs()
+    assert (err <= x[0, :32].double().abs() * 2.0 ** -4 + scale * 2.0 ** -10 + 1e-45).all()
+    assert deq[1, 32:64].sub(3e-37).abs().max() <= 3e-37 * 2.0 ** -4
