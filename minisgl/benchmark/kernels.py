@@ -348,6 +348,26 @@ def bench_moe_mx(T: int, E: int, k: int, H: int, I: int, peaks) -> Dict:
             "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
 
 
+def bench_mx8_quantize(P: int, K: int, tile: int, peaks) -> Dict:
+    """The MXFP8 row quantiser of the block-scaled expert path alone: bf16
+    rows in, E4M3 rows and 512-byte scale blocks out, checked bit for bit
+    against its PyTorch statement, timed against the measured HBM copy
+    bandwidth."""
+    from minisgl.quant import quantize_mx8_reference
+
+    g = torch.Generator(device="cuda").manual_seed(0)
+    x = (torch.randn(P, K, device="cuda", generator=g) * 2).to(torch.bfloat16)
+    q, sf = ops.mx8_quantize(x, tile)
+    torch.cuda.synchronize()
+    wq, wsf = quantize_mx8_reference(x.float(), tile)
+    exact = bool(torch.equal(q, wq) and torch.equal(sf, wsf))
+    ms = time_kernel(lambda: ops.mx8_quantize(x, tile))
+    nbytes = P * K * 2 + P * K + sf.numel()
+    gbs = nbytes / ms / 1e6
+    return {"kernel": "mx8_quantize", "P": P, "K": K, "tile": tile, "exact": exact, "ms": round(ms, 4),
+            "GB/s": round(gbs, 1), "frac_hbm": round(gbs / peaks["hbm_gbs"], 3)}
+
+
 def bench_sample(B: int, V: int, peaks) -> List[Dict]:
     """Sampling from fp32 logits [B, V]: argmax (greedy) and Gumbel-max with
     temperature (counter-based noise); bytes = the logits read once."""
@@ -763,6 +783,8 @@ def main() -> None:
         cases.append((f"moe_mxfp4 T={T}", lambda T=T: bench_moe_mxfp4(T, 16, 8, 7168, 2048, peaks)))
     for T in (16, 256):
         cases.append((f"moe_mx T={T}", lambda T=T: bench_moe_mx(T, 16, 8, 7168, 2048, peaks)))
+    for P, tile in ((2048, 16), (16384, 128)):
+        cases.append((f"mx8_quantize P={P}", lambda P=P, tile=tile: bench_mx8_quantize(P, 7168, tile, peaks)))
     for M in (1, 8, 32, 64, 128, 192, 256):
         cases.append((f"layer_chain M={M};", lambda M=M: bench_layer_chain(M, peaks)))
     cases.append(("rowkernels M=256", lambda: bench_row_kernels(256, peaks)))
