@@ -786,11 +786,11 @@ def main() -> None:
     cases.append(("rowkernels M=256", lambda: bench_row_kernels(256, peaks)))
     for B in (64, 256):
         cases.append((f"sample B={B}", lambda B=B: bench_sample(B, 151936, peaks)))
-    # the block-scaled MX expert path last: the newest kernels
-    for T in (16, 256):
-        cases.append((f"moe_mx T={T}", lambda T=T: bench_moe_mx(T, 16, 8, 7168, 2048, peaks)))
+    # the block-scaled MX expert path last (the newest kernels), its quantiser first
     for P, tile in ((2048, 16), (16384, 128)):
         cases.append((f"mx8_quantize P={P}", lambda P=P, tile=tile: bench_mx8_quantize(P, 7168, tile, peaks)))
+    for T in (16, 256):
+        cases.append((f"moe_mx T={T}", lambda T=T: bench_moe_mx(T, 16, 8, 7168, 2048, peaks)))
     rows: List[Dict] = []
     clocks = SmClockLog(torch.cuda.current_device()).start()
     for label, fn in cases:
